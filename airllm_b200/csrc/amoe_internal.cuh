@@ -1,0 +1,126 @@
+// amoe_internal.cuh -- shared definitions of the B200 MoE-block library.
+//
+// Device data layout (per layer) and the kernel launchers that the C-ABI in
+// ctx.cu strings together.  See include/amoe.h for the public boundary.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace amoe {
+
+// ---------------------------------------------------------------------------
+// Tiled MXFP4 weight layout ("fragment tiles")
+//
+// The GGUF tensor stores, per expert, R rows of K values as K/32 blocks of
+// 17 bytes (1 E8M0 scale byte + 16 bytes of E2M1 nibbles, low nibble = even
+// element).  Upload shuffles those bytes, losslessly, into two planes:
+//
+//   q[e][rt][kt][lane][16 B]   rt = R/16 row tiles, kt = K/64 k tiles
+//   s[e][rt][kt][32 B]
+//
+// A tile is 16 rows x 64 values (2 scale blocks).  Lane (g = lane/4,
+// c = lane%4) holds, in order:
+//   bytes 0-3   tile row g,   block 0, nibble bytes 4c..4c+3
+//   bytes 4-7   tile row g+8, block 0, nibble bytes 4c..4c+3
+//   bytes 8-11  tile row g,   block 1
+//   bytes 12-15 tile row g+8, block 1
+// which is exactly the A-fragment of two m16n8k16 MMAs per block once each
+// byte goes through cvt.rn.f16x2.e2m1x2 (the k order inside a block is
+// permuted consistently with the activation fragment).  Scale byte
+// s[...][4*g + 2*h + b] belongs to tile row g + 8*h, block b.
+//
+// gate_up rows are additionally re-ordered so that tile row g holds the gate
+// row of pair p = 8*rt + g (GGUF row 2p) and tile row g+8 its up row (GGUF
+// row 2p+1): the fused SwiGLU pairs sit in the same thread / TMEM lane + 8.
+// ---------------------------------------------------------------------------
+constexpr int kTileRows = 16;
+constexpr int kTileK = 64;
+constexpr int kTileQBytes = 512;
+constexpr int kTileSBytes = 32;
+
+struct LayerDev {
+    float *norm_gain = nullptr;   // [H]
+    float *router_wt = nullptr;   // [H x E]  (transposed: lane-per-expert loads coalesce)
+    float *router_b = nullptr;    // [E]
+    uint8_t *gu_q = nullptr;      // [E][2I/16][H/64][512]
+    uint8_t *gu_s = nullptr;      // [E][2I/16][H/64][32]
+    float *gu_b = nullptr;        // [E][2I]  GGUF row order
+    uint8_t *dn_q = nullptr;      // [E][H/16][I/64][512]
+    uint8_t *dn_s = nullptr;      // [E][H/16][I/64][32]
+    float *dn_b = nullptr;        // [E][H]
+};
+
+struct Dims {
+    int H, I, E, k;
+    float eps;
+};
+
+// Routing kernels ------------------------------------------------------------
+constexpr int kRouteTokens = 8;  // tokens per routing CTA (one "chunk")
+constexpr int kRouteWarps = 8;
+
+struct RouteOut {
+    __half *x_hi, *x_lo;     // [T][H] fp16 split of RMSNorm(residual): x ~= hi + lo
+    float *logits;           // [T][E]
+    int32_t *topk_idx;       // [T][k]
+    float *topk_w;           // [T][k]
+    int32_t *hist;           // [nchunk][E]
+    int32_t *chunk_base;     // [nchunk][E]
+    int32_t *counts;         // [E]
+    int32_t *offsets;        // [E+1]
+    int32_t *active;         // [E] experts with counts > 0, ascending; then n_active at [E]
+    int32_t *perm_pair;      // [T*k] position -> pair id
+    int32_t *inv;            // [T*k] pair id -> position
+};
+
+// Optional per-stage timing callback: hook(arg, stage) after a stage's launch.
+typedef void (*StageHook)(void *arg, int stage);
+
+// partial/arrivals: split-K scratch for small T (nullable: no split).
+cudaError_t launch_route_impl(const Dims &d, const LayerDev &L, const float *residual, int T,
+                              const RouteOut &o, double *partial, int32_t *arrivals,
+                              cudaStream_t st, StageHook hook = nullptr, void *hook_arg = nullptr);
+// Largest number of doubles the split-K partial buffer needs for any T <= max_tokens.
+size_t route_partial_elems(int max_tokens, int H, int E);
+
+// Weight upload ----------------------------------------------------------------
+// gguf: E*R*(K/32)*17 bytes on the device.  pair_rows: gate_up row re-order.
+cudaError_t launch_repack(const uint8_t *gguf, int E, int R, int K, bool pair_rows,
+                          uint8_t *q, uint8_t *s, cudaStream_t st);
+cudaError_t launch_transpose_router(const float *w, int E, int H, float *wt, cudaStream_t st);
+
+// Expert GEMV (decode) ---------------------------------------------------------
+cudaError_t launch_gemv_gate_up(const Dims &d, const LayerDev &L, const RouteOut &r, int T,
+                                __half *act_hi, __half *act_lo, cudaStream_t st);
+cudaError_t launch_gemv_down(const Dims &d, const LayerDev &L, const RouteOut &r, int T,
+                             const __half *act_hi, const __half *act_lo, float *y,
+                             cudaStream_t st);
+
+// tcgen05 grouped GEMM (prefill) -------------------------------------------------
+size_t tc_scratch_bytes(int max_pairs, int H, int I);
+bool tc_supported();
+// Runs gate_up(+SwiGLU) and down for all pairs; *launches receives the kernel count.
+cudaError_t launch_tc_forward(const Dims &d, const LayerDev &L, const RouteOut &r, int T,
+                              __half *act_hi, __half *act_lo, float *y, void *tc_scratch,
+                              cudaStream_t st, StageHook hook, void *hook_arg, int *launches);
+
+// Combine --------------------------------------------------------------------
+cudaError_t launch_combine(const Dims &d, const float *residual, const RouteOut &r,
+                           const float *y, int T, float *out, cudaStream_t st);
+
+// Shared device helpers ---------------------------------------------------------
+__device__ __forceinline__ float e8m0_to_float(uint32_t b) {
+    // 2^(b-127); b == 0 is the subnormal 2^-127; b == 255 is NaN (tensor.go:152-155)
+    uint32_t bits = b == 0 ? 0x00400000u : (b == 255 ? 0x7fc00000u : (b << 23));
+    return __uint_as_float(bits);
+}
+
+__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
+    uint32_t r;
+    asm("{\n .reg .b8 t;\n cvt.u8.u32 t, %1;\n cvt.rn.f16x2.e2m1x2 %0, t;\n}" : "=r"(r) : "r"(byte));
+    return r;
+}
+
+}  // namespace amoe

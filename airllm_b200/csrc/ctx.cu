@@ -1,0 +1,613 @@
+// ctx.cu -- the C ABI (include/amoe.h): context, weight upload, forward.
+//
+// Host-side orchestration only; the arithmetic lives in route.cu, gemv.cu,
+// combine.cu and gemm_tc.cu.  Error behaviour mirrors the reference's Go
+// error returns (e.g. internal/model/gptoss/layer.go:35-39, tensor.go:95-97,
+// moe.go:13-18): every failure is a negative status plus a message, never an
+// abort.
+#include "../../include/amoe.h"
+#include "amoe_internal.cuh"
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+namespace amoe {
+
+
+namespace {
+
+thread_local std::string g_create_error;
+
+struct Status {
+    int code;
+    std::string msg;
+};
+
+struct LayerBlock {
+    // byte offsets inside one layer's device-format block (256-B aligned parts)
+    size_t norm, router_wt, router_b, gu_b, dn_b, gu_s, dn_s, gu_q, dn_q, total;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+LayerBlock layer_block(const Dims &d) {
+    LayerBlock b{};
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        size_t at = o;
+        o = align256(o + bytes);
+        return at;
+    };
+    const size_t H = d.H, I = d.I, E = d.E;
+    b.norm = take(H * 4);
+    b.router_wt = take(H * E * 4);
+    b.router_b = take(E * 4);
+    b.gu_b = take(E * 2 * I * 4);
+    b.dn_b = take(E * H * 4);
+    b.gu_s = take(E * 2 * I * (H / 32));
+    b.dn_s = take(E * H * (I / 32));
+    b.gu_q = take(E * 2 * I * (H / 2));
+    b.dn_q = take(E * H * (I / 2));
+    b.total = o;
+    return b;
+}
+
+LayerDev layer_view(uint8_t *base, const LayerBlock &b) {
+    LayerDev L;
+    L.norm_gain = reinterpret_cast<float *>(base + b.norm);
+    L.router_wt = reinterpret_cast<float *>(base + b.router_wt);
+    L.router_b = reinterpret_cast<float *>(base + b.router_b);
+    L.gu_b = reinterpret_cast<float *>(base + b.gu_b);
+    L.dn_b = reinterpret_cast<float *>(base + b.dn_b);
+    L.gu_s = base + b.gu_s;
+    L.dn_s = base + b.dn_s;
+    L.gu_q = base + b.gu_q;
+    L.dn_q = base + b.dn_q;
+    return L;
+}
+
+}  // namespace
+}  // namespace amoe
+
+using namespace amoe;
+
+struct amoe_ctx {
+    amoe_config cfg{};
+    Dims d{};
+    LayerBlock blk{};
+    cudaStream_t stream = nullptr;       // compute
+    cudaStream_t copy_stream = nullptr;  // layer streaming
+    std::string err;
+
+    // resident mode: one device block per layer; streaming: pinned host blocks + slots
+    std::vector<uint8_t *> layer_dev;    // [layers] (resident) device block or null
+    std::vector<uint8_t *> layer_host;   // [layers] (streaming) pinned block or null
+    std::vector<bool> uploaded;
+    std::vector<uint8_t *> slot_dev;     // [stream_slots]
+    std::vector<int> slot_layer;
+    std::vector<cudaEvent_t> slot_ready, slot_free;
+    std::vector<long long> slot_used;    // LRU stamp
+    long long tick = 0;
+
+    // scratch
+    int max_tokens = 0, nchunk_max = 0;
+    void *scratch = nullptr;
+    RouteOut r{};
+    double *partial = nullptr;
+    int32_t *arrivals = nullptr;
+    __half *act_hi = nullptr, *act_lo = nullptr;
+    float *y = nullptr;
+    void *tc_scratch = nullptr;
+    float *io_in = nullptr, *io_out = nullptr;
+    int32_t *io_idx = nullptr;
+    float *io_w = nullptr;
+    int last_T = 0;
+
+    // diagnostics
+    bool profiling = false;
+    amoe_stats stats{};
+    struct PendingTiming {
+        cudaEvent_t ev[AMOE_STAGES + 1];
+        int stage_of[AMOE_STAGES + 1];
+        int n;
+    };
+    std::vector<PendingTiming> pending;
+    std::vector<cudaEvent_t> event_pool;
+};
+
+namespace {
+
+int fail(amoe_ctx *c, int code, const std::string &msg) {
+    if (c) c->err = msg;
+    return code;
+}
+
+int cuda_fail(amoe_ctx *c, cudaError_t e, const char *what) {
+    std::string m = std::string(what) + ": " + cudaGetErrorString(e);
+    return fail(c, e == cudaErrorMemoryAllocation ? AMOE_ERR_NOMEM : AMOE_ERR_CUDA, m);
+}
+
+#define AMOE_CUDA(ctx, call)                                  \
+    do {                                                      \
+        cudaError_t e_ = (call);                              \
+        if (e_ != cudaSuccess) return cuda_fail(ctx, e_, #call); \
+    } while (0)
+
+std::string validate(const amoe_config *c) {
+    if (!c) return "config must not be NULL";
+    if (c->hidden <= 0 || c->hidden % 64) return "hidden must be a positive multiple of 64";
+    if (c->intermediate <= 0 || c->intermediate % 64)
+        return "intermediate must be a positive multiple of 64";
+    if (c->experts < 1 || c->experts > 256) return "experts must be in [1, 256]";
+    if (c->top_k < 1 || c->top_k > c->experts || c->top_k > 32)
+        return "moe router top-k " + std::to_string(c->top_k) + " outside [1, " +
+               std::to_string(c->experts < 32 ? c->experts : 32) + "]";
+    if (c->layers < 1) return "layers must be positive";
+    if (!(c->rms_eps > 0.0f) || !std::isfinite(c->rms_eps))
+        return "rmsnorm epsilon must be positive";
+    if (c->swiglu_alpha != 1.702f || c->swiglu_limit != 7.0f)
+        return "gpt-oss swiglu constants are fixed at alpha 1.702, limit 7";
+    if (c->max_tokens < 1) return "max_tokens must be positive";
+    if (c->stream_slots != 0 && c->stream_slots < 2) return "stream_slots must be 0 or >= 2";
+    if (c->ep_size < 1 || c->ep_rank < 0 || c->ep_rank >= c->ep_size)
+        return "ep_rank must be in [0, ep_size)";
+    if (c->ep_size > 1) return "expert parallelism is not available in this build";
+    if (c->path < AMOE_PATH_AUTO || c->path > AMOE_PATH_TENSOR) return "unknown path";
+    return "";
+}
+
+int alloc_scratch(amoe_ctx *c) {
+    const Dims &d = c->d;
+    const size_t T = c->cfg.max_tokens, P = T * d.k;
+    c->max_tokens = (int)T;
+    c->nchunk_max = (int)((T + kRouteTokens - 1) / kRouteTokens);
+    const size_t partial = route_partial_elems((int)T, d.H, d.E);
+    size_t off = 0;
+    struct Part {
+        void **dst;
+        size_t bytes;
+    };
+    std::vector<Part> parts = {
+        {(void **)&c->r.x_hi, T * d.H * 2},
+        {(void **)&c->r.x_lo, T * d.H * 2},
+        {(void **)&c->r.logits, T * d.E * 4},
+        {(void **)&c->r.topk_idx, P * 4},
+        {(void **)&c->r.topk_w, P * 4},
+        {(void **)&c->r.hist, (size_t)c->nchunk_max * d.E * 4},
+        {(void **)&c->r.chunk_base, (size_t)c->nchunk_max * d.E * 4},
+        {(void **)&c->r.counts, (size_t)d.E * 4},
+        {(void **)&c->r.offsets, (size_t)(d.E + 1) * 4},
+        {(void **)&c->r.active, (size_t)(d.E + 1) * 4},
+        {(void **)&c->r.perm_pair, P * 4},
+        {(void **)&c->r.inv, P * 4},
+        {(void **)&c->partial, partial * 8},
+        {(void **)&c->arrivals, (size_t)c->nchunk_max * 4},
+        {(void **)&c->act_hi, P * d.I * 2},
+        {(void **)&c->act_lo, P * d.I * 2},
+        {(void **)&c->y, P * d.H * 4},
+        {(void **)&c->tc_scratch, tc_scratch_bytes((int)P, d.H, d.I)},
+        {(void **)&c->io_in, T * d.H * 4},
+        {(void **)&c->io_out, T * d.H * 4},
+        {(void **)&c->io_idx, P * 4},
+        {(void **)&c->io_w, P * 4},
+    };
+    std::vector<size_t> at(parts.size());
+    for (size_t i = 0; i < parts.size(); ++i) {
+        at[i] = off;
+        off = align256(off + parts[i].bytes);
+    }
+    AMOE_CUDA(c, cudaMalloc(&c->scratch, off));
+    uint8_t *base = static_cast<uint8_t *>(c->scratch);
+    for (size_t i = 0; i < parts.size(); ++i) *parts[i].dst = parts[i].bytes ? base + at[i] : nullptr;
+    AMOE_CUDA(c, cudaMemset(c->arrivals, 0, (size_t)c->nchunk_max * 4));
+    return AMOE_OK;
+}
+
+cudaEvent_t pool_event(amoe_ctx *c) {
+    if (!c->event_pool.empty()) {
+        cudaEvent_t e = c->event_pool.back();
+        c->event_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+// Stage timer for one forward: records an event before the first stage and
+// after every stage on the launch stream (profiling only).
+struct StageTimer {
+    amoe_ctx *c;
+    cudaStream_t st;
+    amoe_ctx::PendingTiming t{};
+    StageTimer(amoe_ctx *c_, cudaStream_t st_) : c(c_), st(st_) {
+        if (c->profiling) {
+            t.ev[0] = pool_event(c);
+            t.stage_of[0] = -1;
+            t.n = 1;
+            cudaEventRecord(t.ev[0], st);
+        }
+    }
+    void mark(int stage) {
+        if (!c->profiling || t.n > AMOE_STAGES) return;
+        t.ev[t.n] = pool_event(c);
+        t.stage_of[t.n] = stage;
+        cudaEventRecord(t.ev[t.n], st);
+        ++t.n;
+    }
+    void finish() {
+        if (c->profiling && t.n > 1) {
+            c->pending.push_back(t);
+            c->stats.timed_forwards++;
+        } else if (c->profiling) {
+            c->event_pool.push_back(t.ev[0]);
+        }
+    }
+};
+
+void fold_timings(amoe_ctx *c) {
+    for (auto &t : c->pending) {
+        for (int i = 1; i < t.n; ++i) {
+            float ms = 0.0f;
+            if (cudaEventElapsedTime(&ms, t.ev[i - 1], t.ev[i]) == cudaSuccess)
+                c->stats.stage_ms[t.stage_of[i]] += ms;
+        }
+        for (int i = 0; i < t.n; ++i) c->event_pool.push_back(t.ev[i]);
+    }
+    c->pending.clear();
+}
+
+void release(amoe_ctx *c) {
+    if (!c) return;
+    cudaSetDevice(c->cfg.device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
+    for (auto p : c->layer_dev) if (p) cudaFree(p);
+    for (auto p : c->layer_host) if (p) cudaFreeHost(p);
+    for (auto p : c->slot_dev) if (p) cudaFree(p);
+    for (auto e : c->slot_ready) if (e) cudaEventDestroy(e);
+    for (auto e : c->slot_free) if (e) cudaEventDestroy(e);
+    if (c->scratch) cudaFree(c->scratch);
+    for (auto &t : c->pending)
+        for (int i = 0; i < t.n; ++i) cudaEventDestroy(t.ev[i]);
+    for (auto e : c->event_pool) cudaEventDestroy(e);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
+}
+
+bool streaming(const amoe_ctx *c) { return c->cfg.stream_slots >= 2; }
+
+// Makes `layer` available in a device slot and returns its view; the compute
+// stream `st` is made to wait for the copy.  Streaming mode only.
+int acquire_slot(amoe_ctx *c, int layer, cudaStream_t st, int *slot_out) {
+    const int n = (int)c->slot_dev.size();
+    int slot = -1;
+    for (int i = 0; i < n; ++i)
+        if (c->slot_layer[i] == layer) slot = i;
+    if (slot < 0) {
+        // least recently used slot
+        slot = 0;
+        for (int i = 1; i < n; ++i)
+            if (c->slot_used[i] < c->slot_used[slot]) slot = i;
+        AMOE_CUDA(c, cudaStreamWaitEvent(c->copy_stream, c->slot_free[slot], 0));
+        AMOE_CUDA(c, cudaMemcpyAsync(c->slot_dev[slot], c->layer_host[layer], c->blk.total,
+                                     cudaMemcpyHostToDevice, c->copy_stream));
+        AMOE_CUDA(c, cudaEventRecord(c->slot_ready[slot], c->copy_stream));
+        c->slot_layer[slot] = layer;
+    }
+    c->slot_used[slot] = ++c->tick;
+    if (st) AMOE_CUDA(c, cudaStreamWaitEvent(st, c->slot_ready[slot], 0));
+    *slot_out = slot;
+    return AMOE_OK;
+}
+
+void timer_hook(void *timer, int stage) { static_cast<StageTimer *>(timer)->mark(stage); }
+
+int check_ctx(amoe_ctx *c) {
+    if (!c) return AMOE_ERR_INVALID;
+    cudaError_t e = cudaSetDevice(c->cfg.device);
+    if (e != cudaSuccess) return cuda_fail(c, e, "cudaSetDevice");
+    return AMOE_OK;
+}
+
+int use_tensor_path(const amoe_ctx *c, int T) {
+    if (c->cfg.path == AMOE_PATH_GEMV) return 0;
+    if (c->cfg.path == AMOE_PATH_TENSOR) return 1;
+    // AUTO: the GEMV streams each selected weight tile once per 32 tokens of
+    // an expert; past ~32 tokens per expert the tcgen05 GEMM wins.
+    const long long pairs_per_expert = (long long)T * c->d.k / c->d.E;
+    return tc_supported() && pairs_per_expert >= 32;
+}
+
+}  // namespace
+
+extern "C" {
+
+int amoe_abi_version(void) { return AMOE_ABI_VERSION; }
+
+const char *amoe_last_error(const amoe_ctx *ctx) {
+    return ctx ? ctx->err.c_str() : g_create_error.c_str();
+}
+
+int amoe_create(const amoe_config *cfg, amoe_ctx **out) {
+    g_create_error.clear();
+    if (!out) {
+        g_create_error = "out must not be NULL";
+        return AMOE_ERR_INVALID;
+    }
+    *out = nullptr;
+    std::string v = validate(cfg);
+    if (!v.empty()) {
+        g_create_error = v;
+        return AMOE_ERR_INVALID;
+    }
+    amoe_ctx *c = new (std::nothrow) amoe_ctx();
+    if (!c) {
+        g_create_error = "out of host memory";
+        return AMOE_ERR_NOMEM;
+    }
+    c->cfg = *cfg;
+    c->cfg.nccl_id = nullptr;
+    c->d = Dims{cfg->hidden, cfg->intermediate, cfg->experts, cfg->top_k, cfg->rms_eps};
+    c->blk = layer_block(c->d);
+    int rc = AMOE_OK;
+    do {
+        cudaError_t e = cudaSetDevice(cfg->device);
+        if (e != cudaSuccess) { rc = cuda_fail(c, e, "cudaSetDevice"); break; }
+        e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+        if (e != cudaSuccess) { rc = cuda_fail(c, e, "cudaStreamCreate"); break; }
+        e = cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking);
+        if (e != cudaSuccess) { rc = cuda_fail(c, e, "cudaStreamCreate"); break; }
+        c->layer_dev.assign(cfg->layers, nullptr);
+        c->layer_host.assign(cfg->layers, nullptr);
+        c->uploaded.assign(cfg->layers, false);
+        if (cfg->stream_slots >= 2) {
+            for (int i = 0; i < cfg->stream_slots && rc == AMOE_OK; ++i) {
+                uint8_t *p = nullptr;
+                e = cudaMalloc(&p, c->blk.total);
+                if (e != cudaSuccess) { rc = cuda_fail(c, e, "cudaMalloc(stream slot)"); break; }
+                c->slot_dev.push_back(p);
+                c->slot_layer.push_back(-1);
+                c->slot_used.push_back(0);
+                cudaEvent_t a, b;
+                cudaEventCreateWithFlags(&a, cudaEventDisableTiming);
+                cudaEventCreateWithFlags(&b, cudaEventDisableTiming);
+                c->slot_ready.push_back(a);
+                c->slot_free.push_back(b);
+                cudaEventRecord(b, c->stream);
+            }
+            if (rc != AMOE_OK) break;
+        }
+        rc = alloc_scratch(c);
+    } while (0);
+    if (rc != AMOE_OK) {
+        g_create_error = c->err;
+        release(c);
+        delete c;
+        return rc;
+    }
+    *out = c;
+    return AMOE_OK;
+}
+
+void amoe_destroy(amoe_ctx *ctx) {
+    if (!ctx) return;
+    release(ctx);
+    delete ctx;
+}
+
+int amoe_upload_layer(amoe_ctx *c, int32_t layer, const float *norm_gain, const float *router_w,
+                      const float *router_b, const uint8_t *gate_up, const float *gate_up_b,
+                      const uint8_t *down, const float *down_b) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (layer < 0 || layer >= c->cfg.layers)
+        return fail(c, AMOE_ERR_INVALID, "layer " + std::to_string(layer) + " outside [0, " +
+                                             std::to_string(c->cfg.layers) + ")");
+    if (!norm_gain || !router_w || !router_b || !gate_up || !gate_up_b || !down || !down_b)
+        return fail(c, AMOE_ERR_INVALID, "layer tensors must not be NULL");
+    const Dims &d = c->d;
+    const size_t H = d.H, I = d.I, E = d.E;
+    const size_t gu_bytes = E * 2 * I * (H / 32) * 17, dn_bytes = E * H * (I / 32) * 17;
+    // Device-format block: built in a temporary device buffer, then kept there
+    // (resident) or copied to pinned host memory (streaming).
+    uint8_t *blockp = nullptr, *staging = nullptr;
+    float *router_tmp = nullptr;
+    const size_t stage_bytes = gu_bytes > dn_bytes ? gu_bytes : dn_bytes;
+    auto cleanup = [&]() {
+        if (staging) cudaFree(staging);
+        if (router_tmp) cudaFree(router_tmp);
+        if (streaming(c) && blockp) cudaFree(blockp);
+    };
+    cudaError_t e;
+#define UP_CUDA(call)                                       \
+    do {                                                    \
+        e = (call);                                         \
+        if (e != cudaSuccess) {                             \
+            cleanup();                                      \
+            return cuda_fail(c, e, #call);                  \
+        }                                                   \
+    } while (0)
+    if (!streaming(c)) {
+        if (!c->layer_dev[layer]) {
+            e = cudaMalloc(&c->layer_dev[layer], c->blk.total);
+            if (e != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(layer)");
+        }
+        blockp = c->layer_dev[layer];
+    } else {
+        if (!c->layer_host[layer]) {
+            e = cudaHostAlloc(&c->layer_host[layer], c->blk.total, cudaHostAllocDefault);
+            if (e != cudaSuccess) return cuda_fail(c, e, "cudaHostAlloc(layer)");
+        }
+        UP_CUDA(cudaMalloc(&blockp, c->blk.total));
+    }
+    UP_CUDA(cudaMalloc(&staging, stage_bytes));
+    UP_CUDA(cudaMalloc(&router_tmp, E * H * 4));
+    const LayerDev L = layer_view(blockp, c->blk);
+    cudaStream_t st = c->stream;
+    UP_CUDA(cudaMemcpyAsync(L.norm_gain, norm_gain, H * 4, cudaMemcpyHostToDevice, st));
+    UP_CUDA(cudaMemcpyAsync(router_tmp, router_w, E * H * 4, cudaMemcpyHostToDevice, st));
+    UP_CUDA(launch_transpose_router(router_tmp, (int)E, (int)H, L.router_wt, st));
+    UP_CUDA(cudaMemcpyAsync(L.router_b, router_b, E * 4, cudaMemcpyHostToDevice, st));
+    UP_CUDA(cudaMemcpyAsync(L.gu_b, gate_up_b, E * 2 * I * 4, cudaMemcpyHostToDevice, st));
+    UP_CUDA(cudaMemcpyAsync(L.dn_b, down_b, E * H * 4, cudaMemcpyHostToDevice, st));
+    UP_CUDA(cudaMemcpyAsync(staging, gate_up, gu_bytes, cudaMemcpyHostToDevice, st));
+    UP_CUDA(launch_repack(staging, (int)E, (int)(2 * I), (int)H, true, L.gu_q, L.gu_s, st));
+    UP_CUDA(cudaStreamSynchronize(st));  // staging is reused for down
+    UP_CUDA(cudaMemcpyAsync(staging, down, dn_bytes, cudaMemcpyHostToDevice, st));
+    UP_CUDA(launch_repack(staging, (int)E, (int)H, (int)I, false, L.dn_q, L.dn_s, st));
+    if (streaming(c)) {
+        UP_CUDA(cudaMemcpyAsync(c->layer_host[layer], blockp, c->blk.total, cudaMemcpyDeviceToHost, st));
+        // a slot holding a stale copy of this layer must be refilled
+        for (size_t i = 0; i < c->slot_layer.size(); ++i)
+            if (c->slot_layer[i] == layer) c->slot_layer[i] = -1;
+    }
+    UP_CUDA(cudaStreamSynchronize(st));
+#undef UP_CUDA
+    cleanup();
+    c->uploaded[layer] = true;
+    return AMOE_OK;
+}
+
+int amoe_prefetch_layer(amoe_ctx *c, int32_t layer) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (!streaming(c)) return fail(c, AMOE_ERR_STATE, "prefetch needs stream_slots >= 2");
+    if (layer < 0 || layer >= c->cfg.layers || !c->uploaded[layer])
+        return fail(c, AMOE_ERR_STATE, "layer " + std::to_string(layer) + " is not uploaded");
+    int slot;
+    return acquire_slot(c, layer, nullptr, &slot);
+}
+
+int amoe_forward_device(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, float *out,
+                        int32_t *topk_idx, float *topk_w, void *stream) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (layer < 0 || layer >= c->cfg.layers || !c->uploaded[layer])
+        return fail(c, AMOE_ERR_STATE, "layer " + std::to_string(layer) + " is not uploaded");
+    if (T <= 0) return fail(c, AMOE_ERR_INVALID, "gptoss: prefill sequence length must be positive");
+    if (T > c->max_tokens)
+        return fail(c, AMOE_ERR_INVALID, "T " + std::to_string(T) + " exceeds max_tokens " +
+                                             std::to_string(c->max_tokens));
+    if (!residual || !out) return fail(c, AMOE_ERR_INVALID, "residual and out must not be NULL");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    LayerDev L;
+    int slot = -1;
+    if (streaming(c)) {
+        rc = acquire_slot(c, layer, st, &slot);
+        if (rc) return rc;
+        L = layer_view(c->slot_dev[slot], c->blk);
+    } else {
+        L = layer_view(c->layer_dev[layer], c->blk);
+    }
+    const Dims &d = c->d;
+    StageTimer timer(c, st);
+    AMOE_CUDA(c, launch_route_impl(d, L, residual, T, c->r, c->partial, c->arrivals, st, &timer_hook, &timer));
+    c->stats.launches += 2;
+    const bool tc = use_tensor_path(c, T);
+    if (tc) {
+        int n = 0;
+        AMOE_CUDA(c, launch_tc_forward(d, L, c->r, T, c->act_hi, c->act_lo, c->y, c->tc_scratch, st,
+                                       &timer_hook, &timer, &n));
+        c->stats.launches += n;
+    } else {
+        AMOE_CUDA(c, launch_gemv_gate_up(d, L, c->r, T, c->act_hi, c->act_lo, st));
+        timer.mark(2);
+        AMOE_CUDA(c, launch_gemv_down(d, L, c->r, T, c->act_hi, c->act_lo, c->y, st));
+        timer.mark(3);
+        c->stats.launches += 2;
+    }
+    AMOE_CUDA(c, launch_combine(d, residual, c->r, c->y, T, out, st));
+    timer.mark(4);
+    timer.finish();
+    c->stats.launches += 1;
+    c->stats.forwards += 1;
+    c->stats.last_path = tc ? AMOE_PATH_TENSOR : AMOE_PATH_GEMV;
+    if (slot >= 0) AMOE_CUDA(c, cudaEventRecord(c->slot_free[slot], st));
+    if (topk_idx)
+        AMOE_CUDA(c, cudaMemcpyAsync(topk_idx, c->r.topk_idx, (size_t)T * d.k * 4,
+                                     cudaMemcpyDeviceToDevice, st));
+    if (topk_w)
+        AMOE_CUDA(c, cudaMemcpyAsync(topk_w, c->r.topk_w, (size_t)T * d.k * 4,
+                                     cudaMemcpyDeviceToDevice, st));
+    c->last_T = T;
+    return AMOE_OK;
+}
+
+int amoe_forward(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, float *out,
+                 int32_t *topk_idx, float *topk_w) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (T <= 0) return fail(c, AMOE_ERR_INVALID, "gptoss: prefill sequence length must be positive");
+    if (T > c->max_tokens)
+        return fail(c, AMOE_ERR_INVALID, "T " + std::to_string(T) + " exceeds max_tokens " +
+                                             std::to_string(c->max_tokens));
+    if (!residual || !out) return fail(c, AMOE_ERR_INVALID, "residual and out must not be NULL");
+    const Dims &d = c->d;
+    cudaStream_t st = c->stream;
+    AMOE_CUDA(c, cudaMemcpyAsync(c->io_in, residual, (size_t)T * d.H * 4, cudaMemcpyHostToDevice, st));
+    rc = amoe_forward_device(c, layer, c->io_in, T, c->io_out, nullptr, nullptr, st);
+    if (rc) return rc;
+    AMOE_CUDA(c, cudaMemcpyAsync(out, c->io_out, (size_t)T * d.H * 4, cudaMemcpyDeviceToHost, st));
+    if (topk_idx)
+        AMOE_CUDA(c, cudaMemcpyAsync(topk_idx, c->r.topk_idx, (size_t)T * d.k * 4,
+                                     cudaMemcpyDeviceToHost, st));
+    if (topk_w)
+        AMOE_CUDA(c, cudaMemcpyAsync(topk_w, c->r.topk_w, (size_t)T * d.k * 4,
+                                     cudaMemcpyDeviceToHost, st));
+    AMOE_CUDA(c, cudaStreamSynchronize(st));
+    return AMOE_OK;
+}
+
+int amoe_synchronize(amoe_ctx *c) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    AMOE_CUDA(c, cudaStreamSynchronize(c->stream));
+    AMOE_CUDA(c, cudaStreamSynchronize(c->copy_stream));
+    return AMOE_OK;
+}
+
+int amoe_last_routing(amoe_ctx *c, float *logits, int32_t *perm_pair, int32_t *counts,
+                      int32_t *offsets) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (c->last_T <= 0) return fail(c, AMOE_ERR_STATE, "no forward has run yet");
+    const Dims &d = c->d;
+    const size_t T = c->last_T;
+    AMOE_CUDA(c, cudaStreamSynchronize(c->stream));
+    if (logits) AMOE_CUDA(c, cudaMemcpy(logits, c->r.logits, T * d.E * 4, cudaMemcpyDeviceToHost));
+    if (perm_pair)
+        AMOE_CUDA(c, cudaMemcpy(perm_pair, c->r.perm_pair, T * d.k * 4, cudaMemcpyDeviceToHost));
+    if (counts) AMOE_CUDA(c, cudaMemcpy(counts, c->r.counts, (size_t)d.E * 4, cudaMemcpyDeviceToHost));
+    if (offsets)
+        AMOE_CUDA(c, cudaMemcpy(offsets, c->r.offsets, (size_t)(d.E + 1) * 4, cudaMemcpyDeviceToHost));
+    return AMOE_OK;
+}
+
+int amoe_set_profiling(amoe_ctx *c, int32_t on) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    c->profiling = on != 0;
+    return AMOE_OK;
+}
+
+int amoe_get_stats(amoe_ctx *c, amoe_stats *out, int32_t reset) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (!out) return fail(c, AMOE_ERR_INVALID, "stats must not be NULL");
+    AMOE_CUDA(c, cudaStreamSynchronize(c->stream));
+    AMOE_CUDA(c, cudaDeviceSynchronize());
+    fold_timings(c);
+    *out = c->stats;
+    if (reset) {
+        const int32_t last = c->stats.last_path;
+        c->stats = amoe_stats{};
+        c->stats.last_path = last;
+    }
+    return AMOE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,240 @@
+// gemv.cu -- K7: expert GEMV for small per-expert token counts (decode).
+//
+// Computes, for every selected (token, expert) pair,
+//   gate_up = x . W_gu^T + b_gu  -> clamped SwiGLU (fused)   (layer.go:139-148, 175;
+//                                                              primitives.go:138-149)
+//   y       = act . W_dn^T + b_dn                             (layer.go:179-187)
+// directly from the tiled MXFP4 planes (no dequantised copy in memory).
+//
+// One warp owns a 16-row weight tile and streams it once over K; the per-
+// expert tokens ride along as the n=8 columns of mma.sync.m16n8k16 (up to
+// 8*NG tokens per pass).  Each MXFP4 byte becomes an f16x2 A-fragment register
+// with one cvt.rn.f16x2.e2m1x2 (E2M1 values are exact in fp16); the E8M0 block
+// scale is applied to the f32 partial of each 32-value block, so the scale
+// never has to fit fp16's range.  Activations enter as an fp16 hi + lo split
+// (x ~= hi + lo to ~2^-22 relative), two MMAs per k-step.  The kernel is
+// HBM-bound: its work per weight byte is one cvt and a quarter MMA.
+#include "amoe_internal.cuh"
+
+namespace amoe {
+
+namespace {
+
+constexpr int kGemvWarps = 4;
+
+struct GemvParams {
+    const uint8_t *q;      // tiled nibbles
+    const uint8_t *s;      // tiled scales
+    const float *bias;     // [E][R] (GGUF row order)
+    const __half *x_hi;    // activation rows [*][K]
+    const __half *x_lo;
+    const int32_t *perm_pair;
+    const int32_t *offsets;
+    const int32_t *active;
+    int R, K, E, k;
+    // outputs
+    __half *act_hi, *act_lo;  // gate_up: [P][R/2]
+    float *y;                 // down:    [P][R]
+};
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t ldg_nc_u32(const void *p) {
+    uint32_t r;
+    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(r) : "l"(p));
+    return r;
+}
+
+// GPT-OSS clamped SwiGLU in f32 with Go's math.Min/Max NaN semantics
+// (primitives.go:144-146): NaN propagates.
+__device__ __forceinline__ float swiglu(float gate, float up) {
+    float g = isnan(gate) ? gate : fminf(gate, 7.0f);
+    float u = isnan(up) ? up : fminf(fmaxf(up, -7.0f), 7.0f);
+    return g / (1.0f + expf(-1.702f * g)) * (u + 1.0f);
+}
+
+template <bool GATE_UP, int NG>
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
+    const int slot = blockIdx.y;
+    const int n_active = p.active[p.E];
+    if (slot >= n_active) return;
+    const int e = p.active[slot];
+    const int base = p.offsets[e];
+    const int m_e = p.offsets[e + 1] - base;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nrt = p.R / kTileRows;
+    const int rt = blockIdx.x * kGemvWarps + warp;
+    if (rt >= nrt) return;
+    const int g = lane >> 2, c = lane & 3;
+    const int nkt = p.K / kTileK;
+    const uint8_t *qt = p.q + ((size_t)e * nrt + rt) * nkt * kTileQBytes + lane * 16;
+    const uint8_t *st = p.s + ((size_t)e * nrt + rt) * nkt * kTileSBytes + 4 * g;
+
+    for (int tok0 = 0; tok0 < m_e; tok0 += 8 * NG) {
+        const __half *xh[NG];
+        const __half *xl[NG];
+        bool valid[NG];
+        int ng_live = 0;
+#pragma unroll
+        for (int n = 0; n < NG; ++n) {
+            const int tok = tok0 + 8 * n + g;
+            valid[n] = tok < m_e;
+            int row = 0;
+            if (valid[n]) row = GATE_UP ? p.perm_pair[base + tok] / p.k : base + tok;
+            xh[n] = p.x_hi + (size_t)row * p.K + 8 * c;
+            xl[n] = p.x_lo + (size_t)row * p.K + 8 * c;
+            if (tok0 + 8 * n < m_e) ng_live = n + 1;
+        }
+        float acc[NG][4];
+#pragma unroll
+        for (int n = 0; n < NG; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[n][i] = 0.0f;
+
+        uint4 qv = ldg_nc_v4(qt);
+        uint32_t sv = ldg_nc_u32(st);
+        for (int kt = 0; kt < nkt; ++kt) {
+            uint4 qn = qv;
+            uint32_t sn = sv;
+            if (kt + 1 < nkt) {  // one k-tile of weights in flight ahead
+                qn = ldg_nc_v4(qt + (size_t)(kt + 1) * kTileQBytes);
+                sn = ldg_nc_u32(st + (size_t)(kt + 1) * kTileSBytes);
+            }
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+                const uint32_t wg = b ? qv.z : qv.x;   // tile row g
+                const uint32_t wg8 = b ? qv.w : qv.y;  // tile row g+8
+                const uint32_t s0a0 = e2m1x2_to_f16x2(wg & 0xff);
+                const uint32_t s0a1 = e2m1x2_to_f16x2(wg8 & 0xff);
+                const uint32_t s0a2 = e2m1x2_to_f16x2((wg >> 8) & 0xff);
+                const uint32_t s0a3 = e2m1x2_to_f16x2((wg8 >> 8) & 0xff);
+                const uint32_t s1a0 = e2m1x2_to_f16x2((wg >> 16) & 0xff);
+                const uint32_t s1a1 = e2m1x2_to_f16x2((wg8 >> 16) & 0xff);
+                const uint32_t s1a2 = e2m1x2_to_f16x2(wg >> 24);
+                const uint32_t s1a3 = e2m1x2_to_f16x2(wg8 >> 24);
+                const float sc_g = e8m0_to_float((sv >> (8 * b)) & 0xff);
+                const float sc_g8 = e8m0_to_float((sv >> (8 * (2 + b))) & 0xff);
+#pragma unroll
+                for (int n = 0; n < NG; ++n) {
+                    if (n >= ng_live) break;
+                    uint4 h = make_uint4(0, 0, 0, 0), l = make_uint4(0, 0, 0, 0);
+                    if (valid[n]) {
+                        h = *reinterpret_cast<const uint4 *>(xh[n] + kt * kTileK + b * 32);
+                        l = *reinterpret_cast<const uint4 *>(xl[n] + kt * kTileK + b * 32);
+                    }
+                    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    mma16816(d, s0a0, s0a1, s0a2, s0a3, h.x, h.y);
+                    mma16816(d, s0a0, s0a1, s0a2, s0a3, l.x, l.y);
+                    mma16816(d, s1a0, s1a1, s1a2, s1a3, h.z, h.w);
+                    mma16816(d, s1a0, s1a1, s1a2, s1a3, l.z, l.w);
+                    acc[n][0] = fmaf(d[0], sc_g, acc[n][0]);
+                    acc[n][1] = fmaf(d[1], sc_g, acc[n][1]);
+                    acc[n][2] = fmaf(d[2], sc_g8, acc[n][2]);
+                    acc[n][3] = fmaf(d[3], sc_g8, acc[n][3]);
+                }
+            }
+            qv = qn;
+            sv = sn;
+        }
+
+        // epilogue: thread holds rows (g, g+8) for tokens 2c, 2c+1 of each n-group
+#pragma unroll
+        for (int n = 0; n < NG; ++n) {
+            if (n >= ng_live) break;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int tok = tok0 + 8 * n + 2 * c + j;
+                if (tok >= m_e) continue;
+                const int pos = base + tok;
+                if (GATE_UP) {
+                    const int pr = 8 * rt + g;  // SwiGLU pair index
+                    const float gate = acc[n][j] + p.bias[(size_t)e * p.R + 2 * pr];
+                    const float up = acc[n][2 + j] + p.bias[(size_t)e * p.R + 2 * pr + 1];
+                    const float a = swiglu(gate, up);
+                    const __half hi = __float2half_rn(a);
+                    const __half lo = __float2half_rn(a - __half2float(hi));
+                    p.act_hi[(size_t)pos * (p.R / 2) + pr] = hi;
+                    p.act_lo[(size_t)pos * (p.R / 2) + pr] = lo;
+                } else {
+                    const int h = kTileRows * rt + g;
+                    p.y[(size_t)pos * p.R + h] = acc[n][j] + p.bias[(size_t)e * p.R + h];
+                    p.y[(size_t)pos * p.R + h + 8] = acc[n][2 + j] + p.bias[(size_t)e * p.R + h + 8];
+                }
+            }
+        }
+    }
+}
+
+template <bool GATE_UP>
+cudaError_t launch(const GemvParams &p, int T, int max_active, cudaStream_t st) {
+    const int nrt = p.R / kTileRows;
+    dim3 grid((nrt + kGemvWarps - 1) / kGemvWarps, max_active);
+    if (T <= 8)
+        gemv_kernel<GATE_UP, 1><<<grid, kGemvWarps * 32, 0, st>>>(p);
+    else if (T <= 16)
+        gemv_kernel<GATE_UP, 2><<<grid, kGemvWarps * 32, 0, st>>>(p);
+    else
+        gemv_kernel<GATE_UP, 4><<<grid, kGemvWarps * 32, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gemv_gate_up(const Dims &d, const LayerDev &L, const RouteOut &r, int T,
+                                __half *act_hi, __half *act_lo, cudaStream_t st) {
+    GemvParams p{};
+    p.q = L.gu_q;
+    p.s = L.gu_s;
+    p.bias = L.gu_b;
+    p.x_hi = r.x_hi;
+    p.x_lo = r.x_lo;
+    p.perm_pair = r.perm_pair;
+    p.offsets = r.offsets;
+    p.active = r.active;
+    p.R = 2 * d.I;
+    p.K = d.H;
+    p.E = d.E;
+    p.k = d.k;
+    p.act_hi = act_hi;
+    p.act_lo = act_lo;
+    const int max_active = T * d.k < d.E ? T * d.k : d.E;
+    return launch<true>(p, T, max_active, st);
+}
+
+cudaError_t launch_gemv_down(const Dims &d, const LayerDev &L, const RouteOut &r, int T,
+                             const __half *act_hi, const __half *act_lo, float *y,
+                             cudaStream_t st) {
+    GemvParams p{};
+    p.q = L.dn_q;
+    p.s = L.dn_s;
+    p.bias = L.dn_b;
+    p.x_hi = act_hi;
+    p.x_lo = act_lo;
+    p.perm_pair = r.perm_pair;
+    p.offsets = r.offsets;
+    p.active = r.active;
+    p.R = d.H;
+    p.K = d.I;
+    p.E = d.E;
+    p.k = d.k;
+    p.y = y;
+    const int max_active = T * d.k < d.E ? T * d.k : d.E;
+    return launch<false>(p, T, max_active, st);
+}
+
+}  // namespace amoe

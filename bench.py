@@ -1,0 +1,316 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 GPT-OSS MoE block (one JSON line on rank 0).
+
+Workload (default): the 20B-shaped block at prefill -- 4096 tokens, hidden
+2880, 32 experts, top-4, intermediate 2880, MXFP4 experts, Zipf(1.1)-skewed
+router bias (busiest expert ~3x mean load), seed 1; synthetic seeded data.
+A "step" is one forward of the block over those 4096 tokens.
+
+  value     tokens/s over all ranks, inputs resident in HBM, device-timed
+            (CUDA events around each step; L2 flushed between steps)
+  e2e       the same through the C ABI's host-buffer call (amoe_forward) with
+            pinned host input/output: H2D + block + D2H per step
+  roofline  dominant kernel, from the library's per-stage CUDA events taken
+            inside the timed region
+  N > 1     independent replicas, one per GPU (tokens are independent: weak
+            scaling, no collective on the data path)
+
+--impl reference times the reference's CPU path (the C restatement in
+oracle/, faithful mode: every (token, expert) re-decodes the MXFP4 expert as
+readExpert does) on a bounded token sample with all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from airllm_b200 import workloads as W  # noqa: E402
+
+METRIC = "MoE-block tokens/s per B200 (prefill T=4096, GPT-OSS-20B shape)"
+UNIT = "tokens/s"
+FLOP_PER_PAIR = 2 * 2880 * (2 * 2880 + 2880)  # 49,766,400
+MEASURED_PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
+TRAFFIC_FILE = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+def peaks():
+    try:
+        p = json.load(open(MEASURED_PEAKS))
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained"), "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def workload_desc(config: int, T: int) -> dict:
+    shape = W.CONFIG_SHAPE[config]
+    names = {0: "gptoss20b-moe-decode", 1: "gptoss20b-moe-prefill-zipf", 3: "gptoss120b-moe"}
+    return {"workload": f"{names.get(config, 'moe')} T={T} H={shape.hidden} I={shape.intermediate} "
+                        f"E={shape.experts} k={shape.top_k} mxfp4",
+            "config_index": config, "tokens": T, "hidden": shape.hidden, "intermediate": shape.intermediate,
+            "experts": shape.experts, "top_k": shape.top_k, "weights": "MXFP4 (E2M1 + E8M0 per 32)",
+            "l2": "flushed (256 MiB write) before every timed step"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks during the timed region (start before, stop after)."""
+
+    def __init__(self, device: int):
+        self.path = tempfile.mktemp(suffix=".csv")
+        self.proc = None
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(device)],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_reference_run(layer, x, sample: int, threads: int):
+    """One bounded sample of the reference CPU path; returns (seconds, tokens)."""
+    import oracle  # the CPU restatement of the reference (baseline leg only)
+
+    t0 = time.perf_counter()
+    oracle.moe_block(layer, x[:sample], faithful=True, threads=threads)
+    return time.perf_counter() - t0, sample
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    layer = W.config_layer(args.config)
+    T = W.CONFIG_TOKENS[args.config]
+    x = W.config_tokens(args.config)
+    sample = min(T, max(8, 2 * threads))
+    for _ in range(args.warmup):
+        cpu_reference_run(layer, x, min(sample, threads), threads)
+    times = []
+    for _ in range(args.steps):
+        s, n = cpu_reference_run(layer, x, sample, threads)
+        times.append(s)
+    sec = statistics.mean(times)
+    value = sample / sec
+    desc = f"{sample} of {T} tokens per step (oracle restatement, faithful MXFP4 re-decode per (token, expert))"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64-accumulate (reference CPU path)",
+        "data": "synthetic (seeded)", "config": workload_desc(args.config, T),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def algorithmic(config: int, T: int, layer, idx, stage: str):
+    """Algorithmic FLOPs and bytes of one launch of `stage` for this routing."""
+    H, I, E, k = layer["hidden"], layer["intermediate"], layer["experts"], layer["top_k"]
+    pairs = T * k
+    active = len(np.unique(idx))
+    if stage == "gate_up":
+        flops = 2.0 * pairs * 2 * I * H
+        bytes_ = active * (2 * I * H // 2 + 2 * I * H // 32 + 2 * I * 4) + T * H * 4 + pairs * I * 4
+    else:  # down
+        flops = 2.0 * pairs * H * I
+        bytes_ = active * (H * I // 2 + H * I // 32 + H * 4) + pairs * I * 4 + pairs * H * 4
+    return flops, bytes_
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--path", type=int, default=0, help="0 auto, 1 GEMV, 2 tcgen05")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    from airllm_b200 import moe
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    cfg = args.config
+    layer = W.config_layer(cfg)
+    T = W.CONFIG_TOKENS[cfg]
+    x = W.config_tokens(cfg)
+    blk = moe.MoEBlock.for_layer(layer, max_tokens=T, device=local, path=args.path)
+    blk.upload_layer(0, layer)
+
+    stream = torch.cuda.current_stream()
+    xd = torch.from_numpy(x).cuda()
+    od = torch.empty_like(xd)
+    idd = torch.empty((T, layer["top_k"]), dtype=torch.int32, device="cuda")
+    wd = torch.empty((T, layer["top_k"]), dtype=torch.float32, device="cuda")
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+
+    for _ in range(args.warmup):
+        blk.forward_device(xd, od, topk_idx=idd, topk_w=wd, stream=stream)
+    torch.cuda.synchronize()
+    blk.stats(reset=True)
+
+    # ---- device-timed region ------------------------------------------------
+    blk.set_profiling(True)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    torch.cuda.synchronize()
+    barrier()
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        starts[i].record(stream)
+        blk.forward_device(xd, od, topk_idx=idd, topk_w=wd, stream=stream)
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    blk.set_profiling(False)
+    st = blk.stats(reset=True)
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    ms = max_over_ranks(statistics.mean(step_ms))
+    value = world * T / (ms / 1e3)
+
+    # ---- end-to-end through the host-buffer C-ABI call ----------------------
+    xh = torch.from_numpy(x).pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    for _ in range(2):
+        blk.forward_into(xh.numpy(), oh.numpy())
+    e2e_s = []
+    barrier()
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        blk.forward_into(xh.numpy(), oh.numpy())
+        e2e_s.append(time.perf_counter() - t0)
+    barrier()
+    e2e_ms = max_over_ranks(statistics.mean(e2e_s) * 1e3)
+    e2e = {"value": world * T / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": T * layer["hidden"] * 4,
+           "d2h_bytes_per_step": T * layer["hidden"] * 4, "ms_per_step": e2e_ms,
+           "call": "amoe_forward (pinned host in/out)"}
+
+    # ---- roofline of the dominant kernel --------------------------------------
+    pk = peaks()
+    idx_host = idd.cpu().numpy()
+    n = max(st["timed_forwards"], 1)
+    stage_avg = {k: v / n for k, v in st["stage_ms"].items() if v > 0}
+    dom = max(("gate_up", "down"), key=lambda s: stage_avg.get(s, 0.0))
+    flops, bytes_ = algorithmic(cfg, T, layer, idx_host, dom)
+    dom_ms = stage_avg.get(dom, float("nan"))
+    pairs_per_expert = T * layer["top_k"] / layer["experts"]
+    kernel_name = {1: "gemv_kernel (mma.sync MXFP4)", 2: "tc_gemm (tcgen05)"}[st["last_path"] or 1]
+    traffic = None
+    try:
+        traffic = json.load(open(TRAFFIC_FILE)).get(f"{dom}:{cfg}")
+    except Exception:
+        pass
+    if pairs_per_expert >= 32:
+        achieved = flops / (dom_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": achieved / pk["bf16_tflops"], "traffic": traffic,
+                "kernel": f"{dom} {kernel_name}", "algorithmic_flop_per_launch": flops,
+                "launch_ms": dom_ms, "peak_source": f"{pk['source']} bf16 dense (burst)",
+                "frac_of_fp4_dense_nominal_9pflops": achieved / 9000.0}
+    else:
+        achieved = bytes_ / (dom_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / pk["hbm_gbs"], "traffic": traffic, "kernel": f"{dom} {kernel_name}",
+                "algorithmic_bytes_per_launch": bytes_, "launch_ms": dom_ms,
+                "peak_source": f"{pk['source']} HBM copy"}
+
+    # ---- CPU baseline (rank 0, N=1 only) --------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        sample = min(T, max(8, 2 * threads))
+        sec, ntok = cpu_reference_run(layer, x, sample, threads)
+        cpu = {"value": ntok / sec, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{ntok} of {T} tokens, oracle faithful mode (MXFP4 re-decode per (token, expert))"}
+
+    launches_per_step = st["launches"] / max(st["forwards"], 1)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "mxfp4 x fp16-hi/lo -> f32 (router f64)",
+        "data": "synthetic (seeded MXFP4 weights, N(0,1) tokens)",
+        "config": dict(workload_desc(cfg, T), parallelism=f"replicas x{world}"),
+        "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": int(st["launches"]), "gpu_launches_per_step": launches_per_step,
+        "stage_ms_per_step": stage_avg, "clocks": clk,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    blk.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

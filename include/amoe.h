@@ -1,0 +1,156 @@
+/*
+ * amoe.h -- C ABI of the B200 GPT-OSS mixture-of-experts block.
+ *
+ * This is the drop-in boundary for the MoE half of the reference's
+ * DecoderLayer.forward (internal/model/gptoss/layer.go:94-123 plus
+ * forwardExpert, layer.go:126-188).  A Go cgo shim binds these entry points
+ * (see INTEGRATION.md); plain pointers and sizes only, no C++ or torch types.
+ *
+ * Conventions
+ *  - Every entry point returns AMOE_OK (0) or a negative AMOE_ERR_* code and
+ *    never aborts; amoe_last_error() describes the last failure.
+ *  - Host pointers are only read/written during the call (cgo forbids C from
+ *    retaining Go pointers); the context copies what it keeps.
+ *  - A context is thread-compatible, not thread-safe (the reference serialises
+ *    generation with Runtime.mu, runtime.go:108-109).  Each call makes the
+ *    context's device current, because cgo calls may land on any OS thread.
+ *  - Shapes: hidden and intermediate must be multiples of 64 (GPT-OSS: 2880).
+ */
+#ifndef AMOE_H
+#define AMOE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AMOE_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define AMOE_API __attribute__((visibility("default")))
+#else
+#define AMOE_API
+#endif
+
+enum {
+    AMOE_OK = 0,
+    AMOE_ERR_INVALID = -1, /* bad argument or shape (mirrors the reference's length checks) */
+    AMOE_ERR_CUDA = -2,    /* a CUDA runtime call failed */
+    AMOE_ERR_NCCL = -3,    /* an NCCL call failed (expert-parallel mode) */
+    AMOE_ERR_TIMEOUT = -4, /* a bounded wait gave up */
+    AMOE_ERR_STATE = -5,   /* e.g. layer not uploaded, wrong mode */
+    AMOE_ERR_NOMEM = -6    /* device or pinned-host allocation failed */
+};
+
+/* Expert-GEMM implementation selector (amoe_config.path). */
+enum {
+    AMOE_PATH_AUTO = 0,   /* GEMV for small token counts, tcgen05 grouped GEMM otherwise */
+    AMOE_PATH_GEMV = 1,   /* always the MXFP4 GEMV kernels */
+    AMOE_PATH_TENSOR = 2  /* always the tcgen05 grouped GEMM */
+};
+
+typedef struct amoe_ctx amoe_ctx;
+
+typedef struct amoe_config {
+    int32_t hidden;          /* H (GPT-OSS gptoss.embedding_length) */
+    int32_t intermediate;    /* I (gptoss.expert_feed_forward_length) */
+    int32_t experts;         /* E (gptoss.expert_count), 1..256 */
+    int32_t top_k;           /* k (gptoss.expert_used_count), 1..min(E, 32) */
+    int32_t layers;          /* number of layer slots (gptoss.block_count) */
+    float rms_eps;           /* gptoss.attention.layer_norm_rms_epsilon, > 0 */
+    float swiglu_alpha;      /* must be 1.702: hard-coded in primitives.go:146 */
+    float swiglu_limit;      /* must be 7: hard-coded in primitives.go:144-145 */
+    int32_t max_tokens;      /* largest T passed to one forward call (sizes scratch) */
+    int32_t device;          /* CUDA device ordinal */
+    int32_t stream_slots;    /* 0: every layer resident in HBM.  n >= 2: weights live in
+                                pinned host memory, n device slots are filled on a copy stream */
+    int32_t ep_size;         /* expert-parallel group size; 1 = single GPU */
+    int32_t ep_rank;         /* this process's rank in the expert-parallel group */
+    const void *nccl_id;     /* 128-byte ncclUniqueId shared by the group (ep_size > 1) */
+    int32_t path;            /* AMOE_PATH_* */
+} amoe_config;
+
+/* Replaces: gptoss.Open's per-runtime setup (runtime.go:37-60).  Allocates the
+ * per-layer device (or pinned-host) weight storage and the scratch for
+ * max_tokens tokens. */
+AMOE_API int amoe_create(const amoe_config *cfg, amoe_ctx **out);
+
+/* Releases everything the context owns.  NULL is a no-op. */
+AMOE_API void amoe_destroy(amoe_ctx *ctx);
+
+/* Description of the last failure on ctx (ctx NULL: last amoe_create failure
+ * on this thread).  Valid until the next call on the same context. */
+AMOE_API const char *amoe_last_error(const amoe_ctx *ctx);
+
+/* Replaces: loadDecoderLayer's MoE tensors (weights.go:52-54, 80, 84-116) and
+ * the per-call readExpert decode (tensor.go:94-111).  Takes one layer's tensors
+ * in their GGUF storage layout and keeps them on the device in a tiled MXFP4
+ * layout (a lossless byte shuffle: no dequantisation).
+ *   norm_gain  [H] f32                          ffn_norm.weight
+ *   router_w   [E x H] f32 row-major            ffn_gate_inp.weight
+ *   router_b   [E] f32                          ffn_gate_inp.bias
+ *   gate_up    E*2I*(H/32)*17 bytes, MXFP4      ffn_gate_up_exps.weight (rows interleave gate, up)
+ *   gate_up_b  [E x 2I] f32                     ffn_gate_up_exps.bias
+ *   down       E*H*(I/32)*17 bytes, MXFP4       ffn_down_exps.weight
+ *   down_b     [E x H] f32                      ffn_down_exps.bias                    */
+AMOE_API int amoe_upload_layer(amoe_ctx *ctx, int32_t layer, const float *norm_gain,
+                      const float *router_w, const float *router_b, const uint8_t *gate_up,
+                      const float *gate_up_b, const uint8_t *down, const float *down_b);
+
+/* Replaces: the MoE loop of DecoderLayer.forward, layer.go:94-123.
+ * residual [T x H] host f32 (the pre-norm rows); out [T x H] host f32 receives
+ * residual + sum_k p_k * expert_k(RMSNorm(residual)).  topk_idx [T x k] and
+ * topk_w [T x k] (both nullable) receive the routing (MoERouterTopK, moe.go:12-41).
+ * Synchronous.  1 <= T <= max_tokens. */
+AMOE_API int amoe_forward(amoe_ctx *ctx, int32_t layer, const float *residual, int32_t T, float *out,
+                 int32_t *topk_idx, float *topk_w);
+
+/* Same computation on device buffers, enqueued on `stream` (a cudaStream_t;
+ * NULL = the context's own stream); returns without synchronising. */
+AMOE_API int amoe_forward_device(amoe_ctx *ctx, int32_t layer, const float *residual, int32_t T,
+                        float *out, int32_t *topk_idx, float *topk_w, void *stream);
+
+/* Waits for all work the context enqueued. */
+AMOE_API int amoe_synchronize(amoe_ctx *ctx);
+
+/* Streaming mode (stream_slots >= 2): starts copying `layer` from pinned host
+ * memory into a free device slot on the copy stream.  A later forward of that
+ * layer waits for the copy on the device (an event), not on the host.
+ * Replaces the synchronous per-layer reload of Generate, runtime.go:146-199. */
+AMOE_API int amoe_prefetch_layer(amoe_ctx *ctx, int32_t layer);
+
+/* Test/diagnostic hook: copies the routing of the last forward to host.
+ *   logits [T x E] f32 (router logits incl. bias), perm_pair [T*k] (position ->
+ *   pair id t*k+s, pairs ordered stably by expert), counts [E], offsets [E+1].
+ * Any pointer may be NULL. */
+AMOE_API int amoe_last_routing(amoe_ctx *ctx, float *logits, int32_t *perm_pair, int32_t *counts,
+                      int32_t *offsets);
+
+/* Per-stage device timing (CUDA events on the launch stream) and launch count.
+ * Stages: 0 route (RMSNorm+router+top-k), 1 permute, 2 gate_up (+SwiGLU),
+ * 3 down, 4 combine, 5 gather (tensor path), 6-7 reserved. */
+#define AMOE_STAGES 8
+typedef struct amoe_stats {
+    int64_t launches;               /* kernels this context has launched */
+    int64_t forwards;               /* forward calls */
+    int64_t timed_forwards;         /* forwards with profiling on, summed in stage_ms */
+    double stage_ms[AMOE_STAGES];   /* summed event time per stage (profiling on) */
+    int32_t last_path;              /* AMOE_PATH_GEMV or AMOE_PATH_TENSOR of the last forward */
+} amoe_stats;
+
+/* Turns per-stage event timing on (1) or off (0).  Timing adds event records
+ * between kernels; leave it off when measuring whole-forward throughput. */
+AMOE_API int amoe_set_profiling(amoe_ctx *ctx, int32_t on);
+
+/* Synchronises, folds finished stage timings into the counters and copies
+ * them out; reset != 0 clears the counters afterwards. */
+AMOE_API int amoe_get_stats(amoe_ctx *ctx, amoe_stats *out, int32_t reset);
+
+/* ABI version (AMOE_ABI_VERSION). */
+AMOE_API int amoe_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AMOE_H */

@@ -1,0 +1,223 @@
+"""CPU oracle for the GPT-OSS MoE block -- TEST INFRASTRUCTURE ONLY.
+
+A C restatement (moe_oracle.c) of the reference Go CPU path, loaded through
+ctypes.  Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline and
+reference legs import this package; the product library never does.
+
+Reference functions restated (paths relative to the reference project root):
+  RMSNorm            internal/backend/cpuref/primitives.go:50-72
+  Linear/LinearBias  internal/backend/cpuref/primitives.go:11-47
+  MoERouterTopK      internal/backend/cpuref/moe.go:12-41
+  GPTOSSSwiGLU       internal/backend/cpuref/primitives.go:138-149
+  MXFP4 decode       internal/model/gptoss/tensor.go:145-170, gguf/reader.go:442-449
+  MoE block          internal/model/gptoss/layer.go:94-188
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+import threading
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "liboracle.so")
+_lock = threading.Lock()
+_lib = None
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+
+
+class OracleLayer(ctypes.Structure):
+    _fields_ = [
+        ("hidden", ctypes.c_int32),
+        ("intermediate", ctypes.c_int32),
+        ("experts", ctypes.c_int32),
+        ("top_k", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+        ("norm_gain", _f32p),
+        ("router_w", _f32p),
+        ("router_b", _f32p),
+        ("gate_up", _u8p),
+        ("gate_up_b", _f32p),
+        ("down", _u8p),
+        ("down_b", _f32p),
+    ]
+
+
+def build() -> str:
+    """Compile liboracle.so with the committed Makefile (gcc, OpenMP)."""
+    src = [os.path.join(_HERE, f) for f in ("moe_oracle.c", "moe_oracle.h", "Makefile")]
+    if os.path.exists(_LIB_PATH) and all(
+        os.path.getmtime(_LIB_PATH) >= os.path.getmtime(s) for s in src
+    ):
+        return _LIB_PATH
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    with _lock:
+        if _lib is None:
+            build()
+            L = ctypes.CDLL(_LIB_PATH)
+            L.oracle_rmsnorm.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_float, _f32p]
+            L.oracle_linear_bias.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int, _f32p]
+            L.oracle_router_topk.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, _i32p, _f32p]
+            L.oracle_swiglu.argtypes = [_f32p, _f32p, ctypes.c_int, _f32p]
+            L.oracle_mxfp4_decode.argtypes = [_u8p, ctypes.c_int64, ctypes.c_int64, _f32p]
+            L.oracle_mxfp4_encoded_size.argtypes = [ctypes.c_int64]
+            L.oracle_mxfp4_encoded_size.restype = ctypes.c_int64
+            L.oracle_moe_block.argtypes = [
+                ctypes.POINTER(OracleLayer), _f32p, ctypes.c_int, _f32p, _i32p, _f32p, _f32p,
+                _i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+            ]
+            L.oracle_route.argtypes = [
+                ctypes.POINTER(OracleLayer), _f32p, ctypes.c_int, _f32p, _i32p, _f32p, ctypes.c_int,
+            ]
+            L.oracle_permute.argtypes = [_i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                         _i32p, _i32p, _i32p, _i32p]
+            _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray, ty):
+    return a.ctypes.data_as(ty) if a is not None else None
+
+
+def _c(a, dtype):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+class OracleError(RuntimeError):
+    pass
+
+
+def _check(rc: int, what: str):
+    if rc != 0:
+        raise OracleError(f"oracle {what} rejected its arguments")
+
+
+def rmsnorm(x, g, eps):
+    x, g = _c(x, np.float32), _c(g, np.float32)
+    out = np.empty_like(x)
+    _check(lib().oracle_rmsnorm(_p(x, _f32p), _p(g, _f32p), x.size, eps, _p(out, _f32p)), "rmsnorm")
+    return out
+
+
+def linear_bias(x, w, b, in_dim, out_dim):
+    x, w = _c(x, np.float32), _c(w, np.float32)
+    b = _c(b, np.float32) if b is not None else None
+    if x.size != in_dim or w.size != in_dim * out_dim or (b is not None and b.size != out_dim):
+        raise OracleError("linear length mismatch")
+    y = np.empty(out_dim, np.float32)
+    _check(lib().oracle_linear_bias(_p(x, _f32p), _p(w, _f32p), _p(b, _f32p) if b is not None else None,
+                                    in_dim, out_dim, _p(y, _f32p)), "linear")
+    return y
+
+
+def router_topk(logits, k):
+    logits = _c(logits, np.float32)
+    idx = np.empty(max(k, 0), np.int32)
+    w = np.empty(max(k, 0), np.float32)
+    _check(lib().oracle_router_topk(_p(logits, _f32p), logits.size, k, _p(idx, _i32p), _p(w, _f32p)),
+           "router_topk")
+    return idx, w
+
+
+def swiglu(gate, up):
+    gate, up = _c(gate, np.float32), _c(up, np.float32)
+    if gate.size != up.size:
+        raise OracleError("swiglu lengths differ")
+    out = np.empty_like(gate)
+    lib().oracle_swiglu(_p(gate, _f32p), _p(up, _f32p), gate.size, _p(out, _f32p))
+    return out
+
+
+def mxfp4_encoded_size(elements: int) -> int:
+    n = lib().oracle_mxfp4_encoded_size(elements)
+    if n < 0:
+        raise OracleError("MXFP4 element count must be divisible by 32")
+    return n
+
+
+def mxfp4_decode(data, elements):
+    data = _c(np.frombuffer(bytes(data), np.uint8) if isinstance(data, (bytes, bytearray)) else data, np.uint8)
+    out = np.empty(elements, np.float32)
+    _check(lib().oracle_mxfp4_decode(_p(data, _u8p), data.size, elements, _p(out, _f32p)), "mxfp4_decode")
+    return out
+
+
+class _Layer:
+    """Keeps the numpy arrays alive for as long as the ctypes struct is used."""
+
+    def __init__(self, layer: dict):
+        self.arrays = {
+            "norm_gain": _c(layer["norm_gain"], np.float32),
+            "router_w": _c(layer["router_w"], np.float32),
+            "router_b": _c(layer["router_b"], np.float32),
+            "gate_up": _c(layer["gate_up"], np.uint8),
+            "gate_up_b": _c(layer["gate_up_b"], np.float32),
+            "down": _c(layer["down"], np.uint8),
+            "down_b": _c(layer["down_b"], np.float32),
+        }
+        a = self.arrays
+        self.s = OracleLayer(
+            layer["hidden"], layer["intermediate"], layer["experts"], layer["top_k"], layer["eps"],
+            _p(a["norm_gain"], _f32p), _p(a["router_w"], _f32p), _p(a["router_b"], _f32p),
+            _p(a["gate_up"], _u8p), _p(a["gate_up_b"], _f32p), _p(a["down"], _u8p),
+            _p(a["down_b"], _f32p),
+        )
+
+
+def moe_block(layer: dict, residual, tokens=None, faithful=False, threads=None):
+    """Run the reference MoE block.  Returns (out, topk_idx, topk_w, logits).
+
+    tokens: optional row indices to compute (others stay NaN / -1)."""
+    L = _Layer(layer)
+    res = _c(residual, np.float32)
+    T = res.shape[0]
+    H, k, E = layer["hidden"], layer["top_k"], layer["experts"]
+    out = np.full((T, H), np.nan, np.float32)
+    idx = np.full((T, k), -1, np.int32)
+    w = np.full((T, k), np.nan, np.float32)
+    logits = np.full((T, E), np.nan, np.float32)
+    tok = _c(tokens, np.int32) if tokens is not None else None
+    threads = threads or os.cpu_count() or 1
+    rc = lib().oracle_moe_block(ctypes.byref(L.s), _p(res, _f32p), T, _p(out, _f32p), _p(idx, _i32p),
+                                _p(w, _f32p), _p(logits, _f32p), _p(tok, _i32p) if tok is not None else None,
+                                0 if tok is None else tok.size, 1 if faithful else 0, threads)
+    _check(rc, "moe_block")
+    return out, idx, w, logits
+
+
+def route(layer: dict, residual, threads=None):
+    """Router only for all rows: (logits, topk_idx, topk_w)."""
+    L = _Layer(layer)
+    res = _c(residual, np.float32)
+    T = res.shape[0]
+    k, E = layer["top_k"], layer["experts"]
+    logits = np.empty((T, E), np.float32)
+    idx = np.empty((T, k), np.int32)
+    w = np.empty((T, k), np.float32)
+    rc = lib().oracle_route(ctypes.byref(L.s), _p(res, _f32p), T, _p(logits, _f32p), _p(idx, _i32p),
+                            _p(w, _f32p), threads or os.cpu_count() or 1)
+    _check(rc, "route")
+    return logits, idx, w
+
+
+def permute(topk_idx, experts):
+    """Stable (expert, token, slot) order: (perm_pair, counts, offsets, inv)."""
+    idx = _c(topk_idx, np.int32)
+    T, k = idx.shape
+    perm = np.empty(T * k, np.int32)
+    counts = np.empty(experts, np.int32)
+    offsets = np.empty(experts + 1, np.int32)
+    inv = np.empty(T * k, np.int32)
+    _check(lib().oracle_permute(_p(idx, _i32p), T, k, experts, _p(perm, _i32p), _p(counts, _i32p),
+                                _p(offsets, _i32p), _p(inv, _i32p)), "permute")
+    return perm, counts, offsets, inv

@@ -1,0 +1,357 @@
+/*
+ * moe_oracle.c -- CPU restatement of the GPT-OSS MoE block of lutikk/airllm.
+ *
+ * TEST INFRASTRUCTURE ONLY (the checker).  Not part of the product library.
+ *
+ * Arithmetic follows the reference Go code exactly:
+ *   - every dot product accumulates float64(x)*float64(w) sequentially over the
+ *     input index and rounds to float32 once (primitives.go:23-30); a product of
+ *     two float32 values is exact in float64, so contraction into FMA cannot
+ *     change a result;
+ *   - biases are added in float32 after that rounding (primitives.go:43-45);
+ *   - MXFP4 weights are float32(scale) * table[nibble] (tensor.go:152-159);
+ *   - the top-k order is a stable descending order with ties to the lower
+ *     expert id, the softmax runs in float64 over the selected logits only
+ *     (moe.go:20-39);
+ *   - the expert mixture accumulates float64(p)*float64(y) in slot order and is
+ *     added to the pre-norm row in float32 (layer.go:109-121).
+ * Compile without -ffast-math (denormal MXFP4 scales must not be flushed).
+ */
+#include "moe_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* E2M1 code -> value, internal/model/gptoss/tensor.go:167-170 */
+static const float kE2M1[16] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f,
+                                -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f};
+
+/* E8M0 block scale, tensor.go:152-155: 2^(b-127), 0xff is NaN. */
+static inline float e8m0_scale(uint8_t b) {
+    if (b == 0xff) return NAN;
+    return (float)ldexp(1.0, (int)b - 127);
+}
+
+int64_t oracle_mxfp4_encoded_size(int64_t elements) {
+    /* reader.go:442-449 */
+    if (elements < 0 || elements % 32 != 0) return -1;
+    return elements / 32 * 17;
+}
+
+int oracle_mxfp4_decode(const uint8_t *data, int64_t nbytes, int64_t elements, float *out) {
+    /* tensor.go:145-160: 17-byte blocks; byte j (1..16) low nibble -> element
+     * 2(j-1), high nibble -> element 2(j-1)+1. */
+    if (elements % 32 != 0 || nbytes != elements / 32 * 17) return -1;
+    for (int64_t blk = 0; blk < elements / 32; ++blk) {
+        const uint8_t *enc = data + blk * 17;
+        float scale = e8m0_scale(enc[0]);
+        for (int i = 0; i < 16; ++i) {
+            uint8_t packed = enc[1 + i];
+            out[blk * 32 + 2 * i] = scale * kE2M1[packed & 0x0f];
+            out[blk * 32 + 2 * i + 1] = scale * kE2M1[packed >> 4];
+        }
+    }
+    return 0;
+}
+
+int oracle_rmsnorm(const float *x, const float *g, int n, float eps, float *out) {
+    /* primitives.go:50-72 */
+    if (n <= 0) return -1;
+    if (!(eps > 0.0f)) return -1; /* also rejects NaN */
+    double sum_squares = 0.0;
+    for (int i = 0; i < n; ++i) sum_squares += (double)x[i] * (double)x[i];
+    double inverse_rms = 1.0 / sqrt(sum_squares / (double)n + (double)eps);
+    for (int i = 0; i < n; ++i) out[i] = (float)((double)x[i] * inverse_rms * (double)g[i]);
+    return 0;
+}
+
+int oracle_linear_bias(const float *x, const float *w, const float *b, int in_dim,
+                       int out_dim, float *y) {
+    /* primitives.go:11-47 */
+    if (in_dim <= 0 || out_dim <= 0) return -1;
+    for (int o = 0; o < out_dim; ++o) {
+        const float *row = w + (int64_t)o * in_dim;
+        double sum = 0.0;
+        for (int i = 0; i < in_dim; ++i) sum += (double)x[i] * (double)row[i];
+        y[o] = (float)sum;
+    }
+    if (b)
+        for (int o = 0; o < out_dim; ++o) y[o] += b[o];
+    return 0;
+}
+
+int oracle_router_topk(const float *logits, int n, int k, int32_t *idx, float *w) {
+    /* moe.go:12-41.  The first k entries of a stable descending sort equal k
+     * rounds of "largest remaining value, lowest index among equals" for
+     * ordered (non-NaN) inputs; NaN logits have no defined order in either. */
+    if (n <= 0 || k <= 0 || k > n) return -1;
+    unsigned char used_stack[1024];
+    unsigned char *used = n <= 1024 ? used_stack : (unsigned char *)calloc((size_t)n, 1);
+    if (!used) return -1;
+    memset(used, 0, (size_t)n);
+    for (int s = 0; s < k; ++s) {
+        int best = -1;
+        for (int e = 0; e < n; ++e) {
+            if (used[e]) continue;
+            if (best < 0 || logits[e] > logits[best]) best = e;
+        }
+        used[best] = 1;
+        idx[s] = best;
+    }
+    if (used != used_stack) free(used);
+    double max_logit = (double)logits[idx[0]];
+    double denominator = 0.0;
+    for (int s = 0; s < k; ++s) {
+        double weight = exp((double)logits[idx[s]] - max_logit);
+        w[s] = (float)weight;
+        denominator += weight;
+    }
+    for (int s = 0; s < k; ++s) w[s] = (float)((double)w[s] / denominator);
+    return 0;
+}
+
+/* Go math.Min / math.Max semantics for the operands used here: NaN wins. */
+static inline double go_min(double a, double b) {
+    if (isnan(a) || isnan(b)) return NAN;
+    return a < b ? a : b;
+}
+static inline double go_max(double a, double b) {
+    if (isnan(a) || isnan(b)) return NAN;
+    return a > b ? a : b;
+}
+
+int oracle_swiglu(const float *gate, const float *up, int n, float *out) {
+    /* primitives.go:138-149 */
+    for (int i = 0; i < n; ++i) {
+        double g = go_min((double)gate[i], 7.0);
+        double u = go_max(-7.0, go_min(7.0, (double)up[i]));
+        out[i] = (float)(g / (1.0 + exp(-1.702 * g)) * (u + 1.0));
+    }
+    return 0;
+}
+
+/* Dot product of float32 x with one MXFP4 row decoded on the fly; identical
+ * to decoding the row first and calling Linear.  Four rows are interleaved to
+ * give the CPU independent dependency chains; each chain keeps the sequential
+ * input order, so results are bit-identical to one row at a time. */
+static void mxfp4_rows4(const float *x, const uint8_t *rows, int64_t row_bytes, int nrows,
+                        int in_dim, double *sums) {
+    double s[4] = {0, 0, 0, 0};
+    const int nblk = in_dim / 32;
+    for (int blk = 0; blk < nblk; ++blk) {
+        float scale[4];
+        const uint8_t *enc[4];
+        for (int r = 0; r < nrows; ++r) {
+            enc[r] = rows + r * row_bytes + (int64_t)blk * 17;
+            scale[r] = e8m0_scale(enc[r][0]);
+        }
+        const float *xb = x + blk * 32;
+        for (int i = 0; i < 16; ++i) {
+            double x0 = (double)xb[2 * i], x1 = (double)xb[2 * i + 1];
+            for (int r = 0; r < nrows; ++r) {
+                uint8_t p = enc[r][1 + i];
+                s[r] += x0 * (double)(scale[r] * kE2M1[p & 0x0f]);
+                s[r] += x1 * (double)(scale[r] * kE2M1[p >> 4]);
+            }
+        }
+    }
+    for (int r = 0; r < nrows; ++r) sums[r] = s[r];
+}
+
+static void linear_bias_mxfp4(const float *x, const uint8_t *w, const float *b, int in_dim,
+                              int out_dim, float *y) {
+    const int64_t row_bytes = (int64_t)in_dim / 32 * 17;
+    for (int o = 0; o < out_dim; o += 4) {
+        int nrows = out_dim - o < 4 ? out_dim - o : 4;
+        double sums[4];
+        mxfp4_rows4(x, w + (int64_t)o * row_bytes, row_bytes, nrows, in_dim, sums);
+        for (int r = 0; r < nrows; ++r) y[o + r] = (float)sums[r];
+    }
+    for (int o = 0; o < out_dim; ++o) y[o] += b[o];
+}
+
+typedef struct {
+    float *normalized, *logits, *gate_up, *gate, *up, *act, *down;
+    double *mixture;
+    float *wgu, *wdn; /* faithful mode: one decoded expert */
+} scratch;
+
+static int scratch_init(scratch *s, const oracle_layer *L, int faithful) {
+    const int H = L->hidden, I = L->intermediate, E = L->experts;
+    memset(s, 0, sizeof(*s));
+    s->normalized = (float *)malloc(sizeof(float) * H);
+    s->logits = (float *)malloc(sizeof(float) * E);
+    s->gate_up = (float *)malloc(sizeof(float) * 2 * I);
+    s->gate = (float *)malloc(sizeof(float) * I);
+    s->up = (float *)malloc(sizeof(float) * I);
+    s->act = (float *)malloc(sizeof(float) * I);
+    s->down = (float *)malloc(sizeof(float) * H);
+    s->mixture = (double *)malloc(sizeof(double) * H);
+    if (faithful) {
+        s->wgu = (float *)malloc(sizeof(float) * (size_t)2 * I * H);
+        s->wdn = (float *)malloc(sizeof(float) * (size_t)H * I);
+    }
+    return (s->normalized && s->logits && s->gate_up && s->gate && s->up && s->act &&
+            s->down && s->mixture && (!faithful || (s->wgu && s->wdn)))
+               ? 0
+               : -1;
+}
+
+static void scratch_free(scratch *s) {
+    free(s->normalized); free(s->logits); free(s->gate_up); free(s->gate); free(s->up);
+    free(s->act); free(s->down); free(s->mixture); free(s->wgu); free(s->wdn);
+}
+
+/* forwardExpert, layer.go:126-188 (fused gate_up dialect, layer.go:130-148). */
+static int forward_expert(const oracle_layer *L, const float *hidden, int expert, int faithful,
+                          scratch *s) {
+    const int H = L->hidden, I = L->intermediate;
+    const int64_t gu_bytes = (int64_t)2 * I * (H / 32) * 17;
+    const int64_t dn_bytes = (int64_t)H * (I / 32) * 17;
+    const uint8_t *gu = L->gate_up + (int64_t)expert * gu_bytes; /* tensor.go:101-103 */
+    const uint8_t *dn = L->down + (int64_t)expert * dn_bytes;
+    const float *gub = L->gate_up_b + (int64_t)expert * 2 * I;
+    const float *dnb = L->down_b + (int64_t)expert * H;
+    if (faithful) {
+        if (oracle_mxfp4_decode(gu, gu_bytes, (int64_t)2 * I * H, s->wgu)) return -1;
+        oracle_linear_bias(hidden, s->wgu, gub, H, 2 * I, s->gate_up);
+    } else {
+        linear_bias_mxfp4(hidden, gu, gub, H, 2 * I, s->gate_up);
+    }
+    for (int i = 0; i < I; ++i) { /* layer.go:145-148 */
+        s->gate[i] = s->gate_up[2 * i];
+        s->up[i] = s->gate_up[2 * i + 1];
+    }
+    oracle_swiglu(s->gate, s->up, I, s->act);
+    if (faithful) {
+        if (oracle_mxfp4_decode(dn, dn_bytes, (int64_t)H * I, s->wdn)) return -1;
+        oracle_linear_bias(s->act, s->wdn, dnb, I, H, s->down);
+    } else {
+        linear_bias_mxfp4(s->act, dn, dnb, I, H, s->down);
+    }
+    return 0;
+}
+
+static int validate(const oracle_layer *L) {
+    if (!L || L->hidden <= 0 || L->intermediate <= 0 || L->experts <= 0) return -1;
+    if (L->hidden % 32 || L->intermediate % 32) return -1;
+    if (L->top_k <= 0 || L->top_k > L->experts) return -1;
+    return 0;
+}
+
+static int route_row(const oracle_layer *L, const float *row, scratch *s, int32_t *idx,
+                     float *w) {
+    if (oracle_rmsnorm(row, L->norm_gain, L->hidden, L->eps, s->normalized)) return -1;
+    oracle_linear_bias(s->normalized, L->router_w, L->router_b, L->hidden, L->experts,
+                       s->logits);
+    return oracle_router_topk(s->logits, L->experts, L->top_k, idx, w);
+}
+
+int oracle_route(const oracle_layer *L, const float *residual, int T, float *logits,
+                 int32_t *topk_idx, float *topk_w, int threads) {
+    if (validate(L) || T < 0) return -1;
+    int status = 0;
+#pragma omp parallel num_threads(threads > 0 ? threads : 1)
+    {
+        scratch s;
+        int ok = scratch_init(&s, L, 0) == 0;
+        if (!ok) {
+#pragma omp atomic write
+            status = -1;
+        }
+#pragma omp for schedule(static)
+        for (int t = 0; t < T; ++t) {
+            if (!ok) continue;
+            const float *row = residual + (int64_t)t * L->hidden;
+            if (route_row(L, row, &s, topk_idx + (int64_t)t * L->top_k,
+                          topk_w + (int64_t)t * L->top_k)) {
+#pragma omp atomic write
+                status = -1;
+            }
+            if (logits) memcpy(logits + (int64_t)t * L->experts, s.logits, sizeof(float) * L->experts);
+        }
+        scratch_free(&s);
+    }
+    return status;
+}
+
+int oracle_moe_block(const oracle_layer *L, const float *residual, int T, float *out,
+                     int32_t *topk_idx, float *topk_w, float *logits, const int32_t *tokens,
+                     int n_tokens, int faithful, int threads) {
+    if (validate(L) || T < 0) return -1;
+    const int H = L->hidden, k = L->top_k;
+    const int n = tokens ? n_tokens : T;
+    int status = 0;
+#pragma omp parallel num_threads(threads > 0 ? threads : 1)
+    {
+        scratch s;
+        int ok = scratch_init(&s, L, faithful) == 0;
+        if (!ok) {
+#pragma omp atomic write
+            status = -1;
+        }
+        int32_t idx[256];
+        float w[256];
+#pragma omp for schedule(dynamic, 1)
+        for (int j = 0; j < n; ++j) {
+            if (!ok) continue;
+            const int t = tokens ? tokens[j] : j;
+            if (t < 0 || t >= T || k > 256) {
+#pragma omp atomic write
+                status = -1;
+                continue;
+            }
+            const float *row = residual + (int64_t)t * H; /* layer.go:96 */
+            if (route_row(L, row, &s, idx, w)) {          /* layer.go:97-108 */
+#pragma omp atomic write
+                status = -1;
+                continue;
+            }
+            for (int i = 0; i < H; ++i) s.mixture[i] = 0.0;
+            for (int slot = 0; slot < k; ++slot) { /* layer.go:110-118 */
+                if (forward_expert(L, s.normalized, idx[slot], faithful, &s)) {
+#pragma omp atomic write
+                    status = -1;
+                    break;
+                }
+                for (int i = 0; i < H; ++i) s.mixture[i] += (double)w[slot] * (double)s.down[i];
+            }
+            for (int i = 0; i < H; ++i) /* layer.go:119-121 */
+                out[(int64_t)t * H + i] = row[i] + (float)s.mixture[i];
+            if (topk_idx) memcpy(topk_idx + (int64_t)t * k, idx, sizeof(int32_t) * k);
+            if (topk_w) memcpy(topk_w + (int64_t)t * k, w, sizeof(float) * k);
+            if (logits) memcpy(logits + (int64_t)t * L->experts, s.logits, sizeof(float) * L->experts);
+        }
+        scratch_free(&s);
+    }
+    return status;
+}
+
+int oracle_permute(const int32_t *topk_idx, int T, int k, int E, int32_t *perm_pair,
+                   int32_t *counts, int32_t *offsets, int32_t *inv) {
+    if (T < 0 || k <= 0 || E <= 0) return -1;
+    for (int e = 0; e < E; ++e) counts[e] = 0;
+    for (int64_t p = 0; p < (int64_t)T * k; ++p) {
+        int e = topk_idx[p];
+        if (e < 0 || e >= E) return -1;
+        counts[e]++;
+    }
+    offsets[0] = 0;
+    for (int e = 0; e < E; ++e) offsets[e + 1] = offsets[e] + counts[e];
+    int32_t *cursor = (int32_t *)malloc(sizeof(int32_t) * E);
+    if (!cursor) return -1;
+    memcpy(cursor, offsets, sizeof(int32_t) * E);
+    /* pairs visited in (t, s) order: a stable counting sort by expert */
+    for (int64_t p = 0; p < (int64_t)T * k; ++p) {
+        int e = topk_idx[p];
+        int32_t pos = cursor[e]++;
+        perm_pair[pos] = (int32_t)p;
+        inv[p] = pos;
+    }
+    free(cursor);
+    return 0;
+}

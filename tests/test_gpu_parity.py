@@ -1,0 +1,183 @@
+"""CUDA path vs the oracle, through the C ABI (ctypes -> libamoe.so)."""
+import numpy as np
+import pytest
+
+import oracle
+from airllm_b200 import moe
+from airllm_b200 import workloads as W
+from parity_util import assert_block_parity, routing_mismatches
+
+pytestmark = pytest.mark.gpu
+
+PATHS = [moe.PATH_GEMV]
+
+
+def run_block(layer, x, path=moe.PATH_AUTO, max_tokens=None):
+    blk = moe.MoEBlock.for_layer(layer, max_tokens=max_tokens or max(x.shape[0], 1), path=path)
+    blk.upload_layer(0, layer)
+    out, idx, w = blk.forward(x)
+    routing = blk.last_routing(x.shape[0])
+    blk.close()
+    return out, idx, w, routing
+
+
+def check_against_oracle(layer, x, path, tokens=None):
+    out, idx, w, (logits, perm, counts, offsets) = run_block(layer, x, path)
+    ref_lg, ref_idx, ref_w = oracle.route(layer, x)
+    ties, bad = routing_mismatches(idx, ref_idx, ref_lg)
+    assert not bad, f"routing differs beyond ties on rows {bad[:10]}"
+    # logits: float64 sums in another order -> equal or 1 ulp apart
+    np.testing.assert_array_almost_equal_nulp(logits, ref_lg, nulp=2)
+    # the permutation is the stable (expert, token, slot) order of the GPU's own routing
+    p_ref, c_ref, o_ref, _ = oracle.permute(idx, layer["experts"])
+    assert np.array_equal(perm, p_ref) and np.array_equal(counts, c_ref) and np.array_equal(offsets, o_ref)
+    if not ties:
+        np.testing.assert_allclose(w, ref_w, rtol=2e-6, atol=0)
+    rows = np.arange(x.shape[0]) if tokens is None else np.asarray(tokens)
+    rows = np.setdiff1d(rows, ties)
+    ref_out = oracle.moe_block(layer, x, tokens=rows)[0]
+    return assert_block_parity(out, ref_out, rows)
+
+
+def test_tiny_fixture_all_ties_and_bias_path(cuda_device):
+    """MXFP4 analogue of the synthetic model of internal/model/gptoss/runtime_test.go:123-189:
+    zero router (all logits tie -> experts 0..3 in index order, weights 1/4), zero expert
+    weights, a down bias per expert; the block adds sum_k 1/4 * bias_k to the residual."""
+    H, I, E, k = 64, 64, 4, 4
+    layer = W.small_layer(hidden=H, intermediate=I, experts=E, top_k=k, seed=0)
+    layer["router_w"][:] = 0
+    layer["router_b"][:] = 0
+    layer["gate_up"].reshape(-1, 17)[:, 1:] = 0  # every nibble is +0
+    layer["down"].reshape(-1, 17)[:, 1:] = 0
+    layer["gate_up_b"][:] = 0
+    layer["down_b"][:] = np.array([[0.25], [0.25], [0.0], [0.0]], np.float32)
+    x = W.make_tokens(W.MoEShape(H, I, E, k), 3, 0)
+    out, idx, w, _ = run_block(layer, x, moe.PATH_GEMV)
+    assert (idx == np.arange(4)).all()
+    assert (w == np.float32(0.25)).all()
+    np.testing.assert_array_equal(out, x + np.float32(0.125))
+
+
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("H,I,E,k,T", [
+    (64, 128, 8, 4, 1), (64, 128, 8, 4, 3), (64, 128, 8, 4, 8), (64, 128, 8, 4, 9),
+    (64, 128, 8, 4, 37), (128, 64, 5, 2, 17), (192, 320, 16, 4, 64), (64, 64, 128, 4, 40),
+    (64, 64, 256, 8, 11), (128, 128, 3, 1, 5),
+])
+def test_small_layers_match_oracle(cuda_device, path, H, I, E, k, T):
+    layer = W.small_layer(hidden=H, intermediate=I, experts=E, top_k=k, seed=H + I + E + T)
+    x = W.make_tokens(W.MoEShape(H, I, E, k), T, T)
+    check_against_oracle(layer, x, path)
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_extreme_scales_incl_denormal(cuda_device, path):
+    layer = W.small_layer(hidden=128, intermediate=128, experts=8, top_k=4, seed=4, scale_lo=0, scale_hi=140)
+    x = W.make_tokens(W.MoEShape(128, 128, 8, 4), 6, 4)
+    check_against_oracle(layer, x, path)
+
+
+def test_nan_scale_propagates_like_reference(cuda_device):
+    layer = W.small_layer(hidden=64, intermediate=64, experts=4, top_k=4, seed=9)
+    layer["down"].reshape(-1, 17)[5, 0] = 0xFF  # expert 0, one block of down row 2
+    x = W.make_tokens(W.MoEShape(64, 64, 4, 4), 2, 9)
+    out, idx, w, _ = run_block(layer, x, moe.PATH_GEMV)
+    ref = oracle.moe_block(layer, x)[0]
+    assert np.array_equal(np.isnan(out), np.isnan(ref)) and np.isnan(ref).any()
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_config0_decode_token(cuda_device, path):
+    layer = W.config_layer(0)
+    x = W.config_tokens(0)
+    max_abs, rel = check_against_oracle(layer, x, path)
+    print(f"config0 max-abs {max_abs:.3e} rel-L2 {rel:.3e}")
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_config1_prefill_4096_sampled_rows(cuda_device, path):
+    layer = W.config_layer(1)
+    x = W.config_tokens(1)
+    _, ref_idx, _ = oracle.route(layer, x)
+    counts = np.bincount(ref_idx.ravel(), minlength=32)
+    busiest = np.nonzero((ref_idx == counts.argmax()).any(axis=1))[0][:6]
+    idlest = np.nonzero((ref_idx == counts.argmin()).any(axis=1))[0][:4]
+    rows = np.unique(np.concatenate([[0, 1, 4095], busiest, idlest, np.arange(100, 4096, 509)]))
+    max_abs, rel = check_against_oracle(layer, x, path, tokens=rows)
+    print(f"config1 rows={len(rows)} max-abs {max_abs:.3e} rel-L2 {rel:.3e}")
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_config3_decode_batch_128_experts(cuda_device, path):
+    layer = W.config_layer(3)
+    x = W.config_tokens(3)
+    rows = np.arange(0, 256, 17)
+    check_against_oracle(layer, x, path, tokens=rows)
+
+
+def test_device_forward_matches_host_forward_and_is_deterministic(cuda_device):
+    import torch
+
+    layer = W.small_layer(hidden=192, intermediate=128, experts=16, top_k=4, seed=21)
+    x = W.make_tokens(W.MoEShape(192, 128, 16, 4), 33, 21)
+    blk = moe.MoEBlock.for_layer(layer, max_tokens=64)
+    blk.upload_layer(0, layer)
+    out1, idx1, w1 = blk.forward(x)
+    out2, _, _ = blk.forward(x)
+    assert np.array_equal(out1, out2)
+    xd = torch.from_numpy(x).cuda()
+    od = torch.empty_like(xd)
+    idd = torch.empty((33, 4), dtype=torch.int32, device="cuda")
+    wd = torch.empty((33, 4), dtype=torch.float32, device="cuda")
+    blk.forward_device(xd, od, topk_idx=idd, topk_w=wd)
+    blk.synchronize()
+    assert np.array_equal(od.cpu().numpy(), out1)
+    assert np.array_equal(idd.cpu().numpy(), idx1) and np.array_equal(wd.cpu().numpy(), w1)
+    blk.close()
+
+
+def test_errors_are_status_codes(cuda_device):
+    layer = W.small_layer()
+    blk = moe.MoEBlock.for_layer(layer, max_tokens=8)
+    x = W.make_tokens(W.MoEShape(64, 128, 8, 4), 9, 0)
+    with pytest.raises(moe.AmoeError) as e:
+        blk.forward(x[:2])  # layer 0 not uploaded yet
+    assert e.value.code == moe.AMOE_ERR_STATE
+    blk.upload_layer(0, layer)
+    with pytest.raises(moe.AmoeError) as e:
+        blk.forward(x)  # 9 > max_tokens
+    assert e.value.code == moe.AMOE_ERR_INVALID
+    with pytest.raises(moe.AmoeError) as e:
+        blk.forward(x[:0])
+    assert e.value.code == moe.AMOE_ERR_INVALID
+    bad = dict(layer)
+    bad["down"] = layer["down"][:-1]
+    with pytest.raises(moe.AmoeError):
+        blk.upload_layer(0, bad)
+    with pytest.raises(moe.AmoeError) as e:
+        blk.upload_layer(3, layer)
+    assert e.value.code == moe.AMOE_ERR_INVALID
+    out, _, _ = blk.forward(x[:2])  # still usable
+    assert np.isfinite(out).all()
+    blk.close()
+
+
+def test_streaming_slots_match_resident_layers(cuda_device):
+    shape = W.MoEShape(128, 128, 8, 4)
+    layers = [W.make_layer(shape, 50 + i) for i in range(3)]
+    x = W.make_tokens(shape, 5, 50)
+    res = moe.MoEBlock(128, 128, 8, 4, layers=3, max_tokens=8)
+    stm = moe.MoEBlock(128, 128, 8, 4, layers=3, max_tokens=8, stream_slots=2)
+    for i, L in enumerate(layers):
+        res.upload_layer(i, L)
+        stm.upload_layer(i, L)
+    h_res, h_stm = x, x
+    for step in range(2):
+        for i in range(3):
+            if i + 1 < 3:
+                stm.prefetch_layer(i + 1)
+            h_res = res.forward(h_res, layer=i)[0]
+            h_stm = stm.forward(h_stm, layer=i)[0]
+            assert np.array_equal(h_res, h_stm)
+    res.close()
+    stm.close()
