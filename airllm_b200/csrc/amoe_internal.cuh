@@ -50,6 +50,8 @@ struct LayerDev {
     uint8_t *dn_q = nullptr;      // [E][H/16][I/64][512]
     uint8_t *dn_s = nullptr;      // [E][H/16][I/64][32]
     float *dn_b = nullptr;        // [E][H]
+    int32_t *gu_cexp = nullptr;   // [E] power-of-two bias of the fp16 weight expansion (tcgen05 path)
+    int32_t *dn_cexp = nullptr;   // [E]
 };
 
 struct Dims {
@@ -104,7 +106,13 @@ bool tc_supported();
 // Runs gate_up(+SwiGLU) and down for all pairs; *launches receives the kernel count.
 cudaError_t launch_tc_forward(const Dims &d, const LayerDev &L, const RouteOut &r, int T,
                               __half *act_hi, __half *act_lo, float *y, void *tc_scratch,
-                              cudaStream_t st, StageHook hook, void *hook_arg, int *launches);
+                              int max_pairs, cudaStream_t st, StageHook hook, void *hook_arg,
+                              int *launches);
+// Per-expert exponent bias from a tiled scale plane (upload time).
+cudaError_t launch_cexp(const uint8_t *s_plane, size_t bytes_per_expert, int E, int32_t *out,
+                        cudaStream_t st);
+// Device word the tcgen05 kernels set when a bounded wait gives up (0 = fine).
+int32_t *tc_error_flag(void *tc_scratch, int max_pairs, int H);
 
 // Combine --------------------------------------------------------------------
 cudaError_t launch_combine(const Dims &d, const float *residual, const RouteOut &r,

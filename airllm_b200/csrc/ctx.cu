@@ -28,7 +28,7 @@ struct Status {
 
 struct LayerBlock {
     // byte offsets inside one layer's device-format block (256-B aligned parts)
-    size_t norm, router_wt, router_b, gu_b, dn_b, gu_s, dn_s, gu_q, dn_q, total;
+    size_t norm, router_wt, router_b, gu_b, dn_b, gu_cexp, dn_cexp, gu_s, dn_s, gu_q, dn_q, total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -47,6 +47,8 @@ LayerBlock layer_block(const Dims &d) {
     b.router_b = take(E * 4);
     b.gu_b = take(E * 2 * I * 4);
     b.dn_b = take(E * H * 4);
+    b.gu_cexp = take(E * 4);
+    b.dn_cexp = take(E * 4);
     b.gu_s = take(E * 2 * I * (H / 32));
     b.dn_s = take(E * H * (I / 32));
     b.gu_q = take(E * 2 * I * (H / 2));
@@ -62,6 +64,8 @@ LayerDev layer_view(uint8_t *base, const LayerBlock &b) {
     L.router_b = reinterpret_cast<float *>(base + b.router_b);
     L.gu_b = reinterpret_cast<float *>(base + b.gu_b);
     L.dn_b = reinterpret_cast<float *>(base + b.dn_b);
+    L.gu_cexp = reinterpret_cast<int32_t *>(base + b.gu_cexp);
+    L.dn_cexp = reinterpret_cast<int32_t *>(base + b.dn_cexp);
     L.gu_s = base + b.gu_s;
     L.dn_s = base + b.dn_s;
     L.gu_q = base + b.gu_q;
@@ -203,6 +207,7 @@ int alloc_scratch(amoe_ctx *c) {
     uint8_t *base = static_cast<uint8_t *>(c->scratch);
     for (size_t i = 0; i < parts.size(); ++i) *parts[i].dst = parts[i].bytes ? base + at[i] : nullptr;
     AMOE_CUDA(c, cudaMemset(c->arrivals, 0, (size_t)c->nchunk_max * 4));
+    AMOE_CUDA(c, cudaMemset(tc_error_flag(c->tc_scratch, (int)P, d.H), 0, sizeof(int32_t)));
     return AMOE_OK;
 }
 
@@ -305,6 +310,19 @@ int acquire_slot(amoe_ctx *c, int layer, cudaStream_t st, int *slot_out) {
 }
 
 void timer_hook(void *timer, int stage) { static_cast<StageTimer *>(timer)->mark(stage); }
+
+// A tcgen05 kernel that gave up on a bounded wait leaves a code in its flag.
+int check_device_flag(amoe_ctx *c) {
+    int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * c->d.k, c->d.H);
+    int32_t v = 0;
+    cudaError_t e = cudaMemcpy(&v, flag, sizeof(v), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(c, e, "read device error flag");
+    if (v != 0) {
+        cudaMemset(flag, 0, sizeof(int32_t));
+        return fail(c, AMOE_ERR_TIMEOUT, "tcgen05 pipeline wait timed out (code " + std::to_string(v) + ")");
+    }
+    return AMOE_OK;
+}
 
 int check_ctx(amoe_ctx *c) {
     if (!c) return AMOE_ERR_INVALID;
@@ -459,6 +477,8 @@ int amoe_upload_layer(amoe_ctx *c, int32_t layer, const float *norm_gain, const 
     UP_CUDA(cudaStreamSynchronize(st));  // staging is reused for down
     UP_CUDA(cudaMemcpyAsync(staging, down, dn_bytes, cudaMemcpyHostToDevice, st));
     UP_CUDA(launch_repack(staging, (int)E, (int)H, (int)I, false, L.dn_q, L.dn_s, st));
+    UP_CUDA(launch_cexp(L.gu_s, 2 * I * (H / 32), (int)E, L.gu_cexp, st));
+    UP_CUDA(launch_cexp(L.dn_s, H * (I / 32), (int)E, L.dn_cexp, st));
     if (streaming(c)) {
         UP_CUDA(cudaMemcpyAsync(c->layer_host[layer], blockp, c->blk.total, cudaMemcpyDeviceToHost, st));
         // a slot holding a stale copy of this layer must be refilled
@@ -510,8 +530,8 @@ int amoe_forward_device(amoe_ctx *c, int32_t layer, const float *residual, int32
     const bool tc = use_tensor_path(c, T);
     if (tc) {
         int n = 0;
-        AMOE_CUDA(c, launch_tc_forward(d, L, c->r, T, c->act_hi, c->act_lo, c->y, c->tc_scratch, st,
-                                       &timer_hook, &timer, &n));
+        AMOE_CUDA(c, launch_tc_forward(d, L, c->r, T, c->act_hi, c->act_lo, c->y, c->tc_scratch,
+                                       c->max_tokens * d.k, st, &timer_hook, &timer, &n));
         c->stats.launches += n;
     } else {
         AMOE_CUDA(c, launch_gemv_gate_up(d, L, c->r, T, c->act_hi, c->act_lo, st));
@@ -559,7 +579,7 @@ int amoe_forward(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, f
         AMOE_CUDA(c, cudaMemcpyAsync(topk_w, c->r.topk_w, (size_t)T * d.k * 4,
                                      cudaMemcpyDeviceToHost, st));
     AMOE_CUDA(c, cudaStreamSynchronize(st));
-    return AMOE_OK;
+    return check_device_flag(c);
 }
 
 int amoe_synchronize(amoe_ctx *c) {
@@ -567,7 +587,8 @@ int amoe_synchronize(amoe_ctx *c) {
     if (rc) return rc;
     AMOE_CUDA(c, cudaStreamSynchronize(c->stream));
     AMOE_CUDA(c, cudaStreamSynchronize(c->copy_stream));
-    return AMOE_OK;
+    AMOE_CUDA(c, cudaDeviceSynchronize());
+    return check_device_flag(c);
 }
 
 int amoe_last_routing(amoe_ctx *c, float *logits, int32_t *perm_pair, int32_t *counts,

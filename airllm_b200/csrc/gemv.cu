@@ -20,7 +20,7 @@ namespace amoe {
 
 namespace {
 
-constexpr int kGemvWarps = 4;
+constexpr int kGemvWarps = 8;
 
 struct GemvParams {
     const uint8_t *q;      // tiled nibbles
@@ -68,22 +68,33 @@ __device__ __forceinline__ float swiglu(float gate, float up) {
     return g / (1.0f + expf(-1.702f * g)) * (u + 1.0f);
 }
 
+// CTA = kGemvTiles row tiles x kGemvKSplit warps each: the warps of a row tile
+// split K, keep kGemvUnroll k-tiles of weights in flight, and their partial
+// sums meet in shared memory in a fixed order (deterministic).
+constexpr int kGemvKSplit = 4;
+constexpr int kGemvTiles = 2;
+constexpr int kGemvUnroll = 4;
+
 template <bool GATE_UP, int NG>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
+    __shared__ float red[kGemvTiles][kGemvKSplit][NG][4][32];
     const int slot = blockIdx.y;
     const int n_active = p.active[p.E];
-    if (slot >= n_active) return;
+    if (slot >= n_active) return;  // uniform for the whole CTA
     const int e = p.active[slot];
     const int base = p.offsets[e];
     const int m_e = p.offsets[e + 1] - base;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile_local = warp / kGemvKSplit, ks = warp % kGemvKSplit;
     const int nrt = p.R / kTileRows;
-    const int rt = blockIdx.x * kGemvWarps + warp;
-    if (rt >= nrt) return;
+    const int rt = blockIdx.x * kGemvTiles + tile_local;
+    const bool live = rt < nrt;
     const int g = lane >> 2, c = lane & 3;
     const int nkt = p.K / kTileK;
-    const uint8_t *qt = p.q + ((size_t)e * nrt + rt) * nkt * kTileQBytes + lane * 16;
-    const uint8_t *st = p.s + ((size_t)e * nrt + rt) * nkt * kTileSBytes + 4 * g;
+    const int per = (nkt + kGemvKSplit - 1) / kGemvKSplit;
+    const int kbeg = min(nkt, ks * per), kend = min(nkt, kbeg + per);
+    const uint8_t *qt = p.q + ((size_t)e * nrt + (live ? rt : 0)) * nkt * kTileQBytes + lane * 16;
+    const uint8_t *st = p.s + ((size_t)e * nrt + (live ? rt : 0)) * nkt * kTileSBytes + 4 * g;
 
     for (int tok0 = 0; tok0 < m_e; tok0 += 8 * NG) {
         const __half *xh[NG];
@@ -106,84 +117,107 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
 #pragma unroll
             for (int i = 0; i < 4; ++i) acc[n][i] = 0.0f;
 
-        uint4 qv = ldg_nc_v4(qt);
-        uint32_t sv = ldg_nc_u32(st);
-        for (int kt = 0; kt < nkt; ++kt) {
-            uint4 qn = qv;
-            uint32_t sn = sv;
-            if (kt + 1 < nkt) {  // one k-tile of weights in flight ahead
-                qn = ldg_nc_v4(qt + (size_t)(kt + 1) * kTileQBytes);
-                sn = ldg_nc_u32(st + (size_t)(kt + 1) * kTileSBytes);
-            }
+        if (live) {
+            for (int kt0 = kbeg; kt0 < kend; kt0 += kGemvUnroll) {
+                uint4 qv[kGemvUnroll];
+                uint32_t sv[kGemvUnroll];
 #pragma unroll
-            for (int b = 0; b < 2; ++b) {
-                const uint32_t wg = b ? qv.z : qv.x;   // tile row g
-                const uint32_t wg8 = b ? qv.w : qv.y;  // tile row g+8
-                const uint32_t s0a0 = e2m1x2_to_f16x2(wg & 0xff);
-                const uint32_t s0a1 = e2m1x2_to_f16x2(wg8 & 0xff);
-                const uint32_t s0a2 = e2m1x2_to_f16x2((wg >> 8) & 0xff);
-                const uint32_t s0a3 = e2m1x2_to_f16x2((wg8 >> 8) & 0xff);
-                const uint32_t s1a0 = e2m1x2_to_f16x2((wg >> 16) & 0xff);
-                const uint32_t s1a1 = e2m1x2_to_f16x2((wg8 >> 16) & 0xff);
-                const uint32_t s1a2 = e2m1x2_to_f16x2(wg >> 24);
-                const uint32_t s1a3 = e2m1x2_to_f16x2(wg8 >> 24);
-                const float sc_g = e8m0_to_float((sv >> (8 * b)) & 0xff);
-                const float sc_g8 = e8m0_to_float((sv >> (8 * (2 + b))) & 0xff);
-#pragma unroll
-                for (int n = 0; n < NG; ++n) {
-                    if (n >= ng_live) break;
-                    uint4 h = make_uint4(0, 0, 0, 0), l = make_uint4(0, 0, 0, 0);
-                    if (valid[n]) {
-                        h = *reinterpret_cast<const uint4 *>(xh[n] + kt * kTileK + b * 32);
-                        l = *reinterpret_cast<const uint4 *>(xl[n] + kt * kTileK + b * 32);
+                for (int u = 0; u < kGemvUnroll; ++u) {
+                    if (kt0 + u < kend) {
+                        qv[u] = ldg_nc_v4(qt + (size_t)(kt0 + u) * kTileQBytes);
+                        sv[u] = ldg_nc_u32(st + (size_t)(kt0 + u) * kTileSBytes);
                     }
-                    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    mma16816(d, s0a0, s0a1, s0a2, s0a3, h.x, h.y);
-                    mma16816(d, s0a0, s0a1, s0a2, s0a3, l.x, l.y);
-                    mma16816(d, s1a0, s1a1, s1a2, s1a3, h.z, h.w);
-                    mma16816(d, s1a0, s1a1, s1a2, s1a3, l.z, l.w);
-                    acc[n][0] = fmaf(d[0], sc_g, acc[n][0]);
-                    acc[n][1] = fmaf(d[1], sc_g, acc[n][1]);
-                    acc[n][2] = fmaf(d[2], sc_g8, acc[n][2]);
-                    acc[n][3] = fmaf(d[3], sc_g8, acc[n][3]);
+                }
+#pragma unroll
+                for (int u = 0; u < kGemvUnroll; ++u) {
+                    if (kt0 + u >= kend) break;
+                    const int kt = kt0 + u;
+#pragma unroll
+                    for (int b = 0; b < 2; ++b) {
+                        const uint32_t wg = b ? qv[u].z : qv[u].x;   // tile row g
+                        const uint32_t wg8 = b ? qv[u].w : qv[u].y;  // tile row g+8
+                        const uint32_t s0a0 = e2m1x2_to_f16x2(wg & 0xff);
+                        const uint32_t s0a1 = e2m1x2_to_f16x2(wg8 & 0xff);
+                        const uint32_t s0a2 = e2m1x2_to_f16x2((wg >> 8) & 0xff);
+                        const uint32_t s0a3 = e2m1x2_to_f16x2((wg8 >> 8) & 0xff);
+                        const uint32_t s1a0 = e2m1x2_to_f16x2((wg >> 16) & 0xff);
+                        const uint32_t s1a1 = e2m1x2_to_f16x2((wg8 >> 16) & 0xff);
+                        const uint32_t s1a2 = e2m1x2_to_f16x2(wg >> 24);
+                        const uint32_t s1a3 = e2m1x2_to_f16x2(wg8 >> 24);
+                        const float sc_g = e8m0_to_float((sv[u] >> (8 * b)) & 0xff);
+                        const float sc_g8 = e8m0_to_float((sv[u] >> (8 * (2 + b))) & 0xff);
+#pragma unroll
+                        for (int n = 0; n < NG; ++n) {
+                            if (n >= ng_live) break;
+                            uint4 h = make_uint4(0, 0, 0, 0), l = make_uint4(0, 0, 0, 0);
+                            if (valid[n]) {
+                                h = *reinterpret_cast<const uint4 *>(xh[n] + kt * kTileK + b * 32);
+                                l = *reinterpret_cast<const uint4 *>(xl[n] + kt * kTileK + b * 32);
+                            }
+                            float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                            mma16816(d, s0a0, s0a1, s0a2, s0a3, h.x, h.y);
+                            mma16816(d, s0a0, s0a1, s0a2, s0a3, l.x, l.y);
+                            mma16816(d, s1a0, s1a1, s1a2, s1a3, h.z, h.w);
+                            mma16816(d, s1a0, s1a1, s1a2, s1a3, l.z, l.w);
+                            acc[n][0] = fmaf(d[0], sc_g, acc[n][0]);
+                            acc[n][1] = fmaf(d[1], sc_g, acc[n][1]);
+                            acc[n][2] = fmaf(d[2], sc_g8, acc[n][2]);
+                            acc[n][3] = fmaf(d[3], sc_g8, acc[n][3]);
+                        }
+                    }
                 }
             }
-            qv = qn;
-            sv = sn;
         }
+#pragma unroll
+        for (int n = 0; n < NG; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) red[tile_local][ks][n][i][lane] = acc[n][i];
+        __syncthreads();
 
-        // epilogue: thread holds rows (g, g+8) for tokens 2c, 2c+1 of each n-group
+        if (live && ks == 0) {
+            // fixed-order sum of the K-slices, then the epilogue: thread holds rows
+            // (g, g+8) for tokens 2c, 2c+1 of each n-group
 #pragma unroll
-        for (int n = 0; n < NG; ++n) {
-            if (n >= ng_live) break;
+            for (int n = 0; n < NG; ++n) {
+                if (n >= ng_live) break;
+                float v[4];
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int tok = tok0 + 8 * n + 2 * c + j;
-                if (tok >= m_e) continue;
-                const int pos = base + tok;
-                if (GATE_UP) {
-                    const int pr = 8 * rt + g;  // SwiGLU pair index
-                    const float gate = acc[n][j] + p.bias[(size_t)e * p.R + 2 * pr];
-                    const float up = acc[n][2 + j] + p.bias[(size_t)e * p.R + 2 * pr + 1];
-                    const float a = swiglu(gate, up);
-                    const __half hi = __float2half_rn(a);
-                    const __half lo = __float2half_rn(a - __half2float(hi));
-                    p.act_hi[(size_t)pos * (p.R / 2) + pr] = hi;
-                    p.act_lo[(size_t)pos * (p.R / 2) + pr] = lo;
-                } else {
-                    const int h = kTileRows * rt + g;
-                    p.y[(size_t)pos * p.R + h] = acc[n][j] + p.bias[(size_t)e * p.R + h];
-                    p.y[(size_t)pos * p.R + h + 8] = acc[n][2 + j] + p.bias[(size_t)e * p.R + h + 8];
+                for (int i = 0; i < 4; ++i) {
+                    float sum = red[tile_local][0][n][i][lane];
+#pragma unroll
+                    for (int q = 1; q < kGemvKSplit; ++q) sum += red[tile_local][q][n][i][lane];
+                    v[i] = sum;
+                }
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const int tok = tok0 + 8 * n + 2 * c + j;
+                    if (tok >= m_e) continue;
+                    const int pos = base + tok;
+                    if (GATE_UP) {
+                        const int pr = 8 * rt + g;  // SwiGLU pair index
+                        const float gate = v[j] + p.bias[(size_t)e * p.R + 2 * pr];
+                        const float up = v[2 + j] + p.bias[(size_t)e * p.R + 2 * pr + 1];
+                        const float a = swiglu(gate, up);
+                        const __half hi = __float2half_rn(a);
+                        const __half lo = __float2half_rn(a - __half2float(hi));
+                        p.act_hi[(size_t)pos * (p.R / 2) + pr] = hi;
+                        p.act_lo[(size_t)pos * (p.R / 2) + pr] = lo;
+                    } else {
+                        const int h = kTileRows * rt + g;
+                        p.y[(size_t)pos * p.R + h] = v[j] + p.bias[(size_t)e * p.R + h];
+                        p.y[(size_t)pos * p.R + h + 8] = v[2 + j] + p.bias[(size_t)e * p.R + h + 8];
+                    }
                 }
             }
         }
+        __syncthreads();  // red[] is rewritten by the next token pass
     }
 }
 
 template <bool GATE_UP>
 cudaError_t launch(const GemvParams &p, int T, int max_active, cudaStream_t st) {
     const int nrt = p.R / kTileRows;
-    dim3 grid((nrt + kGemvWarps - 1) / kGemvWarps, max_active);
+    dim3 grid((nrt + kGemvTiles - 1) / kGemvTiles, max_active);
     if (T <= 8)
         gemv_kernel<GATE_UP, 1><<<grid, kGemvWarps * 32, 0, st>>>(p);
     else if (T <= 16)

@@ -50,22 +50,30 @@ __device__ __forceinline__ bool better(float v1, int e1, float v2, int e2) {
 template <int NT, int EPL>
 __device__ __forceinline__ void partial_logits(const float *xn, int H, const float *wt, int E,
                                                int k0, int k1, int lane, double (&acc)[EPL][NT]) {
+    // U router rows in flight per batch: the loads of a batch are independent
+    constexpr int U = EPL >= 8 ? 2 : 8 / EPL;
 #pragma unroll
     for (int j = 0; j < EPL; ++j)
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[j][t] = 0.0;
-    for (int kk = k0; kk < k1; ++kk) {
-        double wv[EPL];
+    for (int kb = k0; kb < k1; kb += U) {
+        float wv[U][EPL];
 #pragma unroll
-        for (int j = 0; j < EPL; ++j) {
-            int e = lane + 32 * j;
-            wv[j] = e < E ? (double)__ldg(wt + (size_t)kk * E + e) : 0.0;
-        }
+        for (int u = 0; u < U; ++u)
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            double xv = (double)xn[t * H + kk];
+            for (int j = 0; j < EPL; ++j) {
+                const int e = lane + 32 * j;
+                wv[u][j] = (kb + u < k1 && e < E) ? __ldg(wt + (size_t)(kb + u) * E + e) : 0.0f;
+            }
 #pragma unroll
-            for (int j = 0; j < EPL; ++j) acc[j][t] += xv * wv[j];
+        for (int u = 0; u < U; ++u) {
+            if (kb + u >= k1) break;
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const double xv = (double)xn[t * H + kb + u];
+#pragma unroll
+                for (int j = 0; j < EPL; ++j) acc[j][t] += xv * (double)wv[u][j];
+            }
         }
     }
 }

@@ -204,6 +204,8 @@ class MoEBlock:
         st = None
         if stream is not None:
             st = stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+            if st == 0:
+                st = 1  # torch's default stream is the legacy stream (cudaStreamLegacy); NULL means "own stream"
         self._check(self._lib.amoe_forward_device(self._h, layer, _ptr(residual), T, _ptr(out),
                                                   _ptr(topk_idx), _ptr(topk_w), st))
 

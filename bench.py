@@ -203,7 +203,8 @@ def main():
     blk = moe.MoEBlock.for_layer(layer, max_tokens=T, device=local, path=args.path)
     blk.upload_layer(0, layer)
 
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     xd = torch.from_numpy(x).cuda()
     od = torch.empty_like(xd)
     idd = torch.empty((T, layer["top_k"]), dtype=torch.int32, device="cuda")
