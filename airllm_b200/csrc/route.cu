@@ -95,29 +95,75 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteParams p) 
     const int nt = min(kRouteTokens, p.T - t0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    // 1. RMSNorm of token t0 + warp (primitives.go:61-70)
-    if (warp < nt) {
-        const float *x = p.residual + (size_t)(t0 + warp) * H;
-        double ss = 0.0;
-        for (int i = lane; i < H; i += 32) {
-            double v = (double)x[i];
-            ss += v * v;
-        }
-        ss = warp_sum_f64(ss);
-        const double inv = 1.0 / sqrt(ss / (double)H + (double)p.eps);
-        const bool write_split = ks == 0;
-        for (int i = lane; i < H; i += 32) {
-            float v = (float)((double)x[i] * inv * (double)p.gain[i]);
-            xn[warp * H + i] = v;
-            if (write_split) {
-                __half hi = __float2half_rn(v);
-                __half lo = __float2half_rn(v - __half2float(hi));
-                p.o.x_hi[(size_t)(t0 + warp) * H + i] = hi;
-                p.o.x_lo[(size_t)(t0 + warp) * H + i] = lo;
+    // 1. RMSNorm (primitives.go:61-70).  All threads sweep the chunk's rows with
+    //    float4 loads (every token's loads in flight together); float64 sums of
+    //    squares per token, reduced per warp and then across warps.
+    __shared__ double ssq[kRouteWarps][kRouteTokens];
+    __shared__ double inv_s[kRouteTokens];
+    {
+        const int H4 = H / 4;
+        const float4 *res4 = reinterpret_cast<const float4 *>(p.residual + (size_t)t0 * H);
+        double ss[kRouteTokens];
+#pragma unroll
+        for (int t = 0; t < kRouteTokens; ++t) ss[t] = 0.0;
+        for (int i = threadIdx.x; i < H4; i += blockDim.x) {
+            float4 v[kRouteTokens];
+#pragma unroll
+            for (int t = 0; t < kRouteTokens; ++t)
+                if (t < nt) v[t] = __ldg(res4 + (size_t)t * H4 + i);
+#pragma unroll
+            for (int t = 0; t < kRouteTokens; ++t) {
+                if (t < nt) {
+                    ss[t] += (double)v[t].x * (double)v[t].x;
+                    ss[t] += (double)v[t].y * (double)v[t].y;
+                    ss[t] += (double)v[t].z * (double)v[t].z;
+                    ss[t] += (double)v[t].w * (double)v[t].w;
+                }
             }
         }
-    } else if (warp < kRouteTokens) {
-        for (int i = lane; i < H; i += 32) xn[warp * H + i] = 0.0f;
+#pragma unroll
+        for (int t = 0; t < kRouteTokens; ++t) {
+            const double w = warp_sum_f64(ss[t]);
+            if (lane == 0) ssq[warp][t] = w;
+        }
+        __syncthreads();
+        if (threadIdx.x < kRouteTokens) {
+            double sum = 0.0;
+            for (int w = 0; w < kRouteWarps; ++w) sum += ssq[w][threadIdx.x];
+            inv_s[threadIdx.x] = 1.0 / sqrt(sum / (double)H + (double)p.eps);
+        }
+        __syncthreads();
+        const float4 *g4 = reinterpret_cast<const float4 *>(p.gain);
+        const bool write_split = ks == 0;
+        for (int i = threadIdx.x; i < H4; i += blockDim.x) {
+            const float4 g = __ldg(g4 + i);
+#pragma unroll
+            for (int t = 0; t < kRouteTokens; ++t) {
+                float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (t < nt) {
+                    const float4 x = __ldg(res4 + (size_t)t * H4 + i);
+                    const double inv = inv_s[t];
+                    // float32(float64(x) * inverseRMS * float64(g)), evaluated left to right
+                    o.x = (float)((double)x.x * inv * (double)g.x);
+                    o.y = (float)((double)x.y * inv * (double)g.y);
+                    o.z = (float)((double)x.z * inv * (double)g.z);
+                    o.w = (float)((double)x.w * inv * (double)g.w);
+                    if (write_split) {
+                        const __half2 h01 = __floats2half2_rn(o.x, o.y), h23 = __floats2half2_rn(o.z, o.w);
+                        const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+                        const __half2 l01 = __floats2half2_rn(o.x - f01.x, o.y - f01.y);
+                        const __half2 l23 = __floats2half2_rn(o.z - f23.x, o.w - f23.y);
+                        __half2 *dh = reinterpret_cast<__half2 *>(p.o.x_hi + (size_t)(t0 + t) * H + 4 * i);
+                        __half2 *dl = reinterpret_cast<__half2 *>(p.o.x_lo + (size_t)(t0 + t) * H + 4 * i);
+                        dh[0] = h01;
+                        dh[1] = h23;
+                        dl[0] = l01;
+                        dl[1] = l23;
+                    }
+                }
+                reinterpret_cast<float4 *>(xn + t * H)[i] = o;
+            }
+        }
     }
     for (int e = threadIdx.x; e < E; e += blockDim.x) hist_s[e] = 0;
     __syncthreads();
@@ -241,6 +287,35 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteParams p) 
     }
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) p.o.hist[(size_t)chunk * E + e] = hist_s[e];
+    if (gridDim.x == 1) {
+        // T <= kRouteTokens: this CTA holds every pair, so it also writes the
+        // stable (expert, token, slot) permutation and the launch of K2 is skipped.
+        __shared__ int offs[257];
+        const int npairs = p.T * p.k;
+        if (threadIdx.x == 0) {
+            int acc = 0, na = 0;
+            for (int e = 0; e < E; ++e) {
+                offs[e] = acc;
+                p.o.offsets[e] = acc;
+                p.o.counts[e] = hist_s[e];
+                p.o.chunk_base[e] = acc;
+                if (hist_s[e] > 0) p.o.active[na++] = e;
+                acc += hist_s[e];
+            }
+            offs[E] = acc;
+            p.o.offsets[E] = acc;
+            p.o.active[E] = na;
+        }
+        __syncthreads();
+        for (int q = threadIdx.x; q < npairs; q += blockDim.x) {
+            const int ex = p.o.topk_idx[q];
+            int rank = 0;
+            for (int r = 0; r < q; ++r) rank += p.o.topk_idx[r] == ex;
+            const int pos = offs[ex] + rank;
+            p.o.perm_pair[pos] = q;
+            p.o.inv[q] = pos;
+        }
+    }
 }
 
 // K2: one CTA.  Column scan of the per-chunk expert histograms, then every pair
@@ -369,6 +444,7 @@ cudaError_t launch_route_impl(const Dims &d, const LayerDev &L, const float *res
     err = cudaGetLastError();
     if (err != cudaSuccess) return err;
     if (hook) hook(hook_arg, 0);
+    if (nchunk == 1) return cudaSuccess;  // permutation written by route_kernel
     const int threads = 1024;
     const int groups = threads / d.E > 0 ? threads / d.E : 1;
     const size_t psmem = (size_t)(groups * d.E + d.E + d.E + 1) * sizeof(int);
