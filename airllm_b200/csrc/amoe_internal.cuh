@@ -8,6 +8,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string>
+
 namespace amoe {
 
 // ---------------------------------------------------------------------------
@@ -117,6 +119,9 @@ int32_t *tc_error_flag(void *tc_scratch, int max_pairs, int H);
 // Combine --------------------------------------------------------------------
 cudaError_t launch_combine(const Dims &d, const float *residual, const RouteOut &r,
                            const float *y, int T, float *out, cudaStream_t st);
+
+// Sets the message amoe_last_error(NULL) returns on the calling thread.
+void set_thread_error(const std::string &msg);
 
 // Shared device helpers ---------------------------------------------------------
 __device__ __forceinline__ float e8m0_to_float(uint32_t b) {

@@ -74,6 +74,9 @@ LayerDev layer_view(uint8_t *base, const LayerBlock &b) {
 }
 
 }  // namespace
+
+void set_thread_error(const std::string &msg) { g_create_error = msg; }
+
 }  // namespace amoe
 
 using namespace amoe;

@@ -79,6 +79,8 @@ SIGNATURES = {
     "amoe_last_routing": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp]),
     "amoe_set_profiling": (ctypes.c_int, [_vp, _i32]),
     "amoe_get_stats": (ctypes.c_int, [_vp, ctypes.POINTER(AmoeStats), _i32]),
+    "amoe_route_noalloc": (ctypes.c_int, [_i32, _i32, _i32, _i32, ctypes.c_float, _vp, _i32, _vp, _vp, _vp,
+                                          _vp, _vp, _vp, _vp]),
 }
 
 _lib = None

@@ -79,8 +79,9 @@ AMOE_API int amoe_create(const amoe_config *cfg, amoe_ctx **out);
 /* Releases everything the context owns.  NULL is a no-op. */
 AMOE_API void amoe_destroy(amoe_ctx *ctx);
 
-/* Description of the last failure on ctx (ctx NULL: last amoe_create failure
- * on this thread).  Valid until the next call on the same context. */
+/* Description of the last failure on ctx (ctx NULL: the last failure of a
+ * context-free call -- amoe_create, amoe_route_noalloc -- on this thread).
+ * Valid until the next call on the same context. */
 AMOE_API const char *amoe_last_error(const amoe_ctx *ctx);
 
 /* Replaces: loadDecoderLayer's MoE tensors (weights.go:52-54, 80, 84-116) and
@@ -146,6 +147,28 @@ AMOE_API int amoe_set_profiling(amoe_ctx *ctx, int32_t on);
 /* Synchronises, folds finished stage timings into the counters and copies
  * them out; reset != 0 clears the counters afterwards. */
 AMOE_API int amoe_get_stats(amoe_ctx *ctx, amoe_stats *out, int32_t reset);
+
+/* No counterpart in the reference: the routing step (RMSNorm, router
+ * LinearBias, top-k, selected softmax -- the same kernels and results as the
+ * routing inside amoe_forward) for callers that cannot allocate device memory,
+ * e.g. a runtime that plans all device memory up front and hands out fixed
+ * regions, or a process whose GPU memory is already reserved by another
+ * allocator.  It needs no context and calls no cudaMalloc/cudaFree: its scratch
+ * is one fixed device array of 4.1 MB that every GPU loading this library holds
+ * until exit.  Limits: 1 <= T <= 64, hidden a multiple of 64 up to 4096,
+ * experts <= 128, top_k <= min(experts, 32); larger sizes return
+ * AMOE_ERR_INVALID with a message in amoe_last_error(NULL).
+ *   residual [T x H], norm_gain [H], router_w [E x H] (GGUF layout), router_b [E]:
+ *     device inputs;  logits [T x E], topk_idx [T x k], topk_w [T x k]: device outputs.
+ * Enqueued on `stream` (a cudaStream_t; NULL = the legacy default stream).
+ * The first call on a device resolves the array's device address; make that
+ * first call before any stream capture.  All calls share the array and it
+ * keeps the last call's contents (the counters that must start at zero are
+ * cleared by each call), so calls that overlap on the GPU race. */
+AMOE_API int amoe_route_noalloc(int32_t device, int32_t hidden, int32_t experts, int32_t top_k,
+                                float rms_eps, const float *residual, int32_t T,
+                                const float *norm_gain, const float *router_w, const float *router_b,
+                                float *logits, int32_t *topk_idx, float *topk_w, void *stream);
 
 /* ABI version (AMOE_ABI_VERSION). */
 AMOE_API int amoe_abi_version(void);
