@@ -18,8 +18,8 @@
 //     = activations as an fp16 hi + lo split (x ~= hi + lo), TMA SWIZZLE_128B;
 //       two MMAs (hi, lo) per k-step accumulate into the same TMEM tile.
 //   D = f32 in TMEM, 128 lanes x N columns per UMMA, double-buffered.
-// Warp roles: 0 TMA producer, 1 MMA issuer (+TMEM owner), 2-5 converters,
-// 6-9 epilogue.  Persistent CTAs walk the tile list (expert-major, then
+// Warp roles: 0 TMA producer, 1 MMA issuer (+TMEM owner), 2-9 converters,
+// 10-13 epilogue.  Persistent CTAs walk the tile list (expert-major, then
 // 256-row weight block, then token block).  Every mbarrier wait is bounded;
 // on timeout the kernel records an error code and unwinds.
 #include "amoe_internal.cuh"
@@ -38,7 +38,7 @@ constexpr int MT = 2;                   // UMMAs per CTA tile along M
 constexpr int BN = 128;                 // max tokens per CTA tile (UMMA N)
 constexpr int BK = 64;                  // K per pipeline stage (one 128-B swizzle atom)
 constexpr int STAGES = 3;               // TMA ring depth
-constexpr int CSTAGES = 2;              // converted-A ring depth
+constexpr int CSTAGES = 3;              // converted-A ring depth
 constexpr int ROWS = BM * MT;           // 256 weight rows per CTA tile
 constexpr int ROW_TILES = ROWS / kTileRows;  // 16 fragment tiles per stage
 constexpr int B_BYTES = BN * BK * 2;         // 16 KB (hi or lo)
@@ -47,13 +47,16 @@ constexpr int ASC_BYTES = ROW_TILES * kTileSBytes;   // 512 B
 constexpr int ACONV_MT_BYTES = BM * BK * 2;          // 16 KB per UMMA A tile
 constexpr int ACONV_BYTES = MT * ACONV_MT_BYTES;     // 32 KB
 constexpr int TX_BYTES = 2 * B_BYTES + ARAW_BYTES + ASC_BYTES;
-constexpr int NUM_THREADS = 320;
+constexpr int CONV_WARPS = 8;           // converter warps (two per scheduler)
+constexpr int CONV_THREADS = 32 * CONV_WARPS;
+constexpr int EPI_WARP0 = 2 + CONV_WARPS;  // first of the 4 epilogue warps
+constexpr int NUM_THREADS = 32 * (EPI_WARP0 + 4);
 constexpr int TMEM_COLS = 512;          // 2 buffers x MT x BN
 constexpr int MAX_E = 256;
 
 constexpr size_t SMEM_BYTES = 1024 /*alignment slack*/ + CSTAGES * ACONV_BYTES +
                               STAGES * (2 * B_BYTES + ARAW_BYTES + ASC_BYTES) +
-                              (2 * STAGES + 8) * 8 /*barriers*/ + 16 + (MAX_E + 1) * 4;
+                              (2 * STAGES + 2 * CSTAGES + 4) * 8 /*barriers*/ + 16 + (MAX_E + 1) * 4;
 
 static_assert(2 * MT * BN <= TMEM_COLS, "TMEM budget");
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -173,18 +176,25 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// f16x2 holding 2^(s - 127 - c) twice; 0 below fp16's range, NaN for s == 255.
+// f16x2 holding 2^(s - 127 - c) twice: built as an f32 power of two (biased
+// exponent s - c <= 140) and rounded to fp16 (0 below fp16's range); NaN for 255.
 __device__ __forceinline__ uint32_t scale_f16x2(uint32_t s, int c) {
-    uint32_t h;
-    if (s == 255u) {
-        h = 0x7E00u;
-    } else {
-        const int e = (int)s - 127 - c;  // <= 13 by the choice of c
-        if (e >= -14) h = (uint32_t)(e + 15) << 10;
-        else if (e >= -24) h = 1u << (e + 24);
-        else h = 0u;
-    }
-    return h | (h << 16);
+    const int ex = (int)s - c;
+    float f = __uint_as_float(ex > 0 ? (uint32_t)ex << 23 : 0u);
+    if (s == 255u) f = __uint_as_float(0x7fc00000u);
+    const __half2 h = __float2half2_rn(f);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// Eight E2M1 values (four bytes, low nibble first) -> four f16x2.
+__device__ __forceinline__ uint4 e2m1x8_to_f16(uint32_t w) {
+    uint4 o;
+    asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+        " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+        " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
+        : "=r"(o.x), "=r"(o.y), "=r"(o.z), "=r"(o.w)
+        : "r"(w));
+    return o;
 }
 
 __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
@@ -237,8 +247,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint8_t *asc = araw + STAGES * ARAW_BYTES;
     uint64_t *bars = reinterpret_cast<uint64_t *>(asc + STAGES * ASC_BYTES);
     uint64_t *full = bars, *empty = bars + STAGES;
-    uint64_t *cfull = bars + 2 * STAGES, *cempty = cfull + 2;
-    uint64_t *afull = cempty + 2, *aempty = afull + 2;
+    uint64_t *cfull = bars + 2 * STAGES, *cempty = cfull + CSTAGES;
+    uint64_t *afull = cempty + CSTAGES, *aempty = afull + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(aempty + 2);
     int *tile_start = reinterpret_cast<int *>(tmem_slot + 4);
 
@@ -247,13 +257,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(full + s, 1);
-            mbar_init(empty + s, 1 + 128);  // MMA commit + every converter thread
+            mbar_init(empty + s, 1 + CONV_THREADS);  // MMA commit + every converter thread
         }
-        for (int c = 0; c < 2; ++c) {
-            mbar_init(cfull + c, 128);
+        for (int c = 0; c < CSTAGES; ++c) {
+            mbar_init(cfull + c, CONV_THREADS);
             mbar_init(cempty + c, 1);
-            mbar_init(afull + c, 1);
-            mbar_init(aempty + c, 128);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(afull + b, 1);
+            mbar_init(aempty + b, 128);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -337,9 +349,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 umma_commit(afull + buf);
             }
         }
-    } else if (warp < 6) {
+    } else if (warp < EPI_WARP0) {
         // ---------------- converters: raw MXFP4 tiles -> fp16 SW128 A tiles ----------------
-        const int ct = threadIdx.x - 64;  // 0..127
+        const int ct = threadIdx.x - 64;  // 0..CONV_THREADS-1
         int it = 0, cit = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
             const TileInfo ti = decode_tile(t, tile_start, p.offsets, E, p.mblocks);
@@ -352,26 +364,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 const uint8_t *ss = asc + s * ASC_BYTES;
                 uint8_t *dst = aconv + cs * ACONV_BYTES;
 #pragma unroll
-                for (int task = 0; task < 4; ++task) {
-                    const int chunk = ct + 128 * task;  // 0..511
+                for (int task = 0; task < (ROW_TILES * 32) / CONV_THREADS; ++task) {
+                    const int chunk = ct + CONV_THREADS * task;  // one 16-B lane chunk of a fragment tile
                     const int rtl = chunk >> 5, ln = chunk & 31;
                     const int g = ln >> 2, c = ln & 3;
                     const uint4 raw = *reinterpret_cast<const uint4 *>(rs + rtl * kTileQBytes + ln * 16);
                     const uint32_t scl = *reinterpret_cast<const uint32_t *>(ss + rtl * kTileSBytes + 4 * g);
-                    const int m = rtl >> 3;
+                    uint8_t *mt = dst + (rtl >> 3) * ACONV_MT_BYTES;
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         const int row = (rtl & 7) * 16 + g + 8 * h;  // row within the UMMA A tile
-                        uint8_t *rowp = dst + m * ACONV_MT_BYTES + row * 128;
+                        uint8_t *rowp = mt + row * 128;
 #pragma unroll
-                        for (int b = 0; b < 2; ++b) {
+                        for (int bb = 0; bb < 2; ++bb) {
+                            // odd rows store their blocks in the other order, so the 8 lanes of
+                            // each quarter-warp hit 8 distinct 16-B slots of the swizzled rows
+                            const int b = bb ^ (g & 1);
                             const uint32_t w = b ? (h ? raw.w : raw.z) : (h ? raw.y : raw.x);
                             const uint32_t sc = scale_f16x2((scl >> (8 * (2 * h + b))) & 0xffu, ce);
-                            uint4 o;
-                            o.x = hmul2_bits(e2m1x2_to_f16x2(w & 0xffu), sc);
-                            o.y = hmul2_bits(e2m1x2_to_f16x2((w >> 8) & 0xffu), sc);
-                            o.z = hmul2_bits(e2m1x2_to_f16x2((w >> 16) & 0xffu), sc);
-                            o.w = hmul2_bits(e2m1x2_to_f16x2(w >> 24), sc);
+                            uint4 o = e2m1x8_to_f16(w);
+                            o.x = hmul2_bits(o.x, sc);
+                            o.y = hmul2_bits(o.y, sc);
+                            o.z = hmul2_bits(o.z, sc);
+                            o.w = hmul2_bits(o.w, sc);
                             const int chunk16 = 4 * b + c;  // 16-B chunk of the 128-B row (k = 32b + 8c ..)
                             *reinterpret_cast<uint4 *>(rowp + ((chunk16 ^ (row & 7)) << 4)) = o;
                         }
@@ -385,6 +400,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     } else {
         // ---------------- epilogue: TMEM -> bias (+SwiGLU) -> global ----------------
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        const int g16 = lane & 15;   // row within its 16-row fragment tile
+        const bool gate_lane = g16 < 8;
         int tc = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x, ++tc) {
             const TileInfo ti = decode_tile(t, tile_start, p.offsets, E, p.mblocks);
@@ -398,27 +415,46 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int m = 0; m < MT; ++m) {
                 const int rrow = ti.mb * ROWS + m * BM + 32 * q + lane;  // tile-order weight row
                 const bool row_ok = rrow < p.R;
+                // gate_up: a gate lane (tile row g) and the up lane 8 above it share pair pr;
+                // the gate lane finishes even tokens and the up lane odd ones.
+                const int pr = (rrow >> 4) * 8 + (g16 & 7);
+                float bg = 0.0f, bu = 0.0f, bd = 0.0f;
+                if (row_ok) {
+                    if (p.gate_up) {
+                        bg = bias[2 * pr];
+                        bu = bias[2 * pr + 1];
+                    } else {
+                        bd = bias[rrow];
+                    }
+                }
                 for (int col0 = 0; col0 < n16; col0 += 16) {
                     uint32_t v[16];
                     tmem_ld16(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)((buf * MT + m) * BN + col0), v);
+                    if (p.gate_up) {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int tok = col0 + j;
-                        const float val = __uint_as_float(v[j]) * scale;
-                        if (p.gate_up) {
-                            const float up = __shfl_down_sync(0xffffffffu, val, 8);
-                            const int g16 = rrow & 15;
-                            if (tok < ti.ntok && row_ok && g16 < 8) {
-                                const int pr = (rrow >> 4) * 8 + g16;  // SwiGLU pair index
-                                const float a = swiglu(val + bias[2 * pr], up + bias[2 * pr + 1]);
+                        for (int jj = 0; jj < 8; ++jj) {
+                            const float x0 = __uint_as_float(v[2 * jj]) * scale;
+                            const float x1 = __uint_as_float(v[2 * jj + 1]) * scale;
+                            const float from_up = __shfl_down_sync(0xffffffffu, x0, 8);
+                            const float from_gate = __shfl_up_sync(0xffffffffu, x1, 8);
+                            const float gv = gate_lane ? x0 : from_gate;
+                            const float uv = gate_lane ? from_up : x1;
+                            const int tok = col0 + 2 * jj + (gate_lane ? 0 : 1);
+                            if (tok < ti.ntok && row_ok) {
+                                const float a = swiglu(gv + bg, uv + bu);
                                 const __half hi = __float2half_rn(a);
                                 const __half lo = __float2half_rn(a - __half2float(hi));
                                 const size_t o = (size_t)(ti.pos0 + tok) * (p.R / 2) + pr;
                                 p.act_hi[o] = hi;
                                 p.act_lo[o] = lo;
                             }
-                        } else if (tok < ti.ntok && row_ok) {
-                            p.y[(size_t)(ti.pos0 + tok) * p.R + rrow] = val + bias[rrow];
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int tok = col0 + j;
+                            if (tok < ti.ntok && row_ok)
+                                p.y[(size_t)(ti.pos0 + tok) * p.R + rrow] = __uint_as_float(v[j]) * scale + bd;
                         }
                     }
                 }
