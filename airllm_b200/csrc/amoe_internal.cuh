@@ -44,7 +44,7 @@ constexpr int kTileSBytes = 32;
 
 struct LayerDev {
     float *norm_gain = nullptr;   // [H]
-    float *router_wt = nullptr;   // [H x E]  (transposed: lane-per-expert loads coalesce)
+    float *router_w = nullptr;    // [E x H]  (GGUF layout)
     float *router_b = nullptr;    // [E]
     uint8_t *gu_q = nullptr;      // [E][2I/16][H/64][512]
     uint8_t *gu_s = nullptr;      // [E][2I/16][H/64][32]
@@ -86,6 +86,11 @@ typedef void (*StageHook)(void *arg, int stage);
 cudaError_t launch_route_impl(const Dims &d, const LayerDev &L, const float *residual, int T,
                               const RouteOut &o, double *partial, int32_t *arrivals,
                               cudaStream_t st, StageHook hook = nullptr, void *hook_arg = nullptr);
+// Stable token->expert positions (perm_pair, inv) from the chunk bases; with
+// gather, also the expert-sorted copy of x_hi/x_lo.  Needed when T > 8 (the
+// router writes the permutation itself for a single chunk) or for the gather.
+cudaError_t launch_scatter(const Dims &d, int T, const RouteOut &o, bool gather, __half *xp_hi,
+                           __half *xp_lo, cudaStream_t st);
 // Largest number of doubles the split-K partial buffer needs for any T <= max_tokens.
 size_t route_partial_elems(int max_tokens, int H, int E);
 
@@ -93,13 +98,12 @@ size_t route_partial_elems(int max_tokens, int H, int E);
 // gguf: E*R*(K/32)*17 bytes on the device.  pair_rows: gate_up row re-order.
 cudaError_t launch_repack(const uint8_t *gguf, int E, int R, int K, bool pair_rows,
                           uint8_t *q, uint8_t *s, cudaStream_t st);
-cudaError_t launch_transpose_router(const float *w, int E, int H, float *wt, cudaStream_t st);
 
 // Expert GEMV (decode) ---------------------------------------------------------
 cudaError_t launch_gemv_gate_up(const Dims &d, const LayerDev &L, const RouteOut &r, int T,
-                                __half *act_hi, __half *act_lo, cudaStream_t st);
+                                __half *act_hi, __half *act_lo, int32_t *err, cudaStream_t st);
 cudaError_t launch_gemv_down(const Dims &d, const LayerDev &L, const RouteOut &r, int T,
-                             const __half *act_hi, const __half *act_lo, float *y,
+                             const __half *act_hi, const __half *act_lo, float *y, int32_t *err,
                              cudaStream_t st);
 
 // tcgen05 grouped GEMM (prefill) -------------------------------------------------

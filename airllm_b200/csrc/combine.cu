@@ -1,5 +1,5 @@
 // combine.cu -- K6: routing-weighted combine and residual add, and the K8
-// upload-time kernels (MXFP4 repack, router transpose).
+// upload-time MXFP4 repack.
 #include "amoe_internal.cuh"
 
 namespace amoe {
@@ -78,13 +78,6 @@ __global__ void repack_kernel(const uint8_t *__restrict__ gguf, int E, int R, in
     }
 }
 
-__global__ void transpose_kernel(const float *__restrict__ w, int E, int H, float *__restrict__ wt) {
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (long long)E * H) return;
-    const int e = (int)(i / H), h = (int)(i % H);
-    wt[(size_t)h * E + e] = w[i];
-}
-
 }  // namespace
 
 cudaError_t launch_combine(const Dims &d, const float *residual, const RouteOut &r,
@@ -99,12 +92,6 @@ cudaError_t launch_repack(const uint8_t *gguf, int E, int R, int K, bool pair_ro
     const int threads = 256;
     const long long blocks = (total + threads - 1) / threads;
     repack_kernel<<<(unsigned)blocks, threads, 0, st>>>(gguf, E, R, K, pair_rows ? 1 : 0, q, s);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_transpose_router(const float *w, int E, int H, float *wt, cudaStream_t st) {
-    const long long n = (long long)E * H;
-    transpose_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w, E, H, wt);
     return cudaGetLastError();
 }
 

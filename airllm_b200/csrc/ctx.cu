@@ -28,7 +28,7 @@ struct Status {
 
 struct LayerBlock {
     // byte offsets inside one layer's device-format block (256-B aligned parts)
-    size_t norm, router_wt, router_b, gu_b, dn_b, gu_cexp, dn_cexp, gu_s, dn_s, gu_q, dn_q, total;
+    size_t norm, router_w, router_b, gu_b, dn_b, gu_cexp, dn_cexp, gu_s, dn_s, gu_q, dn_q, total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -43,7 +43,7 @@ LayerBlock layer_block(const Dims &d) {
     };
     const size_t H = d.H, I = d.I, E = d.E;
     b.norm = take(H * 4);
-    b.router_wt = take(H * E * 4);
+    b.router_w = take(H * E * 4);
     b.router_b = take(E * 4);
     b.gu_b = take(E * 2 * I * 4);
     b.dn_b = take(E * H * 4);
@@ -60,7 +60,7 @@ LayerBlock layer_block(const Dims &d) {
 LayerDev layer_view(uint8_t *base, const LayerBlock &b) {
     LayerDev L;
     L.norm_gain = reinterpret_cast<float *>(base + b.norm);
-    L.router_wt = reinterpret_cast<float *>(base + b.router_wt);
+    L.router_w = reinterpret_cast<float *>(base + b.router_w);
     L.router_b = reinterpret_cast<float *>(base + b.router_b);
     L.gu_b = reinterpret_cast<float *>(base + b.gu_b);
     L.dn_b = reinterpret_cast<float *>(base + b.dn_b);
@@ -436,11 +436,9 @@ int amoe_upload_layer(amoe_ctx *c, int32_t layer, const float *norm_gain, const 
     // Device-format block: built in a temporary device buffer, then kept there
     // (resident) or copied to pinned host memory (streaming).
     uint8_t *blockp = nullptr, *staging = nullptr;
-    float *router_tmp = nullptr;
     const size_t stage_bytes = gu_bytes > dn_bytes ? gu_bytes : dn_bytes;
     auto cleanup = [&]() {
         if (staging) cudaFree(staging);
-        if (router_tmp) cudaFree(router_tmp);
         if (streaming(c) && blockp) cudaFree(blockp);
     };
     cudaError_t e;
@@ -466,12 +464,10 @@ int amoe_upload_layer(amoe_ctx *c, int32_t layer, const float *norm_gain, const 
         UP_CUDA(cudaMalloc(&blockp, c->blk.total));
     }
     UP_CUDA(cudaMalloc(&staging, stage_bytes));
-    UP_CUDA(cudaMalloc(&router_tmp, E * H * 4));
     const LayerDev L = layer_view(blockp, c->blk);
     cudaStream_t st = c->stream;
     UP_CUDA(cudaMemcpyAsync(L.norm_gain, norm_gain, H * 4, cudaMemcpyHostToDevice, st));
-    UP_CUDA(cudaMemcpyAsync(router_tmp, router_w, E * H * 4, cudaMemcpyHostToDevice, st));
-    UP_CUDA(launch_transpose_router(router_tmp, (int)E, (int)H, L.router_wt, st));
+    UP_CUDA(cudaMemcpyAsync(L.router_w, router_w, E * H * 4, cudaMemcpyHostToDevice, st));
     UP_CUDA(cudaMemcpyAsync(L.router_b, router_b, E * 4, cudaMemcpyHostToDevice, st));
     UP_CUDA(cudaMemcpyAsync(L.gu_b, gate_up_b, E * 2 * I * 4, cudaMemcpyHostToDevice, st));
     UP_CUDA(cudaMemcpyAsync(L.dn_b, down_b, E * H * 4, cudaMemcpyHostToDevice, st));
@@ -529,17 +525,24 @@ int amoe_forward_device(amoe_ctx *c, int32_t layer, const float *residual, int32
     const Dims &d = c->d;
     StageTimer timer(c, st);
     AMOE_CUDA(c, launch_route_impl(d, L, residual, T, c->r, c->partial, c->arrivals, st, &timer_hook, &timer));
-    c->stats.launches += 2;
+    const int nchunk = (T + kRouteTokens - 1) / kRouteTokens;
+    c->stats.launches += nchunk > 1 ? 2 : 1;
     const bool tc = use_tensor_path(c, T);
+    if (!tc && nchunk > 1) {
+        AMOE_CUDA(c, launch_scatter(d, T, c->r, false, nullptr, nullptr, st));
+        c->stats.launches += 1;
+    }
+    timer.mark(1);
     if (tc) {
         int n = 0;
         AMOE_CUDA(c, launch_tc_forward(d, L, c->r, T, c->act_hi, c->act_lo, c->y, c->tc_scratch,
                                        c->max_tokens * d.k, st, &timer_hook, &timer, &n));
         c->stats.launches += n;
     } else {
-        AMOE_CUDA(c, launch_gemv_gate_up(d, L, c->r, T, c->act_hi, c->act_lo, st));
+        int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H);
+        AMOE_CUDA(c, launch_gemv_gate_up(d, L, c->r, T, c->act_hi, c->act_lo, flag, st));
         timer.mark(2);
-        AMOE_CUDA(c, launch_gemv_down(d, L, c->r, T, c->act_hi, c->act_lo, c->y, st));
+        AMOE_CUDA(c, launch_gemv_down(d, L, c->r, T, c->act_hi, c->act_lo, c->y, flag, st));
         timer.mark(3);
         c->stats.launches += 2;
     }

@@ -472,25 +472,6 @@ done:
     }
 }
 
-// x_perm[pos] = x[token(pos)] for the gate_up B operand (hi and lo planes).
-__global__ void gather_rows_kernel(const __half *__restrict__ x_hi, const __half *__restrict__ x_lo,
-                                   const int32_t *__restrict__ perm_pair, int k, int H, int P,
-                                   __half *__restrict__ out_hi, __half *__restrict__ out_lo) {
-    const int warps = blockDim.x >> 5;
-    const int pos = blockIdx.x * warps + (threadIdx.x >> 5);
-    if (pos >= P) return;
-    const int lane = threadIdx.x & 31;
-    const int tok = perm_pair[pos] / k;
-    const uint4 *sh = reinterpret_cast<const uint4 *>(x_hi + (size_t)tok * H);
-    const uint4 *sl = reinterpret_cast<const uint4 *>(x_lo + (size_t)tok * H);
-    uint4 *dh = reinterpret_cast<uint4 *>(out_hi + (size_t)pos * H);
-    uint4 *dl = reinterpret_cast<uint4 *>(out_lo + (size_t)pos * H);
-    for (int i = lane; i < H / 8; i += 32) {
-        dh[i] = sh[i];
-        dl[i] = sl[i];
-    }
-}
-
 // Per-expert exponent bias for the fp16 weight expansion: c = max finite E8M0
 // byte - 140, so the largest scaled E2M1 value (6 * 2^13) still fits fp16 and
 // every block within 36 binades of it is exact.
@@ -612,11 +593,10 @@ cudaError_t launch_tc_forward(const Dims &d, const LayerDev &L, const RouteOut &
         attr_set = true;
     }
     const TcScratch ts = carve(tc_scratch, max_pairs, d.H);
-    const int P = T * d.k;
     *launches = 0;
-    // 1. expert-sorted fp16 hi/lo copy of the normalized rows (gate_up B operand)
-    gather_rows_kernel<<<(P + 7) / 8, 256, 0, st>>>(r.x_hi, r.x_lo, r.perm_pair, d.k, d.H, P, ts.xp_hi, ts.xp_lo);
-    cudaError_t e = cudaGetLastError();
+    // 1. stable token->expert positions and the expert-sorted fp16 hi/lo copy of the
+    //    normalized rows (the gate_up B operand)
+    cudaError_t e = launch_scatter(d, T, r, true, ts.xp_hi, ts.xp_lo, st);
     if (e != cudaSuccess) return e;
     ++*launches;
     if (hook) hook(hook_arg, 5);

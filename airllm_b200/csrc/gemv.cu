@@ -6,8 +6,8 @@
 //   y       = act . W_dn^T + b_dn                             (layer.go:179-187)
 // directly from the tiled MXFP4 planes (no dequantised copy in memory).
 //
-// One warp owns a 16-row weight tile and streams it once over K; the per-
-// expert tokens ride along as the n=8 columns of mma.sync.m16n8k16 (up to
+// Warps own a 16-row weight tile's K-range and stream it once from HBM; the
+// per-expert tokens ride along as the n=8 columns of mma.sync.m16n8k16 (up to
 // 8*NG tokens per pass).  Each MXFP4 byte becomes an f16x2 A-fragment register
 // with one cvt.rn.f16x2.e2m1x2 (E2M1 values are exact in fp16); the E8M0 block
 // scale is applied to the f32 partial of each 32-value block, so the scale
@@ -32,6 +32,7 @@ struct GemvParams {
     const int32_t *offsets;
     const int32_t *active;
     int R, K, E, k;
+    int32_t *err;  // set when a bounded wait gives up
     // outputs
     __half *act_hi, *act_lo;  // gate_up: [P][R/2]
     float *y;                 // down:    [P][R]
@@ -68,16 +69,54 @@ __device__ __forceinline__ float swiglu(float gate, float up) {
     return g / (1.0f + expf(-1.702f * g)) * (u + 1.0f);
 }
 
-// CTA = kGemvTiles row tiles x kGemvKSplit warps each: the warps of a row tile
-// split K, keep kGemvUnroll k-tiles of weights in flight, and their partial
-// sums meet in shared memory in a fixed order (deterministic).
+// CTA = kGemvTiles row tiles x kGemvKSplit warps each.  Each warp owns a
+// contiguous K-range of one row tile: one elected lane brings that range's
+// nibbles and scales to shared memory with two cp.async.bulk copies on the
+// warp's mbarrier (a single round trip to HBM, no registers held), and the
+// weights then serve every token pass.  The warps' partial sums meet in shared
+// memory in a fixed order (deterministic).
 constexpr int kGemvKSplit = 4;
 constexpr int kGemvTiles = 2;
-constexpr int kGemvUnroll = 4;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Bounded mbarrier wait (about a second of clock); false after recording a timeout.
+__device__ __forceinline__ bool gemv_wait(uint64_t *bar, int32_t *err) {
+    const long long t0 = clock64();
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n selp.u32 %0, 1, 0, p;\n}"
+            : "=r"(ok)
+            : "r"(smem_addr(bar))
+            : "memory");
+        if (ok) return true;
+        if (clock64() - t0 > 2000000000LL) {
+            atomicCAS(err, 0, 20);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+
+size_t gemv_smem_bytes(int K) {
+    const int nkt = K / kTileK;
+    const int per = (nkt + kGemvKSplit - 1) / kGemvKSplit;
+    return (size_t)kGemvTiles * kGemvKSplit * per * (kTileQBytes + kTileSBytes) + kGemvTiles * kGemvKSplit * 8;
+}
 
 template <bool GATE_UP, int NG>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
     __shared__ float red[kGemvTiles][kGemvKSplit][NG][4][32];
+    extern __shared__ __align__(128) uint8_t wsm[];
     const int slot = blockIdx.y;
     const int n_active = p.active[p.E];
     if (slot >= n_active) return;  // uniform for the whole CTA
@@ -93,8 +132,28 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
     const int nkt = p.K / kTileK;
     const int per = (nkt + kGemvKSplit - 1) / kGemvKSplit;
     const int kbeg = min(nkt, ks * per), kend = min(nkt, kbeg + per);
-    const uint8_t *qt = p.q + ((size_t)e * nrt + (live ? rt : 0)) * nkt * kTileQBytes + lane * 16;
-    const uint8_t *st = p.s + ((size_t)e * nrt + (live ? rt : 0)) * nkt * kTileSBytes + 4 * g;
+    // this warp's weights: [per][512] nibbles then [per][32] scales, then the mbarriers
+    uint8_t *wq = wsm + (size_t)warp * per * (kTileQBytes + kTileSBytes);
+    uint8_t *ws = wq + (size_t)per * kTileQBytes;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(wsm + (size_t)kGemvWarps * per * (kTileQBytes + kTileSBytes)) + warp;
+    const int nk = kend - kbeg;
+    bool have = false;
+    if (live && nk > 0) {
+        if (lane == 0) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar)));
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+            const size_t tile0 = ((size_t)e * nrt + rt) * nkt + kbeg;
+            const uint32_t qb = (uint32_t)nk * kTileQBytes, sb = (uint32_t)nk * kTileSBytes;
+            asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}" ::"r"(
+                             smem_addr(bar)),
+                         "r"(qb + sb)
+                         : "memory");
+            bulk_g2s(wq, p.q + tile0 * kTileQBytes, qb, bar);
+            bulk_g2s(ws, p.s + tile0 * kTileSBytes, sb, bar);
+        }
+        __syncwarp();
+        have = gemv_wait(bar, p.err);
+    }
 
     for (int tok0 = 0; tok0 < m_e; tok0 += 8 * NG) {
         const __half *xh[NG];
@@ -117,53 +176,42 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
 #pragma unroll
             for (int i = 0; i < 4; ++i) acc[n][i] = 0.0f;
 
-        if (live) {
-            for (int kt0 = kbeg; kt0 < kend; kt0 += kGemvUnroll) {
-                uint4 qv[kGemvUnroll];
-                uint32_t sv[kGemvUnroll];
+        if (have) {
+            for (int j = 0; j < nk; ++j) {
+                const int kt = kbeg + j;
+                const uint4 qv = *reinterpret_cast<const uint4 *>(wq + j * kTileQBytes + lane * 16);
+                const uint32_t sv = *reinterpret_cast<const uint32_t *>(ws + j * kTileSBytes + 4 * g);
 #pragma unroll
-                for (int u = 0; u < kGemvUnroll; ++u) {
-                    if (kt0 + u < kend) {
-                        qv[u] = ldg_nc_v4(qt + (size_t)(kt0 + u) * kTileQBytes);
-                        sv[u] = ldg_nc_u32(st + (size_t)(kt0 + u) * kTileSBytes);
-                    }
-                }
+                for (int b = 0; b < 2; ++b) {
+                    const uint32_t wg = b ? qv.z : qv.x;   // tile row g
+                    const uint32_t wg8 = b ? qv.w : qv.y;  // tile row g+8
+                    const uint32_t s0a0 = e2m1x2_to_f16x2(wg & 0xff);
+                    const uint32_t s0a1 = e2m1x2_to_f16x2(wg8 & 0xff);
+                    const uint32_t s0a2 = e2m1x2_to_f16x2((wg >> 8) & 0xff);
+                    const uint32_t s0a3 = e2m1x2_to_f16x2((wg8 >> 8) & 0xff);
+                    const uint32_t s1a0 = e2m1x2_to_f16x2((wg >> 16) & 0xff);
+                    const uint32_t s1a1 = e2m1x2_to_f16x2((wg8 >> 16) & 0xff);
+                    const uint32_t s1a2 = e2m1x2_to_f16x2(wg >> 24);
+                    const uint32_t s1a3 = e2m1x2_to_f16x2(wg8 >> 24);
+                    const float sc_g = e8m0_to_float((sv >> (8 * b)) & 0xff);
+                    const float sc_g8 = e8m0_to_float((sv >> (8 * (2 + b))) & 0xff);
 #pragma unroll
-                for (int u = 0; u < kGemvUnroll; ++u) {
-                    if (kt0 + u >= kend) break;
-                    const int kt = kt0 + u;
-#pragma unroll
-                    for (int b = 0; b < 2; ++b) {
-                        const uint32_t wg = b ? qv[u].z : qv[u].x;   // tile row g
-                        const uint32_t wg8 = b ? qv[u].w : qv[u].y;  // tile row g+8
-                        const uint32_t s0a0 = e2m1x2_to_f16x2(wg & 0xff);
-                        const uint32_t s0a1 = e2m1x2_to_f16x2(wg8 & 0xff);
-                        const uint32_t s0a2 = e2m1x2_to_f16x2((wg >> 8) & 0xff);
-                        const uint32_t s0a3 = e2m1x2_to_f16x2((wg8 >> 8) & 0xff);
-                        const uint32_t s1a0 = e2m1x2_to_f16x2((wg >> 16) & 0xff);
-                        const uint32_t s1a1 = e2m1x2_to_f16x2((wg8 >> 16) & 0xff);
-                        const uint32_t s1a2 = e2m1x2_to_f16x2(wg >> 24);
-                        const uint32_t s1a3 = e2m1x2_to_f16x2(wg8 >> 24);
-                        const float sc_g = e8m0_to_float((sv[u] >> (8 * b)) & 0xff);
-                        const float sc_g8 = e8m0_to_float((sv[u] >> (8 * (2 + b))) & 0xff);
-#pragma unroll
-                        for (int n = 0; n < NG; ++n) {
-                            if (n >= ng_live) break;
-                            uint4 h = make_uint4(0, 0, 0, 0), l = make_uint4(0, 0, 0, 0);
-                            if (valid[n]) {
-                                h = *reinterpret_cast<const uint4 *>(xh[n] + kt * kTileK + b * 32);
-                                l = *reinterpret_cast<const uint4 *>(xl[n] + kt * kTileK + b * 32);
-                            }
-                            float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                            mma16816(d, s0a0, s0a1, s0a2, s0a3, h.x, h.y);
-                            mma16816(d, s0a0, s0a1, s0a2, s0a3, l.x, l.y);
-                            mma16816(d, s1a0, s1a1, s1a2, s1a3, h.z, h.w);
-                            mma16816(d, s1a0, s1a1, s1a2, s1a3, l.z, l.w);
-                            acc[n][0] = fmaf(d[0], sc_g, acc[n][0]);
-                            acc[n][1] = fmaf(d[1], sc_g, acc[n][1]);
-                            acc[n][2] = fmaf(d[2], sc_g8, acc[n][2]);
-                            acc[n][3] = fmaf(d[3], sc_g8, acc[n][3]);
+                    for (int n = 0; n < NG; ++n) {
+                        if (n >= ng_live) break;
+                        uint4 h = make_uint4(0, 0, 0, 0), l = make_uint4(0, 0, 0, 0);
+                        if (valid[n]) {
+                            h = *reinterpret_cast<const uint4 *>(xh[n] + kt * kTileK + b * 32);
+                            l = *reinterpret_cast<const uint4 *>(xl[n] + kt * kTileK + b * 32);
                         }
+                        float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        mma16816(d, s0a0, s0a1, s0a2, s0a3, h.x, h.y);
+                        mma16816(d, s0a0, s0a1, s0a2, s0a3, l.x, l.y);
+                        mma16816(d, s1a0, s1a1, s1a2, s1a3, h.z, h.w);
+                        mma16816(d, s1a0, s1a1, s1a2, s1a3, l.z, l.w);
+                        acc[n][0] = fmaf(d[0], sc_g, acc[n][0]);
+                        acc[n][1] = fmaf(d[1], sc_g, acc[n][1]);
+                        acc[n][2] = fmaf(d[2], sc_g8, acc[n][2]);
+                        acc[n][3] = fmaf(d[3], sc_g8, acc[n][3]);
                     }
                 }
             }
@@ -218,20 +266,28 @@ template <bool GATE_UP>
 cudaError_t launch(const GemvParams &p, int T, int max_active, cudaStream_t st) {
     const int nrt = p.R / kTileRows;
     dim3 grid((nrt + kGemvTiles - 1) / kGemvTiles, max_active);
-    if (T <= 8)
-        gemv_kernel<GATE_UP, 1><<<grid, kGemvWarps * 32, 0, st>>>(p);
-    else if (T <= 16)
-        gemv_kernel<GATE_UP, 2><<<grid, kGemvWarps * 32, 0, st>>>(p);
-    else
-        gemv_kernel<GATE_UP, 4><<<grid, kGemvWarps * 32, 0, st>>>(p);
+    const size_t smem = gemv_smem_bytes(p.K);
+    cudaError_t e;
+#define AMOE_GEMV(NG)                                                                              \
+    do {                                                                                           \
+        e = cudaFuncSetAttribute(gemv_kernel<GATE_UP, NG>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                 (int)smem);                                                       \
+        if (e != cudaSuccess) return e;                                                            \
+        gemv_kernel<GATE_UP, NG><<<grid, kGemvWarps * 32, smem, st>>>(p);                          \
+    } while (0)
+    if (T <= 8) AMOE_GEMV(1);
+    else if (T <= 16) AMOE_GEMV(2);
+    else AMOE_GEMV(4);
+#undef AMOE_GEMV
     return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_gemv_gate_up(const Dims &d, const LayerDev &L, const RouteOut &r, int T,
-                                __half *act_hi, __half *act_lo, cudaStream_t st) {
+                                __half *act_hi, __half *act_lo, int32_t *err, cudaStream_t st) {
     GemvParams p{};
+    p.err = err;
     p.q = L.gu_q;
     p.s = L.gu_s;
     p.bias = L.gu_b;
@@ -251,9 +307,10 @@ cudaError_t launch_gemv_gate_up(const Dims &d, const LayerDev &L, const RouteOut
 }
 
 cudaError_t launch_gemv_down(const Dims &d, const LayerDev &L, const RouteOut &r, int T,
-                             const __half *act_hi, const __half *act_lo, float *y,
+                             const __half *act_hi, const __half *act_lo, float *y, int32_t *err,
                              cudaStream_t st) {
     GemvParams p{};
+    p.err = err;
     p.q = L.dn_q;
     p.s = L.dn_s;
     p.bias = L.dn_b;

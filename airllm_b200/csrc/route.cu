@@ -22,7 +22,7 @@ constexpr int kMaxKSplit = 16;
 struct RouteParams {
     const float *residual;
     const float *gain;
-    const float *wt;   // [H][E]
+    const float *w;    // [E][H] router weight (GGUF layout)
     const float *bias; // [E]
     int T, H, E, k, ksplit;
     float eps;
@@ -47,59 +47,96 @@ __device__ __forceinline__ bool better(float v1, int e1, float v2, int e2) {
     return v1 > v2 || (v1 == v2 && e1 < e2);
 }
 
-template <int NT, int EPL>
-__device__ __forceinline__ void partial_logits(const float *xn, int H, const float *wt, int E,
-                                               int k0, int k1, int lane, double (&acc)[EPL][NT]) {
-    // U router rows in flight per batch: the loads of a batch are independent
-    constexpr int U = EPL >= 8 ? 2 : 8 / EPL;
+__device__ __forceinline__ void dmma884(double &d0, double &d1, double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+                 : "+d"(d0), "+d"(d1)
+                 : "d"(a), "d"(b));
+}
+
+
+// Partial router logits of the chunk's 8 tokens over k in [k0, k1) on the FP64
+// tensor path (mma.m8n8k4: f64 products, f64 accumulation) for experts
+// [8*nb0, 8*(nb0+NB)).  Lane (g = lane/4, c = lane%4) loads 4 consecutive k of
+// token g (A) and of expert 8*nb+g (B) per 16-k group and feeds them to 4 MMAs
+// as k-columns c of each: the same k permutation on both operands.  A is the
+// RMSNorm output computed right here from the residual (primitives.go:68-70,
+// float32(float64(x) * inverseRMS * float64(g)) left to right); the first pass
+// also stores its fp16 hi/lo split for the expert GEMMs.
+template <int NB>
+__device__ __forceinline__ void logits_pass(const RouteParams &p, const double *inv, int t0, int nt, int k0,
+                                            int k1, int nb0, int lane, bool write_split,
+                                            double (&acc)[NB][2]) {
+    const int g = lane >> 2, c = lane & 3;
+    const int H = p.H;
 #pragma unroll
-    for (int j = 0; j < EPL; ++j)
-#pragma unroll
-        for (int t = 0; t < NT; ++t) acc[j][t] = 0.0;
-    for (int kb = k0; kb < k1; kb += U) {
-        float wv[U][EPL];
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-#pragma unroll
-            for (int j = 0; j < EPL; ++j) {
-                const int e = lane + 32 * j;
-                wv[u][j] = (kb + u < k1 && e < E) ? __ldg(wt + (size_t)(kb + u) * E + e) : 0.0f;
+    for (int nb = 0; nb < NB; ++nb) acc[nb][0] = acc[nb][1] = 0.0;
+    const bool tok_ok = g < nt;
+    const float *xrow = p.residual + (size_t)(t0 + g) * H;
+    const double iv = inv[g];
+    for (int kb = k0; kb < k1; kb += 16) {
+        const int k = kb + 4 * c;
+        const bool kin = k < k1;  // k1 - k0 is a multiple of 16 except at H (a multiple of 64)
+        double a[4] = {0.0, 0.0, 0.0, 0.0};
+        if (kin && tok_ok) {
+            const float4 x = __ldg(reinterpret_cast<const float4 *>(xrow + k));
+            const float4 gn = __ldg(reinterpret_cast<const float4 *>(p.gain + k));
+            const float n0 = (float)((double)x.x * iv * (double)gn.x);
+            const float n1 = (float)((double)x.y * iv * (double)gn.y);
+            const float n2 = (float)((double)x.z * iv * (double)gn.z);
+            const float n3 = (float)((double)x.w * iv * (double)gn.w);
+            a[0] = n0; a[1] = n1; a[2] = n2; a[3] = n3;
+            if (write_split) {
+                const __half2 h01 = __floats2half2_rn(n0, n1), h23 = __floats2half2_rn(n2, n3);
+                const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+                const __half2 l01 = __floats2half2_rn(n0 - f01.x, n1 - f01.y);
+                const __half2 l23 = __floats2half2_rn(n2 - f23.x, n3 - f23.y);
+                __half2 *dh = reinterpret_cast<__half2 *>(p.o.x_hi + (size_t)(t0 + g) * H + k);
+                __half2 *dl = reinterpret_cast<__half2 *>(p.o.x_lo + (size_t)(t0 + g) * H + k);
+                dh[0] = h01;
+                dh[1] = h23;
+                dl[0] = l01;
+                dl[1] = l23;
             }
+        }
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            if (kb + u >= k1) break;
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                const double xv = (double)xn[t * H + kb + u];
-#pragma unroll
-                for (int j = 0; j < EPL; ++j) acc[j][t] += xv * (double)wv[u][j];
-            }
+        for (int nb = 0; nb < NB; ++nb) {
+            const int e = 8 * (nb0 + nb) + g;
+            float4 wv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (kin && e < p.E) wv = __ldg(reinterpret_cast<const float4 *>(p.w + (size_t)e * H + k));
+            dmma884(acc[nb][0], acc[nb][1], a[0], (double)wv.x);
+            dmma884(acc[nb][0], acc[nb][1], a[1], (double)wv.y);
+            dmma884(acc[nb][0], acc[nb][1], a[2], (double)wv.z);
+            dmma884(acc[nb][0], acc[nb][1], a[3], (double)wv.w);
         }
     }
 }
 
-// One CTA = one chunk of kRouteTokens tokens x one K-slice.  With ksplit > 1
-// the last CTA of a chunk to finish (arrival counter) reduces the partial sums
-// in fixed slice order and runs top-k, so the result does not depend on timing.
-template <int EPL>
+// One CTA = one chunk of kRouteTokens tokens x one K-slice (ksplit > 1 for
+// small T spreads the router weight over more SMs).  Phases: (1) each token's
+// sum of squares over its full row (primitives.go:61-65) in float64; (2) the
+// slice's normalized values feed the DMMA logits directly (and their fp16 split
+// is stored); (3) fixed-order reduction of the warps' partials; with ksplit > 1
+// the last CTA of a chunk (arrival counter) sums the slices in slice order;
+// (4) per token: logits = f32(sum) + bias, top-k, softmax over the selected.
+// Every step is deterministic.
+// NB: expert blocks of 8 per DMMA pass (4 for E <= 32, 8 for <= 64, 16 beyond,
+// looping passes past 128 experts).
+template <int NB>
 __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteParams p) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int H = p.H, E = p.E;
-    float *xn = reinterpret_cast<float *>(smem);                                  // [8][H]
-    double *part = reinterpret_cast<double *>(xn + kRouteTokens * H);             // [warps][8][E]
+    double *part = reinterpret_cast<double *>(smem);                              // [warps][8][E]
     int *hist_s = reinterpret_cast<int *>(part + kRouteWarps * kRouteTokens * E); // [E]
     __shared__ int is_last;
+    __shared__ double ssq[kRouteWarps][kRouteTokens];
+    __shared__ double inv_s[kRouteTokens];
 
     const int chunk = blockIdx.x, ks = blockIdx.y;
     const int t0 = chunk * kRouteTokens;
     const int nt = min(kRouteTokens, p.T - t0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    // 1. RMSNorm (primitives.go:61-70).  All threads sweep the chunk's rows with
-    //    float4 loads (every token's loads in flight together); float64 sums of
-    //    squares per token, reduced per warp and then across warps.
-    __shared__ double ssq[kRouteWarps][kRouteTokens];
-    __shared__ double inv_s[kRouteTokens];
+    // 1. float64 sums of squares of the chunk's rows (all threads, float4 loads)
     {
         const int H4 = H / 4;
         const float4 *res4 = reinterpret_cast<const float4 *>(p.residual + (size_t)t0 * H);
@@ -126,6 +163,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteParams p) 
             const double w = warp_sum_f64(ss[t]);
             if (lane == 0) ssq[warp][t] = w;
         }
+        for (int e = threadIdx.x; e < E; e += blockDim.x) hist_s[e] = 0;
         __syncthreads();
         if (threadIdx.x < kRouteTokens) {
             double sum = 0.0;
@@ -133,73 +171,26 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteParams p) 
             inv_s[threadIdx.x] = 1.0 / sqrt(sum / (double)H + (double)p.eps);
         }
         __syncthreads();
-        const float4 *g4 = reinterpret_cast<const float4 *>(p.gain);
-        const bool write_split = ks == 0;
-        for (int i = threadIdx.x; i < H4; i += blockDim.x) {
-            const float4 g = __ldg(g4 + i);
-#pragma unroll
-            for (int t = 0; t < kRouteTokens; ++t) {
-                float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (t < nt) {
-                    const float4 x = __ldg(res4 + (size_t)t * H4 + i);
-                    const double inv = inv_s[t];
-                    // float32(float64(x) * inverseRMS * float64(g)), evaluated left to right
-                    o.x = (float)((double)x.x * inv * (double)g.x);
-                    o.y = (float)((double)x.y * inv * (double)g.y);
-                    o.z = (float)((double)x.z * inv * (double)g.z);
-                    o.w = (float)((double)x.w * inv * (double)g.w);
-                    if (write_split) {
-                        const __half2 h01 = __floats2half2_rn(o.x, o.y), h23 = __floats2half2_rn(o.z, o.w);
-                        const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
-                        const __half2 l01 = __floats2half2_rn(o.x - f01.x, o.y - f01.y);
-                        const __half2 l23 = __floats2half2_rn(o.z - f23.x, o.w - f23.y);
-                        __half2 *dh = reinterpret_cast<__half2 *>(p.o.x_hi + (size_t)(t0 + t) * H + 4 * i);
-                        __half2 *dl = reinterpret_cast<__half2 *>(p.o.x_lo + (size_t)(t0 + t) * H + 4 * i);
-                        dh[0] = h01;
-                        dh[1] = h23;
-                        dl[0] = l01;
-                        dl[1] = l23;
-                    }
-                }
-                reinterpret_cast<float4 *>(xn + t * H)[i] = o;
-            }
-        }
     }
-    for (int e = threadIdx.x; e < E; e += blockDim.x) hist_s[e] = 0;
-    __syncthreads();
 
-    // 2. partial router logits over this CTA's K-slice, split across warps
-    const int kslice = (H + p.ksplit - 1) / p.ksplit;
-    const int kbeg = ks * kslice, kend = min(H, kbeg + kslice);
-    const int wslice = (kend - kbeg + kRouteWarps - 1) / kRouteWarps;
+    // 2. partial logits over this CTA's K-slice, the slice split across warps in
+    //    16-aligned ranges
+    const int kslice = ((H + p.ksplit - 1) / p.ksplit + 15) & ~15;
+    const int kbeg = min(H, ks * kslice), kend = min(H, kbeg + kslice);
+    const int wslice = ((kend - kbeg + kRouteWarps - 1) / kRouteWarps + 15) & ~15;
     const int k0 = min(kend, kbeg + warp * wslice), k1 = min(kend, k0 + wslice);
     {
-        double acc[EPL][kRouteTokens];
-        if (nt == 1) {
-            double a1[EPL][1];
-            partial_logits<1, EPL>(xn, H, p.wt, E, k0, k1, lane, a1);
+        const int g = lane >> 2, c = lane & 3;
+        for (int nb0 = 0; 8 * nb0 < E; nb0 += NB) {
+            double acc[NB][2];
+            logits_pass<NB>(p, inv_s, t0, nt, k0, k1, nb0, lane, nb0 == 0, acc);
 #pragma unroll
-            for (int j = 0; j < EPL; ++j) {
-                acc[j][0] = a1[j][0];
+            for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-                for (int t = 1; t < kRouteTokens; ++t) acc[j][t] = 0.0;
-            }
-        } else if (nt <= 4) {
-            double a4[EPL][4];
-            partial_logits<4, EPL>(xn, H, p.wt, E, k0, k1, lane, a4);
-#pragma unroll
-            for (int j = 0; j < EPL; ++j)
-#pragma unroll
-                for (int t = 0; t < kRouteTokens; ++t) acc[j][t] = t < 4 ? a4[j][t] : 0.0;
-        } else {
-            partial_logits<kRouteTokens, EPL>(xn, H, p.wt, E, k0, k1, lane, acc);
-        }
-#pragma unroll
-        for (int j = 0; j < EPL; ++j) {
-            int e = lane + 32 * j;
-            if (e < E)
-#pragma unroll
-                for (int t = 0; t < kRouteTokens; ++t) part[(warp * kRouteTokens + t) * E + e] = acc[j][t];
+                for (int i = 0; i < 2; ++i) {
+                    const int e = 8 * (nb0 + nb) + 2 * c + i;
+                    if (e < E) part[(warp * kRouteTokens + g) * E + e] = acc[nb][i];
+                }
         }
     }
     __syncthreads();
@@ -227,6 +218,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteParams p) 
     // 3. token t0 + warp: logits, top-k, softmax over the selected logits
     if (warp < nt) {
         const int t = t0 + warp;
+        constexpr int EPL = 8;  // up to 256 experts, lane + 32 j
         float lg[EPL];
 #pragma unroll
         for (int j = 0; j < EPL; ++j) {
@@ -318,10 +310,10 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteParams p) 
     }
 }
 
-// K2: one CTA.  Column scan of the per-chunk expert histograms, then every pair
-// (t, s) gets position offsets[e] + (#pairs of expert e in earlier chunks) +
-// (#earlier pairs of expert e in its own chunk): a stable sort by (e, t, s).
-__global__ void __launch_bounds__(1024) permute_kernel(int T, int E, int k, RouteOut o) {
+// K2a: one CTA.  Column scan of the per-chunk expert histograms: expert
+// offsets (exclusive scan of the counts), the active-expert list, and for every
+// chunk the first position of each expert's pairs in that chunk.
+__global__ void __launch_bounds__(1024) scan_kernel(int T, int E, RouteOut o) {
     extern __shared__ int sm[];
     const int nchunk = (T + kRouteTokens - 1) / kRouteTokens;
     const int groups = max(1, (int)blockDim.x / E);
@@ -369,17 +361,76 @@ __global__ void __launch_bounds__(1024) permute_kernel(int T, int E, int k, Rout
             s += o.hist[(size_t)c * E + e];
         }
     }
+}
+
+// K2b: one warp per chunk.  Pair (t, s) goes to chunk_base[chunk][e] + the number
+// of earlier pairs of expert e in the chunk (match_any ranks, carried across
+// 32-pair rounds): a stable sort by (e, t, s).  With GATHER the warp also copies
+// the chunk's normalized rows (fp16 hi/lo) to their expert-sorted positions,
+// which is the B operand of the tensor-core gate_up GEMM.
+constexpr int kScatterWarps = 4;
+
+// Stable positions of one chunk's pairs, computed by one warp; returns nothing,
+// writes perm_pair/inv and (if pos_s) the positions to shared memory.
+__device__ __forceinline__ void chunk_positions(int chunk, int T, int E, int k, const RouteOut &o, int *carry,
+                                                int *pos_s, int lane) {
+    for (int e = lane; e < E; e += 32) carry[e] = 0;
+    __syncwarp();
+    const int first = chunk * kRouteTokens * k;
+    const int last = min(T * k, first + kRouteTokens * k);
+    const unsigned lt = (1u << lane) - 1u;
+    for (int q0 = first; q0 < last; q0 += 32) {
+        const int q = q0 + lane;
+        const bool valid = q < last;
+        const int ex = valid ? o.topk_idx[q] : E;  // E: sentinel group for idle lanes
+        const unsigned peers = __match_any_sync(0xffffffffu, ex);
+        if (valid) {
+            const int pos = o.chunk_base[(size_t)chunk * E + ex] + carry[ex] + __popc(peers & lt);
+            o.perm_pair[pos] = q;
+            o.inv[q] = pos;
+            if (pos_s) pos_s[q - first] = pos;
+        }
+        __syncwarp();
+        if (valid && (peers >> lane) == 1u) carry[ex] += __popc(peers);  // last lane of its group
+        __syncwarp();
+    }
+}
+
+// K2b (GEMV path): one warp per chunk.  Pair (t, s) goes to chunk_base[chunk][e]
+// + the number of earlier pairs of expert e in the chunk: a stable sort by
+// (e, t, s).
+__global__ void __launch_bounds__(kScatterWarps * 32) scatter_kernel(int T, int E, int k, RouteOut o) {
+    extern __shared__ int carry_all[];  // [warps][E]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nchunk = (T + kRouteTokens - 1) / kRouteTokens;
+    const int chunk = blockIdx.x * kScatterWarps + warp;
+    if (chunk >= nchunk) return;  // whole warp
+    chunk_positions(chunk, T, E, k, o, carry_all + warp * E, nullptr, lane);
+}
+
+// K2b (tensor path): one CTA per chunk.  Warp 0 computes the positions, then
+// warp t copies token t's normalized row (fp16 hi/lo) to its k expert-sorted
+// positions: the B operand of the tensor-core gate_up GEMM.
+__global__ void __launch_bounds__(kRouteTokens * 32)
+    scatter_gather_kernel(int T, int E, int k, int H, RouteOut o, __half *xp_hi, __half *xp_lo) {
+    extern __shared__ int sg_smem[];  // carry [E], positions [kRouteTokens * k]
+    int *carry = sg_smem, *pos_s = sg_smem + E;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int chunk = blockIdx.x;
+    if (warp == 0) chunk_positions(chunk, T, E, k, o, carry, pos_s, lane);
     __syncthreads();
-    const int npairs = T * k;
-    for (int pidx = tid; pidx < npairs; pidx += blockDim.x) {
-        const int ex = o.topk_idx[pidx];
-        const int c = (pidx / k) / kRouteTokens;
-        const int first = c * kRouteTokens * k;
-        int rank = 0;
-        for (int q = first; q < pidx; ++q) rank += o.topk_idx[q] == ex;
-        const int pos = o.chunk_base[(size_t)c * E + ex] + rank;
-        o.perm_pair[pos] = pidx;
-        o.inv[pidx] = pos;
+    const int t = chunk * kRouteTokens + warp;
+    if (t >= T) return;
+    const uint4 *sh = reinterpret_cast<const uint4 *>(o.x_hi + (size_t)t * H);
+    const uint4 *sl = reinterpret_cast<const uint4 *>(o.x_lo + (size_t)t * H);
+    const int H8 = H / 8;
+    for (int i = lane; i < H8; i += 32) {
+        const uint4 vh = sh[i], vl = sl[i];
+        for (int sidx = 0; sidx < k; ++sidx) {
+            const int pos = pos_s[warp * k + sidx];
+            reinterpret_cast<uint4 *>(xp_hi + (size_t)pos * H)[i] = vh;
+            reinterpret_cast<uint4 *>(xp_lo + (size_t)pos * H)[i] = vl;
+        }
     }
 }
 
@@ -388,8 +439,8 @@ __global__ void __launch_bounds__(1024) permute_kernel(int T, int E, int k, Rout
 static int route_ksplit(int H, int nchunk) {
     int ksplit = (2 * 148 + nchunk - 1) / nchunk;
     ksplit = ksplit < 1 ? 1 : (ksplit > kMaxKSplit ? kMaxKSplit : ksplit);
-    // every K-slice must be non-empty
-    while (ksplit > 1 && (H + ksplit - 1) / ksplit * (ksplit - 1) >= H) --ksplit;
+    // every 16-aligned K-slice must be non-empty
+    while (ksplit > 1 && (((H + ksplit - 1) / ksplit + 15) & ~15) * (ksplit - 1) >= H) --ksplit;
     return ksplit;
 }
 
@@ -414,7 +465,7 @@ cudaError_t launch_route_impl(const Dims &d, const LayerDev &L, const float *res
     RouteParams p;
     p.residual = residual;
     p.gain = L.norm_gain;
-    p.wt = L.router_wt;
+    p.w = L.router_w;
     p.bias = L.router_b;
     p.T = T;
     p.H = d.H;
@@ -425,33 +476,43 @@ cudaError_t launch_route_impl(const Dims &d, const LayerDev &L, const float *res
     p.o = o;
     p.partial = partial;
     p.arrivals = arrivals;
-    const size_t smem = (size_t)kRouteTokens * d.H * sizeof(float) +
-                        (size_t)kRouteWarps * kRouteTokens * d.E * sizeof(double) + d.E * sizeof(int);
-    dim3 grid(nchunk, ksplit);
+    const size_t smem = (size_t)kRouteWarps * kRouteTokens * d.E * sizeof(double) + d.E * sizeof(int);
+    const dim3 grid(nchunk, ksplit);
     cudaError_t err;
-#define AMOE_ROUTE(EPL)                                                                         \
-    do {                                                                                        \
-        err = cudaFuncSetAttribute(route_kernel<EPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                   (int)smem);                                                  \
-        if (err != cudaSuccess) return err;                                                     \
-        route_kernel<EPL><<<grid, kRouteWarps * 32, smem, st>>>(p);                             \
+#define AMOE_ROUTE(NB)                                                                            \
+    do {                                                                                          \
+        err = cudaFuncSetAttribute(route_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                   (int)smem);                                                    \
+        if (err != cudaSuccess) return err;                                                       \
+        route_kernel<NB><<<grid, kRouteWarps * 32, smem, st>>>(p);                                \
     } while (0)
-    if (d.E <= 32) AMOE_ROUTE(1);
-    else if (d.E <= 64) AMOE_ROUTE(2);
-    else if (d.E <= 128) AMOE_ROUTE(4);
-    else AMOE_ROUTE(8);
+    if (d.E <= 32) AMOE_ROUTE(4);
+    else if (d.E <= 64) AMOE_ROUTE(8);
+    else AMOE_ROUTE(16);
 #undef AMOE_ROUTE
     err = cudaGetLastError();
     if (err != cudaSuccess) return err;
     if (hook) hook(hook_arg, 0);
-    if (nchunk == 1) return cudaSuccess;  // permutation written by route_kernel
+    if (nchunk == 1) return cudaSuccess;  // counts, offsets and chunk bases written by route_kernel
     const int threads = 1024;
     const int groups = threads / d.E > 0 ? threads / d.E : 1;
     const size_t psmem = (size_t)(groups * d.E + d.E + d.E + 1) * sizeof(int);
-    permute_kernel<<<1, threads, psmem, st>>>(T, d.E, d.k, o);
-    err = cudaGetLastError();
-    if (hook) hook(hook_arg, 1);
-    return err;
+    scan_kernel<<<1, threads, psmem, st>>>(T, d.E, o);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_scatter(const Dims &d, int T, const RouteOut &o, bool gather, __half *xp_hi,
+                           __half *xp_lo, cudaStream_t st) {
+    const int nchunk = (T + kRouteTokens - 1) / kRouteTokens;
+    if (gather) {
+        const size_t smem = (size_t)(d.E + kRouteTokens * d.k) * sizeof(int);
+        scatter_gather_kernel<<<nchunk, kRouteTokens * 32, smem, st>>>(T, d.E, d.k, d.H, o, xp_hi, xp_lo);
+    } else {
+        const size_t smem = (size_t)kScatterWarps * d.E * sizeof(int);
+        scatter_kernel<<<(nchunk + kScatterWarps - 1) / kScatterWarps, kScatterWarps * 32, smem, st>>>(T, d.E,
+                                                                                                   d.k, o);
+    }
+    return cudaGetLastError();
 }
 
 }  // namespace amoe

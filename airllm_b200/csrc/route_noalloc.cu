@@ -7,8 +7,8 @@
 // which another allocator (for example PyTorch's caching allocator) has already
 // reserved the GPU, so a fresh cudaMalloc can fail or synchronise the device.
 // amoe_route_noalloc takes only caller-owned inputs and outputs and keeps its
-// scratch (transposed router weight, split-K partial sums, arrival counters,
-// the per-chunk histograms and the permutation) in one file-scope device array
+// scratch (split-K partial sums, arrival counters, the fp16 split of the
+// normalized rows, the per-chunk histograms and the permutation) in one file-scope device array
 // of fixed size, kNoAllocScratchBytes.  It calls no cudaMalloc/cudaFree.
 //
 // The array is shared by every call on a device and keeps the last call's
@@ -34,8 +34,7 @@ constexpr int kNoAllocMaxDevices = 64;
 
 // Byte layout of the scratch array (each part 256-B aligned).
 constexpr size_t al(size_t x) { return (x + 255) & ~size_t(255); }
-constexpr size_t kOffWt = 0;                                                          // f32 [H][E]
-constexpr size_t kOffXhi = kOffWt + al((size_t)kNoAllocMaxHidden * kNoAllocMaxExperts * 4);
+constexpr size_t kOffXhi = 0;
 constexpr size_t kOffXlo = kOffXhi + al((size_t)kNoAllocMaxTokens * kNoAllocMaxHidden * 2);
 constexpr size_t kOffPartial = kOffXlo + al((size_t)kNoAllocMaxTokens * kNoAllocMaxHidden * 2);
 constexpr size_t kPartialElems = (size_t)16 * kNoAllocMaxTokens * kNoAllocMaxExperts;  // ksplit <= 16
@@ -133,12 +132,11 @@ extern "C" AMOE_API int amoe_route_noalloc(int32_t device, int32_t hidden, int32
 
     LayerDev L;
     L.norm_gain = const_cast<float *>(norm_gain);
-    L.router_wt = reinterpret_cast<float *>(base + kOffWt);
+    L.router_w = const_cast<float *>(router_w);
     L.router_b = const_cast<float *>(router_b);
 
     // the split-K arrival counters must start at zero
     e = cudaMemsetAsync(arrivals, 0, (size_t)nchunk * sizeof(int32_t), st);
-    if (e == cudaSuccess) e = launch_transpose_router(router_w, experts, hidden, L.router_wt, st);
     const Dims d{hidden, 0, experts, top_k, rms_eps};
     if (e == cudaSuccess) e = launch_route_impl(d, L, residual, T, o, partial, arrivals, st);
     if (e != cudaSuccess) {

@@ -129,8 +129,9 @@ AMOE_API int amoe_last_routing(amoe_ctx *ctx, float *logits, int32_t *perm_pair,
                       int32_t *offsets);
 
 /* Per-stage device timing (CUDA events on the launch stream) and launch count.
- * Stages: 0 route (RMSNorm+router+top-k), 1 permute, 2 gate_up (+SwiGLU),
- * 3 down, 4 combine, 5 gather (tensor path), 6-7 reserved. */
+ * Stages: 0 route (RMSNorm+router+top-k), 1 expert-offset scan (+ scatter on
+ * the GEMV path), 2 gate_up (+SwiGLU), 3 down, 4 combine, 5 scatter + gather
+ * of the expert-sorted rows (tensor path), 6-7 reserved. */
 #define AMOE_STAGES 8
 typedef struct amoe_stats {
     int64_t launches;               /* kernels this context has launched */
@@ -154,7 +155,7 @@ AMOE_API int amoe_get_stats(amoe_ctx *ctx, amoe_stats *out, int32_t reset);
  * e.g. a runtime that plans all device memory up front and hands out fixed
  * regions, or a process whose GPU memory is already reserved by another
  * allocator.  It needs no context and calls no cudaMalloc/cudaFree: its scratch
- * is one fixed device array of 4.1 MB that every GPU loading this library holds
+ * is one fixed device array of 2.1 MB that every GPU loading this library holds
  * until exit.  Limits: 1 <= T <= 64, hidden a multiple of 64 up to 4096,
  * experts <= 128, top_k <= min(experts, 32); larger sizes return
  * AMOE_ERR_INVALID with a message in amoe_last_error(NULL).
