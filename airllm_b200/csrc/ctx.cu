@@ -552,7 +552,19 @@ int amoe_forward_device(amoe_ctx *c, int32_t layer, const float *residual, int32
     c->stats.launches += 1;
     c->stats.forwards += 1;
     c->stats.last_path = tc ? AMOE_PATH_TENSOR : AMOE_PATH_GEMV;
-    if (slot >= 0) AMOE_CUDA(c, cudaEventRecord(c->slot_free[slot], st));
+    if (slot >= 0) {
+        AMOE_CUDA(c, cudaEventRecord(c->slot_free[slot], st));
+        // AirLLM-style streaming: start copying the next layer into the least
+        // recently used slot while this layer computes.
+        if (c->cfg.layers > (int)c->slot_dev.size()) {
+            const int next = (layer + 1) % c->cfg.layers;
+            int next_slot;
+            if (c->uploaded[next]) {
+                rc = acquire_slot(c, next, nullptr, &next_slot);
+                if (rc) return rc;
+            }
+        }
+    }
     if (topk_idx)
         AMOE_CUDA(c, cudaMemcpyAsync(topk_idx, c->r.topk_idx, (size_t)T * d.k * 4,
                                      cudaMemcpyDeviceToDevice, st));

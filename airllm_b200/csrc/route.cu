@@ -227,8 +227,12 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteParams p) 
             if (e < E) {
                 double s = 0.0;
                 if (p.ksplit > 1) {
-                    for (int q = 0; q < p.ksplit; ++q)
-                        s += __ldcg(p.partial + ((size_t)q * p.T + t) * E + e);
+                    double sl[kMaxKSplit];  // all slice loads in flight, then a fixed-order sum
+#pragma unroll
+                    for (int q = 0; q < kMaxKSplit; ++q)
+                        sl[q] = q < p.ksplit ? __ldcg(p.partial + ((size_t)q * p.T + t) * E + e) : 0.0;
+#pragma unroll
+                    for (int q = 0; q < kMaxKSplit; ++q) s += sl[q];
                 } else {
                     for (int w = 0; w < kRouteWarps; ++w) s += part[(w * kRouteTokens + warp) * E + e];
                 }

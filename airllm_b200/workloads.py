@@ -55,8 +55,8 @@ def _mxfp4_bytes(rng, rows: int, cols: int, scale_lo=119, scale_hi=123) -> np.nd
     return data
 
 
-def make_layer(shape: MoEShape, seed: int) -> dict:
-    """One MoE layer (weights only) drawn from `seed`."""
+def make_layer(shape: MoEShape, seed) -> dict:
+    """One MoE layer (weights only) drawn from `seed` (an int or a tuple of ints)."""
     H, I, E = shape.hidden, shape.intermediate, shape.experts
     r = _streams(seed, 6)
     return {
@@ -115,6 +115,15 @@ def config_layer(config: int) -> dict:
         layer["router_b"] = b.astype(np.float32)
         return layer
     raise ValueError(f"no workload configuration {config}")
+
+
+STREAM_LAYERS = 24
+STREAM_DECODE_TOKENS = 64
+
+
+def stream_layer(index: int) -> dict:
+    """Layer `index` of the 24-layer streamed stack: config-0 statistics, seed (2, index)."""
+    return make_layer(GPTOSS_20B, (2, index))
 
 
 CONFIG_TOKENS = {0: 1, 1: 4096, 2: 1, 3: 256, 4: 16384}

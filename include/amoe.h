@@ -116,8 +116,10 @@ AMOE_API int amoe_forward_device(amoe_ctx *ctx, int32_t layer, const float *resi
 AMOE_API int amoe_synchronize(amoe_ctx *ctx);
 
 /* Streaming mode (stream_slots >= 2): starts copying `layer` from pinned host
- * memory into a free device slot on the copy stream.  A later forward of that
- * layer waits for the copy on the device (an event), not on the host.
+ * memory into the least recently used device slot on the copy stream.  A later
+ * forward of that layer waits for the copy on the device (an event), not on
+ * the host.  After every forward of layer L the context itself starts copying
+ * layer (L+1) mod layers, so a sequential layer loop needs no explicit call.
  * Replaces the synchronous per-layer reload of Generate, runtime.go:146-199. */
 AMOE_API int amoe_prefetch_layer(amoe_ctx *ctx, int32_t layer);
 

@@ -187,8 +187,11 @@ def test_streaming_slots_match_resident_layers(cuda_device):
     h_res, h_stm = x, x
     for step in range(2):
         for i in range(3):
-            if i + 1 < 3:
-                stm.prefetch_layer(i + 1)
+            h_res = res.forward(h_res, layer=i)[0]
+            h_stm = stm.forward(h_stm, layer=i)[0]  # copies layer i+1 behind this forward
+            assert np.array_equal(h_res, h_stm)
+        stm.prefetch_layer(2)  # explicit request, then out-of-order use
+        for i in (2, 0, 1):
             h_res = res.forward(h_res, layer=i)[0]
             h_stm = stm.forward(h_stm, layer=i)[0]
             assert np.array_equal(h_res, h_stm)
