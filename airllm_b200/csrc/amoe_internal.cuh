@@ -8,7 +8,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <nccl.h>
+
 #include <string>
+#include <vector>
 
 namespace amoe {
 
@@ -100,9 +103,19 @@ cudaError_t launch_repack(const uint8_t *gguf, int E, int R, int K, bool pair_ro
                           uint8_t *q, uint8_t *s, cudaStream_t st);
 
 // Expert GEMV (decode) ---------------------------------------------------------
-cudaError_t launch_gemv_gate_up(const Dims &d, const LayerDev &L, const RouteOut &r, int T,
+// Expert-sorted rows the GEMV stages work on.
+struct GemvRows {
+    const __half *x_hi, *x_lo;  // gate_up input rows: by token (perm_pair) or by position
+    const int32_t *perm_pair;   // position -> pair id (t*k+s); NULL: x rows are positions
+    const int32_t *offsets;     // [E+1] expert row ranges
+    const int32_t *active;      // [E] experts with rows, then their count at [E]
+    const int32_t *y_rows;      // down output row per position (NULL: the position)
+    int max_active;             // grid bound on the active list
+};
+// T: upper bound on any expert's row count (sizes the token groups per pass).
+cudaError_t launch_gemv_gate_up(const Dims &d, const LayerDev &L, const GemvRows &rows, int T,
                                 __half *act_hi, __half *act_lo, int32_t *err, cudaStream_t st);
-cudaError_t launch_gemv_down(const Dims &d, const LayerDev &L, const RouteOut &r, int T,
+cudaError_t launch_gemv_down(const Dims &d, const LayerDev &L, const GemvRows &rows, int T,
                              const __half *act_hi, const __half *act_lo, float *y, int32_t *err,
                              cudaStream_t st);
 
@@ -114,15 +127,56 @@ cudaError_t launch_tc_forward(const Dims &d, const LayerDev &L, const RouteOut &
                               __half *act_hi, __half *act_lo, float *y, void *tc_scratch,
                               int max_pairs, cudaStream_t st, StageHook hook, void *hook_arg,
                               int *launches);
+// The two grouped GEMMs alone, on rows that are already expert-sorted:
+// gate_up from (b_hi, b_lo) [rows_cap][H] into act [rows_cap][I], then down into
+// y[y_rows ? y_rows[pos] : pos][H].
+cudaError_t launch_tc_experts(const Dims &d, const LayerDev &L, const int32_t *offsets, const __half *b_hi,
+                              const __half *b_lo, int rows_cap, __half *act_hi, __half *act_lo, float *y,
+                              const int32_t *y_rows, int32_t *err, cudaStream_t st, StageHook hook,
+                              void *hook_arg, int *launches);
 // Per-expert exponent bias from a tiled scale plane (upload time).
 cudaError_t launch_cexp(const uint8_t *s_plane, size_t bytes_per_expert, int E, int32_t *out,
                         cudaStream_t st);
 // Device word the tcgen05 kernels set when a bounded wait gives up (0 = fine).
 int32_t *tc_error_flag(void *tc_scratch, int max_pairs, int H);
+// The expert-sorted fp16 hi/lo row buffers inside the tensor-path scratch.
+void tc_rows(void *tc_scratch, int max_pairs, int H, __half **xp_hi, __half **xp_lo);
 
 // Combine --------------------------------------------------------------------
 cudaError_t launch_combine(const Dims &d, const float *residual, const RouteOut &r,
                            const float *y, int T, float *out, cudaStream_t st);
+
+// Expert parallelism --------------------------------------------------------------
+struct EpPlan {
+    int N = 0, E_loc = 0, R = 0;                         // R: rows this rank receives
+    std::vector<int> send_off, send_rows;                 // [N] local expert-sorted rows per destination
+    std::vector<int> recv_off, recv_rows;                 // [N] received rows per source (source-major)
+    std::vector<int> offsets_loc;                         // [E_loc+1] expert-major row ranges
+    std::vector<int> seg;                                 // [N*E_loc][3] (source row, expert-major row, length)
+};
+// Host-only planning of one exchange.  local_offsets [N*E_loc+1]: this rank's
+// expert-sorted pair ranges; recv_counts [N][E_loc]: pairs each source routes to
+// this rank's experts.  Returns 0, or -1 on inconsistent input.
+int ep_plan(int N, int E_loc, int rank, const int32_t *local_offsets, const int32_t *recv_counts, EpPlan *p);
+
+struct NcclApi {
+    ncclResult_t (*ncclGetUniqueId)(ncclUniqueId *);
+    ncclResult_t (*ncclCommInitRank)(ncclComm_t *, int, ncclUniqueId, int);
+    ncclResult_t (*ncclCommDestroy)(ncclComm_t);
+    ncclResult_t (*ncclCommAbort)(ncclComm_t);
+    ncclResult_t (*ncclGroupStart)();
+    ncclResult_t (*ncclGroupEnd)();
+    ncclResult_t (*ncclSend)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+    ncclResult_t (*ncclRecv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+    const char *(*ncclGetErrorString)(ncclResult_t);
+    ncclResult_t (*ncclCommGetAsyncError)(ncclComm_t, ncclResult_t *);
+};
+extern NcclApi g_nccl;
+// Resolves NCCL from libnccl.so.2 once; false (with a reason) if unavailable.
+bool nccl_load(std::string *err);
+cudaError_t launch_ep_reorder(const int32_t *seg_dev, int nseg, int H, const __half *src_hi, const __half *src_lo,
+                              __half *dst_hi, __half *dst_lo, int32_t *ret_map, cudaStream_t st);
+cudaError_t launch_ep_active(const int32_t *offsets, int E_loc, int32_t *active, cudaStream_t st);
 
 // Sets the message amoe_last_error(NULL) returns on the calling thread.
 void set_thread_error(const std::string &msg);

@@ -8,6 +8,7 @@
 #include "../../include/amoe.h"
 #include "amoe_internal.cuh"
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -33,7 +34,8 @@ struct LayerBlock {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-LayerBlock layer_block(const Dims &d) {
+// Dims d: router over d.E experts; experts E_x of them stored (E_x < d.E in EP mode).
+LayerBlock layer_block(const Dims &d, int E_x) {
     LayerBlock b{};
     size_t o = 0;
     auto take = [&](size_t bytes) {
@@ -41,10 +43,10 @@ LayerBlock layer_block(const Dims &d) {
         o = align256(o + bytes);
         return at;
     };
-    const size_t H = d.H, I = d.I, E = d.E;
+    const size_t H = d.H, I = d.I, E = E_x;
     b.norm = take(H * 4);
-    b.router_w = take(H * E * 4);
-    b.router_b = take(E * 4);
+    b.router_w = take(H * (size_t)d.E * 4);
+    b.router_b = take((size_t)d.E * 4);
     b.gu_b = take(E * 2 * I * 4);
     b.dn_b = take(E * H * 4);
     b.gu_cexp = take(E * 4);
@@ -83,7 +85,8 @@ using namespace amoe;
 
 struct amoe_ctx {
     amoe_config cfg{};
-    Dims d{};
+    Dims d{};       // routing (all experts)
+    Dims dx{};      // expert stage (this rank's experts)
     LayerBlock blk{};
     cudaStream_t stream = nullptr;       // compute
     cudaStream_t copy_stream = nullptr;  // layer streaming
@@ -112,6 +115,17 @@ struct amoe_ctx {
     int32_t *io_idx = nullptr;
     float *io_w = nullptr;
     int last_T = 0;
+
+    // expert parallelism (ep_size > 1)
+    int ep_n = 1, ep_rank = 0, e_loc = 0;
+    ncclComm_t comm = nullptr;
+    size_t r_max = 0;                          // rows this rank can receive
+    __half *recv_hi = nullptr, *recv_lo = nullptr, *ex_hi = nullptr, *ex_lo = nullptr;
+    float *y_send = nullptr;
+    int32_t *ret_map = nullptr, *seg_dev = nullptr, *offsets_loc = nullptr, *active_loc = nullptr,
+            *recv_counts = nullptr;
+    int32_t *h_stage = nullptr;                // pinned: offsets, recv counts, segments
+    EpPlan plan;
 
     // diagnostics
     bool profiling = false;
@@ -161,7 +175,11 @@ std::string validate(const amoe_config *c) {
     if (c->stream_slots != 0 && c->stream_slots < 2) return "stream_slots must be 0 or >= 2";
     if (c->ep_size < 1 || c->ep_rank < 0 || c->ep_rank >= c->ep_size)
         return "ep_rank must be in [0, ep_size)";
-    if (c->ep_size > 1) return "expert parallelism is not available in this build";
+    if (c->ep_size > 1) {
+        if (c->experts % c->ep_size) return "experts must divide evenly over ep_size";
+        if (!c->nccl_id) return "nccl_id must be set when ep_size > 1";
+        if (c->stream_slots) return "expert parallelism keeps every layer resident (stream_slots 0)";
+    }
     if (c->path < AMOE_PATH_AUTO || c->path > AMOE_PATH_TENSOR) return "unknown path";
     return "";
 }
@@ -172,6 +190,10 @@ int alloc_scratch(amoe_ctx *c) {
     c->max_tokens = (int)T;
     c->nchunk_max = (int)((T + kRouteTokens - 1) / kRouteTokens);
     const size_t partial = route_partial_elems((int)T, d.H, d.E);
+    const size_t R = c->ep_n > 1 ? (size_t)c->ep_n * P : 0;  // worst case: every source sends all pairs here
+    c->r_max = R;
+    const size_t A = R > P ? R : P;  // rows of the expert stage
+    const size_t nseg = (size_t)c->ep_n * (c->e_loc > 0 ? c->e_loc : 1);
     size_t off = 0;
     struct Part {
         void **dst;
@@ -192,14 +214,24 @@ int alloc_scratch(amoe_ctx *c) {
         {(void **)&c->r.inv, P * 4},
         {(void **)&c->partial, partial * 8},
         {(void **)&c->arrivals, (size_t)c->nchunk_max * 4},
-        {(void **)&c->act_hi, P * d.I * 2},
-        {(void **)&c->act_lo, P * d.I * 2},
+        {(void **)&c->act_hi, A * d.I * 2},
+        {(void **)&c->act_lo, A * d.I * 2},
         {(void **)&c->y, P * d.H * 4},
         {(void **)&c->tc_scratch, tc_scratch_bytes((int)P, d.H, d.I)},
         {(void **)&c->io_in, T * d.H * 4},
         {(void **)&c->io_out, T * d.H * 4},
         {(void **)&c->io_idx, P * 4},
         {(void **)&c->io_w, P * 4},
+        {(void **)&c->recv_hi, R * d.H * 2},
+        {(void **)&c->recv_lo, R * d.H * 2},
+        {(void **)&c->ex_hi, R * d.H * 2},
+        {(void **)&c->ex_lo, R * d.H * 2},
+        {(void **)&c->y_send, R * d.H * 4},
+        {(void **)&c->ret_map, R * 4},
+        {(void **)&c->seg_dev, R ? nseg * 3 * 4 : 0},
+        {(void **)&c->offsets_loc, R ? (size_t)(c->e_loc + 1) * 4 : 0},
+        {(void **)&c->active_loc, R ? (size_t)(c->e_loc + 1) * 4 : 0},
+        {(void **)&c->recv_counts, R ? nseg * 4 : 0},
     };
     std::vector<size_t> at(parts.size());
     for (size_t i = 0; i < parts.size(); ++i) {
@@ -211,6 +243,7 @@ int alloc_scratch(amoe_ctx *c) {
     for (size_t i = 0; i < parts.size(); ++i) *parts[i].dst = parts[i].bytes ? base + at[i] : nullptr;
     AMOE_CUDA(c, cudaMemset(c->arrivals, 0, (size_t)c->nchunk_max * 4));
     AMOE_CUDA(c, cudaMemset(tc_error_flag(c->tc_scratch, (int)P, d.H), 0, sizeof(int32_t)));
+    if (R) AMOE_CUDA(c, cudaHostAlloc(&c->h_stage, ((size_t)d.E + 1 + nseg + nseg * 3 + 64) * 4, 0));
     return AMOE_OK;
 }
 
@@ -279,6 +312,8 @@ void release(amoe_ctx *c) {
     for (auto e : c->slot_ready) if (e) cudaEventDestroy(e);
     for (auto e : c->slot_free) if (e) cudaEventDestroy(e);
     if (c->scratch) cudaFree(c->scratch);
+    if (c->h_stage) cudaFreeHost(c->h_stage);
+    if (c->comm) g_nccl.ncclCommDestroy(c->comm);
     for (auto &t : c->pending)
         for (int i = 0; i < t.n; ++i) cudaEventDestroy(t.ev[i]);
     for (auto e : c->event_pool) cudaEventDestroy(e);
@@ -343,6 +378,106 @@ int use_tensor_path(const amoe_ctx *c, int T) {
     return tc_supported() && pairs_per_expert >= 32;
 }
 
+int nccl_fail(amoe_ctx *c, ncclResult_t r, const char *what) {
+    return fail(c, AMOE_ERR_NCCL, std::string(what) + ": " + g_nccl.ncclGetErrorString(r));
+}
+
+#define AMOE_NCCL(ctx, call)                                     \
+    do {                                                         \
+        ncclResult_t r_ = (call);                                \
+        if (r_ != ncclSuccess) return nccl_fail(ctx, r_, #call); \
+    } while (0)
+
+// Expert-parallel expert stage: send each routed row to the rank that owns its
+// expert, run this rank's experts on what arrives, and bring the outputs back
+// into c->y at the rows' local positions (where the combine reads them).
+int ep_experts(amoe_ctx *c, const LayerDev &L, int T, cudaStream_t st, StageTimer &timer, bool *used_tc) {
+    const Dims &d = c->d;
+    const int N = c->ep_n, El = c->e_loc, H = d.H;
+    const int P_cap = c->max_tokens * d.k;
+    __half *xp_hi, *xp_lo;
+    tc_rows(c->tc_scratch, P_cap, H, &xp_hi, &xp_lo);
+    // 1. local expert-sorted rows (positions + gather)
+    AMOE_CUDA(c, launch_scatter(d, T, c->r, true, xp_hi, xp_lo, st));
+    c->stats.launches += 1;
+    // 2. per-expert counts to every rank
+    AMOE_NCCL(c, g_nccl.ncclGroupStart());
+    for (int q = 0; q < N; ++q) {
+        AMOE_NCCL(c, g_nccl.ncclSend(c->r.counts + (size_t)q * El, El, ncclInt32, q, c->comm, st));
+        AMOE_NCCL(c, g_nccl.ncclRecv(c->recv_counts + (size_t)q * El, El, ncclInt32, q, c->comm, st));
+    }
+    AMOE_NCCL(c, g_nccl.ncclGroupEnd());
+    int32_t *h_off = c->h_stage, *h_recv = c->h_stage + d.E + 1, *h_seg = h_recv + (size_t)N * El;
+    AMOE_CUDA(c, cudaMemcpyAsync(h_off, c->r.offsets, (size_t)(d.E + 1) * 4, cudaMemcpyDeviceToHost, st));
+    AMOE_CUDA(c, cudaMemcpyAsync(h_recv, c->recv_counts, (size_t)N * El * 4, cudaMemcpyDeviceToHost, st));
+    AMOE_CUDA(c, cudaStreamSynchronize(st));
+    // 3. plan
+    if (ep_plan(N, El, c->ep_rank, h_off, h_recv, &c->plan))
+        return fail(c, AMOE_ERR_STATE, "inconsistent expert counts from the expert-parallel group");
+    const EpPlan &pl = c->plan;
+    if ((size_t)pl.R > c->r_max)
+        return fail(c, AMOE_ERR_STATE, "expert-parallel receive exceeds this rank's buffers");
+    // 4. dispatch the rows (fp16 hi and lo planes)
+    AMOE_NCCL(c, g_nccl.ncclGroupStart());
+    for (int q = 0; q < N; ++q) {
+        const size_t so = (size_t)pl.send_off[q] * H, sn = (size_t)pl.send_rows[q] * H;
+        const size_t ro = (size_t)pl.recv_off[q] * H, rn = (size_t)pl.recv_rows[q] * H;
+        if (sn) {
+            AMOE_NCCL(c, g_nccl.ncclSend(xp_hi + so, sn, ncclFloat16, q, c->comm, st));
+            AMOE_NCCL(c, g_nccl.ncclSend(xp_lo + so, sn, ncclFloat16, q, c->comm, st));
+        }
+        if (rn) {
+            AMOE_NCCL(c, g_nccl.ncclRecv(c->recv_hi + ro, rn, ncclFloat16, q, c->comm, st));
+            AMOE_NCCL(c, g_nccl.ncclRecv(c->recv_lo + ro, rn, ncclFloat16, q, c->comm, st));
+        }
+    }
+    AMOE_NCCL(c, g_nccl.ncclGroupEnd());
+    timer.mark(5);
+    // 5. expert-major order for this rank's experts
+    std::memcpy(h_seg, pl.seg.data(), pl.seg.size() * 4);
+    std::memcpy(h_seg + pl.seg.size(), pl.offsets_loc.data(), pl.offsets_loc.size() * 4);
+    AMOE_CUDA(c, cudaMemcpyAsync(c->seg_dev, h_seg, pl.seg.size() * 4, cudaMemcpyHostToDevice, st));
+    AMOE_CUDA(c, cudaMemcpyAsync(c->offsets_loc, h_seg + pl.seg.size(), pl.offsets_loc.size() * 4,
+                                 cudaMemcpyHostToDevice, st));
+    AMOE_CUDA(c, launch_ep_reorder(c->seg_dev, N * El, H, c->recv_hi, c->recv_lo, c->ex_hi, c->ex_lo, c->ret_map,
+                                   st));
+    AMOE_CUDA(c, launch_ep_active(c->offsets_loc, El, c->active_loc, st));
+    c->stats.launches += 2;
+    // 6. this rank's experts; down writes straight into the return buffer
+    int max_rows = 0;
+    for (int e = 0; e < El; ++e) max_rows = std::max(max_rows, pl.offsets_loc[e + 1] - pl.offsets_loc[e]);
+    int32_t *flag = tc_error_flag(c->tc_scratch, P_cap, H);
+    const bool tc = c->cfg.path == AMOE_PATH_TENSOR ||
+                    (c->cfg.path == AMOE_PATH_AUTO && tc_supported() && pl.R >= 32 * El);
+    *used_tc = tc;
+    if (pl.R > 0) {
+        if (tc) {
+            int n = 0;
+            AMOE_CUDA(c, launch_tc_experts(c->dx, L, c->offsets_loc, c->ex_hi, c->ex_lo, (int)c->r_max, c->act_hi,
+                                           c->act_lo, c->y_send, c->ret_map, flag, st, &timer_hook, &timer, &n));
+            c->stats.launches += n;
+        } else {
+            GemvRows rows{c->ex_hi, c->ex_lo, nullptr, c->offsets_loc, c->active_loc, c->ret_map,
+                          std::min(pl.R, El)};
+            AMOE_CUDA(c, launch_gemv_gate_up(c->dx, L, rows, max_rows, c->act_hi, c->act_lo, flag, st));
+            timer.mark(2);
+            AMOE_CUDA(c, launch_gemv_down(c->dx, L, rows, max_rows, c->act_hi, c->act_lo, c->y_send, flag, st));
+            timer.mark(3);
+            c->stats.launches += 2;
+        }
+    }
+    // 7. outputs back to the ranks the rows came from, at their local positions
+    AMOE_NCCL(c, g_nccl.ncclGroupStart());
+    for (int q = 0; q < N; ++q) {
+        const size_t so = (size_t)pl.send_off[q] * H, sn = (size_t)pl.send_rows[q] * H;
+        const size_t ro = (size_t)pl.recv_off[q] * H, rn = (size_t)pl.recv_rows[q] * H;
+        if (rn) AMOE_NCCL(c, g_nccl.ncclSend(c->y_send + ro, rn, ncclFloat32, q, c->comm, st));
+        if (sn) AMOE_NCCL(c, g_nccl.ncclRecv(c->y + so, sn, ncclFloat32, q, c->comm, st));
+    }
+    AMOE_NCCL(c, g_nccl.ncclGroupEnd());
+    return AMOE_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -373,7 +508,11 @@ int amoe_create(const amoe_config *cfg, amoe_ctx **out) {
     c->cfg = *cfg;
     c->cfg.nccl_id = nullptr;
     c->d = Dims{cfg->hidden, cfg->intermediate, cfg->experts, cfg->top_k, cfg->rms_eps};
-    c->blk = layer_block(c->d);
+    c->ep_n = cfg->ep_size;
+    c->ep_rank = cfg->ep_rank;
+    c->e_loc = cfg->experts / cfg->ep_size;
+    c->dx = Dims{cfg->hidden, cfg->intermediate, c->e_loc, cfg->top_k, cfg->rms_eps};
+    c->blk = layer_block(c->d, c->e_loc);
     int rc = AMOE_OK;
     do {
         cudaError_t e = cudaSetDevice(cfg->device);
@@ -382,6 +521,18 @@ int amoe_create(const amoe_config *cfg, amoe_ctx **out) {
         if (e != cudaSuccess) { rc = cuda_fail(c, e, "cudaStreamCreate"); break; }
         e = cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking);
         if (e != cudaSuccess) { rc = cuda_fail(c, e, "cudaStreamCreate"); break; }
+        if (c->ep_n > 1) {
+            std::string why;
+            if (!nccl_load(&why)) { rc = fail(c, AMOE_ERR_NCCL, why); break; }
+            ncclUniqueId id;
+            std::memcpy(&id, cfg->nccl_id, sizeof(id));
+            const ncclResult_t nr = g_nccl.ncclCommInitRank(&c->comm, c->ep_n, id, c->ep_rank);
+            if (nr != ncclSuccess) {
+                c->comm = nullptr;
+                rc = fail(c, AMOE_ERR_NCCL, std::string("ncclCommInitRank: ") + g_nccl.ncclGetErrorString(nr));
+                break;
+            }
+        }
         c->layer_dev.assign(cfg->layers, nullptr);
         c->layer_host.assign(cfg->layers, nullptr);
         c->uploaded.assign(cfg->layers, false);
@@ -431,8 +582,11 @@ int amoe_upload_layer(amoe_ctx *c, int32_t layer, const float *norm_gain, const 
     if (!norm_gain || !router_w || !router_b || !gate_up || !gate_up_b || !down || !down_b)
         return fail(c, AMOE_ERR_INVALID, "layer tensors must not be NULL");
     const Dims &d = c->d;
-    const size_t H = d.H, I = d.I, E = d.E;
-    const size_t gu_bytes = E * 2 * I * (H / 32) * 17, dn_bytes = E * H * (I / 32) * 17;
+    const size_t H = d.H, I = d.I, E_all = d.E;
+    // this context stores experts [e0, e0 + E) (all of them unless expert-parallel)
+    const size_t E = (size_t)c->e_loc, e0 = (size_t)c->ep_rank * c->e_loc;
+    const size_t gu_expert = 2 * I * (H / 32) * 17, dn_expert = H * (I / 32) * 17;
+    const size_t gu_bytes = E * gu_expert, dn_bytes = E * dn_expert;
     // Device-format block: built in a temporary device buffer, then kept there
     // (resident) or copied to pinned host memory (streaming).
     uint8_t *blockp = nullptr, *staging = nullptr;
@@ -467,14 +621,14 @@ int amoe_upload_layer(amoe_ctx *c, int32_t layer, const float *norm_gain, const 
     const LayerDev L = layer_view(blockp, c->blk);
     cudaStream_t st = c->stream;
     UP_CUDA(cudaMemcpyAsync(L.norm_gain, norm_gain, H * 4, cudaMemcpyHostToDevice, st));
-    UP_CUDA(cudaMemcpyAsync(L.router_w, router_w, E * H * 4, cudaMemcpyHostToDevice, st));
-    UP_CUDA(cudaMemcpyAsync(L.router_b, router_b, E * 4, cudaMemcpyHostToDevice, st));
-    UP_CUDA(cudaMemcpyAsync(L.gu_b, gate_up_b, E * 2 * I * 4, cudaMemcpyHostToDevice, st));
-    UP_CUDA(cudaMemcpyAsync(L.dn_b, down_b, E * H * 4, cudaMemcpyHostToDevice, st));
-    UP_CUDA(cudaMemcpyAsync(staging, gate_up, gu_bytes, cudaMemcpyHostToDevice, st));
+    UP_CUDA(cudaMemcpyAsync(L.router_w, router_w, E_all * H * 4, cudaMemcpyHostToDevice, st));
+    UP_CUDA(cudaMemcpyAsync(L.router_b, router_b, E_all * 4, cudaMemcpyHostToDevice, st));
+    UP_CUDA(cudaMemcpyAsync(L.gu_b, gate_up_b + e0 * 2 * I, E * 2 * I * 4, cudaMemcpyHostToDevice, st));
+    UP_CUDA(cudaMemcpyAsync(L.dn_b, down_b + e0 * H, E * H * 4, cudaMemcpyHostToDevice, st));
+    UP_CUDA(cudaMemcpyAsync(staging, gate_up + e0 * gu_expert, gu_bytes, cudaMemcpyHostToDevice, st));
     UP_CUDA(launch_repack(staging, (int)E, (int)(2 * I), (int)H, true, L.gu_q, L.gu_s, st));
     UP_CUDA(cudaStreamSynchronize(st));  // staging is reused for down
-    UP_CUDA(cudaMemcpyAsync(staging, down, dn_bytes, cudaMemcpyHostToDevice, st));
+    UP_CUDA(cudaMemcpyAsync(staging, down + e0 * dn_expert, dn_bytes, cudaMemcpyHostToDevice, st));
     UP_CUDA(launch_repack(staging, (int)E, (int)H, (int)I, false, L.dn_q, L.dn_s, st));
     UP_CUDA(launch_cexp(L.gu_s, 2 * I * (H / 32), (int)E, L.gu_cexp, st));
     UP_CUDA(launch_cexp(L.dn_s, H * (I / 32), (int)E, L.dn_cexp, st));
@@ -527,22 +681,30 @@ int amoe_forward_device(amoe_ctx *c, int32_t layer, const float *residual, int32
     AMOE_CUDA(c, launch_route_impl(d, L, residual, T, c->r, c->partial, c->arrivals, st, &timer_hook, &timer));
     const int nchunk = (T + kRouteTokens - 1) / kRouteTokens;
     c->stats.launches += nchunk > 1 ? 2 : 1;
-    const bool tc = use_tensor_path(c, T);
-    if (!tc && nchunk > 1) {
+    bool tc = use_tensor_path(c, T);
+    if (c->ep_n > 1) {
+        timer.mark(1);
+        rc = ep_experts(c, L, T, st, timer, &tc);
+        if (rc) return rc;
+    } else if (!tc && nchunk > 1) {
         AMOE_CUDA(c, launch_scatter(d, T, c->r, false, nullptr, nullptr, st));
         c->stats.launches += 1;
     }
-    timer.mark(1);
-    if (tc) {
+    if (c->ep_n > 1) {
+    } else if (tc) {
+        timer.mark(1);
         int n = 0;
         AMOE_CUDA(c, launch_tc_forward(d, L, c->r, T, c->act_hi, c->act_lo, c->y, c->tc_scratch,
                                        c->max_tokens * d.k, st, &timer_hook, &timer, &n));
         c->stats.launches += n;
     } else {
+        timer.mark(1);
         int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H);
-        AMOE_CUDA(c, launch_gemv_gate_up(d, L, c->r, T, c->act_hi, c->act_lo, flag, st));
+        GemvRows rows{c->r.x_hi, c->r.x_lo, c->r.perm_pair, c->r.offsets, c->r.active, nullptr,
+                      std::min(T * d.k, d.E)};
+        AMOE_CUDA(c, launch_gemv_gate_up(d, L, rows, T, c->act_hi, c->act_lo, flag, st));
         timer.mark(2);
-        AMOE_CUDA(c, launch_gemv_down(d, L, c->r, T, c->act_hi, c->act_lo, c->y, flag, st));
+        AMOE_CUDA(c, launch_gemv_down(d, L, rows, T, c->act_hi, c->act_lo, c->y, flag, st));
         timer.mark(3);
         c->stats.launches += 2;
     }
@@ -623,6 +785,50 @@ int amoe_last_routing(amoe_ctx *c, float *logits, int32_t *perm_pair, int32_t *c
     if (counts) AMOE_CUDA(c, cudaMemcpy(counts, c->r.counts, (size_t)d.E * 4, cudaMemcpyDeviceToHost));
     if (offsets)
         AMOE_CUDA(c, cudaMemcpy(offsets, c->r.offsets, (size_t)(d.E + 1) * 4, cudaMemcpyDeviceToHost));
+    return AMOE_OK;
+}
+
+int amoe_ep_unique_id(void *out) {
+    if (!out) {
+        set_thread_error("out must not be NULL");
+        return AMOE_ERR_INVALID;
+    }
+    std::string why;
+    if (!nccl_load(&why)) {
+        set_thread_error(why);
+        return AMOE_ERR_NCCL;
+    }
+    ncclUniqueId id;
+    const ncclResult_t r = g_nccl.ncclGetUniqueId(&id);
+    if (r != ncclSuccess) {
+        set_thread_error(std::string("ncclGetUniqueId: ") + g_nccl.ncclGetErrorString(r));
+        return AMOE_ERR_NCCL;
+    }
+    std::memcpy(out, &id, sizeof(id));
+    return AMOE_OK;
+}
+
+int amoe_ep_plan(int32_t n_ranks, int32_t experts_per_rank, int32_t rank, const int32_t *local_offsets,
+                 const int32_t *recv_counts, int32_t *send_off, int32_t *send_rows, int32_t *recv_off,
+                 int32_t *recv_rows, int32_t *offsets_loc, int32_t *segments) {
+    if (!local_offsets || !recv_counts) {
+        set_thread_error("counts must not be NULL");
+        return AMOE_ERR_INVALID;
+    }
+    EpPlan p;
+    if (ep_plan(n_ranks, experts_per_rank, rank, local_offsets, recv_counts, &p)) {
+        set_thread_error("inconsistent expert-parallel counts");
+        return AMOE_ERR_INVALID;
+    }
+    auto put = [](int32_t *dst, const std::vector<int> &v) {
+        if (dst) std::memcpy(dst, v.data(), v.size() * 4);
+    };
+    put(send_off, p.send_off);
+    put(send_rows, p.send_rows);
+    put(recv_off, p.recv_off);
+    put(recv_rows, p.recv_rows);
+    put(offsets_loc, p.offsets_loc);
+    put(segments, p.seg);
     return AMOE_OK;
 }
 

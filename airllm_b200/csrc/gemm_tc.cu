@@ -69,6 +69,7 @@ struct TcParams {
     int gate_up;
     __half *act_hi, *act_lo;  // [P][R/2]
     float *y;                 // [P][R]
+    const int32_t *y_rows;    // output row of each position (NULL: the position)
     int32_t *err;
 };
 
@@ -453,8 +454,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
                             const int tok = col0 + j;
-                            if (tok < ti.ntok && row_ok)
-                                p.y[(size_t)(ti.pos0 + tok) * p.R + rrow] = __uint_as_float(v[j]) * scale + bd;
+                            if (tok < ti.ntok && row_ok) {
+                                const int pos = ti.pos0 + tok;
+                                const size_t orow = p.y_rows ? (size_t)p.y_rows[pos] : (size_t)pos;
+                                p.y[orow * p.R + rrow] = __uint_as_float(v[j]) * scale + bd;
+                            }
                         }
                     }
                 }
@@ -581,9 +585,16 @@ cudaError_t launch_cexp(const uint8_t *s_plane, size_t bytes_per_expert, int E, 
 
 int32_t *tc_error_flag(void *tc_scratch, int max_pairs, int H) { return carve(tc_scratch, max_pairs, H).err; }
 
-cudaError_t launch_tc_forward(const Dims &d, const LayerDev &L, const RouteOut &r, int T, __half *act_hi,
-                              __half *act_lo, float *y, void *tc_scratch, int max_pairs, cudaStream_t st,
-                              StageHook hook, void *hook_arg, int *launches) {
+void tc_rows(void *tc_scratch, int max_pairs, int H, __half **xp_hi, __half **xp_lo) {
+    const TcScratch t = carve(tc_scratch, max_pairs, H);
+    *xp_hi = t.xp_hi;
+    *xp_lo = t.xp_lo;
+}
+
+cudaError_t launch_tc_experts(const Dims &d, const LayerDev &L, const int32_t *offsets, const __half *b_hi,
+                              const __half *b_lo, int rows_cap, __half *act_hi, __half *act_lo, float *y,
+                              const int32_t *y_rows, int32_t *err, cudaStream_t st, StageHook hook,
+                              void *hook_arg, int *launches) {
     if (!tc_supported()) return cudaErrorNotSupported;
     static bool attr_set = false;
     if (!attr_set) {
@@ -592,22 +603,15 @@ cudaError_t launch_tc_forward(const Dims &d, const LayerDev &L, const RouteOut &
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
-    const TcScratch ts = carve(tc_scratch, max_pairs, d.H);
-    *launches = 0;
-    // 1. stable token->expert positions and the expert-sorted fp16 hi/lo copy of the
-    //    normalized rows (the gate_up B operand)
-    cudaError_t e = launch_scatter(d, T, r, true, ts.xp_hi, ts.xp_lo, st);
-    if (e != cudaSuccess) return e;
-    ++*launches;
-    if (hook) hook(hook_arg, 5);
     const int grid = g_num_sms > 0 ? g_num_sms : 148;
-    // 2. gate_up + SwiGLU
+    cudaError_t e;
+    // gate_up + SwiGLU
     {
         Maps m;
-        e = make_maps(m, ts.xp_hi, ts.xp_lo, d.H, max_pairs, L.gu_q, L.gu_s, d.E, 2 * d.I);
+        e = make_maps(m, b_hi, b_lo, d.H, rows_cap, L.gu_q, L.gu_s, d.E, 2 * d.I);
         if (e != cudaSuccess) return e;
         TcParams p{};
-        p.offsets = r.offsets;
+        p.offsets = offsets;
         p.cexp = L.gu_cexp;
         p.bias = L.gu_b;
         p.R = 2 * d.I;
@@ -618,20 +622,20 @@ cudaError_t launch_tc_forward(const Dims &d, const LayerDev &L, const RouteOut &
         p.gate_up = 1;
         p.act_hi = act_hi;
         p.act_lo = act_lo;
-        p.err = ts.err;
+        p.err = err;
         tc_gemm_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(m.bhi, m.blo, m.araw, m.asc, p);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         ++*launches;
         if (hook) hook(hook_arg, 2);
     }
-    // 3. down
+    // down
     {
         Maps m;
-        e = make_maps(m, act_hi, act_lo, d.I, max_pairs, L.dn_q, L.dn_s, d.E, d.H);
+        e = make_maps(m, act_hi, act_lo, d.I, rows_cap, L.dn_q, L.dn_s, d.E, d.H);
         if (e != cudaSuccess) return e;
         TcParams p{};
-        p.offsets = r.offsets;
+        p.offsets = offsets;
         p.cexp = L.dn_cexp;
         p.bias = L.dn_b;
         p.R = d.H;
@@ -641,7 +645,8 @@ cudaError_t launch_tc_forward(const Dims &d, const LayerDev &L, const RouteOut &
         p.mblocks = (p.R + ROWS - 1) / ROWS;
         p.gate_up = 0;
         p.y = y;
-        p.err = ts.err;
+        p.y_rows = y_rows;
+        p.err = err;
         tc_gemm_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(m.bhi, m.blo, m.araw, m.asc, p);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
@@ -649,6 +654,26 @@ cudaError_t launch_tc_forward(const Dims &d, const LayerDev &L, const RouteOut &
         if (hook) hook(hook_arg, 3);
     }
     return cudaSuccess;
+}
+
+cudaError_t launch_tc_forward(const Dims &d, const LayerDev &L, const RouteOut &r, int T, __half *act_hi,
+                              __half *act_lo, float *y, void *tc_scratch, int max_pairs, cudaStream_t st,
+                              StageHook hook, void *hook_arg, int *launches) {
+    if (!tc_supported()) return cudaErrorNotSupported;
+    const TcScratch ts = carve(tc_scratch, max_pairs, d.H);
+    *launches = 0;
+    // 1. stable token->expert positions and the expert-sorted fp16 hi/lo copy of the
+    //    normalized rows (the gate_up B operand)
+    cudaError_t e = launch_scatter(d, T, r, true, ts.xp_hi, ts.xp_lo, st);
+    if (e != cudaSuccess) return e;
+    ++*launches;
+    if (hook) hook(hook_arg, 5);
+    // 2. the two grouped GEMMs
+    int n = 0;
+    e = launch_tc_experts(d, L, r.offsets, ts.xp_hi, ts.xp_lo, max_pairs, act_hi, act_lo, y, nullptr, ts.err, st,
+                          hook, hook_arg, &n);
+    *launches += n;
+    return e;
 }
 
 }  // namespace amoe

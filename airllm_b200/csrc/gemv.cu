@@ -28,7 +28,8 @@ struct GemvParams {
     const float *bias;     // [E][R] (GGUF row order)
     const __half *x_hi;    // activation rows [*][K]
     const __half *x_lo;
-    const int32_t *perm_pair;
+    const int32_t *perm_pair;  // gate_up: position -> pair id; NULL: rows are indexed by position
+    const int32_t *y_rows;     // down: output row of each position; NULL: the position itself
     const int32_t *offsets;
     const int32_t *active;
     int R, K, E, k;
@@ -165,7 +166,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
             const int tok = tok0 + 8 * n + g;
             valid[n] = tok < m_e;
             int row = 0;
-            if (valid[n]) row = GATE_UP ? p.perm_pair[base + tok] / p.k : base + tok;
+            if (valid[n]) row = (GATE_UP && p.perm_pair) ? p.perm_pair[base + tok] / p.k : base + tok;
             xh[n] = p.x_hi + (size_t)row * p.K + 8 * c;
             xl[n] = p.x_lo + (size_t)row * p.K + 8 * c;
             if (tok0 + 8 * n < m_e) ng_live = n + 1;
@@ -252,8 +253,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
                         p.act_lo[(size_t)pos * (p.R / 2) + pr] = lo;
                     } else {
                         const int h = kTileRows * rt + g;
-                        p.y[(size_t)pos * p.R + h] = v[j] + p.bias[(size_t)e * p.R + h];
-                        p.y[(size_t)pos * p.R + h + 8] = v[2 + j] + p.bias[(size_t)e * p.R + h + 8];
+                        const size_t orow = p.y_rows ? (size_t)p.y_rows[pos] : (size_t)pos;
+                        p.y[orow * p.R + h] = v[j] + p.bias[(size_t)e * p.R + h];
+                        p.y[orow * p.R + h + 8] = v[2 + j] + p.bias[(size_t)e * p.R + h + 8];
                     }
                 }
             }
@@ -284,29 +286,29 @@ cudaError_t launch(const GemvParams &p, int T, int max_active, cudaStream_t st) 
 
 }  // namespace
 
-cudaError_t launch_gemv_gate_up(const Dims &d, const LayerDev &L, const RouteOut &r, int T,
+cudaError_t launch_gemv_gate_up(const Dims &d, const LayerDev &L, const GemvRows &rows, int T,
                                 __half *act_hi, __half *act_lo, int32_t *err, cudaStream_t st) {
     GemvParams p{};
     p.err = err;
     p.q = L.gu_q;
     p.s = L.gu_s;
     p.bias = L.gu_b;
-    p.x_hi = r.x_hi;
-    p.x_lo = r.x_lo;
-    p.perm_pair = r.perm_pair;
-    p.offsets = r.offsets;
-    p.active = r.active;
+    p.x_hi = rows.x_hi;
+    p.x_lo = rows.x_lo;
+    p.perm_pair = rows.perm_pair;
+    p.offsets = rows.offsets;
+    p.active = rows.active;
     p.R = 2 * d.I;
     p.K = d.H;
     p.E = d.E;
     p.k = d.k;
     p.act_hi = act_hi;
     p.act_lo = act_lo;
-    const int max_active = T * d.k < d.E ? T * d.k : d.E;
+    const int max_active = rows.max_active;
     return launch<true>(p, T, max_active, st);
 }
 
-cudaError_t launch_gemv_down(const Dims &d, const LayerDev &L, const RouteOut &r, int T,
+cudaError_t launch_gemv_down(const Dims &d, const LayerDev &L, const GemvRows &rows, int T,
                              const __half *act_hi, const __half *act_lo, float *y, int32_t *err,
                              cudaStream_t st) {
     GemvParams p{};
@@ -316,15 +318,16 @@ cudaError_t launch_gemv_down(const Dims &d, const LayerDev &L, const RouteOut &r
     p.bias = L.dn_b;
     p.x_hi = act_hi;
     p.x_lo = act_lo;
-    p.perm_pair = r.perm_pair;
-    p.offsets = r.offsets;
-    p.active = r.active;
+    p.perm_pair = nullptr;
+    p.y_rows = rows.y_rows;
+    p.offsets = rows.offsets;
+    p.active = rows.active;
     p.R = d.H;
     p.K = d.I;
     p.E = d.E;
     p.k = d.k;
     p.y = y;
-    const int max_active = T * d.k < d.E ? T * d.k : d.E;
+    const int max_active = rows.max_active;
     return launch<false>(p, T, max_active, st);
 }
 

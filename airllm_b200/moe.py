@@ -79,6 +79,8 @@ SIGNATURES = {
     "amoe_last_routing": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp]),
     "amoe_set_profiling": (ctypes.c_int, [_vp, _i32]),
     "amoe_get_stats": (ctypes.c_int, [_vp, ctypes.POINTER(AmoeStats), _i32]),
+    "amoe_ep_unique_id": (ctypes.c_int, [_vp]),
+    "amoe_ep_plan": (ctypes.c_int, [_i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "amoe_route_noalloc": (ctypes.c_int, [_i32, _i32, _i32, _i32, ctypes.c_float, _vp, _i32, _vp, _vp, _vp,
                                           _vp, _vp, _vp, _vp]),
 }
@@ -122,6 +124,33 @@ def _ptr(a) -> int | None:
 
 def _c(a, dtype):
     return np.ascontiguousarray(a, dtype=dtype)
+
+
+def ep_unique_id() -> bytes:
+    """A fresh 128-byte NCCL unique id for an expert-parallel group (rank 0 makes it)."""
+    lib = load_library()
+    buf = ctypes.create_string_buffer(128)
+    rc = lib.amoe_ep_unique_id(buf)
+    if rc != AMOE_OK:
+        raise AmoeError(rc, lib.amoe_last_error(None).decode())
+    return buf.raw
+
+
+def ep_plan(n_ranks: int, experts_per_rank: int, rank: int, local_offsets, recv_counts) -> dict:
+    """Host planning of one expert-parallel exchange (amoe_ep_plan; no GPU needed)."""
+    lib = load_library()
+    lo = np.ascontiguousarray(local_offsets, np.int32)
+    rc_ = np.ascontiguousarray(recv_counts, np.int32)
+    N, El = n_ranks, experts_per_rank
+    out = {k: np.zeros(n, np.int32) for k, n in [("send_off", N), ("send_rows", N), ("recv_off", N),
+                                                  ("recv_rows", N), ("offsets_loc", El + 1),
+                                                  ("segments", N * El * 3)]}
+    rc = lib.amoe_ep_plan(N, El, rank, lo.ctypes.data, rc_.ctypes.data, *[out[k].ctypes.data for k in
+                          ("send_off", "send_rows", "recv_off", "recv_rows", "offsets_loc", "segments")])
+    if rc != AMOE_OK:
+        raise AmoeError(rc, lib.amoe_last_error(None).decode())
+    out["segments"] = out["segments"].reshape(N * El, 3)
+    return out
 
 
 class MoEBlock:

@@ -79,6 +79,8 @@ def lib():
             L.oracle_route.argtypes = [
                 ctypes.POINTER(OracleLayer), _f32p, ctypes.c_int, _f32p, _i32p, _f32p, ctypes.c_int,
             ]
+            L.oracle_expert_rows.argtypes = [ctypes.POINTER(OracleLayer), ctypes.c_int, _f32p, ctypes.c_int,
+                                             _f32p, ctypes.c_int]
             L.oracle_permute.argtypes = [_i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                          _i32p, _i32p, _i32p, _i32p]
             _lib = L
@@ -208,6 +210,22 @@ def route(layer: dict, residual, threads=None):
                             _p(w, _f32p), threads or os.cpu_count() or 1)
     _check(rc, "route")
     return logits, idx, w
+
+
+def expert_rows(layer: dict, expert: int, x_norm, threads=None):
+    """forwardExpert of `expert` on normalized rows x_norm [n, H] -> y [n, H]."""
+    L = _Layer(layer)
+    x = _c(x_norm, np.float32).reshape(-1, layer["hidden"])
+    y = np.empty_like(x)
+    _check(lib().oracle_expert_rows(ctypes.byref(L.s), expert, _p(x, _f32p), x.shape[0], _p(y, _f32p),
+                                    threads or os.cpu_count() or 1), "expert_rows")
+    return y
+
+
+def normalize_rows(layer: dict, residual):
+    """RMSNorm of every row with the layer's gain (primitives.go:50-72)."""
+    res = _c(residual, np.float32)
+    return np.stack([rmsnorm(r, layer["norm_gain"], layer["eps"]) for r in res]) if len(res) else res
 
 
 def permute(topk_idx, experts):

@@ -331,6 +331,27 @@ int oracle_moe_block(const oracle_layer *L, const float *residual, int T, float 
     return status;
 }
 
+int oracle_expert_rows(const oracle_layer *L, int expert, const float *x, int n, float *y, int threads) {
+    if (validate(L) || expert < 0 || expert >= L->experts || n < 0) return -1;
+    int status = 0;
+#pragma omp parallel num_threads(threads > 0 ? threads : 1)
+    {
+        scratch s;
+        int ok = scratch_init(&s, L, 0) == 0;
+#pragma omp for schedule(dynamic, 1)
+        for (int j = 0; j < n; ++j) {
+            if (!ok || forward_expert(L, x + (int64_t)j * L->hidden, expert, 0, &s)) {
+#pragma omp atomic write
+                status = -1;
+                continue;
+            }
+            memcpy(y + (int64_t)j * L->hidden, s.down, sizeof(float) * L->hidden);
+        }
+        scratch_free(&s);
+    }
+    return status;
+}
+
 int oracle_permute(const int32_t *topk_idx, int T, int k, int E, int32_t *perm_pair,
                    int32_t *counts, int32_t *offsets, int32_t *inv) {
     if (T < 0 || k <= 0 || E <= 0) return -1;

@@ -71,6 +71,10 @@ int oracle_moe_block(const oracle_layer *L, const float *residual, int T, float 
                      int32_t *topk_idx, float *topk_w, float *logits,
                      const int32_t *tokens, int n_tokens, int faithful, int threads);
 
+/* forwardExpert (layer.go:126-188) of expert e on n normalized rows x [n x H]:
+ * y [n x H] = down(SwiGLU(gate_up(x))) with biases. */
+int oracle_expert_rows(const oracle_layer *L, int expert, const float *x, int n, float *y, int threads);
+
 /* Router only (RMSNorm + LinearBias + top-k + selected softmax) for all T rows. */
 int oracle_route(const oracle_layer *L, const float *residual, int T, float *logits,
                  int32_t *topk_idx, float *topk_w, int threads);
