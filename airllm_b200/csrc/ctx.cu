@@ -243,7 +243,8 @@ int alloc_scratch(amoe_ctx *c) {
     for (size_t i = 0; i < parts.size(); ++i) *parts[i].dst = parts[i].bytes ? base + at[i] : nullptr;
     AMOE_CUDA(c, cudaMemset(c->arrivals, 0, (size_t)c->nchunk_max * 4));
     AMOE_CUDA(c, cudaMemset(tc_error_flag(c->tc_scratch, (int)P, d.H), 0, sizeof(int32_t)));
-    if (R) AMOE_CUDA(c, cudaHostAlloc(&c->h_stage, ((size_t)d.E + 1 + nseg + nseg * 3 + 64) * 4, 0));
+    // pinned staging: offsets [E+1], receive counts [nseg], segments [3*nseg], local offsets [E_loc+1]
+    if (R) AMOE_CUDA(c, cudaHostAlloc(&c->h_stage, ((size_t)d.E + 1 + nseg * 4 + c->e_loc + 1) * 4, 0));
     return AMOE_OK;
 }
 

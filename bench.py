@@ -223,6 +223,100 @@ def run_streaming(args):
     return 0
 
 
+def run_ep(args):
+    """Configs 3 and 4: the GPT-OSS-120B-shaped block (128 experts) with its
+    experts sharded 128/N over the N GPUs (expert parallelism, NCCL all-to-all
+    dispatch and return).  Total tokens are fixed (strong scaling); each rank
+    routes T/N of them.  Timed per step with CUDA events, max over ranks."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from airllm_b200 import moe
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    cfg = args.config
+    T = args.tokens or (8192 if cfg == 3 else W.CONFIG_TOKENS[cfg])
+    if T % world:
+        raise SystemExit("tokens must divide by the GPU count")
+    Tr = T // world
+    layer = W.config_layer(cfg)
+    x = W.make_tokens(W.CONFIG_SHAPE[cfg], T, cfg)[rank * Tr:(rank + 1) * Tr]
+    uid = None
+    if world > 1:
+        obj = [moe.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        uid = obj[0]
+    blk = moe.MoEBlock.for_layer(layer, max_tokens=Tr, device=local, path=args.path,
+                                 ep_size=world, ep_rank=rank, nccl_id=uid)
+    blk.upload_layer(0, layer)
+    del layer
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    xd = torch.from_numpy(x).cuda()
+    od = torch.empty_like(xd)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    for _ in range(args.warmup):
+        blk.forward_device(xd, od, stream=stream)
+    torch.cuda.synchronize()
+    blk.stats(reset=True)
+    blk.set_profiling(True)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        starts[i].record(stream)
+        blk.forward_device(xd, od, stream=stream)
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    blk.set_profiling(False)
+    st = blk.stats(reset=True)
+    ms_local = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    ms = ms_local
+    per_rank = [ms_local]
+    if world > 1:
+        t = torch.tensor([ms_local], dtype=torch.float64, device="cuda")
+        allt = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(allt, t)
+        per_rank = [float(v.item()) for v in allt]
+        ms = max(per_rank)
+    n = max(st["timed_forwards"], 1)
+    stage = {k: v / n for k, v in st["stage_ms"].items() if v > 0}
+    flops = T * 4 * FLOP_PER_PAIR
+    pk = peaks()
+    line = {
+        "metric": f"MoE-block tokens/s, GPT-OSS-120B shape (E=128), expert parallel over {world} GPU(s)",
+        "value": T / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "mxfp4 x fp16-hi/lo -> f32 (router f64)", "data": "synthetic (seeded)",
+        "config": {"workload": f"gptoss120b-moe-ep T={T} E=128 k=4 H=I=2880 mxfp4"
+                               + (" adversarial(8 hot experts on rank 0)" if cfg == 4 else ""),
+                   "config_index": cfg, "tokens": T, "tokens_per_rank": Tr, "experts_per_rank": 128 // world,
+                   "parallelism": f"ep{world}", "l2": "flushed (256 MiB write) before every timed step"},
+        "per_rank_ms": per_rank, "stage_ms_per_step_rank0": stage,
+        "tensor_tflops_algorithmic": flops / (ms / 1e3) / 1e12, "peak_bf16_tflops": pk["bf16_tflops"] * world,
+        "gpu_launches": int(st["launches"]), "clocks": clk,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    blk.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -232,6 +326,7 @@ def main():
     ap.add_argument("--config", type=int, default=1)
     ap.add_argument("--path", type=int, default=0, help="0 auto, 1 GEMV, 2 tcgen05")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=0, help="configs 3/4: total tokens (default 8192 / 16384)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -239,6 +334,8 @@ def main():
         return run_reference(args)
     if args.config == 2:
         return run_streaming(args)
+    if args.config in (3, 4):
+        return run_ep(args)
 
     import torch
     import torch.distributed as dist
