@@ -112,6 +112,20 @@ struct GemvRows {
     const int32_t *y_rows;      // down output row per position (NULL: the position)
     int max_active;             // grid bound on the active list
 };
+// Fused decode expert stage (decode.cu): gate_up + SwiGLU, down, combine in one
+// cooperative launch for T <= kDecodeMaxTokens.
+constexpr int kDecodeMaxTokens = 4;
+constexpr int kDecodeMaxCtas = 1024;
+struct DecodeBarrier {
+    unsigned epoch[kDecodeMaxCtas];   // launches CTA b has completed (written only by CTA b)
+    unsigned arrive[kDecodeMaxCtas];  // last grid barrier CTA b arrived at
+    unsigned release;                 // last grid barrier CTA 0 released
+};
+bool decode_supported(const Dims &d, int T, int device);
+cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, const float *residual, int T,
+                          __half *act_hi, __half *act_lo, float *y, float *out, DecodeBarrier *bar, int32_t *err,
+                          int device, cudaStream_t st);
+
 // T: upper bound on any expert's row count (sizes the token groups per pass).
 cudaError_t launch_gemv_gate_up(const Dims &d, const LayerDev &L, const GemvRows &rows, int T,
                                 __half *act_hi, __half *act_lo, int32_t *err, cudaStream_t st);
@@ -186,6 +200,33 @@ __device__ __forceinline__ float e8m0_to_float(uint32_t b) {
     // 2^(b-127); b == 0 is the subnormal 2^-127; b == 255 is NaN (tensor.go:152-155)
     uint32_t bits = b == 0 ? 0x00400000u : (b == 255 ? 0x7fc00000u : (b << 23));
     return __uint_as_float(bits);
+}
+
+// Four E8M0 bytes -> 2^(b-127) each.  Fast path (no byte is 0 or 255): the byte
+// shifted into the f32 exponent field; otherwise the exact per-byte rule.
+__device__ __forceinline__ void e8m0x4_to_float(uint32_t sv, float (&f)[4]) {
+    const uint32_t zero = (sv - 0x01010101u) & ~sv & 0x80808080u;  // some byte == 0x00
+    const uint32_t ones = (~sv - 0x01010101u) & sv & 0x80808080u;  // some byte == 0xFF
+    if ((zero | ones) == 0u) {
+        f[0] = __uint_as_float((sv << 23) & 0x7f800000u);
+        f[1] = __uint_as_float((sv << 15) & 0x7f800000u);
+        f[2] = __uint_as_float((sv << 7) & 0x7f800000u);
+        f[3] = __uint_as_float((sv >> 1) & 0x7f800000u);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) f[j] = e8m0_to_float((sv >> (8 * j)) & 0xffu);
+    }
+}
+
+// Eight E2M1 values (four bytes, low nibble first) -> four f16x2, one per byte.
+__device__ __forceinline__ uint4 e2m1x8_to_f16(uint32_t w) {
+    uint4 o;
+    asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+        " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+        " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
+        : "=r"(o.x), "=r"(o.y), "=r"(o.z), "=r"(o.w)
+        : "r"(w));
+    return o;
 }
 
 __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {

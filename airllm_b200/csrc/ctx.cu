@@ -111,6 +111,7 @@ struct amoe_ctx {
     __half *act_hi = nullptr, *act_lo = nullptr;
     float *y = nullptr;
     void *tc_scratch = nullptr;
+    DecodeBarrier *dec_bar = nullptr;  // grid barrier state of the fused decode kernel
     float *io_in = nullptr, *io_out = nullptr;
     int32_t *io_idx = nullptr;
     float *io_w = nullptr;
@@ -218,6 +219,7 @@ int alloc_scratch(amoe_ctx *c) {
         {(void **)&c->act_lo, A * d.I * 2},
         {(void **)&c->y, P * d.H * 4},
         {(void **)&c->tc_scratch, tc_scratch_bytes((int)P, d.H, d.I)},
+        {(void **)&c->dec_bar, sizeof(DecodeBarrier)},
         {(void **)&c->io_in, T * d.H * 4},
         {(void **)&c->io_out, T * d.H * 4},
         {(void **)&c->io_idx, P * 4},
@@ -242,6 +244,7 @@ int alloc_scratch(amoe_ctx *c) {
     uint8_t *base = static_cast<uint8_t *>(c->scratch);
     for (size_t i = 0; i < parts.size(); ++i) *parts[i].dst = parts[i].bytes ? base + at[i] : nullptr;
     AMOE_CUDA(c, cudaMemset(c->arrivals, 0, (size_t)c->nchunk_max * 4));
+    AMOE_CUDA(c, cudaMemset(c->dec_bar, 0, sizeof(DecodeBarrier)));
     AMOE_CUDA(c, cudaMemset(tc_error_flag(c->tc_scratch, (int)P, d.H), 0, sizeof(int32_t)));
     // pinned staging: offsets [E+1], receive counts [nseg], segments [3*nseg], local offsets [E_loc+1]
     if (R) AMOE_CUDA(c, cudaHostAlloc(&c->h_stage, ((size_t)d.E + 1 + nseg * 4 + c->e_loc + 1) * 4, 0));
@@ -358,7 +361,8 @@ int check_device_flag(amoe_ctx *c) {
     if (e != cudaSuccess) return cuda_fail(c, e, "read device error flag");
     if (v != 0) {
         cudaMemset(flag, 0, sizeof(int32_t));
-        return fail(c, AMOE_ERR_TIMEOUT, "tcgen05 pipeline wait timed out (code " + std::to_string(v) + ")");
+        if (v == 21) return fail(c, AMOE_ERR_STATE, "expert GEMV: an expert received more rows than the launch bound");
+        return fail(c, AMOE_ERR_TIMEOUT, "device pipeline wait timed out (code " + std::to_string(v) + ")");
     }
     return AMOE_OK;
 }
@@ -691,7 +695,17 @@ int amoe_forward_device(amoe_ctx *c, int32_t layer, const float *residual, int32
         AMOE_CUDA(c, launch_scatter(d, T, c->r, false, nullptr, nullptr, st));
         c->stats.launches += 1;
     }
+    bool fused = false;
     if (c->ep_n > 1) {
+    } else if (!tc && nchunk == 1 && decode_supported(d, T, c->cfg.device)) {
+        // decode: gate_up, down and the combine in one cooperative launch
+        timer.mark(1);
+        int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H);
+        AMOE_CUDA(c, launch_decode(d, L, c->r, residual, T, c->act_hi, c->act_lo, c->y, out, c->dec_bar, flag,
+                                   c->cfg.device, st));
+        timer.mark(6);
+        c->stats.launches += 1;
+        fused = true;
     } else if (tc) {
         timer.mark(1);
         int n = 0;
@@ -709,10 +723,12 @@ int amoe_forward_device(amoe_ctx *c, int32_t layer, const float *residual, int32
         timer.mark(3);
         c->stats.launches += 2;
     }
-    AMOE_CUDA(c, launch_combine(d, residual, c->r, c->y, T, out, st));
-    timer.mark(4);
+    if (!fused) {
+        AMOE_CUDA(c, launch_combine(d, residual, c->r, c->y, T, out, st));
+        timer.mark(4);
+        c->stats.launches += 1;
+    }
     timer.finish();
-    c->stats.launches += 1;
     c->stats.forwards += 1;
     c->stats.last_path = tc ? AMOE_PATH_TENSOR : AMOE_PATH_GEMV;
     if (slot >= 0) {

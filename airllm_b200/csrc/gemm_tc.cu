@@ -9,17 +9,18 @@
 // per-expert token counts only pad to 16:
 //   A (M = 128 weight rows per UMMA, two UMMAs per CTA tile = 256 rows)
 //     = MXFP4 weights.  TMA brings the raw fragment tiles (4-bit nibbles + E8M0
-//       bytes) to shared memory; four converter warps expand them to fp16 in
+//       bytes) to shared memory; sixteen converter warps expand them to fp16 in
 //       the canonical K-major SWIZZLE_128B layout (cvt.rn.f16x2.e2m1x2 and one
 //       f16x2 multiply by 2^(s-127-c_e)).  c_e is a per-expert power of two
-//       chosen at upload so every scaled weight is exact in fp16; the epilogue
-//       multiplies by 2^c_e again.
+//       chosen at upload so every scaled weight of a block within 27 binades of
+//       the expert's largest block is exact in fp16 (blocks further below are
+//       flushed to zero); the epilogue multiplies by 2^c_e again.
 //   B (N = tokens of the tile, multiple of 16, <= 128)
 //     = activations as an fp16 hi + lo split (x ~= hi + lo), TMA SWIZZLE_128B;
 //       two MMAs (hi, lo) per k-step accumulate into the same TMEM tile.
 //   D = f32 in TMEM, 128 lanes x N columns per UMMA, double-buffered.
-// Warp roles: 0 TMA producer, 1 MMA issuer (+TMEM owner), 2-9 converters,
-// 10-13 epilogue.  Persistent CTAs walk the tile list (expert-major, then
+// Warp roles: 0 TMA producer, 1 MMA issuer (+TMEM owner), 2-17 converters,
+// 18-21 epilogue.  Persistent CTAs walk the tile list (expert-major, then
 // 256-row weight block, then token block).  Every mbarrier wait is bounded;
 // on timeout the kernel records an error code and unwinds.
 #include "amoe_internal.cuh"
@@ -47,7 +48,7 @@ constexpr int ASC_BYTES = ROW_TILES * kTileSBytes;   // 512 B
 constexpr int ACONV_MT_BYTES = BM * BK * 2;          // 16 KB per UMMA A tile
 constexpr int ACONV_BYTES = MT * ACONV_MT_BYTES;     // 32 KB
 constexpr int TX_BYTES = 2 * B_BYTES + ARAW_BYTES + ASC_BYTES;
-constexpr int CONV_WARPS = 8;           // converter warps (two per scheduler)
+constexpr int CONV_WARPS = 16;          // converter warps (four per scheduler, one chunk per thread)
 constexpr int CONV_THREADS = 32 * CONV_WARPS;
 constexpr int EPI_WARP0 = 2 + CONV_WARPS;  // first of the 4 epilogue warps
 constexpr int NUM_THREADS = 32 * (EPI_WARP0 + 4);
@@ -154,11 +155,16 @@ __device__ __forceinline__ uint32_t idesc_f16(int M, int N) {
     return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+// The hi and lo MMAs of one k-step share their A tile: the first reads it from
+// shared memory into the A collector buffer, the second reuses it from there, so
+// the weights cross the shared-memory port once per k-step.
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a, uint64_t b_hi, uint64_t b_lo,
+                                              uint32_t idesc, uint32_t acc) {
     asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        "{\n .reg .pred p, q;\n setp.ne.b32 p, %5, 0;\n setp.eq.b32 q, %5, %5;\n"
+        " tcgen05.mma.cta_group::1.kind::f16.collector::a::fill [%0], %1, %2, %4, p;\n"
+        " tcgen05.mma.cta_group::1.kind::f16.collector::a::lastuse [%0], %1, %3, %4, q;\n}" ::"r"(d_tmem),
+        "l"(a), "l"(b_hi), "l"(b_lo), "r"(idesc), "r"(acc)
         : "memory");
 }
 
@@ -175,27 +181,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
           "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// f16x2 holding 2^(s - 127 - c) twice: built as an f32 power of two (biased
-// exponent s - c <= 140) and rounded to fp16 (0 below fp16's range); NaN for 255.
-__device__ __forceinline__ uint32_t scale_f16x2(uint32_t s, int c) {
-    const int ex = (int)s - c;
-    float f = __uint_as_float(ex > 0 ? (uint32_t)ex << 23 : 0u);
-    if (s == 255u) f = __uint_as_float(0x7fc00000u);
-    const __half2 h = __float2half2_rn(f);
-    return *reinterpret_cast<const uint32_t *>(&h);
-}
-
-// Eight E2M1 values (four bytes, low nibble first) -> four f16x2.
-__device__ __forceinline__ uint4 e2m1x8_to_f16(uint32_t w) {
-    uint4 o;
-    asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
-        " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
-        " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
-        : "=r"(o.x), "=r"(o.y), "=r"(o.z), "=r"(o.w)
-        : "r"(w));
-    return o;
 }
 
 __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
@@ -339,9 +324,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         const uint32_t a = smem_u32(aconv + cs * ACONV_BYTES + m * ACONV_MT_BYTES);
 #pragma unroll
                         for (int kk = 0; kk < BK / 16; ++kk) {
-                            const uint64_t ad = sw128_desc(a + kk * 32);
-                            umma_f16(d, ad, sw128_desc(bh + kk * 32), idesc, (kt | kk) != 0);
-                            umma_f16(d, ad, sw128_desc(bl + kk * 32), idesc, 1u);
+                            umma_f16_pair(d, sw128_desc(a + kk * 32), sw128_desc(bh + kk * 32),
+                                          sw128_desc(bl + kk * 32), idesc, (kt | kk) != 0);
                         }
                     }
                     umma_commit(empty + s);
@@ -352,45 +336,56 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
     } else if (warp < EPI_WARP0) {
         // ---------------- converters: raw MXFP4 tiles -> fp16 SW128 A tiles ----------------
-        const int ct = threadIdx.x - 64;  // 0..CONV_THREADS-1
+        // Thread ct owns one 16-B lane chunk (g, c) of fragment tile rtl in every stage:
+        // 8 nibble bytes of rows g and g+8 per block; all its offsets are fixed.
+        static_assert(ROW_TILES * 32 == CONV_THREADS, "one chunk per converter thread");
+        const int ct = threadIdx.x - 64;
+        const int rtl = ct >> 5, ln = ct & 31, g = ln >> 2, c = ln & 3;
+        const int src_q = rtl * kTileQBytes + ln * 16, src_s = rtl * kTileSBytes + 4 * g;
+        int dst[2][2];  // [h][bb]: byte offset of the 16-B chunk in a converted stage
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int row = (rtl & 7) * 16 + g + 8 * h;  // row within the UMMA A tile (row & 7 == g)
+#pragma unroll
+            for (int bb = 0; bb < 2; ++bb) {
+                // odd rows store their blocks in the other order, so the 8 lanes of each
+                // quarter-warp hit 8 distinct 16-B slots of the swizzled rows
+                const int b = bb ^ (g & 1);
+                dst[h][bb] = (rtl >> 3) * ACONV_MT_BYTES + row * 128 + (((4 * b + c) ^ g) << 4);
+            }
+        }
         int it = 0, cit = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
             const TileInfo ti = decode_tile(t, tile_start, p.offsets, E, p.mblocks);
-            const int ce = p.cexp[ti.e];
+            // fp16 biased exponent of 2^(s-127-c_e) is s - K with K = c_e + 112 (<= 28 by the
+            // choice of c_e); bytes at or below K are flushed to zero (>27 binades below the
+            // expert's largest block), 255 is NaN.
+            const int K = p.cexp[ti.e] + 112;
+            const uint32_t kb = (uint32_t)(K >= 0 ? K : -K) * 0x01010101u;
             for (int kt = 0; kt < nkt; ++kt, ++it, ++cit) {
                 const int s = it % STAGES, cs = cit % CSTAGES;
                 if (!mbar_wait(full + s, (it / STAGES) & 1, p.err, 6)) goto done;
                 if (!mbar_wait(cempty + cs, ((cit / CSTAGES) & 1) ^ 1, p.err, 7)) goto done;
-                const uint8_t *rs = araw + s * ARAW_BYTES;
-                const uint8_t *ss = asc + s * ASC_BYTES;
-                uint8_t *dst = aconv + cs * ACONV_BYTES;
+                const uint4 raw = *reinterpret_cast<const uint4 *>(araw + s * ARAW_BYTES + src_q);
+                const uint32_t scl = *reinterpret_cast<const uint32_t *>(asc + s * ASC_BYTES + src_s);
+                const uint32_t eb = K >= 0 ? __vsubus4(scl, kb) : __vadd4(scl, kb);
+                const uint32_t nan4 = __vcmpeq4(scl, 0xffffffffu);
+                uint8_t *dstage = aconv + cs * ACONV_BYTES;
 #pragma unroll
-                for (int task = 0; task < (ROW_TILES * 32) / CONV_THREADS; ++task) {
-                    const int chunk = ct + CONV_THREADS * task;  // one 16-B lane chunk of a fragment tile
-                    const int rtl = chunk >> 5, ln = chunk & 31;
-                    const int g = ln >> 2, c = ln & 3;
-                    const uint4 raw = *reinterpret_cast<const uint4 *>(rs + rtl * kTileQBytes + ln * 16);
-                    const uint32_t scl = *reinterpret_cast<const uint32_t *>(ss + rtl * kTileSBytes + 4 * g);
-                    uint8_t *mt = dst + (rtl >> 3) * ACONV_MT_BYTES;
+                for (int h = 0; h < 2; ++h) {
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int row = (rtl & 7) * 16 + g + 8 * h;  // row within the UMMA A tile
-                        uint8_t *rowp = mt + row * 128;
-#pragma unroll
-                        for (int bb = 0; bb < 2; ++bb) {
-                            // odd rows store their blocks in the other order, so the 8 lanes of
-                            // each quarter-warp hit 8 distinct 16-B slots of the swizzled rows
-                            const int b = bb ^ (g & 1);
-                            const uint32_t w = b ? (h ? raw.w : raw.z) : (h ? raw.y : raw.x);
-                            const uint32_t sc = scale_f16x2((scl >> (8 * (2 * h + b))) & 0xffu, ce);
-                            uint4 o = e2m1x8_to_f16(w);
-                            o.x = hmul2_bits(o.x, sc);
-                            o.y = hmul2_bits(o.y, sc);
-                            o.z = hmul2_bits(o.z, sc);
-                            o.w = hmul2_bits(o.w, sc);
-                            const int chunk16 = 4 * b + c;  // 16-B chunk of the 128-B row (k = 32b + 8c ..)
-                            *reinterpret_cast<uint4 *>(rowp + ((chunk16 ^ (row & 7)) << 4)) = o;
-                        }
+                    for (int bb = 0; bb < 2; ++bb) {
+                        const int b = bb ^ (g & 1);
+                        const uint32_t w = b ? (h ? raw.w : raw.z) : (h ? raw.y : raw.x);
+                        const uint32_t sel = (uint32_t)(2 * h + b) * 0x0101u + 0x4040u;  // byte j -> halves 0, 2
+                        uint32_t sc = __byte_perm(eb, 0u, sel) << 10;
+                        if (__byte_perm(nan4, 0u, sel)) sc = 0x7e007e00u;
+                        uint4 o = e2m1x8_to_f16(w);
+                        o.x = hmul2_bits(o.x, sc);
+                        o.y = hmul2_bits(o.y, sc);
+                        o.z = hmul2_bits(o.z, sc);
+                        o.w = hmul2_bits(o.w, sc);
+                        *reinterpret_cast<uint4 *>(dstage + dst[h][bb]) = o;
                     }
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -478,7 +473,7 @@ done:
 
 // Per-expert exponent bias for the fp16 weight expansion: c = max finite E8M0
 // byte - 140, so the largest scaled E2M1 value (6 * 2^13) still fits fp16 and
-// every block within 36 binades of it is exact.
+// the block scales within 27 binades of it are normal fp16 numbers.
 __global__ void cexp_kernel(const uint8_t *__restrict__ s_plane, size_t bytes_per_expert, int32_t *out) {
     __shared__ int mx;
     if (threadIdx.x == 0) mx = -1;

@@ -33,7 +33,8 @@ struct GemvParams {
     const int32_t *offsets;
     const int32_t *active;
     int R, K, E, k;
-    int32_t *err;  // set when a bounded wait gives up
+    int x_rows;    // staged activation rows the launch provides (NG == 1)
+    int32_t *err;  // set when a bounded wait gives up (20) or an expert has more rows than staged (21)
     // outputs
     __half *act_hi, *act_lo;  // gate_up: [P][R/2]
     float *y;                 // down:    [P][R]
@@ -46,20 +47,6 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
         "{%8,%9}, {%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
-    uint4 r;
-    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p));
-    return r;
-}
-
-__device__ __forceinline__ uint32_t ldg_nc_u32(const void *p) {
-    uint32_t r;
-    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(r) : "l"(p));
-    return r;
 }
 
 // GPT-OSS clamped SwiGLU in f32 with Go's math.Min/Max NaN semantics
@@ -108,10 +95,19 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                  : "memory");
 }
 
-size_t gemv_smem_bytes(int K) {
+// Staged activation rows (NG == 1): hi rows 0..x_rows-1, then the lo rows.  The
+// 64-byte pad puts rows g and g+1 in opposite halves of the bank space, so the
+// quarter-warp (g, c) loads of one k-step are conflict-free.
+__host__ __device__ constexpr int gemv_x_stride(int K) { return 2 * K + 64; }
+
+__host__ __device__ inline size_t gemv_weight_bytes(int K) {
     const int nkt = K / kTileK;
     const int per = (nkt + kGemvKSplit - 1) / kGemvKSplit;
     return (size_t)kGemvTiles * kGemvKSplit * per * (kTileQBytes + kTileSBytes) + kGemvTiles * kGemvKSplit * 8;
+}
+
+size_t gemv_smem_bytes(int K, int x_rows) {
+    return gemv_weight_bytes(K) + (size_t)x_rows * 2 * gemv_x_stride(K);
 }
 
 template <bool GATE_UP, int NG>
@@ -124,6 +120,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
     const int e = p.active[slot];
     const int base = p.offsets[e];
     const int m_e = p.offsets[e + 1] - base;
+    if (NG == 1 && min(8, m_e) > p.x_rows) {  // the launch bound T was violated: uniform exit
+        if (threadIdx.x == 0) atomicCAS(p.err, 0, 21);
+        return;
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tile_local = warp / kGemvKSplit, ks = warp % kGemvKSplit;
     const int nrt = p.R / kTileRows;
@@ -137,9 +137,14 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
     uint8_t *wq = wsm + (size_t)warp * per * (kTileQBytes + kTileSBytes);
     uint8_t *ws = wq + (size_t)per * kTileQBytes;
     uint64_t *bar = reinterpret_cast<uint64_t *>(wsm + (size_t)kGemvWarps * per * (kTileQBytes + kTileSBytes)) + warp;
+    // NG == 1: the pass's (<= 8) activation rows are staged in shared memory once
+    // per CTA, so the k-loop never waits on a global load.
+    uint8_t *xs = wsm + gemv_weight_bytes(p.K);
+    const int xstride = gemv_x_stride(p.K);
     const int nk = kend - kbeg;
+    const bool issued = live && nk > 0;
     bool have = false;
-    if (live && nk > 0) {
+    if (issued) {
         if (lane == 0) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar)));
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -153,10 +158,41 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
             bulk_g2s(ws, p.s + tile0 * kTileSBytes, sb, bar);
         }
         __syncwarp();
-        have = gemv_wait(bar, p.err);
     }
+    bool waited = false;
 
     for (int tok0 = 0; tok0 < m_e; tok0 += 8 * NG) {
+        if (NG == 1) {
+            // all threads: <= 8 rows x (hi, lo) x K halves, 16-B loads all in flight
+            const int nv = min(8, m_e - tok0);
+            const int chunks = p.K / 8;
+            const int total = nv * 2 * chunks;
+            for (int i0 = threadIdx.x; i0 < total; i0 += 4 * kGemvWarps * 32) {
+                uint4 v[4];
+                uint8_t *dst[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int i = i0 + u * kGemvWarps * 32;
+                    dst[u] = nullptr;
+                    if (i < total) {
+                        const int r = i / (2 * chunks), rem = i - r * 2 * chunks;
+                        const int lo = rem >= chunks, ch = rem - (lo ? chunks : 0);
+                        const int tok = tok0 + r;
+                        const int row = (GATE_UP && p.perm_pair) ? p.perm_pair[base + tok] / p.k : base + tok;
+                        v[u] = *reinterpret_cast<const uint4 *>((lo ? p.x_lo : p.x_hi) + (size_t)row * p.K + 8 * ch);
+                        dst[u] = xs + (size_t)(lo * p.x_rows + r) * xstride + 16 * ch;
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (dst[u]) *reinterpret_cast<uint4 *>(dst[u]) = v[u];
+            }
+            __syncthreads();
+        }
+        if (issued && !waited) {
+            have = gemv_wait(bar, p.err);
+            waited = true;
+        }
         const __half *xh[NG];
         const __half *xl[NG];
         bool valid[NG];
@@ -165,10 +201,15 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
         for (int n = 0; n < NG; ++n) {
             const int tok = tok0 + 8 * n + g;
             valid[n] = tok < m_e;
-            int row = 0;
-            if (valid[n]) row = (GATE_UP && p.perm_pair) ? p.perm_pair[base + tok] / p.k : base + tok;
-            xh[n] = p.x_hi + (size_t)row * p.K + 8 * c;
-            xl[n] = p.x_lo + (size_t)row * p.K + 8 * c;
+            if (NG == 1) {
+                xh[n] = reinterpret_cast<const __half *>(xs + (size_t)g * xstride) + 8 * c;
+                xl[n] = reinterpret_cast<const __half *>(xs + (size_t)(p.x_rows + g) * xstride) + 8 * c;
+            } else {
+                int row = 0;
+                if (valid[n]) row = (GATE_UP && p.perm_pair) ? p.perm_pair[base + tok] / p.k : base + tok;
+                xh[n] = p.x_hi + (size_t)row * p.K + 8 * c;
+                xl[n] = p.x_lo + (size_t)row * p.K + 8 * c;
+            }
             if (tok0 + 8 * n < m_e) ng_live = n + 1;
         }
         float acc[NG][4];
@@ -268,14 +309,17 @@ template <bool GATE_UP>
 cudaError_t launch(const GemvParams &p, int T, int max_active, cudaStream_t st) {
     const int nrt = p.R / kTileRows;
     dim3 grid((nrt + kGemvTiles - 1) / kGemvTiles, max_active);
-    const size_t smem = gemv_smem_bytes(p.K);
+    // T bounds the rows of any one expert
+    GemvParams q = p;
+    q.x_rows = T <= 8 ? T : 0;
+    const size_t smem = gemv_smem_bytes(p.K, q.x_rows);
     cudaError_t e;
 #define AMOE_GEMV(NG)                                                                              \
     do {                                                                                           \
         e = cudaFuncSetAttribute(gemv_kernel<GATE_UP, NG>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                  (int)smem);                                                       \
         if (e != cudaSuccess) return e;                                                            \
-        gemv_kernel<GATE_UP, NG><<<grid, kGemvWarps * 32, smem, st>>>(p);                          \
+        gemv_kernel<GATE_UP, NG><<<grid, kGemvWarps * 32, smem, st>>>(q);                          \
     } while (0)
     if (T <= 8) AMOE_GEMV(1);
     else if (T <= 16) AMOE_GEMV(2);

@@ -52,7 +52,7 @@ class AmoeConfig(ctypes.Structure):
 
 
 AMOE_STAGES = 8
-STAGE_NAMES = ["route", "scan", "gate_up", "down", "combine", "scatter_gather", "reserved6", "reserved7"]
+STAGE_NAMES = ["route", "scan", "gate_up", "down", "combine", "scatter_gather", "decode_experts", "reserved7"]
 
 
 class AmoeStats(ctypes.Structure):

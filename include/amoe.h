@@ -133,7 +133,8 @@ AMOE_API int amoe_last_routing(amoe_ctx *ctx, float *logits, int32_t *perm_pair,
 /* Per-stage device timing (CUDA events on the launch stream) and launch count.
  * Stages: 0 route (RMSNorm+router+top-k), 1 expert-offset scan (+ scatter on
  * the GEMV path), 2 gate_up (+SwiGLU), 3 down, 4 combine, 5 scatter + gather
- * of the expert-sorted rows (tensor path), 6-7 reserved. */
+ * of the expert-sorted rows (tensor path), 6 fused decode expert stage (gate_up,
+ * down and combine in one launch, T <= 4), 7 reserved. */
 #define AMOE_STAGES 8
 typedef struct amoe_stats {
     int64_t launches;               /* kernels this context has launched */

@@ -72,6 +72,29 @@ def test_small_layers_match_oracle(cuda_device, path, H, I, E, k, T):
     check_against_oracle(layer, x, path)
 
 
+@pytest.mark.parametrize("H,I,E,k,T", [
+    (64, 128, 8, 4, 1), (192, 320, 16, 4, 2), (320, 192, 32, 4, 3), (128, 128, 128, 4, 4),
+    (64, 64, 256, 8, 4), (128, 64, 5, 2, 4), (2880, 2880, 32, 4, 2),
+])
+def test_fused_decode_stage_matches_oracle(cuda_device, H, I, E, k, T):
+    # T <= 4 on the GEMV path runs gate_up, down and the combine as one cooperative
+    # launch (two grid barriers); the stage timer shows which kernel ran
+    layer = W.small_layer(hidden=H, intermediate=I, experts=E, top_k=k, seed=7 * T + E)
+    x = W.make_tokens(W.MoEShape(H, I, E, k), T, T + 1)
+    blk = moe.MoEBlock.for_layer(layer, max_tokens=T, path=moe.PATH_GEMV)
+    blk.upload_layer(0, layer)
+    blk.set_profiling(True)
+    outs = [blk.forward(x)[0] for _ in range(3)]  # the grid barrier state carries across launches
+    st = blk.stats(reset=True)
+    blk.close()
+    assert st["stage_ms"]["decode_experts"] > 0 and st["stage_ms"]["gate_up"] == 0
+    assert all(np.array_equal(o, outs[0]) for o in outs)
+    ref_idx = oracle.route(layer, x)[1]
+    ref = oracle.moe_block(layer, x)[0]
+    assert_block_parity(outs[0], ref)
+    assert ref_idx.shape == (T, k)
+
+
 @pytest.mark.parametrize("path", PATHS)
 def test_extreme_scales_incl_denormal(cuda_device, path):
     # E8M0 bytes 0..123: the subnormal 2^-127 scale and ~120 binades of small scales,
