@@ -57,7 +57,44 @@ struct LayerDev {
     float *dn_b = nullptr;        // [E][H]
     int32_t *gu_cexp = nullptr;   // [E] power-of-two bias of the fp16 weight expansion (tcgen05 path)
     int32_t *dn_cexp = nullptr;   // [E]
+    // Block-scaled tensor-core planes (see "TMA planes" below)
+    uint8_t *gu_tq = nullptr;     // [E][2I/128][Hp/128][128][64] E2M1 boxes, rows in fragment order
+    uint8_t *gu_tsf = nullptr;    // [E][2I/128][Hp/128][512] E8M0 in scale-factor chunks
+    uint8_t *dn_tq = nullptr;     // [E][ceil(H/128)][Ip/128][128][64]
+    uint8_t *dn_tsf = nullptr;    // [E][ceil(H/128)][Ip/128][512]
 };
+
+// ---------------------------------------------------------------------------
+// TMA planes for the block-scaled tensor-core path (tcgen05.mma
+// kind::mxf8f6f4.block_scale: E2M1 weights x E4M3 activations, E8M0 scales).
+//
+//   tq[e][m][kb][r][64]  box (m, kb): rows 128m..128m+127, elements
+//                   128kb..128kb+127, as the rows' GGUF nibble bytes unchanged
+//                   (byte j: low nibble element 2j, high nibble 2j+1); K padded
+//                   with zeros to Kp = K rounded up to 128 (the TMA 4-bit
+//                   unpacking box is 128 elements wide), rows past R zero.
+//                   Each box is 8 KB contiguous in HBM (whole DRAM pages, not
+//                   64-byte pieces of 128 long rows); TMA loads it as
+//                   CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B into SWIZZLE_128B
+//                   shared memory, the layout the tensor core reads.
+//   tsf[e][m][kc][512]  the E8M0 bytes of the 128-row tile m and the four
+//                   32-element blocks 4kc..4kc+3, at byte
+//                   (r % 32) * 16 + (r / 32) * 4 + j: the scale-factor chunk that
+//                   tcgen05.cp.32x128b.warpx4 spreads over the 128 TMEM lanes
+//                   (lane r, column base + r / 32, byte j).  Padding rows and
+//                   blocks hold 127 (2^0) over zero weights.
+// gate_up rows use the fragment order of the tiled planes (row 16t + j, j < 8:
+// gate of pair 8t + j; j >= 8: its up row), so a SwiGLU pair sits in TMEM
+// lanes 8 apart.
+// ---------------------------------------------------------------------------
+constexpr int kTmaBoxK = 128;
+inline int kpad128(int K) { return (K + kTmaBoxK - 1) / kTmaBoxK * kTmaBoxK; }
+inline size_t tq_bytes(int E, int R, int K) { return (size_t)E * ((R + 127) / 128) * 128 * (kpad128(K) / 2); }
+inline size_t tsf_bytes(int E, int R, int K) {
+    return (size_t)E * ((R + 127) / 128) * (kpad128(K) / kTmaBoxK) * 512;
+}
+cudaError_t launch_repack_tma(const uint8_t *gguf, int E, int R, int K, bool pair_rows, uint8_t *tq, uint8_t *tsf,
+                              cudaStream_t st);
 
 struct Dims {
     int H, I, E, k;
@@ -122,9 +159,12 @@ struct DecodeBarrier {
     unsigned release;                 // last grid barrier CTA 0 released
 };
 bool decode_supported(const Dims &d, int T, int device);
+// scratch: decode_scratch_bytes(), prepared once by init_decode_scratch()
+size_t decode_scratch_bytes(const Dims &d, int device);
+cudaError_t init_decode_scratch(const Dims &d, int device, void *scratch, cudaStream_t st);
 cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, const float *residual, int T,
-                          __half *act_hi, __half *act_lo, float *y, float *out, DecodeBarrier *bar, int32_t *err,
-                          int device, cudaStream_t st);
+                          void *scratch, float *y, float *out, DecodeBarrier *bar, int32_t *err, int device,
+                          cudaStream_t st);
 
 // T: upper bound on any expert's row count (sizes the token groups per pass).
 cudaError_t launch_gemv_gate_up(const Dims &d, const LayerDev &L, const GemvRows &rows, int T,

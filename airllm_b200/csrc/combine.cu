@@ -78,7 +78,50 @@ __global__ void repack_kernel(const uint8_t *__restrict__ gguf, int E, int R, in
     }
 }
 
+// K8b: GGUF MXFP4 -> TMA planes (amoe_internal.cuh).  One thread per
+// (expert, padded row, 32-element block) of the padded K range; lossless.
+__global__ void repack_tma_kernel(const uint8_t *__restrict__ gguf, int E, int R, int K, int pair_rows,
+                                  uint8_t *__restrict__ tq, uint8_t *__restrict__ tsf) {
+    const int Kp = (K + kTmaBoxK - 1) / kTmaBoxK * kTmaBoxK;
+    const int nblk = K / 32, nblkp = Kp / 32, nmt = (R + 127) / 128, Rp = nmt * 128;
+    const long long total = (long long)E * Rp * nblkp;
+    const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (tid >= total) return;
+    const int kb = (int)(tid % nblkp);
+    const long long er = tid / nblkp;
+    const int r = (int)(er % Rp), e = (int)(er / Rp);
+    int grow = r;
+    if (pair_rows) {
+        const int t = r / 16, j = r % 16;
+        grow = j < 8 ? 2 * (8 * t + j) : 2 * (8 * t + j - 8) + 1;
+    }
+    uint4 q = make_uint4(0, 0, 0, 0);
+    uint8_t scale = 127;
+    if (kb < nblk && r < R) {
+        const uint8_t *src = gguf + (((size_t)e * R + grow) * nblk + kb) * 17;
+        scale = src[0];
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            w[i] = src[1 + 4 * i] | (src[2 + 4 * i] << 8) | (src[3 + 4 * i] << 16) | ((uint32_t)src[4 + 4 * i] << 24);
+        q = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    const int mt = r / 128, rr = r % 128, kc = kb / 4, j = kb % 4;
+    const size_t box = ((size_t)e * nmt + mt) * (Kp / kTmaBoxK) + kc;
+    *reinterpret_cast<uint4 *>(tq + box * (128 * 64) + (size_t)rr * 64 + (size_t)j * 16) = q;
+    tsf[box * 512 + (rr % 32) * 16 + (rr / 32) * 4 + j] = scale;
+}
+
 }  // namespace
+
+cudaError_t launch_repack_tma(const uint8_t *gguf, int E, int R, int K, bool pair_rows, uint8_t *tq, uint8_t *tsf,
+                              cudaStream_t st) {
+    const long long total = (long long)E * ((R + 127) / 128) * 128 * (kpad128(K) / 32);
+    const int threads = 256;
+    repack_tma_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, st>>>(gguf, E, R, K,
+                                                                                       pair_rows ? 1 : 0, tq, tsf);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_combine(const Dims &d, const float *residual, const RouteOut &r,
                            const float *y, int T, float *out, cudaStream_t st) {

@@ -29,7 +29,8 @@ struct Status {
 
 struct LayerBlock {
     // byte offsets inside one layer's device-format block (256-B aligned parts)
-    size_t norm, router_w, router_b, gu_b, dn_b, gu_cexp, dn_cexp, gu_s, dn_s, gu_q, dn_q, total;
+    size_t norm, router_w, router_b, gu_b, dn_b, gu_cexp, dn_cexp, gu_s, dn_s, gu_q, dn_q, gu_tsf, dn_tsf, gu_tq,
+        dn_tq, total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -55,6 +56,10 @@ LayerBlock layer_block(const Dims &d, int E_x) {
     b.dn_s = take(E * H * (I / 32));
     b.gu_q = take(E * 2 * I * (H / 2));
     b.dn_q = take(E * H * (I / 2));
+    b.gu_tsf = take(tsf_bytes((int)E, (int)(2 * I), (int)H));
+    b.dn_tsf = take(tsf_bytes((int)E, (int)H, (int)I));
+    b.gu_tq = take(tq_bytes((int)E, (int)(2 * I), (int)H));
+    b.dn_tq = take(tq_bytes((int)E, (int)H, (int)I));
     b.total = o;
     return b;
 }
@@ -72,6 +77,10 @@ LayerDev layer_view(uint8_t *base, const LayerBlock &b) {
     L.dn_s = base + b.dn_s;
     L.gu_q = base + b.gu_q;
     L.dn_q = base + b.dn_q;
+    L.gu_tsf = base + b.gu_tsf;
+    L.dn_tsf = base + b.dn_tsf;
+    L.gu_tq = base + b.gu_tq;
+    L.dn_tq = base + b.dn_tq;
     return L;
 }
 
@@ -112,6 +121,7 @@ struct amoe_ctx {
     float *y = nullptr;
     void *tc_scratch = nullptr;
     DecodeBarrier *dec_bar = nullptr;  // grid barrier state of the fused decode kernel
+    void *dec_scratch = nullptr;       // its activation operand, partial tiles and tile counters
     float *io_in = nullptr, *io_out = nullptr;
     int32_t *io_idx = nullptr;
     float *io_w = nullptr;
@@ -220,6 +230,7 @@ int alloc_scratch(amoe_ctx *c) {
         {(void **)&c->y, P * d.H * 4},
         {(void **)&c->tc_scratch, tc_scratch_bytes((int)P, d.H, d.I)},
         {(void **)&c->dec_bar, sizeof(DecodeBarrier)},
+        {(void **)&c->dec_scratch, decode_scratch_bytes(d, c->cfg.device)},
         {(void **)&c->io_in, T * d.H * 4},
         {(void **)&c->io_out, T * d.H * 4},
         {(void **)&c->io_idx, P * 4},
@@ -245,6 +256,8 @@ int alloc_scratch(amoe_ctx *c) {
     for (size_t i = 0; i < parts.size(); ++i) *parts[i].dst = parts[i].bytes ? base + at[i] : nullptr;
     AMOE_CUDA(c, cudaMemset(c->arrivals, 0, (size_t)c->nchunk_max * 4));
     AMOE_CUDA(c, cudaMemset(c->dec_bar, 0, sizeof(DecodeBarrier)));
+    AMOE_CUDA(c, init_decode_scratch(d, c->cfg.device, c->dec_scratch, nullptr));
+    AMOE_CUDA(c, cudaDeviceSynchronize());
     AMOE_CUDA(c, cudaMemset(tc_error_flag(c->tc_scratch, (int)P, d.H), 0, sizeof(int32_t)));
     // pinned staging: offsets [E+1], receive counts [nseg], segments [3*nseg], local offsets [E_loc+1]
     if (R) AMOE_CUDA(c, cudaHostAlloc(&c->h_stage, ((size_t)d.E + 1 + nseg * 4 + c->e_loc + 1) * 4, 0));
@@ -632,9 +645,11 @@ int amoe_upload_layer(amoe_ctx *c, int32_t layer, const float *norm_gain, const 
     UP_CUDA(cudaMemcpyAsync(L.dn_b, down_b + e0 * H, E * H * 4, cudaMemcpyHostToDevice, st));
     UP_CUDA(cudaMemcpyAsync(staging, gate_up + e0 * gu_expert, gu_bytes, cudaMemcpyHostToDevice, st));
     UP_CUDA(launch_repack(staging, (int)E, (int)(2 * I), (int)H, true, L.gu_q, L.gu_s, st));
+    UP_CUDA(launch_repack_tma(staging, (int)E, (int)(2 * I), (int)H, true, L.gu_tq, L.gu_tsf, st));
     UP_CUDA(cudaStreamSynchronize(st));  // staging is reused for down
     UP_CUDA(cudaMemcpyAsync(staging, down + e0 * dn_expert, dn_bytes, cudaMemcpyHostToDevice, st));
     UP_CUDA(launch_repack(staging, (int)E, (int)H, (int)I, false, L.dn_q, L.dn_s, st));
+    UP_CUDA(launch_repack_tma(staging, (int)E, (int)H, (int)I, false, L.dn_tq, L.dn_tsf, st));
     UP_CUDA(launch_cexp(L.gu_s, 2 * I * (H / 32), (int)E, L.gu_cexp, st));
     UP_CUDA(launch_cexp(L.dn_s, H * (I / 32), (int)E, L.dn_cexp, st));
     if (streaming(c)) {
@@ -701,7 +716,7 @@ int amoe_forward_device(amoe_ctx *c, int32_t layer, const float *residual, int32
         // decode: gate_up, down and the combine in one cooperative launch
         timer.mark(1);
         int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H);
-        AMOE_CUDA(c, launch_decode(d, L, c->r, residual, T, c->act_hi, c->act_lo, c->y, out, c->dec_bar, flag,
+        AMOE_CUDA(c, launch_decode(d, L, c->r, residual, T, c->dec_scratch, c->y, out, c->dec_bar, flag,
                                    c->cfg.device, st));
         timer.mark(6);
         c->stats.launches += 1;

@@ -1,32 +1,38 @@
-// decode.cu -- K9: the expert stage of a decode step (T <= kDecodeMaxTokens
-// tokens) as ONE cooperative persistent kernel:
+// decode.cu -- K9: the expert stage of a decode step (T <= kDecodeMaxTokens)
+// as ONE cooperative persistent kernel on the block-scaled tensor cores:
 //
 //   phase 1  gate_up = x . W_gu^T + b_gu -> clamped SwiGLU      (layer.go:139-148, 175;
 //                                                                primitives.go:138-149)
-//   -------- grid barrier (every act row written)
+//   -------- grid barrier (every activation row written)
 //   phase 2  y = act . W_dn^T + b_dn                             (layer.go:179-187)
 //   -------- grid barrier (every y row written)
 //   phase 3  out = residual + f32(sum_s f64(w_s) * f64(y_s))      (layer.go:109-121)
 //
-// Why one kernel: at decode sizes each separate launch is dominated by its
-// ramp-up, its tail and a few dependent memory round trips, not by its bytes.
-// Here one CTA per SM streams a balanced, contiguous run of 16-row weight
-// tiles (whole row tiles; gate_up tiles of every selected expert first, then
-// down tiles) through a ring of shared-memory stages filled by one producer
-// lane with cp.async.bulk.  The down tiles do not depend on phase 1, so the
-// producer keeps HBM busy straight through the grid barrier; only the MMAs
-// wait for it.
+// The MXFP4 experts are consumed as stored: tcgen05.mma kind::mxf8f6f4 with
+// A = E2M1 weights straight from the TMA planes (TMA unpacks the nibbles into
+// the tensor core's 16-byte-aligned shared-memory format) and the GGUF E8M0
+// bytes as the hardware block scales of A.  The activations enter as four
+// E4M3 terms x ~= sum_j q_j * 2^(e - 4j) per 32-element block (B scale
+// factors), one term per MMA column, so one MMA computes all four partial
+// products; the epilogue adds the columns.  Four terms carry ~16 significant
+// bits; accumulation is f32 in TMEM.
 //
-// Arithmetic is the GEMV kernel's (gemv.cu): each MXFP4 byte becomes an f16x2
-// A-fragment with one cvt.rn.f16x2.e2m1x2; activations ride as the n=8 columns
-// of mma.sync.m16n8k16 as an fp16 hi + lo split; the E8M0 block scale is
-// applied to each 32-value block's f32 partial.  A stage's 16 compute warps
-// take every 16th k-tile of the row tile and meet in shared memory in a fixed
-// order (deterministic).
+// Work split: all selected experts' 128-row weight tiles of a phase form one
+// sequence of 128-element K boxes; CTA b takes the contiguous run
+// [n*b/G, n*(b+1)/G) (stream-K), so every SM streams the same number of
+// bytes.  A tile cut between CTAs is summed by whichever of its CTAs arrives
+// last (self-resetting counter), adding the partials in CTA order
+// (deterministic).  The down boxes do not depend on phase 1, so the producer
+// streams them before the grid barrier; only their activation operand waits.
 //
-// Waits: every mbarrier wait and the grid barrier give up after ~1 s of clock,
-// record a code in the error flag and carry on, so the kernel always ends.
+// Roles: warps 0-3 TMA producers (stage i filled by warp i % 4), warp 4 MMA
+// issuer and TMEM owner, warps 5-8 epilogue (TMEM lane quadrants 1, 2, 3, 0).
+// Every wait is bounded (~1 s of clock): it records a code in the error flag
+// and the kernel winds down.
 #include "amoe_internal.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include <mutex>
 
@@ -34,13 +40,29 @@ namespace amoe {
 
 namespace {
 
-constexpr int kDecWarps = 16;                      // compute warps
-constexpr int kDecThreads = (kDecWarps + 1) * 32;  // + one producer warp
-constexpr int kDecComputeThreads = kDecWarps * 32;
-constexpr int kDecMaxStages = 8;
-constexpr int kDecRed = 4;                         // reduction buffers in flight
-constexpr size_t kDecSmemBudget = 220 * 1024;
-constexpr long long kWaitLimit = 2000000000LL;     // clock cycles (~1 s)
+// Copies issued by one warp are serviced one after another (~0.4 us each at
+// load), so four producer warps fill the ring's stages round-robin.
+constexpr int kProdWarps = 4;
+constexpr int kMmaWarp = kProdWarps;
+constexpr int kEpiWarp0 = kProdWarps + 1;
+constexpr int kEpiWarps = 4;
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kDecThreads = (kEpiWarp0 + kEpiWarps) * 32;
+constexpr int kNMax = 16;                       // MMA N: up to 4 tokens x 4 terms
+constexpr int kBoxes = 2;                       // 128-element K boxes per pipeline stage
+constexpr int kMaxStages = 6;
+constexpr uint32_t kABytes = 128 * 128;         // unpacked A box in shared memory
+constexpr uint32_t kAPacked = 128 * 64;         // its bytes in global memory (TMA transaction size)
+constexpr uint32_t kTmemCols = 128;             // 2 accumulators + 16 scale columns per stage
+constexpr long long kWaitLimit = 2000000000LL;  // clock cycles (~1 s)
+constexpr size_t kSmemBudget = 225 * 1024;
+constexpr int kTilesPerSlot = 64;               // tile counters per slot and phase
+
+// Stage: kBoxes A boxes | their scale chunks | kBoxes B boxes | their scale chunks.
+__host__ __device__ constexpr uint32_t b_box_bytes(int nt) { return (uint32_t)nt * 128; }
+__host__ __device__ constexpr uint32_t stage_bytes(int nt) {
+    return (kBoxes * kABytes + kBoxes * 512 + kBoxes * b_box_bytes(nt) + kBoxes * 512 + 1023) & ~1023u;
+}
 
 struct DecodeParams {
     const float *residual;
@@ -48,35 +70,33 @@ struct DecodeParams {
     const __half *x_hi, *x_lo;  // [T][H] normalized rows
     const int32_t *perm_pair, *offsets, *active, *inv;
     const float *topk_w;
-    const uint8_t *gu_q, *gu_s, *dn_q, *dn_s;
+    const uint8_t *gu_tsf, *dn_tsf;
     const float *gu_b, *dn_b;
-    __half *act_hi, *act_lo;  // [P][I]
-    float *y;                 // [P][H]
-    int T, H, I, E, k;
-    int stages;
-    uint32_t stage_bytes;
-    int nkt_max;
+    uint8_t *act_q;             // [S][16][Ip] E4M3 terms of each slot's activation rows
+    uint8_t *act_sf;            // [S][Ip/128][512] their scale-factor chunks
+    float *y;                   // [P][H]
+    float *partial;             // [G][2][128][kNMax]
+    uint32_t *cnt;              // [2][S][kTilesPerSlot] self-resetting tile counters
     DecodeBarrier *bar;
     int32_t *err;
+    int T, H, I, E, k, Hp, Ip, S;
+    int stages;
+    int N;                      // MMA N (8 or 16)
 };
-
-// Staged activation rows: hi rows 0..T-1, then lo rows; the stride is 2*Kmax+64
-// bytes, so rows g and g+1 sit 16 banks apart (conflict-free (g, c) loads).
-__host__ __device__ inline uint32_t dec_xstride(int H, int I) { return 2u * (uint32_t)(H > I ? H : I) + 64u; }
 
 struct DecLayout {
-    uint32_t ring, x, red, offs, act, perm, inv, w, bars, total;
+    uint32_t ring, b1, sfb1, offs, act, perm, inv, w, xchg, bars, tmem_slot, total;
 };
 
-__host__ __device__ inline DecLayout dec_layout(int T, int H, int I, int E, int k, int stages, uint32_t stage_bytes) {
+__host__ __device__ inline DecLayout dec_layout(int T, int Hp, int E, int k, int stages, int nt) {
     DecLayout L;
     uint32_t o = 0;
     L.ring = o;
-    o += (uint32_t)stages * stage_bytes;
-    L.x = o;
-    o += 2u * (uint32_t)T * dec_xstride(H, I);
-    L.red = o;
-    o += (uint32_t)kDecRed * kDecWarps * 32 * 8;
+    o += (uint32_t)stages * stage_bytes(nt);
+    L.b1 = o;
+    o += (uint32_t)(Hp / 128) * b_box_bytes(nt);
+    L.sfb1 = o;
+    o += (uint32_t)(Hp / 128) * 512;
     L.offs = o;
     o += (uint32_t)(E + 1) * 4;
     L.act = o;
@@ -88,23 +108,23 @@ __host__ __device__ inline DecLayout dec_layout(int T, int H, int I, int E, int 
     o += P * 4;
     L.w = o;
     o += P * 4;
+    L.xchg = o;
+    o += 64;  // block maxima of the activation quantization + flags
     o = (o + 7u) & ~7u;
     L.bars = o;
-    o += (2u * (uint32_t)stages + 2u * kDecRed) * 8;
-    L.total = o;
+    o += (2u * (uint32_t)stages + 5u) * 8;
+    L.tmem_slot = o;
+    o += 16;
+    L.total = o + 1024;  // base alignment slack
     return L;
 }
 
-__host__ __device__ inline uint32_t dec_stage_bytes(int H, int I) {
-    const int nkt = (H > I ? H : I) / kTileK;
-    return ((uint32_t)nkt * (kTileQBytes + kTileSBytes) + 64u + 127u) & ~127u;
-}
-
+// ---- PTX helpers -------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int32_t *err, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int32_t *err, int code) {
     const long long t0 = clock64();
     for (;;) {
         uint32_t ok;
@@ -121,8 +141,35 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     }
 }
 
+__device__ __forceinline__ void mbar_init(uint64_t *bar, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}" ::"r"(
+                     smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_3d(void *dst, const CUtensorMap *tm, uint64_t *bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *tm, uint64_t *bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
 }
 
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
@@ -132,26 +179,71 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                  : "memory");
 }
 
-__device__ __forceinline__ void compute_bar() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kDecComputeThreads) : "memory");
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major SWIZZLE_128B operand: 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1u << 16;
+    d |= (uint64_t)(1024u >> 4) << 32;
+    d |= (uint64_t)1u << 46;
+    d |= (uint64_t)2u << 61;
+    return d;
 }
 
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
+// Scale-factor chunk for tcgen05.cp: 32 rows of 16 B, no swizzle, 8-row core
+// matrices 128 B apart.
+__device__ __forceinline__ uint64_t desc_sf(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)(128u >> 4) << 16;
+    d |= (uint64_t)(128u >> 4) << 32;
+    d |= (uint64_t)1u << 46;
+    return d;
+}
+
+__device__ __forceinline__ void sf_copy(uint32_t tmem_col, uint32_t saddr) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tmem_col), "l"(desc_sf(saddr)) : "memory");
+}
+
+// Instruction descriptor, kind::mxf8f6f4 block-scaled: A E2M1, B E4M3, both
+// K-major, E8M0 scales, M = 128, N = n; sf_id picks the byte (32-element
+// block) of the scale words.
+__device__ __forceinline__ uint32_t idesc_bs(uint32_t sf_id, int n) {
+    return (sf_id << 4) | (5u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24) |
+           (sf_id << 29);
+}
+
+__device__ __forceinline__ void umma_bs(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc, uint32_t sfa,
+                                        uint32_t sfb) {
     asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-        "{%8,%9}, {%0,%1,%2,%3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
+        : "memory");
 }
 
-// GPT-OSS clamped SwiGLU in f32 with Go's math.Min/Max NaN semantics
-// (primitives.go:144-146): NaN propagates.
-__device__ __forceinline__ float swiglu(float gate, float up) {
-    float g = isnan(gate) ? gate : fminf(gate, 7.0f);
-    float u = isnan(up) ? up : fminf(fmaxf(up, -7.0f), 7.0f);
-    return g / (1.0f + expf(-1.702f * g)) * (u + 1.0f);
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
 }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
     unsigned v;
@@ -163,75 +255,180 @@ __device__ __forceinline__ void st_release(unsigned *p, unsigned v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Grid barrier over the compute warps of all CTAs (the launch is cooperative,
-// so every CTA is resident).  Barrier values grow monotonically across launches
-// (2 per launch, from each CTA's own epoch counter), so nothing is ever reset:
-// CTA b publishes its arrival in its own word; CTA 0 polls all arrival words,
-// then publishes the release word that every CTA polls.  No two CTAs write the
-// same word, so the barrier costs a few L2 round trips rather than a chain of
-// same-address atomics.
-__device__ void grid_barrier(DecodeBarrier *bar, unsigned v, int32_t *err) {
-    compute_bar();
-    if (threadIdx.x == 0) {
+// E4M3 with round-to-nearest, saturating to +-448 (NaN stays NaN).
+__device__ __forceinline__ uint32_t to_e4m3(float v) {
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %1;" : "=h"(r) : "f"(v));
+    return r & 0xffu;
+}
+
+__device__ __forceinline__ float from_e4m3(uint32_t b) {
+    uint32_t h;
+    const uint16_t two = (uint16_t)(b | (b << 8));
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(two));
+    return __half2float(__ushort_as_half((unsigned short)(h & 0xffffu)));
+}
+
+// Scale exponent of a 32-element block with largest magnitude amax: amax /
+// 2^e0 lies in [128, 256) (inside E4M3's 448); term j uses 2^(e0 - 4j).
+__device__ __forceinline__ int block_exp(float amax) {
+    const int e = (int)((__float_as_uint(amax) >> 23) & 0xffu) - 127;
+    return e - 7;
+}
+
+__device__ __forceinline__ int term_scale_byte(int e0, int j) { return max(e0 - 4 * j + 127, 1); }
+
+// Four E4M3 terms of v for block exponent e0: v ~= sum_j q_j 2^(e0 - 4j), each
+// term rounding what the previous ones left.  Scale bytes clamp at 1 (2^-126):
+// such blocks are ~2^-120 small.
+__device__ __forceinline__ uint32_t quant4(float v, int e0) {
+    uint32_t out = 0;
+    float r = v;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int eb = term_scale_byte(e0, j);
+        const float s = __uint_as_float((uint32_t)eb << 23);
+        const float inv = __uint_as_float((uint32_t)(254 - eb) << 23);
+        const uint32_t q = to_e4m3(r * inv);
+        r -= from_e4m3(q) * s;
+        out |= q << (8 * j);
+    }
+    return out;
+}
+
+// GPT-OSS clamped SwiGLU in f32 with Go's math.Min/Max NaN semantics
+// (primitives.go:144-146): NaN propagates.
+__device__ __forceinline__ float swiglu(float gate, float up) {
+    float g = isnan(gate) ? gate : fminf(gate, 7.0f);
+    float u = isnan(up) ? up : fminf(fmaxf(up, -7.0f), 7.0f);
+    return g / (1.0f + expf(-1.702f * g)) * (u + 1.0f);
+}
+
+// Grid barrier among the epilogue warps of all CTAs (the launch is
+// cooperative, so every CTA is resident).  Barrier values grow monotonically
+// across launches (from each CTA's own epoch counter), so nothing is reset:
+// CTA b publishes its arrival in its own word; CTA 0 polls all of them and
+// publishes the release word every CTA polls.
+__device__ void grid_barrier(DecodeBarrier *bar, unsigned v, int32_t *err, int et) {
+    epi_bar();
+    if (et == 0) {
         __threadfence();
         st_release(&bar->arrive[blockIdx.x], v);
     }
     if (blockIdx.x == 0) {
-        for (int j = threadIdx.x; j < (int)gridDim.x; j += kDecComputeThreads) {
+        for (int j = et; j < (int)gridDim.x; j += kEpiThreads) {
             const long long t0 = clock64();
             while ((int)(ld_acquire(&bar->arrive[j]) - v) < 0) {
                 if (clock64() - t0 > kWaitLimit) {
-                    atomicCAS(err, 0, 32);
+                    atomicCAS(err, 0, 42);
                     break;
                 }
                 __nanosleep(32);
             }
         }
-        compute_bar();
-        if (threadIdx.x == 0) st_release(&bar->release, v);
+        epi_bar();
+        if (et == 0) st_release(&bar->release, v);
     }
-    if (threadIdx.x == 0) {
+    if (et == 0) {
         const long long t0 = clock64();
         while ((int)(ld_acquire(&bar->release) - v) < 0) {
             if (clock64() - t0 > kWaitLimit) {
-                atomicCAS(err, 0, 32);
+                atomicCAS(err, 0, 42);
                 break;
             }
             __nanosleep(32);
         }
         __threadfence();
     }
-    compute_bar();
+    epi_bar();
 }
 
-// Per-slot facts a warp caches while it walks the CTA's tiles.
-struct SlotInfo {
-    int e, base, m_e, xrow;  // xrow: staged row of this lane's token (phase 1)
+// A phase's geometry: the whole phase's box sequence and this CTA's run.
+struct Phase {
+    int nmt, nkb;  // 128-row tiles per expert, 128-element K boxes per tile
+    int nbox;      // boxes of the whole phase
+    int lo, hi;    // this CTA's boxes [lo, hi)
 };
 
-__launch_bounds__(kDecThreads, 1) __global__ void decode_kernel(DecodeParams p) {
-    extern __shared__ __align__(128) uint8_t sm[];
-    const DecLayout lay = dec_layout(p.T, p.H, p.I, p.E, p.k, p.stages, p.stage_bytes);
+__device__ __forceinline__ int run_start(int nbox, int b, int G) { return (int)((long long)nbox * b / G); }
+
+__device__ __forceinline__ Phase make_phase(int nmt, int nkb, int n_active) {
+    Phase ph;
+    ph.nmt = nmt;
+    ph.nkb = nkb;
+    ph.nbox = n_active * nmt * nkb;
+    ph.lo = run_start(ph.nbox, blockIdx.x, gridDim.x);
+    ph.hi = run_start(ph.nbox, blockIdx.x + 1, gridDim.x);
+    return ph;
+}
+
+// Largest b whose run starts at or before box x (the CTA whose run holds x).
+__device__ __forceinline__ int cta_of_box(int x, int nbox, int G) {
+    return (int)(((long long)(x + 1) * G - 1) / nbox);
+}
+
+// Walks a CTA's run in pipeline stages: up to kBoxes consecutive boxes of one
+// tile per stage, indices advanced without division.
+struct Walker {
+    int x, hi, nkb, nmt;
+    int slot, mt, kb;  // position of box x
+    __device__ __forceinline__ Walker(const Phase &q) : x(q.lo), hi(q.hi), nkb(q.nkb), nmt(q.nmt) {
+        const int tile = q.nkb > 0 ? q.lo / q.nkb : 0;
+        kb = q.lo - tile * q.nkb;
+        slot = q.nmt > 0 ? tile / q.nmt : 0;
+        mt = tile - slot * q.nmt;
+    }
+    __device__ __forceinline__ bool more() const { return x < hi; }
+    __device__ __forceinline__ int boxes() const { return min(kBoxes, min(nkb - kb, hi - x)); }
+    __device__ __forceinline__ void advance(int nb) {
+        x += nb;
+        kb += nb;
+        if (kb == nkb) {
+            kb = 0;
+            if (++mt == nmt) {
+                mt = 0;
+                ++slot;
+            }
+        }
+    }
+};
+
+template <int NT>
+__launch_bounds__(kDecThreads, 1) __global__
+    void decode_kernel(const __grid_constant__ CUtensorMap tm_gu, const __grid_constant__ CUtensorMap tm_dn,
+                       const __grid_constant__ CUtensorMap tm_act, DecodeParams p) {
+    constexpr uint32_t kBBox = b_box_bytes(NT);
+    constexpr uint32_t kStage = stage_bytes(NT);
+    extern __shared__ __align__(1024) uint8_t sm_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
+    const DecLayout lay = dec_layout(p.T, p.Hp, p.E, p.k, p.stages, NT);
     uint8_t *ring = sm + lay.ring;
-    uint8_t *xs = sm + lay.x;
-    float2 *red = reinterpret_cast<float2 *>(sm + lay.red);  // [kDecRed][warp][lane]
+    uint8_t *b1 = sm + lay.b1;
+    uint8_t *sfb1 = sm + lay.sfb1;
     int32_t *offs_s = reinterpret_cast<int32_t *>(sm + lay.offs);
     int32_t *act_s = reinterpret_cast<int32_t *>(sm + lay.act);
     int32_t *perm_s = reinterpret_cast<int32_t *>(sm + lay.perm);
     int32_t *inv_s = reinterpret_cast<int32_t *>(sm + lay.inv);
     float *w_s = reinterpret_cast<float *>(sm + lay.w);
+    float *xchg = reinterpret_cast<float *>(sm + lay.xchg);
+    volatile int *last_flag = reinterpret_cast<volatile int *>(sm + lay.xchg + 32);
+    volatile int *act_ready = reinterpret_cast<volatile int *>(sm + lay.xchg + 48);
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + lay.bars);
     uint64_t *empty = full + p.stages;
-    uint64_t *redfull = empty + p.stages;  // [kDecRed] every warp's partials written
-    uint64_t *reddone = redfull + kDecRed;  // [kDecRed] the reducer has read them
+    uint64_t *accfull = empty + p.stages;  // [2]
+    uint64_t *accempty = accfull + 2;      // [2]
+    uint64_t *b1ready = accempty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + lay.tmem_slot);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int E = p.E, P = p.T * p.k, R = p.stages;
-    const uint32_t xstride = dec_xstride(p.H, p.I);
-    // this launch's number, from the CTA's own count of completed launches
+    const int E = p.E, P = p.T * p.k, R = p.stages, G = gridDim.x;
     const unsigned epoch = p.bar->epoch[blockIdx.x] + 1u;
 
-    // routing tables (written by the router launch before this one)
+    if (tid == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_gu)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_dn)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_act)) : "memory");
+    }
     for (int i = tid; i <= E; i += kDecThreads) {
         offs_s[i] = p.offsets[i];
         act_s[i] = p.active[i];
@@ -243,216 +440,392 @@ __launch_bounds__(kDecThreads, 1) __global__ void decode_kernel(DecodeParams p) 
     }
     if (tid == 0) {
         for (int s = 0; s < R; ++s) {
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(full + s)));
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(empty + s)), "r"(kDecWarps));
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 1);
         }
-        for (int s = 0; s < kDecRed; ++s) {
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(redfull + s)), "r"(kDecWarps));
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(reddone + s)));
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(accfull + b, 1);
+            mbar_init(accempty + b, kEpiThreads);
         }
+        mbar_init(b1ready, kEpiThreads);
+        *last_flag = 0;
+        *act_ready = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
 
     const int n_active = act_s[E];
-    const int nrt1 = 2 * p.I / kTileRows, nkt1 = p.H / kTileK;
-    const int nrt2 = p.H / kTileRows, nkt2 = p.I / kTileK;
-    const long long N1 = (long long)n_active * nrt1, N2 = (long long)n_active * nrt2;
-    const int G = gridDim.x, b = blockIdx.x;
-    const int lo1 = (int)(N1 * b / G), n1 = (int)(N1 * (b + 1) / G) - lo1;
-    const int lo2 = (int)(N2 * b / G), n2 = (int)(N2 * (b + 1) / G) - lo2;
+    const int nkb1 = p.Hp / 128, nkb2 = p.Ip / 128;
+    const int nmt1 = 2 * p.I / 128, nmt2 = (p.H + 127) / 128;
+    const Phase ph[2] = {make_phase(nmt1, nkb1, n_active), make_phase(nmt2, nkb2, n_active)};
 
-    if (warp == kDecWarps) {
-        // ---------------- producer: one lane streams the CTA's row tiles ----------------
+    if (warp < kProdWarps) {
+        // ---------------- producers: stage i is warp i % kProdWarps's ----------------
         if (lane == 0) {
             int i = 0;
-            for (int phase = 0; phase < 2; ++phase) {
-                const int n = phase ? n2 : n1, nrt = phase ? nrt2 : nrt1, nkt = phase ? nkt2 : nkt1;
-                const int lo = phase ? lo2 : lo1;
-                int slot = lo / nrt, rt = lo - slot * nrt;
-                const uint32_t qb = (uint32_t)nkt * kTileQBytes, sb = (uint32_t)nkt * kTileSBytes;
-                for (int j = 0; j < n; ++j, ++i) {
-                    const int s = i % R;
-                    if (i >= R && !mbar_wait_bounded(empty + s, ((i / R) - 1) & 1, p.err, 30)) return;
-                    const int e = act_s[slot];
-                    const size_t tile0 = ((size_t)e * nrt + rt) * nkt;
-                    const uint8_t *q = (phase ? p.dn_q : p.gu_q) + tile0 * kTileQBytes;
-                    const uint8_t *sc = (phase ? p.dn_s : p.gu_s) + tile0 * kTileSBytes;
-                    const float *bias =
-                        (phase ? p.dn_b + (size_t)e * p.H : p.gu_b + (size_t)e * 2 * p.I) + kTileRows * rt;
-                    uint8_t *dst = ring + (size_t)s * p.stage_bytes;
-                    asm volatile(
-                        "{\n .reg .b64 st;\n mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}" ::"r"(
-                            smem_u32(full + s)),
-                        "r"(qb + sb + 64u)
-                        : "memory");
-                    bulk_g2s(dst, q, qb, full + s);
-                    bulk_g2s(dst + (size_t)p.nkt_max * kTileQBytes, sc, sb, full + s);
-                    bulk_g2s(dst + (size_t)p.nkt_max * (kTileQBytes + kTileSBytes), bias, 64u, full + s);
-                    if (++rt == nrt) {
-                        rt = 0;
-                        ++slot;
+            bool dead = false;
+            for (int f = 0; f < 2 && !dead; ++f) {
+                const CUtensorMap *tma = f ? &tm_dn : &tm_gu;
+                const uint8_t *tsf = f ? p.dn_tsf : p.gu_tsf;
+                const int nmt = ph[f].nmt, nkb = ph[f].nkb;
+                for (Walker w(ph[f]); w.more(); ++i) {
+                    const int s = i % R, nb = w.boxes();
+                    if (i % kProdWarps != warp) {
+                        w.advance(nb);
+                        continue;
                     }
+                    if (i >= R && !mbar_wait(empty + s, ((i / R) - 1) & 1, p.err, 30)) {
+                        dead = true;
+                        break;
+                    }
+                    const int e = act_s[w.slot];
+                    uint8_t *st = ring + (size_t)s * kStage;
+                    mbar_expect_tx(full + s, (uint32_t)nb * (kAPacked + 512 + (f ? kBBox + 512 : 0)));
+                    const int box0 = (e * nmt + w.mt) * nkb + w.kb;  // box-tiled plane: row origin 128 * box
+                    for (int b = 0; b < nb; ++b) tma_2d(st + b * kABytes, tma, full + s, 0, (box0 + b) * 128);
+                    bulk_g2s(st + kBoxes * kABytes, tsf + (((size_t)e * nmt + w.mt) * nkb + w.kb) * 512, nb * 512,
+                             full + s);
+                    if (f) {
+                        // the activation operand exists once every CTA has finished phase 1
+                        if (*act_ready == 0) {
+                            const long long t0 = clock64();
+                            while (*act_ready == 0) {
+                                if (clock64() - t0 > kWaitLimit) {
+                                    atomicCAS(p.err, 0, 31);
+                                    break;
+                                }
+                                __nanosleep(64);
+                            }
+                        }
+                        uint8_t *bst = st + kBoxes * (kABytes + 512);
+                        for (int b = 0; b < nb; ++b) tma_3d(bst + b * kBBox, &tm_act, full + s, (w.kb + b) * 128, 0, w.slot);
+                        bulk_g2s(bst + kBoxes * kBBox, p.act_sf + ((size_t)w.slot * nkb2 + w.kb) * 512, nb * 512,
+                                 full + s);
+                    }
+                    w.advance(nb);
                 }
             }
         }
-        return;
-    }
-
-    // ---------------- compute warps ----------------
-    // B fragment of lane (g, c): column g = token g/2, fp16 hi (g even) or lo (g odd)
-    // part of its row; D columns 2c, 2c+1 are then token c's hi and lo products.
-    const int g = lane >> 2, c = lane & 3, tok = g >> 1, part = g & 1;
-    {
-        const int chunks = p.H / 8;
-        const int total = p.T * 2 * chunks;
-        for (int i = tid; i < total; i += kDecComputeThreads) {
-            const int r = i / (2 * chunks), rem = i - r * 2 * chunks;
-            const int lo = rem >= chunks, ch = rem - (lo ? chunks : 0);
-            const uint4 v = *reinterpret_cast<const uint4 *>((lo ? p.x_lo : p.x_hi) + (size_t)r * p.H + 8 * ch);
-            *reinterpret_cast<uint4 *>(xs + (size_t)(lo * p.T + r) * xstride + 16 * ch) = v;
-        }
-    }
-    compute_bar();
-
-    int i = 0;
-    for (int phase = 0; phase < 2; ++phase) {
-        const int n = phase ? n2 : n1, nrt = phase ? nrt2 : nrt1, nkt = phase ? nkt2 : nkt1;
-        const int lo = phase ? lo2 : lo1;
-        if (phase == 1) grid_barrier(p.bar, 2u * epoch, p.err);  // every act row of phase 1 written
-        int slot = lo / nrt, rt = lo - slot * nrt;
-        int cur = -1;
-        SlotInfo si{0, 0, 0, 0};
-        for (int j = 0; j < n; ++j, ++i) {
-            if (slot != cur) {
-                si.e = act_s[slot];
-                si.base = offs_s[si.e];
-                si.m_e = offs_s[si.e + 1] - si.base;
-                if (si.m_e > p.T) {  // top-k picks distinct experts: at most one pair per token
-                    if (tid == 0) atomicCAS(p.err, 0, 33);
-                    si.m_e = p.T;
-                }
-                if (phase == 0) {
-                    si.xrow = tok < si.m_e ? perm_s[si.base + tok] / p.k : 0;
-                } else {
-                    // restage: the slot's act rows (positions base..base+m_e-1), read from L2
-                    compute_bar();
-                    const int chunks = p.I / 8;
-                    const int total = si.m_e * 2 * chunks;
-                    for (int q = tid; q < total; q += kDecComputeThreads) {
-                        const int r = q / (2 * chunks), rem = q - r * 2 * chunks;
-                        const int lo_ = rem >= chunks, ch = rem - (lo_ ? chunks : 0);
-                        const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(
-                                                   (lo_ ? p.act_lo : p.act_hi) + (size_t)(si.base + r) * p.I) +
-                                               ch);
-                        *reinterpret_cast<uint4 *>(xs + (size_t)(lo_ * p.T + r) * xstride + 16 * ch) = v;
-                    }
-                    compute_bar();
-                    si.xrow = tok;
-                }
-                cur = slot;
-            }
-            const int s = i % R;
-            const bool ok = mbar_wait_bounded(full + s, (i / R) & 1, p.err, 31);
-            const uint8_t *stq = ring + (size_t)s * p.stage_bytes;
-            const uint8_t *sts = stq + (size_t)p.nkt_max * kTileQBytes;
-            const bool valid = tok < si.m_e;
-            const uint8_t *xb = xs + (size_t)(part * p.T + si.xrow) * xstride + 16 * c;
-            float acc0 = 0.0f, acc1 = 0.0f;  // rows g, g+8 of the tile, token c
-            if (ok) {
-#pragma unroll 2
-                for (int kt = warp; kt < nkt; kt += kDecWarps) {
-                    const uint4 qv = *reinterpret_cast<const uint4 *>(stq + kt * kTileQBytes + lane * 16);
-                    float sc[4];
-                    e8m0x4_to_float(*reinterpret_cast<const uint32_t *>(sts + kt * kTileSBytes + 4 * g), sc);
-                    uint4 xv0 = make_uint4(0, 0, 0, 0), xv1 = make_uint4(0, 0, 0, 0);
-                    if (valid) {
-                        xv0 = *reinterpret_cast<const uint4 *>(xb + kt * 128);
-                        xv1 = *reinterpret_cast<const uint4 *>(xb + kt * 128 + 64);
-                    }
-                    const uint4 a0 = e2m1x8_to_f16(qv.x), a1 = e2m1x8_to_f16(qv.y);  // block 0: rows g, g+8
-                    const uint4 b0 = e2m1x8_to_f16(qv.z), b1 = e2m1x8_to_f16(qv.w);  // block 1
-                    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    mma16816(d, a0.x, a1.x, a0.y, a1.y, xv0.x, xv0.y);
-                    mma16816(d, a0.z, a1.z, a0.w, a1.w, xv0.z, xv0.w);
-                    float f[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    mma16816(f, b0.x, b1.x, b0.y, b1.y, xv1.x, xv1.y);
-                    mma16816(f, b0.z, b1.z, b0.w, b1.w, xv1.z, xv1.w);
-                    acc0 = fmaf(d[0] + d[1], sc[0], acc0);
-                    acc1 = fmaf(d[2] + d[3], sc[2], acc1);
-                    acc0 = fmaf(f[0] + f[1], sc[1], acc0);
-                    acc1 = fmaf(f[2] + f[3], sc[3], acc1);
-                }
-            }
-            const int rbuf = i % kDecRed;
-            if (i >= kDecRed) mbar_wait_bounded(reddone + rbuf, ((i / kDecRed) - 1) & 1, p.err, 34);
-            float2 *rb = red + (size_t)rbuf * kDecWarps * 32;
-            rb[warp * 32 + lane] = make_float2(acc0, acc1);
-            __syncwarp();
-            const bool reducer = warp == i % kDecWarps;
-            if (lane == 0) {
-                mbar_arrive(redfull + rbuf);
-                if (!reducer) mbar_arrive(empty + s);  // done with the stage's smem
-            }
-            if (reducer) {
-                mbar_wait_bounded(redfull + rbuf, (i / kDecRed) & 1, p.err, 35);
-                float v0 = 0.0f, v1 = 0.0f;
+    } else if (warp == kMmaWarp) {
+        // ---------------- MMA issuer ----------------
+        // The whole warp walks the stages (warp-uniform descriptors stay in
+        // uniform registers); one elected lane issues the tcgen05 operations.
+        uint32_t elected;
+        asm volatile("{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}" : "=r"(elected));
+        uint32_t idesc[4];
 #pragma unroll
-                for (int w = 0; w < kDecWarps; ++w) {  // fixed order: deterministic
-                    const float2 t = rb[w * 32 + lane];
-                    v0 += t.x;
-                    v1 += t.y;
+        for (int kk = 0; kk < 4; ++kk) idesc[kk] = idesc_bs(kk, NT);
+        const uint32_t ring_a = smem_u32(ring), b1_a = smem_u32(b1), sfb1_a = smem_u32(sfb1);
+        int i = 0, seg = 0;
+        bool ok = mbar_wait(b1ready, 0, p.err, 32);
+        for (int f = 0; f < 2 && ok; ++f) {
+            Walker w(ph[f]);
+            while (w.more() && ok) {
+                // one segment: this CTA's boxes of one tile
+                const int buf = seg & 1;
+                if (!mbar_wait(accempty + buf, ((seg >> 1) & 1) ^ 1, p.err, 33)) {
+                    ok = false;
+                    break;
                 }
-                const float *stb =
-                    reinterpret_cast<const float *>(stq + (size_t)p.nkt_max * (kTileQBytes + kTileSBytes));
-                if (c < si.m_e) {
-                    const size_t pos = (size_t)si.base + c;
-                    if (phase == 0) {
-                        const int pr = 8 * rt + g;  // SwiGLU pair: GGUF rows 2pr (gate), 2pr+1 (up)
-                        const float a = swiglu(v0 + stb[2 * g], v1 + stb[2 * g + 1]);
-                        const __half hi = __float2half_rn(a);
-                        const __half lo_ = __float2half_rn(a - __half2float(hi));
-                        p.act_hi[pos * p.I + pr] = hi;
-                        p.act_lo[pos * p.I + pr] = lo_;
-                    } else {
-                        const int h = kTileRows * rt + g;
-                        p.y[pos * p.H + h] = v0 + stb[g];
-                        p.y[pos * p.H + h + 8] = v1 + stb[g + 8];
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(buf * NT);
+                uint32_t acc = 0;
+                for (;;) {
+                    const int s = i % R, nb = w.boxes();
+                    if (!mbar_wait(full + s, (i / R) & 1, p.err, 34)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t st = ring_a + (uint32_t)s * kStage;
+                    const uint32_t sfa = tmem + 32u + 16u * (uint32_t)s, sfb = sfa + 8u;
+                    for (int b = 0; b < nb; ++b) {
+                        const uint32_t bsrc = f ? st + kBoxes * (kABytes + 512) + b * kBBox : b1_a + (uint32_t)(w.kb + b) * kBBox;
+                        const uint32_t sfb_src = f ? st + kBoxes * (kABytes + 512 + kBBox) + 512 * b
+                                                   : sfb1_a + (uint32_t)(w.kb + b) * 512;
+                        const uint32_t a0 = st + b * kABytes;
+                        if (elected) {
+                            sf_copy(sfa + 4 * b, st + kBoxes * kABytes + 512 * b);
+                            sf_copy(sfb + 4 * b, sfb_src);
+#pragma unroll
+                            for (int kk = 0; kk < 4; ++kk) {
+                                umma_bs(d, desc_sw128(a0 + 32 * kk), desc_sw128(bsrc + 32 * kk), idesc[kk], acc,
+                                        sfa + 4 * b, sfb + 4 * b);
+                                acc = 1u;
+                            }
+                        }
+                        acc = 1u;
+                    }
+                    if (elected) umma_commit(empty + s);
+                    __syncwarp();
+                    ++i;
+                    const bool tile_end = w.kb + nb == w.nkb;
+                    w.advance(nb);
+                    if (tile_end || !w.more()) break;
+                }
+                if (elected) umma_commit(accfull + buf);
+                __syncwarp();
+                ++seg;
+            }
+        }
+    } else {
+        // ---------------- epilogue warps ----------------
+        const int et = tid - kEpiWarp0 * 32;  // 0..127
+        const int quad = warp & 3;         // TMEM lane quadrant
+        const int row = quad * 32 + lane;  // row of the 128-row tile this thread owns
+        // (a) phase-1 operand: every token's normalized row as four E4M3 terms.
+        //     Item = 8 elements; four consecutive lanes hold one 32-element block.
+        {
+            const int n8 = p.Hp / 8, total = p.T * n8;
+            for (int base = 0; base < total; base += kEpiThreads) {
+                const int it = base + et;
+                const bool valid = it < total;
+                const int t = valid ? it / n8 : 0, k8 = valid ? it - t * n8 : 0;
+                const int k0 = 8 * k8;
+                float v[8];
+                float amax = 0.0f;
+                uint4 h = make_uint4(0, 0, 0, 0), l = make_uint4(0, 0, 0, 0);
+                if (valid && k0 < p.H) {
+                    h = *reinterpret_cast<const uint4 *>(p.x_hi + (size_t)t * p.H + k0);
+                    l = *reinterpret_cast<const uint4 *>(p.x_lo + (size_t)t * p.H + k0);
+                }
+                const __half2 *hh = reinterpret_cast<const __half2 *>(&h);
+                const __half2 *ll = reinterpret_cast<const __half2 *>(&l);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float2 a = __half22float2(hh[u]), bb = __half22float2(ll[u]);
+                    v[2 * u] = a.x + bb.x;
+                    v[2 * u + 1] = a.y + bb.y;
+                    amax = fmaxf(amax, fmaxf(fabsf(v[2 * u]), fabsf(v[2 * u + 1])));
+                }
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+                if (!valid) continue;
+                const int e0 = block_exp(amax);
+                uint32_t lo4[4] = {0, 0, 0, 0}, hi4[4] = {0, 0, 0, 0};  // [term]: elements 0-3, 4-7
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const uint32_t q = quant4(v[i], e0);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint32_t byte = ((q >> (8 * j)) & 0xffu) << (8 * (i & 3));
+                        if (i < 4) lo4[j] |= byte;
+                        else hi4[j] |= byte;
                     }
                 }
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(reddone + rbuf);
-                    mbar_arrive(empty + s);  // bias read: the stage may be refilled
+                const int box = k0 / 128, chunk = (k0 % 128) / 16, half = (k0 % 16) / 8;
+                uint8_t *bx = b1 + (size_t)box * kBBox;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int n = 4 * t + j;  // B row: token t, term j (SWIZZLE_128B: chunk ^ row % 8)
+                    uint8_t *dst = bx + (n >> 3) * 1024 + (n & 7) * 128 + ((chunk ^ (n & 7)) << 4) + 8 * half;
+                    *reinterpret_cast<uint2 *>(dst) = make_uint2(lo4[j], hi4[j]);
+                    if ((k8 & 3) == 0) sfb1[(size_t)box * 512 + n * 16 + (k0 % 128) / 32] = (uint8_t)term_scale_byte(e0, j);
                 }
             }
-            if (++rt == nrt) {
-                rt = 0;
-                ++slot;
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(b1ready);
+        }
+        // (b) the CTA's tile segments, phase 1 then phase 2
+        float *part = p.partial + (size_t)blockIdx.x * 2 * 128 * kNMax;
+        int seg = 0;
+        for (int f = 0; f < 2; ++f) {
+            const Phase &q = ph[f];
+            if (f == 1) {
+                grid_barrier(p.bar, 2u * epoch, p.err, et);
+                if (et == 0) *act_ready = 1;
+            }
+            int x = q.lo;
+            while (x < q.hi) {
+                const int tile = x / q.nkb;
+                const int tbeg = tile * q.nkb, tend_full = tbeg + q.nkb;
+                const int tend = min(tend_full, q.hi);
+                const int slot = tile / q.nmt, mt = tile - slot * q.nmt;
+                const int e = act_s[slot];
+                const int base = offs_s[e];
+                int m_e = offs_s[e + 1] - base;
+                if (m_e > p.T) m_e = p.T;  // at most one pair per token (distinct top-k experts)
+                // this row's bias, loaded while the MMAs run
+                const int grp = row >> 4, j16 = row & 15;
+                const bool gate_lane = j16 < 8;
+                const int pr = 64 * mt + 8 * grp + (j16 & 7);  // phase 1: SwiGLU pair = activation column
+                const int h = 128 * mt + row;                   // phase 2: output row
+                float bias = 0.0f;
+                if (f == 0) bias = p.gu_b[(size_t)e * 2 * p.I + 2 * pr + (gate_lane ? 0 : 1)];
+                else if (h < p.H) bias = p.dn_b[(size_t)e * p.H + h];
+                const int buf = seg & 1;
+                float v[NT];
+                mbar_wait(accfull + buf, (seg >> 1) & 1, p.err, 35);
+                tc_fence_after();
+                {
+                    float t16[16];
+                    tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * NT), t16);
+#pragma unroll
+                    for (int c = 0; c < NT; ++c) v[c] = t16[c];
+                }
+                tc_fence_before();
+                mbar_arrive(accempty + buf);
+                ++seg;
+                const bool whole = x == tbeg && tend == tend_full;
+                const bool head = x == q.lo;
+                x = tend;
+                if (!whole) {
+                    // a split tile: the last of its CTAs to arrive adds the partials in CTA order
+                    const int b_first = cta_of_box(tbeg, q.nbox, G), b_last = cta_of_box(tend_full - 1, q.nbox, G);
+                    float *mine = part + (size_t)(head ? 0 : 1) * 128 * kNMax + (size_t)row * kNMax;
+#pragma unroll
+                    for (int c = 0; c < NT; c += 4)
+                        __stcg(reinterpret_cast<float4 *>(mine + c), make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]));
+                    __threadfence();
+                    epi_bar();
+                    if (et == 0) {
+                        unsigned nseg = 0;
+                        for (int b = b_first; b <= b_last; ++b)
+                            nseg += run_start(q.nbox, b + 1, G) > run_start(q.nbox, b, G) ? 1u : 0u;
+                        const unsigned old =
+                            atomicInc(p.cnt + ((size_t)f * p.S + slot) * kTilesPerSlot + mt, nseg - 1u);
+                        *last_flag = old == nseg - 1u;
+                    }
+                    epi_bar();
+                    const bool last = *last_flag != 0;
+                    epi_bar();
+                    if (!last) continue;
+                    __threadfence();
+#pragma unroll
+                    for (int c = 0; c < NT; ++c) v[c] = 0.0f;
+                    for (int b = b_first; b <= b_last; ++b) {
+                        const int blo = run_start(q.nbox, b, G), bhi = run_start(q.nbox, b + 1, G);
+                        if (bhi <= blo) continue;  // empty run: no piece
+                        // CTA b's piece: the head of its run if the run starts inside this tile
+                        const float *src =
+                            p.partial + ((size_t)b * 2 + (blo >= tbeg ? 0 : 1)) * 128 * kNMax + (size_t)row * kNMax;
+#pragma unroll
+                        for (int c = 0; c < NT; c += 4) {
+                            const float4 t4 = __ldcg(reinterpret_cast<const float4 *>(src + c));
+                            v[c] += t4.x;
+                            v[c + 1] += t4.y;
+                            v[c + 2] += t4.z;
+                            v[c + 3] += t4.w;
+                        }
+                    }
+                }
+                // ---- finalize the tile ----
+                if (f == 0) {
+                    // rows 16g'+j (j < 8) hold the gate of pair 8g'+j, row +8 its up row
+                    for (int g = 0; g < m_e; ++g) {
+                        const int t = perm_s[base + g] / p.k;
+                        float val = 0.0f;
+#pragma unroll
+                        for (int c = 0; c < NT; c += 4)
+                            if (c / 4 == t) val = v[c] + v[c + 1] + v[c + 2] + v[c + 3];
+                        val += bias;
+                        const float up = __shfl_down_sync(0xffffffffu, val, 8);
+                        const float a = gate_lane ? swiglu(val, up) : 0.0f;
+                        // the 32-pair block of this row: rows 0-63 (quadrants 0, 1) or 64-127 (2, 3)
+                        float m = gate_lane ? fabsf(a) : 0.0f;
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                        if (lane == 0) xchg[quad] = m;
+                        epi_bar();
+                        const float amax = fmaxf(xchg[quad & 2], xchg[(quad & 2) + 1]);
+                        epi_bar();
+                        const int e0 = block_exp(amax);
+                        if (gate_lane) {
+                            const uint32_t q4 = quant4(a, e0);
+                            uint8_t *dst = p.act_q + ((size_t)slot * 16 + 4 * g) * p.Ip + pr;
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) dst[(size_t)j * p.Ip] = (uint8_t)(q4 >> (8 * j));
+                        }
+                        if (lane == 0 && (quad & 1) == 0) {  // one writer per block of 32 pairs
+                            const int blk = 2 * mt + (quad >> 1);
+                            uint8_t *sfd = p.act_sf + ((size_t)slot * (p.Ip / 128) + blk / 4) * 512;
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+                                sfd[(4 * g + j) * 16 + (blk % 4)] = (uint8_t)term_scale_byte(e0, j);
+                        }
+                    }
+                } else if (h < p.H) {
+#pragma unroll
+                    for (int c = 0; c < NT; c += 4)
+                        if (c / 4 < m_e) p.y[(size_t)(base + c / 4) * p.H + h] = v[c] + v[c + 1] + v[c + 2] + v[c + 3] + bias;
+                }
             }
         }
-    }
-    grid_barrier(p.bar, 2u * epoch + 1u, p.err);  // every y row written
-
-    // ---------------- phase 3: slot-order combine + residual ----------------
-    const int H4 = p.H / 4;
-    const long long items = (long long)p.T * H4;
-    for (long long it = (long long)b * kDecComputeThreads + tid; it < items; it += (long long)G * kDecComputeThreads) {
-        const int t = (int)(it / H4), i4 = (int)(it - (long long)t * H4);
-        double m0 = 0.0, m1 = 0.0, m2 = 0.0, m3 = 0.0;
-        for (int s = 0; s < p.k; ++s) {
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(p.y + (size_t)inv_s[t * p.k + s] * p.H) + i4);
-            const double ws = (double)w_s[t * p.k + s];
-            m0 += ws * (double)v.x;
-            m1 += ws * (double)v.y;
-            m2 += ws * (double)v.z;
-            m3 += ws * (double)v.w;
+        grid_barrier(p.bar, 2u * epoch + 1u, p.err, et);
+        // (c) slot-order combine with the residual
+        const int H4 = p.H / 4;
+        const long long items = (long long)p.T * H4;
+        for (long long it = (long long)blockIdx.x * kEpiThreads + et; it < items; it += (long long)G * kEpiThreads) {
+            const int t = (int)(it / H4), i4 = (int)(it - (long long)t * H4);
+            double m0 = 0.0, m1 = 0.0, m2 = 0.0, m3 = 0.0;
+            for (int s = 0; s < p.k; ++s) {
+                const float4 yv = __ldcg(reinterpret_cast<const float4 *>(p.y + (size_t)inv_s[t * p.k + s] * p.H) + i4);
+                const double ws = (double)w_s[t * p.k + s];
+                m0 += ws * (double)yv.x;
+                m1 += ws * (double)yv.y;
+                m2 += ws * (double)yv.z;
+                m3 += ws * (double)yv.w;
+            }
+            const float4 r = reinterpret_cast<const float4 *>(p.residual + (size_t)t * p.H)[i4];
+            reinterpret_cast<float4 *>(p.out + (size_t)t * p.H)[i4] =
+                make_float4(r.x + (float)m0, r.y + (float)m1, r.z + (float)m2, r.w + (float)m3);
         }
-        const float4 r = reinterpret_cast<const float4 *>(p.residual + (size_t)t * p.H)[i4];
-        reinterpret_cast<float4 *>(p.out + (size_t)t * p.H)[i4] =
-            make_float4(r.x + (float)m0, r.y + (float)m1, r.z + (float)m2, r.w + (float)m3);
+        if (et == 0) p.bar->epoch[blockIdx.x] = epoch;
     }
-    if (tid == 0) p.bar->epoch[blockIdx.x] = epoch;
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == kMmaWarp)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+}
+
+// ---- host side -------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool get_encode() {
+    std::call_once(g_encode_once, []() {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    return g_encode != nullptr;
+}
+
+// Box-tiled E2M1 plane: rows of 128 packed 4-bit elements (64 B), 128-row boxes.
+cudaError_t map_boxes(CUtensorMap *tm, void *base, uint64_t rows) {
+    cuuint64_t dims[2] = {128, rows};
+    cuuint64_t strides[1] = {64};
+    cuuint32_t box[2] = {128, 128};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 2, base, dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// 3-D map over [z][y][x]: x packed 4-bit (fp4) or bytes, boxes 128 x box_y x 1,
+// SWIZZLE_128B, zero fill out of bounds.
+cudaError_t map3d(CUtensorMap *tm, void *base, bool fp4, uint64_t x, uint64_t y, uint64_t z, uint32_t box_y) {
+    const uint64_t row_bytes = fp4 ? x / 2 : x;
+    cuuint64_t dims[3] = {x, y, z};
+    cuuint64_t strides[2] = {row_bytes, row_bytes * y};
+    cuuint32_t box[3] = {128, box_y, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = g_encode(tm, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base,
+                          dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
 struct DecodeCaps {
@@ -473,25 +846,52 @@ const DecodeCaps &caps(int device) {
     return g_caps[device];
 }
 
-int dec_stages(int T, int H, int I, int E, int k) {
-    const uint32_t sb = dec_stage_bytes(H, I);
-    const DecLayout none = dec_layout(T, H, I, E, k, 0, sb);
-    if (none.total >= kDecSmemBudget) return 0;
-    int st = (int)((kDecSmemBudget - none.total) / (sb + 16));
-    return st > kDecMaxStages ? kDecMaxStages : st;
+int dec_n(int T) { return 4 * T <= 8 ? 8 : 16; }
+
+int dec_stages(int T, int Hp, int E, int k) {
+    const int nt = dec_n(T);
+    const DecLayout none = dec_layout(T, Hp, E, k, 0, nt);
+    if (none.total >= kSmemBudget) return 0;
+    const int st = (int)((kSmemBudget - none.total) / (stage_bytes(nt) + 16));
+    return st > kMaxStages ? kMaxStages : st;
 }
 
+int dec_slots(const Dims &d) { return d.E < kDecodeMaxTokens * d.k ? d.E : kDecodeMaxTokens * d.k; }
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
 }  // namespace
+
+size_t decode_scratch_bytes(const Dims &d, int device) {
+    const int G = device >= 0 && device < 64 && caps(device).sms > 0 ? caps(device).sms : 1;
+    const int S = dec_slots(d), Ip = kpad128(d.I);
+    return align256((size_t)S * 16 * Ip) + align256((size_t)S * (Ip / 128) * 512) +
+           align256((size_t)G * 2 * 128 * kNMax * 4) + (size_t)2 * S * kTilesPerSlot * 4;
+}
+
+cudaError_t init_decode_scratch(const Dims &d, int device, void *scratch, cudaStream_t st) {
+    const int S = dec_slots(d), Ip = kpad128(d.I);
+    uint8_t *b = static_cast<uint8_t *>(scratch);
+    cudaError_t e = cudaMemsetAsync(b, 0, decode_scratch_bytes(d, device), st);
+    if (e != cudaSuccess) return e;
+    // activation scale bytes: 2^0 wherever no block is ever written (K padding)
+    return cudaMemsetAsync(b + align256((size_t)S * 16 * Ip), 127, (size_t)S * (Ip / 128) * 512, st);
+}
 
 bool decode_supported(const Dims &d, int T, int device) {
     if (T < 1 || T > kDecodeMaxTokens || device < 0 || device >= 64) return false;
     const DecodeCaps &cp = caps(device);
-    return cp.coop && cp.sms > 0 && cp.sms <= kDecodeMaxCtas && dec_stages(T, d.H, d.I, d.E, d.k) >= 2;
+    if (!cp.coop || cp.sms <= 0 || cp.sms > kDecodeMaxCtas || !get_encode()) return false;
+    if ((2 * d.I) % 128 || 2 * d.I / 128 > kTilesPerSlot || (d.H + 127) / 128 > kTilesPerSlot) return false;
+    return dec_stages(T, kpad128(d.H), d.E, d.k) >= 2;
 }
 
 cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, const float *residual, int T,
-                          __half *act_hi, __half *act_lo, float *y, float *out, DecodeBarrier *bar, int32_t *err,
-                          int device, cudaStream_t st) {
+                          void *scratch, float *y, float *out, DecodeBarrier *bar, int32_t *err, int device,
+                          cudaStream_t st) {
+    const int S = dec_slots(d), Hp = kpad128(d.H), Ip = kpad128(d.I);
+    const int G = caps(device).sms;
+    uint8_t *b = static_cast<uint8_t *>(scratch);
     DecodeParams p{};
     p.residual = residual;
     p.out = out;
@@ -502,31 +902,42 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
     p.active = r.active;
     p.inv = r.inv;
     p.topk_w = r.topk_w;
-    p.gu_q = L.gu_q;
-    p.gu_s = L.gu_s;
-    p.dn_q = L.dn_q;
-    p.dn_s = L.dn_s;
+    p.gu_tsf = L.gu_tsf;
+    p.dn_tsf = L.dn_tsf;
     p.gu_b = L.gu_b;
     p.dn_b = L.dn_b;
-    p.act_hi = act_hi;
-    p.act_lo = act_lo;
+    p.act_q = b;
+    b += align256((size_t)S * 16 * Ip);
+    p.act_sf = b;
+    b += align256((size_t)S * (Ip / 128) * 512);
+    p.partial = reinterpret_cast<float *>(b);
+    b += align256((size_t)G * 2 * 128 * kNMax * 4);
+    p.cnt = reinterpret_cast<uint32_t *>(b);
     p.y = y;
+    p.bar = bar;
+    p.err = err;
     p.T = T;
     p.H = d.H;
     p.I = d.I;
     p.E = d.E;
     p.k = d.k;
-    p.stages = dec_stages(T, d.H, d.I, d.E, d.k);
-    p.stage_bytes = dec_stage_bytes(d.H, d.I);
-    p.nkt_max = (d.H > d.I ? d.H : d.I) / kTileK;
-    p.bar = bar;
-    p.err = err;
-    if (p.stages < 2) return cudaErrorInvalidValue;
-    const size_t smem = dec_layout(T, d.H, d.I, d.E, d.k, p.stages, p.stage_bytes).total;
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    p.Hp = Hp;
+    p.Ip = Ip;
+    p.S = S;
+    p.stages = dec_stages(T, Hp, d.E, d.k);
+    p.N = dec_n(T);
+    if (p.stages < 2 || !get_encode()) return cudaErrorInvalidValue;
+    CUtensorMap tm_gu, tm_dn, tm_act;
+    cudaError_t e = map_boxes(&tm_gu, L.gu_tq, tq_bytes(d.E, 2 * d.I, d.H) / 64);
+    if (e == cudaSuccess) e = map_boxes(&tm_dn, L.dn_tq, tq_bytes(d.E, d.H, d.I) / 64);
+    if (e == cudaSuccess) e = map3d(&tm_act, p.act_q, false, (uint64_t)Ip, 16, (uint64_t)S, (uint32_t)p.N);
+    if (e != cudaSuccess) return e;
+    const size_t smem = dec_layout(T, Hp, d.E, d.k, p.stages, p.N).total;
+    auto kern = p.N == 8 ? decode_kernel<8> : decode_kernel<16>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(caps(device).sms);
+    cfg.gridDim = dim3(G);
     cfg.blockDim = dim3(kDecThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -535,8 +946,7 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, decode_kernel, p);
-    return e;
+    return cudaLaunchKernelEx(&cfg, kern, tm_gu, tm_dn, tm_act, p);
 }
 
 }  // namespace amoe
