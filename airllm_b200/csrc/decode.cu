@@ -3,10 +3,12 @@
 //
 //   phase 1  gate_up = x . W_gu^T + b_gu -> clamped SwiGLU      (layer.go:139-148, 175;
 //                                                                primitives.go:138-149)
-//   -------- grid barrier (every activation row written)
 //   phase 2  y = act . W_dn^T + b_dn                             (layer.go:179-187)
-//   -------- grid barrier (every y row written)
 //   phase 3  out = residual + f32(sum_s f64(w_s) * f64(y_s))      (layer.go:109-121)
+//
+// No grid-wide barrier: a finished tile publishes a per-launch flag; an
+// expert's down tiles wait for that expert's gate_up tiles, and each 128-row
+// slice of the combine waits for the down tiles of those rows.
 //
 // The MXFP4 experts are consumed as stored: tcgen05.mma kind::mxf8f6f4 with
 // A = E2M1 weights straight from the TMA planes (TMA unpacks the nibbles into
@@ -22,11 +24,12 @@
 // [n*b/G, n*(b+1)/G) (stream-K), so every SM streams the same number of
 // bytes.  A tile cut between CTAs is summed by whichever of its CTAs arrives
 // last (self-resetting counter), adding the partials in CTA order
-// (deterministic).  The down boxes do not depend on phase 1, so the producer
-// streams them before the grid barrier; only their activation operand waits.
+// (deterministic).  The down boxes do not depend on phase 1, so the producers
+// stream them early; only their activation operand waits for its expert.
 //
 // Roles: warps 0-3 TMA producers (stage i filled by warp i % 4), warp 4 MMA
-// issuer and TMEM owner, warps 5-8 epilogue (TMEM lane quadrants 1, 2, 3, 0).
+// issuer and TMEM owner, warps 5-8 epilogue (TMEM lane quadrants 1, 2, 3, 0),
+// warp 9 watches the gate_up tiles this CTA's down boxes depend on.
 // Every wait is bounded (~1 s of clock): it records a code in the error flag
 // and the kernel winds down.
 #include "amoe_internal.cuh"
@@ -47,7 +50,8 @@ constexpr int kMmaWarp = kProdWarps;
 constexpr int kEpiWarp0 = kProdWarps + 1;
 constexpr int kEpiWarps = 4;
 constexpr int kEpiThreads = kEpiWarps * 32;
-constexpr int kDecThreads = (kEpiWarp0 + kEpiWarps) * 32;
+constexpr int kWatchWarp = kEpiWarp0 + kEpiWarps;  // polls other CTAs' tile flags
+constexpr int kDecThreads = (kWatchWarp + 1) * 32;
 constexpr int kNMax = 16;                       // MMA N: up to 4 tokens x 4 terms
 constexpr int kBoxes = 2;                       // 128-element K boxes per pipeline stage
 constexpr int kMaxStages = 6;
@@ -77,6 +81,7 @@ struct DecodeParams {
     float *y;                   // [P][H]
     float *partial;             // [G][2][128][kNMax]
     uint32_t *cnt;              // [2][S][kTilesPerSlot] self-resetting tile counters
+    unsigned *tflag;            // [2][S][kTilesPerSlot] launch epoch of each finished tile
     DecodeBarrier *bar;
     int32_t *err;
     int T, H, I, E, k, Hp, Ip, S;
@@ -85,7 +90,7 @@ struct DecodeParams {
 };
 
 struct DecLayout {
-    uint32_t ring, b1, sfb1, offs, act, perm, inv, w, xchg, bars, tmem_slot, total;
+    uint32_t ring, b1, sfb1, offs, act, perm, inv, w, ready, xchg, bars, tmem_slot, total;
 };
 
 __host__ __device__ inline DecLayout dec_layout(int T, int Hp, int E, int k, int stages, int nt) {
@@ -108,6 +113,8 @@ __host__ __device__ inline DecLayout dec_layout(int T, int Hp, int E, int k, int
     o += P * 4;
     L.w = o;
     o += P * 4;
+    L.ready = o;  // [min(E, P)] phase-2 operand of the slot complete
+    o += (uint32_t)(E < (int)P ? E : (int)P) * 4;
     L.xchg = o;
     o += 64;  // block maxima of the activation quantization + flags
     o = (o + 7u) & ~7u;
@@ -304,43 +311,27 @@ __device__ __forceinline__ float swiglu(float gate, float up) {
     return g / (1.0f + expf(-1.702f * g)) * (u + 1.0f);
 }
 
-// Grid barrier among the epilogue warps of all CTAs (the launch is
-// cooperative, so every CTA is resident).  Barrier values grow monotonically
-// across launches (from each CTA's own epoch counter), so nothing is reset:
-// CTA b publishes its arrival in its own word; CTA 0 polls all of them and
-// publishes the release word every CTA polls.
-__device__ void grid_barrier(DecodeBarrier *bar, unsigned v, int32_t *err, int et) {
-    epi_bar();
-    if (et == 0) {
-        __threadfence();
-        st_release(&bar->arrive[blockIdx.x], v);
-    }
-    if (blockIdx.x == 0) {
-        for (int j = et; j < (int)gridDim.x; j += kEpiThreads) {
-            const long long t0 = clock64();
-            while ((int)(ld_acquire(&bar->arrive[j]) - v) < 0) {
-                if (clock64() - t0 > kWaitLimit) {
-                    atomicCAS(err, 0, 42);
-                    break;
-                }
-                __nanosleep(32);
-            }
-        }
-        epi_bar();
-        if (et == 0) st_release(&bar->release, v);
-    }
-    if (et == 0) {
-        const long long t0 = clock64();
-        while ((int)(ld_acquire(&bar->release) - v) < 0) {
+// Cross-CTA dependencies are per tile: the CTA that finishes a tile publishes
+// the launch epoch in the tile's flag (values grow with every launch, so no
+// flag is ever reset), and whoever needs the tile polls for it.  The launch is
+// cooperative, so every producing CTA is resident while others wait.
+__device__ __forceinline__ void publish(unsigned *flag, unsigned v) {
+    __threadfence();
+    st_release(flag, v);
+}
+
+// Warp-wide: returns once flags[0..n) all reached v (lane j polls j, j+32, ...).
+__device__ void wait_flags(const unsigned *flags, int n, unsigned v, int lane, int32_t *err, int code) {
+    const long long t0 = clock64();
+    for (int j = lane; j < n; j += 32) {
+        while ((int)(ld_acquire(flags + j) - v) < 0) {
             if (clock64() - t0 > kWaitLimit) {
-                atomicCAS(err, 0, 42);
-                break;
+                atomicCAS(err, 0, code);
+                return;
             }
             __nanosleep(32);
         }
-        __threadfence();
     }
-    epi_bar();
 }
 
 // A phase's geometry: the whole phase's box sequence and this CTA's run.
@@ -412,7 +403,7 @@ __launch_bounds__(kDecThreads, 1) __global__
     float *w_s = reinterpret_cast<float *>(sm + lay.w);
     float *xchg = reinterpret_cast<float *>(sm + lay.xchg);
     volatile int *last_flag = reinterpret_cast<volatile int *>(sm + lay.xchg + 32);
-    volatile int *act_ready = reinterpret_cast<volatile int *>(sm + lay.xchg + 48);
+    volatile int *ready_s = reinterpret_cast<volatile int *>(sm + lay.ready);
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + lay.bars);
     uint64_t *empty = full + p.stages;
     uint64_t *accfull = empty + p.stages;  // [2]
@@ -438,6 +429,7 @@ __launch_bounds__(kDecThreads, 1) __global__
         inv_s[i] = p.inv[i];
         w_s[i] = p.topk_w[i];
     }
+    for (int i = tid; i < (E < P ? E : P); i += kDecThreads) ready_s[i] = 0;
     if (tid == 0) {
         for (int s = 0; s < R; ++s) {
             mbar_init(full + s, 1);
@@ -449,7 +441,6 @@ __launch_bounds__(kDecThreads, 1) __global__
         }
         mbar_init(b1ready, kEpiThreads);
         *last_flag = 0;
-        *act_ready = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == kMmaWarp) {
@@ -494,10 +485,10 @@ __launch_bounds__(kDecThreads, 1) __global__
                     bulk_g2s(st + kBoxes * kABytes, tsf + (((size_t)e * nmt + w.mt) * nkb + w.kb) * 512, nb * 512,
                              full + s);
                     if (f) {
-                        // the activation operand exists once every CTA has finished phase 1
-                        if (*act_ready == 0) {
+                        // the slot's activation operand: ready once all its gate_up tiles are done
+                        if (ready_s[w.slot] == 0) {
                             const long long t0 = clock64();
-                            while (*act_ready == 0) {
+                            while (ready_s[w.slot] == 0) {
                                 if (clock64() - t0 > kWaitLimit) {
                                     atomicCAS(p.err, 0, 31);
                                     break;
@@ -512,6 +503,17 @@ __launch_bounds__(kDecThreads, 1) __global__
                     }
                     w.advance(nb);
                 }
+            }
+        }
+    } else if (warp == kWatchWarp) {
+        // ---------------- watcher: which phase-2 slots may load their operand ----------------
+        const Phase &q = ph[1];
+        if (q.hi > q.lo) {
+            const int per_slot = q.nmt * q.nkb;
+            for (int slot = q.lo / per_slot; slot <= (q.hi - 1) / per_slot; ++slot) {
+                wait_flags(p.tflag + (size_t)slot * kTilesPerSlot, nmt1, epoch, lane, p.err, 36);
+                __syncwarp();
+                if (lane == 0) ready_s[slot] = 1;
             }
         }
     } else if (warp == kMmaWarp) {
@@ -585,20 +587,29 @@ __launch_bounds__(kDecThreads, 1) __global__
         //     Item = 8 elements; four consecutive lanes hold one 32-element block.
         {
             const int n8 = p.Hp / 8, total = p.T * n8;
-            for (int base = 0; base < total; base += kEpiThreads) {
-                const int it = base + et;
+            constexpr int kBatch = 4;  // items per thread whose loads are in flight together
+            for (int base0 = 0; base0 < total; base0 += kBatch * kEpiThreads) {
+              uint4 hv[kBatch], lv[kBatch];
+#pragma unroll
+              for (int u = 0; u < kBatch; ++u) {
+                const int it = base0 + u * kEpiThreads + et;
+                const int t = it / n8, k0 = 8 * (it - t * n8);
+                hv[u] = lv[u] = make_uint4(0, 0, 0, 0);
+                if (it < total && k0 < p.H) {
+                    hv[u] = *reinterpret_cast<const uint4 *>(p.x_hi + (size_t)t * p.H + k0);
+                    lv[u] = *reinterpret_cast<const uint4 *>(p.x_lo + (size_t)t * p.H + k0);
+                }
+              }
+#pragma unroll
+              for (int u = 0; u < kBatch; ++u) {
+                const int it = base0 + u * kEpiThreads + et;
                 const bool valid = it < total;
                 const int t = valid ? it / n8 : 0, k8 = valid ? it - t * n8 : 0;
                 const int k0 = 8 * k8;
                 float v[8];
                 float amax = 0.0f;
-                uint4 h = make_uint4(0, 0, 0, 0), l = make_uint4(0, 0, 0, 0);
-                if (valid && k0 < p.H) {
-                    h = *reinterpret_cast<const uint4 *>(p.x_hi + (size_t)t * p.H + k0);
-                    l = *reinterpret_cast<const uint4 *>(p.x_lo + (size_t)t * p.H + k0);
-                }
-                const __half2 *hh = reinterpret_cast<const __half2 *>(&h);
-                const __half2 *ll = reinterpret_cast<const __half2 *>(&l);
+                const __half2 *hh = reinterpret_cast<const __half2 *>(&hv[u]);
+                const __half2 *ll = reinterpret_cast<const __half2 *>(&lv[u]);
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const float2 a = __half22float2(hh[u]), bb = __half22float2(ll[u]);
@@ -630,6 +641,7 @@ __launch_bounds__(kDecThreads, 1) __global__
                     *reinterpret_cast<uint2 *>(dst) = make_uint2(lo4[j], hi4[j]);
                     if ((k8 & 3) == 0) sfb1[(size_t)box * 512 + n * 16 + (k0 % 128) / 32] = (uint8_t)term_scale_byte(e0, j);
                 }
+              }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(b1ready);
@@ -639,10 +651,6 @@ __launch_bounds__(kDecThreads, 1) __global__
         int seg = 0;
         for (int f = 0; f < 2; ++f) {
             const Phase &q = ph[f];
-            if (f == 1) {
-                grid_barrier(p.bar, 2u * epoch, p.err, et);
-                if (et == 0) *act_ready = 1;
-            }
             int x = q.lo;
             while (x < q.hi) {
                 const int tile = x / q.nkb;
@@ -757,26 +765,33 @@ __launch_bounds__(kDecThreads, 1) __global__
                     for (int c = 0; c < NT; c += 4)
                         if (c / 4 < m_e) p.y[(size_t)(base + c / 4) * p.H + h] = v[c] + v[c + 1] + v[c + 2] + v[c + 3] + bias;
                 }
+                // the tile is complete: publish it to the CTAs that consume it
+                __threadfence();
+                epi_bar();
+                if (et == 0) publish(p.tflag + ((size_t)f * p.S + slot) * kTilesPerSlot + mt, epoch);
             }
         }
-        grid_barrier(p.bar, 2u * epoch + 1u, p.err, et);
-        // (c) slot-order combine with the residual
-        const int H4 = p.H / 4;
-        const long long items = (long long)p.T * H4;
-        for (long long it = (long long)blockIdx.x * kEpiThreads + et; it < items; it += (long long)G * kEpiThreads) {
-            const int t = (int)(it / H4), i4 = (int)(it - (long long)t * H4);
-            double m0 = 0.0, m1 = 0.0, m2 = 0.0, m3 = 0.0;
-            for (int s = 0; s < p.k; ++s) {
-                const float4 yv = __ldcg(reinterpret_cast<const float4 *>(p.y + (size_t)inv_s[t * p.k + s] * p.H) + i4);
-                const double ws = (double)w_s[t * p.k + s];
-                m0 += ws * (double)yv.x;
-                m1 += ws * (double)yv.y;
-                m2 += ws * (double)yv.z;
-                m3 += ws * (double)yv.w;
+        // (c) slot-order combine with the residual: CTA b owns output rows
+        //     128b..128b+127 and waits only for those rows' down tiles
+        if ((int)blockIdx.x < nmt2) {
+            const int mt2 = blockIdx.x;
+            if (et < 32) {
+                for (int s0 = 0; s0 < n_active; s0 += 32) {
+                    const int ns = min(32, n_active - s0);
+                    if (lane < ns)
+                        wait_flags(p.tflag + ((size_t)p.S + s0 + lane) * kTilesPerSlot + mt2, 1, epoch, 0, p.err, 37);
+                }
             }
-            const float4 r = reinterpret_cast<const float4 *>(p.residual + (size_t)t * p.H)[i4];
-            reinterpret_cast<float4 *>(p.out + (size_t)t * p.H)[i4] =
-                make_float4(r.x + (float)m0, r.y + (float)m1, r.z + (float)m2, r.w + (float)m3);
+            epi_bar();
+            const int h = 128 * mt2 + et;
+            if (h < p.H) {
+                for (int t = 0; t < p.T; ++t) {
+                    double m = 0.0;
+                    for (int s = 0; s < p.k; ++s)
+                        m += (double)w_s[t * p.k + s] * (double)__ldcg(p.y + (size_t)inv_s[t * p.k + s] * p.H + h);
+                    p.out[(size_t)t * p.H + h] = p.residual[(size_t)t * p.H + h] + (float)m;
+                }
+            }
         }
         if (et == 0) p.bar->epoch[blockIdx.x] = epoch;
     }
@@ -866,7 +881,7 @@ size_t decode_scratch_bytes(const Dims &d, int device) {
     const int G = device >= 0 && device < 64 && caps(device).sms > 0 ? caps(device).sms : 1;
     const int S = dec_slots(d), Ip = kpad128(d.I);
     return align256((size_t)S * 16 * Ip) + align256((size_t)S * (Ip / 128) * 512) +
-           align256((size_t)G * 2 * 128 * kNMax * 4) + (size_t)2 * S * kTilesPerSlot * 4;
+           align256((size_t)G * 2 * 128 * kNMax * 4) + (size_t)2 * 2 * S * kTilesPerSlot * 4;
 }
 
 cudaError_t init_decode_scratch(const Dims &d, int device, void *scratch, cudaStream_t st) {
@@ -913,6 +928,7 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
     p.partial = reinterpret_cast<float *>(b);
     b += align256((size_t)G * 2 * 128 * kNMax * 4);
     p.cnt = reinterpret_cast<uint32_t *>(b);
+    p.tflag = reinterpret_cast<unsigned *>(p.cnt + (size_t)2 * S * kTilesPerSlot);
     p.y = y;
     p.bar = bar;
     p.err = err;
