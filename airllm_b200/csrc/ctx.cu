@@ -698,22 +698,25 @@ int amoe_forward_device(amoe_ctx *c, int32_t layer, const float *residual, int32
     }
     const Dims &d = c->d;
     StageTimer timer(c, st);
-    AMOE_CUDA(c, launch_route_impl(d, L, residual, T, c->r, c->partial, c->arrivals, st, &timer_hook, &timer));
     const int nchunk = (T + kRouteTokens - 1) / kRouteTokens;
-    c->stats.launches += nchunk > 1 ? 2 : 1;
     bool tc = use_tensor_path(c, T);
+    // decode: routing, gate_up, down and the combine in one cooperative launch
+    const bool fused_decode = c->ep_n == 1 && !tc && decode_supported(d, T, c->cfg.device);
+    if (!fused_decode) {
+        AMOE_CUDA(c, launch_route_impl(d, L, residual, T, c->r, c->partial, c->arrivals, st, &timer_hook, &timer));
+        c->stats.launches += nchunk > 1 ? 2 : 1;
+    }
     if (c->ep_n > 1) {
         timer.mark(1);
         rc = ep_experts(c, L, T, st, timer, &tc);
         if (rc) return rc;
-    } else if (!tc && nchunk > 1) {
+    } else if (!tc && nchunk > 1 && !fused_decode) {
         AMOE_CUDA(c, launch_scatter(d, T, c->r, false, nullptr, nullptr, st));
         c->stats.launches += 1;
     }
     bool fused = false;
     if (c->ep_n > 1) {
-    } else if (!tc && nchunk == 1 && decode_supported(d, T, c->cfg.device)) {
-        // decode: gate_up, down and the combine in one cooperative launch
+    } else if (fused_decode) {
         timer.mark(1);
         int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H);
         AMOE_CUDA(c, launch_decode(d, L, c->r, residual, T, c->dec_scratch, c->y, out, c->dec_bar, flag,

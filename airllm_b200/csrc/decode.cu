@@ -32,16 +32,13 @@
 // warp 9 watches the gate_up tiles this CTA's down boxes depend on.
 // Every wait is bounded (~1 s of clock): it records a code in the error flag
 // and the kernel winds down.
-#include "amoe_internal.cuh"
-
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
-#include <mutex>
+#include "tc_ptx.cuh"
 
 namespace amoe {
 
 namespace {
+
+using namespace bs;
 
 // Copies issued by one warp are serviced one after another (~0.4 us each at
 // load), so four producer warps fill the ring's stages round-robin.
@@ -58,7 +55,6 @@ constexpr int kMaxStages = 6;
 constexpr uint32_t kABytes = 128 * 128;         // unpacked A box in shared memory
 constexpr uint32_t kAPacked = 128 * 64;         // its bytes in global memory (TMA transaction size)
 constexpr uint32_t kTmemCols = 128;             // 2 accumulators + 16 scale columns per stage
-constexpr long long kWaitLimit = 2000000000LL;  // clock cycles (~1 s)
 constexpr size_t kSmemBudget = 225 * 1024;
 constexpr int kTilesPerSlot = 64;               // tile counters per slot and phase
 
@@ -71,9 +67,10 @@ __host__ __device__ constexpr uint32_t stage_bytes(int nt) {
 struct DecodeParams {
     const float *residual;
     float *out;
-    const __half *x_hi, *x_lo;  // [T][H] normalized rows
-    const int32_t *perm_pair, *offsets, *active, *inv;
-    const float *topk_w;
+    const float *gain, *router_w, *router_b;  // RMSNorm gain [H], router [E][H] and bias [E]
+    float eps;
+    RouteOut route;             // routing outputs (logits doubles as the cross-CTA exchange buffer)
+    unsigned *rflag;            // [G] launch epoch once a CTA's router dot products are stored
     const uint8_t *gu_tsf, *dn_tsf;
     const float *gu_b, *dn_b;
     uint8_t *act_q;             // [S][16][Ip] E4M3 terms of each slot's activation rows
@@ -90,7 +87,7 @@ struct DecodeParams {
 };
 
 struct DecLayout {
-    uint32_t ring, b1, sfb1, offs, act, perm, inv, w, ready, xchg, bars, tmem_slot, total;
+    uint32_t ring, b1, sfb1, offs, act, perm, inv, w, ready, rms, lg, tk, xchg, bars, tmem_slot, total;
 };
 
 __host__ __device__ inline DecLayout dec_layout(int T, int Hp, int E, int k, int stages, int nt) {
@@ -115,6 +112,13 @@ __host__ __device__ inline DecLayout dec_layout(int T, int Hp, int E, int k, int
     o += P * 4;
     L.ready = o;  // [min(E, P)] phase-2 operand of the slot complete
     o += (uint32_t)(E < (int)P ? E : (int)P) * 4;
+    o = (o + 7u) & ~7u;
+    L.rms = o;  // [4] inverse RMS per token, then [warps][4] partial sums (f64)
+    o += (uint32_t)(4 + (kDecThreads / 32) * 4) * 8;
+    L.lg = o;  // [T*E] router logits
+    o += (uint32_t)(T * E) * 4;
+    L.tk = o;  // [P] selected experts in slot order
+    o += P * 4;
     L.xchg = o;
     o += 64;  // block maxima of the activation quantization + flags
     o = (o + 7u) & ~7u;
@@ -126,213 +130,7 @@ __host__ __device__ inline DecLayout dec_layout(int T, int Hp, int E, int k, int
     return L;
 }
 
-// ---- PTX helpers -------------------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int32_t *err, int code) {
-    const long long t0 = clock64();
-    for (;;) {
-        uint32_t ok;
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-            : "=r"(ok)
-            : "r"(smem_u32(bar)), "r"(parity)
-            : "memory");
-        if (ok) return true;
-        if (clock64() - t0 > kWaitLimit) {
-            atomicCAS(err, 0, code);
-            return false;
-        }
-    }
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, int count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-    asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}" ::"r"(
-                     smem_u32(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ void tma_3d(void *dst, const CUtensorMap *tm, uint64_t *bar, int x, int y, int z) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-        "[%5];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *tm, uint64_t *bar, int x, int y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// K-major SWIZZLE_128B operand: 8-row groups 1024 B apart.
-__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-    d |= (uint64_t)1u << 16;
-    d |= (uint64_t)(1024u >> 4) << 32;
-    d |= (uint64_t)1u << 46;
-    d |= (uint64_t)2u << 61;
-    return d;
-}
-
-// Scale-factor chunk for tcgen05.cp: 32 rows of 16 B, no swizzle, 8-row core
-// matrices 128 B apart.
-__device__ __forceinline__ uint64_t desc_sf(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-    d |= (uint64_t)(128u >> 4) << 16;
-    d |= (uint64_t)(128u >> 4) << 32;
-    d |= (uint64_t)1u << 46;
-    return d;
-}
-
-__device__ __forceinline__ void sf_copy(uint32_t tmem_col, uint32_t saddr) {
-    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tmem_col), "l"(desc_sf(saddr)) : "memory");
-}
-
-// Instruction descriptor, kind::mxf8f6f4 block-scaled: A E2M1, B E4M3, both
-// K-major, E8M0 scales, M = 128, N = n; sf_id picks the byte (32-element
-// block) of the scale words.
-__device__ __forceinline__ uint32_t idesc_bs(uint32_t sf_id, int n) {
-    return (sf_id << 4) | (5u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24) |
-           (sf_id << 29);
-}
-
-__device__ __forceinline__ void umma_bs(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc, uint32_t sfa,
-                                        uint32_t sfb) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n}" ::"r"(d),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
-        : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
-
-__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void st_release(unsigned *p, unsigned v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// E4M3 with round-to-nearest, saturating to +-448 (NaN stays NaN).
-__device__ __forceinline__ uint32_t to_e4m3(float v) {
-    uint16_t r;
-    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %1;" : "=h"(r) : "f"(v));
-    return r & 0xffu;
-}
-
-__device__ __forceinline__ float from_e4m3(uint32_t b) {
-    uint32_t h;
-    const uint16_t two = (uint16_t)(b | (b << 8));
-    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(two));
-    return __half2float(__ushort_as_half((unsigned short)(h & 0xffffu)));
-}
-
-// Scale exponent of a 32-element block with largest magnitude amax: amax /
-// 2^e0 lies in [128, 256) (inside E4M3's 448); term j uses 2^(e0 - 4j).
-__device__ __forceinline__ int block_exp(float amax) {
-    const int e = (int)((__float_as_uint(amax) >> 23) & 0xffu) - 127;
-    return e - 7;
-}
-
-__device__ __forceinline__ int term_scale_byte(int e0, int j) { return max(e0 - 4 * j + 127, 1); }
-
-// Four E4M3 terms of v for block exponent e0: v ~= sum_j q_j 2^(e0 - 4j), each
-// term rounding what the previous ones left.  Scale bytes clamp at 1 (2^-126):
-// such blocks are ~2^-120 small.
-__device__ __forceinline__ uint32_t quant4(float v, int e0) {
-    uint32_t out = 0;
-    float r = v;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int eb = term_scale_byte(e0, j);
-        const float s = __uint_as_float((uint32_t)eb << 23);
-        const float inv = __uint_as_float((uint32_t)(254 - eb) << 23);
-        const uint32_t q = to_e4m3(r * inv);
-        r -= from_e4m3(q) * s;
-        out |= q << (8 * j);
-    }
-    return out;
-}
-
-// GPT-OSS clamped SwiGLU in f32 with Go's math.Min/Max NaN semantics
-// (primitives.go:144-146): NaN propagates.
-__device__ __forceinline__ float swiglu(float gate, float up) {
-    float g = isnan(gate) ? gate : fminf(gate, 7.0f);
-    float u = isnan(up) ? up : fminf(fmaxf(up, -7.0f), 7.0f);
-    return g / (1.0f + expf(-1.702f * g)) * (u + 1.0f);
-}
-
-// Cross-CTA dependencies are per tile: the CTA that finishes a tile publishes
-// the launch epoch in the tile's flag (values grow with every launch, so no
-// flag is ever reset), and whoever needs the tile polls for it.  The launch is
-// cooperative, so every producing CTA is resident while others wait.
-__device__ __forceinline__ void publish(unsigned *flag, unsigned v) {
-    __threadfence();
-    st_release(flag, v);
-}
-
-// Warp-wide: returns once flags[0..n) all reached v (lane j polls j, j+32, ...).
-__device__ void wait_flags(const unsigned *flags, int n, unsigned v, int lane, int32_t *err, int code) {
-    const long long t0 = clock64();
-    for (int j = lane; j < n; j += 32) {
-        while ((int)(ld_acquire(flags + j) - v) < 0) {
-            if (clock64() - t0 > kWaitLimit) {
-                atomicCAS(err, 0, code);
-                return;
-            }
-            __nanosleep(32);
-        }
-    }
-}
 
 // A phase's geometry: the whole phase's box sequence and this CTA's run.
 struct Phase {
@@ -420,14 +218,246 @@ __launch_bounds__(kDecThreads, 1) __global__
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_dn)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_act)) : "memory");
     }
-    for (int i = tid; i <= E; i += kDecThreads) {
-        offs_s[i] = p.offsets[i];
-        act_s[i] = p.active[i];
-    }
-    for (int i = tid; i < P; i += kDecThreads) {
-        perm_s[i] = p.perm_pair[i];
-        inv_s[i] = p.inv[i];
-        w_s[i] = p.topk_w[i];
+    // ---------------- routing, in every CTA ----------------
+    // RMSNorm (primitives.go:50-72), router logits (primitives.go:11-47), top-k and
+    // softmax over the selected logits (moe.go:12-41), stable (expert, token, slot)
+    // permutation.  The T x E router dot products are spread over the CTAs; each
+    // publishes its flag, and every CTA then reads all logits and derives the same
+    // routing.
+    {
+        constexpr int kWarps = kDecThreads / 32;
+        double *rms_s = reinterpret_cast<double *>(sm + lay.rms);
+        double *red_s = rms_s + 4;
+        float *lg_s = reinterpret_cast<float *>(sm + lay.lg);
+        int *tk_s = reinterpret_cast<int *>(sm + lay.tk);
+        const int T = p.T, H = p.H;
+        // (1) float64 sums of squares of the T residual rows (loads unrolled: in flight together)
+        constexpr int kPer = (4096 + kDecThreads - 1) / kDecThreads;  // elements per thread, H <= 4096
+        double ss[kDecodeMaxTokens];
+#pragma unroll
+        for (int t = 0; t < kDecodeMaxTokens; ++t) {
+            ss[t] = 0.0;
+            if (t < T) {
+                float xv[kPer];
+#pragma unroll
+                for (int r = 0; r < kPer; ++r) {
+                    const int i = tid + r * kDecThreads;
+                    xv[r] = i < H ? p.residual[(size_t)t * H + i] : 0.0f;
+                }
+#pragma unroll
+                for (int r = 0; r < kPer; ++r) ss[t] += (double)xv[r] * (double)xv[r];
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < kDecodeMaxTokens; ++t) {
+            double v = ss[t];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) red_s[warp * 4 + t] = v;
+        }
+        __syncthreads();
+        if (tid < T) {
+            double sum = 0.0;
+            for (int w = 0; w < kWarps; ++w) sum += red_s[w * 4 + tid];
+            rms_s[tid] = 1.0 / sqrt(sum / (double)H + (double)p.eps);
+        }
+        __syncthreads();
+        // (2) router dot products, one per CTA (dot d on CTA d mod G):
+        //     logit = f32(sum f64(x_n) f64(W)) + b, partials added in a fixed order
+        const int ndots = T * E;
+        for (int dd = blockIdx.x; dd < ndots; dd += G) {
+            const int t = dd / E, e = dd - t * E;
+            const float *xr = p.residual + (size_t)t * H;
+            const float *wr = p.router_w + (size_t)e * H;
+            const double inv = rms_s[t];
+            float xv[kPer], gv[kPer], wv[kPer];
+#pragma unroll
+            for (int r = 0; r < kPer; ++r) {
+                const int i = tid + r * kDecThreads;
+                const bool in = i < H;
+                xv[r] = in ? xr[i] : 0.0f;
+                gv[r] = in ? p.gain[i] : 0.0f;
+                wv[r] = in ? wr[i] : 0.0f;
+            }
+            double acc = 0.0;
+#pragma unroll
+            for (int r = 0; r < kPer; ++r) {
+                const float xn = (float)((double)xv[r] * inv * (double)gv[r]);
+                acc = fma((double)xn, (double)wv[r], acc);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            __syncthreads();  // red_s reuse
+            if (lane == 0) red_s[warp] = acc;
+            __syncthreads();
+            if (tid == 0) {
+                double sum = 0.0;
+                for (int w = 0; w < kWarps; ++w) sum += red_s[w];
+                p.route.logits[dd] = (float)sum + p.router_b[e];
+            }
+        }
+        __syncthreads();
+        if (tid == 0 && (int)blockIdx.x < min(G, ndots)) publish(p.rflag + blockIdx.x, epoch);
+        // (2b) the phase-1 operand, while other CTAs finish their dot products: every
+        //      token's normalized row as four E4M3 terms.  Item = 8 elements; four
+        //      consecutive lanes hold one 32-element block.
+        {
+            const int n8 = p.Hp / 8, total = p.T * n8;
+            constexpr int kBatch = 4;  // items per thread whose loads are in flight together
+            for (int base0 = 0; base0 < total; base0 += kBatch * kDecThreads) {
+              float4 xv[kBatch][2], gv[kBatch][2];
+#pragma unroll
+              for (int u = 0; u < kBatch; ++u) {
+                const int it = base0 + u * kDecThreads + tid;
+                const int t = it / n8, k0 = 8 * (it - t * n8);
+                xv[u][0] = xv[u][1] = gv[u][0] = gv[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (it < total && k0 < p.H) {
+                    xv[u][0] = *reinterpret_cast<const float4 *>(p.residual + (size_t)t * p.H + k0);
+                    xv[u][1] = *reinterpret_cast<const float4 *>(p.residual + (size_t)t * p.H + k0 + 4);
+                    gv[u][0] = *reinterpret_cast<const float4 *>(p.gain + k0);
+                    gv[u][1] = *reinterpret_cast<const float4 *>(p.gain + k0 + 4);
+                }
+              }
+#pragma unroll
+              for (int u = 0; u < kBatch; ++u) {
+                const int it = base0 + u * kDecThreads + tid;
+                const bool valid = it < total;
+                const int t = valid ? it / n8 : 0, k8 = valid ? it - t * n8 : 0;
+                const int k0 = 8 * k8;
+                // normalized row, rounded to f32 as RMSNorm stores it (primitives.go:68-70)
+                const double inv = rms_s[t];
+                const float xs[8] = {xv[u][0].x, xv[u][0].y, xv[u][0].z, xv[u][0].w,
+                                     xv[u][1].x, xv[u][1].y, xv[u][1].z, xv[u][1].w};
+                const float gs[8] = {gv[u][0].x, gv[u][0].y, gv[u][0].z, gv[u][0].w,
+                                     gv[u][1].x, gv[u][1].y, gv[u][1].z, gv[u][1].w};
+                float v[8];
+                float amax = 0.0f;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    v[q] = (float)((double)xs[q] * inv * (double)gs[q]);
+                    amax = fmaxf(amax, fabsf(v[q]));
+                }
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+                if (!valid) continue;
+                const int e0 = block_exp(amax);
+                uint32_t lo4[4] = {0, 0, 0, 0}, hi4[4] = {0, 0, 0, 0};  // [term]: elements 0-3, 4-7
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const uint32_t q = quant4(v[i], e0);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint32_t byte = ((q >> (8 * j)) & 0xffu) << (8 * (i & 3));
+                        if (i < 4) lo4[j] |= byte;
+                        else hi4[j] |= byte;
+                    }
+                }
+                const int box = k0 / 128, chunk = (k0 % 128) / 16, half = (k0 % 16) / 8;
+                uint8_t *bx = b1 + (size_t)box * kBBox;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int n = 4 * t + j;  // B row: token t, term j (SWIZZLE_128B: chunk ^ row % 8)
+                    uint8_t *dst = bx + (n >> 3) * 1024 + (n & 7) * 128 + ((chunk ^ (n & 7)) << 4) + 8 * half;
+                    *reinterpret_cast<uint2 *>(dst) = make_uint2(lo4[j], hi4[j]);
+                    if ((k8 & 3) == 0) sfb1[(size_t)box * 512 + n * 16 + (k0 % 128) / 32] = (uint8_t)term_scale_byte(e0, j);
+                }
+              }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        }
+        const int dot_ctas = min(G, ndots);
+        // (3) every CTA's logits
+        if (warp == 0) wait_flags(p.rflag, dot_ctas, epoch, lane, p.err, 38);
+        __syncthreads();
+        for (int i = tid; i < ndots; i += kDecThreads) lg_s[i] = __ldcg(p.route.logits + i);
+        __syncthreads();
+        // (4) top-k: the rank of every (token, expert) in the stable descending order
+        //     (moe.go:20-27) in parallel; ranks below k are the selected slots.  Then
+        //     the softmax over the selected logits per token (moe.go:29-39).
+        for (int te = tid; te < ndots; te += kDecThreads) {
+            const int t = te / E, e = te - t * E;
+            const float v = lg_s[te];
+            int rank = 0;
+            for (int f2 = 0; f2 < E; ++f2) rank += topk_better(lg_s[t * E + f2], f2, v, e);
+            if (rank < p.k) tk_s[t * p.k + rank] = e;
+        }
+        __syncthreads();
+        if (tid < T) {
+            const int t = tid;
+            const double maxv = (double)lg_s[t * E + tk_s[t * p.k]];
+            double den = 0.0;
+            for (int sl = 0; sl < p.k; ++sl) den += exp((double)lg_s[t * E + tk_s[t * p.k + sl]] - maxv);
+            for (int sl = 0; sl < p.k; ++sl) {
+                const float wf = (float)exp((double)lg_s[t * E + tk_s[t * p.k + sl]] - maxv);
+                w_s[t * p.k + sl] = (float)((double)wf / den);
+            }
+        }
+        __syncthreads();
+        // (5) counts, offsets, active experts and the stable permutation
+        for (int e = tid; e <= E; e += kDecThreads) offs_s[e] = 0;
+        __syncthreads();
+        for (int q = tid; q < P; q += kDecThreads) atomicAdd(&offs_s[tk_s[q]], 1);
+        __syncthreads();
+        if (warp == 0) {
+            // warp scan over experts (lane owns experts 8 lane .. 8 lane + 7; E <= 256)
+            int c[8], a[8];
+            int cs = 0, as = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int e = 8 * lane + j;
+                c[j] = e < E ? offs_s[e] : 0;
+                a[j] = c[j] > 0;
+                cs += c[j];
+                as += a[j];
+            }
+            int cx = cs, ax = as;  // inclusive warp prefix sums
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int cu = __shfl_up_sync(0xffffffffu, cx, o), au = __shfl_up_sync(0xffffffffu, ax, o);
+                if (lane >= o) {
+                    cx += cu;
+                    ax += au;
+                }
+            }
+            int co = cx - cs, ao = ax - as;
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int e = 8 * lane + j;
+                if (e < E) {
+                    offs_s[e] = co;
+                    if (a[j]) act_s[ao] = e;
+                }
+                co += c[j];
+                ao += a[j];
+            }
+            if (lane == 31) {
+                offs_s[E] = cx;
+                act_s[E] = ax;
+            }
+        }
+        __syncthreads();
+        for (int q = tid; q < P; q += kDecThreads) {  // pairs in (token, slot) order land stably
+            const int e = tk_s[q];
+            int pos = offs_s[e];
+            for (int r = 0; r < q; ++r) pos += tk_s[r] == e;
+            perm_s[pos] = q;
+            inv_s[q] = pos;
+        }
+        __syncthreads();
+        if (blockIdx.x == 0) {  // the routing the C ABI reports
+            for (int q = tid; q < P; q += kDecThreads) {
+                p.route.topk_idx[q] = tk_s[q];
+                p.route.topk_w[q] = w_s[q];
+                p.route.perm_pair[q] = perm_s[q];
+                p.route.inv[q] = inv_s[q];
+            }
+            for (int e = tid; e <= E; e += kDecThreads) {
+                p.route.offsets[e] = offs_s[e];
+                p.route.active[e] = act_s[e];
+                if (e < E) p.route.counts[e] = offs_s[e + 1] - offs_s[e];
+            }
+        }
     }
     for (int i = tid; i < (E < P ? E : P); i += kDecThreads) ready_s[i] = 0;
     if (tid == 0) {
@@ -439,7 +469,6 @@ __launch_bounds__(kDecThreads, 1) __global__
             mbar_init(accfull + b, 1);
             mbar_init(accempty + b, kEpiThreads);
         }
-        mbar_init(b1ready, kEpiThreads);
         *last_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -527,7 +556,7 @@ __launch_bounds__(kDecThreads, 1) __global__
         for (int kk = 0; kk < 4; ++kk) idesc[kk] = idesc_bs(kk, NT);
         const uint32_t ring_a = smem_u32(ring), b1_a = smem_u32(b1), sfb1_a = smem_u32(sfb1);
         int i = 0, seg = 0;
-        bool ok = mbar_wait(b1ready, 0, p.err, 32);
+        bool ok = true;  // the phase-1 operand was built before the roles split
         for (int f = 0; f < 2 && ok; ++f) {
             Walker w(ph[f]);
             while (w.more() && ok) {
@@ -583,69 +612,6 @@ __launch_bounds__(kDecThreads, 1) __global__
         const int et = tid - kEpiWarp0 * 32;  // 0..127
         const int quad = warp & 3;         // TMEM lane quadrant
         const int row = quad * 32 + lane;  // row of the 128-row tile this thread owns
-        // (a) phase-1 operand: every token's normalized row as four E4M3 terms.
-        //     Item = 8 elements; four consecutive lanes hold one 32-element block.
-        {
-            const int n8 = p.Hp / 8, total = p.T * n8;
-            constexpr int kBatch = 4;  // items per thread whose loads are in flight together
-            for (int base0 = 0; base0 < total; base0 += kBatch * kEpiThreads) {
-              uint4 hv[kBatch], lv[kBatch];
-#pragma unroll
-              for (int u = 0; u < kBatch; ++u) {
-                const int it = base0 + u * kEpiThreads + et;
-                const int t = it / n8, k0 = 8 * (it - t * n8);
-                hv[u] = lv[u] = make_uint4(0, 0, 0, 0);
-                if (it < total && k0 < p.H) {
-                    hv[u] = *reinterpret_cast<const uint4 *>(p.x_hi + (size_t)t * p.H + k0);
-                    lv[u] = *reinterpret_cast<const uint4 *>(p.x_lo + (size_t)t * p.H + k0);
-                }
-              }
-#pragma unroll
-              for (int u = 0; u < kBatch; ++u) {
-                const int it = base0 + u * kEpiThreads + et;
-                const bool valid = it < total;
-                const int t = valid ? it / n8 : 0, k8 = valid ? it - t * n8 : 0;
-                const int k0 = 8 * k8;
-                float v[8];
-                float amax = 0.0f;
-                const __half2 *hh = reinterpret_cast<const __half2 *>(&hv[u]);
-                const __half2 *ll = reinterpret_cast<const __half2 *>(&lv[u]);
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const float2 a = __half22float2(hh[u]), bb = __half22float2(ll[u]);
-                    v[2 * u] = a.x + bb.x;
-                    v[2 * u + 1] = a.y + bb.y;
-                    amax = fmaxf(amax, fmaxf(fabsf(v[2 * u]), fabsf(v[2 * u + 1])));
-                }
-                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-                if (!valid) continue;
-                const int e0 = block_exp(amax);
-                uint32_t lo4[4] = {0, 0, 0, 0}, hi4[4] = {0, 0, 0, 0};  // [term]: elements 0-3, 4-7
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const uint32_t q = quant4(v[i], e0);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint32_t byte = ((q >> (8 * j)) & 0xffu) << (8 * (i & 3));
-                        if (i < 4) lo4[j] |= byte;
-                        else hi4[j] |= byte;
-                    }
-                }
-                const int box = k0 / 128, chunk = (k0 % 128) / 16, half = (k0 % 16) / 8;
-                uint8_t *bx = b1 + (size_t)box * kBBox;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int n = 4 * t + j;  // B row: token t, term j (SWIZZLE_128B: chunk ^ row % 8)
-                    uint8_t *dst = bx + (n >> 3) * 1024 + (n & 7) * 128 + ((chunk ^ (n & 7)) << 4) + 8 * half;
-                    *reinterpret_cast<uint2 *>(dst) = make_uint2(lo4[j], hi4[j]);
-                    if ((k8 & 3) == 0) sfb1[(size_t)box * 512 + n * 16 + (k0 % 128) / 32] = (uint8_t)term_scale_byte(e0, j);
-                }
-              }
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(b1ready);
-        }
         // (b) the CTA's tile segments, phase 1 then phase 2
         float *part = p.partial + (size_t)blockIdx.x * 2 * 128 * kNMax;
         int seg = 0;
@@ -803,46 +769,6 @@ __launch_bounds__(kDecThreads, 1) __global__
 }
 
 // ---- host side -------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-std::once_flag g_encode_once;
-
-bool get_encode() {
-    std::call_once(g_encode_once, []() {
-        void *fn = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    });
-    return g_encode != nullptr;
-}
-
-// Box-tiled E2M1 plane: rows of 128 packed 4-bit elements (64 B), 128-row boxes.
-cudaError_t map_boxes(CUtensorMap *tm, void *base, uint64_t rows) {
-    cuuint64_t dims[2] = {128, rows};
-    cuuint64_t strides[1] = {64};
-    cuuint32_t box[2] = {128, 128};
-    cuuint32_t es[2] = {1, 1};
-    CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 2, base, dims, strides, box, es,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
-}
-
-// 3-D map over [z][y][x]: x packed 4-bit (fp4) or bytes, boxes 128 x box_y x 1,
-// SWIZZLE_128B, zero fill out of bounds.
-cudaError_t map3d(CUtensorMap *tm, void *base, bool fp4, uint64_t x, uint64_t y, uint64_t z, uint32_t box_y) {
-    const uint64_t row_bytes = fp4 ? x / 2 : x;
-    cuuint64_t dims[3] = {x, y, z};
-    cuuint64_t strides[2] = {row_bytes, row_bytes * y};
-    cuuint32_t box[3] = {128, box_y, 1};
-    cuuint32_t es[3] = {1, 1, 1};
-    CUresult r = g_encode(tm, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base,
-                          dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
-}
-
 struct DecodeCaps {
     int sms = 0;
     bool coop = false;
@@ -881,7 +807,7 @@ size_t decode_scratch_bytes(const Dims &d, int device) {
     const int G = device >= 0 && device < 64 && caps(device).sms > 0 ? caps(device).sms : 1;
     const int S = dec_slots(d), Ip = kpad128(d.I);
     return align256((size_t)S * 16 * Ip) + align256((size_t)S * (Ip / 128) * 512) +
-           align256((size_t)G * 2 * 128 * kNMax * 4) + (size_t)2 * 2 * S * kTilesPerSlot * 4;
+           align256((size_t)G * 2 * 128 * kNMax * 4) + (size_t)2 * 2 * S * kTilesPerSlot * 4 + (size_t)G * 4;
 }
 
 cudaError_t init_decode_scratch(const Dims &d, int device, void *scratch, cudaStream_t st) {
@@ -910,13 +836,11 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
     DecodeParams p{};
     p.residual = residual;
     p.out = out;
-    p.x_hi = r.x_hi;
-    p.x_lo = r.x_lo;
-    p.perm_pair = r.perm_pair;
-    p.offsets = r.offsets;
-    p.active = r.active;
-    p.inv = r.inv;
-    p.topk_w = r.topk_w;
+    p.gain = L.norm_gain;
+    p.router_w = L.router_w;
+    p.router_b = L.router_b;
+    p.eps = d.eps;
+    p.route = r;
     p.gu_tsf = L.gu_tsf;
     p.dn_tsf = L.dn_tsf;
     p.gu_b = L.gu_b;
@@ -929,6 +853,7 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
     b += align256((size_t)G * 2 * 128 * kNMax * 4);
     p.cnt = reinterpret_cast<uint32_t *>(b);
     p.tflag = reinterpret_cast<unsigned *>(p.cnt + (size_t)2 * S * kTilesPerSlot);
+    p.rflag = p.tflag + (size_t)2 * S * kTilesPerSlot;
     p.y = y;
     p.bar = bar;
     p.err = err;

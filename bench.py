@@ -172,11 +172,13 @@ def algorithmic(config: int, T: int, layer, idx, stage: str):
         flops = 2.0 * pairs * 2 * I * H
         bytes_ = active * (2 * I * H // 2 + 2 * I * H // 32 + 2 * I * 4) + T * H * 4 + pairs * I * 4
     elif stage == "decode_experts":
-        # fused gate_up + down + combine: both weight sets of the selected experts and
-        # their biases, the fp16 hi/lo input rows, the residual in and the output out
-        # (act and y stay in L2 between the phases)
+        # fused routing + gate_up + down + combine: both weight sets of the selected
+        # experts and their biases, the residual in and the output out (act and y stay
+        # in L2 between the phases)
+        # (the fused kernel also routes: router weights, bias and the RMSNorm gain)
         flops = 2.0 * pairs * 3 * I * H
-        bytes_ = active * (3 * I * H // 2 + 3 * I * H // 32 + 2 * I * 4 + H * 4) + T * H * 4 + 2 * T * H * 4
+        bytes_ = (active * (3 * I * H // 2 + 3 * I * H // 32 + 2 * I * 4 + H * 4) + 2 * T * H * 4
+                  + E * H * 4 + E * 4 + H * 4)
     else:  # down
         flops = 2.0 * pairs * H * I
         bytes_ = active * (H * I // 2 + H * I // 32 + H * 4) + pairs * I * 4 + pairs * H * 4
@@ -475,7 +477,7 @@ def main():
     pairs_per_expert = T * layer["top_k"] / layer["experts"]
     kernel_name = {1: "gemv_kernel (mma.sync MXFP4)", 2: "tc_gemm (tcgen05)"}[st["last_path"] or 1]
     if dom == "decode_experts":
-        kernel_name = "decode_kernel (cooperative: gate_up + down + combine, mma.sync MXFP4)"
+        kernel_name = "decode_kernel (one cooperative launch: routing + gate_up + down + combine, tcgen05 mxf8f6f4 block-scaled)"
     traffic = None
     try:
         traffic = json.load(open(TRAFFIC_FILE)).get(f"{dom}:{cfg}")
