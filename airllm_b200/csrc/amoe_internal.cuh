@@ -139,6 +139,8 @@ size_t route_partial_elems(int max_tokens, int H, int E);
 cudaError_t launch_repack(const uint8_t *gguf, int E, int R, int K, bool pair_rows,
                           uint8_t *q, uint8_t *s, cudaStream_t st);
 
+struct EpReturn;  // expert-parallel down epilogue (below)
+
 // Expert GEMV (decode) ---------------------------------------------------------
 // Expert-sorted rows the GEMV stages work on.
 struct GemvRows {
@@ -148,6 +150,8 @@ struct GemvRows {
     const int32_t *active;      // [E] experts with rows, then their count at [E]
     const int32_t *y_rows;      // down output row per position (NULL: the position)
     int max_active;             // grid bound on the active list
+    const int32_t *gate = nullptr;  // if set, the launch does nothing unless *gate == gate_want
+    int gate_want = 0;
 };
 // Fused decode expert stage (decode.cu): gate_up + SwiGLU, down, combine in one
 // cooperative launch for T <= kDecodeMaxTokens.
@@ -171,7 +175,7 @@ cudaError_t launch_gemv_gate_up(const Dims &d, const LayerDev &L, const GemvRows
                                 __half *act_hi, __half *act_lo, int32_t *err, cudaStream_t st);
 cudaError_t launch_gemv_down(const Dims &d, const LayerDev &L, const GemvRows &rows, int T,
                              const __half *act_hi, const __half *act_lo, float *y, int32_t *err,
-                             cudaStream_t st);
+                             cudaStream_t st, const EpReturn *ret = nullptr);
 
 // tcgen05 grouped GEMM (prefill) -------------------------------------------------
 size_t tc_scratch_bytes(int max_pairs, int H, int I);
@@ -183,11 +187,12 @@ cudaError_t launch_tc_forward(const Dims &d, const LayerDev &L, const RouteOut &
                               int *launches);
 // The two grouped GEMMs alone, on rows that are already expert-sorted:
 // gate_up from (b_hi, b_lo) [rows_cap][H] into act [rows_cap][I], then down into
-// y[y_rows ? y_rows[pos] : pos][H].
+// y[y_rows ? y_rows[pos] : pos][H] (with ret: the source rank's y, see EpReturn).
 cudaError_t launch_tc_experts(const Dims &d, const LayerDev &L, const int32_t *offsets, const __half *b_hi,
                               const __half *b_lo, int rows_cap, __half *act_hi, __half *act_lo, float *y,
                               const int32_t *y_rows, int32_t *err, cudaStream_t st, StageHook hook,
-                              void *hook_arg, int *launches);
+                              void *hook_arg, int *launches, const EpReturn *ret = nullptr,
+                              const int32_t *gate = nullptr, int gate_want = 0);
 // Per-expert exponent bias from a tiled scale plane (upload time).
 cudaError_t launch_cexp(const uint8_t *s_plane, size_t bytes_per_expert, int E, int32_t *out,
                         cudaStream_t st);
@@ -201,36 +206,94 @@ cudaError_t launch_combine(const Dims &d, const float *residual, const RouteOut 
                            const float *y, int T, float *out, cudaStream_t st);
 
 // Expert parallelism --------------------------------------------------------------
-struct EpPlan {
-    int N = 0, E_loc = 0, R = 0;                         // R: rows this rank receives
-    std::vector<int> send_off, send_rows;                 // [N] local expert-sorted rows per destination
-    std::vector<int> recv_off, recv_rows;                 // [N] received rows per source (source-major)
-    std::vector<int> offsets_loc;                         // [E_loc+1] expert-major row ranges
-    std::vector<int> seg;                                 // [N*E_loc][3] (source row, expert-major row, length)
+// Rank r of N owns experts [r*El, (r+1)*El).  Every rank exports one device
+// window to its peers (CUDA IPC, mapped over NVLink); all data moves as stores
+// into the receiver's window, and per-source epoch flags order them:
+//   1. count kernel: this rank's per-expert pair counts go into row `me` of every
+//      rank's count table; once all N rows are in, each rank derives the whole
+//      exchange layout (where its rows land, its expert-major row ranges, where
+//      each received row returns to) on the device;
+//   2. dispatch kernel: each routed row (fp16 hi/lo of the normalized token) is
+//      stored straight into the owner's receive buffer, expert-major;
+//   3. the expert GEMMs run on the receive buffer; the down epilogue stores each
+//      output row into its source rank's window at the row's local sorted
+//      position, where the source's combine reads it.
+// No host synchronisation and no collective library on the data path; NCCL
+// only exchanges the IPC handles when the context is created.
+constexpr int kMaxEpRanks = 8;
+constexpr int kEpRowShift = 28;  // y_rows entry: (source rank << 28) | row in that rank's y
+constexpr uint32_t kEpRowMask = (1u << kEpRowShift) - 1;
+enum { kEpFlagCount = 0, kEpFlagDispatch = 1, kEpFlagReturn = 2 };
+
+// Byte offsets inside each rank's window (identical on every rank).
+struct EpWindow {
+    size_t flags;             // int32 [3][kMaxEpRanks]: count / dispatch / return flag per source rank
+    size_t table;             // int32 [N][E]: pairs source s routes to global expert e
+    size_t recv_hi, recv_lo;  // fp16 [r_cap][H]: rows for this rank's experts, expert-major
+    size_t y;                 // f32 [p_cap][H]: outputs for this rank's pairs, at their sorted position
+    size_t bytes;
 };
-// Host-only planning of one exchange.  local_offsets [N*E_loc+1]: this rank's
-// expert-sorted pair ranges; recv_counts [N][E_loc]: pairs each source routes to
-// this rank's experts.  Returns 0, or -1 on inconsistent input.
-int ep_plan(int N, int E_loc, int rank, const int32_t *local_offsets, const int32_t *recv_counts, EpPlan *p);
+EpWindow ep_window(int N, int E, int H, int p_cap, int r_cap);
+
+// Device scratch of the exchange (local to each rank).
+struct EpMeta {
+    int32_t *send_base;    // [E] receive row of this rank's first pair of expert e (in e's owner)
+    int32_t *offsets_loc;  // [El+1] expert-major row ranges of this rank's experts
+    int32_t *active_loc;   // [El+1] local experts with rows, then their count at [El]
+    int32_t *seg_start;    // [El][N] first expert-major row of source s's rows for local expert el
+    int32_t *src_pos;      // [El][N] sorted position of those rows in source s
+    int32_t *y_rows;       // [r_cap] return target of each received row: (source << 28) | position
+    int32_t *status;       // [1] 1 while this exchange is intact, 0 after a failed wait
+    int32_t *mode;         // [1] expert path of this exchange: 1 tcgen05 GEMM, 0 GEMV
+    unsigned *arrive;      // [2] CTA arrival counters (dispatch kernel, down GEMM)
+    uint8_t **win;         // [kMaxEpRanks] every rank's window as mapped here
+    float **ret_y;         // [kMaxEpRanks] every rank's y (inside its window)
+    int32_t **ret_flag;    // [kMaxEpRanks] this rank's return flag inside every rank's window
+};
+
+struct EpArgs {
+    int N, me, E, El, H, k, r_cap, p_cap, epoch;
+    int path;               // 1 GEMV, 2 tcgen05, 0 auto: tcgen05 once the group has >= 32 pairs per expert
+    long long limit_ns;  // bounded waits
+    EpWindow w;
+    EpMeta m;
+    const int32_t *counts, *offsets, *topk_idx, *perm_pair;  // this rank's routing
+    const __half *x_hi, *x_lo;                                // its normalized rows, by token
+    int32_t *err;
+};
+
+// Down-GEMM epilogue of an expert-parallel step: output row y_rows[pos] goes to
+// ret_y[rank] at its position; the last CTA to finish publishes `epoch` in
+// every source's return flag (only while *status is 1).
+struct EpReturn {
+    float *const *y = nullptr;
+    int32_t *const *flag = nullptr;
+    unsigned *arrive = nullptr;
+    const int32_t *status = nullptr;
+    int n = 0, epoch = 0;
+};
+
+// Layout of one exchange from the count table (host restatement of the count
+// kernel's arithmetic, for tests): returns 0, or -1 on negative counts.
+int ep_layout(int N, int El, int me, const int32_t *table, int32_t *send_base, int32_t *offsets_loc,
+              int32_t *seg_start, int32_t *src_pos);
+
+cudaError_t launch_ep_counts(const EpArgs &a, cudaStream_t st);
+cudaError_t launch_ep_dispatch(const EpArgs &a, int grid, cudaStream_t st);
+// Waits (bounded) for flags[0..n) >= epoch; on timeout records `code`, clears
+// *status and, when offsets_loc is set, empties the expert ranges.
+cudaError_t launch_ep_wait(const EpArgs &a, int which, int code, cudaStream_t st);
 
 struct NcclApi {
     ncclResult_t (*ncclGetUniqueId)(ncclUniqueId *);
     ncclResult_t (*ncclCommInitRank)(ncclComm_t *, int, ncclUniqueId, int);
     ncclResult_t (*ncclCommDestroy)(ncclComm_t);
-    ncclResult_t (*ncclCommAbort)(ncclComm_t);
-    ncclResult_t (*ncclGroupStart)();
-    ncclResult_t (*ncclGroupEnd)();
-    ncclResult_t (*ncclSend)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
-    ncclResult_t (*ncclRecv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+    ncclResult_t (*ncclAllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
     const char *(*ncclGetErrorString)(ncclResult_t);
-    ncclResult_t (*ncclCommGetAsyncError)(ncclComm_t, ncclResult_t *);
 };
 extern NcclApi g_nccl;
 // Resolves NCCL from libnccl.so.2 once; false (with a reason) if unavailable.
 bool nccl_load(std::string *err);
-cudaError_t launch_ep_reorder(const int32_t *seg_dev, int nseg, int H, const __half *src_hi, const __half *src_lo,
-                              __half *dst_hi, __half *dst_lo, int32_t *ret_map, cudaStream_t st);
-cudaError_t launch_ep_active(const int32_t *offsets, int E_loc, int32_t *active, cudaStream_t st);
 
 // Sets the message amoe_last_error(NULL) returns on the calling thread.
 void set_thread_error(const std::string &msg);
@@ -273,6 +336,44 @@ __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
     uint32_t r;
     asm("{\n .reg .b8 t;\n cvt.u8.u32 t, %1;\n cvt.rn.f16x2.e2m1x2 %0, t;\n}" : "=r"(r) : "r"(byte));
     return r;
+}
+
+// Expert-parallel epilogue helpers ------------------------------------------------
+__device__ __forceinline__ void st_release_sys(int32_t *p, int32_t v) {
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int32_t ld_acquire_sys(const int32_t *p) {
+    int32_t v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Output row base for down-GEMM position `pos`: the local y (row y_rows[pos] or
+// pos), or, expert-parallel, the source rank's y at the packed row.
+__device__ __forceinline__ float *ep_out_row(float *y, const int32_t *y_rows, const EpReturn &ret, int pos,
+                                             int R) {
+    if (!y_rows) return y + (size_t)pos * R;
+    const uint32_t v = (uint32_t)y_rows[pos];
+    if (ret.n == 0) return y + (size_t)v * R;
+    return ret.y[v >> kEpRowShift] + (size_t)(v & kEpRowMask) * R;
+}
+
+// Called by every thread of every CTA of an expert-parallel down GEMM once its
+// last store is issued: the CTA's stores to peer memory are fenced at system
+// scope, and the last CTA to arrive (the counter wraps to 0 for the next
+// launch) publishes the epoch in every source rank's return flag.
+__device__ __forceinline__ void ep_return_done(const EpReturn &ret) {
+    if (ret.n == 0) return;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+        if (atomicInc(ret.arrive, total - 1) == total - 1) {
+            __threadfence_system();
+            if (*reinterpret_cast<const volatile int32_t *>(ret.status) == 1)
+                for (int q = 0; q < ret.n; ++q) st_release_sys(ret.flag[q], ret.epoch);
+        }
+    }
 }
 
 }  // namespace amoe

@@ -11,6 +11,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -129,14 +130,16 @@ struct amoe_ctx {
 
     // expert parallelism (ep_size > 1)
     int ep_n = 1, ep_rank = 0, e_loc = 0;
-    ncclComm_t comm = nullptr;
-    size_t r_max = 0;                          // rows this rank can receive
-    __half *recv_hi = nullptr, *recv_lo = nullptr, *ex_hi = nullptr, *ex_lo = nullptr;
-    float *y_send = nullptr;
-    int32_t *ret_map = nullptr, *seg_dev = nullptr, *offsets_loc = nullptr, *active_loc = nullptr,
-            *recv_counts = nullptr;
-    int32_t *h_stage = nullptr;                // pinned: offsets, recv counts, segments
-    EpPlan plan;
+    ncclComm_t comm = nullptr;                 // setup only (IPC handle exchange)
+    size_t r_max = 0;                          // rows this rank can receive (every source's pairs)
+    uint8_t *ep_win = nullptr;                 // this rank's exported window
+    std::vector<uint8_t *> ep_peer;            // every rank's window as mapped here (self: ep_win)
+    EpWindow ep_w{};
+    EpMeta ep_m{};
+    int ep_epoch = 0;                          // forwards so far (the exchange's flag value)
+    bool ep_broken = false;                    // a wait failed: the group is out of step
+    long long ep_wait_ns = 0;                  // bound on each exchange wait
+    int sms = 0;
 
     // diagnostics
     bool profiling = false;
@@ -187,7 +190,10 @@ std::string validate(const amoe_config *c) {
     if (c->ep_size < 1 || c->ep_rank < 0 || c->ep_rank >= c->ep_size)
         return "ep_rank must be in [0, ep_size)";
     if (c->ep_size > 1) {
+        if (c->ep_size > kMaxEpRanks) return "ep_size must be at most 8 (the GPUs of one box)";
         if (c->experts % c->ep_size) return "experts must divide evenly over ep_size";
+        if ((long long)c->max_tokens * c->top_k * c->ep_size >= (1LL << kEpRowShift))
+            return "max_tokens * top_k * ep_size must stay below 2^28";
         if (!c->nccl_id) return "nccl_id must be set when ep_size > 1";
         if (c->stream_slots) return "expert parallelism keeps every layer resident (stream_slots 0)";
     }
@@ -235,16 +241,17 @@ int alloc_scratch(amoe_ctx *c) {
         {(void **)&c->io_out, T * d.H * 4},
         {(void **)&c->io_idx, P * 4},
         {(void **)&c->io_w, P * 4},
-        {(void **)&c->recv_hi, R * d.H * 2},
-        {(void **)&c->recv_lo, R * d.H * 2},
-        {(void **)&c->ex_hi, R * d.H * 2},
-        {(void **)&c->ex_lo, R * d.H * 2},
-        {(void **)&c->y_send, R * d.H * 4},
-        {(void **)&c->ret_map, R * 4},
-        {(void **)&c->seg_dev, R ? nseg * 3 * 4 : 0},
-        {(void **)&c->offsets_loc, R ? (size_t)(c->e_loc + 1) * 4 : 0},
-        {(void **)&c->active_loc, R ? (size_t)(c->e_loc + 1) * 4 : 0},
-        {(void **)&c->recv_counts, R ? nseg * 4 : 0},
+        {(void **)&c->ep_m.send_base, R ? (size_t)d.E * 4 : 0},
+        {(void **)&c->ep_m.offsets_loc, R ? (size_t)(c->e_loc + 1) * 4 : 0},
+        {(void **)&c->ep_m.active_loc, R ? (size_t)(c->e_loc + 1) * 4 : 0},
+        {(void **)&c->ep_m.seg_start, R ? nseg * 4 : 0},
+        {(void **)&c->ep_m.src_pos, R ? nseg * 4 : 0},
+        {(void **)&c->ep_m.y_rows, R * 4},
+        {(void **)&c->ep_m.status, R ? size_t(16) : 0},
+        {(void **)&c->ep_m.arrive, R ? size_t(16) : 0},
+        {(void **)&c->ep_m.win, R ? size_t(kMaxEpRanks * 8) : 0},
+        {(void **)&c->ep_m.ret_y, R ? size_t(kMaxEpRanks * 8) : 0},
+        {(void **)&c->ep_m.ret_flag, R ? size_t(kMaxEpRanks * 8) : 0},
     };
     std::vector<size_t> at(parts.size());
     for (size_t i = 0; i < parts.size(); ++i) {
@@ -259,8 +266,11 @@ int alloc_scratch(amoe_ctx *c) {
     AMOE_CUDA(c, init_decode_scratch(d, c->cfg.device, c->dec_scratch, nullptr));
     AMOE_CUDA(c, cudaDeviceSynchronize());
     AMOE_CUDA(c, cudaMemset(tc_error_flag(c->tc_scratch, (int)P, d.H), 0, sizeof(int32_t)));
-    // pinned staging: offsets [E+1], receive counts [nseg], segments [3*nseg], local offsets [E_loc+1]
-    if (R) AMOE_CUDA(c, cudaHostAlloc(&c->h_stage, ((size_t)d.E + 1 + nseg * 4 + c->e_loc + 1) * 4, 0));
+    if (R) {
+        AMOE_CUDA(c, cudaMemset(c->ep_m.status, 0, 16));
+        c->ep_m.mode = c->ep_m.status + 1;
+        AMOE_CUDA(c, cudaMemset(c->ep_m.arrive, 0, 16));
+    }
     return AMOE_OK;
 }
 
@@ -329,7 +339,9 @@ void release(amoe_ctx *c) {
     for (auto e : c->slot_ready) if (e) cudaEventDestroy(e);
     for (auto e : c->slot_free) if (e) cudaEventDestroy(e);
     if (c->scratch) cudaFree(c->scratch);
-    if (c->h_stage) cudaFreeHost(c->h_stage);
+    for (size_t q = 0; q < c->ep_peer.size(); ++q)
+        if (c->ep_peer[q] && c->ep_peer[q] != c->ep_win) cudaIpcCloseMemHandle(c->ep_peer[q]);
+    if (c->ep_win) cudaFree(c->ep_win);
     if (c->comm) g_nccl.ncclCommDestroy(c->comm);
     for (auto &t : c->pending)
         for (int i = 0; i < t.n; ++i) cudaEventDestroy(t.ev[i]);
@@ -375,6 +387,15 @@ int check_device_flag(amoe_ctx *c) {
     if (v != 0) {
         cudaMemset(flag, 0, sizeof(int32_t));
         if (v == 21) return fail(c, AMOE_ERR_STATE, "expert GEMV: an expert received more rows than the launch bound");
+        if (v >= 30 && v <= 33) {
+            // the ranks are out of step (a peer failed, left or never called):
+            // the group cannot be resumed
+            c->ep_broken = true;
+            static const char *what[] = {"count exchange", "row dispatch", "output return",
+                                         "row dispatch (inconsistent counts)"};
+            return fail(c, v == 33 ? AMOE_ERR_STATE : AMOE_ERR_TIMEOUT,
+                        std::string("expert-parallel ") + what[v - 30] + " failed (code " + std::to_string(v) + ")");
+        }
         return fail(c, AMOE_ERR_TIMEOUT, "device pipeline wait timed out (code " + std::to_string(v) + ")");
     }
     return AMOE_OK;
@@ -396,103 +417,158 @@ int use_tensor_path(const amoe_ctx *c, int T) {
     return tc_supported() && pairs_per_expert >= 32;
 }
 
-int nccl_fail(amoe_ctx *c, ncclResult_t r, const char *what) {
-    return fail(c, AMOE_ERR_NCCL, std::string(what) + ": " + g_nccl.ncclGetErrorString(r));
+// Bound on every wait of the exchange (AMOE_EP_WAIT_MS overrides it).  The count
+// exchange at the start of a forward also absorbs the ranks' host-side skew,
+// hence seconds, not microseconds.
+constexpr long long kEpWaitNs = 20000000000LL;
+
+long long ep_wait_ns() {
+    const char *v = std::getenv("AMOE_EP_WAIT_MS");
+    if (!v || !*v) return kEpWaitNs;
+    const long long ms = std::atoll(v);
+    return ms > 0 ? ms * 1000000LL : kEpWaitNs;
 }
 
-#define AMOE_NCCL(ctx, call)                                     \
-    do {                                                         \
-        ncclResult_t r_ = (call);                                \
-        if (r_ != ncclSuccess) return nccl_fail(ctx, r_, #call); \
-    } while (0)
-
-// Expert-parallel expert stage: send each routed row to the rank that owns its
-// expert, run this rank's experts on what arrives, and bring the outputs back
-// into c->y at the rows' local positions (where the combine reads them).
-int ep_experts(amoe_ctx *c, const LayerDev &L, int T, cudaStream_t st, StageTimer &timer, bool *used_tc) {
+// Maps every rank's window into this process: the windows' IPC handles and the
+// block shape go round once through an NCCL all-gather (the only NCCL use).
+int ep_setup(amoe_ctx *c) {
     const Dims &d = c->d;
-    const int N = c->ep_n, El = c->e_loc, H = d.H;
-    const int P_cap = c->max_tokens * d.k;
-    __half *xp_hi, *xp_lo;
-    tc_rows(c->tc_scratch, P_cap, H, &xp_hi, &xp_lo);
-    // 1. local expert-sorted rows (positions + gather)
-    AMOE_CUDA(c, launch_scatter(d, T, c->r, true, xp_hi, xp_lo, st));
-    c->stats.launches += 1;
-    // 2. per-expert counts to every rank
-    AMOE_NCCL(c, g_nccl.ncclGroupStart());
-    for (int q = 0; q < N; ++q) {
-        AMOE_NCCL(c, g_nccl.ncclSend(c->r.counts + (size_t)q * El, El, ncclInt32, q, c->comm, st));
-        AMOE_NCCL(c, g_nccl.ncclRecv(c->recv_counts + (size_t)q * El, El, ncclInt32, q, c->comm, st));
-    }
-    AMOE_NCCL(c, g_nccl.ncclGroupEnd());
-    int32_t *h_off = c->h_stage, *h_recv = c->h_stage + d.E + 1, *h_seg = h_recv + (size_t)N * El;
-    AMOE_CUDA(c, cudaMemcpyAsync(h_off, c->r.offsets, (size_t)(d.E + 1) * 4, cudaMemcpyDeviceToHost, st));
-    AMOE_CUDA(c, cudaMemcpyAsync(h_recv, c->recv_counts, (size_t)N * El * 4, cudaMemcpyDeviceToHost, st));
-    AMOE_CUDA(c, cudaStreamSynchronize(st));
-    // 3. plan
-    if (ep_plan(N, El, c->ep_rank, h_off, h_recv, &c->plan))
-        return fail(c, AMOE_ERR_STATE, "inconsistent expert counts from the expert-parallel group");
-    const EpPlan &pl = c->plan;
-    if ((size_t)pl.R > c->r_max)
-        return fail(c, AMOE_ERR_STATE, "expert-parallel receive exceeds this rank's buffers");
-    // 4. dispatch the rows (fp16 hi and lo planes)
-    AMOE_NCCL(c, g_nccl.ncclGroupStart());
-    for (int q = 0; q < N; ++q) {
-        const size_t so = (size_t)pl.send_off[q] * H, sn = (size_t)pl.send_rows[q] * H;
-        const size_t ro = (size_t)pl.recv_off[q] * H, rn = (size_t)pl.recv_rows[q] * H;
-        if (sn) {
-            AMOE_NCCL(c, g_nccl.ncclSend(xp_hi + so, sn, ncclFloat16, q, c->comm, st));
-            AMOE_NCCL(c, g_nccl.ncclSend(xp_lo + so, sn, ncclFloat16, q, c->comm, st));
+    const int N = c->ep_n, me = c->ep_rank;
+    c->ep_w = ep_window(N, d.E, d.H, c->max_tokens * d.k, (int)c->r_max);
+    AMOE_CUDA(c, cudaMalloc(&c->ep_win, c->ep_w.bytes));
+    AMOE_CUDA(c, cudaMemset(c->ep_win, 0, c->ep_w.table));  // the flags
+    AMOE_CUDA(c, cudaDeviceSynchronize());
+    struct Hello {
+        cudaIpcMemHandle_t handle;
+        int64_t shape[8];
+    };
+    Hello mine{};
+    AMOE_CUDA(c, cudaIpcGetMemHandle(&mine.handle, c->ep_win));
+    const int64_t shape[8] = {N, d.H, d.I, d.E, d.k, c->max_tokens, (int64_t)c->ep_w.bytes, c->cfg.path};
+    std::memcpy(mine.shape, shape, sizeof(shape));
+    std::vector<Hello> all(N);
+    uint8_t *buf = nullptr;
+    AMOE_CUDA(c, cudaMalloc(&buf, sizeof(Hello) * (N + 1)));
+    cudaError_t e = cudaMemcpy(buf, &mine, sizeof(Hello), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        const ncclResult_t r = g_nccl.ncclAllGather(buf, buf + sizeof(Hello), sizeof(Hello), ncclUint8, c->comm,
+                                                    c->stream);
+        if (r != ncclSuccess) {
+            cudaFree(buf);
+            return fail(c, AMOE_ERR_NCCL, std::string("ncclAllGather: ") + g_nccl.ncclGetErrorString(r));
         }
-        if (rn) {
-            AMOE_NCCL(c, g_nccl.ncclRecv(c->recv_hi + ro, rn, ncclFloat16, q, c->comm, st));
-            AMOE_NCCL(c, g_nccl.ncclRecv(c->recv_lo + ro, rn, ncclFloat16, q, c->comm, st));
-        }
+        e = cudaStreamSynchronize(c->stream);
+        if (e == cudaSuccess) e = cudaMemcpy(all.data(), buf + sizeof(Hello), sizeof(Hello) * N, cudaMemcpyDeviceToHost);
     }
-    AMOE_NCCL(c, g_nccl.ncclGroupEnd());
+    cudaFree(buf);
+    AMOE_CUDA(c, e);
+    for (int q = 0; q < N; ++q)
+        if (std::memcmp(all[q].shape, shape, sizeof(shape)) != 0)
+            return fail(c, AMOE_ERR_INVALID, "expert-parallel rank " + std::to_string(q) +
+                                                 " has another block shape, max_tokens or path");
+    c->ep_peer.assign(N, nullptr);
+    for (int q = 0; q < N; ++q) {
+        if (q == me) {
+            c->ep_peer[q] = c->ep_win;
+            continue;
+        }
+        void *p = nullptr;
+        e = cudaIpcOpenMemHandle(&p, all[q].handle, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess)
+            return cuda_fail(c, e, ("cudaIpcOpenMemHandle(rank " + std::to_string(q) + ")").c_str());
+        c->ep_peer[q] = static_cast<uint8_t *>(p);
+    }
+    uint8_t *win[kMaxEpRanks] = {};
+    float *ret_y[kMaxEpRanks] = {};
+    int32_t *ret_flag[kMaxEpRanks] = {};
+    for (int q = 0; q < N; ++q) {
+        win[q] = c->ep_peer[q];
+        ret_y[q] = reinterpret_cast<float *>(win[q] + c->ep_w.y);
+        ret_flag[q] = reinterpret_cast<int32_t *>(win[q] + c->ep_w.flags) + kEpFlagReturn * kMaxEpRanks + me;
+    }
+    AMOE_CUDA(c, cudaMemcpy(c->ep_m.win, win, sizeof(win), cudaMemcpyHostToDevice));
+    AMOE_CUDA(c, cudaMemcpy(c->ep_m.ret_y, ret_y, sizeof(ret_y), cudaMemcpyHostToDevice));
+    AMOE_CUDA(c, cudaMemcpy(c->ep_m.ret_flag, ret_flag, sizeof(ret_flag), cudaMemcpyHostToDevice));
+    return AMOE_OK;
+}
+
+// Expert-parallel expert stage: each routed row goes to the rank that owns its
+// expert, this rank's experts run on what arrives, and their outputs land in
+// the source ranks' windows at the rows' local sorted positions (where the
+// combine reads them).  Device-side throughout: no host synchronisation.
+int ep_experts(amoe_ctx *c, const LayerDev &L, int T, int nchunk, cudaStream_t st, StageTimer &timer,
+               bool *used_tc) {
+    const Dims &d = c->d;
+    const int N = c->ep_n, El = c->e_loc;
+    int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H);
+    if (nchunk > 1) {  // the stable permutation (one routing chunk writes it itself)
+        AMOE_CUDA(c, launch_scatter(d, T, c->r, false, nullptr, nullptr, st));
+        c->stats.launches += 1;
+    }
+    EpArgs a{};
+    a.N = N;
+    a.me = c->ep_rank;
+    a.E = d.E;
+    a.El = El;
+    a.H = d.H;
+    a.k = d.k;
+    a.r_cap = (int)c->r_max;
+    a.p_cap = c->max_tokens * d.k;
+    a.epoch = ++c->ep_epoch;
+    a.limit_ns = c->ep_wait_ns;
+    a.w = c->ep_w;
+    a.m = c->ep_m;
+    a.counts = c->r.counts;
+    a.offsets = c->r.offsets;
+    a.topk_idx = c->r.topk_idx;
+    a.perm_pair = c->r.perm_pair;
+    a.x_hi = c->r.x_hi;
+    a.x_lo = c->r.x_lo;
+    a.err = flag;
+    a.path = c->cfg.path == AMOE_PATH_GEMV ? 1 : c->cfg.path == AMOE_PATH_TENSOR ? 2 : 0;
+    if (a.path == 0 && !tc_supported()) a.path = 1;
+    AMOE_CUDA(c, launch_ep_counts(a, st));
+    AMOE_CUDA(c, launch_ep_dispatch(a, 2 * c->sms, st));
     timer.mark(5);
-    // 5. expert-major order for this rank's experts
-    std::memcpy(h_seg, pl.seg.data(), pl.seg.size() * 4);
-    std::memcpy(h_seg + pl.seg.size(), pl.offsets_loc.data(), pl.offsets_loc.size() * 4);
-    AMOE_CUDA(c, cudaMemcpyAsync(c->seg_dev, h_seg, pl.seg.size() * 4, cudaMemcpyHostToDevice, st));
-    AMOE_CUDA(c, cudaMemcpyAsync(c->offsets_loc, h_seg + pl.seg.size(), pl.offsets_loc.size() * 4,
-                                 cudaMemcpyHostToDevice, st));
-    AMOE_CUDA(c, launch_ep_reorder(c->seg_dev, N * El, H, c->recv_hi, c->recv_lo, c->ex_hi, c->ex_lo, c->ret_map,
-                                   st));
-    AMOE_CUDA(c, launch_ep_active(c->offsets_loc, El, c->active_loc, st));
-    c->stats.launches += 2;
-    // 6. this rank's experts; down writes straight into the return buffer
-    int max_rows = 0;
-    for (int e = 0; e < El; ++e) max_rows = std::max(max_rows, pl.offsets_loc[e + 1] - pl.offsets_loc[e]);
-    int32_t *flag = tc_error_flag(c->tc_scratch, P_cap, H);
-    const bool tc = c->cfg.path == AMOE_PATH_TENSOR ||
-                    (c->cfg.path == AMOE_PATH_AUTO && tc_supported() && pl.R >= 32 * El);
-    *used_tc = tc;
-    if (pl.R > 0) {
-        if (tc) {
-            int n = 0;
-            AMOE_CUDA(c, launch_tc_experts(c->dx, L, c->offsets_loc, c->ex_hi, c->ex_lo, (int)c->r_max, c->act_hi,
-                                           c->act_lo, c->y_send, c->ret_map, flag, st, &timer_hook, &timer, &n));
-            c->stats.launches += n;
-        } else {
-            GemvRows rows{c->ex_hi, c->ex_lo, nullptr, c->offsets_loc, c->active_loc, c->ret_map,
-                          std::min(pl.R, El)};
-            AMOE_CUDA(c, launch_gemv_gate_up(c->dx, L, rows, max_rows, c->act_hi, c->act_lo, flag, st));
-            timer.mark(2);
-            AMOE_CUDA(c, launch_gemv_down(c->dx, L, rows, max_rows, c->act_hi, c->act_lo, c->y_send, flag, st));
-            timer.mark(3);
-            c->stats.launches += 2;
-        }
+    AMOE_CUDA(c, launch_ep_wait(a, kEpFlagDispatch, 31, st));
+    c->stats.launches += 3;
+    // this rank's experts on the receive buffer; down stores into the sources' windows
+    __half *rh = reinterpret_cast<__half *>(c->ep_win + c->ep_w.recv_hi);
+    __half *rl = reinterpret_cast<__half *>(c->ep_win + c->ep_w.recv_lo);
+    float *y_own = reinterpret_cast<float *>(c->ep_win + c->ep_w.y);
+    EpReturn ret;
+    ret.y = c->ep_m.ret_y;
+    ret.flag = c->ep_m.ret_flag;
+    ret.arrive = c->ep_m.arrive + 1;
+    ret.status = c->ep_m.status;
+    ret.n = N;
+    ret.epoch = a.epoch;
+    // Expert path: AUTO is decided on the device by the count kernel from the
+    // whole group's pairs (the single-GPU rule on the group's tokens), so every
+    // rank agrees and the result equals one GPU's; both paths are launched and
+    // the one not chosen returns at once.
+    const bool run_tc = tc_supported() && a.path != 1;
+    const bool run_gemv = a.path != 2;
+    const int32_t *gate = run_tc && run_gemv ? c->ep_m.mode : nullptr;
+    *used_tc = run_tc && (a.path == 2 || (long long)N * T * d.k >= 32LL * d.E);  // stats guess
+    if (run_tc) {
+        int n = 0;
+        AMOE_CUDA(c, launch_tc_experts(c->dx, L, c->ep_m.offsets_loc, rh, rl, (int)c->r_max, c->act_hi, c->act_lo,
+                                       y_own, c->ep_m.y_rows, flag, st, &timer_hook, &timer, &n, &ret, gate, 1));
+        c->stats.launches += n;
     }
-    // 7. outputs back to the ranks the rows came from, at their local positions
-    AMOE_NCCL(c, g_nccl.ncclGroupStart());
-    for (int q = 0; q < N; ++q) {
-        const size_t so = (size_t)pl.send_off[q] * H, sn = (size_t)pl.send_rows[q] * H;
-        const size_t ro = (size_t)pl.recv_off[q] * H, rn = (size_t)pl.recv_rows[q] * H;
-        if (rn) AMOE_NCCL(c, g_nccl.ncclSend(c->y_send + ro, rn, ncclFloat32, q, c->comm, st));
-        if (sn) AMOE_NCCL(c, g_nccl.ncclRecv(c->y + so, sn, ncclFloat32, q, c->comm, st));
+    if (run_gemv) {
+        // any expert's rows: at most one per token of the group
+        const int bound = N * c->max_tokens;
+        GemvRows rows{rh, rl, nullptr, c->ep_m.offsets_loc, c->ep_m.active_loc, c->ep_m.y_rows, El, gate, 0};
+        AMOE_CUDA(c, launch_gemv_gate_up(c->dx, L, rows, bound, c->act_hi, c->act_lo, flag, st));
+        timer.mark(2);
+        AMOE_CUDA(c, launch_gemv_down(c->dx, L, rows, bound, c->act_hi, c->act_lo, y_own, flag, st, &ret));
+        timer.mark(3);
+        c->stats.launches += 2;
     }
-    AMOE_NCCL(c, g_nccl.ncclGroupEnd());
+    AMOE_CUDA(c, launch_ep_wait(a, kEpFlagReturn, 32, st));
+    c->stats.launches += 1;
     return AMOE_OK;
 }
 
@@ -572,6 +648,13 @@ int amoe_create(const amoe_config *cfg, amoe_ctx **out) {
             if (rc != AMOE_OK) break;
         }
         rc = alloc_scratch(c);
+        if (rc == AMOE_OK) {
+            int sms = 0;
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cfg->device);
+            c->sms = sms > 0 ? sms : 148;
+        }
+        c->ep_wait_ns = ep_wait_ns();
+        if (rc == AMOE_OK && c->ep_n > 1) rc = ep_setup(c);
     } while (0);
     if (rc != AMOE_OK) {
         g_create_error = c->err;
@@ -707,8 +790,11 @@ int amoe_forward_device(amoe_ctx *c, int32_t layer, const float *residual, int32
         c->stats.launches += nchunk > 1 ? 2 : 1;
     }
     if (c->ep_n > 1) {
+        if (c->ep_broken)
+            return fail(c, AMOE_ERR_STATE, "expert-parallel group is out of step after a failed exchange; "
+                                           "recreate the contexts");
         timer.mark(1);
-        rc = ep_experts(c, L, T, st, timer, &tc);
+        rc = ep_experts(c, L, T, nchunk, st, timer, &tc);
         if (rc) return rc;
     } else if (!tc && nchunk > 1 && !fused_decode) {
         AMOE_CUDA(c, launch_scatter(d, T, c->r, false, nullptr, nullptr, st));
@@ -742,7 +828,8 @@ int amoe_forward_device(amoe_ctx *c, int32_t layer, const float *residual, int32
         c->stats.launches += 2;
     }
     if (!fused) {
-        AMOE_CUDA(c, launch_combine(d, residual, c->r, c->y, T, out, st));
+        const float *y = c->ep_n > 1 ? reinterpret_cast<const float *>(c->ep_win + c->ep_w.y) : c->y;
+        AMOE_CUDA(c, launch_combine(d, residual, c->r, y, T, out, st));
         timer.mark(4);
         c->stats.launches += 1;
     }
@@ -843,27 +930,13 @@ int amoe_ep_unique_id(void *out) {
     return AMOE_OK;
 }
 
-int amoe_ep_plan(int32_t n_ranks, int32_t experts_per_rank, int32_t rank, const int32_t *local_offsets,
-                 const int32_t *recv_counts, int32_t *send_off, int32_t *send_rows, int32_t *recv_off,
-                 int32_t *recv_rows, int32_t *offsets_loc, int32_t *segments) {
-    if (!local_offsets || !recv_counts) {
-        set_thread_error("counts must not be NULL");
+int amoe_ep_layout(int32_t n_ranks, int32_t experts_per_rank, int32_t rank, const int32_t *table,
+                   int32_t *send_base, int32_t *offsets_loc, int32_t *seg_start, int32_t *src_pos) {
+    if (ep_layout(n_ranks, experts_per_rank, rank, table, send_base, offsets_loc, seg_start, src_pos)) {
+        set_thread_error("expert-parallel layout needs 1 <= n_ranks <= 8, experts_per_rank >= 1, "
+                         "0 <= rank < n_ranks and a non-negative count table");
         return AMOE_ERR_INVALID;
     }
-    EpPlan p;
-    if (ep_plan(n_ranks, experts_per_rank, rank, local_offsets, recv_counts, &p)) {
-        set_thread_error("inconsistent expert-parallel counts");
-        return AMOE_ERR_INVALID;
-    }
-    auto put = [](int32_t *dst, const std::vector<int> &v) {
-        if (dst) std::memcpy(dst, v.data(), v.size() * 4);
-    };
-    put(send_off, p.send_off);
-    put(send_rows, p.send_rows);
-    put(recv_off, p.recv_off);
-    put(recv_rows, p.recv_rows);
-    put(offsets_loc, p.offsets_loc);
-    put(segments, p.seg);
     return AMOE_OK;
 }
 

@@ -206,7 +206,6 @@ __launch_bounds__(kDecThreads, 1) __global__
     uint64_t *empty = full + p.stages;
     uint64_t *accfull = empty + p.stages;  // [2]
     uint64_t *accempty = accfull + 2;      // [2]
-    uint64_t *b1ready = accempty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + lay.tmem_slot);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;

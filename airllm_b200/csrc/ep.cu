@@ -1,15 +1,26 @@
-// ep.cu -- expert parallelism: experts sharded over the GPUs of one box, with
-// NCCL all-to-all dispatch of token rows to the expert's GPU and return of the
-// expert outputs (no counterpart in the reference, which is single-threaded
-// CPU code; the single-GPU path is its oracle).
+// ep.cu -- expert parallelism: experts sharded over the GPUs of one box, rows
+// exchanged by stores into peer memory over NVLink (no counterpart in the
+// reference, which is single-threaded CPU code; the single-GPU path is its
+// oracle: the per-row arithmetic is the same, so outputs match bit for bit).
 //
-// Rank r owns experts [r*E_loc, (r+1)*E_loc).  Its locally routed pairs are
-// already sorted by expert, hence by destination rank.  The exchange:
-//   1. per-expert pair counts -> every rank (grouped ncclSend/ncclRecv);
-//   2. ep_plan() turns them into send/receive row ranges and the segments that
-//      reorder received rows (source-major) into expert-major order;
-//   3. the fp16 hi/lo rows go out, the expert GEMMs run on the received rows,
-//      their f32 outputs go back in the order they came.
+// Per forward, on every rank, in stream order:
+//   ep_counts_kernel    (1 CTA)  counts -> every rank's table, wait for all rows,
+//                                derive the exchange layout
+//   ep_dispatch_kernel  (grid)   rows -> owners' receive buffers (expert-major);
+//                                return targets of the rows this rank receives;
+//                                last CTA publishes the dispatch flags
+//   ep_wait_kernel      (1 warp) all dispatch flags of this epoch are in
+//   gate_up, down GEMMs          down stores outputs into the sources' windows,
+//                                last CTA publishes the return flags
+//   ep_wait_kernel      (1 warp) all return flags are in; then the combine
+// Flags hold the epoch (forward count), which grows monotonically, so none is
+// ever reset.  A rank writes into a peer's buffers only after the peer has
+// finished reading them for the previous epoch: a peer's receive buffer is
+// consumed before the peer returns outputs, and a rank dispatches epoch f+1 only
+// after every peer's epoch-f returns reached it.  Every wait is bounded (global
+// timer); a failed wait records an error code, empties the expert ranges and
+// withholds this rank's later flags, so peers time out instead of reading
+// incomplete data.
 #include "amoe_internal.cuh"
 
 #include <dlfcn.h>
@@ -18,7 +29,7 @@
 
 namespace amoe {
 
-// ---- NCCL, resolved at run time (same soname torch loads; no link dependency) ----
+// ---- NCCL (setup only: IPC handle exchange), resolved at run time ----------------
 NcclApi g_nccl;
 
 bool nccl_load(std::string *err) {
@@ -40,13 +51,8 @@ bool nccl_load(std::string *err) {
         AMOE_SYM(ncclGetUniqueId)
         AMOE_SYM(ncclCommInitRank)
         AMOE_SYM(ncclCommDestroy)
-        AMOE_SYM(ncclCommAbort)
-        AMOE_SYM(ncclGroupStart)
-        AMOE_SYM(ncclGroupEnd)
-        AMOE_SYM(ncclSend)
-        AMOE_SYM(ncclRecv)
+        AMOE_SYM(ncclAllGather)
         AMOE_SYM(ncclGetErrorString)
-        AMOE_SYM(ncclCommGetAsyncError)
 #undef AMOE_SYM
         ok = true;
     });
@@ -54,52 +60,74 @@ bool nccl_load(std::string *err) {
     return ok;
 }
 
-// ---- exchange plan (host only) --------------------------------------------------
-int ep_plan(int N, int E_loc, int rank, const int32_t *local_offsets, const int32_t *recv_counts, EpPlan *p) {
-    if (N < 1 || E_loc < 1 || rank < 0 || rank >= N) return -1;
-    p->N = N;
-    p->E_loc = E_loc;
-    p->send_off.assign(N, 0);
-    p->send_rows.assign(N, 0);
-    p->recv_off.assign(N, 0);
-    p->recv_rows.assign(N, 0);
-    p->offsets_loc.assign(E_loc + 1, 0);
-    p->seg.assign((size_t)N * E_loc * 3, 0);
-    for (int d = 0; d < N; ++d) {
-        p->send_off[d] = local_offsets[d * E_loc];
-        p->send_rows[d] = local_offsets[(d + 1) * E_loc] - local_offsets[d * E_loc];
-        if (p->send_rows[d] < 0) return -1;
-    }
-    int acc = 0;
-    for (int s = 0; s < N; ++s) {
-        int rows = 0;
-        for (int e = 0; e < E_loc; ++e) {
-            const int v = recv_counts[s * E_loc + e];
-            if (v < 0) return -1;
-            rows += v;
+namespace {
+inline size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
+}  // namespace
+
+EpWindow ep_window(int N, int E, int H, int p_cap, int r_cap) {
+    EpWindow w{};
+    size_t off = 0;
+    w.flags = off;
+    off = up256(off + 3 * kMaxEpRanks * 4);
+    w.table = off;
+    off = up256(off + (size_t)N * E * 4);
+    w.recv_hi = off;
+    off = up256(off + (size_t)r_cap * H * 2);
+    w.recv_lo = off;
+    off = up256(off + (size_t)r_cap * H * 2);
+    w.y = off;
+    off = up256(off + (size_t)p_cap * H * 4);
+    w.bytes = off;
+    return w;
+}
+
+// ---- layout of one exchange ------------------------------------------------------
+// table[s][e]: pairs source s routes to global expert e; colsum(e) = sum_s table[s][e].
+//   send_base[e]       = sum_{owner(e)*El <= e' < e} colsum(e') + sum_{s < me} table[s][e]
+//   offsets_loc[el]    = sum_{me*El <= e' < me*El + el} colsum(e')
+//   seg_start[el][s]   = offsets_loc[el] + sum_{s' < s} table[s'][me*El + el]
+//   src_pos[el][s]     = sum_{e' < me*El + el} table[s][e']
+// so the owner's receive buffer holds expert el's rows source by source, each
+// source's rows in its own (token, slot) order -- the order the single-GPU path
+// gives them when the ranks' tokens are concatenated.
+int ep_layout(int N, int El, int me, const int32_t *table, int32_t *send_base, int32_t *offsets_loc,
+              int32_t *seg_start, int32_t *src_pos) {
+    if (N < 1 || N > kMaxEpRanks || El < 1 || me < 0 || me >= N || !table) return -1;
+    const int E = N * El;
+    for (int i = 0; i < N * E; ++i)
+        if (table[i] < 0) return -1;
+    std::vector<long long> col(E, 0);
+    for (int s = 0; s < N; ++s)
+        for (int e = 0; e < E; ++e) col[e] += table[s * E + e];
+    for (int q = 0; q < N; ++q) {
+        long long acc = 0;
+        for (int el = 0; el < El; ++el) {
+            const int e = q * El + el;
+            long long lower = 0;
+            for (int s = 0; s < me; ++s) lower += table[s * E + e];
+            if (send_base) send_base[e] = (int32_t)(acc + lower);
+            if (q == me && offsets_loc) offsets_loc[el] = (int32_t)acc;
+            acc += col[e];
         }
-        p->recv_off[s] = acc;
-        p->recv_rows[s] = rows;
-        acc += rows;
+        if (q == me && offsets_loc) offsets_loc[El] = (int32_t)acc;
     }
-    p->R = acc;
-    // expert-major order: expert e's rows from source 0, then source 1, ...
-    for (int e = 0; e < E_loc; ++e) {
-        int c = 0;
-        for (int s = 0; s < N; ++s) c += recv_counts[s * E_loc + e];
-        p->offsets_loc[e + 1] = p->offsets_loc[e] + c;
-    }
-    std::vector<int> dst_cursor(p->offsets_loc.begin(), p->offsets_loc.end() - 1);
     for (int s = 0; s < N; ++s) {
-        int src = p->recv_off[s];
-        for (int e = 0; e < E_loc; ++e) {
-            const int len = recv_counts[s * E_loc + e];
-            int *g = &p->seg[((size_t)s * E_loc + e) * 3];
-            g[0] = src;
-            g[1] = dst_cursor[e];
-            g[2] = len;
-            src += len;
-            dst_cursor[e] += len;
+        long long pre = 0;
+        for (int e = 0; e < me * El; ++e) pre += table[s * E + e];
+        for (int el = 0; el < El; ++el) {
+            const int e = me * El + el;
+            if (src_pos) src_pos[el * N + s] = (int32_t)pre;
+            pre += table[s * E + e];
+        }
+    }
+    if (seg_start) {
+        long long acc = 0;
+        for (int el = 0; el < El; ++el) {
+            const int e = me * El + el;
+            for (int s = 0; s < N; ++s) {
+                seg_start[el * N + s] = (int32_t)acc;
+                acc += table[s * E + e];
+            }
         }
     }
     return 0;
@@ -107,49 +135,236 @@ int ep_plan(int N, int E_loc, int rank, const int32_t *local_offsets, const int3
 
 namespace {
 
-// One CTA per (source, expert) segment: copy `len` received rows (fp16 hi/lo)
-// to their expert-major positions and record where each came from.
-__global__ void __launch_bounds__(256) ep_reorder_kernel(const int32_t *__restrict__ seg, int H,
-                                                         const __half *__restrict__ src_hi,
-                                                         const __half *__restrict__ src_lo,
-                                                         __half *__restrict__ dst_hi, __half *__restrict__ dst_lo,
-                                                         int32_t *__restrict__ ret_map) {
-    const int src = seg[blockIdx.x * 3], dst = seg[blockIdx.x * 3 + 1], len = seg[blockIdx.x * 3 + 2];
-    const int H8 = H / 8;
-    const int warps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int j = warp; j < len; j += warps) {
-        const uint4 *sh = reinterpret_cast<const uint4 *>(src_hi + (size_t)(src + j) * H);
-        const uint4 *sl = reinterpret_cast<const uint4 *>(src_lo + (size_t)(src + j) * H);
-        uint4 *dh = reinterpret_cast<uint4 *>(dst_hi + (size_t)(dst + j) * H);
-        uint4 *dl = reinterpret_cast<uint4 *>(dst_lo + (size_t)(dst + j) * H);
-        for (int i = lane; i < H8; i += 32) {
-            dh[i] = sh[i];
-            dl[i] = sl[i];
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait for *flag >= epoch (system scope); false once limit_ns passed.
+__device__ bool wait_epoch(const int32_t *flag, int epoch, long long limit_ns) {
+    const unsigned long long t0 = global_ns();
+    while (ld_acquire_sys(flag) - epoch < 0) {
+        if ((long long)(global_ns() - t0) > limit_ns) return false;
+        __nanosleep(64);
+    }
+    return true;
+}
+
+__device__ __forceinline__ int32_t *win_flag(uint8_t *win, const EpWindow &w, int which, int src) {
+    return reinterpret_cast<int32_t *>(win + w.flags) + which * kMaxEpRanks + src;
+}
+
+// Empties this rank's expert ranges so that the GEMMs do nothing (failed wait).
+__device__ void empty_ranges(const EpArgs &a) {
+    for (int i = threadIdx.x; i <= a.El; i += blockDim.x) {
+        a.m.offsets_loc[i] = 0;
+        a.m.active_loc[i] = 0;
+    }
+    if (threadIdx.x == 0) *a.m.status = 0;
+}
+
+constexpr int kCountThreads = 256;
+
+// One CTA.  E <= 256 (validated at create), N <= kMaxEpRanks.
+__global__ void __launch_bounds__(kCountThreads) ep_counts_kernel(EpArgs a) {
+    __shared__ int32_t tab[kMaxEpRanks * 256];
+    __shared__ int32_t col[256], lower[256], inblock[256];
+    __shared__ int32_t total_loc;
+    __shared__ uint8_t *win[kMaxEpRanks];
+    __shared__ int ok;
+    const int tid = threadIdx.x, N = a.N, E = a.E, El = a.El, me = a.me;
+    if (tid < N) win[tid] = a.m.win[tid];
+    if (tid == 0) ok = 1;
+    __syncthreads();
+    // 1. this rank's counts into row `me` of every rank's table, then its count flags
+    for (int i = tid; i < N * E; i += kCountThreads) {
+        const int q = i / E, e = i - q * E;
+        reinterpret_cast<int32_t *>(win[q] + a.w.table)[me * E + e] = a.counts[e];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (tid < N) st_release_sys(win_flag(win[tid], a.w, kEpFlagCount, me), a.epoch);
+    // 2. every rank's row of this epoch
+    if (tid < N && !wait_epoch(win_flag(win[me], a.w, kEpFlagCount, tid), a.epoch, a.limit_ns)) {
+        ok = 0;
+        atomicCAS(a.err, 0, 30);
+    }
+    __syncthreads();
+    if (!ok) {
+        empty_ranges(a);
+        return;
+    }
+    const int32_t *tg = reinterpret_cast<const int32_t *>(win[me] + a.w.table);
+    for (int i = tid; i < N * E; i += kCountThreads) tab[i] = __ldcv(tg + i);
+    __syncthreads();
+    // 3. column sums and the rows of lower ranks, per expert
+    if (tid < E) {
+        int s = 0, lo = 0;
+        for (int q = 0; q < N; ++q) {
+            const int v = tab[q * E + tid];
+            if (q < me) lo += v;
+            s += v;
         }
-        if (lane == 0) ret_map[dst + j] = src + j;
+        col[tid] = s;
+        lower[tid] = lo;
+    }
+    __syncthreads();
+    // 4. exclusive prefix of the column sums inside each owner's expert block
+    if (tid < N) {
+        int acc = 0;
+        for (int el = 0; el < El; ++el) {
+            inblock[tid * El + el] = acc;
+            acc += col[tid * El + el];
+        }
+        if (tid == me) total_loc = acc;
+    } else if (tid >= 32 && tid - 32 < N) {
+        // 5. src_pos: source s's sorted position of its first pair for each local expert
+        const int s = tid - 32;
+        int pre = 0;
+        for (int e = 0; e < me * El; ++e) pre += tab[s * E + e];
+        for (int el = 0; el < El; ++el) {
+            a.m.src_pos[el * N + s] = pre;
+            pre += tab[s * E + me * El + el];
+        }
+    }
+    __syncthreads();
+    if (tid < E) a.m.send_base[tid] = inblock[tid] + lower[tid];
+    for (int el = tid; el <= El; el += kCountThreads) a.m.offsets_loc[el] = el < El ? inblock[me * El + el] : total_loc;
+    for (int el = tid; el < El; el += kCountThreads) {
+        int acc = inblock[me * El + el];
+        for (int s = 0; s < N; ++s) {
+            a.m.seg_start[el * N + s] = acc;
+            acc += tab[s * E + me * El + el];
+        }
+    }
+    if (tid == 0) {
+        int na = 0;
+        for (int el = 0; el < El; ++el)
+            if (col[me * El + el] > 0) a.m.active_loc[na++] = el;
+        a.m.active_loc[El] = na;
+        // expert path: every rank reaches the same choice from the same table,
+        // and it is the single-GPU rule applied to the group's tokens
+        long long pairs = 0;
+        for (int e = 0; e < E; ++e) pairs += col[e];
+        *a.m.mode = a.path == 2 || (a.path == 0 && pairs >= 32LL * E) ? 1 : 0;
+        *a.m.status = 1;
     }
 }
 
-// Experts with rows, ascending, then their count at [E_loc] (the GEMV's list).
-__global__ void ep_active_kernel(const int32_t *__restrict__ offsets, int E_loc, int32_t *__restrict__ active) {
-    if (threadIdx.x != 0) return;
-    int na = 0;
-    for (int e = 0; e < E_loc; ++e)
-        if (offsets[e + 1] > offsets[e]) active[na++] = e;
-    active[E_loc] = na;
+constexpr int kDispatchThreads = 256;
+constexpr int kDispatchUnroll = 4;
+
+// Grid-stride over this rank's expert-sorted pairs, one warp per row: the fp16
+// hi and lo rows of the pair's token go into the owner's receive buffer.  Then
+// the return targets of the rows this rank receives.
+__global__ void __launch_bounds__(kDispatchThreads) ep_dispatch_kernel(EpArgs a) {
+    __shared__ uint8_t *win[kMaxEpRanks];
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (tid < a.N) win[tid] = a.m.win[tid];
+    __syncthreads();
+    const bool ok = *reinterpret_cast<const volatile int32_t *>(a.m.status) == 1;
+    if (ok) {
+        const int P = a.offsets[a.E];
+        const int H8 = a.H / 8;
+        const int warps = kDispatchThreads / 32;
+        for (int q = blockIdx.x * warps + (tid >> 5); q < P; q += gridDim.x * warps) {
+            const int pair = a.perm_pair[q];
+            const int e = a.topk_idx[pair];
+            const int t = pair / a.k;
+            const int dst = e / a.El;
+            const int row = a.m.send_base[e] + (q - a.offsets[e]);
+            if (row < 0 || row >= a.r_cap || dst >= a.N) {  // inconsistent counts: skip the store
+                if (lane == 0) atomicCAS(a.err, 0, 33);
+                continue;
+            }
+            const uint4 *sh = reinterpret_cast<const uint4 *>(a.x_hi + (size_t)t * a.H);
+            const uint4 *sl = reinterpret_cast<const uint4 *>(a.x_lo + (size_t)t * a.H);
+            uint4 *dh = reinterpret_cast<uint4 *>(win[dst] + a.w.recv_hi + (size_t)row * a.H * 2);
+            uint4 *dl = reinterpret_cast<uint4 *>(win[dst] + a.w.recv_lo + (size_t)row * a.H * 2);
+            for (int i0 = 0; i0 < H8; i0 += 32 * kDispatchUnroll) {
+                uint4 vh[kDispatchUnroll], vl[kDispatchUnroll];
+#pragma unroll
+                for (int u = 0; u < kDispatchUnroll; ++u) {
+                    const int i = i0 + u * 32 + lane;
+                    if (i < H8) {
+                        vh[u] = __ldg(sh + i);
+                        vl[u] = __ldg(sl + i);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < kDispatchUnroll; ++u) {
+                    const int i = i0 + u * 32 + lane;
+                    if (i < H8) {
+                        dh[i] = vh[u];
+                        dl[i] = vl[u];
+                    }
+                }
+            }
+        }
+        // return targets: received row p of local expert el came from source s
+        const int N = a.N, El = a.El;
+        const int R = min(a.m.offsets_loc[El], a.r_cap);
+        for (int p = blockIdx.x * kDispatchThreads + tid; p < R; p += gridDim.x * kDispatchThreads) {
+            int lo = 0, hi = El;  // last el with offsets_loc[el] <= p
+            while (hi - lo > 1) {
+                const int mid = (lo + hi) >> 1;
+                if (a.m.offsets_loc[mid] <= p) lo = mid;
+                else hi = mid;
+            }
+            const int32_t *ss = a.m.seg_start + lo * N;
+            int s = 0;
+            while (s + 1 < N && ss[s + 1] <= p) ++s;
+            int pos = a.m.src_pos[lo * N + s] + p - ss[s];
+            if (pos < 0 || pos >= a.p_cap) {  // inconsistent counts: keep the store in bounds
+                atomicCAS(a.err, 0, 33);
+                pos = 0;
+            }
+            a.m.y_rows[p] = (int32_t)(((uint32_t)s << kEpRowShift) | (uint32_t)pos);
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned total = gridDim.x;
+        if (atomicInc(a.m.arrive, total - 1) == total - 1 && ok) {
+            __threadfence_system();
+            for (int q = 0; q < a.N; ++q) st_release_sys(win_flag(win[q], a.w, kEpFlagDispatch, a.me), a.epoch);
+        }
+    }
+}
+
+// One warp: lane s < N waits for this rank's flag `which` from source s.  After
+// an earlier failed wait of this exchange (status 0) it returns at once: the
+// error is recorded and this rank's flags are withheld, so its peers fail too.
+__global__ void ep_wait_kernel(EpArgs a, int which, int code) {
+    const int lane = threadIdx.x;
+    if (*reinterpret_cast<const volatile int32_t *>(a.m.status) != 1) return;
+    uint8_t *own = a.m.win[a.me];
+    bool good = true;
+    if (lane < a.N) good = wait_epoch(win_flag(own, a.w, which, lane), a.epoch, a.limit_ns);
+    if (__any_sync(0xffffffffu, !good)) {
+        if (lane == 0) atomicCAS(a.err, 0, code);
+        if (which == kEpFlagDispatch) empty_ranges(a);
+        else if (lane == 0) *a.m.status = 0;
+    }
 }
 
 }  // namespace
 
-cudaError_t launch_ep_reorder(const int32_t *seg_dev, int nseg, int H, const __half *src_hi, const __half *src_lo,
-                              __half *dst_hi, __half *dst_lo, int32_t *ret_map, cudaStream_t st) {
-    if (nseg <= 0) return cudaSuccess;
-    ep_reorder_kernel<<<nseg, 256, 0, st>>>(seg_dev, H, src_hi, src_lo, dst_hi, dst_lo, ret_map);
+cudaError_t launch_ep_counts(const EpArgs &a, cudaStream_t st) {
+    if (a.E > 256 || a.N > kMaxEpRanks) return cudaErrorInvalidValue;
+    ep_counts_kernel<<<1, kCountThreads, 0, st>>>(a);
     return cudaGetLastError();
 }
 
-cudaError_t launch_ep_active(const int32_t *offsets, int E_loc, int32_t *active, cudaStream_t st) {
-    ep_active_kernel<<<1, 32, 0, st>>>(offsets, E_loc, active);
+cudaError_t launch_ep_dispatch(const EpArgs &a, int grid, cudaStream_t st) {
+    ep_dispatch_kernel<<<grid, kDispatchThreads, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_wait(const EpArgs &a, int which, int code, cudaStream_t st) {
+    ep_wait_kernel<<<1, 32, 0, st>>>(a, which, code);
     return cudaGetLastError();
 }
 

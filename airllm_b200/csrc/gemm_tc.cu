@@ -72,6 +72,9 @@ struct TcParams {
     float *y;                 // [P][R]
     const int32_t *y_rows;    // output row of each position (NULL: the position)
     int32_t *err;
+    EpReturn ret;             // expert-parallel down: rows go to their source rank
+    const int32_t *gate;      // if set: nothing to do unless *gate == gate_want (path chosen on the device)
+    int gate_want;
 };
 
 // ---- PTX helpers ----------------------------------------------------------------
@@ -225,6 +228,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                    const __grid_constant__ CUtensorMap tm_araw, const __grid_constant__ CUtensorMap tm_asc,
                    TcParams p) {
     extern __shared__ uint8_t smem_raw[];
+    if (p.gate && *p.gate != p.gate_want) return;  // the other expert path runs this step
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *aconv = smem;
     uint8_t *bhi = aconv + CSTAGES * ACONV_BYTES;
@@ -449,11 +453,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
                             const int tok = col0 + j;
-                            if (tok < ti.ntok && row_ok) {
-                                const int pos = ti.pos0 + tok;
-                                const size_t orow = p.y_rows ? (size_t)p.y_rows[pos] : (size_t)pos;
-                                p.y[orow * p.R + rrow] = __uint_as_float(v[j]) * scale + bd;
-                            }
+                            if (tok < ti.ntok && row_ok)
+                                ep_out_row(p.y, p.y_rows, p.ret, ti.pos0 + tok, p.R)[rrow] =
+                                    __uint_as_float(v[j]) * scale + bd;
                         }
                     }
                 }
@@ -469,6 +471,7 @@ done:
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
     }
+    ep_return_done(p.ret);  // expert-parallel down: outputs are in the source ranks' windows
 }
 
 // Per-expert exponent bias for the fp16 weight expansion: c = max finite E8M0
@@ -589,7 +592,8 @@ void tc_rows(void *tc_scratch, int max_pairs, int H, __half **xp_hi, __half **xp
 cudaError_t launch_tc_experts(const Dims &d, const LayerDev &L, const int32_t *offsets, const __half *b_hi,
                               const __half *b_lo, int rows_cap, __half *act_hi, __half *act_lo, float *y,
                               const int32_t *y_rows, int32_t *err, cudaStream_t st, StageHook hook,
-                              void *hook_arg, int *launches) {
+                              void *hook_arg, int *launches, const EpReturn *ret, const int32_t *gate,
+                              int gate_want) {
     if (!tc_supported()) return cudaErrorNotSupported;
     static bool attr_set = false;
     if (!attr_set) {
@@ -618,6 +622,8 @@ cudaError_t launch_tc_experts(const Dims &d, const LayerDev &L, const int32_t *o
         p.act_hi = act_hi;
         p.act_lo = act_lo;
         p.err = err;
+        p.gate = gate;
+        p.gate_want = gate_want;
         tc_gemm_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(m.bhi, m.blo, m.araw, m.asc, p);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
@@ -642,6 +648,9 @@ cudaError_t launch_tc_experts(const Dims &d, const LayerDev &L, const int32_t *o
         p.y = y;
         p.y_rows = y_rows;
         p.err = err;
+        if (ret) p.ret = *ret;
+        p.gate = gate;
+        p.gate_want = gate_want;
         tc_gemm_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(m.bhi, m.blo, m.araw, m.asc, p);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;

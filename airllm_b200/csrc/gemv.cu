@@ -35,6 +35,9 @@ struct GemvParams {
     int R, K, E, k;
     int x_rows;    // staged activation rows the launch provides (NG == 1)
     int32_t *err;  // set when a bounded wait gives up (20) or an expert has more rows than staged (21)
+    EpReturn ret;  // expert-parallel down: rows go to their source rank
+    const int32_t *gate;  // if set: nothing to do unless *gate == gate_want (path chosen on the device)
+    int gate_want;
     // outputs
     __half *act_hi, *act_lo;  // gate_up: [P][R/2]
     float *y;                 // down:    [P][R]
@@ -114,14 +117,19 @@ template <bool GATE_UP, int NG>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
     __shared__ float red[kGemvTiles][kGemvKSplit][NG][4][32];
     extern __shared__ __align__(128) uint8_t wsm[];
+    if (p.gate && *p.gate != p.gate_want) return;  // the other expert path runs this step
     const int slot = blockIdx.y;
     const int n_active = p.active[p.E];
-    if (slot >= n_active) return;  // uniform for the whole CTA
+    if (slot >= n_active) {  // uniform for the whole CTA
+        ep_return_done(p.ret);
+        return;
+    }
     const int e = p.active[slot];
     const int base = p.offsets[e];
     const int m_e = p.offsets[e + 1] - base;
     if (NG == 1 && min(8, m_e) > p.x_rows) {  // the launch bound T was violated: uniform exit
         if (threadIdx.x == 0) atomicCAS(p.err, 0, 21);
+        ep_return_done(p.ret);
         return;
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -294,15 +302,16 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
                         p.act_lo[(size_t)pos * (p.R / 2) + pr] = lo;
                     } else {
                         const int h = kTileRows * rt + g;
-                        const size_t orow = p.y_rows ? (size_t)p.y_rows[pos] : (size_t)pos;
-                        p.y[orow * p.R + h] = v[j] + p.bias[(size_t)e * p.R + h];
-                        p.y[orow * p.R + h + 8] = v[2 + j] + p.bias[(size_t)e * p.R + h + 8];
+                        float *yrow = ep_out_row(p.y, p.y_rows, p.ret, pos, p.R);
+                        yrow[h] = v[j] + p.bias[(size_t)e * p.R + h];
+                        yrow[h + 8] = v[2 + j] + p.bias[(size_t)e * p.R + h + 8];
                     }
                 }
             }
         }
         __syncthreads();  // red[] is rewritten by the next token pass
     }
+    ep_return_done(p.ret);
 }
 
 template <bool GATE_UP>
@@ -340,6 +349,8 @@ cudaError_t launch_gemv_gate_up(const Dims &d, const LayerDev &L, const GemvRows
     p.x_hi = rows.x_hi;
     p.x_lo = rows.x_lo;
     p.perm_pair = rows.perm_pair;
+    p.gate = rows.gate;
+    p.gate_want = rows.gate_want;
     p.offsets = rows.offsets;
     p.active = rows.active;
     p.R = 2 * d.I;
@@ -354,7 +365,7 @@ cudaError_t launch_gemv_gate_up(const Dims &d, const LayerDev &L, const GemvRows
 
 cudaError_t launch_gemv_down(const Dims &d, const LayerDev &L, const GemvRows &rows, int T,
                              const __half *act_hi, const __half *act_lo, float *y, int32_t *err,
-                             cudaStream_t st) {
+                             cudaStream_t st, const EpReturn *ret) {
     GemvParams p{};
     p.err = err;
     p.q = L.dn_q;
@@ -363,6 +374,8 @@ cudaError_t launch_gemv_down(const Dims &d, const LayerDev &L, const GemvRows &r
     p.x_hi = act_hi;
     p.x_lo = act_lo;
     p.perm_pair = nullptr;
+    p.gate = rows.gate;
+    p.gate_want = rows.gate_want;
     p.y_rows = rows.y_rows;
     p.offsets = rows.offsets;
     p.active = rows.active;
@@ -371,6 +384,7 @@ cudaError_t launch_gemv_down(const Dims &d, const LayerDev &L, const GemvRows &r
     p.E = d.E;
     p.k = d.k;
     p.y = y;
+    if (ret) p.ret = *ret;
     const int max_active = rows.max_active;
     return launch<false>(p, T, max_active, st);
 }

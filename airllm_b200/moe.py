@@ -80,7 +80,7 @@ SIGNATURES = {
     "amoe_set_profiling": (ctypes.c_int, [_vp, _i32]),
     "amoe_get_stats": (ctypes.c_int, [_vp, ctypes.POINTER(AmoeStats), _i32]),
     "amoe_ep_unique_id": (ctypes.c_int, [_vp]),
-    "amoe_ep_plan": (ctypes.c_int, [_i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "amoe_ep_layout": (ctypes.c_int, [_i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
     "amoe_route_noalloc": (ctypes.c_int, [_i32, _i32, _i32, _i32, ctypes.c_float, _vp, _i32, _vp, _vp, _vp,
                                           _vp, _vp, _vp, _vp]),
 }
@@ -136,20 +136,22 @@ def ep_unique_id() -> bytes:
     return buf.raw
 
 
-def ep_plan(n_ranks: int, experts_per_rank: int, rank: int, local_offsets, recv_counts) -> dict:
-    """Host planning of one expert-parallel exchange (amoe_ep_plan; no GPU needed)."""
+def ep_layout(n_ranks: int, experts_per_rank: int, rank: int, table) -> dict:
+    """Layout of one expert-parallel exchange from the count table [N][E]
+    (amoe_ep_layout; the arithmetic the device runs, here on the host)."""
     lib = load_library()
-    lo = np.ascontiguousarray(local_offsets, np.int32)
-    rc_ = np.ascontiguousarray(recv_counts, np.int32)
     N, El = n_ranks, experts_per_rank
-    out = {k: np.zeros(n, np.int32) for k, n in [("send_off", N), ("send_rows", N), ("recv_off", N),
-                                                  ("recv_rows", N), ("offsets_loc", El + 1),
-                                                  ("segments", N * El * 3)]}
-    rc = lib.amoe_ep_plan(N, El, rank, lo.ctypes.data, rc_.ctypes.data, *[out[k].ctypes.data for k in
-                          ("send_off", "send_rows", "recv_off", "recv_rows", "offsets_loc", "segments")])
+    tab = np.ascontiguousarray(table, np.int32)
+    if tab.shape != (N, N * El):
+        raise AmoeError(AMOE_ERR_INVALID, f"table must be [{N}][{N * El}]")
+    out = {"send_base": np.zeros(N * El, np.int32), "offsets_loc": np.zeros(El + 1, np.int32),
+           "seg_start": np.zeros(El * N, np.int32), "src_pos": np.zeros(El * N, np.int32)}
+    rc = lib.amoe_ep_layout(N, El, rank, tab.ctypes.data, *[out[k].ctypes.data for k in
+                            ("send_base", "offsets_loc", "seg_start", "src_pos")])
     if rc != AMOE_OK:
         raise AmoeError(rc, lib.amoe_last_error(None).decode())
-    out["segments"] = out["segments"].reshape(N * El, 3)
+    out["seg_start"] = out["seg_start"].reshape(El, N)
+    out["src_pos"] = out["src_pos"].reshape(El, N)
     return out
 
 

@@ -253,9 +253,10 @@ def run_streaming(args):
 
 def run_ep(args):
     """Configs 3 and 4: the GPT-OSS-120B-shaped block (128 experts) with its
-    experts sharded 128/N over the N GPUs (expert parallelism, NCCL all-to-all
-    dispatch and return).  Total tokens are fixed (strong scaling); each rank
-    routes T/N of them.  Timed per step with CUDA events, max over ranks."""
+    experts sharded 128/N over the N GPUs (expert parallelism: rows dispatched
+    and outputs returned by stores into the peers' memory over NVLink).  Total
+    tokens are fixed (strong scaling); each rank routes T/N of them.  Timed per
+    step with CUDA events, max over ranks."""
     import datetime
 
     import torch
@@ -291,7 +292,8 @@ def run_ep(args):
     xd = torch.from_numpy(x).cuda()
     od = torch.empty_like(xd)
     flush = L2Flush(torch)
-    for _ in range(args.warmup):
+    for i in range(args.warmup):
+        flush(i)  # its first call allocates (a host stall the other ranks would wait out)
         blk.forward_device(xd, od, stream=stream)
     torch.cuda.synchronize()
     blk.stats(reset=True)
@@ -301,11 +303,13 @@ def run_ep(args):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    h0 = time.perf_counter()
     for i in range(args.steps):
         flush(i)
         starts[i].record(stream)
         blk.forward_device(xd, od, stream=stream)
         ends[i].record(stream)
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps  # enqueue cost per step
     torch.cuda.synchronize()
     clk = clocks.stop()
     launches = int(blk.stats(reset=True)["launches"])
@@ -329,7 +333,12 @@ def run_ep(args):
         per_rank = [float(v.item()) for v in allt]
         ms = max(per_rank)
     n = max(st["timed_forwards"], 1)
-    stage = {k: v / n for k, v in st["stage_ms"].items() if v > 0}
+    stage = {k: round(v / n, 4) for k, v in st["stage_ms"].items() if v > 0}
+    stages_by_rank, host_by_rank = [stage], [host_ms]
+    if world > 1:
+        stages_by_rank, host_by_rank = [None] * world, [None] * world
+        dist.all_gather_object(stages_by_rank, stage)
+        dist.all_gather_object(host_by_rank, host_ms)
     flops = T * 4 * FLOP_PER_PAIR
     pk = peaks()
     line = {
@@ -341,12 +350,15 @@ def run_ep(args):
                                + (" adversarial(8 hot experts on rank 0)" if cfg == 4 else ""),
                    "config_index": cfg, "tokens": T, "tokens_per_rank": Tr, "experts_per_rank": 128 // world,
                    "parallelism": f"ep{world}", "l2": L2_NOTE},
-        "per_rank_ms": per_rank, "stage_ms_per_step_rank0": stage,
+        "per_rank_ms": per_rank, "stage_ms_per_step_by_rank": stages_by_rank,
+        "host_enqueue_ms_per_step_by_rank": host_by_rank,
         "tensor_tflops_algorithmic": flops / (ms / 1e3) / 1e12, "peak_bf16_tflops": pk["bf16_tflops"] * world,
         "gpu_launches": launches, "clocks": clk,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()  # no rank frees its window while a peer may still store into it
     blk.close()
     if world > 1:
         dist.destroy_process_group()
@@ -412,7 +424,8 @@ def main():
     wd = torch.empty((T, layer["top_k"]), dtype=torch.float32, device="cuda")
     flush = L2Flush(torch)
 
-    for _ in range(args.warmup):
+    for i in range(args.warmup):
+        flush(i)
         blk.forward_device(xd, od, topk_idx=idd, topk_w=wd, stream=stream)
     torch.cuda.synchronize()
     blk.stats(reset=True)
@@ -519,6 +532,8 @@ def main():
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()  # no rank frees its window while a peer may still store into it
     blk.close()
     if world > 1:
         dist.destroy_process_group()

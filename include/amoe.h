@@ -174,25 +174,31 @@ AMOE_API int amoe_route_noalloc(int32_t device, int32_t hidden, int32_t experts,
                                 const float *norm_gain, const float *router_w, const float *router_b,
                                 float *logits, int32_t *topk_idx, float *topk_w, void *stream);
 
-/* Expert parallelism (ep_size > 1): experts [r*E/N, (r+1)*E/N) live on rank r;
- * each rank routes its own tokens and exchanges rows with NCCL (no counterpart
- * in the reference, which is single-process CPU code).  All ranks must call
- * amoe_upload_layer / amoe_forward* for the same layer in the same order.
+/* Expert parallelism (ep_size > 1, at most 8 GPUs of one box): experts
+ * [r*E/N, (r+1)*E/N) live on rank r; each rank routes its own tokens.  Rows move
+ * by stores into the other ranks' device memory over NVLink (CUDA IPC windows
+ * mapped at amoe_create), ordered by per-source epoch flags, with no host
+ * synchronisation inside a forward (no counterpart in the reference, which is
+ * single-process CPU code).  NCCL is used once, at amoe_create, to exchange the
+ * windows' IPC handles.  All ranks must call amoe_forward* for the same layer in
+ * the same order with the same max_tokens; a wait that runs out (a rank failed
+ * or never called) returns AMOE_ERR_TIMEOUT and the group must be recreated.
  * amoe_ep_unique_id fills the 128-byte ncclUniqueId that rank 0 creates and
  * passes to the others (amoe_config.nccl_id). */
 AMOE_API int amoe_ep_unique_id(void *out);
 
-/* Host-side planning step of one expert-parallel exchange (no GPU needed):
- *   local_offsets [N*El + 1]: this rank's expert-sorted pair offsets (all experts),
- *   recv_counts [N][El]: pairs each source rank routes to this rank's El experts.
- * Out (each nullable): send_off/send_rows [N] rows sent to each rank,
- * recv_off/recv_rows [N] rows received from each rank (source-major),
- * offsets_loc [El+1] expert-major row ranges, segments [N*El][3]
- * (received row, expert-major row, length). */
-AMOE_API int amoe_ep_plan(int32_t n_ranks, int32_t experts_per_rank, int32_t rank,
-                          const int32_t *local_offsets, const int32_t *recv_counts,
-                          int32_t *send_off, int32_t *send_rows, int32_t *recv_off,
-                          int32_t *recv_rows, int32_t *offsets_loc, int32_t *segments);
+/* Layout of one expert-parallel exchange as rank `rank` derives it on the device
+ * from the all-gathered count table (no GPU needed here):
+ *   table [N][E], E = N*El: pairs each source rank routes to each global expert.
+ * Out (each nullable):
+ *   send_base [E]: row, in the owning rank's expert-major receive buffer, of
+ *                  this rank's first pair for expert e;
+ *   offsets_loc [El+1]: expert-major row ranges of this rank's experts;
+ *   seg_start [El][N]: first expert-major row of source s's rows for local expert el;
+ *   src_pos [El][N]: sorted position of those rows on source s (where outputs return). */
+AMOE_API int amoe_ep_layout(int32_t n_ranks, int32_t experts_per_rank, int32_t rank,
+                            const int32_t *table, int32_t *send_base, int32_t *offsets_loc,
+                            int32_t *seg_start, int32_t *src_pos);
 
 /* ABI version (AMOE_ABI_VERSION). */
 AMOE_API int amoe_abi_version(void);
