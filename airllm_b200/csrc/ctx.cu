@@ -93,6 +93,10 @@ void set_thread_error(const std::string &msg) { g_create_error = msg; }
 
 using namespace amoe;
 
+// amoe_forward splits large calls into at most this many token slices, so that
+// host copies overlap the compute of neighbouring slices.
+constexpr int kMaxIoChunks = 8;
+
 struct amoe_ctx {
     amoe_config cfg{};
     Dims d{};       // routing (all experts)
@@ -127,6 +131,10 @@ struct amoe_ctx {
     int32_t *io_idx = nullptr;
     float *io_w = nullptr;
     int last_T = 0;
+    std::vector<int> last_chunks;           // token counts of the last call's passes (routing slices)
+    cudaStream_t h2d_stream = nullptr, d2h_stream = nullptr;  // host-buffer forward pipeline
+    int32_t *h_flag = nullptr;              // pinned copy of the device error flag
+    cudaEvent_t io_in_ready[kMaxIoChunks] = {}, io_out_ready[kMaxIoChunks] = {};
 
     // expert parallelism (ep_size > 1)
     int ep_n = 1, ep_rank = 0, e_loc = 0;
@@ -224,9 +232,9 @@ int alloc_scratch(amoe_ctx *c) {
         {(void **)&c->r.topk_w, P * 4},
         {(void **)&c->r.hist, (size_t)c->nchunk_max * d.E * 4},
         {(void **)&c->r.chunk_base, (size_t)c->nchunk_max * d.E * 4},
-        {(void **)&c->r.counts, (size_t)d.E * 4},
-        {(void **)&c->r.offsets, (size_t)(d.E + 1) * 4},
-        {(void **)&c->r.active, (size_t)(d.E + 1) * 4},
+        {(void **)&c->r.counts, (size_t)kMaxIoChunks * d.E * 4},
+        {(void **)&c->r.offsets, (size_t)kMaxIoChunks * (d.E + 1) * 4},
+        {(void **)&c->r.active, (size_t)kMaxIoChunks * (d.E + 1) * 4},
         {(void **)&c->r.perm_pair, P * 4},
         {(void **)&c->r.inv, P * 4},
         {(void **)&c->partial, partial * 8},
@@ -333,6 +341,8 @@ void release(amoe_ctx *c) {
     cudaSetDevice(c->cfg.device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
+    if (c->h2d_stream) cudaStreamSynchronize(c->h2d_stream);
+    if (c->d2h_stream) cudaStreamSynchronize(c->d2h_stream);
     for (auto p : c->layer_dev) if (p) cudaFree(p);
     for (auto p : c->layer_host) if (p) cudaFreeHost(p);
     for (auto p : c->slot_dev) if (p) cudaFree(p);
@@ -346,6 +356,13 @@ void release(amoe_ctx *c) {
     for (auto &t : c->pending)
         for (int i = 0; i < t.n; ++i) cudaEventDestroy(t.ev[i]);
     for (auto e : c->event_pool) cudaEventDestroy(e);
+    for (int i = 0; i < kMaxIoChunks; ++i) {
+        if (c->io_in_ready[i]) cudaEventDestroy(c->io_in_ready[i]);
+        if (c->io_out_ready[i]) cudaEventDestroy(c->io_out_ready[i]);
+    }
+    if (c->h_flag) cudaFreeHost(c->h_flag);
+    if (c->h2d_stream) cudaStreamDestroy(c->h2d_stream);
+    if (c->d2h_stream) cudaStreamDestroy(c->d2h_stream);
     if (c->stream) cudaStreamDestroy(c->stream);
     if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
 }
@@ -379,11 +396,15 @@ int acquire_slot(amoe_ctx *c, int layer, cudaStream_t st, int *slot_out) {
 void timer_hook(void *timer, int stage) { static_cast<StageTimer *>(timer)->mark(stage); }
 
 // A tcgen05 kernel that gave up on a bounded wait leaves a code in its flag.
-int check_device_flag(amoe_ctx *c) {
+// `known`: the flag's value already copied to the host behind the call's work
+// (-1: read it now).
+int check_device_flag(amoe_ctx *c, int32_t known = -1) {
     int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * c->d.k, c->d.H);
-    int32_t v = 0;
-    cudaError_t e = cudaMemcpy(&v, flag, sizeof(v), cudaMemcpyDeviceToHost);
-    if (e != cudaSuccess) return cuda_fail(c, e, "read device error flag");
+    int32_t v = known;
+    if (v < 0) {
+        cudaError_t e = cudaMemcpy(&v, flag, sizeof(v), cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return cuda_fail(c, e, "read device error flag");
+    }
     if (v != 0) {
         cudaMemset(flag, 0, sizeof(int32_t));
         if (v == 21) return fail(c, AMOE_ERR_STATE, "expert GEMV: an expert received more rows than the launch bound");
@@ -496,13 +517,13 @@ int ep_setup(amoe_ctx *c) {
 // expert, this rank's experts run on what arrives, and their outputs land in
 // the source ranks' windows at the rows' local sorted positions (where the
 // combine reads them).  Device-side throughout: no host synchronisation.
-int ep_experts(amoe_ctx *c, const LayerDev &L, int T, int nchunk, cudaStream_t st, StageTimer &timer,
-               bool *used_tc) {
+int ep_experts(amoe_ctx *c, const LayerDev &L, const RouteOut &r, int T, int nchunk, cudaStream_t st,
+               StageTimer &timer, bool *used_tc) {
     const Dims &d = c->d;
     const int N = c->ep_n, El = c->e_loc;
     int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H);
     if (nchunk > 1) {  // the stable permutation (one routing chunk writes it itself)
-        AMOE_CUDA(c, launch_scatter(d, T, c->r, false, nullptr, nullptr, st));
+        AMOE_CUDA(c, launch_scatter(d, T, r, false, nullptr, nullptr, st));
         c->stats.launches += 1;
     }
     EpArgs a{};
@@ -518,12 +539,12 @@ int ep_experts(amoe_ctx *c, const LayerDev &L, int T, int nchunk, cudaStream_t s
     a.limit_ns = c->ep_wait_ns;
     a.w = c->ep_w;
     a.m = c->ep_m;
-    a.counts = c->r.counts;
-    a.offsets = c->r.offsets;
-    a.topk_idx = c->r.topk_idx;
-    a.perm_pair = c->r.perm_pair;
-    a.x_hi = c->r.x_hi;
-    a.x_lo = c->r.x_lo;
+    a.counts = r.counts;
+    a.offsets = r.offsets;
+    a.topk_idx = r.topk_idx;
+    a.perm_pair = r.perm_pair;
+    a.x_hi = r.x_hi;
+    a.x_lo = r.x_lo;
     a.err = flag;
     a.path = c->cfg.path == AMOE_PATH_GEMV ? 1 : c->cfg.path == AMOE_PATH_TENSOR ? 2 : 0;
     if (a.path == 0 && !tc_supported()) a.path = 1;
@@ -572,6 +593,151 @@ int ep_experts(amoe_ctx *c, const LayerDev &L, int T, int nchunk, cudaStream_t s
     return AMOE_OK;
 }
 
+// Routing arrays of the pass over tokens [t0, t0 + T) of a call: token- and
+// pair-indexed arrays are offset into the call's arrays; the per-expert ones
+// (counts, offsets, active) are the pass's own copy.
+RouteOut route_view(const amoe_ctx *c, int t0, int pass) {
+    const Dims &d = c->d;
+    RouteOut r = c->r;
+    r.x_hi += (size_t)t0 * d.H;
+    r.x_lo += (size_t)t0 * d.H;
+    r.logits += (size_t)t0 * d.E;
+    r.topk_idx += (size_t)t0 * d.k;
+    r.topk_w += (size_t)t0 * d.k;
+    r.perm_pair += (size_t)t0 * d.k;
+    r.inv += (size_t)t0 * d.k;
+    r.hist += (size_t)(t0 / kRouteTokens) * d.E;
+    r.chunk_base += (size_t)(t0 / kRouteTokens) * d.E;
+    r.counts += (size_t)pass * d.E;
+    r.offsets += (size_t)pass * (d.E + 1);
+    r.active += (size_t)pass * (d.E + 1);
+    return r;
+}
+
+// One forward pass (arguments already validated) on stream st with routing view r.
+int forward_impl(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, float *out, int32_t *topk_idx,
+                 float *topk_w, cudaStream_t st, const RouteOut &r) {
+    int rc = AMOE_OK;
+    LayerDev L;
+    int slot = -1;
+    if (streaming(c)) {
+        rc = acquire_slot(c, layer, st, &slot);
+        if (rc) return rc;
+        L = layer_view(c->slot_dev[slot], c->blk);
+    } else {
+        L = layer_view(c->layer_dev[layer], c->blk);
+    }
+    const Dims &d = c->d;
+    StageTimer timer(c, st);
+    const int nchunk = (T + kRouteTokens - 1) / kRouteTokens;
+    bool tc = use_tensor_path(c, T);
+    // decode: routing, gate_up, down and the combine in one cooperative launch
+    const bool fused_decode = c->ep_n == 1 && !tc && decode_supported(d, T, c->cfg.device);
+    if (!fused_decode) {
+        AMOE_CUDA(c, launch_route_impl(d, L, residual, T, r, c->partial, c->arrivals, st, &timer_hook, &timer));
+        c->stats.launches += nchunk > 1 ? 2 : 1;
+    }
+    if (c->ep_n > 1) {
+        if (c->ep_broken)
+            return fail(c, AMOE_ERR_STATE, "expert-parallel group is out of step after a failed exchange; "
+                                           "recreate the contexts");
+        timer.mark(1);
+        rc = ep_experts(c, L, r, T, nchunk, st, timer, &tc);
+        if (rc) return rc;
+    } else if (!tc && nchunk > 1 && !fused_decode) {
+        AMOE_CUDA(c, launch_scatter(d, T, r, false, nullptr, nullptr, st));
+        c->stats.launches += 1;
+    }
+    bool fused = false;
+    if (c->ep_n > 1) {
+    } else if (fused_decode) {
+        timer.mark(1);
+        int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H);
+        AMOE_CUDA(c, launch_decode(d, L, r, residual, T, c->dec_scratch, c->y, out, c->dec_bar, flag,
+                                   c->cfg.device, st));
+        timer.mark(6);
+        c->stats.launches += 1;
+        fused = true;
+    } else if (tc) {
+        timer.mark(1);
+        int n = 0;
+        AMOE_CUDA(c, launch_tc_forward(d, L, r, T, c->act_hi, c->act_lo, c->y, c->tc_scratch,
+                                       c->max_tokens * d.k, st, &timer_hook, &timer, &n));
+        c->stats.launches += n;
+    } else {
+        timer.mark(1);
+        int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H);
+        GemvRows rows{r.x_hi, r.x_lo, r.perm_pair, r.offsets, r.active, nullptr,
+                      std::min(T * d.k, d.E)};
+        AMOE_CUDA(c, launch_gemv_gate_up(d, L, rows, T, c->act_hi, c->act_lo, flag, st));
+        timer.mark(2);
+        AMOE_CUDA(c, launch_gemv_down(d, L, rows, T, c->act_hi, c->act_lo, c->y, flag, st));
+        timer.mark(3);
+        c->stats.launches += 2;
+    }
+    if (!fused) {
+        const float *y = c->ep_n > 1 ? reinterpret_cast<const float *>(c->ep_win + c->ep_w.y) : c->y;
+        AMOE_CUDA(c, launch_combine(d, residual, r, y, T, out, st));
+        timer.mark(4);
+        c->stats.launches += 1;
+    }
+    timer.finish();
+    c->stats.forwards += 1;
+    c->stats.last_path = tc ? AMOE_PATH_TENSOR : AMOE_PATH_GEMV;
+    if (slot >= 0) {
+        AMOE_CUDA(c, cudaEventRecord(c->slot_free[slot], st));
+        // AirLLM-style streaming: start copying the next layer into the least
+        // recently used slot while this layer computes.
+        if (c->cfg.layers > (int)c->slot_dev.size()) {
+            const int next = (layer + 1) % c->cfg.layers;
+            int next_slot;
+            if (c->uploaded[next]) {
+                rc = acquire_slot(c, next, nullptr, &next_slot);
+                if (rc) return rc;
+            }
+        }
+    }
+    if (topk_idx)
+        AMOE_CUDA(c, cudaMemcpyAsync(topk_idx, r.topk_idx, (size_t)T * d.k * 4,
+                                     cudaMemcpyDeviceToDevice, st));
+    if (topk_w)
+        AMOE_CUDA(c, cudaMemcpyAsync(topk_w, r.topk_w, (size_t)T * d.k * 4,
+                                     cudaMemcpyDeviceToDevice, st));
+    return AMOE_OK;
+}
+
+int check_forward_args(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, const float *out) {
+    if (layer < 0 || layer >= c->cfg.layers || !c->uploaded[layer])
+        return fail(c, AMOE_ERR_STATE, "layer " + std::to_string(layer) + " is not uploaded");
+    if (T <= 0) return fail(c, AMOE_ERR_INVALID, "gptoss: prefill sequence length must be positive");
+    if (T > c->max_tokens)
+        return fail(c, AMOE_ERR_INVALID, "T " + std::to_string(T) + " exceeds max_tokens " +
+                                             std::to_string(c->max_tokens));
+    if (!residual || !out) return fail(c, AMOE_ERR_INVALID, "residual and out must not be NULL");
+    return AMOE_OK;
+}
+
+// Token slices of a host-buffer call: one pass unless the call is large enough
+// that overlapping its host copies with compute pays (>= 2048 tokens), and only
+// when every slice takes the same expert path as the whole call (so the output
+// is bit-identical to one pass: tokens are independent).  Expert-parallel calls
+// stay whole: every rank must make the same sequence of exchanges.
+std::vector<int> plan_passes(const amoe_ctx *c, int T) {
+    std::vector<int> one{T};
+    if (T < 2048 || c->ep_n > 1) return one;
+    const int target = std::max(1024, (T + kMaxIoChunks - 1) / kMaxIoChunks);
+    const int n = (T + target - 1) / target;
+    int len = (T + n - 1) / n;
+    len = (len + kRouteTokens - 1) / kRouteTokens * kRouteTokens;  // slices start on routing-chunk bounds
+    std::vector<int> passes;
+    for (int t0 = 0; t0 < T; t0 += len) passes.push_back(std::min(len, T - t0));
+    if (passes.size() < 2 || (int)passes.size() > kMaxIoChunks) return one;
+    const int smallest = *std::min_element(passes.begin(), passes.end());
+    if (use_tensor_path(c, smallest) != use_tensor_path(c, T)) return one;
+    if (decode_supported(c->d, smallest, c->cfg.device) && !use_tensor_path(c, smallest)) return one;
+    return passes;
+}
+
 }  // namespace
 
 extern "C" {
@@ -615,6 +781,14 @@ int amoe_create(const amoe_config *cfg, amoe_ctx **out) {
         if (e != cudaSuccess) { rc = cuda_fail(c, e, "cudaStreamCreate"); break; }
         e = cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking);
         if (e != cudaSuccess) { rc = cuda_fail(c, e, "cudaStreamCreate"); break; }
+        e = cudaStreamCreateWithFlags(&c->h2d_stream, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->d2h_stream, cudaStreamNonBlocking);
+        for (int i = 0; i < kMaxIoChunks && e == cudaSuccess; ++i) {
+            e = cudaEventCreateWithFlags(&c->io_in_ready[i], cudaEventDisableTiming);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->io_out_ready[i], cudaEventDisableTiming);
+        }
+        if (e == cudaSuccess) e = cudaHostAlloc(&c->h_flag, sizeof(int32_t), cudaHostAllocDefault);
+        if (e != cudaSuccess) { rc = cuda_fail(c, e, "cudaStreamCreate/cudaEventCreate/cudaHostAlloc"); break; }
         if (c->ep_n > 1) {
             std::string why;
             if (!nccl_load(&why)) { rc = fail(c, AMOE_ERR_NCCL, why); break; }
@@ -762,100 +936,13 @@ int amoe_forward_device(amoe_ctx *c, int32_t layer, const float *residual, int32
                         int32_t *topk_idx, float *topk_w, void *stream) {
     int rc = check_ctx(c);
     if (rc) return rc;
-    if (layer < 0 || layer >= c->cfg.layers || !c->uploaded[layer])
-        return fail(c, AMOE_ERR_STATE, "layer " + std::to_string(layer) + " is not uploaded");
-    if (T <= 0) return fail(c, AMOE_ERR_INVALID, "gptoss: prefill sequence length must be positive");
-    if (T > c->max_tokens)
-        return fail(c, AMOE_ERR_INVALID, "T " + std::to_string(T) + " exceeds max_tokens " +
-                                             std::to_string(c->max_tokens));
-    if (!residual || !out) return fail(c, AMOE_ERR_INVALID, "residual and out must not be NULL");
+    rc = check_forward_args(c, layer, residual, T, out);
+    if (rc) return rc;
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
-    LayerDev L;
-    int slot = -1;
-    if (streaming(c)) {
-        rc = acquire_slot(c, layer, st, &slot);
-        if (rc) return rc;
-        L = layer_view(c->slot_dev[slot], c->blk);
-    } else {
-        L = layer_view(c->layer_dev[layer], c->blk);
-    }
-    const Dims &d = c->d;
-    StageTimer timer(c, st);
-    const int nchunk = (T + kRouteTokens - 1) / kRouteTokens;
-    bool tc = use_tensor_path(c, T);
-    // decode: routing, gate_up, down and the combine in one cooperative launch
-    const bool fused_decode = c->ep_n == 1 && !tc && decode_supported(d, T, c->cfg.device);
-    if (!fused_decode) {
-        AMOE_CUDA(c, launch_route_impl(d, L, residual, T, c->r, c->partial, c->arrivals, st, &timer_hook, &timer));
-        c->stats.launches += nchunk > 1 ? 2 : 1;
-    }
-    if (c->ep_n > 1) {
-        if (c->ep_broken)
-            return fail(c, AMOE_ERR_STATE, "expert-parallel group is out of step after a failed exchange; "
-                                           "recreate the contexts");
-        timer.mark(1);
-        rc = ep_experts(c, L, T, nchunk, st, timer, &tc);
-        if (rc) return rc;
-    } else if (!tc && nchunk > 1 && !fused_decode) {
-        AMOE_CUDA(c, launch_scatter(d, T, c->r, false, nullptr, nullptr, st));
-        c->stats.launches += 1;
-    }
-    bool fused = false;
-    if (c->ep_n > 1) {
-    } else if (fused_decode) {
-        timer.mark(1);
-        int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H);
-        AMOE_CUDA(c, launch_decode(d, L, c->r, residual, T, c->dec_scratch, c->y, out, c->dec_bar, flag,
-                                   c->cfg.device, st));
-        timer.mark(6);
-        c->stats.launches += 1;
-        fused = true;
-    } else if (tc) {
-        timer.mark(1);
-        int n = 0;
-        AMOE_CUDA(c, launch_tc_forward(d, L, c->r, T, c->act_hi, c->act_lo, c->y, c->tc_scratch,
-                                       c->max_tokens * d.k, st, &timer_hook, &timer, &n));
-        c->stats.launches += n;
-    } else {
-        timer.mark(1);
-        int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H);
-        GemvRows rows{c->r.x_hi, c->r.x_lo, c->r.perm_pair, c->r.offsets, c->r.active, nullptr,
-                      std::min(T * d.k, d.E)};
-        AMOE_CUDA(c, launch_gemv_gate_up(d, L, rows, T, c->act_hi, c->act_lo, flag, st));
-        timer.mark(2);
-        AMOE_CUDA(c, launch_gemv_down(d, L, rows, T, c->act_hi, c->act_lo, c->y, flag, st));
-        timer.mark(3);
-        c->stats.launches += 2;
-    }
-    if (!fused) {
-        const float *y = c->ep_n > 1 ? reinterpret_cast<const float *>(c->ep_win + c->ep_w.y) : c->y;
-        AMOE_CUDA(c, launch_combine(d, residual, c->r, y, T, out, st));
-        timer.mark(4);
-        c->stats.launches += 1;
-    }
-    timer.finish();
-    c->stats.forwards += 1;
-    c->stats.last_path = tc ? AMOE_PATH_TENSOR : AMOE_PATH_GEMV;
-    if (slot >= 0) {
-        AMOE_CUDA(c, cudaEventRecord(c->slot_free[slot], st));
-        // AirLLM-style streaming: start copying the next layer into the least
-        // recently used slot while this layer computes.
-        if (c->cfg.layers > (int)c->slot_dev.size()) {
-            const int next = (layer + 1) % c->cfg.layers;
-            int next_slot;
-            if (c->uploaded[next]) {
-                rc = acquire_slot(c, next, nullptr, &next_slot);
-                if (rc) return rc;
-            }
-        }
-    }
-    if (topk_idx)
-        AMOE_CUDA(c, cudaMemcpyAsync(topk_idx, c->r.topk_idx, (size_t)T * d.k * 4,
-                                     cudaMemcpyDeviceToDevice, st));
-    if (topk_w)
-        AMOE_CUDA(c, cudaMemcpyAsync(topk_w, c->r.topk_w, (size_t)T * d.k * 4,
-                                     cudaMemcpyDeviceToDevice, st));
+    rc = forward_impl(c, layer, residual, T, out, topk_idx, topk_w, st, route_view(c, 0, 0));
+    if (rc) return rc;
     c->last_T = T;
+    c->last_chunks.assign(1, T);
     return AMOE_OK;
 }
 
@@ -863,25 +950,68 @@ int amoe_forward(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, f
                  int32_t *topk_idx, float *topk_w) {
     int rc = check_ctx(c);
     if (rc) return rc;
-    if (T <= 0) return fail(c, AMOE_ERR_INVALID, "gptoss: prefill sequence length must be positive");
-    if (T > c->max_tokens)
-        return fail(c, AMOE_ERR_INVALID, "T " + std::to_string(T) + " exceeds max_tokens " +
-                                             std::to_string(c->max_tokens));
-    if (!residual || !out) return fail(c, AMOE_ERR_INVALID, "residual and out must not be NULL");
-    const Dims &d = c->d;
-    cudaStream_t st = c->stream;
-    AMOE_CUDA(c, cudaMemcpyAsync(c->io_in, residual, (size_t)T * d.H * 4, cudaMemcpyHostToDevice, st));
-    rc = amoe_forward_device(c, layer, c->io_in, T, c->io_out, nullptr, nullptr, st);
+    rc = check_forward_args(c, layer, residual, T, out);
     if (rc) return rc;
-    AMOE_CUDA(c, cudaMemcpyAsync(out, c->io_out, (size_t)T * d.H * 4, cudaMemcpyDeviceToHost, st));
-    if (topk_idx)
-        AMOE_CUDA(c, cudaMemcpyAsync(topk_idx, c->r.topk_idx, (size_t)T * d.k * 4,
+    const Dims &d = c->d;
+    const size_t H = d.H, k = d.k;
+    const std::vector<int> passes = plan_passes(c, T);
+    cudaStream_t st = c->stream;
+    if (passes.size() == 1) {
+        AMOE_CUDA(c, cudaMemcpyAsync(c->io_in, residual, (size_t)T * H * 4, cudaMemcpyHostToDevice, st));
+        rc = forward_impl(c, layer, c->io_in, T, c->io_out, nullptr, nullptr, st, route_view(c, 0, 0));
+        if (rc) return rc;
+        AMOE_CUDA(c, cudaMemcpyAsync(out, c->io_out, (size_t)T * H * 4, cudaMemcpyDeviceToHost, st));
+        if (topk_idx)
+            AMOE_CUDA(c, cudaMemcpyAsync(topk_idx, c->r.topk_idx, (size_t)T * k * 4, cudaMemcpyDeviceToHost, st));
+        if (topk_w)
+            AMOE_CUDA(c, cudaMemcpyAsync(topk_w, c->r.topk_w, (size_t)T * k * 4, cudaMemcpyDeviceToHost, st));
+        AMOE_CUDA(c, cudaMemcpyAsync(c->h_flag, tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H), 4,
                                      cudaMemcpyDeviceToHost, st));
-    if (topk_w)
-        AMOE_CUDA(c, cudaMemcpyAsync(topk_w, c->r.topk_w, (size_t)T * d.k * 4,
-                                     cudaMemcpyDeviceToHost, st));
+    } else {
+        // Pipeline: every slice's rows go up on the H2D stream at once; slice i
+        // computes once its rows are in, and its outputs come down on the D2H
+        // stream while slice i+1 computes (two copy engines, both directions).
+        AMOE_CUDA(c, cudaEventRecord(c->io_out_ready[0], st));  // earlier work on the compute stream
+        AMOE_CUDA(c, cudaStreamWaitEvent(c->h2d_stream, c->io_out_ready[0], 0));
+        int t0 = 0;
+        for (size_t i = 0; i < passes.size(); ++i) {
+            AMOE_CUDA(c, cudaMemcpyAsync(c->io_in + (size_t)t0 * H, residual + (size_t)t0 * H,
+                                         (size_t)passes[i] * H * 4, cudaMemcpyHostToDevice, c->h2d_stream));
+            AMOE_CUDA(c, cudaEventRecord(c->io_in_ready[i], c->h2d_stream));
+            t0 += passes[i];
+        }
+        t0 = 0;
+        for (size_t i = 0; i < passes.size(); ++i) {
+            const int Tp = passes[i];
+            AMOE_CUDA(c, cudaStreamWaitEvent(st, c->io_in_ready[i], 0));
+            const RouteOut r = route_view(c, t0, (int)i);
+            rc = forward_impl(c, layer, c->io_in + (size_t)t0 * H, Tp, c->io_out + (size_t)t0 * H, nullptr, nullptr,
+                              st, r);
+            if (rc) {
+                cudaStreamSynchronize(c->h2d_stream);
+                cudaStreamSynchronize(st);
+                return rc;
+            }
+            AMOE_CUDA(c, cudaEventRecord(c->io_out_ready[i], st));
+            AMOE_CUDA(c, cudaStreamWaitEvent(c->d2h_stream, c->io_out_ready[i], 0));
+            AMOE_CUDA(c, cudaMemcpyAsync(out + (size_t)t0 * H, c->io_out + (size_t)t0 * H, (size_t)Tp * H * 4,
+                                         cudaMemcpyDeviceToHost, c->d2h_stream));
+            if (topk_idx)
+                AMOE_CUDA(c, cudaMemcpyAsync(topk_idx + (size_t)t0 * k, r.topk_idx, (size_t)Tp * k * 4,
+                                             cudaMemcpyDeviceToHost, c->d2h_stream));
+            if (topk_w)
+                AMOE_CUDA(c, cudaMemcpyAsync(topk_w + (size_t)t0 * k, r.topk_w, (size_t)Tp * k * 4,
+                                             cudaMemcpyDeviceToHost, c->d2h_stream));
+            t0 += Tp;
+        }
+        AMOE_CUDA(c, cudaMemcpyAsync(c->h_flag, tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H), 4,
+                                     cudaMemcpyDeviceToHost, c->d2h_stream));  // after the last pass
+        AMOE_CUDA(c, cudaStreamSynchronize(c->d2h_stream));
+    }
     AMOE_CUDA(c, cudaStreamSynchronize(st));
-    return check_device_flag(c);
+    c->last_T = T;
+    c->last_chunks = passes;
+    return check_device_flag(c, *c->h_flag);
 }
 
 int amoe_synchronize(amoe_ctx *c) {
@@ -899,14 +1029,43 @@ int amoe_last_routing(amoe_ctx *c, float *logits, int32_t *perm_pair, int32_t *c
     if (rc) return rc;
     if (c->last_T <= 0) return fail(c, AMOE_ERR_STATE, "no forward has run yet");
     const Dims &d = c->d;
-    const size_t T = c->last_T;
+    const size_t T = c->last_T, E = d.E, k = d.k;
     AMOE_CUDA(c, cudaStreamSynchronize(c->stream));
-    if (logits) AMOE_CUDA(c, cudaMemcpy(logits, c->r.logits, T * d.E * 4, cudaMemcpyDeviceToHost));
-    if (perm_pair)
-        AMOE_CUDA(c, cudaMemcpy(perm_pair, c->r.perm_pair, T * d.k * 4, cudaMemcpyDeviceToHost));
-    if (counts) AMOE_CUDA(c, cudaMemcpy(counts, c->r.counts, (size_t)d.E * 4, cudaMemcpyDeviceToHost));
-    if (offsets)
-        AMOE_CUDA(c, cudaMemcpy(offsets, c->r.offsets, (size_t)(d.E + 1) * 4, cudaMemcpyDeviceToHost));
+    if (logits) AMOE_CUDA(c, cudaMemcpy(logits, c->r.logits, T * E * 4, cudaMemcpyDeviceToHost));
+    const size_t np = c->last_chunks.size();
+    if (np <= 1) {
+        if (perm_pair) AMOE_CUDA(c, cudaMemcpy(perm_pair, c->r.perm_pair, T * k * 4, cudaMemcpyDeviceToHost));
+        if (counts) AMOE_CUDA(c, cudaMemcpy(counts, c->r.counts, E * 4, cudaMemcpyDeviceToHost));
+        if (offsets) AMOE_CUDA(c, cudaMemcpy(offsets, c->r.offsets, (E + 1) * 4, cudaMemcpyDeviceToHost));
+        return AMOE_OK;
+    }
+    // A call made in several passes: each pass sorted its own pairs; the call's
+    // stable (expert, token, slot) order is, per expert, the passes' runs in
+    // token order, with pass-local pair ids shifted by the pass's first pair.
+    std::vector<int32_t> cnt(np * E), off(np * (E + 1)), perm(T * k);
+    AMOE_CUDA(c, cudaMemcpy(cnt.data(), c->r.counts, np * E * 4, cudaMemcpyDeviceToHost));
+    AMOE_CUDA(c, cudaMemcpy(off.data(), c->r.offsets, np * (E + 1) * 4, cudaMemcpyDeviceToHost));
+    AMOE_CUDA(c, cudaMemcpy(perm.data(), c->r.perm_pair, T * k * 4, cudaMemcpyDeviceToHost));
+    std::vector<int32_t> total(E + 1, 0);
+    for (size_t e = 0; e < E; ++e) {
+        int32_t s = 0;
+        for (size_t i = 0; i < np; ++i) s += cnt[i * E + e];
+        total[e + 1] = total[e] + s;
+    }
+    if (counts)
+        for (size_t e = 0; e < E; ++e) counts[e] = total[e + 1] - total[e];
+    if (offsets) std::memcpy(offsets, total.data(), (E + 1) * 4);
+    if (perm_pair) {
+        size_t pos = 0;
+        for (size_t e = 0; e < E; ++e) {
+            size_t t0 = 0;
+            for (size_t i = 0; i < np; ++i) {
+                const int32_t *o = &off[i * (E + 1)];
+                for (int32_t j = o[e]; j < o[e + 1]; ++j) perm_pair[pos++] = perm[t0 * k + j] + (int32_t)(t0 * k);
+                t0 += c->last_chunks[i];
+            }
+        }
+    }
     return AMOE_OK;
 }
 

@@ -533,7 +533,7 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        dist.barrier()  # no rank frees its window while a peer may still store into it
+        dist.barrier()  # ranks leave together
     blk.close()
     if world > 1:
         dist.destroy_process_group()

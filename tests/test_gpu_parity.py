@@ -220,3 +220,30 @@ def test_streaming_slots_match_resident_layers(cuda_device):
             assert np.array_equal(h_res, h_stm)
     res.close()
     stm.close()
+
+
+@pytest.mark.parametrize("path,T,E", [(moe.PATH_AUTO, 3000, 8), (moe.PATH_GEMV, 2500, 16), (moe.PATH_TENSOR, 4100, 32)])
+def test_pipelined_host_call_matches_one_device_pass(cuda_device, path, T, E):
+    """amoe_forward splits calls of >= 2048 tokens into passes whose host copies
+    overlap the neighbouring passes' compute; every pass keeps the call's expert
+    path, so outputs, top-k and the reassembled routing equal one device pass."""
+    import torch
+
+    layer = W.small_layer(hidden=192, intermediate=128, experts=E, top_k=4, seed=T)
+    x = W.make_tokens(W.MoEShape(192, 128, E, 4), T, T)
+    blk = moe.MoEBlock.for_layer(layer, max_tokens=T, path=path)
+    blk.upload_layer(0, layer)
+    out, idx, w = blk.forward(x)  # host buffers: pipelined passes
+    routing = blk.last_routing(T)
+    xd = torch.from_numpy(x).cuda()
+    od = torch.empty_like(xd)
+    idd = torch.empty((T, 4), dtype=torch.int32, device="cuda")
+    wd = torch.empty((T, 4), dtype=torch.float32, device="cuda")
+    blk.forward_device(xd, od, topk_idx=idd, topk_w=wd)  # one pass
+    blk.synchronize()
+    routing1 = blk.last_routing(T)
+    blk.close()
+    assert np.array_equal(out, od.cpu().numpy())
+    assert np.array_equal(idx, idd.cpu().numpy()) and np.array_equal(w, wd.cpu().numpy())
+    for a, b in zip(routing, routing1):
+        assert np.array_equal(a, b)
