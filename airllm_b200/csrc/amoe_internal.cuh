@@ -193,6 +193,19 @@ cudaError_t launch_tc_experts(const Dims &d, const LayerDev &L, const int32_t *o
                               const int32_t *y_rows, int32_t *err, cudaStream_t st, StageHook hook,
                               void *hook_arg, int *launches, const EpReturn *ret = nullptr,
                               const int32_t *gate = nullptr, int gate_want = 0);
+// Block-scaled grouped GEMMs (gemm_bs.cu): gate_up(+SwiGLU) and down over
+// expert-sorted rows.  Rows come from (x_hi, x_lo) [*][H] through perm (position
+// -> pair id, token = pair / k) or, with perm NULL, by position; rows_cap bounds
+// the positions.  Outputs go to y[y_rows ? y_rows[pos] : pos][H] (with ret: the
+// source rank's y, see EpReturn).  scratch: bs_scratch_bytes(), prepared once by
+// init_bs_scratch().
+size_t bs_scratch_bytes(int rows_cap, int E, int H, int I);
+cudaError_t init_bs_scratch(void *scratch, int rows_cap, int E, int H, int I);
+cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *offsets, const __half *x_hi,
+                              const __half *x_lo, const int32_t *perm, int rows_cap, void *scratch, float *y,
+                              const int32_t *y_rows, int32_t *err, cudaStream_t st, StageHook hook, void *hook_arg,
+                              int *launches, const EpReturn *ret = nullptr, const int32_t *gate = nullptr,
+                              int gate_want = 0);
 // Per-expert exponent bias from a tiled scale plane (upload time).
 cudaError_t launch_cexp(const uint8_t *s_plane, size_t bytes_per_expert, int E, int32_t *out,
                         cudaStream_t st);

@@ -125,6 +125,7 @@ struct amoe_ctx {
     __half *act_hi = nullptr, *act_lo = nullptr;
     float *y = nullptr;
     void *tc_scratch = nullptr;
+    void *bs_scratch = nullptr;  // token tiles and the E4M3-term operands of the block-scaled GEMMs
     DecodeBarrier *dec_bar = nullptr;  // grid barrier state of the fused decode kernel
     void *dec_scratch = nullptr;       // its activation operand, partial tiles and tile counters
     float *io_in = nullptr, *io_out = nullptr;
@@ -243,6 +244,7 @@ int alloc_scratch(amoe_ctx *c) {
         {(void **)&c->act_lo, A * d.I * 2},
         {(void **)&c->y, P * d.H * 4},
         {(void **)&c->tc_scratch, tc_scratch_bytes((int)P, d.H, d.I)},
+        {(void **)&c->bs_scratch, bs_scratch_bytes((int)A, c->dx.E, d.H, d.I)},
         {(void **)&c->dec_bar, sizeof(DecodeBarrier)},
         {(void **)&c->dec_scratch, decode_scratch_bytes(d, c->cfg.device)},
         {(void **)&c->io_in, T * d.H * 4},
@@ -272,6 +274,7 @@ int alloc_scratch(amoe_ctx *c) {
     AMOE_CUDA(c, cudaMemset(c->arrivals, 0, (size_t)c->nchunk_max * 4));
     AMOE_CUDA(c, cudaMemset(c->dec_bar, 0, sizeof(DecodeBarrier)));
     AMOE_CUDA(c, init_decode_scratch(d, c->cfg.device, c->dec_scratch, nullptr));
+    AMOE_CUDA(c, init_bs_scratch(c->bs_scratch, (int)A, c->dx.E, d.H, d.I));
     AMOE_CUDA(c, cudaDeviceSynchronize());
     AMOE_CUDA(c, cudaMemset(tc_error_flag(c->tc_scratch, (int)P, d.H), 0, sizeof(int32_t)));
     if (R) {
@@ -574,7 +577,7 @@ int ep_experts(amoe_ctx *c, const LayerDev &L, const RouteOut &r, int T, int nch
     *used_tc = run_tc && (a.path == 2 || (long long)N * T * d.k >= 32LL * d.E);  // stats guess
     if (run_tc) {
         int n = 0;
-        AMOE_CUDA(c, launch_tc_experts(c->dx, L, c->ep_m.offsets_loc, rh, rl, (int)c->r_max, c->act_hi, c->act_lo,
+        AMOE_CUDA(c, launch_bs_experts(c->dx, L, c->ep_m.offsets_loc, rh, rl, nullptr, (int)c->r_max, c->bs_scratch,
                                        y_own, c->ep_m.y_rows, flag, st, &timer_hook, &timer, &n, &ret, gate, 1));
         c->stats.launches += n;
     }
@@ -660,9 +663,14 @@ int forward_impl(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, f
         fused = true;
     } else if (tc) {
         timer.mark(1);
+        if (nchunk > 1) {  // the stable permutation (one routing chunk writes it itself)
+            AMOE_CUDA(c, launch_scatter(d, T, r, false, nullptr, nullptr, st));
+            c->stats.launches += 1;
+        }
         int n = 0;
-        AMOE_CUDA(c, launch_tc_forward(d, L, r, T, c->act_hi, c->act_lo, c->y, c->tc_scratch,
-                                       c->max_tokens * d.k, st, &timer_hook, &timer, &n));
+        int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H);
+        AMOE_CUDA(c, launch_bs_experts(d, L, r.offsets, r.x_hi, r.x_lo, r.perm_pair, c->max_tokens * d.k,
+                                       c->bs_scratch, c->y, nullptr, flag, st, &timer_hook, &timer, &n));
         c->stats.launches += n;
     } else {
         timer.mark(1);

@@ -1,0 +1,520 @@
+// gemm_bs.cu -- K4/K5: the grouped expert GEMMs of prefill on the block-scaled
+// 5th-generation tensor cores (tcgen05.mma kind::mxf8f6f4.block_scale).
+//
+// Per expert e with m_e routed rows (positions offsets[e]..offsets[e+1] of the
+// expert-sorted pairs):
+//   gate_up: act = SwiGLU(W_gu . x + b_gu)   (layer.go:139-148, 175; primitives.go:138-149)
+//   down:    y   = W_dn . act + b_dn          (layer.go:179-187)
+//
+// A = the MXFP4 weights as stored: E2M1 nibbles from the box-tiled TMA planes
+//     (TMA unpacks them into the tensor core's shared-memory format) with the
+//     GGUF E8M0 bytes as the hardware block scales -- no conversion pass.
+// B = the activations as four E4M3 terms per element, x ~= sum_j q_j 2^(e0-4j)
+//     per 32-element block (e0 from the block's largest magnitude), one term per
+//     MMA column: a tile of 60 tokens is N = 240 columns, and the epilogue adds
+//     each token's four columns.  Four terms carry ~16 significant bits; the
+//     tensor core accumulates in f32.
+//
+// Tokens are tiled per expert (60 per tile, the last tile of an expert ragged),
+// and the B operand of every (tile, 128-element K box) sits in global memory as
+// one pre-swizzled 30 KB block plus its two 512-byte scale chunks, so a stage is
+// one TMA box (A) and three bulk copies.  gate_up's epilogue writes down's B
+// operand in that same form: SwiGLU, block maxima across the four epilogue warps,
+// quantization to four terms, staged in shared memory and stored as 16-byte
+// swizzled chunks.
+//
+// CTA work item = (token tile, 128-row weight tile), persistent CTAs striding
+// over items.  Roles: warps 0-3 TMA producers (stage i by warp i % 4), warp 4
+// MMA issuer and TMEM owner, warps 5-8 epilogue (TMEM lane quadrants).  TMEM:
+// two 240-column accumulators (the epilogue of one item overlaps the next
+// item's MMAs) and two 12-column scale-factor slots.  Every wait is bounded;
+// on timeout the kernel records a code in the error flag and winds down.
+#include "tc_ptx.cuh"
+
+namespace amoe {
+
+namespace {
+
+using namespace bs;
+
+constexpr int kTok = 60;                          // tokens per tile
+constexpr int kN = 4 * kTok;                      // MMA N: four E4M3 terms per token
+constexpr uint32_t kBBox = kN * 128;              // 30720: one tile's B box (K = 128), pre-swizzled
+constexpr uint32_t kBSf = 1024;                   // its scale chunks: rows 0-127, 128-239
+constexpr uint32_t kABox = 128 * 128;             // unpacked A box in shared memory
+constexpr uint32_t kAPacked = 128 * 64;           // its bytes in global memory (TMA transaction size)
+constexpr uint32_t kStageBytes = 49152;           // A | B | SFA | SFB, padded to 1 KB
+constexpr int kStages = 4;
+constexpr int kProdWarps = 4;
+constexpr int kMmaWarp = kProdWarps;
+constexpr int kEpiWarp0 = kMmaWarp + 1;
+constexpr int kThreads = (kEpiWarp0 + 4) * 32;    // 288
+constexpr uint32_t kSfCol = 2 * kN;               // TMEM column of scale-factor slot 0 (slot 1: +16)
+constexpr int kActPitch = 68;                     // gate_up epilogue staging: [60 tokens][64 pairs] f32, padded rows
+constexpr uint32_t kOutStage = kTok * kActPitch * 4;
+constexpr size_t kSmem = 1024 + kStages * kStageBytes + kOutStage + 16 * 8 + 16;
+
+static_assert(kABox + kBBox + 512 + kBSf <= kStageBytes && kStageBytes % 1024 == 0, "stage layout");
+static_assert(kSfCol + 16 + 12 <= 512, "TMEM budget");
+static_assert(kSmem <= 232448, "shared memory budget");
+
+struct BsParams {
+    const uint8_t *bq;     // [tiles][nkb][240][128] B boxes (E4M3 terms, pre-swizzled)
+    const uint8_t *bsf;    // [tiles][nkb][1024] their E8M0 chunks
+    const uint8_t *asf;    // weight scale chunks [E][nmt][nkb][512]
+    const int4 *tiles;     // [tiles] {expert, first position, tokens, 0}
+    const int32_t *ntiles;
+    const float *bias;     // [E][R], GGUF row order
+    int R, nmt, nkb;
+    int gate_up;
+    // gate_up: down's B operand
+    uint8_t *oq, *osf;
+    int onkb;
+    // down
+    float *y;
+    const int32_t *y_rows;
+    EpReturn ret;
+    int32_t *err;
+    const int32_t *gate;   // if set: nothing to do unless *gate == gate_want (path chosen on the device)
+    int gate_want;
+};
+
+// B box byte offset of (row r, 16-byte chunk c): SWIZZLE_128B, 8-row groups of 1 KB.
+__device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)r * 128u + (uint32_t)((c ^ (r & 7)) << 4); }
+
+// Scale byte of B row r (token 4i + term j), 32-element block jb of a box:
+// chunk r / 128 in the layout tcgen05.cp.32x128b.warpx4 spreads over TMEM.
+__device__ __forceinline__ uint32_t sf_at(int r, int jb) {
+    return (uint32_t)(r >> 7) * 512u + (uint32_t)(r & 31) * 16u + (uint32_t)((r & 127) >> 5) * 4u + (uint32_t)jb;
+}
+
+// Token tiles of every expert: tile t = {e, first position, tokens}.
+__global__ void __launch_bounds__(256) bs_plan_kernel(const int32_t *__restrict__ offsets, int E, int4 *tiles,
+                                                      int32_t *ntiles, int max_tiles, int32_t *err) {
+    __shared__ int start[257];
+    const int e = threadIdx.x;
+    const int cnt = e < E ? offsets[e + 1] - offsets[e] : 0;
+    const int n = (cnt + kTok - 1) / kTok;
+    if (e < 256) start[e + 1] = n;
+    __syncthreads();
+    if (e == 0) {
+        start[0] = 0;
+        for (int i = 0; i < 256; ++i) start[i + 1] += start[i];
+        *ntiles = min(start[256], max_tiles);
+        if (start[256] > max_tiles) atomicCAS(err, 0, 46);
+    }
+    __syncthreads();
+    for (int j = 0; j < n; ++j) {
+        const int t = start[e] + j;
+        if (t < max_tiles) tiles[t] = make_int4(e, offsets[e] + kTok * j, min(kTok, cnt - kTok * j), 0);
+    }
+}
+
+// The gate_up B operand: one CTA per (tile, K box), one thread per (token, 32-element
+// block).  Rows are the fp16 hi + lo split of the normalized tokens, gathered
+// through the permutation (or, with perm NULL, already by position).
+__global__ void __launch_bounds__(256) bs_quant_kernel(const __half *__restrict__ x_hi, const __half *__restrict__ x_lo,
+                                                       const int32_t *__restrict__ perm, int k, int K, int nkb,
+                                                       const int4 *__restrict__ tiles, const int32_t *ntiles,
+                                                       uint8_t *bq, uint8_t *bsf) {
+    const int t = blockIdx.x / nkb, kb = blockIdx.x - t * nkb;
+    if (t >= *ntiles || threadIdx.x >= kTok * 4) return;
+    const int4 ti = tiles[t];
+    const int i = threadIdx.x >> 2, jb = threadIdx.x & 3;
+    const int k0 = kb * 128 + jb * 32;
+    float x[32];
+    bool live = i < ti.z && k0 < K;
+    if (live) {
+        const int pos = ti.y + i;
+        const size_t row = perm ? (size_t)(perm[pos] / k) : (size_t)pos;
+        const uint4 *h = reinterpret_cast<const uint4 *>(x_hi + row * K + k0);
+        const uint4 *l = reinterpret_cast<const uint4 *>(x_lo + row * K + k0);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint4 hv = __ldg(h + c), lv = __ldg(l + c);
+            const __half2 *hh = reinterpret_cast<const __half2 *>(&hv);
+            const __half2 *ll = reinterpret_cast<const __half2 *>(&lv);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float2 a = __half22float2(hh[q]), b = __half22float2(ll[q]);
+                x[8 * c + 2 * q] = a.x + b.x;
+                x[8 * c + 2 * q + 1] = a.y + b.y;
+            }
+        }
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) amax = live ? fmaxf(amax, fabsf(x[j])) : 0.0f;
+    const int e0 = block_exp(amax);
+    uint32_t q[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) q[j] = live ? quant4(x[j], e0) : 0u;
+    uint8_t *box = bq + ((size_t)t * nkb + kb) * kBBox;
+    uint8_t *sf = bsf + ((size_t)t * nkb + kb) * kBSf;
+#pragma unroll
+    for (int term = 0; term < 4; ++term) {
+        uint32_t w[8];
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            uint32_t v = 0;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) v |= ((q[4 * g + b] >> (8 * term)) & 0xffu) << (8 * b);
+            w[g] = v;
+        }
+        const int r = 4 * i + term;
+        *reinterpret_cast<uint4 *>(box + swz(r, 2 * jb)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4 *>(box + swz(r, 2 * jb + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+        sf[sf_at(r, jb)] = live ? (uint8_t)term_scale_byte(e0, term) : (uint8_t)127;
+    }
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__global__ void __launch_bounds__(kThreads, 1)
+    bs_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, BsParams p) {
+    extern __shared__ __align__(1024) uint8_t sm_raw[];
+    if (p.gate && *p.gate != p.gate_want) return;  // the other expert path runs this step
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *ring = sm;
+    float *act_s = reinterpret_cast<float *>(ring + kStages * kStageBytes);  // gate_up SwiGLU outputs
+    uint64_t *full = reinterpret_cast<uint64_t *>(act_s + kTok * kActPitch);
+    uint64_t *empty = full + kStages;
+    uint64_t *accfull = empty + kStages;  // [2]
+    uint64_t *accempty = accfull + 2;     // [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accempty + 2);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int items = *p.ntiles * p.nmt;
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(accfull + b, 1);
+            mbar_init(accempty + b, 128);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp < kProdWarps) {
+        // ---------------- TMA producers ----------------
+        if (lane == 0) {
+            int i = 0;
+            bool ok = true;
+            for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
+                const int t = w / p.nmt, m = w - t * p.nmt;
+                const int e = p.tiles[t].x;
+                for (int kb = 0; kb < p.nkb; ++kb, ++i) {
+                    if (i % kProdWarps != warp) continue;
+                    const int s = i % kStages;
+                    if (i >= kStages && !mbar_wait(empty + s, ((i / kStages) - 1) & 1, p.err, 40)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *st = ring + (size_t)s * kStageBytes;
+                    const int box = (e * p.nmt + m) * p.nkb + kb;  // box-tiled plane: row origin 128 * box
+                    const size_t bb = (size_t)t * p.nkb + kb;
+                    mbar_expect_tx(full + s, kAPacked + kBBox + 512 + kBSf);
+                    tma_2d(st, &tm_a, full + s, 0, box * 128);
+                    bulk_g2s(st + kABox, p.bq + bb * kBBox, kBBox, full + s);
+                    bulk_g2s(st + kABox + kBBox, p.asf + (size_t)box * 512, 512, full + s);
+                    bulk_g2s(st + kABox + kBBox + 512, p.bsf + bb * kBSf, kBSf, full + s);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == kMmaWarp) {
+        // ---------------- MMA issuer ----------------
+        uint32_t elected;
+        asm volatile("{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}" : "=r"(elected));
+        uint32_t idesc[4];
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) idesc[kk] = idesc_bs(kk, kN);
+        const uint32_t ring_a = smem_u32(ring);
+        int i = 0, it = 0;
+        bool ok = true;
+        for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++it) {
+            const int buf = it & 1;
+            if (!mbar_wait(accempty + buf, ((it >> 1) & 1) ^ 1, p.err, 41)) break;
+            tc_fence_after();
+            const uint32_t d = tmem + (uint32_t)(buf * kN);
+            for (int kb = 0; kb < p.nkb; ++kb, ++i) {
+                const int s = i % kStages;
+                // scale-factor slot i % 2 is free once the MMAs of iteration i - 2 completed
+                if (!mbar_wait(full + s, (i / kStages) & 1, p.err, 42) ||
+                    (i >= 2 && !mbar_wait(empty + (i - 2) % kStages, ((i - 2) / kStages) & 1, p.err, 43))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t st = ring_a + (uint32_t)s * kStageBytes;
+                const uint32_t sf = tmem + kSfCol + 16u * (uint32_t)(i & 1);
+                if (elected) {
+                    sf_copy(sf, st + kABox + kBBox);                 // A scales
+                    sf_copy(sf + 4, st + kABox + kBBox + 512);       // B scales, rows 0-127
+                    sf_copy(sf + 8, st + kABox + kBBox + 512 + 512); // rows 128-239
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_bs(d, desc_sw128(st + 32 * kk), desc_sw128(st + kABox + 32 * kk), idesc[kk],
+                                (kb | kk) ? 1u : 0u, sf, sf + 4);
+                    umma_commit(empty + s);
+                }
+                __syncwarp();
+            }
+            if (!ok) break;
+            if (elected) umma_commit(accfull + buf);
+            __syncwarp();
+        }
+    } else {
+        // ---------------- epilogue (warps 5-8; TMEM lane quadrant = warp % 4) ----------------
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;  // row of the 128-row weight tile
+        const int et = tid - kEpiWarp0 * 32;
+        int it = 0;
+        bool ok = true;
+        for (int w = blockIdx.x; w < items; w += gridDim.x, ++it) {
+            const int t = w / p.nmt, m = w - t * p.nmt;
+            const int4 ti = p.tiles[t];
+            const int e = ti.x;
+            const int buf = it & 1;
+            float v[kTok];
+            if (ok) ok = mbar_wait(accfull + buf, (it >> 1) & 1, p.err, 44);
+            if (ok) {
+                tc_fence_after();
+                const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * kN);
+#pragma unroll
+                for (int g = 0; g < kN / 32; ++g) {  // 8 tokens per load
+                    float r32[32];
+                    tmem_ld32(ta + 32u * g, r32);
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        v[8 * g + u] = ((r32[4 * u] + r32[4 * u + 1]) + r32[4 * u + 2]) + r32[4 * u + 3];
+                }
+                {
+                    float r16[16];
+                    tmem_ld16(ta + 32u * (kN / 32), r16);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        v[8 * (kN / 32) + u] = ((r16[4 * u] + r16[4 * u + 1]) + r16[4 * u + 2]) + r16[4 * u + 3];
+                }
+                tc_fence_before();
+                mbar_arrive(accempty + buf);
+            } else {
+#pragma unroll
+                for (int c = 0; c < kTok; ++c) v[c] = 0.0f;
+            }
+            if (!p.gate_up) {
+                const int h = 128 * m + row;
+                if (ok && h < p.R) {
+                    const float bias = p.bias[(size_t)e * p.R + h];
+#pragma unroll
+                    for (int c = 0; c < kTok; ++c)
+                        if (c < ti.z) ep_out_row(p.y, p.y_rows, p.ret, ti.y + c, p.R)[h] = v[c] + bias;
+                }
+                continue;
+            }
+            // gate_up: rows 16g + j (j < 8) hold the gate of pair 8g + j, row + 8 its up row
+            const int j16 = row & 15;
+            const bool gate_lane = j16 < 8;
+            const int pl = 8 * (row >> 4) + (j16 & 7);  // pair within this tile (0..63)
+            const float bias = p.bias[(size_t)e * p.R + 2 * (64 * m + pl) + (gate_lane ? 0 : 1)];
+#pragma unroll
+            for (int c = 0; c < kTok; ++c) {
+                const float val = v[c] + bias;
+                const float up = __shfl_down_sync(0xffffffffu, val, 8);
+                if (gate_lane) act_s[c * kActPitch + pl] = swiglu(val, up);
+            }
+            epi_bar();
+            // one thread per (token, 32-pair block): block maximum, four E4M3 terms, their
+            // scales, written into down's B box (pairs 64(m%2).. of box m/2)
+            if (et < 2 * kTok) {
+                const int c = et >> 1, b = et & 1;
+                const float4 *src = reinterpret_cast<const float4 *>(act_s + c * kActPitch + 32 * b);
+                float x[32];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float4 f = src[q];
+                    x[4 * q] = f.x;
+                    x[4 * q + 1] = f.y;
+                    x[4 * q + 2] = f.z;
+                    x[4 * q + 3] = f.w;
+                }
+                float amax = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(x[j]));
+                const int e0 = block_exp(amax);
+                uint32_t q4[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) q4[j] = quant4(x[j], e0);
+                const size_t ob = (size_t)t * p.onkb + (m >> 1);
+                uint8_t *box = p.oq + ob * kBBox;
+                uint8_t *sf = p.osf + ob * kBSf;
+                const int chunk = 4 * (m & 1) + 2 * b, jb = 2 * (m & 1) + b;
+#pragma unroll
+                for (int term = 0; term < 4; ++term) {
+                    uint32_t w[8];
+#pragma unroll
+                    for (int g = 0; g < 8; ++g) {
+                        uint32_t u = 0;
+#pragma unroll
+                        for (int y = 0; y < 4; ++y) u |= ((q4[4 * g + y] >> (8 * term)) & 0xffu) << (8 * y);
+                        w[g] = u;
+                    }
+                    const int r = 4 * c + term;
+                    *reinterpret_cast<uint4 *>(box + swz(r, chunk)) = make_uint4(w[0], w[1], w[2], w[3]);
+                    *reinterpret_cast<uint4 *>(box + swz(r, chunk + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+                    sf[sf_at(r, jb)] = (uint8_t)term_scale_byte(e0, term);
+                }
+            }
+            epi_bar();  // act_s is rewritten by the next item
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+    }
+    ep_return_done(p.ret);  // expert-parallel down: outputs are in the source ranks' windows
+}
+
+}  // namespace
+
+// ---- host side ------------------------------------------------------------------
+
+namespace {
+
+struct BsScratch {
+    int4 *tiles;
+    int32_t *ntiles;
+    uint8_t *xq, *xsf, *aq, *asf;
+    int max_tiles;
+};
+
+inline size_t up1k(size_t v) { return (v + 1023) & ~size_t(1023); }
+
+BsScratch carve_bs(void *base, int rows_cap, int E, int H, int I) {
+    BsScratch s{};
+    s.max_tiles = (rows_cap + kTok - 1) / kTok + E;
+    const size_t nkb_gu = kpad128(H) / 128, nkb_dn = kpad128(I) / 128;
+    uint8_t *p = static_cast<uint8_t *>(base);
+    size_t off = 0;
+    s.tiles = reinterpret_cast<int4 *>(p + off);
+    off = up1k(off + (size_t)s.max_tiles * sizeof(int4));
+    s.ntiles = reinterpret_cast<int32_t *>(p + off);
+    off = up1k(off + 16);
+    s.xq = p + off;
+    off = up1k(off + (size_t)s.max_tiles * nkb_gu * kBBox);
+    s.xsf = p + off;
+    off = up1k(off + (size_t)s.max_tiles * nkb_gu * kBSf);
+    s.aq = p + off;
+    off = up1k(off + (size_t)s.max_tiles * nkb_dn * kBBox);
+    s.asf = p + off;
+    return s;
+}
+
+}  // namespace
+
+size_t bs_scratch_bytes(int rows_cap, int E, int H, int I) {
+    const size_t max_tiles = (size_t)(rows_cap + kTok - 1) / kTok + E;
+    const size_t nkb_gu = kpad128(H) / 128, nkb_dn = kpad128(I) / 128;
+    return up1k(max_tiles * sizeof(int4)) + 1024 + up1k(max_tiles * nkb_gu * kBBox) + up1k(max_tiles * nkb_gu * kBSf) +
+           up1k(max_tiles * nkb_dn * kBBox) + up1k(max_tiles * nkb_dn * kBSf);
+}
+
+cudaError_t init_bs_scratch(void *scratch, int rows_cap, int E, int H, int I) {
+    // down's B operand: bytes no gate_up tile writes (K padding past I) must read as
+    // zero terms with a unit scale
+    const BsScratch s = carve_bs(scratch, rows_cap, E, H, I);
+    const size_t nkb_dn = kpad128(I) / 128;
+    cudaError_t e = cudaMemset(s.aq, 0, (size_t)s.max_tiles * nkb_dn * kBBox);
+    if (e == cudaSuccess) e = cudaMemset(s.asf, 127, (size_t)s.max_tiles * nkb_dn * kBSf);
+    return e;
+}
+
+cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *offsets, const __half *x_hi,
+                              const __half *x_lo, const int32_t *perm, int rows_cap, void *scratch, float *y,
+                              const int32_t *y_rows, int32_t *err, cudaStream_t st, StageHook hook, void *hook_arg,
+                              int *launches, const EpReturn *ret, const int32_t *gate, int gate_want) {
+    if (!get_encode()) return cudaErrorNotSupported;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(bs_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+    const BsScratch s = carve_bs(scratch, rows_cap, d.E, d.H, d.I);
+    const int nkb_gu = kpad128(d.H) / 128, nkb_dn = kpad128(d.I) / 128;
+    const int nmt_gu = (2 * d.I + 127) / 128, nmt_dn = (d.H + 127) / 128;
+    *launches = 0;
+    // 1. token tiles, then the gate_up B operand
+    bs_plan_kernel<<<1, 256, 0, st>>>(offsets, d.E, s.tiles, s.ntiles, s.max_tiles, err);
+    bs_quant_kernel<<<s.max_tiles * nkb_gu, 256, 0, st>>>(x_hi, x_lo, perm, d.k, d.H, nkb_gu, s.tiles, s.ntiles,
+                                                         s.xq, s.xsf);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    *launches += 2;
+    if (hook) hook(hook_arg, 5);
+    // 2. gate_up + SwiGLU, writing down's B operand
+    CUtensorMap tm_gu, tm_dn;
+    e = map_boxes(&tm_gu, L.gu_tq, tq_bytes(d.E, 2 * d.I, d.H) / 64);
+    if (e == cudaSuccess) e = map_boxes(&tm_dn, L.dn_tq, tq_bytes(d.E, d.H, d.I) / 64);
+    if (e != cudaSuccess) return e;
+    BsParams p{};
+    p.tiles = s.tiles;
+    p.ntiles = s.ntiles;
+    p.err = err;
+    p.gate = gate;
+    p.gate_want = gate_want;
+    p.bq = s.xq;
+    p.bsf = s.xsf;
+    p.asf = L.gu_tsf;
+    p.bias = L.gu_b;
+    p.R = 2 * d.I;
+    p.nmt = nmt_gu;
+    p.nkb = nkb_gu;
+    p.gate_up = 1;
+    p.oq = s.aq;
+    p.osf = s.asf;
+    p.onkb = nkb_dn;
+    bs_gemm_kernel<<<sms, kThreads, kSmem, st>>>(tm_gu, p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    ++*launches;
+    if (hook) hook(hook_arg, 2);
+    // 3. down
+    p.bq = s.aq;
+    p.bsf = s.asf;
+    p.asf = L.dn_tsf;
+    p.bias = L.dn_b;
+    p.R = d.H;
+    p.nmt = nmt_dn;
+    p.nkb = nkb_dn;
+    p.gate_up = 0;
+    p.oq = nullptr;
+    p.osf = nullptr;
+    p.y = y;
+    p.y_rows = y_rows;
+    if (ret) p.ret = *ret;
+    bs_gemm_kernel<<<sms, kThreads, kSmem, st>>>(tm_dn, p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    ++*launches;
+    if (hook) hook(hook_arg, 3);
+    return cudaSuccess;
+}
+
+}  // namespace amoe
