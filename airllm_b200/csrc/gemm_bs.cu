@@ -27,7 +27,8 @@
 // over items.  Roles: warps 0-3 TMA producers (stage i by warp i % 4), warp 4
 // MMA issuer and TMEM owner, warps 5-8 epilogue (TMEM lane quadrants).  TMEM:
 // two 240-column accumulators (the epilogue of one item overlaps the next
-// item's MMAs) and two 12-column scale-factor slots.  Every wait is bounded;
+// item's MMAs) and two 12-column scale-factor slots.  Eight epilogue warps: two
+// per TMEM lane quadrant, splitting the tile's tokens.  Every wait is bounded;
 // on timeout the kernel records a code in the error flag and winds down.
 #include "tc_ptx.cuh"
 
@@ -48,7 +49,9 @@ constexpr int kStages = 4;
 constexpr int kProdWarps = 4;
 constexpr int kMmaWarp = kProdWarps;
 constexpr int kEpiWarp0 = kMmaWarp + 1;
-constexpr int kThreads = (kEpiWarp0 + 4) * 32;    // 288
+constexpr int kEpiWarps = 8;                      // two per TMEM lane quadrant (token halves 0-31, 32-59)
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 416
 constexpr uint32_t kSfCol = 2 * kN;               // TMEM column of scale-factor slot 0 (slot 1: +16)
 constexpr int kActPitch = 68;                     // gate_up epilogue staging: [60 tokens][64 pairs] f32, padded rows
 constexpr uint32_t kOutStage = kTok * kActPitch * 4;
@@ -168,7 +171,16 @@ __global__ void __launch_bounds__(256) bs_quant_kernel(const __half *__restrict_
     }
 }
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
+
+// GPT-OSS clamped SwiGLU (primitives.go:144-146; NaN propagates) with the fast
+// exponential and division: the result is rounded to 16 significant bits (four
+// E4M3 terms) right after, far coarser than their error.
+__device__ __forceinline__ float swiglu_fast(float gate, float up) {
+    const float g = isnan(gate) ? gate : fminf(gate, 7.0f);
+    const float u = isnan(up) ? up : fminf(fmaxf(up, -7.0f), 7.0f);
+    return __fdividef(g, 1.0f + __expf(-1.702f * g)) * (u + 1.0f);
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     bs_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, BsParams p) {
@@ -192,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(accfull + b, 1);
-            mbar_init(accempty + b, 128);
+            mbar_init(accempty + b, kEpiThreads);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -275,10 +287,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
         }
     } else {
-        // ---------------- epilogue (warps 5-8; TMEM lane quadrant = warp % 4) ----------------
+        // ---------------- epilogue (warps 5-12; TMEM lane quadrant = warp % 4) ----------------
         const int quad = warp & 3;
         const int row = quad * 32 + lane;  // row of the 128-row weight tile
         const int et = tid - kEpiWarp0 * 32;
+        const int c0 = (et >> 7) * 32;     // this warp's tokens: c0 .. c0 + 31 (the second half has 28)
         int it = 0;
         bool ok = true;
         for (int w = blockIdx.x; w < items; w += gridDim.x, ++it) {
@@ -286,39 +299,40 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int4 ti = p.tiles[t];
             const int e = ti.x;
             const int buf = it & 1;
-            float v[kTok];
+            float v[32];
+#pragma unroll
+            for (int c = 0; c < 32; ++c) v[c] = 0.0f;
             if (ok) ok = mbar_wait(accfull + buf, (it >> 1) & 1, p.err, 44);
             if (ok) {
                 tc_fence_after();
-                const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * kN);
+                const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * kN + 4 * c0);
 #pragma unroll
-                for (int g = 0; g < kN / 32; ++g) {  // 8 tokens per load
-                    float r32[32];
-                    tmem_ld32(ta + 32u * g, r32);
+                for (int g = 0; g < 4; ++g) {  // 8 tokens per load
+                    if (c0 != 0 && g == 3) {
+                        float r16[16];
+                        tmem_ld16(ta + 96u, r16);
 #pragma unroll
-                    for (int u = 0; u < 8; ++u)
-                        v[8 * g + u] = ((r32[4 * u] + r32[4 * u + 1]) + r32[4 * u + 2]) + r32[4 * u + 3];
-                }
-                {
-                    float r16[16];
-                    tmem_ld16(ta + 32u * (kN / 32), r16);
+                        for (int u = 0; u < 4; ++u)
+                            v[24 + u] = ((r16[4 * u] + r16[4 * u + 1]) + r16[4 * u + 2]) + r16[4 * u + 3];
+                    } else {
+                        float r32[32];
+                        tmem_ld32(ta + 32u * g, r32);
 #pragma unroll
-                    for (int u = 0; u < 4; ++u)
-                        v[8 * (kN / 32) + u] = ((r16[4 * u] + r16[4 * u + 1]) + r16[4 * u + 2]) + r16[4 * u + 3];
+                        for (int u = 0; u < 8; ++u)
+                            v[8 * g + u] = ((r32[4 * u] + r32[4 * u + 1]) + r32[4 * u + 2]) + r32[4 * u + 3];
+                    }
                 }
                 tc_fence_before();
                 mbar_arrive(accempty + buf);
-            } else {
-#pragma unroll
-                for (int c = 0; c < kTok; ++c) v[c] = 0.0f;
             }
+            const int nc = min(32, kTok - c0);
             if (!p.gate_up) {
                 const int h = 128 * m + row;
                 if (ok && h < p.R) {
                     const float bias = p.bias[(size_t)e * p.R + h];
 #pragma unroll
-                    for (int c = 0; c < kTok; ++c)
-                        if (c < ti.z) ep_out_row(p.y, p.y_rows, p.ret, ti.y + c, p.R)[h] = v[c] + bias;
+                    for (int c = 0; c < 32; ++c)
+                        if (c < nc && c0 + c < ti.z) ep_out_row(p.y, p.y_rows, p.ret, ti.y + c0 + c, p.R)[h] = v[c] + bias;
                 }
                 continue;
             }
@@ -328,51 +342,52 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int pl = 8 * (row >> 4) + (j16 & 7);  // pair within this tile (0..63)
             const float bias = p.bias[(size_t)e * p.R + 2 * (64 * m + pl) + (gate_lane ? 0 : 1)];
 #pragma unroll
-            for (int c = 0; c < kTok; ++c) {
+            for (int c = 0; c < 32; ++c) {
                 const float val = v[c] + bias;
                 const float up = __shfl_down_sync(0xffffffffu, val, 8);
-                if (gate_lane) act_s[c * kActPitch + pl] = swiglu(val, up);
+                if (gate_lane && c < nc) act_s[(c0 + c) * kActPitch + pl] = swiglu_fast(val, up);
             }
             epi_bar();
-            // one thread per (token, 32-pair block): block maximum, four E4M3 terms, their
-            // scales, written into down's B box (pairs 64(m%2).. of box m/2)
-            if (et < 2 * kTok) {
-                const int c = et >> 1, b = et & 1;
-                const float4 *src = reinterpret_cast<const float4 *>(act_s + c * kActPitch + 32 * b);
-                float x[32];
+            // two threads per (token, 32-pair block), 16 pairs each: block maximum, four
+            // E4M3 terms, their scales, written into down's B box (pairs 64(m%2).. of box m/2)
+            {
+                const bool live = et < 4 * kTok;  // the shuffle below runs on every lane
+                const int c = min(et >> 2, kTok - 1), b = (et >> 1) & 1, sub = et & 1;
+                const float4 *src = reinterpret_cast<const float4 *>(act_s + c * kActPitch + 32 * b + 16 * sub);
+                float x[16];
+                float amax = 0.0f;
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const float4 f = src[q];
+                for (int q = 0; q < 4; ++q) {
+                    const float4 f = live ? src[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                     x[4 * q] = f.x;
                     x[4 * q + 1] = f.y;
                     x[4 * q + 2] = f.z;
                     x[4 * q + 3] = f.w;
                 }
-                float amax = 0.0f;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(x[j]));
+                for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(x[j]));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
                 const int e0 = block_exp(amax);
-                uint32_t q4[32];
+                uint32_t q4[16];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) q4[j] = quant4(x[j], e0);
+                for (int j = 0; j < 16; ++j) q4[j] = quant4(x[j], e0);
                 const size_t ob = (size_t)t * p.onkb + (m >> 1);
                 uint8_t *box = p.oq + ob * kBBox;
                 uint8_t *sf = p.osf + ob * kBSf;
-                const int chunk = 4 * (m & 1) + 2 * b, jb = 2 * (m & 1) + b;
+                const int chunk = 4 * (m & 1) + 2 * b + sub, jb = 2 * (m & 1) + b;
 #pragma unroll
                 for (int term = 0; term < 4; ++term) {
-                    uint32_t w[8];
+                    uint32_t w4[4];
 #pragma unroll
-                    for (int g = 0; g < 8; ++g) {
+                    for (int g = 0; g < 4; ++g) {
                         uint32_t u = 0;
 #pragma unroll
                         for (int y = 0; y < 4; ++y) u |= ((q4[4 * g + y] >> (8 * term)) & 0xffu) << (8 * y);
-                        w[g] = u;
+                        w4[g] = u;
                     }
                     const int r = 4 * c + term;
-                    *reinterpret_cast<uint4 *>(box + swz(r, chunk)) = make_uint4(w[0], w[1], w[2], w[3]);
-                    *reinterpret_cast<uint4 *>(box + swz(r, chunk + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
-                    sf[sf_at(r, jb)] = (uint8_t)term_scale_byte(e0, term);
+                    if (live) *reinterpret_cast<uint4 *>(box + swz(r, chunk)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    if (live && sub == 0) sf[sf_at(r, jb)] = (uint8_t)term_scale_byte(e0, term);
                 }
             }
             epi_bar();  // act_s is rewritten by the next item
