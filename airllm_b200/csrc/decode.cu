@@ -488,6 +488,9 @@ __launch_bounds__(kDecThreads, 1) __global__
 
     if (warp < kProdWarps) {
         // ---------------- producers: stage i is warp i % kProdWarps's ----------------
+        // With R >= kProdWarps stages, the wait for iteration i - R's slot comes after
+        // this warp's wait for iteration i - kProdWarps - R, so the slot's earlier
+        // phase (iteration i - 2R) has completed and the parity wait is unambiguous.
         if (lane == 0) {
             int i = 0;
             bool dead = false;
@@ -823,7 +826,9 @@ bool decode_supported(const Dims &d, int T, int device) {
     const DecodeCaps &cp = caps(device);
     if (!cp.coop || cp.sms <= 0 || cp.sms > kDecodeMaxCtas || !get_encode()) return false;
     if ((2 * d.I) % 128 || 2 * d.I / 128 > kTilesPerSlot || (d.H + 127) / 128 > kTilesPerSlot) return false;
-    return dec_stages(T, kpad128(d.H), d.E, d.k) >= 2;
+    // a ring of at least kProdWarps stages: producer warp w's waits on a slot's
+    // empty barrier then follow the phases in order (see the producers)
+    return dec_stages(T, kpad128(d.H), d.E, d.k) >= kProdWarps;
 }
 
 cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, const float *residual, int T,
@@ -866,7 +871,7 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
     p.S = S;
     p.stages = dec_stages(T, Hp, d.E, d.k);
     p.N = dec_n(T);
-    if (p.stages < 2 || !get_encode()) return cudaErrorInvalidValue;
+    if (p.stages < kProdWarps || !get_encode()) return cudaErrorInvalidValue;
     CUtensorMap tm_gu, tm_dn, tm_act;
     cudaError_t e = map_boxes(&tm_gu, L.gu_tq, tq_bytes(d.E, 2 * d.I, d.H) / 64);
     if (e == cudaSuccess) e = map_boxes(&tm_dn, L.dn_tq, tq_bytes(d.E, d.H, d.I) / 64);

@@ -17,19 +17,20 @@
 //
 // Tokens are tiled per expert (60 per tile, the last tile of an expert ragged),
 // and the B operand of every (tile, 128-element K box) sits in global memory as
-// one pre-swizzled 30 KB block plus its two 512-byte scale chunks, so a stage is
-// one TMA box (A) and three bulk copies.  gate_up's epilogue writes down's B
-// operand in that same form: SwiGLU, block maxima across the four epilogue warps,
-// quantization to four terms, staged in shared memory and stored as 16-byte
-// swizzled chunks.
+// one blob: the pre-swizzled 30 KB box, then its two 512-byte scale chunks.  A
+// stage is one TMA box (A) and two bulk copies (the blob, A's scale chunk):
+// copies issued by one warp complete one after another, so each ring slot has
+// its own producer warp.  gate_up's epilogue writes down's B operand in
+// the same form: SwiGLU, block maxima, quantization to four terms, 16-byte
+// swizzled stores.
 //
 // CTA work item = (token tile, 128-row weight tile), persistent CTAs striding
 // over items.  Roles: warps 0-3 TMA producers (stage i by warp i % 4), warp 4
-// MMA issuer and TMEM owner, warps 5-8 epilogue (TMEM lane quadrants).  TMEM:
-// two 240-column accumulators (the epilogue of one item overlaps the next
-// item's MMAs) and two 12-column scale-factor slots.  Eight epilogue warps: two
-// per TMEM lane quadrant, splitting the tile's tokens.  Every wait is bounded;
-// on timeout the kernel records a code in the error flag and winds down.
+// MMA issuer and TMEM owner, warps 5-12 epilogue (two per TMEM lane quadrant,
+// splitting the tile's tokens).  TMEM: two 240-column accumulators (the
+// epilogue of one item overlaps the next item's MMAs) and two 12-column
+// scale-factor slots.  Every wait is bounded; on timeout the kernel records a
+// code in the error flag and winds down.
 #include "tc_ptx.cuh"
 
 namespace amoe {
@@ -42,6 +43,7 @@ constexpr int kTok = 60;                          // tokens per tile
 constexpr int kN = 4 * kTok;                      // MMA N: four E4M3 terms per token
 constexpr uint32_t kBBox = kN * 128;              // 30720: one tile's B box (K = 128), pre-swizzled
 constexpr uint32_t kBSf = 1024;                   // its scale chunks: rows 0-127, 128-239
+constexpr uint32_t kBlob = kBBox + kBSf;          // box and scales, contiguous: one bulk copy
 constexpr uint32_t kABox = 128 * 128;             // unpacked A box in shared memory
 constexpr uint32_t kAPacked = 128 * 64;           // its bytes in global memory (TMA transaction size)
 constexpr uint32_t kStageBytes = 49152;           // A | B | SFA | SFB, padded to 1 KB
@@ -57,13 +59,16 @@ constexpr int kActPitch = 68;                     // gate_up epilogue staging: [
 constexpr uint32_t kOutStage = kTok * kActPitch * 4;
 constexpr size_t kSmem = 1024 + kStages * kStageBytes + kOutStage + 16 * 8 + 16;
 
-static_assert(kABox + kBBox + 512 + kBSf <= kStageBytes && kStageBytes % 1024 == 0, "stage layout");
+static_assert(kABox + kBlob + 512 <= kStageBytes && kStageBytes % 1024 == 0, "stage layout");
+// Each producer warp owns one ring slot, so its waits on that slot's empty
+// barrier are for consecutive phases (a parity wait two phases ahead would pass).
+static_assert(kProdWarps == kStages, "one producer warp per ring slot");
 static_assert(kSfCol + 16 + 12 <= 512, "TMEM budget");
 static_assert(kSmem <= 232448, "shared memory budget");
 
 struct BsParams {
-    const uint8_t *bq;     // [tiles][nkb][240][128] B boxes (E4M3 terms, pre-swizzled)
-    const uint8_t *bsf;    // [tiles][nkb][1024] their E8M0 chunks
+    const uint8_t *bq;     // [tiles][nkb] blobs: B box [240][128] (E4M3 terms, pre-swizzled), then its
+                           // two E8M0 chunks
     const uint8_t *asf;    // weight scale chunks [E][nmt][nkb][512]
     const int4 *tiles;     // [tiles] {expert, first position, tokens, 0}
     const int32_t *ntiles;
@@ -71,7 +76,7 @@ struct BsParams {
     int R, nmt, nkb;
     int gate_up;
     // gate_up: down's B operand
-    uint8_t *oq, *osf;
+    uint8_t *oq;
     int onkb;
     // down
     float *y;
@@ -119,7 +124,7 @@ __global__ void __launch_bounds__(256) bs_plan_kernel(const int32_t *__restrict_
 __global__ void __launch_bounds__(256) bs_quant_kernel(const __half *__restrict__ x_hi, const __half *__restrict__ x_lo,
                                                        const int32_t *__restrict__ perm, int k, int K, int nkb,
                                                        const int4 *__restrict__ tiles, const int32_t *ntiles,
-                                                       uint8_t *bq, uint8_t *bsf) {
+                                                       uint8_t *bq) {
     const int t = blockIdx.x / nkb, kb = blockIdx.x - t * nkb;
     if (t >= *ntiles || threadIdx.x >= kTok * 4) return;
     const int4 ti = tiles[t];
@@ -149,24 +154,24 @@ __global__ void __launch_bounds__(256) bs_quant_kernel(const __half *__restrict_
 #pragma unroll
     for (int j = 0; j < 32; ++j) amax = live ? fmaxf(amax, fabsf(x[j])) : 0.0f;
     const int e0 = block_exp(amax);
-    uint32_t q[32];
+    const TermScales ts = term_scales(e0);
+    uint32_t w[4][8];  // [term][4 elements]
 #pragma unroll
-    for (int j = 0; j < 32; ++j) q[j] = live ? quant4(x[j], e0) : 0u;
-    uint8_t *box = bq + ((size_t)t * nkb + kb) * kBBox;
-    uint8_t *sf = bsf + ((size_t)t * nkb + kb) * kBSf;
+    for (int g = 0; g < 8; ++g) {
+        uint32_t lo[4], hi[4];
+        quant4_pair(live ? x[4 * g] : 0.0f, live ? x[4 * g + 1] : 0.0f, ts, lo);
+        quant4_pair(live ? x[4 * g + 2] : 0.0f, live ? x[4 * g + 3] : 0.0f, ts, hi);
+#pragma unroll
+        for (int term = 0; term < 4; ++term) w[term][g] = (lo[term] & 0xffffu) | (hi[term] << 16);
+    }
+    uint8_t *box = bq + ((size_t)t * nkb + kb) * kBlob;
+    uint8_t *sf = box + kBBox;
 #pragma unroll
     for (int term = 0; term < 4; ++term) {
-        uint32_t w[8];
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-            uint32_t v = 0;
-#pragma unroll
-            for (int b = 0; b < 4; ++b) v |= ((q[4 * g + b] >> (8 * term)) & 0xffu) << (8 * b);
-            w[g] = v;
-        }
+        const uint32_t *wt = w[term];
         const int r = 4 * i + term;
-        *reinterpret_cast<uint4 *>(box + swz(r, 2 * jb)) = make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4 *>(box + swz(r, 2 * jb + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+        *reinterpret_cast<uint4 *>(box + swz(r, 2 * jb)) = make_uint4(wt[0], wt[1], wt[2], wt[3]);
+        *reinterpret_cast<uint4 *>(box + swz(r, 2 * jb + 1)) = make_uint4(wt[4], wt[5], wt[6], wt[7]);
         sf[sf_at(r, jb)] = live ? (uint8_t)term_scale_byte(e0, term) : (uint8_t)127;
     }
 }
@@ -235,11 +240,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint8_t *st = ring + (size_t)s * kStageBytes;
                     const int box = (e * p.nmt + m) * p.nkb + kb;  // box-tiled plane: row origin 128 * box
                     const size_t bb = (size_t)t * p.nkb + kb;
-                    mbar_expect_tx(full + s, kAPacked + kBBox + 512 + kBSf);
+                    mbar_expect_tx(full + s, kAPacked + kBlob + 512);
                     tma_2d(st, &tm_a, full + s, 0, box * 128);
-                    bulk_g2s(st + kABox, p.bq + bb * kBBox, kBBox, full + s);
-                    bulk_g2s(st + kABox + kBBox, p.asf + (size_t)box * 512, 512, full + s);
-                    bulk_g2s(st + kABox + kBBox + 512, p.bsf + bb * kBSf, kBSf, full + s);
+                    bulk_g2s(st + kABox, p.bq + bb * kBlob, kBlob, full + s);
+                    bulk_g2s(st + kABox + kBlob, p.asf + (size_t)box * 512, 512, full + s);
                 }
             }
         }
@@ -271,9 +275,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t st = ring_a + (uint32_t)s * kStageBytes;
                 const uint32_t sf = tmem + kSfCol + 16u * (uint32_t)(i & 1);
                 if (elected) {
-                    sf_copy(sf, st + kABox + kBBox);                 // A scales
-                    sf_copy(sf + 4, st + kABox + kBBox + 512);       // B scales, rows 0-127
-                    sf_copy(sf + 8, st + kABox + kBBox + 512 + 512); // rows 128-239
+                    sf_copy(sf, st + kABox + kBlob);                 // A scales
+                    sf_copy(sf + 4, st + kABox + kBBox);             // B scales, rows 0-127
+                    sf_copy(sf + 8, st + kABox + kBBox + 512);       // rows 128-239
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
                         umma_bs(d, desc_sw128(st + 32 * kk), desc_sw128(st + kABox + 32 * kk), idesc[kk],
@@ -368,25 +372,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(x[j]));
                 amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
                 const int e0 = block_exp(amax);
-                uint32_t q4[16];
+                const TermScales ts = term_scales(e0);
+                uint32_t w[4][4];  // [term][4 pairs]
 #pragma unroll
-                for (int j = 0; j < 16; ++j) q4[j] = quant4(x[j], e0);
+                for (int g = 0; g < 4; ++g) {
+                    uint32_t lo[4], hi[4];
+                    quant4_pair(x[4 * g], x[4 * g + 1], ts, lo);
+                    quant4_pair(x[4 * g + 2], x[4 * g + 3], ts, hi);
+#pragma unroll
+                    for (int term = 0; term < 4; ++term) w[term][g] = (lo[term] & 0xffffu) | (hi[term] << 16);
+                }
                 const size_t ob = (size_t)t * p.onkb + (m >> 1);
-                uint8_t *box = p.oq + ob * kBBox;
-                uint8_t *sf = p.osf + ob * kBSf;
+                uint8_t *box = p.oq + ob * kBlob;
+                uint8_t *sf = box + kBBox;
                 const int chunk = 4 * (m & 1) + 2 * b + sub, jb = 2 * (m & 1) + b;
 #pragma unroll
                 for (int term = 0; term < 4; ++term) {
-                    uint32_t w4[4];
-#pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        uint32_t u = 0;
-#pragma unroll
-                        for (int y = 0; y < 4; ++y) u |= ((q4[4 * g + y] >> (8 * term)) & 0xffu) << (8 * y);
-                        w4[g] = u;
-                    }
                     const int r = 4 * c + term;
-                    if (live) *reinterpret_cast<uint4 *>(box + swz(r, chunk)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    if (live)
+                        *reinterpret_cast<uint4 *>(box + swz(r, chunk)) = make_uint4(w[term][0], w[term][1], w[term][2], w[term][3]);
                     if (live && sub == 0) sf[sf_at(r, jb)] = (uint8_t)term_scale_byte(e0, term);
                 }
             }
@@ -411,7 +415,7 @@ namespace {
 struct BsScratch {
     int4 *tiles;
     int32_t *ntiles;
-    uint8_t *xq, *xsf, *aq, *asf;
+    uint8_t *xq, *aq;  // B blobs of gate_up (quantized tokens) and down (quantized activations)
     int max_tiles;
 };
 
@@ -428,12 +432,8 @@ BsScratch carve_bs(void *base, int rows_cap, int E, int H, int I) {
     s.ntiles = reinterpret_cast<int32_t *>(p + off);
     off = up1k(off + 16);
     s.xq = p + off;
-    off = up1k(off + (size_t)s.max_tiles * nkb_gu * kBBox);
-    s.xsf = p + off;
-    off = up1k(off + (size_t)s.max_tiles * nkb_gu * kBSf);
+    off = up1k(off + (size_t)s.max_tiles * nkb_gu * kBlob);
     s.aq = p + off;
-    off = up1k(off + (size_t)s.max_tiles * nkb_dn * kBBox);
-    s.asf = p + off;
     return s;
 }
 
@@ -442,8 +442,7 @@ BsScratch carve_bs(void *base, int rows_cap, int E, int H, int I) {
 size_t bs_scratch_bytes(int rows_cap, int E, int H, int I) {
     const size_t max_tiles = (size_t)(rows_cap + kTok - 1) / kTok + E;
     const size_t nkb_gu = kpad128(H) / 128, nkb_dn = kpad128(I) / 128;
-    return up1k(max_tiles * sizeof(int4)) + 1024 + up1k(max_tiles * nkb_gu * kBBox) + up1k(max_tiles * nkb_gu * kBSf) +
-           up1k(max_tiles * nkb_dn * kBBox) + up1k(max_tiles * nkb_dn * kBSf);
+    return up1k(max_tiles * sizeof(int4)) + 1024 + up1k(max_tiles * nkb_gu * kBlob) + up1k(max_tiles * nkb_dn * kBlob);
 }
 
 cudaError_t init_bs_scratch(void *scratch, int rows_cap, int E, int H, int I) {
@@ -451,8 +450,9 @@ cudaError_t init_bs_scratch(void *scratch, int rows_cap, int E, int H, int I) {
     // zero terms with a unit scale
     const BsScratch s = carve_bs(scratch, rows_cap, E, H, I);
     const size_t nkb_dn = kpad128(I) / 128;
-    cudaError_t e = cudaMemset(s.aq, 0, (size_t)s.max_tiles * nkb_dn * kBBox);
-    if (e == cudaSuccess) e = cudaMemset(s.asf, 127, (size_t)s.max_tiles * nkb_dn * kBSf);
+    const size_t blobs = (size_t)s.max_tiles * nkb_dn;
+    cudaError_t e = cudaMemset(s.aq, 0, blobs * kBlob);
+    if (e == cudaSuccess) e = cudaMemset2D(s.aq + kBBox, kBlob, 127, kBSf, blobs);
     return e;
 }
 
@@ -478,7 +478,7 @@ cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *o
     // 1. token tiles, then the gate_up B operand
     bs_plan_kernel<<<1, 256, 0, st>>>(offsets, d.E, s.tiles, s.ntiles, s.max_tiles, err);
     bs_quant_kernel<<<s.max_tiles * nkb_gu, 256, 0, st>>>(x_hi, x_lo, perm, d.k, d.H, nkb_gu, s.tiles, s.ntiles,
-                                                         s.xq, s.xsf);
+                                                         s.xq);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     *launches += 2;
@@ -495,7 +495,6 @@ cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *o
     p.gate = gate;
     p.gate_want = gate_want;
     p.bq = s.xq;
-    p.bsf = s.xsf;
     p.asf = L.gu_tsf;
     p.bias = L.gu_b;
     p.R = 2 * d.I;
@@ -503,7 +502,6 @@ cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *o
     p.nkb = nkb_gu;
     p.gate_up = 1;
     p.oq = s.aq;
-    p.osf = s.asf;
     p.onkb = nkb_dn;
     bs_gemm_kernel<<<sms, kThreads, kSmem, st>>>(tm_gu, p);
     e = cudaGetLastError();
@@ -512,7 +510,6 @@ cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *o
     if (hook) hook(hook_arg, 2);
     // 3. down
     p.bq = s.aq;
-    p.bsf = s.asf;
     p.asf = L.dn_tsf;
     p.bias = L.dn_b;
     p.R = d.H;
@@ -520,7 +517,6 @@ cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *o
     p.nkb = nkb_dn;
     p.gate_up = 0;
     p.oq = nullptr;
-    p.osf = nullptr;
     p.y = y;
     p.y_rows = y_rows;
     if (ret) p.ret = *ret;

@@ -210,6 +210,40 @@ static __device__ __forceinline__ uint32_t quant4(float v, int e0) {
     return out;
 }
 
+// The scales of a block's four terms (2^(e0 - 4j), clamped as in quant4) and
+// their reciprocals.
+struct TermScales {
+    float s[4], inv[4];
+};
+
+static __device__ __forceinline__ TermScales term_scales(int e0) {
+    TermScales t;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int eb = term_scale_byte(e0, j);
+        t.s[j] = __uint_as_float((uint32_t)eb << 23);
+        t.inv[j] = __uint_as_float((uint32_t)(254 - eb) << 23);
+    }
+    return t;
+}
+
+// quant4 on two elements at once (bit-identical): q[j] holds term j of a in its
+// low byte and of b in its high byte.
+static __device__ __forceinline__ void quant4_pair(float a, float b, const TermScales &t, uint32_t (&q)[4]) {
+    float r0 = a, r1 = b;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        uint16_t p;
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(p) : "f"(r1 * t.inv[j]), "f"(r0 * t.inv[j]));
+        uint32_t h;
+        asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(p));
+        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&h));
+        r0 = fmaf(-f.x, t.s[j], r0);
+        r1 = fmaf(-f.y, t.s[j], r1);
+        q[j] = p;
+    }
+}
+
 // GPT-OSS clamped SwiGLU in f32 with Go's math.Min/Max NaN semantics
 // (primitives.go:144-146): NaN propagates.
 // (value, expert) order of the reference's stable descending sort
