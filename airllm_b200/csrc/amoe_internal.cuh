@@ -55,8 +55,6 @@ struct LayerDev {
     uint8_t *dn_q = nullptr;      // [E][H/16][I/64][512]
     uint8_t *dn_s = nullptr;      // [E][H/16][I/64][32]
     float *dn_b = nullptr;        // [E][H]
-    int32_t *gu_cexp = nullptr;   // [E] power-of-two bias of the fp16 weight expansion (tcgen05 path)
-    int32_t *dn_cexp = nullptr;   // [E]
     // Block-scaled tensor-core planes (see "TMA planes" below)
     uint8_t *gu_tq = nullptr;     // [E][2I/128][Hp/128][128][64] E2M1 boxes, rows in fragment order
     uint8_t *gu_tsf = nullptr;    // [E][2I/128][Hp/128][512] E8M0 in scale-factor chunks
@@ -177,22 +175,9 @@ cudaError_t launch_gemv_down(const Dims &d, const LayerDev &L, const GemvRows &r
                              const __half *act_hi, const __half *act_lo, float *y, int32_t *err,
                              cudaStream_t st, const EpReturn *ret = nullptr);
 
-// tcgen05 grouped GEMM (prefill) -------------------------------------------------
-size_t tc_scratch_bytes(int max_pairs, int H, int I);
+// tcgen05 grouped GEMMs (prefill) -------------------------------------------------
+// True on an sm_100 device once the TMA tensor-map encoder is resolved.
 bool tc_supported();
-// Runs gate_up(+SwiGLU) and down for all pairs; *launches receives the kernel count.
-cudaError_t launch_tc_forward(const Dims &d, const LayerDev &L, const RouteOut &r, int T,
-                              __half *act_hi, __half *act_lo, float *y, void *tc_scratch,
-                              int max_pairs, cudaStream_t st, StageHook hook, void *hook_arg,
-                              int *launches);
-// The two grouped GEMMs alone, on rows that are already expert-sorted:
-// gate_up from (b_hi, b_lo) [rows_cap][H] into act [rows_cap][I], then down into
-// y[y_rows ? y_rows[pos] : pos][H] (with ret: the source rank's y, see EpReturn).
-cudaError_t launch_tc_experts(const Dims &d, const LayerDev &L, const int32_t *offsets, const __half *b_hi,
-                              const __half *b_lo, int rows_cap, __half *act_hi, __half *act_lo, float *y,
-                              const int32_t *y_rows, int32_t *err, cudaStream_t st, StageHook hook,
-                              void *hook_arg, int *launches, const EpReturn *ret = nullptr,
-                              const int32_t *gate = nullptr, int gate_want = 0);
 // Block-scaled grouped GEMMs (gemm_bs.cu): gate_up(+SwiGLU) and down over
 // expert-sorted rows.  Rows come from (x_hi, x_lo) [*][H] through perm (position
 // -> pair id, token = pair / k) or, with perm NULL, by position; rows_cap bounds
@@ -206,14 +191,6 @@ cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *o
                               const int32_t *y_rows, int32_t *err, cudaStream_t st, StageHook hook, void *hook_arg,
                               int *launches, const EpReturn *ret = nullptr, const int32_t *gate = nullptr,
                               int gate_want = 0);
-// Per-expert exponent bias from a tiled scale plane (upload time).
-cudaError_t launch_cexp(const uint8_t *s_plane, size_t bytes_per_expert, int E, int32_t *out,
-                        cudaStream_t st);
-// Device word the tcgen05 kernels set when a bounded wait gives up (0 = fine).
-int32_t *tc_error_flag(void *tc_scratch, int max_pairs, int H);
-// The expert-sorted fp16 hi/lo row buffers inside the tensor-path scratch.
-void tc_rows(void *tc_scratch, int max_pairs, int H, __half **xp_hi, __half **xp_lo);
-
 // Combine --------------------------------------------------------------------
 cudaError_t launch_combine(const Dims &d, const float *residual, const RouteOut &r,
                            const float *y, int T, float *out, cudaStream_t st);

@@ -1,7 +1,7 @@
 // ctx.cu -- the C ABI (include/amoe.h): context, weight upload, forward.
 //
-// Host-side orchestration only; the arithmetic lives in route.cu, gemv.cu,
-// combine.cu and gemm_tc.cu.  Error behaviour mirrors the reference's Go
+// Host-side orchestration only; the arithmetic lives in route.cu, decode.cu,
+// gemv.cu, gemm_bs.cu, combine.cu and ep.cu.  Error behaviour mirrors the reference's Go
 // error returns (e.g. internal/model/gptoss/layer.go:35-39, tensor.go:95-97,
 // moe.go:13-18): every failure is a negative status plus a message, never an
 // abort.
@@ -30,8 +30,7 @@ struct Status {
 
 struct LayerBlock {
     // byte offsets inside one layer's device-format block (256-B aligned parts)
-    size_t norm, router_w, router_b, gu_b, dn_b, gu_cexp, dn_cexp, gu_s, dn_s, gu_q, dn_q, gu_tsf, dn_tsf, gu_tq,
-        dn_tq, total;
+    size_t norm, router_w, router_b, gu_b, dn_b, gu_s, dn_s, gu_q, dn_q, gu_tsf, dn_tsf, gu_tq, dn_tq, total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -51,8 +50,6 @@ LayerBlock layer_block(const Dims &d, int E_x) {
     b.router_b = take((size_t)d.E * 4);
     b.gu_b = take(E * 2 * I * 4);
     b.dn_b = take(E * H * 4);
-    b.gu_cexp = take(E * 4);
-    b.dn_cexp = take(E * 4);
     b.gu_s = take(E * 2 * I * (H / 32));
     b.dn_s = take(E * H * (I / 32));
     b.gu_q = take(E * 2 * I * (H / 2));
@@ -72,8 +69,6 @@ LayerDev layer_view(uint8_t *base, const LayerBlock &b) {
     L.router_b = reinterpret_cast<float *>(base + b.router_b);
     L.gu_b = reinterpret_cast<float *>(base + b.gu_b);
     L.dn_b = reinterpret_cast<float *>(base + b.dn_b);
-    L.gu_cexp = reinterpret_cast<int32_t *>(base + b.gu_cexp);
-    L.dn_cexp = reinterpret_cast<int32_t *>(base + b.dn_cexp);
     L.gu_s = base + b.gu_s;
     L.dn_s = base + b.dn_s;
     L.gu_q = base + b.gu_q;
@@ -124,7 +119,7 @@ struct amoe_ctx {
     int32_t *arrivals = nullptr;
     __half *act_hi = nullptr, *act_lo = nullptr;
     float *y = nullptr;
-    void *tc_scratch = nullptr;
+    int32_t *err_flag = nullptr;  // set by a kernel whose bounded wait gave up (0 = fine)
     void *bs_scratch = nullptr;  // token tiles and the E4M3-term operands of the block-scaled GEMMs
     DecodeBarrier *dec_bar = nullptr;  // grid barrier state of the fused decode kernel
     void *dec_scratch = nullptr;       // its activation operand, partial tiles and tile counters
@@ -243,7 +238,7 @@ int alloc_scratch(amoe_ctx *c) {
         {(void **)&c->act_hi, A * d.I * 2},
         {(void **)&c->act_lo, A * d.I * 2},
         {(void **)&c->y, P * d.H * 4},
-        {(void **)&c->tc_scratch, tc_scratch_bytes((int)P, d.H, d.I)},
+        {(void **)&c->err_flag, 16},
         {(void **)&c->bs_scratch, bs_scratch_bytes((int)A, c->dx.E, d.H, d.I)},
         {(void **)&c->dec_bar, sizeof(DecodeBarrier)},
         {(void **)&c->dec_scratch, decode_scratch_bytes(d, c->cfg.device)},
@@ -276,7 +271,7 @@ int alloc_scratch(amoe_ctx *c) {
     AMOE_CUDA(c, init_decode_scratch(d, c->cfg.device, c->dec_scratch, nullptr));
     AMOE_CUDA(c, init_bs_scratch(c->bs_scratch, (int)A, c->dx.E, d.H, d.I));
     AMOE_CUDA(c, cudaDeviceSynchronize());
-    AMOE_CUDA(c, cudaMemset(tc_error_flag(c->tc_scratch, (int)P, d.H), 0, sizeof(int32_t)));
+    AMOE_CUDA(c, cudaMemset(c->err_flag, 0, sizeof(int32_t)));
     if (R) {
         AMOE_CUDA(c, cudaMemset(c->ep_m.status, 0, 16));
         c->ep_m.mode = c->ep_m.status + 1;
@@ -402,7 +397,7 @@ void timer_hook(void *timer, int stage) { static_cast<StageTimer *>(timer)->mark
 // `known`: the flag's value already copied to the host behind the call's work
 // (-1: read it now).
 int check_device_flag(amoe_ctx *c, int32_t known = -1) {
-    int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * c->d.k, c->d.H);
+    int32_t *flag = c->err_flag;
     int32_t v = known;
     if (v < 0) {
         cudaError_t e = cudaMemcpy(&v, flag, sizeof(v), cudaMemcpyDeviceToHost);
@@ -524,7 +519,7 @@ int ep_experts(amoe_ctx *c, const LayerDev &L, const RouteOut &r, int T, int nch
                StageTimer &timer, bool *used_tc) {
     const Dims &d = c->d;
     const int N = c->ep_n, El = c->e_loc;
-    int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H);
+    int32_t *flag = c->err_flag;
     if (nchunk > 1) {  // the stable permutation (one routing chunk writes it itself)
         AMOE_CUDA(c, launch_scatter(d, T, r, false, nullptr, nullptr, st));
         c->stats.launches += 1;
@@ -655,7 +650,7 @@ int forward_impl(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, f
     if (c->ep_n > 1) {
     } else if (fused_decode) {
         timer.mark(1);
-        int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H);
+        int32_t *flag = c->err_flag;
         AMOE_CUDA(c, launch_decode(d, L, r, residual, T, c->dec_scratch, c->y, out, c->dec_bar, flag,
                                    c->cfg.device, st));
         timer.mark(6);
@@ -668,13 +663,13 @@ int forward_impl(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, f
             c->stats.launches += 1;
         }
         int n = 0;
-        int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H);
+        int32_t *flag = c->err_flag;
         AMOE_CUDA(c, launch_bs_experts(d, L, r.offsets, r.x_hi, r.x_lo, r.perm_pair, c->max_tokens * d.k,
                                        c->bs_scratch, c->y, nullptr, flag, st, &timer_hook, &timer, &n));
         c->stats.launches += n;
     } else {
         timer.mark(1);
-        int32_t *flag = tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H);
+        int32_t *flag = c->err_flag;
         GemvRows rows{r.x_hi, r.x_lo, r.perm_pair, r.offsets, r.active, nullptr,
                       std::min(T * d.k, d.E)};
         AMOE_CUDA(c, launch_gemv_gate_up(d, L, rows, T, c->act_hi, c->act_lo, flag, st));
@@ -915,8 +910,6 @@ int amoe_upload_layer(amoe_ctx *c, int32_t layer, const float *norm_gain, const 
     UP_CUDA(cudaMemcpyAsync(staging, down + e0 * dn_expert, dn_bytes, cudaMemcpyHostToDevice, st));
     UP_CUDA(launch_repack(staging, (int)E, (int)H, (int)I, false, L.dn_q, L.dn_s, st));
     UP_CUDA(launch_repack_tma(staging, (int)E, (int)H, (int)I, false, L.dn_tq, L.dn_tsf, st));
-    UP_CUDA(launch_cexp(L.gu_s, 2 * I * (H / 32), (int)E, L.gu_cexp, st));
-    UP_CUDA(launch_cexp(L.dn_s, H * (I / 32), (int)E, L.dn_cexp, st));
     if (streaming(c)) {
         UP_CUDA(cudaMemcpyAsync(c->layer_host[layer], blockp, c->blk.total, cudaMemcpyDeviceToHost, st));
         // a slot holding a stale copy of this layer must be refilled
@@ -973,7 +966,7 @@ int amoe_forward(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, f
             AMOE_CUDA(c, cudaMemcpyAsync(topk_idx, c->r.topk_idx, (size_t)T * k * 4, cudaMemcpyDeviceToHost, st));
         if (topk_w)
             AMOE_CUDA(c, cudaMemcpyAsync(topk_w, c->r.topk_w, (size_t)T * k * 4, cudaMemcpyDeviceToHost, st));
-        AMOE_CUDA(c, cudaMemcpyAsync(c->h_flag, tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H), 4,
+        AMOE_CUDA(c, cudaMemcpyAsync(c->h_flag, c->err_flag, 4,
                                      cudaMemcpyDeviceToHost, st));
     } else {
         // Pipeline: every slice's rows go up on the H2D stream at once; slice i
@@ -1012,7 +1005,7 @@ int amoe_forward(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, f
                                              cudaMemcpyDeviceToHost, c->d2h_stream));
             t0 += Tp;
         }
-        AMOE_CUDA(c, cudaMemcpyAsync(c->h_flag, tc_error_flag(c->tc_scratch, c->max_tokens * d.k, d.H), 4,
+        AMOE_CUDA(c, cudaMemcpyAsync(c->h_flag, c->err_flag, 4,
                                      cudaMemcpyDeviceToHost, c->d2h_stream));  // after the last pass
         AMOE_CUDA(c, cudaStreamSynchronize(c->d2h_stream));
     }

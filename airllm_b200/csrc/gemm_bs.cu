@@ -439,6 +439,19 @@ BsScratch carve_bs(void *base, int rows_cap, int E, int H, int I) {
 
 }  // namespace
 
+bool tc_supported() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    static int known[64];  // per device: 0 not asked yet, 1 yes, 2 no (idempotent writes)
+    if (!known[dev]) {
+        int major = 0, minor = 0;
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+        known[dev] = major == 10 && minor == 0 && get_encode() ? 1 : 2;
+    }
+    return known[dev] == 1;
+}
+
 size_t bs_scratch_bytes(int rows_cap, int E, int H, int I) {
     const size_t max_tiles = (size_t)(rows_cap + kTok - 1) / kTok + E;
     const size_t nkb_gu = kpad128(H) / 128, nkb_dn = kpad128(I) / 128;

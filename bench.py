@@ -43,6 +43,10 @@ UNIT = "tokens/s"
 FLOP_PER_PAIR = 2 * 2880 * (2 * 2880 + 2880)  # 49,766,400
 MEASURED_PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_FILE = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+# arithmetic of each expert path (weights stay MXFP4; accumulation f32; router and softmax f64)
+DTYPE_TENSOR = "mxfp4 x e4m3 (4 terms per value) -> f32"
+DTYPE_DECODE = "mxfp4 x e4m3 (4 terms per value) -> f32"
+DTYPE_GEMV = "mxfp4 x fp16 (hi + lo) -> f32"
 FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
 
@@ -239,7 +243,7 @@ def run_streaming(args):
         "metric": "decode tokens/s, 24-layer GPT-OSS-20B-shaped MoE stack streamed from pinned host memory",
         "value": 1e3 / ms, "unit": "tokens/s", "n_gpus": 1, "steps": n, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "mxfp4 x fp16-hi/lo -> f32 (router f64)", "data": "synthetic (seeded, seed (2, layer))",
+        "dtype": DTYPE_DECODE, "data": "synthetic (seeded, seed (2, layer))",
         "config": {"workload": f"gptoss20b-moe-stream layers={L} T=1 slots=2", "config_index": 2,
                    "layer_bytes": layer_bytes, "setup_s": setup_s},
         "h2d_gbs": h2d, "h2d_bytes_per_step": L * layer_bytes,
@@ -345,7 +349,7 @@ def run_ep(args):
         "metric": f"MoE-block tokens/s, GPT-OSS-120B shape (E=128), expert parallel over {world} GPU(s)",
         "value": T / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "mxfp4 x fp16-hi/lo -> f32 (router f64)", "data": "synthetic (seeded)",
+        "dtype": DTYPE_TENSOR, "data": "synthetic (seeded)",
         "config": {"workload": f"gptoss120b-moe-ep T={T} E=128 k=4 H=I=2880 mxfp4"
                                + (" adversarial(8 hot experts on rank 0)" if cfg == 4 else ""),
                    "config_index": cfg, "tokens": T, "tokens_per_rank": Tr, "experts_per_rank": 128 // world,
@@ -488,7 +492,9 @@ def main():
     flops, bytes_ = algorithmic(cfg, T, layer, idx_host, dom)
     dom_ms = stage_avg.get(dom, float("nan"))
     pairs_per_expert = T * layer["top_k"] / layer["experts"]
-    kernel_name = {1: "gemv_kernel (mma.sync MXFP4)", 2: "tc_gemm (tcgen05)"}[st["last_path"] or 1]
+    kernel_name = {1: "gemv_kernel (mma.sync MXFP4)",
+                   2: "bs_gemm_kernel (tcgen05 kind::mxf8f6f4 block-scaled: E2M1 weights x 4-term E4M3 "
+                      "activations)"}[st["last_path"] or 1]
     if dom == "decode_experts":
         kernel_name = "decode_kernel (one cooperative launch: routing + gate_up + down + combine, tcgen05 mxf8f6f4 block-scaled)"
     traffic = None
@@ -523,7 +529,8 @@ def main():
     line = {
         "metric": METRIC_BY_CONFIG.get(cfg, METRIC), "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "mxfp4 x fp16-hi/lo -> f32 (router f64)",
+        "vs_baseline": None, "dtype": {1: DTYPE_GEMV, 2: DTYPE_TENSOR}[st["last_path"] or 1]
+        if dom != "decode_experts" else DTYPE_DECODE,
         "data": "synthetic (seeded MXFP4 weights, N(0,1) tokens)",
         "config": dict(workload_desc(cfg, T), parallelism=f"replicas x{world}"),
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
