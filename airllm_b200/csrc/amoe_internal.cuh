@@ -13,6 +13,8 @@
 #include <string>
 #include <vector>
 
+struct amoe_gguf;  // include/amoe.h: an open GGUF file (gguf.cu)
+
 namespace amoe {
 
 // ---------------------------------------------------------------------------
@@ -284,6 +286,18 @@ struct NcclApi {
 extern NcclApi g_nccl;
 // Resolves NCCL from libnccl.so.2 once; false (with a reason) if unavailable.
 bool nccl_load(std::string *err);
+
+// GGUF (gguf.cu) ---------------------------------------------------------------------
+// One layer's MoE tensors as host pointers (into the mapped file, or into the
+// buffers below when a vector was widened to f32 or split gate/up was interleaved).
+struct GgufLayer {
+    const float *norm = nullptr, *router_w = nullptr, *router_b = nullptr, *gu_b = nullptr, *dn_b = nullptr;
+    const uint8_t *gu = nullptr, *dn = nullptr;
+    std::vector<float> buf[5];
+    std::vector<uint8_t> gu_buf;
+};
+// 0, or -1 with a message in *err.
+int gguf_layer(const ::amoe_gguf *g, int layer, int H, int I, int E, GgufLayer *L, std::string *err);
 
 // Sets the message amoe_last_error(NULL) returns on the calling thread.
 void set_thread_error(const std::string &msg);

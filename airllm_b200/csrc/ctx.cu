@@ -923,6 +923,20 @@ int amoe_upload_layer(amoe_ctx *c, int32_t layer, const float *norm_gain, const 
     return AMOE_OK;
 }
 
+int amoe_upload_layer_gguf(amoe_ctx *c, const amoe_gguf *g, int32_t layer) {
+    int rc = check_ctx(c);
+    if (rc) return rc;
+    if (!g) return fail(c, AMOE_ERR_INVALID, "gguf must not be NULL");
+    if (layer < 0 || layer >= c->cfg.layers)
+        return fail(c, AMOE_ERR_INVALID, "layer " + std::to_string(layer) + " outside [0, " +
+                                             std::to_string(c->cfg.layers) + ")");
+    GgufLayer t;
+    std::string err;
+    if (gguf_layer(g, layer, c->d.H, c->d.I, c->d.E, &t, &err))
+        return fail(c, AMOE_ERR_INVALID, "gptoss: load layer " + std::to_string(layer) + ": " + err);
+    return amoe_upload_layer(c, layer, t.norm, t.router_w, t.router_b, t.gu, t.gu_b, t.dn, t.dn_b);
+}
+
 int amoe_prefetch_layer(amoe_ctx *c, int32_t layer) {
     int rc = check_ctx(c);
     if (rc) return rc;

@@ -83,7 +83,14 @@ SIGNATURES = {
     "amoe_ep_layout": (ctypes.c_int, [_i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
     "amoe_route_noalloc": (ctypes.c_int, [_i32, _i32, _i32, _i32, ctypes.c_float, _vp, _i32, _vp, _vp, _vp,
                                           _vp, _vp, _vp, _vp]),
+    "amoe_gguf_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "amoe_gguf_close": (None, [_vp]),
+    "amoe_gguf_tensor": (ctypes.c_int, [_vp, ctypes.c_char_p, _vp, _vp, _vp, _vp, _vp]),
+    "amoe_gguf_moe_config": (ctypes.c_int, [_vp, ctypes.POINTER(AmoeConfig)]),
+    "amoe_upload_layer_gguf": (ctypes.c_int, [_vp, _vp, _i32]),
 }
+
+GGUF_F32, GGUF_F16, GGUF_BF16, GGUF_MXFP4 = 0, 1, 30, 39
 
 _lib = None
 
@@ -155,6 +162,54 @@ def ep_layout(n_ranks: int, experts_per_rank: int, rank: int, table) -> dict:
     return out
 
 
+class GGUFFile:
+    """An open GGUF file (amoe_gguf_open): the tensor index and the MoE metadata of a
+    GPT-OSS model, as internal/gguf/reader.go and gptoss.go read them."""
+
+    def __init__(self, path: str):
+        self._lib = load_library()
+        h = _vp()
+        rc = self._lib.amoe_gguf_open(os.fsencode(path), ctypes.byref(h))
+        if rc != AMOE_OK:
+            raise AmoeError(rc, self._lib.amoe_last_error(None).decode())
+        self._h = h
+
+    @property
+    def handle(self):
+        return self._h
+
+    def tensor(self, name: str) -> dict:
+        """{"type", "shape", "offset", "bytes"} of one tensor (shape[0] varies fastest)."""
+        t, nd = _i32(), _i32()
+        dims = (ctypes.c_int64 * 4)()
+        off, nbytes = ctypes.c_int64(), ctypes.c_int64()
+        rc = self._lib.amoe_gguf_tensor(self._h, name.encode(), ctypes.byref(t), ctypes.byref(nd), dims,
+                                        ctypes.byref(off), ctypes.byref(nbytes))
+        if rc != AMOE_OK:
+            raise AmoeError(rc, self._lib.amoe_last_error(None).decode())
+        return {"type": t.value, "shape": [dims[i] for i in range(min(nd.value, 4))], "offset": off.value,
+                "bytes": nbytes.value}
+
+    def moe_config(self) -> dict:
+        """hidden, intermediate, experts, top_k, layers, rms_eps from the GPT-OSS metadata."""
+        cfg = AmoeConfig()
+        rc = self._lib.amoe_gguf_moe_config(self._h, ctypes.byref(cfg))
+        if rc != AMOE_OK:
+            raise AmoeError(rc, self._lib.amoe_last_error(None).decode())
+        return {k: getattr(cfg, k) for k in ("hidden", "intermediate", "experts", "top_k", "layers", "rms_eps")}
+
+    def close(self):
+        if self._h:
+            self._lib.amoe_gguf_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class MoEBlock:
     """One B200 MoE-block context (amoe_ctx): weights for `layers` layers plus scratch."""
 
@@ -213,6 +268,10 @@ class MoEBlock:
             if a.size != n:
                 raise AmoeError(AMOE_ERR_INVALID, f"tensor length {a.size}, want {n}")
         self._check(self._lib.amoe_upload_layer(self._h, index, *[a.ctypes.data for a in arrs]))
+
+    def upload_layer_gguf(self, index: int, gguf: "GGUFFile"):
+        """Layer `index` of a GGUF file into slot `index` (amoe_upload_layer_gguf)."""
+        self._check(self._lib.amoe_upload_layer_gguf(self._h, gguf.handle, index))
 
     def forward(self, residual, layer: int = 0):
         """Host-buffer forward (amoe_forward).  Returns (out, topk_idx, topk_w)."""

@@ -200,6 +200,55 @@ AMOE_API int amoe_ep_layout(int32_t n_ranks, int32_t experts_per_rank, int32_t r
                             const int32_t *table, int32_t *send_base, int32_t *offsets_loc,
                             int32_t *seg_start, int32_t *src_pos);
 
+/* ---- GGUF files ------------------------------------------------------------------
+ * GGUF tensor encodings (internal/gguf/reader.go:17-27). */
+enum {
+    AMOE_GGUF_F32 = 0,
+    AMOE_GGUF_F16 = 1,
+    AMOE_GGUF_Q4_0 = 2,
+    AMOE_GGUF_Q8_0 = 8,
+    AMOE_GGUF_Q4_K = 12,
+    AMOE_GGUF_Q5_K = 13,
+    AMOE_GGUF_Q6_K = 14,
+    AMOE_GGUF_BF16 = 30,
+    AMOE_GGUF_MXFP4 = 39
+};
+
+typedef struct amoe_gguf amoe_gguf;
+
+/* Replaces: gguf.Open (internal/gguf/reader.go:74-86, 300-410).  Maps the file
+ * read-only and parses the little-endian GGUF v2/v3 header, metadata and tensor
+ * index; rejects bad magic or version, duplicate keys or tensors, unknown value
+ * or tensor types, and any tensor whose data range passes the end of the file.
+ * Errors: AMOE_ERR_INVALID with the reason in amoe_last_error(NULL). */
+AMOE_API int amoe_gguf_open(const char *path, amoe_gguf **out);
+AMOE_API void amoe_gguf_close(amoe_gguf *g);
+
+/* Replaces: Reader.Tensor (reader.go:130-133).  One tensor of the index: its
+ * encoding (AMOE_GGUF_*), GGUF shape (dims[0] varies fastest; up to 4 entries
+ * written), absolute data offset in the file and encoded size.  Each output is
+ * nullable.  AMOE_ERR_INVALID if the tensor is absent. */
+AMOE_API int amoe_gguf_tensor(const amoe_gguf *g, const char *name, int32_t *type, int32_t *ndims,
+                              int64_t *dims, int64_t *offset, int64_t *bytes);
+
+/* Replaces: GPTOSSMetadata (internal/gguf/gptoss.go:35-95) for the MoE fields:
+ * hidden, intermediate, experts, top_k, layers and rms_eps of *cfg come from the
+ * "gptoss." or "gpt-oss." metadata (embedding_length, expert_feed_forward_length,
+ * expert_count, expert_used_count, block_count, attention.layer_norm_rms_epsilon).
+ * The other fields of *cfg are left as they are.  Nothing changes on error. */
+AMOE_API int amoe_gguf_moe_config(const amoe_gguf *g, amoe_config *cfg);
+
+/* Replaces: loadDecoderLayer's MoE tensors (internal/model/gptoss/weights.go:35-124)
+ * and the per-call readExpert (tensor.go:94-111): uploads layer `layer` of the file
+ * into slot `layer` of the context, as amoe_upload_layer does with host arrays.
+ * Reads blk.<layer>.ffn_norm.weight (or post_attention_norm.weight),
+ * ffn_gate_inp.weight/.bias, ffn_gate_up_exps.weight/.bias (or ffn_gate_exps +
+ * ffn_up_exps, interleaved into the fused row order) and ffn_down_exps.weight/.bias,
+ * with exactly the reference's GGUF shapes.  Vectors may be f32, f16 or bf16;
+ * expert weights must be MXFP4.  The expert bytes go from the mapped file to the
+ * device without a host-side decode. */
+AMOE_API int amoe_upload_layer_gguf(amoe_ctx *ctx, const amoe_gguf *g, int32_t layer);
+
 /* ABI version (AMOE_ABI_VERSION). */
 AMOE_API int amoe_abi_version(void);
 
