@@ -252,9 +252,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- MMA issuer ----------------
         uint32_t elected;
         asm volatile("{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}" : "=r"(elected));
-        uint32_t idesc[4];
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) idesc[kk] = idesc_bs(kk, kN);
         const uint32_t ring_a = smem_u32(ring);
         int i = 0, it = 0;
         bool ok = true;
@@ -263,6 +260,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!mbar_wait(accempty + buf, ((it >> 1) & 1) ^ 1, p.err, 41)) break;
             tc_fence_after();
             const uint32_t d = tmem + (uint32_t)(buf * kN);
+            // MMA N: four columns per token of the tile, rounded up to 16 (an expert's last
+            // tile is ragged; the columns past it are not computed)
+            const int ncol = min(kN, (4 * p.tiles[w / p.nmt].z + 15) & ~15);
+            uint32_t idesc[4];
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) idesc[kk] = idesc_bs(kk, ncol);
             for (int kb = 0; kb < p.nkb; ++kb, ++i) {
                 const int s = i % kStages;
                 // scale-factor slot i % 2 is free once the MMAs of iteration i - 2 completed
