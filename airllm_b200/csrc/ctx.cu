@@ -31,12 +31,15 @@ struct Status {
 struct LayerBlock {
     // byte offsets inside one layer's device-format block (256-B aligned parts)
     size_t norm, router_w, router_b, gu_b, dn_b, gu_s, dn_s, gu_q, dn_q, gu_tsf, dn_tsf, gu_tq, dn_tq, total;
+    bool frag;  // GEMV fragment tiles stored
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Dims d: router over d.E experts; experts E_x of them stored (E_x < d.E in EP mode).
-LayerBlock layer_block(const Dims &d, int E_x) {
+// The parts the tcgen05 kernels read come first; the GEMV fragment tiles (frag)
+// follow, and are left out of streamed layers (only the TMA-plane kernels run there).
+LayerBlock layer_block(const Dims &d, int E_x, bool frag) {
     LayerBlock b{};
     size_t o = 0;
     auto take = [&](size_t bytes) {
@@ -50,14 +53,17 @@ LayerBlock layer_block(const Dims &d, int E_x) {
     b.router_b = take((size_t)d.E * 4);
     b.gu_b = take(E * 2 * I * 4);
     b.dn_b = take(E * H * 4);
-    b.gu_s = take(E * 2 * I * (H / 32));
-    b.dn_s = take(E * H * (I / 32));
-    b.gu_q = take(E * 2 * I * (H / 2));
-    b.dn_q = take(E * H * (I / 2));
     b.gu_tsf = take(tsf_bytes((int)E, (int)(2 * I), (int)H));
     b.dn_tsf = take(tsf_bytes((int)E, (int)H, (int)I));
     b.gu_tq = take(tq_bytes((int)E, (int)(2 * I), (int)H));
     b.dn_tq = take(tq_bytes((int)E, (int)H, (int)I));
+    b.frag = frag;
+    if (frag) {
+        b.gu_s = take(E * 2 * I * (H / 32));
+        b.dn_s = take(E * H * (I / 32));
+        b.gu_q = take(E * 2 * I * (H / 2));
+        b.dn_q = take(E * H * (I / 2));
+    }
     b.total = o;
     return b;
 }
@@ -69,10 +75,12 @@ LayerDev layer_view(uint8_t *base, const LayerBlock &b) {
     L.router_b = reinterpret_cast<float *>(base + b.router_b);
     L.gu_b = reinterpret_cast<float *>(base + b.gu_b);
     L.dn_b = reinterpret_cast<float *>(base + b.dn_b);
-    L.gu_s = base + b.gu_s;
-    L.dn_s = base + b.dn_s;
-    L.gu_q = base + b.gu_q;
-    L.dn_q = base + b.dn_q;
+    if (b.frag) {
+        L.gu_s = base + b.gu_s;
+        L.dn_s = base + b.dn_s;
+        L.gu_q = base + b.gu_q;
+        L.dn_q = base + b.dn_q;
+    }
     L.gu_tsf = base + b.gu_tsf;
     L.dn_tsf = base + b.dn_tsf;
     L.gu_tq = base + b.gu_tq;
@@ -191,6 +199,8 @@ std::string validate(const amoe_config *c) {
         return "gpt-oss swiglu constants are fixed at alpha 1.702, limit 7";
     if (c->max_tokens < 1) return "max_tokens must be positive";
     if (c->stream_slots != 0 && c->stream_slots < 2) return "stream_slots must be 0 or >= 2";
+    if (c->stream_slots >= 2 && c->path == AMOE_PATH_GEMV)
+        return "streamed layers run on the tensor-core kernels: stream_slots needs path AUTO or TENSOR";
     if (c->ep_size < 1 || c->ep_rank < 0 || c->ep_rank >= c->ep_size)
         return "ep_rank must be in [0, ep_size)";
     if (c->ep_size > 1) {
@@ -631,6 +641,7 @@ int forward_impl(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, f
     bool tc = use_tensor_path(c, T);
     // decode: routing, gate_up, down and the combine in one cooperative launch
     const bool fused_decode = c->ep_n == 1 && !tc && decode_supported(d, T, c->cfg.device);
+    if (!c->blk.frag && !fused_decode) tc = true;  // streamed layers carry no GEMV tiles
     if (!fused_decode) {
         AMOE_CUDA(c, launch_route_impl(d, L, residual, T, r, c->partial, c->arrivals, st, &timer_hook, &timer));
         c->stats.launches += nchunk > 1 ? 2 : 1;
@@ -775,7 +786,7 @@ int amoe_create(const amoe_config *cfg, amoe_ctx **out) {
     c->ep_rank = cfg->ep_rank;
     c->e_loc = cfg->experts / cfg->ep_size;
     c->dx = Dims{cfg->hidden, cfg->intermediate, c->e_loc, cfg->top_k, cfg->rms_eps};
-    c->blk = layer_block(c->d, c->e_loc);
+    c->blk = layer_block(c->d, c->e_loc, cfg->stream_slots < 2);
     int rc = AMOE_OK;
     do {
         cudaError_t e = cudaSetDevice(cfg->device);
@@ -904,11 +915,11 @@ int amoe_upload_layer(amoe_ctx *c, int32_t layer, const float *norm_gain, const 
     UP_CUDA(cudaMemcpyAsync(L.gu_b, gate_up_b + e0 * 2 * I, E * 2 * I * 4, cudaMemcpyHostToDevice, st));
     UP_CUDA(cudaMemcpyAsync(L.dn_b, down_b + e0 * H, E * H * 4, cudaMemcpyHostToDevice, st));
     UP_CUDA(cudaMemcpyAsync(staging, gate_up + e0 * gu_expert, gu_bytes, cudaMemcpyHostToDevice, st));
-    UP_CUDA(launch_repack(staging, (int)E, (int)(2 * I), (int)H, true, L.gu_q, L.gu_s, st));
+    if (c->blk.frag) UP_CUDA(launch_repack(staging, (int)E, (int)(2 * I), (int)H, true, L.gu_q, L.gu_s, st));
     UP_CUDA(launch_repack_tma(staging, (int)E, (int)(2 * I), (int)H, true, L.gu_tq, L.gu_tsf, st));
     UP_CUDA(cudaStreamSynchronize(st));  // staging is reused for down
     UP_CUDA(cudaMemcpyAsync(staging, down + e0 * dn_expert, dn_bytes, cudaMemcpyHostToDevice, st));
-    UP_CUDA(launch_repack(staging, (int)E, (int)H, (int)I, false, L.dn_q, L.dn_s, st));
+    if (c->blk.frag) UP_CUDA(launch_repack(staging, (int)E, (int)H, (int)I, false, L.dn_q, L.dn_s, st));
     UP_CUDA(launch_repack_tma(staging, (int)E, (int)H, (int)I, false, L.dn_tq, L.dn_tsf, st));
     if (streaming(c)) {
         UP_CUDA(cudaMemcpyAsync(c->layer_host[layer], blockp, c->blk.total, cudaMemcpyDeviceToHost, st));
@@ -1128,6 +1139,7 @@ int amoe_get_stats(amoe_ctx *c, amoe_stats *out, int32_t reset) {
     AMOE_CUDA(c, cudaStreamSynchronize(c->stream));
     AMOE_CUDA(c, cudaDeviceSynchronize());
     fold_timings(c);
+    c->stats.layer_bytes = (int64_t)c->blk.total;
     *out = c->stats;
     if (reset) {
         const int32_t last = c->stats.last_path;

@@ -62,6 +62,7 @@ class AmoeStats(ctypes.Structure):
         ("timed_forwards", ctypes.c_int64),
         ("stage_ms", ctypes.c_double * AMOE_STAGES),
         ("last_path", _i32),
+        ("layer_bytes", ctypes.c_int64),
     ]
 
 
@@ -317,6 +318,7 @@ class MoEBlock:
             "launches": st.launches, "forwards": st.forwards, "timed_forwards": st.timed_forwards,
             "stage_ms": {STAGE_NAMES[i]: st.stage_ms[i] for i in range(AMOE_STAGES)},
             "last_path": st.last_path,
+            "layer_bytes": st.layer_bytes,
         }
 
     def last_routing(self, T: int):

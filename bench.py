@@ -204,11 +204,11 @@ def run_streaming(args):
     L = W.STREAM_LAYERS
     t0 = time.perf_counter()
     layers = [W.stream_layer(i) for i in range(L)]
-    blk = moe.MoEBlock.for_layer(layers[0], layers=L, max_tokens=1, stream_slots=2, path=moe.PATH_GEMV)
+    blk = moe.MoEBlock.for_layer(layers[0], layers=L, max_tokens=1, stream_slots=2, path=moe.PATH_AUTO)
     for i, layer in enumerate(layers):
         blk.upload_layer(i, layer)
     setup_s = time.perf_counter() - t0
-    layer_bytes = sum(int(np.asarray(v).nbytes) for k, v in layers[0].items() if isinstance(v, np.ndarray))
+    gguf_bytes = sum(int(np.asarray(v).nbytes) for k, v in layers[0].items() if isinstance(v, np.ndarray))
     del layers
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
@@ -238,6 +238,7 @@ def run_streaming(args):
     clk = clocks.stop()
     st = blk.stats(reset=True)
     ms = ev0.elapsed_time(ev1) / n
+    layer_bytes = int(st["layer_bytes"])  # what each layer visit copies (device format)
     h2d = L * layer_bytes / (ms / 1e3) / 1e9
     line = {
         "metric": "decode tokens/s, 24-layer GPT-OSS-20B-shaped MoE stack streamed from pinned host memory",
@@ -248,7 +249,9 @@ def run_streaming(args):
                    "layer_bytes": layer_bytes, "setup_s": setup_s},
         "h2d_gbs": h2d, "h2d_bytes_per_step": L * layer_bytes,
         "gpu_launches": int(st["launches"]), "clocks": clk,
-        "note": "every layer visit copies the whole layer (AirLLM streaming); bound by the host link",
+        "gguf_layer_bytes": gguf_bytes,
+        "note": "every layer visit copies the whole layer (AirLLM streaming): the MXFP4 box planes and scale "
+                "chunks, biases, router; bound by the host link",
     }
     print(json.dumps(line), flush=True)
     blk.close()

@@ -64,7 +64,9 @@ typedef struct amoe_config {
     int32_t max_tokens;      /* largest T passed to one forward call (sizes scratch) */
     int32_t device;          /* CUDA device ordinal */
     int32_t stream_slots;    /* 0: every layer resident in HBM.  n >= 2: weights live in
-                                pinned host memory, n device slots are filled on a copy stream */
+                                pinned host memory, n device slots are filled on a copy stream;
+                                streamed layers hold only the tensor-core planes (path AUTO or
+                                TENSOR) */
     int32_t ep_size;         /* expert-parallel group size; 1 = single GPU */
     int32_t ep_rank;         /* this process's rank in the expert-parallel group */
     const void *nccl_id;     /* 128-byte ncclUniqueId shared by the group (ep_size > 1) */
@@ -142,6 +144,7 @@ typedef struct amoe_stats {
     int64_t timed_forwards;         /* forwards with profiling on, summed in stage_ms */
     double stage_ms[AMOE_STAGES];   /* summed event time per stage (profiling on) */
     int32_t last_path;              /* AMOE_PATH_GEMV or AMOE_PATH_TENSOR of the last forward */
+    int64_t layer_bytes;            /* device-format bytes of one layer (what a streamed layer visit copies) */
 } amoe_stats;
 
 /* Turns per-stage event timing on (1) or off (0).  Timing adds event records

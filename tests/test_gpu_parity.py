@@ -198,12 +198,16 @@ def test_errors_are_status_codes(cuda_device):
     blk.close()
 
 
-def test_streaming_slots_match_resident_layers(cuda_device):
+@pytest.mark.parametrize("T,res_path", [(5, moe.PATH_TENSOR), (3, moe.PATH_AUTO)])
+def test_streaming_slots_match_resident_layers(cuda_device, T, res_path):
+    # streamed layers carry only the tensor-core planes: T <= 4 runs the fused decode
+    # kernel, larger T the block-scaled GEMMs (the resident block is pinned to the same path)
     shape = W.MoEShape(128, 128, 8, 4)
     layers = [W.make_layer(shape, 50 + i) for i in range(3)]
-    x = W.make_tokens(shape, 5, 50)
-    res = moe.MoEBlock(128, 128, 8, 4, layers=3, max_tokens=8)
+    x = W.make_tokens(shape, T, 50)
+    res = moe.MoEBlock(128, 128, 8, 4, layers=3, max_tokens=8, path=res_path)
     stm = moe.MoEBlock(128, 128, 8, 4, layers=3, max_tokens=8, stream_slots=2)
+    assert stm.stats()["layer_bytes"] < res.stats()["layer_bytes"]
     for i, L in enumerate(layers):
         res.upload_layer(i, L)
         stm.upload_layer(i, L)
