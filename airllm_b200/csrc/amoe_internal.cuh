@@ -188,8 +188,10 @@ bool tc_supported();
 // init_bs_scratch().
 size_t bs_scratch_bytes(int rows_cap, int E, int H, int I);
 cudaError_t init_bs_scratch(void *scratch, int rows_cap, int E, int H, int I);
+// scratch_e: the expert count the scratch was sized for (bs_scratch_bytes), >= d.E.
 cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *offsets, const __half *x_hi,
-                              const __half *x_lo, const int32_t *perm, int rows_cap, void *scratch, float *y,
+                              const __half *x_lo, const int32_t *perm, int rows_cap, void *scratch, int scratch_e,
+                              float *y,
                               const int32_t *y_rows, int32_t *err, cudaStream_t st, StageHook hook, void *hook_arg,
                               int *launches, const EpReturn *ret = nullptr, const int32_t *gate = nullptr,
                               int gate_want = 0);

@@ -114,6 +114,14 @@ struct amoe_ctx {
     std::vector<uint8_t *> layer_host;   // [layers] (streaming) pinned block or null
     std::vector<bool> uploaded;
     std::vector<uint8_t *> slot_dev;     // [stream_slots]
+    // stream_experts: every layer's norm and router stay resident; the routed
+    // experts of a call are copied into one compact slot
+    float *router_res = nullptr;         // [layers][H + E*H + E]: norm gain, router weight, router bias
+    uint8_t *xslot = nullptr;            // expert slot: xblk layout for xs experts
+    LayerBlock xblk{};
+    int xs = 0;
+    int32_t *h_sel = nullptr;            // pinned: offsets [E+1], then compact offsets and active [2 (xs+1)]
+    int32_t *sel_dev = nullptr;          // compact offsets [xs+1], active [xs+1]
     std::vector<int> slot_layer;
     std::vector<cudaEvent_t> slot_ready, slot_free;
     std::vector<long long> slot_used;    // LRU stamp
@@ -201,6 +209,8 @@ std::string validate(const amoe_config *c) {
     if (c->stream_slots != 0 && c->stream_slots < 2) return "stream_slots must be 0 or >= 2";
     if (c->stream_slots >= 2 && c->path == AMOE_PATH_GEMV)
         return "streamed layers run on the tensor-core kernels: stream_slots needs path AUTO or TENSOR";
+    if (c->stream_experts != 0 && c->stream_experts != 1) return "stream_experts must be 0 or 1";
+    if (c->stream_experts && c->stream_slots < 2) return "stream_experts needs stream_slots >= 2";
     if (c->ep_size < 1 || c->ep_rank < 0 || c->ep_rank >= c->ep_size)
         return "ep_rank must be in [0, ep_size)";
     if (c->ep_size > 1) {
@@ -354,6 +364,10 @@ void release(amoe_ctx *c) {
     for (auto p : c->layer_dev) if (p) cudaFree(p);
     for (auto p : c->layer_host) if (p) cudaFreeHost(p);
     for (auto p : c->slot_dev) if (p) cudaFree(p);
+    if (c->router_res) cudaFree(c->router_res);
+    if (c->xslot) cudaFree(c->xslot);
+    if (c->sel_dev) cudaFree(c->sel_dev);
+    if (c->h_sel) cudaFreeHost(c->h_sel);
     for (auto e : c->slot_ready) if (e) cudaEventDestroy(e);
     for (auto e : c->slot_free) if (e) cudaEventDestroy(e);
     if (c->scratch) cudaFree(c->scratch);
@@ -583,7 +597,7 @@ int ep_experts(amoe_ctx *c, const LayerDev &L, const RouteOut &r, int T, int nch
     if (run_tc) {
         int n = 0;
         AMOE_CUDA(c, launch_bs_experts(c->dx, L, c->ep_m.offsets_loc, rh, rl, nullptr, (int)c->r_max, c->bs_scratch,
-                                       y_own, c->ep_m.y_rows, flag, st, &timer_hook, &timer, &n, &ret, gate, 1));
+                                       c->dx.E, y_own, c->ep_m.y_rows, flag, st, &timer_hook, &timer, &n, &ret, gate, 1));
         c->stats.launches += n;
     }
     if (run_gemv) {
@@ -622,9 +636,86 @@ RouteOut route_view(const amoe_ctx *c, int t0, int pass) {
     return r;
 }
 
+// Expert streaming (stream_experts): route on the device with the layer's resident
+// norm and router, read back which experts received rows, copy only those experts
+// (box planes, scale chunks, biases) from the pinned host layer into the compact
+// slot, and run the block-scaled expert stage on them.  The compact ids keep the
+// experts' order, so the permutation and every row's arithmetic are those of the
+// whole layer.  The host waits once per call, for the routing.
+int forward_selected(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, float *out, int32_t *topk_idx,
+                     float *topk_w, cudaStream_t st, const RouteOut &r) {
+    const Dims &d = c->d;
+    const size_t H = d.H, E = d.E;
+    StageTimer timer(c, st);
+    const int nchunk = (T + kRouteTokens - 1) / kRouteTokens;
+    LayerDev Lr{};
+    float *res = c->router_res + (size_t)layer * (H + E * H + E);
+    Lr.norm_gain = res;
+    Lr.router_w = res + H;
+    Lr.router_b = res + H + E * H;
+    AMOE_CUDA(c, launch_route_impl(d, Lr, residual, T, r, c->partial, c->arrivals, st, &timer_hook, &timer));
+    c->stats.launches += nchunk > 1 ? 2 : 1;
+    if (nchunk > 1) {
+        AMOE_CUDA(c, launch_scatter(d, T, r, false, nullptr, nullptr, st));
+        c->stats.launches += 1;
+    }
+    int32_t *h_off = c->h_sel, *h_cmp = c->h_sel + E + 1;
+    AMOE_CUDA(c, cudaMemcpyAsync(h_off, r.offsets, (E + 1) * 4, cudaMemcpyDeviceToHost, st));
+    AMOE_CUDA(c, cudaStreamSynchronize(st));
+    timer.mark(1);
+    // the routed experts, ascending, into slot positions 0..n-1
+    const LayerBlock &b = c->blk, &x = c->xblk;
+    const size_t gq = tq_bytes(1, 2 * d.I, d.H), gs = tsf_bytes(1, 2 * d.I, d.H);
+    const size_t dq = tq_bytes(1, d.H, d.I), ds = tsf_bytes(1, d.H, d.I);
+    const size_t gb = (size_t)2 * d.I * 4, db = H * 4;
+    const uint8_t *host = c->layer_host[layer];
+    const int P = h_off[E];
+    int n = 0;
+    for (size_t e = 0; e < E; ++e) {
+        if (h_off[e + 1] == h_off[e]) continue;
+        const size_t j = (size_t)n;
+        struct Part {
+            size_t src, dst, bytes;
+        } parts[] = {{b.gu_tq + e * gq, x.gu_tq + j * gq, gq}, {b.gu_tsf + e * gs, x.gu_tsf + j * gs, gs},
+                     {b.dn_tq + e * dq, x.dn_tq + j * dq, dq}, {b.dn_tsf + e * ds, x.dn_tsf + j * ds, ds},
+                     {b.gu_b + e * gb, x.gu_b + j * gb, gb},    {b.dn_b + e * db, x.dn_b + j * db, db}};
+        for (const Part &q : parts)
+            AMOE_CUDA(c, cudaMemcpyAsync(c->xslot + q.dst, host + q.src, q.bytes, cudaMemcpyHostToDevice, st));
+        h_cmp[n] = h_off[e];
+        h_cmp[c->xs + 1 + n] = n;
+        ++n;
+    }
+    for (int j = n; j <= c->xs; ++j) h_cmp[j] = P;  // empty ranges past the routed experts
+    h_cmp[c->xs + 1 + c->xs] = n;
+    AMOE_CUDA(c, cudaMemcpyAsync(c->sel_dev, h_cmp, (size_t)2 * (c->xs + 1) * 4, cudaMemcpyHostToDevice, st));
+    timer.mark(5);
+    RouteOut rs = r;
+    rs.offsets = c->sel_dev;
+    rs.active = c->sel_dev + c->xs + 1;
+    const Dims dx{d.H, d.I, c->xs, d.k, d.eps};
+    LayerDev Lx = layer_view(c->xslot, x);
+    int launches = 0;
+    AMOE_CUDA(c, launch_bs_experts(dx, Lx, rs.offsets, r.x_hi, r.x_lo, r.perm_pair, c->max_tokens * d.k,
+                                   c->bs_scratch, c->dx.E, c->y, nullptr, c->err_flag, st, &timer_hook, &timer,
+                                   &launches));
+    c->stats.launches += launches;
+    AMOE_CUDA(c, launch_combine(d, residual, r, c->y, T, out, st));
+    timer.mark(4);
+    c->stats.launches += 1;
+    timer.finish();
+    c->stats.forwards += 1;
+    c->stats.last_path = AMOE_PATH_TENSOR;
+    if (topk_idx)
+        AMOE_CUDA(c, cudaMemcpyAsync(topk_idx, r.topk_idx, (size_t)T * d.k * 4, cudaMemcpyDeviceToDevice, st));
+    if (topk_w)
+        AMOE_CUDA(c, cudaMemcpyAsync(topk_w, r.topk_w, (size_t)T * d.k * 4, cudaMemcpyDeviceToDevice, st));
+    return AMOE_OK;
+}
+
 // One forward pass (arguments already validated) on stream st with routing view r.
 int forward_impl(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, float *out, int32_t *topk_idx,
                  float *topk_w, cudaStream_t st, const RouteOut &r) {
+    if (c->router_res) return forward_selected(c, layer, residual, T, out, topk_idx, topk_w, st, r);
     int rc = AMOE_OK;
     LayerDev L;
     int slot = -1;
@@ -676,7 +767,7 @@ int forward_impl(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, f
         int n = 0;
         int32_t *flag = c->err_flag;
         AMOE_CUDA(c, launch_bs_experts(d, L, r.offsets, r.x_hi, r.x_lo, r.perm_pair, c->max_tokens * d.k,
-                                       c->bs_scratch, c->y, nullptr, flag, st, &timer_hook, &timer, &n));
+                                       c->bs_scratch, c->dx.E, c->y, nullptr, flag, st, &timer_hook, &timer, &n));
         c->stats.launches += n;
     } else {
         timer.mark(1);
@@ -818,7 +909,17 @@ int amoe_create(const amoe_config *cfg, amoe_ctx **out) {
         c->layer_dev.assign(cfg->layers, nullptr);
         c->layer_host.assign(cfg->layers, nullptr);
         c->uploaded.assign(cfg->layers, false);
-        if (cfg->stream_slots >= 2) {
+        if (cfg->stream_slots >= 2 && cfg->stream_experts) {
+            const Dims &d = c->d;
+            c->xs = std::min(d.E, cfg->max_tokens * d.k);
+            c->xblk = layer_block(Dims{d.H, d.I, c->xs, d.k, d.eps}, c->xs, false);
+            const size_t per_layer = ((size_t)d.H + (size_t)d.E * d.H + d.E) * 4;
+            e = cudaMalloc(&c->router_res, per_layer * cfg->layers);
+            if (e == cudaSuccess) e = cudaMalloc(&c->xslot, c->xblk.total);
+            if (e == cudaSuccess) e = cudaMalloc(&c->sel_dev, (size_t)2 * (c->xs + 1) * 4);
+            if (e == cudaSuccess) e = cudaHostAlloc(&c->h_sel, ((size_t)d.E + 1 + 2 * (c->xs + 1)) * 4, 0);
+            if (e != cudaSuccess) { rc = cuda_fail(c, e, "expert-streaming buffers"); break; }
+        } else if (cfg->stream_slots >= 2) {
             for (int i = 0; i < cfg->stream_slots && rc == AMOE_OK; ++i) {
                 uint8_t *p = nullptr;
                 e = cudaMalloc(&p, c->blk.total);
@@ -922,6 +1023,12 @@ int amoe_upload_layer(amoe_ctx *c, int32_t layer, const float *norm_gain, const 
     if (c->blk.frag) UP_CUDA(launch_repack(staging, (int)E, (int)H, (int)I, false, L.dn_q, L.dn_s, st));
     UP_CUDA(launch_repack_tma(staging, (int)E, (int)H, (int)I, false, L.dn_tq, L.dn_tsf, st));
     if (streaming(c)) {
+        if (c->router_res) {  // expert streaming: the layer's norm and router stay on the device
+            float *dst = c->router_res + (size_t)layer * (H + E_all * H + E_all);
+            UP_CUDA(cudaMemcpyAsync(dst, L.norm_gain, H * 4, cudaMemcpyDeviceToDevice, st));
+            UP_CUDA(cudaMemcpyAsync(dst + H, L.router_w, E_all * H * 4, cudaMemcpyDeviceToDevice, st));
+            UP_CUDA(cudaMemcpyAsync(dst + H + E_all * H, L.router_b, E_all * 4, cudaMemcpyDeviceToDevice, st));
+        }
         UP_CUDA(cudaMemcpyAsync(c->layer_host[layer], blockp, c->blk.total, cudaMemcpyDeviceToHost, st));
         // a slot holding a stale copy of this layer must be refilled
         for (size_t i = 0; i < c->slot_layer.size(); ++i)
@@ -952,6 +1059,7 @@ int amoe_prefetch_layer(amoe_ctx *c, int32_t layer) {
     int rc = check_ctx(c);
     if (rc) return rc;
     if (!streaming(c)) return fail(c, AMOE_ERR_STATE, "prefetch needs stream_slots >= 2");
+    if (c->cfg.stream_experts) return AMOE_OK;  // which experts a layer needs is known only after routing
     if (layer < 0 || layer >= c->cfg.layers || !c->uploaded[layer])
         return fail(c, AMOE_ERR_STATE, "layer " + std::to_string(layer) + " is not uploaded");
     int slot;

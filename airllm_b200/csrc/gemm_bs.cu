@@ -593,7 +593,8 @@ int pair_grid(int dev) {
 }  // namespace
 
 cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *offsets, const __half *x_hi,
-                              const __half *x_lo, const int32_t *perm, int rows_cap, void *scratch, float *y,
+                              const __half *x_lo, const int32_t *perm, int rows_cap, void *scratch, int scratch_e,
+                              float *y,
                               const int32_t *y_rows, int32_t *err, cudaStream_t st, StageHook hook, void *hook_arg,
                               int *launches, const EpReturn *ret, const int32_t *gate, int gate_want) {
     if (!get_encode()) return cudaErrorNotSupported;
@@ -606,7 +607,7 @@ cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *o
     int dev = 0;
     cudaGetDevice(&dev);
     const int grid = pair_grid(dev);
-    const BsScratch s = carve_bs(scratch, rows_cap, d.E, d.H, d.I);
+    const BsScratch s = carve_bs(scratch, rows_cap, scratch_e, d.H, d.I);
     const int nkb_gu = kpad128(d.H) / 128, nkb_dn = kpad128(d.I) / 128;
     const int nmt_gu = (2 * d.I + 127) / 128, nmt_dn = (d.H + 127) / 128;
     *launches = 0;

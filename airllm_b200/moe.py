@@ -48,6 +48,7 @@ class AmoeConfig(ctypes.Structure):
         ("ep_rank", _i32),
         ("nccl_id", _vp),
         ("path", _i32),
+        ("stream_experts", _i32),
     ]
 
 
@@ -216,14 +217,16 @@ class MoEBlock:
 
     def __init__(self, hidden: int, intermediate: int, experts: int, top_k: int, layers: int = 1,
                  max_tokens: int = 4096, eps: float = 1e-5, device: int = 0, stream_slots: int = 0,
-                 path: int = PATH_AUTO, ep_size: int = 1, ep_rank: int = 0, nccl_id: bytes | None = None):
+                 path: int = PATH_AUTO, ep_size: int = 1, ep_rank: int = 0, nccl_id: bytes | None = None,
+                 stream_experts: int = 0):
         self._lib = load_library()
         self.hidden, self.intermediate, self.experts, self.top_k = hidden, intermediate, experts, top_k
         self.layers, self.max_tokens = layers, max_tokens
         self._nccl_id = ctypes.create_string_buffer(nccl_id, 128) if nccl_id is not None else None
         cfg = AmoeConfig(hidden, intermediate, experts, top_k, layers, eps, 1.702, 7.0, max_tokens, device,
                          stream_slots, ep_size, ep_rank,
-                         ctypes.cast(self._nccl_id, _vp) if self._nccl_id is not None else None, path)
+                         ctypes.cast(self._nccl_id, _vp) if self._nccl_id is not None else None, path,
+                         stream_experts)
         h = _vp()
         rc = self._lib.amoe_create(ctypes.byref(cfg), ctypes.byref(h))
         if rc != AMOE_OK:

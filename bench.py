@@ -204,11 +204,13 @@ def run_streaming(args):
     L = W.STREAM_LAYERS
     t0 = time.perf_counter()
     layers = [W.stream_layer(i) for i in range(L)]
-    blk = moe.MoEBlock.for_layer(layers[0], layers=L, max_tokens=1, stream_slots=2, path=moe.PATH_AUTO)
+    blk = moe.MoEBlock.for_layer(layers[0], layers=L, max_tokens=1, stream_slots=2, path=moe.PATH_AUTO,
+                                 stream_experts=args.stream_experts)
     for i, layer in enumerate(layers):
         blk.upload_layer(i, layer)
     setup_s = time.perf_counter() - t0
     gguf_bytes = sum(int(np.asarray(v).nbytes) for k, v in layers[0].items() if isinstance(v, np.ndarray))
+    dims = (layers[0]["hidden"], layers[0]["intermediate"], layers[0]["top_k"])
     del layers
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
@@ -238,20 +240,33 @@ def run_streaming(args):
     clk = clocks.stop()
     st = blk.stats(reset=True)
     ms = ev0.elapsed_time(ev1) / n
-    layer_bytes = int(st["layer_bytes"])  # what each layer visit copies (device format)
+    if args.stream_experts:
+        # each layer visit copies the routed experts' box planes, scale chunks and biases (k experts at T = 1)
+        def planes(R, K):
+            kp = (K + 127) // 128 * 128
+            return (R + 127) // 128 * 128 * kp // 2 + (R + 127) // 128 * (kp // 128) * 512
+        per_expert = planes(2 * dims[1], dims[0]) + planes(dims[0], dims[1]) + (2 * dims[1] + dims[0]) * 4
+        layer_bytes = dims[2] * per_expert
+    else:
+        layer_bytes = int(st["layer_bytes"])  # what each layer visit copies (device format)
     h2d = L * layer_bytes / (ms / 1e3) / 1e9
     line = {
         "metric": "decode tokens/s, 24-layer GPT-OSS-20B-shaped MoE stack streamed from pinned host memory",
         "value": 1e3 / ms, "unit": "tokens/s", "n_gpus": 1, "steps": n, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": DTYPE_DECODE, "data": "synthetic (seeded, seed (2, layer))",
-        "config": {"workload": f"gptoss20b-moe-stream layers={L} T=1 slots=2", "config_index": 2,
+        "config": {"workload": f"gptoss20b-moe-stream layers={L} T=1 "
+                               + ("routed experts per layer" if args.stream_experts else "whole layers, 2 slots"),
+                   "config_index": 2, "stream_experts": args.stream_experts,
                    "layer_bytes": layer_bytes, "setup_s": setup_s},
         "h2d_gbs": h2d, "h2d_bytes_per_step": L * layer_bytes,
         "gpu_launches": int(st["launches"]), "clocks": clk,
         "gguf_layer_bytes": gguf_bytes,
-        "note": "every layer visit copies the whole layer (AirLLM streaming): the MXFP4 box planes and scale "
-                "chunks, biases, router; bound by the host link",
+        "note": ("each layer visit routes on the device, then copies only the 4 routed experts' MXFP4 box planes, "
+                 "scale chunks and biases (the reference reads only the selected experts too); bound by the host "
+                 "link and the per-layer routing round trip") if args.stream_experts else
+                ("every layer visit copies the whole layer (AirLLM streaming): the MXFP4 box planes and scale "
+                 "chunks, biases, router; bound by the host link"),
     }
     print(json.dumps(line), flush=True)
     blk.close()
@@ -382,6 +397,8 @@ def main():
     ap.add_argument("--path", type=int, default=0, help="0 auto, 1 GEMV, 2 tcgen05")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=0, help="configs 3/4: total tokens (default 8192 / 16384)")
+    ap.add_argument("--stream-experts", type=int, default=1, choices=[0, 1],
+                    help="config 2: 1 copies only each layer's routed experts, 0 whole layers")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

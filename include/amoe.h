@@ -71,6 +71,9 @@ typedef struct amoe_config {
     int32_t ep_rank;         /* this process's rank in the expert-parallel group */
     const void *nccl_id;     /* 128-byte ncclUniqueId shared by the group (ep_size > 1) */
     int32_t path;            /* AMOE_PATH_* */
+    int32_t stream_experts;  /* with stream_slots >= 2: 1 = each forward routes first and copies
+                                only the experts its tokens selected (the reference reads only
+                                those too: tensor.go:94-111) instead of whole layers */
 } amoe_config;
 
 /* Replaces: gptoss.Open's per-runtime setup (runtime.go:37-60).  Allocates the

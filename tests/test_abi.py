@@ -45,6 +45,8 @@ def _cfg(**kw):
     (dict(swiglu_alpha=1.5), "swiglu"),
     (dict(max_tokens=0), "max_tokens"),
     (dict(stream_slots=1), "stream_slots"),
+    (dict(stream_experts=1), "stream_experts"),
+    (dict(stream_slots=2, path=1), "stream_slots needs path"),
     (dict(ep_rank=2, ep_size=2), "ep_rank"),
     (dict(path=7), "path"),
 ])

@@ -251,3 +251,26 @@ def test_pipelined_host_call_matches_one_device_pass(cuda_device, path, T, E):
     assert np.array_equal(idx, idd.cpu().numpy()) and np.array_equal(w, wd.cpu().numpy())
     for a, b in zip(routing, routing1):
         assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("T", [1, 3, 6, 40])
+def test_expert_streaming_matches_resident_layers(cuda_device, T):
+    """stream_experts: each call routes first and copies only its routed experts from
+    pinned host memory; the output equals resident layers on the same kernels."""
+    shape = W.MoEShape(128, 192, 16, 4)
+    layers = [W.make_layer(shape, 60 + i) for i in range(3)]
+    x = W.make_tokens(shape, T, 60 + T)
+    res = moe.MoEBlock(128, 192, 16, 4, layers=3, max_tokens=40, path=moe.PATH_TENSOR)
+    stm = moe.MoEBlock(128, 192, 16, 4, layers=3, max_tokens=40, stream_slots=2, stream_experts=1)
+    for i, L in enumerate(layers):
+        res.upload_layer(i, L)
+        stm.upload_layer(i, L)
+    h_res, h_stm = x, x
+    for i in (0, 1, 2, 1, 0):
+        o_res, idx_res, w_res = res.forward(h_res, layer=i)
+        o_stm, idx_stm, w_stm = stm.forward(h_stm, layer=i)
+        assert np.array_equal(o_res, o_stm) and np.array_equal(idx_res, idx_stm) and np.array_equal(w_res, w_stm)
+        h_res, h_stm = o_res, o_stm
+    stm.prefetch_layer(2)  # nothing to prefetch before routing: a no-op
+    res.close()
+    stm.close()
