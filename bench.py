@@ -40,6 +40,9 @@ from airllm_b200 import workloads as W  # noqa: E402
 METRIC = "MoE-block tokens/s per B200 (prefill T=4096, GPT-OSS-20B shape)"
 METRIC_BY_CONFIG = {0: "MoE-block tokens/s per B200 (decode T=1, GPT-OSS-20B shape)", 1: METRIC}
 UNIT = "tokens/s"
+# Timed steps when --steps is not given: each config's timed region then lasts
+# about half a second, several periods of the clock sampler.
+DEFAULT_STEPS = {0: 2000, 1: 300, 2: 16, 3: 100, 4: 100}
 FLOP_PER_PAIR = 2 * 2880 * (2 * 2880 + 2880)  # 49,766,400
 MEASURED_PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_FILE = os.path.join(ROOT, "profiles", "ncu_traffic.json")
@@ -89,22 +92,50 @@ class L2Flush:
 
 
 class ClockSampler:
-    """nvidia-smi clocks during the timed region (start before, stop after)."""
+    """nvidia-smi clocks during the timed region.
+
+    Create it before the timed region (it waits for the first sample, so the
+    sampler is running when timing starts), call begin() right before the first
+    timed step and stop() after the closing synchronize.  Only samples whose
+    nvidia-smi timestamp falls inside [begin, stop] count; if the region is
+    shorter than the sampling interval the nearest sample stands in and
+    `samples_in_region` says 0."""
+
+    PERIOD_MS = 100
 
     def __init__(self, device: int):
         self.path = tempfile.mktemp(suffix=".csv")
         self.proc = None
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        self.t0 = None
+        q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(device)],
+                                          "-lms", str(self.PERIOD_MS), "-i", str(device)],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        deadline = time.time() + 5.0
+        while time.time() < deadline and self.proc.poll() is None:
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.02)
+
+    def begin(self):
+        self.t0 = time.time()
+
+    @staticmethod
+    def _when(stamp: str):
+        import datetime
+        try:
+            return datetime.datetime.strptime(stamp, "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return None
 
     def stop(self):
+        t1 = time.time()
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -115,17 +146,29 @@ class ClockSampler:
         rows = []
         for line in open(self.path):
             f = [x.strip() for x in line.split(",")]
-            if len(f) >= 9:
+            if len(f) >= 10:
                 rows.append(f)
         os.unlink(self.path)
         if not rows:
             return None
+        t0 = self.t0 if self.t0 is not None else t1
+        stamped = [(self._when(r[0]), r[1:]) for r in rows]
+        inside = [r for w, r in stamped if w is not None and t0 <= w <= t1]
+        n_inside = len(inside)
+        if not inside:
+            mid = 0.5 * (t0 + t1)
+            near = min((abs(w - mid), i) for i, (w, _) in enumerate(stamped) if w is not None) \
+                if any(w is not None for w, _ in stamped) else (0, 0)
+            inside = [stamped[near[1]][1]]
+        rows = inside
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "power_w_max": max(pw) if pw else None, "samples_in_region": n_inside,
+                "period_ms": ClockSampler.PERIOD_MS}
 
 
 def cpu_reference_run(layer, x, sample: int, threads: int):
@@ -156,7 +199,7 @@ def run_reference(args):
     value = sample / sec
     desc = f"{sample} of {T} tokens per step (oracle restatement, faithful MXFP4 re-decode per (token, expert))"
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "impl": "reference", "metric": METRIC_BY_CONFIG.get(args.config, METRIC), "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64-accumulate (reference CPU path)",
         "data": "synthetic (seeded)", "config": workload_desc(args.config, T),
@@ -231,6 +274,7 @@ def run_streaming(args):
     n = min(args.steps, W.STREAM_DECODE_TOKENS)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(0)
+    clocks.begin()
     ev0.record(stream)
     h = x
     for _ in range(n):
@@ -325,6 +369,7 @@ def run_ep(args):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    clocks.begin()
     h0 = time.perf_counter()
     for i in range(args.steps):
         flush(i)
@@ -390,7 +435,8 @@ def run_ep(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=0,
+                    help="timed steps (default per config, so the timed region spans several clock samples)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=1)
@@ -400,6 +446,8 @@ def main():
     ap.add_argument("--stream-experts", type=int, default=1, choices=[0, 1],
                     help="config 2: 1 copies only each layer's routed experts, 0 whole layers")
     args = ap.parse_args()
+    if args.steps <= 0:  # the reference arm's steps are CPU samples of about a second each
+        args.steps = 5 if args.impl == "reference" else DEFAULT_STEPS.get(args.config, 20)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
@@ -460,6 +508,7 @@ def main():
     clocks = ClockSampler(local)
     torch.cuda.synchronize()
     barrier()
+    clocks.begin()
     for i in range(args.steps):
         flush(i)
         starts[i].record(stream)
