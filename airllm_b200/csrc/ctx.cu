@@ -439,6 +439,12 @@ int check_device_flag(amoe_ctx *c, int32_t known = -1) {
             return fail(c, v == 33 ? AMOE_ERR_STATE : AMOE_ERR_TIMEOUT,
                         std::string("expert-parallel ") + what[v - 30] + " failed (code " + std::to_string(v) + ")");
         }
+        if (v >= 50 && v <= 54) {
+            static const char *what[] = {"ring slot release", "weight box arrival", "expert activation",
+                                         "router logits", "copy drain"};
+            return fail(c, AMOE_ERR_TIMEOUT, std::string("decode kernel: wait for the ") + what[v - 50] +
+                                                 " timed out (code " + std::to_string(v) + ")");
+        }
         return fail(c, AMOE_ERR_TIMEOUT, "device pipeline wait timed out (code " + std::to_string(v) + ")");
     }
     return AMOE_OK;

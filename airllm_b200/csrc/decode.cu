@@ -1,37 +1,55 @@
-// decode.cu -- K9: the expert stage of a decode step (T <= kDecodeMaxTokens)
-// as ONE cooperative persistent kernel on the block-scaled tensor cores:
+// decode.cu -- K9: a decode step (T <= kDecodeMaxTokens) as ONE cooperative
+// persistent kernel: routing, gate_up + SwiGLU, down and the combine.
 //
-//   phase 1  gate_up = x . W_gu^T + b_gu -> clamped SwiGLU      (layer.go:139-148, 175;
-//                                                                primitives.go:138-149)
-//   phase 2  y = act . W_dn^T + b_dn                             (layer.go:179-187)
-//   phase 3  out = residual + f32(sum_s f64(w_s) * f64(y_s))      (layer.go:109-121)
+//   routing  RMSNorm, router logits, top-k, softmax     (primitives.go:11-72, moe.go:12-41)
+//   gate_up  act = SwiGLU(x . W_gu^T + b_gu)              (layer.go:139-148, 175; primitives.go:138-149)
+//   down     y = act . W_dn^T + b_dn                      (layer.go:179-187)
+//   combine  out = residual + f32(sum_s f64(w_s) * f64(y_s))  (layer.go:109-121)
 //
-// No grid-wide barrier: a finished tile publishes a per-launch flag; an
-// expert's down tiles wait for that expert's gate_up tiles, and each 128-row
-// slice of the combine waits for the down tiles of those rows.
+// A decode step is a batched matrix-vector product over the selected experts'
+// MXFP4 weights (53 MB per token for the 20B shape): the bound is HBM, and the
+// design goal is to keep every SM streaming weight boxes from the first moment
+// the routing is known to the end.
 //
-// The MXFP4 experts are consumed as stored: tcgen05.mma kind::mxf8f6f4 with
-// A = E2M1 weights straight from the TMA planes (TMA unpacks the nibbles into
-// the tensor core's 16-byte-aligned shared-memory format) and the GGUF E8M0
-// bytes as the hardware block scales of A.  The activations enter as four
-// E4M3 terms x ~= sum_j q_j * 2^(e - 4j) per 32-element block (B scale
-// factors), one term per MMA column, so one MMA computes all four partial
-// products; the epilogue adds the columns.  Four terms carry ~16 significant
-// bits; accumulation is f32 in TMEM.
+// Work.  A unit is one 128-row weight tile of one selected expert over its K
+// range: every gate_up tile over all of K (SwiGLU needs the whole sum), every
+// down tile over one half of K.  A host-built table (longest-processing-time
+// first over the units' box counts, one table per number of active experts)
+// gives each CTA its units: gate_up units first, then down units, both in
+// slot order.  No unit is shared between CTAs, so no tile needs a cross-CTA
+// reduction.  Two hand-offs cross CTAs, both through L2:
+//   - the last gate_up unit of a slot to finish publishes the slot's
+//     activation (a per-slot flag carrying the launch epoch); a down unit
+//     waits for it before it builds its operand (its weights are already
+//     streaming into the ring meanwhile);
+//   - the last down unit of a 128-row output tile to finish combines that
+//     tile for every token (self-resetting arrival counters).
 //
-// Work split: all selected experts' 128-row weight tiles of a phase form one
-// sequence of 128-element K boxes; CTA b takes the contiguous run
-// [n*b/G, n*(b+1)/G) (stream-K), so every SM streams the same number of
-// bytes.  A tile cut between CTAs is summed by whichever of its CTAs arrives
-// last (self-resetting counter), adding the partials in CTA order
-// (deterministic).  The down boxes do not depend on phase 1, so the producers
-// stream them early; only their activation operand waits for its expert.
+// Weights.  The units' boxes stream from the TMA box planes (128 rows x 64 B of
+// GGUF nibble bytes per 128-element K box, 8 KB, plus the box's 512-byte E8M0
+// chunk) into a ring of 17 KB stages, two boxes per stage, with SWIZZLE_64B so
+// the fragment loads below are free of bank conflicts.  There is no producer
+// warp: one thread fills the first stages, and afterwards the last warp to
+// finish with a stage refills its slot with the stage a ring further on (all 16
+// warps then fit four per SM sub-partition with 128 registers each).  The
+// boxes stay packed in shared memory: 16 warps (two groups of 8
+// that take alternate stages) expand them in registers with
+// cvt.rn.f16x2.e2m1x2 (E2M1 is exact in fp16) and multiply on mma.sync
+// m16n8k16, 16 weight rows per warp.  The activations are the n = 8 columns:
+// each token as an fp16 hi + lo pair (x ~= hi + lo to ~2^-22), so one MMA
+// covers up to four tokens.  Byte i of a 32-element block holds elements 2i
+// and 2i+1 (tensor.go:156-158), so lane (g, c)'s four bytes of a block are
+// elements 8c..8c+7: one 32-bit load per row and one 16-byte load of the
+// activation column give both k-steps of the block.  Each block's two MMAs
+// go to a fresh f32 accumulator that is then scaled by the row's E8M0 block
+// scale, so the scale never has to fit fp16's range.
 //
-// Roles: warps 0-3 TMA producers (stage i filled by warp i % 4), warp 4 MMA
-// issuer and TMEM owner, warps 5-8 epilogue (TMEM lane quadrants 1, 2, 3, 0),
-// warp 9 watches the gate_up tiles this CTA's down boxes depend on.
-// Every wait is bounded (~1 s of clock): it records a code in the error flag
-// and the kernel winds down.
+// Every wait is bounded (~1 s of clock): it records a code (50-54) in the error flag,
+// marks the CTA dead (later waits return at once, no further stage is issued,
+// the copies in flight are waited for) and the kernel winds down.
+#include <algorithm>
+#include <vector>
+
 #include "tc_ptx.cuh"
 
 namespace amoe {
@@ -40,28 +58,24 @@ namespace {
 
 using namespace bs;
 
-// Copies issued by one warp are serviced one after another (~0.4 us each at
-// load), so four producer warps fill the ring's stages round-robin.
-constexpr int kProdWarps = 4;
-constexpr int kMmaWarp = kProdWarps;
-constexpr int kEpiWarp0 = kProdWarps + 1;
-constexpr int kEpiWarps = 4;
-constexpr int kEpiThreads = kEpiWarps * 32;
-constexpr int kWatchWarp = kEpiWarp0 + kEpiWarps;  // polls other CTAs' tile flags
-constexpr int kDecThreads = (kWatchWarp + 1) * 32;
-constexpr int kNMax = 16;                       // MMA N: up to 4 tokens x 4 terms
-constexpr int kBoxes = 2;                       // 128-element K boxes per pipeline stage
-constexpr int kMaxStages = 6;
-constexpr uint32_t kABytes = 128 * 128;         // unpacked A box in shared memory
-constexpr uint32_t kAPacked = 128 * 64;         // its bytes in global memory (TMA transaction size)
-constexpr uint32_t kTmemCols = 128;             // 2 accumulators + 16 scale columns per stage
-constexpr size_t kSmemBudget = 225 * 1024;
-constexpr int kTilesPerSlot = 64;               // tile counters per slot and phase
+constexpr int kGroups = 2;                      // consumer groups, alternate stages
+constexpr int kGroupWarps = 8;                  // 8 warps x 16 rows = one 128-row tile
+constexpr int kComputeWarps = kGroups * kGroupWarps;
+constexpr int kComputeThreads = kComputeWarps * 32;
+constexpr int kDecThreads = kComputeWarps * 32;  // no producer warp: the last releaser of a stage refills it
+constexpr uint32_t kBoxBytes = 128 * 64;        // one packed box: 128 rows x 128 E2M1 values
+constexpr uint32_t kStageBytes = 2 * kBoxBytes + 2 * 512;  // two boxes, then their scale chunks
+constexpr int kMaxStages = 12;
+constexpr int kMaxUnits = 64;                   // units per CTA
+constexpr int kSchedWords = 1024;               // one CTA's schedule rows (int32)
+constexpr int kMaxCtaStages = kMaxUnits * 16;   // ring stages of one CTA (a unit has <= 16: K <= 4096)
+constexpr size_t kSmemBudget = 232448;          // dynamic shared memory per block (227 KB)
 
-// Stage: kBoxes A boxes | their scale chunks | kBoxes B boxes | their scale chunks.
-__host__ __device__ constexpr uint32_t b_box_bytes(int nt) { return (uint32_t)nt * 128; }
-__host__ __device__ constexpr uint32_t stage_bytes(int nt) {
-    return (kBoxes * kABytes + kBoxes * 512 + kBoxes * b_box_bytes(nt) + kBoxes * 512 + 1023) & ~1023u;
+static_assert(kStageBytes % 1024 == 0, "stages keep the 1 KB alignment SWIZZLE_64B needs");
+
+// Unit encoding in the schedule table.
+__host__ __device__ constexpr int32_t unit_code(int phase, int slot, int mt, int kpart) {
+    return (phase << 30) | (slot << 20) | (mt << 8) | kpart;
 }
 
 struct DecodeParams {
@@ -73,45 +87,55 @@ struct DecodeParams {
     unsigned *rflag;            // [G] launch epoch once a CTA's router dot products are stored
     const uint8_t *gu_tsf, *dn_tsf;
     const float *gu_b, *dn_b;
-    uint8_t *act_q;             // [S][16][Ip] E4M3 terms of each slot's activation rows
-    uint8_t *act_sf;            // [S][Ip/128][512] their scale-factor chunks
-    float *y;                   // [P][H]
-    float *partial;             // [G][2][128][kNMax]
-    uint32_t *cnt;              // [2][S][kTilesPerSlot] self-resetting tile counters
-    unsigned *tflag;            // [2][S][kTilesPerSlot] launch epoch of each finished tile
+    float *act;                 // [S][T][Ip] SwiGLU outputs of every token for every slot (padding stays 0)
+    float *yb;                  // [S][2][T][H] down outputs, one plane per K half
+    uint32_t *cnt_gu;           // [S] self-resetting arrival counters of the gate_up units
+    uint32_t *cnt_dn;           // [nmt2] ... of the down units per output tile
+    unsigned *aflag;            // [S] launch epoch once the slot's activation is complete
+    const int32_t *sched;       // [G][kSchedWords]: per CTA, [n - 1]..[n] delimit its units when n slots are active
     DecodeBarrier *bar;
     int32_t *err;
     int T, H, I, E, k, Hp, Ip, S;
     int stages;
-    int N;                      // MMA N (8 or 16)
 };
+
+// Shared-memory layout (offsets from a 1 KB-aligned base).
+__host__ __device__ constexpr uint32_t col_stride(int K) { return (uint32_t)(2 * K + 64); }  // fp16 column + pad
 
 struct DecLayout {
-    uint32_t ring, b1, sfb1, offs, act, perm, inv, w, ready, rms, lg, tk, xchg, bars, tmem_slot, total;
+    uint32_t ring, bx, bd, red, units, stg, rel, offs, act, perm, inv, w, sl, rms, lg, tk, misc, bars, total;
 };
 
-__host__ __device__ inline DecLayout dec_layout(int T, int Hp, int E, int k, int stages, int nt) {
+__host__ __device__ inline DecLayout dec_layout(int T, int Hp, int Ip, int E, int k, int stages, int ncol) {
     DecLayout L;
     uint32_t o = 0;
+    const uint32_t P = (uint32_t)(T * k);
     L.ring = o;
-    o += (uint32_t)stages * stage_bytes(nt);
-    L.b1 = o;
-    o += (uint32_t)(Hp / 128) * b_box_bytes(nt);
-    L.sfb1 = o;
-    o += (uint32_t)(Hp / 128) * 512;
+    o += (uint32_t)stages * kStageBytes;
+    L.bx = o;  // gate_up operand: ncol fp16 columns of Hp
+    o += (uint32_t)ncol * col_stride(Hp);
+    L.bd = o;  // down operand: ncol fp16 columns of Ip
+    o += (uint32_t)ncol * col_stride(Ip);
+    L.red = o;  // group 1's accumulators at the end of a unit
+    o += (uint32_t)kGroupWarps * 32 * 4 * 4;
+    L.units = o;
+    o += kMaxUnits * 4;
+    L.stg = o;  // [kMaxCtaStages] this CTA's ring stages: phase << 31 | (boxes - 1) << 30 | first box
+    o += kMaxCtaStages * 4;
+    L.rel = o;  // [stages] warps of the consuming group done with the slot; [stages] last stage issued into it
+    o += 2u * (uint32_t)stages * 4;
     L.offs = o;
     o += (uint32_t)(E + 1) * 4;
     L.act = o;
     o += (uint32_t)(E + 1) * 4;
-    const uint32_t P = (uint32_t)(T * k);
     L.perm = o;
     o += P * 4;
     L.inv = o;
     o += P * 4;
     L.w = o;
     o += P * 4;
-    L.ready = o;  // [min(E, P)] phase-2 operand of the slot complete
-    o += (uint32_t)(E < (int)P ? E : (int)P) * 4;
+    L.sl = o;  // [P] active-slot index of each (token, slot) pair
+    o += P * 4;
     o = (o + 7u) & ~7u;
     L.rms = o;  // [4] inverse RMS per token, then [warps][4] partial sums (f64)
     o += (uint32_t)(4 + (kDecThreads / 32) * 4) * 8;
@@ -119,103 +143,104 @@ __host__ __device__ inline DecLayout dec_layout(int T, int Hp, int E, int k, int
     o += (uint32_t)(T * E) * 4;
     L.tk = o;  // [P] selected experts in slot order
     o += P * 4;
-    L.xchg = o;
-    o += 64;  // block maxima of the activation quantization + flags
+    L.misc = o;  // broadcast words
+    o += 64;
     o = (o + 7u) & ~7u;
-    L.bars = o;
-    o += (2u * (uint32_t)stages + 5u) * 8;
-    L.tmem_slot = o;
-    o += 16;
+    L.bars = o;  // [stages] full barriers
+    o += (uint32_t)stages * 8;
     L.total = o + 1024;  // base alignment slack
     return L;
 }
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
-
-// A phase's geometry: the whole phase's box sequence and this CTA's run.
-struct Phase {
-    int nmt, nkb;  // 128-row tiles per expert, 128-element K boxes per tile
-    int nbox;      // boxes of the whole phase
-    int lo, hi;    // this CTA's boxes [lo, hi)
-};
-
-__device__ __forceinline__ int run_start(int nbox, int b, int G) { return (int)((long long)nbox * b / G); }
-
-__device__ __forceinline__ Phase make_phase(int nmt, int nkb, int n_active) {
-    Phase ph;
-    ph.nmt = nmt;
-    ph.nkb = nkb;
-    ph.nbox = n_active * nmt * nkb;
-    ph.lo = run_start(ph.nbox, blockIdx.x, gridDim.x);
-    ph.hi = run_start(ph.nbox, blockIdx.x + 1, gridDim.x);
-    return ph;
+__device__ __forceinline__ void compute_bar() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kComputeThreads) : "memory");
 }
 
-// Largest b whose run starts at or before box x (the CTA whose run holds x).
-__device__ __forceinline__ int cta_of_box(int x, int nbox, int G) {
-    return (int)(((long long)(x + 1) * G - 1) / nbox);
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Walks a CTA's run in pipeline stages: up to kBoxes consecutive boxes of one
-// tile per stage, indices advanced without division.
-struct Walker {
-    int x, hi, nkb, nmt;
-    int slot, mt, kb;  // position of box x
-    __device__ __forceinline__ Walker(const Phase &q) : x(q.lo), hi(q.hi), nkb(q.nkb), nmt(q.nmt) {
-        const int tile = q.nkb > 0 ? q.lo / q.nkb : 0;
-        kb = q.lo - tile * q.nkb;
-        slot = q.nmt > 0 ? tile / q.nmt : 0;
-        mt = tile - slot * q.nmt;
-    }
-    __device__ __forceinline__ bool more() const { return x < hi; }
-    __device__ __forceinline__ int boxes() const { return min(kBoxes, min(nkb - kb, hi - x)); }
-    __device__ __forceinline__ void advance(int nb) {
-        x += nb;
-        kb += nb;
-        if (kb == nkb) {
-            kb = 0;
-            if (++mt == nmt) {
-                mt = 0;
-                ++slot;
-            }
+// Bounded mbarrier wait that returns at once once the CTA is dead.
+__device__ __forceinline__ bool ring_wait(uint64_t *bar, uint32_t parity, volatile int *dead, int32_t *err,
+                                          int code) {
+    if (*dead) return false;
+    const long long t0 = clock64();
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if (*dead) return false;
+        if (clock64() - t0 > kWaitLimit) {
+            atomicCAS(err, 0, code);
+            *dead = 1;
+            return false;
         }
     }
-};
+}
 
-template <int NT>
+// x (f32, natural order) -> fp16 hi / lo columns 2t, 2t+1 of an operand buffer.
+__device__ __forceinline__ void put_split8(uint8_t *buf, uint32_t stride, int t, int k0, const float (&v)[8]) {
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+        const float2 f = __half22float2(h);
+        const __half2 l = __floats2half2_rn(v[2 * j] - f.x, v[2 * j + 1] - f.y);
+        hi[j] = *reinterpret_cast<const uint32_t *>(&h);
+        lo[j] = *reinterpret_cast<const uint32_t *>(&l);
+    }
+    *reinterpret_cast<uint4 *>(buf + (size_t)(2 * t) * stride + 2 * k0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4 *>(buf + (size_t)(2 * t + 1) * stride + 2 * k0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+}
+
+template <int NCOL>
 __launch_bounds__(kDecThreads, 1) __global__
-    void decode_kernel(const __grid_constant__ CUtensorMap tm_gu, const __grid_constant__ CUtensorMap tm_dn,
-                       const __grid_constant__ CUtensorMap tm_act, DecodeParams p) {
-    constexpr uint32_t kBBox = b_box_bytes(NT);
-    constexpr uint32_t kStage = stage_bytes(NT);
+    void decode_kernel(const __grid_constant__ CUtensorMap tm_gu2, const __grid_constant__ CUtensorMap tm_gu1,
+                       const __grid_constant__ CUtensorMap tm_dn2, const __grid_constant__ CUtensorMap tm_dn1,
+                       DecodeParams p) {
     extern __shared__ __align__(1024) uint8_t sm_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
-    const DecLayout lay = dec_layout(p.T, p.Hp, p.E, p.k, p.stages, NT);
+    const DecLayout lay = dec_layout(p.T, p.Hp, p.Ip, p.E, p.k, p.stages, NCOL);
     uint8_t *ring = sm + lay.ring;
-    uint8_t *b1 = sm + lay.b1;
-    uint8_t *sfb1 = sm + lay.sfb1;
+    uint8_t *bx = sm + lay.bx;
+    uint8_t *bd = sm + lay.bd;
+    float *red = reinterpret_cast<float *>(sm + lay.red);
+    int32_t *units_s = reinterpret_cast<int32_t *>(sm + lay.units);
     int32_t *offs_s = reinterpret_cast<int32_t *>(sm + lay.offs);
     int32_t *act_s = reinterpret_cast<int32_t *>(sm + lay.act);
     int32_t *perm_s = reinterpret_cast<int32_t *>(sm + lay.perm);
     int32_t *inv_s = reinterpret_cast<int32_t *>(sm + lay.inv);
     float *w_s = reinterpret_cast<float *>(sm + lay.w);
-    float *xchg = reinterpret_cast<float *>(sm + lay.xchg);
-    volatile int *last_flag = reinterpret_cast<volatile int *>(sm + lay.xchg + 32);
-    volatile int *ready_s = reinterpret_cast<volatile int *>(sm + lay.ready);
+    int32_t *sl_s = reinterpret_cast<int32_t *>(sm + lay.sl);
+    volatile int *misc = reinterpret_cast<volatile int *>(sm + lay.misc);  // [0] dead, [1] last, [2] units
+    int32_t *stg_s = reinterpret_cast<int32_t *>(sm + lay.stg);
+    int *rel_s = reinterpret_cast<int *>(sm + lay.rel);  // [R] releases, then [R] last stage issued per slot
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + lay.bars);
-    uint64_t *empty = full + p.stages;
-    uint64_t *accfull = empty + p.stages;  // [2]
-    uint64_t *accempty = accfull + 2;      // [2]
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + lay.tmem_slot);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int E = p.E, P = p.T * p.k, R = p.stages, G = gridDim.x;
+    const uint32_t sx = col_stride(p.Hp), sd = col_stride(p.Ip);
     const unsigned epoch = p.bar->epoch[blockIdx.x] + 1u;
 
     if (tid == 0) {
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_gu)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_dn)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_act)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_gu2)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_dn2)) : "memory");
+        misc[0] = 0;
+        for (int s = 0; s < R; ++s) {
+            mbar_init(full + s, 1);
+            rel_s[s] = 0;
+            rel_s[R + s] = -1;
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     // ---------------- routing, in every CTA ----------------
     // RMSNorm (primitives.go:50-72), router logits (primitives.go:11-47), top-k and
@@ -230,8 +255,35 @@ __launch_bounds__(kDecThreads, 1) __global__
         float *lg_s = reinterpret_cast<float *>(sm + lay.lg);
         int *tk_s = reinterpret_cast<int *>(sm + lay.tk);
         const int T = p.T, H = p.H;
-        // (1) float64 sums of squares of the T residual rows (loads unrolled: in flight together)
+        // (0) every global input of the routing in one batch, staged in the ring (no
+        //     copy uses it before the routing is done): this CTA's schedule rows for
+        //     every number of active slots, the T residual rows, the gain and, for a
+        //     CTA that owns a router dot product, the first router row it needs.
         constexpr int kPer = (4096 + kDecThreads - 1) / kDecThreads;  // elements per thread, H <= 4096
+        int32_t *sched_s = reinterpret_cast<int32_t *>(ring);
+        float *xs_s = reinterpret_cast<float *>(ring + kSchedWords * 4);  // [T][Hp] residual rows
+        float *gs_s = xs_s + (size_t)T * p.Hp;                            // [Hp] gain
+        const int ndots = T * E;
+        for (int i = tid; i < kSchedWords; i += kDecThreads)
+            sched_s[i] = __ldg(p.sched + (size_t)blockIdx.x * kSchedWords + i);
+        float wv[kPer];
+        {
+            const int e0 = (int)blockIdx.x < ndots ? (int)blockIdx.x % E : 0;
+            float gv[kPer];
+#pragma unroll
+            for (int r = 0; r < kPer; ++r) {
+                const int i = tid + r * kDecThreads;
+                const bool in = i < H;
+                wv[r] = in && (int)blockIdx.x < ndots ? __ldg(p.router_w + (size_t)e0 * H + i) : 0.0f;
+                gv[r] = in ? __ldg(p.gain + i) : 0.0f;
+            }
+#pragma unroll
+            for (int r = 0; r < kPer; ++r) {
+                const int i = tid + r * kDecThreads;
+                if (i < p.Hp) gs_s[i] = gv[r];
+            }
+        }
+        // (1) float64 sums of squares of the T residual rows
         double ss[kDecodeMaxTokens];
 #pragma unroll
         for (int t = 0; t < kDecodeMaxTokens; ++t) {
@@ -241,10 +293,14 @@ __launch_bounds__(kDecThreads, 1) __global__
 #pragma unroll
                 for (int r = 0; r < kPer; ++r) {
                     const int i = tid + r * kDecThreads;
-                    xv[r] = i < H ? p.residual[(size_t)t * H + i] : 0.0f;
+                    xv[r] = i < H ? __ldg(p.residual + (size_t)t * H + i) : 0.0f;
                 }
 #pragma unroll
-                for (int r = 0; r < kPer; ++r) ss[t] += (double)xv[r] * (double)xv[r];
+                for (int r = 0; r < kPer; ++r) {
+                    const int i = tid + r * kDecThreads;
+                    ss[t] += (double)xv[r] * (double)xv[r];
+                    if (i < p.Hp) xs_s[(size_t)t * p.Hp + i] = xv[r];
+                }
             }
         }
 #pragma unroll
@@ -263,26 +319,18 @@ __launch_bounds__(kDecThreads, 1) __global__
         __syncthreads();
         // (2) router dot products, one per CTA (dot d on CTA d mod G):
         //     logit = f32(sum f64(x_n) f64(W)) + b, partials added in a fixed order
-        const int ndots = T * E;
         for (int dd = blockIdx.x; dd < ndots; dd += G) {
             const int t = dd / E, e = dd - t * E;
-            const float *xr = p.residual + (size_t)t * H;
-            const float *wr = p.router_w + (size_t)e * H;
             const double inv = rms_s[t];
-            float xv[kPer], gv[kPer], wv[kPer];
-#pragma unroll
-            for (int r = 0; r < kPer; ++r) {
-                const int i = tid + r * kDecThreads;
-                const bool in = i < H;
-                xv[r] = in ? xr[i] : 0.0f;
-                gv[r] = in ? p.gain[i] : 0.0f;
-                wv[r] = in ? wr[i] : 0.0f;
-            }
             double acc = 0.0;
 #pragma unroll
             for (int r = 0; r < kPer; ++r) {
-                const float xn = (float)((double)xv[r] * inv * (double)gv[r]);
-                acc = fma((double)xn, (double)wv[r], acc);
+                const int i = tid + r * kDecThreads;
+                if (i < H) {
+                    const float w = dd == (int)blockIdx.x ? wv[r] : __ldg(p.router_w + (size_t)e * H + i);
+                    const float xn = (float)((double)xs_s[(size_t)t * p.Hp + i] * inv * (double)gs_s[i]);
+                    acc = fma((double)xn, (double)w, acc);
+                }
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -297,82 +345,37 @@ __launch_bounds__(kDecThreads, 1) __global__
         }
         __syncthreads();
         if (tid == 0 && (int)blockIdx.x < min(G, ndots)) publish(p.rflag + blockIdx.x, epoch);
-        // (2b) the phase-1 operand, while other CTAs finish their dot products: every
-        //      token's normalized row as four E4M3 terms.  Item = 8 elements; four
-        //      consecutive lanes hold one 32-element block.
+        // (2b) the gate_up operand, while other CTAs finish their dot products: every
+        //      token's normalized row (rounded to f32 as RMSNorm stores it,
+        //      primitives.go:68-70) as fp16 hi / lo columns; zero past H and in the
+        //      columns of absent tokens.
         {
-            const int n8 = p.Hp / 8, total = p.T * n8;
-            constexpr int kBatch = 4;  // items per thread whose loads are in flight together
-            for (int base0 = 0; base0 < total; base0 += kBatch * kDecThreads) {
-              float4 xv[kBatch][2], gv[kBatch][2];
-#pragma unroll
-              for (int u = 0; u < kBatch; ++u) {
-                const int it = base0 + u * kDecThreads + tid;
+            const int n8 = p.Hp / 8;
+            for (int it = tid; it < (NCOL / 2) * n8; it += kDecThreads) {
                 const int t = it / n8, k0 = 8 * (it - t * n8);
-                xv[u][0] = xv[u][1] = gv[u][0] = gv[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (it < total && k0 < p.H) {
-                    xv[u][0] = *reinterpret_cast<const float4 *>(p.residual + (size_t)t * p.H + k0);
-                    xv[u][1] = *reinterpret_cast<const float4 *>(p.residual + (size_t)t * p.H + k0 + 4);
-                    gv[u][0] = *reinterpret_cast<const float4 *>(p.gain + k0);
-                    gv[u][1] = *reinterpret_cast<const float4 *>(p.gain + k0 + 4);
-                }
-              }
-#pragma unroll
-              for (int u = 0; u < kBatch; ++u) {
-                const int it = base0 + u * kDecThreads + tid;
-                const bool valid = it < total;
-                const int t = valid ? it / n8 : 0, k8 = valid ? it - t * n8 : 0;
-                const int k0 = 8 * k8;
-                // normalized row, rounded to f32 as RMSNorm stores it (primitives.go:68-70)
-                const double inv = rms_s[t];
-                const float xs[8] = {xv[u][0].x, xv[u][0].y, xv[u][0].z, xv[u][0].w,
-                                     xv[u][1].x, xv[u][1].y, xv[u][1].z, xv[u][1].w};
-                const float gs[8] = {gv[u][0].x, gv[u][0].y, gv[u][0].z, gv[u][0].w,
-                                     gv[u][1].x, gv[u][1].y, gv[u][1].z, gv[u][1].w};
                 float v[8];
-                float amax = 0.0f;
+                if (t < T && k0 < H) {
+                    const double inv = rms_s[t];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    v[q] = (float)((double)xs[q] * inv * (double)gs[q]);
-                    amax = fmaxf(amax, fabsf(v[q]));
+                    for (int q = 0; q < 8; ++q)
+                        v[q] = (float)((double)xs_s[(size_t)t * p.Hp + k0 + q] * inv * (double)gs_s[k0 + q]);
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) v[q] = 0.0f;
                 }
-                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-                if (!valid) continue;
-                const int e0 = block_exp(amax);
-                uint32_t lo4[4] = {0, 0, 0, 0}, hi4[4] = {0, 0, 0, 0};  // [term]: elements 0-3, 4-7
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const uint32_t q = quant4(v[i], e0);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint32_t byte = ((q >> (8 * j)) & 0xffu) << (8 * (i & 3));
-                        if (i < 4) lo4[j] |= byte;
-                        else hi4[j] |= byte;
-                    }
-                }
-                const int box = k0 / 128, chunk = (k0 % 128) / 16, half = (k0 % 16) / 8;
-                uint8_t *bx = b1 + (size_t)box * kBBox;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int n = 4 * t + j;  // B row: token t, term j (SWIZZLE_128B: chunk ^ row % 8)
-                    uint8_t *dst = bx + (n >> 3) * 1024 + (n & 7) * 128 + ((chunk ^ (n & 7)) << 4) + 8 * half;
-                    *reinterpret_cast<uint2 *>(dst) = make_uint2(lo4[j], hi4[j]);
-                    if ((k8 & 3) == 0) sfb1[(size_t)box * 512 + n * 16 + (k0 % 128) / 32] = (uint8_t)term_scale_byte(e0, j);
-                }
-              }
+                put_split8(bx, sx, t, k0, v);
             }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         }
         const int dot_ctas = min(G, ndots);
         // (3) every CTA's logits
-        if (warp == 0) wait_flags(p.rflag, dot_ctas, epoch, lane, p.err, 38);
+        if (warp == 0) wait_flags(p.rflag, dot_ctas, epoch, lane, p.err, 53);
         __syncthreads();
         for (int i = tid; i < ndots; i += kDecThreads) lg_s[i] = __ldcg(p.route.logits + i);
         __syncthreads();
         // (4) top-k: the rank of every (token, expert) in the stable descending order
         //     (moe.go:20-27) in parallel; ranks below k are the selected slots.  Then
-        //     the softmax over the selected logits per token (moe.go:29-39).
+        //     the softmax over the selected logits per token (moe.go:29-39): the k
+        //     exponentials in parallel, the denominator summed in slot order.
         for (int te = tid; te < ndots; te += kDecThreads) {
             const int t = te / E, e = te - t * E;
             const float v = lg_s[te];
@@ -381,15 +384,13 @@ __launch_bounds__(kDecThreads, 1) __global__
             if (rank < p.k) tk_s[t * p.k + rank] = e;
         }
         __syncthreads();
-        if (tid < T) {
-            const int t = tid;
+        if (warp < T) {
+            const int t = warp;
             const double maxv = (double)lg_s[t * E + tk_s[t * p.k]];
+            const double ex = lane < p.k ? exp((double)lg_s[t * E + tk_s[t * p.k + lane]] - maxv) : 0.0;
             double den = 0.0;
-            for (int sl = 0; sl < p.k; ++sl) den += exp((double)lg_s[t * E + tk_s[t * p.k + sl]] - maxv);
-            for (int sl = 0; sl < p.k; ++sl) {
-                const float wf = (float)exp((double)lg_s[t * E + tk_s[t * p.k + sl]] - maxv);
-                w_s[t * p.k + sl] = (float)((double)wf / den);
-            }
+            for (int sl = 0; sl < p.k; ++sl) den += __shfl_sync(0xffffffffu, ex, sl);
+            if (lane < p.k) w_s[t * p.k + lane] = (float)((double)(float)ex / den);
         }
         __syncthreads();
         // (5) counts, offsets, active experts and the stable permutation
@@ -442,6 +443,17 @@ __launch_bounds__(kDecThreads, 1) __global__
             for (int r = 0; r < q; ++r) pos += tk_s[r] == e;
             perm_s[pos] = q;
             inv_s[q] = pos;
+            int slot = 0;
+            while (act_s[slot] != e) ++slot;  // e is active, so the search ends within act_s[0..E)
+            sl_s[q] = slot;
+        }
+        {
+            // this CTA's units for this number of active slots (its staged schedule rows)
+            const int n_active = act_s[E];
+            const int u0 = sched_s[n_active - 1], u1 = sched_s[n_active];
+            const int n = min(u1 - u0, kMaxUnits);
+            for (int u = tid; u < n; u += kDecThreads) units_s[u] = sched_s[u0 + u];
+            if (tid == 0) misc[2] = n;
         }
         __syncthreads();
         if (blockIdx.x == 0) {  // the routing the C ABI reports
@@ -458,316 +470,221 @@ __launch_bounds__(kDecThreads, 1) __global__
             }
         }
     }
-    for (int i = tid; i < (E < P ? E : P); i += kDecThreads) ready_s[i] = 0;
-    if (tid == 0) {
-        for (int s = 0; s < R; ++s) {
-            mbar_init(full + s, 1);
-            mbar_init(empty + s, 1);
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(accfull + b, 1);
-            mbar_init(accempty + b, kEpiThreads);
-        }
-        *last_flag = 0;
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    if (warp == kMmaWarp) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(kTmemCols));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
 
     const int n_active = act_s[E];
+    const int nunits = misc[2];
     const int nkb1 = p.Hp / 128, nkb2 = p.Ip / 128;
     const int nmt1 = 2 * p.I / 128, nmt2 = (p.H + 127) / 128;
-    const Phase ph[2] = {make_phase(nmt1, nkb1, n_active), make_phase(nmt2, nkb2, n_active)};
+    const int nkp = nkb2 >= 2 ? 2 : 1, half2 = (nkb2 + 1) / 2;  // down units: K halves
+    // a unit's phase (0 gate_up, 1 down), slot, weight tile, K part and box range
+    auto unit_span = [&](int32_t code, int &phase, int &slot, int &mt, int &kpart, int &kb0, int &kb1) {
+        phase = (code >> 30) & 1;
+        slot = (code >> 20) & 1023;
+        mt = (code >> 8) & 4095;
+        kpart = code & 1;
+        kb0 = phase == 0 || kpart == 0 ? 0 : half2;
+        kb1 = phase == 0 ? nkb1 : (nkp == 1 || kpart == 1 ? nkb2 : half2);
+    };
 
-    if (warp < kProdWarps) {
-        // ---------------- producers: stage i is warp i % kProdWarps's ----------------
-        // With R >= kProdWarps stages, the wait for iteration i - R's slot comes after
-        // this warp's wait for iteration i - kProdWarps - R, so the slot's earlier
-        // phase (iteration i - 2R) has completed and the parity wait is unambiguous.
-        if (lane == 0) {
-            int i = 0;
-            bool dead = false;
-            for (int f = 0; f < 2 && !dead; ++f) {
-                const CUtensorMap *tma = f ? &tm_dn : &tm_gu;
-                const uint8_t *tsf = f ? p.dn_tsf : p.gu_tsf;
-                const int nmt = ph[f].nmt, nkb = ph[f].nkb;
-                for (Walker w(ph[f]); w.more(); ++i) {
-                    const int s = i % R, nb = w.boxes();
-                    if (i % kProdWarps != warp) {
-                        w.advance(nb);
-                        continue;
-                    }
-                    if (i >= R && !mbar_wait(empty + s, ((i / R) - 1) & 1, p.err, 30)) {
-                        dead = true;
-                        break;
-                    }
-                    const int e = act_s[w.slot];
-                    uint8_t *st = ring + (size_t)s * kStage;
-                    mbar_expect_tx(full + s, (uint32_t)nb * (kAPacked + 512 + (f ? kBBox + 512 : 0)));
-                    const int box0 = (e * nmt + w.mt) * nkb + w.kb;  // box-tiled plane: row origin 128 * box
-                    for (int b = 0; b < nb; ++b) tma_2d(st + b * kABytes, tma, full + s, 0, (box0 + b) * 128);
-                    bulk_g2s(st + kBoxes * kABytes, tsf + (((size_t)e * nmt + w.mt) * nkb + w.kb) * 512, nb * 512,
-                             full + s);
-                    if (f) {
-                        // the slot's activation operand: ready once all its gate_up tiles are done
-                        if (ready_s[w.slot] == 0) {
-                            const long long t0 = clock64();
-                            while (ready_s[w.slot] == 0) {
-                                if (clock64() - t0 > kWaitLimit) {
-                                    atomicCAS(p.err, 0, 31);
-                                    break;
-                                }
-                                __nanosleep(64);
-                            }
-                        }
-                        uint8_t *bst = st + kBoxes * (kABytes + 512);
-                        for (int b = 0; b < nb; ++b) tma_3d(bst + b * kBBox, &tm_act, full + s, (w.kb + b) * 128, 0, w.slot);
-                        bulk_g2s(bst + kBoxes * kBBox, p.act_sf + ((size_t)w.slot * nkb2 + w.kb) * 512, nb * 512,
-                                 full + s);
-                    }
-                    w.advance(nb);
-                }
-            }
+    // ---------------- the ring: this CTA's stages, two boxes each ----------------
+    // Stage j is filled into slot j % R.  The first R go out now; afterwards the
+    // last warp of the consuming group to finish with a slot refills it with the
+    // stage R further on, so no warp ever polls for free slots.
+    auto issue = [&](int j) {
+        const int32_t code = stg_s[j];
+        const int phase = (int)(((uint32_t)code >> 31) & 1u), nb = ((code >> 30) & 1) + 1;
+        const size_t box = (size_t)(code & 0x3fffffff);  // plane row of the first box: 128 * box
+        const int sl = j % R;
+        uint8_t *st = ring + (size_t)sl * kStageBytes;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the slot's reads before the copy's writes
+        mbar_expect_tx(full + sl, (uint32_t)nb * (kBoxBytes + 512));
+        const CUtensorMap *tm = phase ? (nb == 2 ? &tm_dn2 : &tm_dn1) : (nb == 2 ? &tm_gu2 : &tm_gu1);
+        tma_2d(st, tm, full + sl, 0, (int)(box * 128));
+        bulk_g2s(st + 2 * kBoxBytes, (phase ? p.dn_tsf : p.gu_tsf) + box * 512, (uint32_t)nb * 512, full + sl);
+        rel_s[R + sl] = j;
+    };
+    if (tid == 0) {
+        int j = 0;
+        for (int u = 0; u < nunits; ++u) {
+            int phase, slot, mt, kpart, kb0, kb1;
+            unit_span(units_s[u], phase, slot, mt, kpart, kb0, kb1);
+            const int e = act_s[slot];
+            const int nmt = phase ? nmt2 : nmt1, nkb = phase ? nkb2 : nkb1;
+            for (int kb = kb0; kb < kb1 && j < kMaxCtaStages; kb += 2, ++j)
+                stg_s[j] = (int32_t)(((uint32_t)phase << 31) | ((uint32_t)(min(2, kb1 - kb) - 1) << 30) |
+                                     (uint32_t)(((size_t)e * nmt + mt) * nkb + kb));
         }
-    } else if (warp == kWatchWarp) {
-        // ---------------- watcher: which phase-2 slots may load their operand ----------------
-        const Phase &q = ph[1];
-        if (q.hi > q.lo) {
-            const int per_slot = q.nmt * q.nkb;
-            for (int slot = q.lo / per_slot; slot <= (q.hi - 1) / per_slot; ++slot) {
-                wait_flags(p.tflag + (size_t)slot * kTilesPerSlot, nmt1, epoch, lane, p.err, 36);
+        misc[3] = j;
+        for (int i = 0; i < min(R, j); ++i) issue(i);
+    }
+    __syncthreads();
+    const int nst = misc[3];
+    {
+        // ---------------- consumers: 16 warps, two groups taking alternate stages ----------------
+        const int grp = warp / kGroupWarps, wl = warp % kGroupWarps;
+        const int g = lane >> 2, c = lane & 3;
+        const int r0 = 16 * wl + g;  // this lane's rows r0 and r0 + 8 of the 128-row tile
+        const uint32_t swz = (uint32_t)((r0 >> 1) & 3);  // SWIZZLE_64B: 16-B chunk ^= (row / 2) % 4
+        const uint32_t sc0 = (uint32_t)((r0 & 31) * 16 + (r0 >> 5) * 4);  // E8M0 chunk: byte (r%32)*16 + (r/32)*4 + j
+        const uint32_t sc1 = (uint32_t)(((r0 + 8) & 31) * 16 + ((r0 + 8) >> 5) * 4);
+        uint32_t off[4];  // this lane's 4 bytes of block q in a swizzled 64-B row
+#pragma unroll
+        for (int q = 0; q < 4; ++q) off[q] = (((uint32_t)q ^ swz) << 4) + 4 * c;
+        int i = 0;  // stage counter, the same walk as the producer's
+        for (int u = 0; u < nunits; ++u) {
+            int phase, slot, mt, kpart, kb0, kb1;
+            unit_span(units_s[u], phase, slot, mt, kpart, kb0, kb1);
+            const int e = act_s[slot];
+            if (phase == 1) {
+                // the slot's activation: complete once its last gate_up unit published it
+                if (tid == 0 && !misc[0]) {
+                    const long long t0 = clock64();
+                    while ((int)(ld_acquire(p.aflag + slot) - epoch) < 0) {
+                        if (clock64() - t0 > kWaitLimit) {
+                            atomicCAS(p.err, 0, 52);
+                            misc[0] = 1;
+                            break;
+                        }
+                        __nanosleep(32);
+                    }
+                }
+                compute_bar();
+                // this unit's operand columns: the activation over its K range, fp16 hi / lo
+                const int n8 = 16 * (kb1 - kb0);
+                for (int it = tid; it < (NCOL / 2) * n8; it += kComputeThreads) {
+                    const int t = it / n8, k0 = 128 * kb0 + 8 * (it - t * n8);
+                    float v[8];
+                    if (t < p.T) {
+                        const float *src = p.act + ((size_t)slot * p.T + t) * p.Ip + k0;
+                        const float4 a0 = __ldcg(reinterpret_cast<const float4 *>(src));
+                        const float4 a1 = __ldcg(reinterpret_cast<const float4 *>(src + 4));
+                        v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w;
+                        v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) v[q] = 0.0f;
+                    }
+                    put_split8(bd, sd, t, k0, v);
+                }
+                compute_bar();
+            }
+            const uint8_t *bcol = (phase ? bd : bx) + (size_t)g * (phase ? sd : sx) + 16 * c;
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int kb = kb0; kb < kb1; kb += 2, ++i) {
+                if ((i & 1) != grp) continue;
+                const int nb = min(2, kb1 - kb), s = i % R;
+                ring_wait(full + s, (i / R) & 1, misc, p.err, 51);  // when dead: compute on stale data
+                const uint8_t *st = ring + (size_t)s * kStageBytes;
+                // all of the stage's shared-memory loads first, then up to eight independent blocks
+                uint32_t w0[2][4], w1[2][4], sv0[2], sv1[2];
+                uint4 bv[2][4];
+#pragma unroll
+                for (int b = 0; b < 2; ++b) {
+                    if (b < nb) {
+                        const uint8_t *rows = st + b * kBoxBytes + r0 * 64;
+                        const uint8_t *xk = bcol + 2 * 128 * (kb + b);
+                        sv0[b] = *reinterpret_cast<const uint32_t *>(st + 2 * kBoxBytes + b * 512 + sc0);
+                        sv1[b] = *reinterpret_cast<const uint32_t *>(st + 2 * kBoxBytes + b * 512 + sc1);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            w0[b][q] = *reinterpret_cast<const uint32_t *>(rows + off[q]);
+                            w1[b][q] = *reinterpret_cast<const uint32_t *>(rows + 8 * 64 + off[q]);
+                            bv[b][q] = g < NCOL ? *reinterpret_cast<const uint4 *>(xk + 64 * q) : make_uint4(0u, 0u, 0u, 0u);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int b = 0; b < 2; ++b) {
+                    if (b < nb) {
+                        float f0[4], f1[4];
+                        e8m0x4_to_float(sv0[b], f0);
+                        e8m0x4_to_float(sv1[b], f1);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const uint4 a = e2m1x8_to_f16(w0[b][q]), a8 = e2m1x8_to_f16(w1[b][q]);
+                            // the block's two k-steps into separate accumulators: no MMA waits on another
+                            float d0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, d1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                            mma16816(d0, a.x, a8.x, a.y, a8.y, bv[b][q].x, bv[b][q].y);  // elements 8c..8c+3
+                            mma16816(d1, a.z, a8.z, a.w, a8.w, bv[b][q].z, bv[b][q].w);  // elements 8c+4..8c+7
+                            acc[0] = fmaf(d0[0] + d1[0], f0[q], acc[0]);
+                            acc[1] = fmaf(d0[1] + d1[1], f0[q], acc[1]);
+                            acc[2] = fmaf(d0[2] + d1[2], f1[q], acc[2]);
+                            acc[3] = fmaf(d0[3] + d1[3], f1[q], acc[3]);
+                        }
+                    }
+                }
+                // release the slot; the group's last warp refills it with stage i + R
                 __syncwarp();
-                if (lane == 0) ready_s[slot] = 1;
-            }
-        }
-    } else if (warp == kMmaWarp) {
-        // ---------------- MMA issuer ----------------
-        // The whole warp walks the stages (warp-uniform descriptors stay in
-        // uniform registers); one elected lane issues the tcgen05 operations.
-        uint32_t elected;
-        asm volatile("{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}" : "=r"(elected));
-        uint32_t idesc[4];
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) idesc[kk] = idesc_bs(kk, NT);
-        const uint32_t ring_a = smem_u32(ring), b1_a = smem_u32(b1), sfb1_a = smem_u32(sfb1);
-        int i = 0, seg = 0;
-        bool ok = true;  // the phase-1 operand was built before the roles split
-        for (int f = 0; f < 2 && ok; ++f) {
-            Walker w(ph[f]);
-            while (w.more() && ok) {
-                // one segment: this CTA's boxes of one tile
-                const int buf = seg & 1;
-                if (!mbar_wait(accempty + buf, ((seg >> 1) & 1) ^ 1, p.err, 33)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d = tmem + (uint32_t)(buf * NT);
-                uint32_t acc = 0;
-                for (;;) {
-                    const int s = i % R, nb = w.boxes();
-                    if (!mbar_wait(full + s, (i / R) & 1, p.err, 34)) {
-                        ok = false;
-                        break;
+                if (lane == 0) {
+                    if (atomicAdd(rel_s + s, 1) == kGroupWarps - 1) {
+                        rel_s[s] = 0;
+                        if (i + R < nst && !misc[0]) issue(i + R);
                     }
-                    tc_fence_after();
-                    const uint32_t st = ring_a + (uint32_t)s * kStage;
-                    const uint32_t sfa = tmem + 32u + 16u * (uint32_t)s, sfb = sfa + 8u;
-                    for (int b = 0; b < nb; ++b) {
-                        const uint32_t bsrc = f ? st + kBoxes * (kABytes + 512) + b * kBBox : b1_a + (uint32_t)(w.kb + b) * kBBox;
-                        const uint32_t sfb_src = f ? st + kBoxes * (kABytes + 512 + kBBox) + 512 * b
-                                                   : sfb1_a + (uint32_t)(w.kb + b) * 512;
-                        const uint32_t a0 = st + b * kABytes;
-                        if (elected) {
-                            sf_copy(sfa + 4 * b, st + kBoxes * kABytes + 512 * b);
-                            sf_copy(sfb + 4 * b, sfb_src);
-#pragma unroll
-                            for (int kk = 0; kk < 4; ++kk) {
-                                umma_bs(d, desc_sw128(a0 + 32 * kk), desc_sw128(bsrc + 32 * kk), idesc[kk], acc,
-                                        sfa + 4 * b, sfb + 4 * b);
-                                acc = 1u;
-                            }
-                        }
-                        acc = 1u;
-                    }
-                    if (elected) umma_commit(empty + s);
-                    __syncwarp();
-                    ++i;
-                    const bool tile_end = w.kb + nb == w.nkb;
-                    w.advance(nb);
-                    if (tile_end || !w.more()) break;
                 }
-                if (elected) umma_commit(accfull + buf);
                 __syncwarp();
-                ++seg;
             }
-        }
-    } else {
-        // ---------------- epilogue warps ----------------
-        const int et = tid - kEpiWarp0 * 32;  // 0..127
-        const int quad = warp & 3;         // TMEM lane quadrant
-        const int row = quad * 32 + lane;  // row of the 128-row tile this thread owns
-        // (b) the CTA's tile segments, phase 1 then phase 2
-        float *part = p.partial + (size_t)blockIdx.x * 2 * 128 * kNMax;
-        int seg = 0;
-        for (int f = 0; f < 2; ++f) {
-            const Phase &q = ph[f];
-            int x = q.lo;
-            while (x < q.hi) {
-                const int tile = x / q.nkb;
-                const int tbeg = tile * q.nkb, tend_full = tbeg + q.nkb;
-                const int tend = min(tend_full, q.hi);
-                const int slot = tile / q.nmt, mt = tile - slot * q.nmt;
-                const int e = act_s[slot];
-                const int base = offs_s[e];
-                int m_e = offs_s[e + 1] - base;
-                if (m_e > p.T) m_e = p.T;  // at most one pair per token (distinct top-k experts)
-                // this row's bias, loaded while the MMAs run
-                const int grp = row >> 4, j16 = row & 15;
-                const bool gate_lane = j16 < 8;
-                const int pr = 64 * mt + 8 * grp + (j16 & 7);  // phase 1: SwiGLU pair = activation column
-                const int h = 128 * mt + row;                   // phase 2: output row
-                float bias = 0.0f;
-                if (f == 0) bias = p.gu_b[(size_t)e * 2 * p.I + 2 * pr + (gate_lane ? 0 : 1)];
-                else if (h < p.H) bias = p.dn_b[(size_t)e * p.H + h];
-                const int buf = seg & 1;
-                float v[NT];
-                mbar_wait(accfull + buf, (seg >> 1) & 1, p.err, 35);
-                tc_fence_after();
-                {
-                    float t16[16];
-                    tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * NT), t16);
-#pragma unroll
-                    for (int c = 0; c < NT; ++c) v[c] = t16[c];
-                }
-                tc_fence_before();
-                mbar_arrive(accempty + buf);
-                ++seg;
-                const bool whole = x == tbeg && tend == tend_full;
-                const bool head = x == q.lo;
-                x = tend;
-                if (!whole) {
-                    // a split tile: the last of its CTAs to arrive adds the partials in CTA order
-                    const int b_first = cta_of_box(tbeg, q.nbox, G), b_last = cta_of_box(tend_full - 1, q.nbox, G);
-                    float *mine = part + (size_t)(head ? 0 : 1) * 128 * kNMax + (size_t)row * kNMax;
-#pragma unroll
-                    for (int c = 0; c < NT; c += 4)
-                        __stcg(reinterpret_cast<float4 *>(mine + c), make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]));
-                    __threadfence();
-                    epi_bar();
-                    if (et == 0) {
-                        unsigned nseg = 0;
-                        for (int b = b_first; b <= b_last; ++b)
-                            nseg += run_start(q.nbox, b + 1, G) > run_start(q.nbox, b, G) ? 1u : 0u;
-                        const unsigned old =
-                            atomicInc(p.cnt + ((size_t)f * p.S + slot) * kTilesPerSlot + mt, nseg - 1u);
-                        *last_flag = old == nseg - 1u;
-                    }
-                    epi_bar();
-                    const bool last = *last_flag != 0;
-                    epi_bar();
-                    if (!last) continue;
-                    __threadfence();
-#pragma unroll
-                    for (int c = 0; c < NT; ++c) v[c] = 0.0f;
-                    for (int b = b_first; b <= b_last; ++b) {
-                        const int blo = run_start(q.nbox, b, G), bhi = run_start(q.nbox, b + 1, G);
-                        if (bhi <= blo) continue;  // empty run: no piece
-                        // CTA b's piece: the head of its run if the run starts inside this tile
-                        const float *src =
-                            p.partial + ((size_t)b * 2 + (blo >= tbeg ? 0 : 1)) * 128 * kNMax + (size_t)row * kNMax;
-#pragma unroll
-                        for (int c = 0; c < NT; c += 4) {
-                            const float4 t4 = __ldcg(reinterpret_cast<const float4 *>(src + c));
-                            v[c] += t4.x;
-                            v[c + 1] += t4.y;
-                            v[c + 2] += t4.z;
-                            v[c + 3] += t4.w;
-                        }
+            // ---- unit epilogue: group 1's sums join group 0's (fixed order) ----
+            if (grp == 1)
+                *reinterpret_cast<float4 *>(red + (wl * 32 + lane) * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            compute_bar();
+            if (grp == 0) {
+                const float4 o = *reinterpret_cast<const float4 *>(red + (wl * 32 + lane) * 4);
+                // lane (g, c) holds rows r0, r0 + 8 for columns 2c (hi) and 2c + 1 (lo): token c
+                const float v0 = (acc[0] + o.x) + (acc[1] + o.y);
+                const float v1 = (acc[2] + o.z) + (acc[3] + o.w);
+                if (c < p.T) {
+                    if (phase == 0) {
+                        // rows 16w + g and 16w + g + 8 are the gate and up rows of pair 64 mt + 8w + g
+                        const int pr = 64 * mt + 8 * wl + g;
+                        const float gate = v0 + p.gu_b[(size_t)e * 2 * p.I + 2 * pr];
+                        const float up = v1 + p.gu_b[(size_t)e * 2 * p.I + 2 * pr + 1];
+                        p.act[((size_t)slot * p.T + c) * p.Ip + pr] = swiglu(gate, up);
+                    } else {
+                        const int h0 = 128 * mt + r0, h1 = h0 + 8;
+                        float *yrow = p.yb + (((size_t)slot * 2 + kpart) * p.T + c) * p.H;
+                        if (h0 < p.H) yrow[h0] = v0 + (kpart == 0 ? p.dn_b[(size_t)e * p.H + h0] : 0.0f);
+                        if (h1 < p.H) yrow[h1] = v1 + (kpart == 0 ? p.dn_b[(size_t)e * p.H + h1] : 0.0f);
                     }
                 }
-                // ---- finalize the tile ----
-                if (f == 0) {
-                    // rows 16g'+j (j < 8) hold the gate of pair 8g'+j, row +8 its up row
-                    for (int g = 0; g < m_e; ++g) {
-                        const int t = perm_s[base + g] / p.k;
-                        float val = 0.0f;
-#pragma unroll
-                        for (int c = 0; c < NT; c += 4)
-                            if (c / 4 == t) val = v[c] + v[c + 1] + v[c + 2] + v[c + 3];
-                        val += bias;
-                        const float up = __shfl_down_sync(0xffffffffu, val, 8);
-                        const float a = gate_lane ? swiglu(val, up) : 0.0f;
-                        // the 32-pair block of this row: rows 0-63 (quadrants 0, 1) or 64-127 (2, 3)
-                        float m = gate_lane ? fabsf(a) : 0.0f;
-#pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-                        if (lane == 0) xchg[quad] = m;
-                        epi_bar();
-                        const float amax = fmaxf(xchg[quad & 2], xchg[(quad & 2) + 1]);
-                        epi_bar();
-                        const int e0 = block_exp(amax);
-                        if (gate_lane) {
-                            const uint32_t q4 = quant4(a, e0);
-                            uint8_t *dst = p.act_q + ((size_t)slot * 16 + 4 * g) * p.Ip + pr;
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) dst[(size_t)j * p.Ip] = (uint8_t)(q4 >> (8 * j));
-                        }
-                        if (lane == 0 && (quad & 1) == 0) {  // one writer per block of 32 pairs
-                            const int blk = 2 * mt + (quad >> 1);
-                            uint8_t *sfd = p.act_sf + ((size_t)slot * (p.Ip / 128) + blk / 4) * 512;
-#pragma unroll
-                            for (int j = 0; j < 4; ++j)
-                                sfd[(4 * g + j) * 16 + (blk % 4)] = (uint8_t)term_scale_byte(e0, j);
-                        }
-                    }
-                } else if (h < p.H) {
-#pragma unroll
-                    for (int c = 0; c < NT; c += 4)
-                        if (c / 4 < m_e) p.y[(size_t)(base + c / 4) * p.H + h] = v[c] + v[c + 1] + v[c + 2] + v[c + 3] + bias;
-                }
-                // the tile is complete: publish it to the CTAs that consume it
                 __threadfence();
-                epi_bar();
-                if (et == 0) publish(p.tflag + ((size_t)f * p.S + slot) * kTilesPerSlot + mt, epoch);
             }
-        }
-        // (c) slot-order combine with the residual: CTA b owns output rows
-        //     128b..128b+127 and waits only for those rows' down tiles
-        if ((int)blockIdx.x < nmt2) {
-            const int mt2 = blockIdx.x;
-            if (et < 32) {
-                for (int s0 = 0; s0 < n_active; s0 += 32) {
-                    const int ns = min(32, n_active - s0);
-                    if (lane < ns)
-                        wait_flags(p.tflag + ((size_t)p.S + s0 + lane) * kTilesPerSlot + mt2, 1, epoch, 0, p.err, 37);
-                }
+            compute_bar();
+            if (tid == 0) {
+                const unsigned n = phase == 0 ? (unsigned)nmt1 : (unsigned)(nkp * n_active);
+                unsigned *cnt = phase == 0 ? p.cnt_gu + slot : p.cnt_dn + mt;
+                const unsigned old = atomicInc(cnt, n - 1u);
+                misc[1] = old == n - 1u;
+                if (old == n - 1u && phase == 0) publish(p.aflag + slot, epoch);
             }
-            epi_bar();
-            const int h = 128 * mt2 + et;
-            if (h < p.H) {
-                for (int t = 0; t < p.T; ++t) {
+            compute_bar();
+            if (phase == 1 && misc[1]) {
+                // the last down unit of output tile mt: combine its rows for every token in
+                // slot order (layer.go:109-121)
+                __threadfence();
+                for (int it = tid; it < p.T * 128; it += kComputeThreads) {
+                    const int t = it >> 7, h = 128 * mt + (it & 127);
+                    if (h >= p.H) continue;
                     double m = 0.0;
-                    for (int s = 0; s < p.k; ++s)
-                        m += (double)w_s[t * p.k + s] * (double)__ldcg(p.y + (size_t)inv_s[t * p.k + s] * p.H + h);
+                    for (int s = 0; s < p.k; ++s) {
+                        const int q = t * p.k + s;
+                        const float *yp = p.yb + ((size_t)sl_s[q] * 2 * p.T + t) * p.H + h;
+                        float yv = __ldcg(yp);
+                        if (nkp == 2) yv += __ldcg(yp + (size_t)p.T * p.H);
+                        m += (double)w_s[q] * (double)yv;
+                    }
                     p.out[(size_t)t * p.H + h] = p.residual[(size_t)t * p.H + h] + (float)m;
                 }
             }
         }
-        if (et == 0) p.bar->epoch[blockIdx.x] = epoch;
     }
-    tc_fence_before();
     __syncthreads();
-    tc_fence_after();
-    if (warp == kMmaWarp)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    if (tid == 0) {
+        // copies still in flight (only after a failed wait) land before the CTA exits
+        if (misc[0])
+            for (int sl = 0; sl < R; ++sl)
+                if (rel_s[R + sl] >= 0) mbar_wait(full + sl, (rel_s[R + sl] / R) & 1, p.err, 54);
+        p.bar->epoch[blockIdx.x] = epoch;
+    }
 }
 
 // ---- host side -------------------------------------------------------------------------
@@ -789,53 +706,172 @@ const DecodeCaps &caps(int device) {
     return g_caps[device];
 }
 
-int dec_n(int T) { return 4 * T <= 8 ? 8 : 16; }
+int dec_ncol(int T) { return T <= 1 ? 2 : (T <= 2 ? 4 : 8); }
 
-int dec_stages(int T, int Hp, int E, int k) {
-    const int nt = dec_n(T);
-    const DecLayout none = dec_layout(T, Hp, E, k, 0, nt);
+// Ring stages that fit beside the operand columns (even: each slot serves one group).
+int dec_stages(int T, int Hp, int Ip, int E, int k) {
+    const DecLayout none = dec_layout(T, Hp, Ip, E, k, 0, dec_ncol(T));
     if (none.total >= kSmemBudget) return 0;
-    const int st = (int)((kSmemBudget - none.total) / (stage_bytes(nt) + 16));
-    return st > kMaxStages ? kMaxStages : st;
+    int st = (int)((kSmemBudget - none.total) / (kStageBytes + 16));
+    st = std::min(st, kMaxStages);
+    return st & ~1;
 }
 
 int dec_slots(const Dims &d) { return d.E < kDecodeMaxTokens * d.k ? d.E : kDecodeMaxTokens * d.k; }
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// The units of every CTA for each number of active slots n = 1..S: longest
+// processing time first over the units' box counts (all units of a phase are
+// the same size, so this is a balanced round over the least-loaded CTAs),
+// gate_up units before down units, each in slot order.  CTA b's rows sit in
+// words [b * kSchedWords, (b + 1) * kSchedWords): S + 1 offsets (relative to
+// the row start), then the unit lists for n = 1..S.
+struct Schedule {
+    std::vector<int32_t> rows;   // [G][kSchedWords]
+    int max_units = 0;           // most units of one CTA for one n
+    int max_words = 0;           // most words of one CTA's rows
+};
+
+Schedule build_schedule(const Dims &d, int G) {
+    Schedule s;
+    const int S = dec_slots(d);
+    const int nkb1 = kpad128(d.H) / 128, nkb2 = kpad128(d.I) / 128;
+    const int nmt1 = 2 * d.I / 128, nmt2 = (d.H + 127) / 128;
+    const int nkp = nkb2 >= 2 ? 2 : 1, half2 = (nkb2 + 1) / 2;
+    std::vector<std::vector<int32_t>> rows(G, std::vector<int32_t>(S + 1, 0));
+    std::vector<std::vector<int32_t>> lists(G);
+    std::vector<long long> load(G);
+    for (int b = 0; b < G; ++b) rows[b][0] = S + 1;
+    for (int n = 1; n <= S; ++n) {
+        for (auto &l : lists) l.clear();
+        std::fill(load.begin(), load.end(), 0);
+        auto place = [&](int32_t code, int cost) {
+            int best = 0;
+            for (int b = 1; b < G; ++b)
+                if (load[b] < load[best]) best = b;
+            lists[best].push_back(code);
+            load[best] += cost;
+        };
+        for (int sl = 0; sl < n; ++sl)
+            for (int m = 0; m < nmt1; ++m) place(unit_code(0, sl, m, 0), nkb1);
+        for (int sl = 0; sl < n; ++sl)
+            for (int m = 0; m < nmt2; ++m)
+                for (int kp = 0; kp < nkp; ++kp)
+                    place(unit_code(1, sl, m, kp), nkp == 1 ? nkb2 : (kp ? nkb2 - half2 : half2));
+        for (int b = 0; b < G; ++b) {
+            rows[b].insert(rows[b].end(), lists[b].begin(), lists[b].end());
+            rows[b][n] = (int32_t)rows[b].size();
+            s.max_units = std::max(s.max_units, (int)lists[b].size());
+        }
+    }
+    s.rows.assign((size_t)G * kSchedWords, 0);
+    for (int b = 0; b < G; ++b) {
+        s.max_words = std::max(s.max_words, (int)rows[b].size());
+        std::copy_n(rows[b].begin(), std::min<size_t>(rows[b].size(), kSchedWords), s.rows.begin() + (size_t)b * kSchedWords);
+    }
+    return s;
+}
+
+struct DecScratch {
+    size_t act, yb, cnt_gu, cnt_dn, aflag, rflag, sched, total;
+};
+
+DecScratch dec_scratch(const Dims &d, int G, const Schedule &s) {
+    const int S = dec_slots(d), Ip = kpad128(d.I), nmt2 = (d.H + 127) / 128;
+    DecScratch L;
+    size_t o = 0;
+    L.act = o;
+    o += align256((size_t)S * kDecodeMaxTokens * Ip * 4);
+    L.yb = o;
+    o += align256((size_t)S * 2 * kDecodeMaxTokens * d.H * 4);
+    L.cnt_gu = o;
+    o += align256((size_t)S * 4);
+    L.cnt_dn = o;
+    o += align256((size_t)nmt2 * 4);
+    L.aflag = o;
+    o += align256((size_t)S * 4);
+    L.rflag = o;
+    o += align256((size_t)G * 4);
+    L.sched = o;
+    o += align256(s.rows.size() * 4);
+    L.total = o;
+    return L;
+}
+
+int grid_of(int device) { return device >= 0 && device < 64 && caps(device).sms > 0 ? caps(device).sms : 1; }
+
+// Box-tiled E2M1 plane as bytes: rows of 64 B (128 packed values), boxes of
+// box_rows rows (one or two 128-row K boxes), SWIZZLE_64B.
+cudaError_t map_plane(CUtensorMap *tm, const void *base, uint64_t rows, uint32_t box_rows) {
+    cuuint64_t dims[2] = {64, rows};
+    cuuint64_t strides[1] = {64};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = encode_fn()(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, es,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 }  // namespace
 
 size_t decode_scratch_bytes(const Dims &d, int device) {
-    const int G = device >= 0 && device < 64 && caps(device).sms > 0 ? caps(device).sms : 1;
-    const int S = dec_slots(d), Ip = kpad128(d.I);
-    return align256((size_t)S * 16 * Ip) + align256((size_t)S * (Ip / 128) * 512) +
-           align256((size_t)G * 2 * 128 * kNMax * 4) + (size_t)2 * 2 * S * kTilesPerSlot * 4 + (size_t)G * 4;
+    const int G = grid_of(device);
+    return dec_scratch(d, G, build_schedule(d, G)).total;
 }
 
 cudaError_t init_decode_scratch(const Dims &d, int device, void *scratch, cudaStream_t st) {
-    const int S = dec_slots(d), Ip = kpad128(d.I);
+    (void)st;
+    const int G = grid_of(device);
+    const Schedule s = build_schedule(d, G);
+    const DecScratch L = dec_scratch(d, G, s);
     uint8_t *b = static_cast<uint8_t *>(scratch);
-    cudaError_t e = cudaMemsetAsync(b, 0, decode_scratch_bytes(d, device), st);
-    if (e != cudaSuccess) return e;
-    // activation scale bytes: 2^0 wherever no block is ever written (K padding)
-    return cudaMemsetAsync(b + align256((size_t)S * 16 * Ip), 127, (size_t)S * (Ip / 128) * 512, st);
+    cudaError_t e = cudaMemset(b, 0, L.total);  // activation padding, counters and flags start at 0
+    if (e == cudaSuccess) e = cudaMemcpy(b + L.sched, s.rows.data(), s.rows.size() * 4, cudaMemcpyHostToDevice);
+    return e;
 }
 
 bool decode_supported(const Dims &d, int T, int device) {
     if (T < 1 || T > kDecodeMaxTokens || device < 0 || device >= 64) return false;
     const DecodeCaps &cp = caps(device);
     if (!cp.coop || cp.sms <= 0 || cp.sms > kDecodeMaxCtas || !get_encode()) return false;
-    if ((2 * d.I) % 128 || 2 * d.I / 128 > kTilesPerSlot || (d.H + 127) / 128 > kTilesPerSlot) return false;
-    // a ring of at least kProdWarps stages: producer warp w's waits on a slot's
-    // empty barrier then follow the phases in order (see the producers)
-    return dec_stages(T, kpad128(d.H), d.E, d.k) >= kProdWarps;
+    if ((2 * d.I) % 128 || d.H > 4096 || d.I > 4096 || d.E > 256 || d.k > 32 || dec_slots(d) > 1023) return false;
+    if (2 * d.I / 128 > 4095 || (d.H + 127) / 128 > 4095) return false;
+    if (dec_stages(T, kpad128(d.H), kpad128(d.I), d.E, d.k) < 2) return false;
+    // the routing stages the schedule rows, the residual rows and the gain in the ring
+    const int Hp = kpad128(d.H);
+    if ((size_t)dec_stages(T, Hp, kpad128(d.I), d.E, d.k) * kStageBytes <
+        (size_t)4 * (kSchedWords + (size_t)(T + 1) * Hp))
+        return false;
+    static thread_local Dims last{};
+    static thread_local int last_dev = -1;
+    static thread_local bool last_ok = false;
+    if (last_dev != device || last.H != d.H || last.I != d.I || last.E != d.E || last.k != d.k) {
+        last = d;
+        last_dev = device;
+        const Schedule s = build_schedule(d, cp.sms);
+        last_ok = s.max_units <= kMaxUnits && s.max_words <= kSchedWords;
+    }
+    return last_ok;
 }
 
 cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, const float *residual, int T,
                           void *scratch, float *y, float *out, DecodeBarrier *bar, int32_t *err, int device,
                           cudaStream_t st) {
+    (void)y;  // the kernel keeps its expert outputs in its own scratch
     const int S = dec_slots(d), Hp = kpad128(d.H), Ip = kpad128(d.I);
     const int G = caps(device).sms;
+    const int ncol = dec_ncol(T);
+    // the scratch layout depends only on the shape and the grid: recompute the offsets
+    static thread_local Dims last{};
+    static thread_local int last_dev = -1;
+    static thread_local DecScratch lay{};
+    if (last_dev != device || last.H != d.H || last.I != d.I || last.E != d.E || last.k != d.k) {
+        last = d;
+        last_dev = device;
+        lay = dec_scratch(d, G, build_schedule(d, G));
+    }
     uint8_t *b = static_cast<uint8_t *>(scratch);
     DecodeParams p{};
     p.residual = residual;
@@ -845,20 +881,17 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
     p.router_b = L.router_b;
     p.eps = d.eps;
     p.route = r;
+    p.rflag = reinterpret_cast<unsigned *>(b + lay.rflag);
     p.gu_tsf = L.gu_tsf;
     p.dn_tsf = L.dn_tsf;
     p.gu_b = L.gu_b;
     p.dn_b = L.dn_b;
-    p.act_q = b;
-    b += align256((size_t)S * 16 * Ip);
-    p.act_sf = b;
-    b += align256((size_t)S * (Ip / 128) * 512);
-    p.partial = reinterpret_cast<float *>(b);
-    b += align256((size_t)G * 2 * 128 * kNMax * 4);
-    p.cnt = reinterpret_cast<uint32_t *>(b);
-    p.tflag = reinterpret_cast<unsigned *>(p.cnt + (size_t)2 * S * kTilesPerSlot);
-    p.rflag = p.tflag + (size_t)2 * S * kTilesPerSlot;
-    p.y = y;
+    p.act = reinterpret_cast<float *>(b + lay.act);
+    p.yb = reinterpret_cast<float *>(b + lay.yb);
+    p.cnt_gu = reinterpret_cast<uint32_t *>(b + lay.cnt_gu);
+    p.cnt_dn = reinterpret_cast<uint32_t *>(b + lay.cnt_dn);
+    p.aflag = reinterpret_cast<unsigned *>(b + lay.aflag);
+    p.sched = reinterpret_cast<const int32_t *>(b + lay.sched);
     p.bar = bar;
     p.err = err;
     p.T = T;
@@ -869,16 +902,17 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
     p.Hp = Hp;
     p.Ip = Ip;
     p.S = S;
-    p.stages = dec_stages(T, Hp, d.E, d.k);
-    p.N = dec_n(T);
-    if (p.stages < kProdWarps || !get_encode()) return cudaErrorInvalidValue;
-    CUtensorMap tm_gu, tm_dn, tm_act;
-    cudaError_t e = map_boxes(&tm_gu, L.gu_tq, tq_bytes(d.E, 2 * d.I, d.H) / 64);
-    if (e == cudaSuccess) e = map_boxes(&tm_dn, L.dn_tq, tq_bytes(d.E, d.H, d.I) / 64);
-    if (e == cudaSuccess) e = map3d(&tm_act, p.act_q, false, (uint64_t)Ip, 16, (uint64_t)S, (uint32_t)p.N);
+    p.stages = dec_stages(T, Hp, Ip, d.E, d.k);
+    if (p.stages < 2 || !get_encode()) return cudaErrorInvalidValue;
+    CUtensorMap tm_gu2, tm_gu1, tm_dn2, tm_dn1;
+    const uint64_t gu_rows = tq_bytes(d.E, 2 * d.I, d.H) / 64, dn_rows = tq_bytes(d.E, d.H, d.I) / 64;
+    cudaError_t e = map_plane(&tm_gu2, L.gu_tq, gu_rows, 256);
+    if (e == cudaSuccess) e = map_plane(&tm_gu1, L.gu_tq, gu_rows, 128);
+    if (e == cudaSuccess) e = map_plane(&tm_dn2, L.dn_tq, dn_rows, 256);
+    if (e == cudaSuccess) e = map_plane(&tm_dn1, L.dn_tq, dn_rows, 128);
     if (e != cudaSuccess) return e;
-    const size_t smem = dec_layout(T, Hp, d.E, d.k, p.stages, p.N).total;
-    auto kern = p.N == 8 ? decode_kernel<8> : decode_kernel<16>;
+    const size_t smem = dec_layout(T, Hp, Ip, d.E, d.k, p.stages, ncol).total;
+    auto kern = ncol == 2 ? decode_kernel<2> : (ncol == 4 ? decode_kernel<4> : decode_kernel<8>);
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
@@ -891,7 +925,7 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, tm_gu, tm_dn, tm_act, p);
+    return cudaLaunchKernelEx(&cfg, kern, tm_gu2, tm_gu1, tm_dn2, tm_dn1, p);
 }
 
 }  // namespace amoe
