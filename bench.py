@@ -48,7 +48,7 @@ MEASURED_PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_FILE = os.path.join(ROOT, "profiles", "ncu_traffic.json")
 # arithmetic of each expert path (weights stay MXFP4; accumulation f32; router and softmax f64)
 DTYPE_TENSOR = "mxfp4 x e4m3 (4 terms per value) -> f32"
-DTYPE_DECODE = "mxfp4 x e4m3 (4 terms per value) -> f32"
+DTYPE_DECODE = "mxfp4 x fp16 (hi + lo) -> f32"
 DTYPE_GEMV = "mxfp4 x fp16 (hi + lo) -> f32"
 FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
@@ -298,7 +298,7 @@ def run_streaming(args):
         "metric": "decode tokens/s, 24-layer GPT-OSS-20B-shaped MoE stack streamed from pinned host memory",
         "value": 1e3 / ms, "unit": "tokens/s", "n_gpus": 1, "steps": n, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": DTYPE_DECODE, "data": "synthetic (seeded, seed (2, layer))",
+        "dtype": DTYPE_TENSOR if args.stream_experts else DTYPE_DECODE, "data": "synthetic (seeded, seed (2, layer))",
         "config": {"workload": f"gptoss20b-moe-stream layers={L} T=1 "
                                + ("routed experts per layer" if args.stream_experts else "whole layers, 2 slots"),
                    "config_index": 2, "stream_experts": args.stream_experts,
@@ -565,7 +565,8 @@ def main():
                    2: "bs_gemm_kernel (tcgen05 kind::mxf8f6f4 block-scaled: E2M1 weights x 4-term E4M3 "
                       "activations)"}[st["last_path"] or 1]
     if dom == "decode_experts":
-        kernel_name = "decode_kernel (one cooperative launch: routing + gate_up + down + combine, tcgen05 mxf8f6f4 block-scaled)"
+        kernel_name = ("decode_kernel (one cooperative launch: routing + gate_up + down + combine; packed MXFP4 "
+                       "boxes expanded in registers, mma.sync with fp16 hi/lo activation columns)")
     traffic = None
     try:
         traffic = json.load(open(TRAFFIC_FILE)).get(f"{dom}:{cfg}")
@@ -573,10 +574,15 @@ def main():
         pass
     if pairs_per_expert >= 32:
         achieved = flops / (dom_ms / 1e3) / 1e12
-        roof = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": achieved / pk["bf16_tflops"], "traffic": traffic,
+        # a kernel timed inside a long pass runs at the power-capped clock: the sustained
+        # GEMM figure is its peak; a short burst is compared with the burst figure
+        sustained = (clk is not None and "sw_power_cap" in (clk.get("reasons") or [])) or ms * args.steps >= 250.0
+        peak = pk["bf16_tflops_sustained"] if sustained and pk.get("bf16_tflops_sustained") else pk["bf16_tflops"]
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": traffic,
                 "kernel": f"{dom} {kernel_name}", "algorithmic_flop_per_launch": flops,
-                "launch_ms": dom_ms, "peak_source": f"{pk['source']} bf16 dense (burst)",
+                "launch_ms": dom_ms,
+                "peak_source": f"{pk['source']} bf16 dense ({'sustained' if peak != pk['bf16_tflops'] else 'burst'})",
                 "frac_of_fp4_dense_nominal_9pflops": achieved / 9000.0}
     else:
         achieved = bytes_ / (dom_ms / 1e3) / 1e9
