@@ -153,22 +153,20 @@ struct GemvRows {
     const int32_t *gate = nullptr;  // if set, the launch does nothing unless *gate == gate_want
     int gate_want = 0;
 };
-// Fused decode expert stage (decode.cu): gate_up + SwiGLU, down, combine in one
-// cooperative launch for T <= kDecodeMaxTokens.
+// Fused decode step (decode.cu): routing, gate_up + SwiGLU, down and the combine in
+// one cooperative launch for T <= kDecodeMaxTokens.  Its cross-CTA flags carry the
+// launch count, which each CTA keeps here.
 constexpr int kDecodeMaxTokens = 4;
 constexpr int kDecodeMaxCtas = 1024;
 struct DecodeBarrier {
     unsigned epoch[kDecodeMaxCtas];   // launches CTA b has completed (written only by CTA b)
-    unsigned arrive[kDecodeMaxCtas];  // last grid barrier CTA b arrived at
-    unsigned release;                 // last grid barrier CTA 0 released
 };
 bool decode_supported(const Dims &d, int T, int device);
 // scratch: decode_scratch_bytes(), prepared once by init_decode_scratch()
 size_t decode_scratch_bytes(const Dims &d, int device);
 cudaError_t init_decode_scratch(const Dims &d, int device, void *scratch, cudaStream_t st);
 cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, const float *residual, int T,
-                          void *scratch, float *y, float *out, DecodeBarrier *bar, int32_t *err, int device,
-                          cudaStream_t st);
+                          void *scratch, float *out, DecodeBarrier *bar, int32_t *err, int device, cudaStream_t st);
 
 // T: upper bound on any expert's row count (sizes the token groups per pass).
 cudaError_t launch_gemv_gate_up(const Dims &d, const LayerDev &L, const GemvRows &rows, int T,

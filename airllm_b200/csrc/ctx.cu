@@ -137,7 +137,7 @@ struct amoe_ctx {
     float *y = nullptr;
     int32_t *err_flag = nullptr;  // set by a kernel whose bounded wait gave up (0 = fine)
     void *bs_scratch = nullptr;  // token tiles and the E4M3-term operands of the block-scaled GEMMs
-    DecodeBarrier *dec_bar = nullptr;  // grid barrier state of the fused decode kernel
+    DecodeBarrier *dec_bar = nullptr;  // launch counts of the fused decode kernel's CTAs
     void *dec_scratch = nullptr;       // its activation operand, partial tiles and tile counters
     float *io_in = nullptr, *io_out = nullptr;
     int32_t *io_idx = nullptr;
@@ -759,8 +759,8 @@ int forward_impl(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, f
     } else if (fused_decode) {
         timer.mark(1);
         int32_t *flag = c->err_flag;
-        AMOE_CUDA(c, launch_decode(d, L, r, residual, T, c->dec_scratch, c->y, out, c->dec_bar, flag,
-                                   c->cfg.device, st));
+        AMOE_CUDA(c, launch_decode(d, L, r, residual, T, c->dec_scratch, out, c->dec_bar, flag, c->cfg.device,
+                                   st));
         timer.mark(6);
         c->stats.launches += 1;
         fused = true;

@@ -857,9 +857,7 @@ bool decode_supported(const Dims &d, int T, int device) {
 }
 
 cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, const float *residual, int T,
-                          void *scratch, float *y, float *out, DecodeBarrier *bar, int32_t *err, int device,
-                          cudaStream_t st) {
-    (void)y;  // the kernel keeps its expert outputs in its own scratch
+                          void *scratch, float *out, DecodeBarrier *bar, int32_t *err, int device, cudaStream_t st) {
     const int S = dec_slots(d), Hp = kpad128(d.H), Ip = kpad128(d.I);
     const int G = caps(device).sms;
     const int ncol = dec_ncol(T);

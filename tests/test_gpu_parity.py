@@ -77,14 +77,14 @@ def test_small_layers_match_oracle(cuda_device, path, H, I, E, k, T):
     (64, 64, 256, 8, 4), (128, 64, 5, 2, 4), (2880, 2880, 32, 4, 2),
 ])
 def test_fused_decode_stage_matches_oracle(cuda_device, H, I, E, k, T):
-    # T <= 4 on the GEMV path runs gate_up, down and the combine as one cooperative
-    # launch (two grid barriers); the stage timer shows which kernel ran
+    # T <= 4 on the GEMV path runs routing, gate_up, down and the combine as one
+    # cooperative launch; the stage timer shows which kernel ran
     layer = W.small_layer(hidden=H, intermediate=I, experts=E, top_k=k, seed=7 * T + E)
     x = W.make_tokens(W.MoEShape(H, I, E, k), T, T + 1)
     blk = moe.MoEBlock.for_layer(layer, max_tokens=T, path=moe.PATH_GEMV)
     blk.upload_layer(0, layer)
     blk.set_profiling(True)
-    outs = [blk.forward(x)[0] for _ in range(3)]  # the grid barrier state carries across launches
+    outs = [blk.forward(x)[0] for _ in range(3)]  # epoch flags and arrival counters carry across launches
     st = blk.stats(reset=True)
     blk.close()
     assert st["stage_ms"]["decode_experts"] > 0 and st["stage_ms"]["gate_up"] == 0
