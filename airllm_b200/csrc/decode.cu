@@ -48,8 +48,10 @@
 // marks the CTA dead (later waits return at once, no further stage is issued,
 // the copies in flight are waited for) and the kernel winds down.
 #include <algorithm>
+#include <cstring>
 #include <vector>
 
+#include "../../include/amoe.h"
 #include "tc_ptx.cuh"
 
 namespace amoe {
@@ -68,6 +70,7 @@ constexpr uint32_t kStageBytes = 2 * kBoxBytes + 2 * 512;  // two boxes, then th
 constexpr int kMaxStages = 12;
 constexpr int kMaxUnits = 64;                   // units per CTA
 constexpr int kSchedWords = 1024;               // one CTA's schedule rows (int32)
+static_assert(kSchedWords == AMOE_DECODE_SCHED_WORDS, "the table row size is part of the C ABI");
 constexpr int kMaxCtaStages = kMaxUnits * 16;   // ring stages of one CTA (a unit has <= 16: K <= 4096)
 constexpr size_t kSmemBudget = 232448;          // dynamic shared memory per block (227 KB)
 
@@ -927,3 +930,24 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
 }
 
 }  // namespace amoe
+
+// The decode kernel's work table, as the context builds it (host arithmetic only).
+extern "C" AMOE_API int amoe_decode_schedule(int32_t hidden, int32_t intermediate, int32_t experts, int32_t top_k,
+                                             int32_t ctas, int32_t *rows) {
+    using namespace amoe;
+    if (hidden < 64 || hidden % 64 || hidden > 4096 || intermediate < 64 || intermediate % 64 ||
+        intermediate > 4096 || experts < 1 || experts > 256 || top_k < 1 || top_k > experts || top_k > 32 ||
+        ctas < 1 || ctas > kDecodeMaxCtas) {
+        set_thread_error("decode schedule: hidden and intermediate must be multiples of 64 up to 4096, "
+                         "1 <= top_k <= min(experts, 32), experts <= 256, 1 <= ctas <= 1024");
+        return AMOE_ERR_INVALID;
+    }
+    const Dims d{hidden, intermediate, experts, top_k, 1e-5f};
+    const Schedule s = build_schedule(d, ctas);
+    if (s.max_units > kMaxUnits || s.max_words > kSchedWords) {
+        set_thread_error("decode schedule: a CTA would get more units than its table row holds");
+        return AMOE_ERR_INVALID;
+    }
+    if (rows) std::memcpy(rows, s.rows.data(), s.rows.size() * sizeof(int32_t));
+    return AMOE_OK;
+}

@@ -83,6 +83,7 @@ SIGNATURES = {
     "amoe_get_stats": (ctypes.c_int, [_vp, ctypes.POINTER(AmoeStats), _i32]),
     "amoe_ep_unique_id": (ctypes.c_int, [_vp]),
     "amoe_ep_layout": (ctypes.c_int, [_i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "amoe_decode_schedule": (ctypes.c_int, [_i32, _i32, _i32, _i32, _i32, _vp]),
     "amoe_route_noalloc": (ctypes.c_int, [_i32, _i32, _i32, _i32, ctypes.c_float, _vp, _i32, _vp, _vp, _vp,
                                           _vp, _vp, _vp, _vp]),
     "amoe_gguf_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
@@ -162,6 +163,20 @@ def ep_layout(n_ranks: int, experts_per_rank: int, rank: int, table) -> dict:
     out["seg_start"] = out["seg_start"].reshape(El, N)
     out["src_pos"] = out["src_pos"].reshape(El, N)
     return out
+
+
+DECODE_SCHED_WORDS = 1024
+
+
+def decode_schedule(hidden: int, intermediate: int, experts: int, top_k: int, ctas: int) -> np.ndarray:
+    """The fused decode kernel's work table [ctas][DECODE_SCHED_WORDS]
+    (amoe_decode_schedule; host arithmetic, no GPU needed)."""
+    lib = load_library()
+    rows = np.zeros((ctas, DECODE_SCHED_WORDS), np.int32)
+    rc = lib.amoe_decode_schedule(hidden, intermediate, experts, top_k, ctas, rows.ctypes.data)
+    if rc != AMOE_OK:
+        raise AmoeError(rc, lib.amoe_last_error(None).decode())
+    return rows
 
 
 class GGUFFile:

@@ -206,6 +206,18 @@ AMOE_API int amoe_ep_layout(int32_t n_ranks, int32_t experts_per_rank, int32_t r
                             const int32_t *table, int32_t *send_base, int32_t *offsets_loc,
                             int32_t *seg_start, int32_t *src_pos);
 
+/* The fused decode kernel's work table (T <= 4; no GPU needed): the units each of
+ * `ctas` CTAs runs, built the way the context builds it.  CTA b's row holds
+ * AMOE_DECODE_SCHED_WORDS int32 words: S + 1 offsets (S = min(experts, 4 * top_k)),
+ * then for n = 1..S active experts the units at words [n - 1]..[n] of the row.
+ * A unit is bit 30: phase (0 gate_up, 1 down), bits 20-29: active-slot index,
+ * bits 8-19: 128-row weight tile, bit 0: K half (down units).
+ * rows: [ctas][AMOE_DECODE_SCHED_WORDS], nullable (then the shape is only checked).
+ * AMOE_ERR_INVALID if the decode kernel does not run this shape. */
+#define AMOE_DECODE_SCHED_WORDS 1024
+AMOE_API int amoe_decode_schedule(int32_t hidden, int32_t intermediate, int32_t experts, int32_t top_k,
+                                  int32_t ctas, int32_t *rows);
+
 /* ---- GGUF files ------------------------------------------------------------------
  * GGUF tensor encodings (internal/gguf/reader.go:17-27). */
 enum {
