@@ -933,12 +933,13 @@ int amoe_create(const amoe_config *cfg, amoe_ctx **out) {
                 c->slot_dev.push_back(p);
                 c->slot_layer.push_back(-1);
                 c->slot_used.push_back(0);
-                cudaEvent_t a, b;
-                cudaEventCreateWithFlags(&a, cudaEventDisableTiming);
-                cudaEventCreateWithFlags(&b, cudaEventDisableTiming);
-                c->slot_ready.push_back(a);
-                c->slot_free.push_back(b);
-                cudaEventRecord(b, c->stream);
+                cudaEvent_t a = nullptr, b = nullptr;
+                e = cudaEventCreateWithFlags(&a, cudaEventDisableTiming);
+                if (e == cudaSuccess) e = cudaEventCreateWithFlags(&b, cudaEventDisableTiming);
+                if (a) c->slot_ready.push_back(a);
+                if (b) c->slot_free.push_back(b);
+                if (e == cudaSuccess) e = cudaEventRecord(b, c->stream);
+                if (e != cudaSuccess) { rc = cuda_fail(c, e, "stream slot events"); break; }
             }
             if (rc != AMOE_OK) break;
         }
