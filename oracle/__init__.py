@@ -11,6 +11,11 @@ Reference functions restated (paths relative to the reference project root):
   GPTOSSSwiGLU       internal/backend/cpuref/primitives.go:138-149
   MXFP4 decode       internal/model/gptoss/tensor.go:145-170, gguf/reader.go:442-449
   MoE block          internal/model/gptoss/layer.go:94-188
+  RoPE / YaRNRoPE    internal/backend/cpuref/rope.go:10-86           (attn_oracle.c)
+  KVCache            internal/backend/cpuref/attention.go:8-59       (KVCache below)
+  CausalAttention    internal/backend/cpuref/attention.go:61-171     (attn_oracle.c)
+  attention half     internal/model/gptoss/layer.go:31-92, 189-207   (attn_oracle.c)
+  layer window       internal/model/gptoss/weights.go:118-122
 """
 from __future__ import annotations
 
@@ -48,9 +53,27 @@ class OracleLayer(ctypes.Structure):
     ]
 
 
+class OracleAttnLayer(ctypes.Structure):
+    _fields_ = [
+        ("hidden", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+        ("theta", ctypes.c_double),
+        ("norm1", _f32p),
+        ("qkv_w", _f32p),
+        ("qkv_b", _f32p),
+        ("out_w", _f32p),
+        ("out_b", _f32p),
+        ("sinks", _f32p),
+    ]
+
+
 def build() -> str:
     """Compile liboracle.so with the committed Makefile (gcc, OpenMP)."""
-    src = [os.path.join(_HERE, f) for f in ("moe_oracle.c", "moe_oracle.h", "Makefile")]
+    src = [os.path.join(_HERE, f) for f in ("moe_oracle.c", "moe_oracle.h", "attn_oracle.c", "attn_oracle.h",
+                                            "Makefile")]
     if os.path.exists(_LIB_PATH) and all(
         os.path.getmtime(_LIB_PATH) >= os.path.getmtime(s) for s in src
     ):
@@ -83,6 +106,16 @@ def lib():
                                              _f32p, ctypes.c_int]
             L.oracle_permute.argtypes = [_i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                          _i32p, _i32p, _i32p, _i32p]
+            L.oracle_rope.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_double,
+                                      ctypes.c_int, _f32p]
+            L.oracle_causal_attention.argtypes = [
+                _f32p, ctypes.c_int64, ctypes.c_int, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_double, ctypes.c_double, _f32p,
+            ]
+            L.oracle_attention_half.argtypes = [
+                ctypes.POINTER(OracleAttnLayer), _f32p, ctypes.c_int, _f32p, _f32p, ctypes.POINTER(ctypes.c_int),
+                ctypes.c_int, ctypes.c_int, _f32p,
+            ]
             _lib = L
     return _lib
 
@@ -239,3 +272,109 @@ def permute(topk_idx, experts):
     _check(lib().oracle_permute(_p(idx, _i32p), T, k, experts, _p(perm, _i32p), _p(counts, _i32p),
                                 _p(offsets, _i32p), _p(inv, _i32p)), "permute")
     return perm, counts, offsets, inv
+
+
+# ---- the attention half -------------------------------------------------------------
+
+_ROPE_ERRORS = {-1: "rope head dimension must be positive and even",
+                -2: "rope position offset must be non-negative",
+                -3: "rope theta must be finite and positive",
+                -4: "rope input length is not divisible by the head dimension"}
+
+
+def _rope(x, head_dim, pos_offset, theta, yarn):
+    x = _c(x, np.float32).ravel()
+    out = np.empty_like(x)
+    rc = lib().oracle_rope(_p(x, _f32p), x.size, head_dim, pos_offset, theta, 1 if yarn else 0, _p(out, _f32p))
+    if rc != 0:
+        raise OracleError(_ROPE_ERRORS.get(rc, f"rope rejected its arguments ({rc})"))
+    return out
+
+
+def rope(x, head_dim, pos_offset, theta):
+    """RoPE (rope.go:10-13): rotate-half rotary embedding of [tokens, head_dim]."""
+    return _rope(x, head_dim, pos_offset, theta, False)
+
+
+def yarn_rope(x, head_dim, pos_offset, theta):
+    """YaRNRoPE (rope.go:15-44): the gpt-oss YaRN frequencies and concentration."""
+    return _rope(x, head_dim, pos_offset, theta, True)
+
+
+class KVCache:
+    """KVCache (attention.go:8-59): keys and values [capacity, kv_heads, head_dim];
+    Append is transactional (a rejected append leaves the cache unchanged)."""
+
+    def __init__(self, kv_heads: int, head_dim: int, capacity: int):
+        if kv_heads <= 0 or head_dim <= 0 or capacity <= 0:
+            raise OracleError("kv cache dimensions must be positive")
+        self.kv_heads, self.head_dim, self.capacity, self.length = kv_heads, head_dim, capacity, 0
+        self.keys = np.zeros(capacity * kv_heads * head_dim, np.float32)
+        self.values = np.zeros_like(self.keys)
+
+    def append(self, keys, values, seq: int):
+        if seq <= 0:
+            raise OracleError("kv append sequence length must be positive")
+        if self.length + seq > self.capacity:
+            raise OracleError("kv append exceeds capacity")
+        keys, values = _c(keys, np.float32).ravel(), _c(values, np.float32).ravel()
+        want = seq * self.kv_heads * self.head_dim
+        if keys.size != want or values.size != want:
+            raise OracleError("kv append lengths do not match")
+        start = self.length * self.kv_heads * self.head_dim
+        self.keys[start:start + want] = keys
+        self.values[start:start + want] = values
+        self.length += seq
+
+
+_ATTN_ERRORS = {-1: "attention query heads must be a positive multiple of kv heads",
+                -2: "attention sinks length does not match the query heads",
+                -3: "attention sliding window must be non-negative",
+                -4: "attention query pre-attention scalar must be finite and non-negative",
+                -5: "attention logit softcap must be finite and non-negative",
+                -6: "attention query length is not a non-empty multiple of the query width",
+                -7: "attention query length exceeds cached length",
+                -10: "prefill sequence length must be positive",
+                -11: "kv append exceeds capacity"}
+
+
+def causal_attention(query, q_heads: int, cache: KVCache, sinks=None, window: int = 0,
+                     pre_scalar: float = 0.0, softcap: float = 0.0):
+    """CausalAttentionWithConfig (attention.go:82-171) on the last query tokens."""
+    if cache is None:
+        raise OracleError("attention cache must not be nil")
+    q = _c(query, np.float32).ravel()
+    s = _c(sinks, np.float32).ravel() if sinks is not None else None
+    out = np.empty_like(q)
+    rc = lib().oracle_causal_attention(_p(q, _f32p), q.size, q_heads, _p(cache.keys, _f32p),
+                                       _p(cache.values, _f32p), cache.length, cache.kv_heads, cache.head_dim,
+                                       _p(s, _f32p), 0 if s is None else s.size, window, pre_scalar, softcap,
+                                       _p(out, _f32p))
+    if rc != 0:
+        raise OracleError(_ATTN_ERRORS.get(rc, f"attention rejected its arguments ({rc})"))
+    return out
+
+
+def layer_window(index: int, sliding_window: int) -> int:
+    """loadDecoderLayer's window rule (weights.go:118-122): even layers slide."""
+    return sliding_window if index % 2 == 0 else 0
+
+
+def attention_half(layer: dict, x, cache: KVCache, window: int):
+    """The attention half of DecoderLayer.forward (layer.go:31-92) for the rows x
+    [T, hidden]: returns input + o_proj(attention(YaRN(q), YaRN(k) appended, v))."""
+    x = _c(x, np.float32).reshape(-1, layer["hidden"])
+    keep = {k: _c(layer[k], np.float32) for k in ("norm1", "qkv_w", "qkv_b", "out_w", "out_b", "sinks")}
+    L = OracleAttnLayer(layer["hidden"], layer["heads"], layer["kv_heads"], layer["head_dim"], layer["eps"],
+                        layer["theta"], *[_p(keep[k], _f32p) for k in ("norm1", "qkv_w", "qkv_b", "out_w",
+                                                                        "out_b", "sinks")])
+    out = np.empty_like(x)
+    n = ctypes.c_int(cache.length)
+    rc = lib().oracle_attention_half(ctypes.byref(L), _p(x, _f32p), x.shape[0], _p(cache.keys, _f32p),
+                                     _p(cache.values, _f32p), ctypes.byref(n), cache.capacity, window,
+                                     _p(out, _f32p))
+    if rc != 0:
+        raise OracleError(_ATTN_ERRORS.get(rc, f"attention half rejected its arguments ({rc})"))
+    cache.length = n.value
+    return out
+
