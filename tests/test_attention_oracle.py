@@ -1,7 +1,7 @@
 """The attention-half oracle (oracle/attn_oracle.c) pinned to the reference's own
 golden vectors and validation cases (tests/golden/reference_vectors.json,
-transcribed from internal/backend/cpuref/attention_test.go, rope_test.go and
-gptoss_test.go), cross-checked against an independent numpy restatement, and
+transcribed from internal/backend/cpuref/attention_test.go, rope_test.go,
+gptoss_test.go and gemma_test.go), cross-checked against an independent numpy restatement, and
 checked for the causal-cache property a GPU decode path relies on: decoding
 token by token gives the same rows as one prefill over the whole sequence."""
 import json
@@ -39,11 +39,12 @@ def _cache(g):
     return c
 
 
-@pytest.mark.parametrize("name", ["attention_gqa", "attention_sink", "attention_window"])
+@pytest.mark.parametrize("name", ["attention_gqa", "attention_sink", "attention_window", "attention_scale_softcap"])
 def test_attention_golden(name):
     g = GOLD[name]
     c = _cache(g)
-    got = oracle.causal_attention(g["query"], g["q_heads"], c, sinks=g.get("sinks"), window=g.get("window", 0))
+    got = oracle.causal_attention(g["query"], g["q_heads"], c, sinks=g.get("sinks"), window=g.get("window", 0),
+                                  pre_scalar=g.get("pre_scalar", 0.0), softcap=g.get("softcap", 0.0))
     close(got, g["want"])
 
 
