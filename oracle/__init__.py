@@ -11,6 +11,8 @@ Reference functions restated (paths relative to the reference project root):
   GPTOSSSwiGLU       internal/backend/cpuref/primitives.go:138-149
   MXFP4 decode       internal/model/gptoss/tensor.go:145-170, gguf/reader.go:442-449
   MoE block          internal/model/gptoss/layer.go:94-188
+  FP4 activation terms  no reference counterpart: the bit-exact E2M1-term operand of a
+                     block-scaled FP4 GEMM (oracle_e2m1_terms in moe_oracle.c)
   RoPE / YaRNRoPE    internal/backend/cpuref/rope.go:10-86           (attn_oracle.c)
   KVCache            internal/backend/cpuref/attention.go:8-59       (KVCache below)
   CausalAttention    internal/backend/cpuref/attention.go:61-171     (attn_oracle.c)
@@ -106,6 +108,7 @@ def lib():
                                              _f32p, ctypes.c_int]
             L.oracle_permute.argtypes = [_i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                          _i32p, _i32p, _i32p, _i32p]
+            L.oracle_e2m1_terms.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int, _u8p, _u8p]
             L.oracle_rope.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_double,
                                       ctypes.c_int, _f32p]
             L.oracle_causal_attention.argtypes = [
@@ -272,6 +275,31 @@ def permute(topk_idx, experts):
     _check(lib().oracle_permute(_p(idx, _i32p), T, k, experts, _p(perm, _i32p), _p(counts, _i32p),
                                 _p(offsets, _i32p), _p(inv, _i32p)), "permute")
     return perm, counts, offsets, inv
+
+
+# ---- block-scaled FP4 activation terms ------------------------------------------------
+
+_E2M1 = np.array([0, 0.5, 1, 1.5, 2, 3, 4, 6], np.float64)
+
+
+def e2m1_terms(x, terms: int):
+    """x (length a multiple of 32) as `terms` E2M1 terms with E8M0 scales per 32
+    elements (oracle_e2m1_terms): codes [terms][n/2] (low nibble first) and
+    scales [terms][n/32]."""
+    x = _c(x, np.float32).ravel()
+    codes = np.empty((terms, x.size // 2), np.uint8)
+    scales = np.empty((terms, x.size // 32), np.uint8)
+    _check(lib().oracle_e2m1_terms(_p(x, _f32p), x.size, terms, _p(codes, _u8p), _p(scales, _u8p)), "e2m1_terms")
+    return codes, scales
+
+
+def e2m1_reconstruct(codes, scales):
+    """sum_j q_j 2^(s_j - 127) in float64 from e2m1_terms' output."""
+    codes, scales = np.asarray(codes, np.uint8), np.asarray(scales, np.uint8)
+    nib = np.stack([codes & 15, codes >> 4], -1).reshape(codes.shape[0], -1)
+    val = np.where(nib & 8, -1.0, 1.0) * _E2M1[nib & 7]
+    scale = np.ldexp(1.0, scales.astype(np.int64) - 127).repeat(32, axis=1)
+    return (val * scale).sum(0)
 
 
 # ---- the attention half -------------------------------------------------------------

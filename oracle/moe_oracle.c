@@ -376,3 +376,62 @@ int oracle_permute(const int32_t *topk_idx, int T, int k, int E, int32_t *perm_p
     free(cursor);
     return 0;
 }
+
+/* ---- block-scaled FP4 activation terms (see moe_oracle.h) ---------------------- */
+
+/* E2M1 code of v (|v| <= 6 after saturation), round to nearest, ties to the even
+ * mantissa: the grid is 0, .5, 1, 1.5, 2, 3, 4, 6 (codes 0..7, sign in bit 3). */
+static uint8_t e2m1_rne(float v) {
+    static const float grid[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+    const uint8_t sign = (v < 0.0f) ? 8u : 0u;
+    float a = fabsf(v);
+    if (a >= 6.0f) return (uint8_t)(sign | 7u);
+    int lo = 0;
+    while (lo < 7 && grid[lo + 1] <= a) ++lo;
+    if (lo == 7 || a == grid[lo]) return (uint8_t)(sign | (uint8_t)lo);
+    const float dl = a - grid[lo], dh = grid[lo + 1] - a;
+    int code;
+    if (dl < dh) code = lo;
+    else if (dh < dl) code = lo + 1;
+    else code = (lo & 1) ? lo + 1 : lo; /* tie: the code with an even mantissa bit */
+    if (code == 0) return 0; /* no negative zero code */
+    return (uint8_t)(sign | (uint8_t)code);
+}
+
+static float e2m1_value(uint8_t code) {
+    static const float grid[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+    return (code & 8u) ? -grid[code & 7u] : grid[code & 7u];
+}
+
+int oracle_e2m1_terms(const float *x, int64_t n, int terms, uint8_t *codes, uint8_t *scales) {
+    if (!x || !codes || !scales || n <= 0 || n % 32 != 0 || terms < 1) return -1;
+    for (int64_t i = 0; i < n; ++i)
+        if (!isfinite(x[i])) return -1;
+    const int64_t nb = n / 32;
+    for (int64_t b = 0; b < nb; ++b) {
+        float r[32];
+        memcpy(r, x + b * 32, sizeof(r));
+        for (int j = 0; j < terms; ++j) {
+            float amax = 0.0f;
+            for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(r[i]));
+            int e = 0;
+            if (amax > 0.0f) {
+                int p;
+                const float m = frexpf(amax, &p); /* amax = m 2^p, m in [0.5, 1) */
+                e = (m * 8.0f <= 6.0f) ? p - 3 : p - 2;
+            }
+            if (e < -127) e = -127; /* the smallest E8M0 scale */
+            if (e > 127) return -1;
+            scales[(int64_t)j * nb + b] = (uint8_t)(e + 127);
+            uint8_t *cj = codes + (int64_t)j * (n / 2) + b * 16;
+            for (int i = 0; i < 32; i += 2) {
+                const uint8_t c0 = e2m1_rne(ldexpf(r[i], -e)), c1 = e2m1_rne(ldexpf(r[i + 1], -e));
+                cj[i / 2] = (uint8_t)(c0 | (c1 << 4));
+                r[i] = r[i] - ldexpf(e2m1_value(c0), e);
+                r[i + 1] = r[i + 1] - ldexpf(e2m1_value(c1), e);
+            }
+        }
+    }
+    return 0;
+}
+

@@ -51,6 +51,16 @@ int oracle_swiglu(const float *gate, const float *up, int n, float *out);
 int oracle_mxfp4_decode(const uint8_t *blocks, int64_t nbytes, int64_t elements, float *out);
 /* internal/gguf/reader.go:442-449: bytes for an MXFP4 tensor, -1 on a partial block */
 int64_t oracle_mxfp4_encoded_size(int64_t elements);
+/* Activations as `terms` E2M1 terms with E8M0 scales per 32 elements, the operand
+ * form of a block-scaled FP4 (mxf4) expert GEMM.  No reference counterpart: it
+ * defines, bit for bit, what a GPU quantizer must produce.  Per 32-element block,
+ * term j takes the remainder r_j (r_0 = x, f32), the smallest scale 2^e with
+ * max|r_j| / 2^e <= 6 (E8M0 byte e + 127; 127 for an all-zero remainder), codes
+ * round-to-nearest-even of r_j / 2^e on the E2M1 grid, saturated at +-6, and
+ * r_{j+1} = r_j - q_j 2^e in f32.  codes [terms][n / 2]: two codes per byte, the
+ * lower element in the low nibble; scales [terms][n / 32].  n must be a multiple
+ * of 32 and every value finite.  Returns -1 on bad arguments. */
+int oracle_e2m1_terms(const float *x, int64_t n, int terms, uint8_t *codes, uint8_t *scales);
 
 /* The MoE half of DecoderLayer.forward, internal/model/gptoss/layer.go:94-123,
  * with forwardExpert layer.go:126-188 for each selected expert.
