@@ -246,7 +246,8 @@ struct EpMeta {
 struct EpArgs {
     int N, me, E, El, H, k, r_cap, p_cap, epoch;
     int path;               // 1 GEMV, 2 tcgen05, 0 auto: tcgen05 once the group has >= 32 pairs per expert
-    long long limit_ns;  // bounded waits
+    long long count_limit_ns;  // bound on the count exchange (absorbs the ranks' host-side skew)
+    long long limit_ns;        // bound on the dispatch and return waits (device progress only)
     EpWindow w;
     EpMeta m;
     const int32_t *counts, *offsets, *topk_idx, *perm_pair;  // this rank's routing

@@ -158,7 +158,8 @@ struct amoe_ctx {
     EpMeta ep_m{};
     int ep_epoch = 0;                          // forwards so far (the exchange's flag value)
     bool ep_broken = false;                    // a wait failed: the group is out of step
-    long long ep_wait_ns = 0;                  // bound on each exchange wait
+    long long ep_count_wait_ns = 0;            // bound on the count exchange's wait
+    long long ep_data_wait_ns = 0;             // bound on the dispatch and return waits
     int sms = 0;
 
     // diagnostics
@@ -190,6 +191,37 @@ int cuda_fail(amoe_ctx *c, cudaError_t e, const char *what) {
         cudaError_t e_ = (call);                              \
         if (e_ != cudaSuccess) return cuda_fail(ctx, e_, #call); \
     } while (0)
+
+// Fault injection for the allocation error paths (host side; off unless the
+// environment sets it): AMOE_FAIL_ALLOC_ABOVE=<bytes> makes every device or
+// pinned-host allocation of more than <bytes> fail as out of memory, so that
+// tests can check that amoe_create and amoe_upload_layer report AMOE_ERR_NOMEM
+// and leave the context usable.
+bool injected_alloc_failure(size_t bytes) {
+    const char *v = std::getenv("AMOE_FAIL_ALLOC_ABOVE");
+    if (!v || !*v) return false;
+    char *end = nullptr;
+    const unsigned long long limit = std::strtoull(v, &end, 10);
+    return end != v && bytes > limit;
+}
+
+template <class T>
+cudaError_t dev_alloc(T **p, size_t bytes) {
+    if (injected_alloc_failure(bytes)) {
+        *p = nullptr;
+        return cudaErrorMemoryAllocation;
+    }
+    return cudaMalloc(reinterpret_cast<void **>(p), bytes);
+}
+
+template <class T>
+cudaError_t host_alloc(T **p, size_t bytes, unsigned flags) {
+    if (injected_alloc_failure(bytes)) {
+        *p = nullptr;
+        return cudaErrorMemoryAllocation;
+    }
+    return cudaHostAlloc(reinterpret_cast<void **>(p), bytes, flags);
+}
 
 std::string validate(const amoe_config *c) {
     if (!c) return "config must not be NULL";
@@ -283,7 +315,7 @@ int alloc_scratch(amoe_ctx *c) {
         at[i] = off;
         off = align256(off + parts[i].bytes);
     }
-    AMOE_CUDA(c, cudaMalloc(&c->scratch, off));
+    AMOE_CUDA(c, dev_alloc(&c->scratch, off));
     uint8_t *base = static_cast<uint8_t *>(c->scratch);
     for (size_t i = 0; i < parts.size(); ++i) *parts[i].dst = parts[i].bytes ? base + at[i] : nullptr;
     AMOE_CUDA(c, cudaMemset(c->arrivals, 0, (size_t)c->nchunk_max * 4));
@@ -466,16 +498,19 @@ int use_tensor_path(const amoe_ctx *c, int T) {
     return tc_supported() && pairs_per_expert >= 32;
 }
 
-// Bound on every wait of the exchange (AMOE_EP_WAIT_MS overrides it).  The count
-// exchange at the start of a forward also absorbs the ranks' host-side skew,
-// hence seconds, not microseconds.
-constexpr long long kEpWaitNs = 20000000000LL;
+// Bounds on the exchange's waits (AMOE_EP_WAIT_MS overrides both).  The count
+// exchange at the start of a forward also absorbs the ranks' host-side skew (a
+// rank reaching the forward later than its peers), hence seconds; the dispatch
+// and return waits only wait for the peers' kernels that are already running
+// (the longest is a peer's expert GEMMs, milliseconds), hence one second.
+constexpr long long kEpCountWaitNs = 5000000000LL;
+constexpr long long kEpDataWaitNs = 1000000000LL;
 
-long long ep_wait_ns() {
+long long ep_wait_override_ns() {
     const char *v = std::getenv("AMOE_EP_WAIT_MS");
-    if (!v || !*v) return kEpWaitNs;
+    if (!v || !*v) return 0;
     const long long ms = std::atoll(v);
-    return ms > 0 ? ms * 1000000LL : kEpWaitNs;
+    return ms > 0 ? ms * 1000000LL : 0;
 }
 
 // Maps every rank's window into this process: the windows' IPC handles and the
@@ -484,7 +519,7 @@ int ep_setup(amoe_ctx *c) {
     const Dims &d = c->d;
     const int N = c->ep_n, me = c->ep_rank;
     c->ep_w = ep_window(N, d.E, d.H, c->max_tokens * d.k, (int)c->r_max);
-    AMOE_CUDA(c, cudaMalloc(&c->ep_win, c->ep_w.bytes));
+    AMOE_CUDA(c, dev_alloc(&c->ep_win, c->ep_w.bytes));
     AMOE_CUDA(c, cudaMemset(c->ep_win, 0, c->ep_w.table));  // the flags
     AMOE_CUDA(c, cudaDeviceSynchronize());
     struct Hello {
@@ -497,7 +532,7 @@ int ep_setup(amoe_ctx *c) {
     std::memcpy(mine.shape, shape, sizeof(shape));
     std::vector<Hello> all(N);
     uint8_t *buf = nullptr;
-    AMOE_CUDA(c, cudaMalloc(&buf, sizeof(Hello) * (N + 1)));
+    AMOE_CUDA(c, dev_alloc(&buf, sizeof(Hello) * (N + 1)));
     cudaError_t e = cudaMemcpy(buf, &mine, sizeof(Hello), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) {
         const ncclResult_t r = g_nccl.ncclAllGather(buf, buf + sizeof(Hello), sizeof(Hello), ncclUint8, c->comm,
@@ -564,7 +599,8 @@ int ep_experts(amoe_ctx *c, const LayerDev &L, const RouteOut &r, int T, int nch
     a.r_cap = (int)c->r_max;
     a.p_cap = c->max_tokens * d.k;
     a.epoch = ++c->ep_epoch;
-    a.limit_ns = c->ep_wait_ns;
+    a.count_limit_ns = c->ep_count_wait_ns;
+    a.limit_ns = c->ep_data_wait_ns;
     a.w = c->ep_w;
     a.m = c->ep_m;
     a.counts = r.counts;
@@ -898,7 +934,7 @@ int amoe_create(const amoe_config *cfg, amoe_ctx **out) {
             e = cudaEventCreateWithFlags(&c->io_in_ready[i], cudaEventDisableTiming);
             if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->io_out_ready[i], cudaEventDisableTiming);
         }
-        if (e == cudaSuccess) e = cudaHostAlloc(&c->h_flag, sizeof(int32_t), cudaHostAllocDefault);
+        if (e == cudaSuccess) e = host_alloc(&c->h_flag, sizeof(int32_t), cudaHostAllocDefault);
         if (e != cudaSuccess) { rc = cuda_fail(c, e, "cudaStreamCreate/cudaEventCreate/cudaHostAlloc"); break; }
         if (c->ep_n > 1) {
             std::string why;
@@ -920,15 +956,15 @@ int amoe_create(const amoe_config *cfg, amoe_ctx **out) {
             c->xs = std::min(d.E, cfg->max_tokens * d.k);
             c->xblk = layer_block(Dims{d.H, d.I, c->xs, d.k, d.eps}, c->xs, false);
             const size_t per_layer = ((size_t)d.H + (size_t)d.E * d.H + d.E) * 4;
-            e = cudaMalloc(&c->router_res, per_layer * cfg->layers);
-            if (e == cudaSuccess) e = cudaMalloc(&c->xslot, c->xblk.total);
-            if (e == cudaSuccess) e = cudaMalloc(&c->sel_dev, (size_t)2 * (c->xs + 1) * 4);
-            if (e == cudaSuccess) e = cudaHostAlloc(&c->h_sel, ((size_t)d.E + 1 + 2 * (c->xs + 1)) * 4, 0);
+            e = dev_alloc(&c->router_res, per_layer * cfg->layers);
+            if (e == cudaSuccess) e = dev_alloc(&c->xslot, c->xblk.total);
+            if (e == cudaSuccess) e = dev_alloc(&c->sel_dev, (size_t)2 * (c->xs + 1) * 4);
+            if (e == cudaSuccess) e = host_alloc(&c->h_sel, ((size_t)d.E + 1 + 2 * (c->xs + 1)) * 4, 0);
             if (e != cudaSuccess) { rc = cuda_fail(c, e, "expert-streaming buffers"); break; }
         } else if (cfg->stream_slots >= 2) {
             for (int i = 0; i < cfg->stream_slots && rc == AMOE_OK; ++i) {
                 uint8_t *p = nullptr;
-                e = cudaMalloc(&p, c->blk.total);
+                e = dev_alloc(&p, c->blk.total);
                 if (e != cudaSuccess) { rc = cuda_fail(c, e, "cudaMalloc(stream slot)"); break; }
                 c->slot_dev.push_back(p);
                 c->slot_layer.push_back(-1);
@@ -949,7 +985,9 @@ int amoe_create(const amoe_config *cfg, amoe_ctx **out) {
             cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cfg->device);
             c->sms = sms > 0 ? sms : 148;
         }
-        c->ep_wait_ns = ep_wait_ns();
+        const long long ov = ep_wait_override_ns();
+        c->ep_count_wait_ns = ov ? ov : kEpCountWaitNs;
+        c->ep_data_wait_ns = ov ? ov : kEpDataWaitNs;
         if (rc == AMOE_OK && c->ep_n > 1) rc = ep_setup(c);
     } while (0);
     if (rc != AMOE_OK) {
@@ -1003,18 +1041,18 @@ int amoe_upload_layer(amoe_ctx *c, int32_t layer, const float *norm_gain, const 
     } while (0)
     if (!streaming(c)) {
         if (!c->layer_dev[layer]) {
-            e = cudaMalloc(&c->layer_dev[layer], c->blk.total);
+            e = dev_alloc(&c->layer_dev[layer], c->blk.total);
             if (e != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(layer)");
         }
         blockp = c->layer_dev[layer];
     } else {
         if (!c->layer_host[layer]) {
-            e = cudaHostAlloc(&c->layer_host[layer], c->blk.total, cudaHostAllocDefault);
+            e = host_alloc(&c->layer_host[layer], c->blk.total, cudaHostAllocDefault);
             if (e != cudaSuccess) return cuda_fail(c, e, "cudaHostAlloc(layer)");
         }
-        UP_CUDA(cudaMalloc(&blockp, c->blk.total));
+        UP_CUDA(dev_alloc(&blockp, c->blk.total));
     }
-    UP_CUDA(cudaMalloc(&staging, stage_bytes));
+    UP_CUDA(dev_alloc(&staging, stage_bytes));
     const LayerDev L = layer_view(blockp, c->blk);
     cudaStream_t st = c->stream;
     UP_CUDA(cudaMemcpyAsync(L.norm_gain, norm_gain, H * 4, cudaMemcpyHostToDevice, st));
@@ -1098,56 +1136,71 @@ int amoe_forward(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, f
     const std::vector<int> passes = plan_passes(c, T);
     cudaStream_t st = c->stream;
     if (passes.size() == 1) {
-        AMOE_CUDA(c, cudaMemcpyAsync(c->io_in, residual, (size_t)T * H * 4, cudaMemcpyHostToDevice, st));
-        rc = forward_impl(c, layer, c->io_in, T, c->io_out, nullptr, nullptr, st, route_view(c, 0, 0));
-        if (rc) return rc;
-        AMOE_CUDA(c, cudaMemcpyAsync(out, c->io_out, (size_t)T * H * 4, cudaMemcpyDeviceToHost, st));
-        if (topk_idx)
-            AMOE_CUDA(c, cudaMemcpyAsync(topk_idx, c->r.topk_idx, (size_t)T * k * 4, cudaMemcpyDeviceToHost, st));
-        if (topk_w)
-            AMOE_CUDA(c, cudaMemcpyAsync(topk_w, c->r.topk_w, (size_t)T * k * 4, cudaMemcpyDeviceToHost, st));
-        AMOE_CUDA(c, cudaMemcpyAsync(c->h_flag, c->err_flag, 4,
-                                     cudaMemcpyDeviceToHost, st));
+        auto one_pass = [&]() -> int {
+            AMOE_CUDA(c, cudaMemcpyAsync(c->io_in, residual, (size_t)T * H * 4, cudaMemcpyHostToDevice, st));
+            const int prc = forward_impl(c, layer, c->io_in, T, c->io_out, nullptr, nullptr, st, route_view(c, 0, 0));
+            if (prc) return prc;
+            AMOE_CUDA(c, cudaMemcpyAsync(out, c->io_out, (size_t)T * H * 4, cudaMemcpyDeviceToHost, st));
+            if (topk_idx)
+                AMOE_CUDA(c, cudaMemcpyAsync(topk_idx, c->r.topk_idx, (size_t)T * k * 4, cudaMemcpyDeviceToHost, st));
+            if (topk_w)
+                AMOE_CUDA(c, cudaMemcpyAsync(topk_w, c->r.topk_w, (size_t)T * k * 4, cudaMemcpyDeviceToHost, st));
+            AMOE_CUDA(c, cudaMemcpyAsync(c->h_flag, c->err_flag, 4, cudaMemcpyDeviceToHost, st));
+            return AMOE_OK;
+        };
+        rc = one_pass();
+        if (rc) {
+            cudaStreamSynchronize(st);  // nothing still reads or writes the caller's buffers
+            return rc;
+        }
     } else {
         // Pipeline: every slice's rows go up on the H2D stream at once; slice i
         // computes once its rows are in, and its outputs come down on the D2H
         // stream while slice i+1 computes (two copy engines, both directions).
-        AMOE_CUDA(c, cudaEventRecord(c->io_out_ready[0], st));  // earlier work on the compute stream
-        AMOE_CUDA(c, cudaStreamWaitEvent(c->h2d_stream, c->io_out_ready[0], 0));
-        int t0 = 0;
-        for (size_t i = 0; i < passes.size(); ++i) {
-            AMOE_CUDA(c, cudaMemcpyAsync(c->io_in + (size_t)t0 * H, residual + (size_t)t0 * H,
-                                         (size_t)passes[i] * H * 4, cudaMemcpyHostToDevice, c->h2d_stream));
-            AMOE_CUDA(c, cudaEventRecord(c->io_in_ready[i], c->h2d_stream));
-            t0 += passes[i];
-        }
-        t0 = 0;
-        for (size_t i = 0; i < passes.size(); ++i) {
-            const int Tp = passes[i];
-            AMOE_CUDA(c, cudaStreamWaitEvent(st, c->io_in_ready[i], 0));
-            const RouteOut r = route_view(c, t0, (int)i);
-            rc = forward_impl(c, layer, c->io_in + (size_t)t0 * H, Tp, c->io_out + (size_t)t0 * H, nullptr, nullptr,
-                              st, r);
-            if (rc) {
-                cudaStreamSynchronize(c->h2d_stream);
-                cudaStreamSynchronize(st);
-                return rc;
+        // On any failure all three streams are drained before returning, so no
+        // copy into the caller's buffers is still in flight after the call.
+        auto passes_run = [&]() -> int {
+            AMOE_CUDA(c, cudaEventRecord(c->io_out_ready[0], st));  // earlier work on the compute stream
+            AMOE_CUDA(c, cudaStreamWaitEvent(c->h2d_stream, c->io_out_ready[0], 0));
+            int t0 = 0;
+            for (size_t i = 0; i < passes.size(); ++i) {
+                AMOE_CUDA(c, cudaMemcpyAsync(c->io_in + (size_t)t0 * H, residual + (size_t)t0 * H,
+                                             (size_t)passes[i] * H * 4, cudaMemcpyHostToDevice, c->h2d_stream));
+                AMOE_CUDA(c, cudaEventRecord(c->io_in_ready[i], c->h2d_stream));
+                t0 += passes[i];
             }
-            AMOE_CUDA(c, cudaEventRecord(c->io_out_ready[i], st));
-            AMOE_CUDA(c, cudaStreamWaitEvent(c->d2h_stream, c->io_out_ready[i], 0));
-            AMOE_CUDA(c, cudaMemcpyAsync(out + (size_t)t0 * H, c->io_out + (size_t)t0 * H, (size_t)Tp * H * 4,
-                                         cudaMemcpyDeviceToHost, c->d2h_stream));
-            if (topk_idx)
-                AMOE_CUDA(c, cudaMemcpyAsync(topk_idx + (size_t)t0 * k, r.topk_idx, (size_t)Tp * k * 4,
+            t0 = 0;
+            for (size_t i = 0; i < passes.size(); ++i) {
+                const int Tp = passes[i];
+                AMOE_CUDA(c, cudaStreamWaitEvent(st, c->io_in_ready[i], 0));
+                const RouteOut r = route_view(c, t0, (int)i);
+                const int prc = forward_impl(c, layer, c->io_in + (size_t)t0 * H, Tp, c->io_out + (size_t)t0 * H,
+                                             nullptr, nullptr, st, r);
+                if (prc) return prc;
+                AMOE_CUDA(c, cudaEventRecord(c->io_out_ready[i], st));
+                AMOE_CUDA(c, cudaStreamWaitEvent(c->d2h_stream, c->io_out_ready[i], 0));
+                AMOE_CUDA(c, cudaMemcpyAsync(out + (size_t)t0 * H, c->io_out + (size_t)t0 * H, (size_t)Tp * H * 4,
                                              cudaMemcpyDeviceToHost, c->d2h_stream));
-            if (topk_w)
-                AMOE_CUDA(c, cudaMemcpyAsync(topk_w + (size_t)t0 * k, r.topk_w, (size_t)Tp * k * 4,
-                                             cudaMemcpyDeviceToHost, c->d2h_stream));
-            t0 += Tp;
+                if (topk_idx)
+                    AMOE_CUDA(c, cudaMemcpyAsync(topk_idx + (size_t)t0 * k, r.topk_idx, (size_t)Tp * k * 4,
+                                                 cudaMemcpyDeviceToHost, c->d2h_stream));
+                if (topk_w)
+                    AMOE_CUDA(c, cudaMemcpyAsync(topk_w + (size_t)t0 * k, r.topk_w, (size_t)Tp * k * 4,
+                                                 cudaMemcpyDeviceToHost, c->d2h_stream));
+                t0 += Tp;
+            }
+            AMOE_CUDA(c, cudaMemcpyAsync(c->h_flag, c->err_flag, 4,
+                                         cudaMemcpyDeviceToHost, c->d2h_stream));  // after the last pass
+            AMOE_CUDA(c, cudaStreamSynchronize(c->d2h_stream));
+            return AMOE_OK;
+        };
+        rc = passes_run();
+        if (rc) {
+            cudaStreamSynchronize(c->h2d_stream);
+            cudaStreamSynchronize(st);
+            cudaStreamSynchronize(c->d2h_stream);
+            return rc;
         }
-        AMOE_CUDA(c, cudaMemcpyAsync(c->h_flag, c->err_flag, 4,
-                                     cudaMemcpyDeviceToHost, c->d2h_stream));  // after the last pass
-        AMOE_CUDA(c, cudaStreamSynchronize(c->d2h_stream));
     }
     AMOE_CUDA(c, cudaStreamSynchronize(st));
     c->last_T = T;

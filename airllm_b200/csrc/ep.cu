@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(kCountThreads) ep_counts_kernel(EpArgs a) {
     __syncthreads();
     if (tid < N) st_release_sys(win_flag(win[tid], a.w, kEpFlagCount, me), a.epoch);
     // 2. every rank's row of this epoch
-    if (tid < N && !wait_epoch(win_flag(win[me], a.w, kEpFlagCount, tid), a.epoch, a.limit_ns)) {
+    if (tid < N && !wait_epoch(win_flag(win[me], a.w, kEpFlagCount, tid), a.epoch, a.count_limit_ns)) {
         ok = 0;
         atomicCAS(a.err, 0, 30);
     }

@@ -180,17 +180,31 @@ bool encoded_size(uint32_t type, const std::vector<uint64_t> &shape, int64_t *by
         }
     }
     const uint64_t e = (uint64_t)n;
+    const uint64_t kMax = (uint64_t)std::numeric_limits<int64_t>::max();
+    // every size must fit int64 (reader.go:429-466): "encoded tensor size overflows int64"
+    auto scalar = [&](uint64_t width) {
+        if (e > kMax / width) {
+            *err = "encoded tensor size overflows int64";
+            return false;
+        }
+        *bytes = (int64_t)(e * width);
+        return true;
+    };
     auto blocks = [&](uint64_t per, uint64_t bytes_per, const char *what) {
         if (e % per) {
             *err = std::string(what) + " element count must be divisible by " + std::to_string(per);
+            return false;
+        }
+        if (e / per > kMax / bytes_per) {
+            *err = "encoded tensor size overflows int64";
             return false;
         }
         *bytes = (int64_t)(e / per * bytes_per);
         return true;
     };
     switch (type) {
-        case AMOE_GGUF_F32: *bytes = (int64_t)(e * 4); return true;
-        case AMOE_GGUF_F16: case AMOE_GGUF_BF16: *bytes = (int64_t)(e * 2); return true;
+        case AMOE_GGUF_F32: return scalar(4);
+        case AMOE_GGUF_F16: case AMOE_GGUF_BF16: return scalar(2);
         case AMOE_GGUF_MXFP4: return blocks(32, 17, "MXFP4");
         case AMOE_GGUF_Q8_0: return blocks(32, 34, "Q8_0");
         case AMOE_GGUF_Q4_0: return blocks(32, 18, "Q4_0");

@@ -71,6 +71,20 @@ int scratch_address(int device, unsigned char **out) {
     return AMOE_OK;
 }
 
+// Makes `device` current for the call and gives the calling thread back the
+// device it had: a host whose GPU work another runtime manages keeps its
+// current device across this call.
+struct DeviceScope {
+    int prev = -1;
+    cudaError_t enter(int device) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        return cudaSetDevice(device);
+    }
+    ~DeviceScope() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
 int reject(const std::string &msg) {
     set_thread_error(msg);
     return AMOE_ERR_INVALID;
@@ -103,7 +117,8 @@ extern "C" AMOE_API int amoe_route_noalloc(int32_t device, int32_t hidden, int32
     if (!residual || !norm_gain || !router_w || !router_b || !logits || !topk_idx || !topk_w)
         return reject("inputs and outputs must not be NULL");
 
-    cudaError_t e = cudaSetDevice(device);
+    DeviceScope scope;
+    cudaError_t e = scope.enter(device);
     if (e != cudaSuccess) {
         set_thread_error(std::string("cudaSetDevice: ") + cudaGetErrorString(e));
         return AMOE_ERR_CUDA;

@@ -1,33 +1,44 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 GPT-OSS MoE block (one JSON line on rank 0).
 
-Workload (default): the 20B-shaped block at prefill -- 4096 tokens, hidden
-2880, 32 experts, top-4, intermediate 2880, MXFP4 experts, Zipf(1.1)-skewed
-router bias (busiest expert ~3x mean load), seed 1; synthetic seeded data.
-A "step" is one forward of the block over those 4096 tokens.
+Default line, at every --gpus N (1, 2, 4, 8): the GPT-OSS-120B-shaped block at
+prefill -- 8192 tokens, hidden 2880, 128 experts, top-4, intermediate 2880, MXFP4
+experts, router drawn N(0, 0.02) (logits ~N(0,1) scale), seed 3 -- with its
+experts sharded 128/N over the N GPUs (expert parallelism: each rank routes
+8192/N tokens; rows go to the owning rank and outputs come back by stores into
+the peers' memory over NVLink).  Total work is fixed (strong scaling); at N = 1
+it is the plain single-GPU block.  A "step" is one forward over the 8192 tokens.
 
-  value     tokens/s over all ranks, inputs resident in HBM, device-timed
-            (CUDA events around each step; L2 flushed between steps)
-  e2e       the same through the C ABI's host-buffer call (amoe_forward) with
-            pinned host input/output: H2D + block + D2H per step
-  roofline  dominant kernel, from the library's per-stage CUDA events taken
-            inside the timed region
-  N > 1     independent replicas, one per GPU (tokens are independent: weak
-            scaling, no collective on the data path)
+  value     tokens/s of the whole job, inputs resident in HBM, CUDA events
+            around every step on every rank (L2 flushed between steps), max
+            over ranks
+  e2e       the same through the C ABI's host-buffer call (amoe_forward) on
+            every rank with pinned host input/output: H2D + block + D2H per step
+  roofline  the dominant kernel (gate_up), from the library's per-stage CUDA
+            events in a second pass of the same steps; the rank whose gate_up
+            takes longest
+  sub       N = 1: the 20B-shaped prefill (4096 tokens, Zipf-skewed routing),
+            the 20B decode token and the 24-layer streamed decode stack, each
+            with its own value / e2e / roofline; N = 8: the adversarial
+            16384-token configuration (8 hot experts on rank 0), per-rank times
 
---impl reference times the reference's CPU path (the C restatement in
-oracle/, faithful mode: every (token, expert) re-decodes the MXFP4 expert as
-readExpert does) on a bounded token sample with all host threads.
+--impl reference times the reference's CPU path (the C restatement in oracle/,
+faithful mode: every (token, expert) re-decodes the MXFP4 expert as readExpert
+does) on a bounded sample of the same workload with all host threads, and
+prints the same metric and config.  --config picks a single configuration
+(0-4) instead of the default line.
 """
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
 import subprocess
 import sys
 import tempfile
+import threading
 import time
 
 import numpy as np
@@ -37,12 +48,19 @@ sys.path.insert(0, ROOT)
 
 from airllm_b200 import workloads as W  # noqa: E402
 
-METRIC = "MoE-block tokens/s per B200 (prefill T=4096, GPT-OSS-20B shape)"
-METRIC_BY_CONFIG = {0: "MoE-block tokens/s per B200 (decode T=1, GPT-OSS-20B shape)", 1: METRIC}
+METRIC = "MoE-block prefill tokens/s, GPT-OSS-120B shape (T=8192, E=128), experts sharded over the GPUs"
+METRIC_BY_CONFIG = {
+    0: "MoE-block tokens/s per B200 (decode T=1, GPT-OSS-20B shape)",
+    1: "MoE-block tokens/s per B200 (prefill T=4096, GPT-OSS-20B shape)",
+    2: "decode tokens/s, 24-layer GPT-OSS-20B-shaped MoE stack streamed from pinned host memory",
+    3: METRIC,
+    4: "MoE-block prefill tokens/s, GPT-OSS-120B shape (T=16384, E=128), 8 hot experts on rank 0",
+}
 UNIT = "tokens/s"
-# Timed steps when --steps is not given: each config's timed region then lasts
-# about half a second, several periods of the clock sampler.
-DEFAULT_STEPS = {0: 2000, 1: 300, 2: 16, 3: 100, 4: 100}
+# Timed steps when --steps is not given: each config's timed region lasts about
+# half a second, many periods of the clock sampler.
+DEFAULT_STEPS = {0: 2000, 1: 300, 2: 16, 3: 100, 4: 60}
+MIN_STEPS = {0: 200, 2: 8}  # sub-records: enough steps for a timed region of several ms
 FLOP_PER_PAIR = 2 * 2880 * (2 * 2880 + 2880)  # 49,766,400
 MEASURED_PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_FILE = os.path.join(ROOT, "profiles", "ncu_traffic.json")
@@ -51,6 +69,8 @@ DTYPE_TENSOR = "mxfp4 x e4m3 (4 terms per value) -> f32"
 DTYPE_DECODE = "mxfp4 x fp16 (hi + lo) -> f32"
 DTYPE_GEMV = "mxfp4 x fp16 (hi + lo) -> f32"
 FLUSH_BYTES = 256 << 20  # > 126 MB L2
+L2_NOTE = ("flushed before every timed step: 256 MiB write, then a 256 MiB read of a second buffer "
+           "(the written lines are written back outside the timed region)")
 
 
 def peaks():
@@ -62,6 +82,14 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
+def default_config(world: int) -> dict:
+    """The workload of the default line (identical in both arms at a given N)."""
+    return {"workload": f"gptoss120b-moe-prefill T=8192 H=2880 I=2880 E=128 k=4 mxfp4, experts sharded 128/{world}",
+            "config_index": 3, "tokens": 8192, "tokens_per_rank": 8192 // world, "hidden": 2880,
+            "intermediate": 2880, "experts": 128, "experts_per_rank": 128 // world, "top_k": 4,
+            "weights": "MXFP4 (E2M1 + E8M0 per 32)", "parallelism": f"ep{world}", "l2": L2_NOTE}
+
+
 def workload_desc(config: int, T: int) -> dict:
     shape = W.CONFIG_SHAPE[config]
     names = {0: "gptoss20b-moe-decode", 1: "gptoss20b-moe-prefill-zipf", 3: "gptoss120b-moe"}
@@ -69,11 +97,7 @@ def workload_desc(config: int, T: int) -> dict:
                         f"E={shape.experts} k={shape.top_k} mxfp4",
             "config_index": config, "tokens": T, "hidden": shape.hidden, "intermediate": shape.intermediate,
             "experts": shape.experts, "top_k": shape.top_k, "weights": "MXFP4 (E2M1 + E8M0 per 32)",
-            "l2": L2_NOTE}
-
-
-L2_NOTE = ("flushed before every timed step: 256 MiB write, then a 256 MiB read of a second buffer "
-           "(the written lines are written back outside the timed region)")
+            "parallelism": "ep1", "l2": L2_NOTE}
 
 
 class L2Flush:
@@ -91,8 +115,90 @@ class L2Flush:
         self.sink.copy_(self.r.sum())
 
 
+REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
+
+
+def _clock_record(samples, n_inside, period_ms, source):
+    """samples: [(sm_mhz, max_mhz, power_w, set of reason names)]."""
+    sm = [s[0] for s in samples if s[0] is not None]
+    mx = [s[1] for s in samples if s[1] is not None]
+    pw = [s[2] for s in samples if s[2] is not None]
+    reasons = sorted({r for s in samples for r in s[3]})
+    return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+            "reasons": reasons, "power_w_max": max(pw) if pw else None, "samples_in_region": n_inside,
+            "period_ms": period_ms, "source": source}
+
+
+class NvmlClockSampler:
+    """SM clock, power and clock-event reasons polled through NVML every 10 ms
+    on a background thread; only samples taken between begin() and stop() count."""
+
+    PERIOD_MS = 10
+
+    def __init__(self, device: int, nvml=None):
+        if nvml is None:
+            import pynvml as nvml
+        self.nvml = nvml
+        nvml.nvmlInit()
+        self.h = None
+        try:
+            import torch
+
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.h = nvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid if not uuid.startswith("GPU-") else uuid).encode())
+        except Exception:
+            self.h = None
+        if self.h is None:
+            self.h = nvml.nvmlDeviceGetHandleByIndex(device)
+        self.max_mhz = float(nvml.nvmlDeviceGetMaxClockInfo(self.h, nvml.NVML_CLOCK_SM))
+        self.rows = []
+        self.t0 = self.t1 = None
+        self.stop_ev = threading.Event()
+        self.th = threading.Thread(target=self._loop, daemon=True)
+        self.th.start()
+
+    def _sample(self):
+        n = self.nvml
+        sm = float(n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM))
+        try:
+            pw = n.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+        except Exception:
+            pw = None
+        try:
+            bits = n.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:
+            bits = n.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+        return (sm, self.max_mhz, pw, {k for k, b in REASON_BITS.items() if bits & b})
+
+    def _loop(self):
+        while not self.stop_ev.is_set():
+            try:
+                self.rows.append((time.time(), self._sample()))
+            except Exception:
+                pass
+            time.sleep(self.PERIOD_MS / 1000.0)
+
+    def begin(self):
+        self.t0 = time.time()
+
+    def stop(self):
+        t1 = time.time()
+        self.stop_ev.set()
+        self.th.join(timeout=2)
+        t0 = self.t0 if self.t0 is not None else t1
+        inside = [s for w, s in self.rows if t0 <= w <= t1]
+        n_inside = len(inside)
+        if not inside and self.rows:
+            mid = 0.5 * (t0 + t1)
+            inside = [min(self.rows, key=lambda r: abs(r[0] - mid))[1]]
+        if not inside:
+            return None
+        return _clock_record(inside, n_inside, self.PERIOD_MS, "nvml")
+
+
 class ClockSampler:
-    """nvidia-smi clocks during the timed region.
+    """nvidia-smi clocks during the timed region (the fallback when NVML is not
+    usable).
 
     Create it before the timed region (it waits for the first sample, so the
     sampler is running when timing starts), call begin() right before the first
@@ -101,7 +207,7 @@ class ClockSampler:
     shorter than the sampling interval the nearest sample stands in and
     `samples_in_region` says 0."""
 
-    PERIOD_MS = 100
+    PERIOD_MS = 20
 
     def __init__(self, device: int):
         self.path = tempfile.mktemp(suffix=".csv")
@@ -128,7 +234,6 @@ class ClockSampler:
 
     @staticmethod
     def _when(stamp: str):
-        import datetime
         try:
             return datetime.datetime.strptime(stamp, "%Y/%m/%d %H:%M:%S.%f").timestamp()
         except ValueError:
@@ -160,49 +265,76 @@ class ClockSampler:
             near = min((abs(w - mid), i) for i, (w, _) in enumerate(stamped) if w is not None) \
                 if any(w is not None for w, _ in stamped) else (0, 0)
             inside = [stamped[near[1]][1]]
-        rows = inside
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "power_w_max": max(pw) if pw else None, "samples_in_region": n_inside,
-                "period_ms": ClockSampler.PERIOD_MS}
 
+        def num(v):
+            return float(v) if v.replace(".", "").isdigit() else None
+
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        samples = [(num(r[1]), num(r[2]), num(r[3]), {names[i] for i in range(4) if r[5 + i].lower() == "active"})
+                   for r in inside]
+        return _clock_record(samples, n_inside, self.PERIOD_MS, "nvidia-smi")
+
+
+def clock_sampler(device: int):
+    """NVML at 10 ms when it answers, else nvidia-smi."""
+    try:
+        return NvmlClockSampler(device)
+    except Exception:
+        return ClockSampler(device)
+
+
+# ---- the reference's CPU path ----------------------------------------------------------
 
 def cpu_reference_run(layer, x, sample: int, threads: int):
     """One bounded sample of the reference CPU path; returns (seconds, tokens)."""
-    import oracle  # the CPU restatement of the reference (baseline leg only)
+    import oracle  # the CPU restatement of the reference (baseline legs only)
 
     t0 = time.perf_counter()
     oracle.moe_block(layer, x[:sample], faithful=True, threads=threads)
     return time.perf_counter() - t0, sample
 
 
+def cpu_baseline(layer, x, T: int) -> dict:
+    """The reference's CPU path (oracle, faithful mode) on the host cores: all
+    threads over 2 tokens per thread, and one thread over 2 tokens."""
+    threads = os.cpu_count() or 1
+    sample = min(T, 2 * threads)
+    sec, ntok = cpu_reference_run(layer, x, sample, threads)
+    sec1, ntok1 = cpu_reference_run(layer, x, min(T, 2), 1)
+    return {"value": ntok / sec, "unit": UNIT, "cores": threads, "kind": "port", "nproc": threads,
+            "sample": f"{ntok} of {T} tokens, oracle faithful mode (MXFP4 re-decode per (token, expert)), "
+                      f"{threads} threads",
+            "one_core": {"value": ntok1 / sec1, "unit": UNIT, "cores": 1,
+                         "sample": f"{ntok1} of {T} tokens, 1 thread (the reference is single-threaded)"}}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return 0
+    cfg = 3 if args.config is None else args.config
     threads = os.cpu_count() or 1
-    layer = W.config_layer(args.config)
-    T = W.CONFIG_TOKENS[args.config]
-    x = W.config_tokens(args.config)
-    sample = min(T, max(8, 2 * threads))
+    layer = W.config_layer(cfg)
+    T = 8192 if args.config is None else (args.tokens or W.CONFIG_TOKENS[cfg])
+    x = W.config_tokens(cfg, T) if cfg != 2 else W.make_tokens(W.GPTOSS_20B, 1, 2)
+    sample = min(T, 2 * threads)
     for _ in range(args.warmup):
         cpu_reference_run(layer, x, min(sample, threads), threads)
     times = []
     for _ in range(args.steps):
-        s, n = cpu_reference_run(layer, x, sample, threads)
+        s, _ = cpu_reference_run(layer, x, sample, threads)
         times.append(s)
     sec = statistics.mean(times)
     value = sample / sec
-    desc = f"{sample} of {T} tokens per step (oracle restatement, faithful MXFP4 re-decode per (token, expert))"
+    desc = (f"{sample} of {T} tokens per step (oracle restatement, faithful MXFP4 re-decode per (token, expert)), "
+            f"{threads} threads")
+    config = default_config(world) if args.config is None else workload_desc(cfg, T)
     line = {
-        "impl": "reference", "metric": METRIC_BY_CONFIG.get(args.config, METRIC), "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f64-accumulate (reference CPU path)",
-        "data": "synthetic (seeded)", "config": workload_desc(args.config, T),
+        "impl": "reference", "metric": METRIC if args.config is None else METRIC_BY_CONFIG[cfg], "value": value,
+        "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+        "higher_is_better": True, "scaling": "strong" if cfg in (3, 4) else "weak", "vs_baseline": None,
+        "dtype": "f64-accumulate (reference CPU path)", "data": "synthetic (seeded)", "config": config,
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -210,19 +342,60 @@ def run_reference(args):
     return 0
 
 
-def algorithmic(config: int, T: int, layer, idx, stage: str):
+# ---- shared measurement pieces ----------------------------------------------------------
+
+class Group:
+    """This process's place in the job: rank, world, device, and the helpers that
+    keep every rank in the same collective sequence."""
+
+    def __init__(self):
+        import torch
+        import torch.distributed as dist
+
+        self.torch, self.dist = torch, dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def gather(self, obj):
+        if self.world == 1:
+            return [obj]
+        out = [None] * self.world
+        self.dist.all_gather_object(out, obj)
+        return out
+
+    def close(self):
+        if self.world > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def algorithmic(T: int, layer, idx, stage: str, pairs=None, active=None):
     """Algorithmic FLOPs and bytes of one launch of `stage` for this routing."""
-    H, I, E, k = layer["hidden"], layer["intermediate"], layer["experts"], layer["top_k"]
-    pairs = T * k
-    active = len(np.unique(idx))
+    H, I, E = layer["hidden"], layer["intermediate"], layer["experts"]
+    pairs = T * layer["top_k"] if pairs is None else pairs
+    active = len(np.unique(idx)) if active is None else active
     if stage == "gate_up":
         flops = 2.0 * pairs * 2 * I * H
         bytes_ = active * (2 * I * H // 2 + 2 * I * H // 32 + 2 * I * 4) + T * H * 4 + pairs * I * 4
     elif stage == "decode_experts":
         # fused routing + gate_up + down + combine: both weight sets of the selected
-        # experts and their biases, the residual in and the output out (act and y stay
-        # in L2 between the phases)
-        # (the fused kernel also routes: router weights, bias and the RMSNorm gain)
+        # experts and their biases, the router, the residual in and the output out
         flops = 2.0 * pairs * 3 * I * H
         bytes_ = (active * (3 * I * H // 2 + 3 * I * H // 32 + 2 * I * 4 + H * 4) + 2 * T * H * 4
                   + E * H * 4 + E * 4 + H * 4)
@@ -232,29 +405,242 @@ def algorithmic(config: int, T: int, layer, idx, stage: str):
     return flops, bytes_
 
 
-def run_streaming(args):
+def kernel_name(stage: str, path: int) -> str:
+    if stage == "decode_experts":
+        return ("decode_kernel (one cooperative launch: routing + gate_up + down + combine; packed MXFP4 boxes "
+                "expanded in registers, mma.sync with fp16 hi/lo activation columns)")
+    return {1: "gemv_kernel (mma.sync MXFP4)",
+            2: "bs_gemm_kernel (tcgen05 kind::mxf8f6f4 block-scaled: E2M1 weights x 4-term E4M3 activations)"}[path or 1]
+
+
+def roofline(stage: str, flops: float, bytes_: float, launch_ms: float, tensor: bool, clk, timed_ms: float,
+             traffic_key: str, path: int) -> dict:
+    pk = peaks()
+    traffic = None
+    try:
+        traffic = json.load(open(TRAFFIC_FILE)).get(traffic_key)
+    except Exception:
+        pass
+    if tensor:
+        achieved = flops / (launch_ms / 1e3) / 1e12
+        # a kernel timed inside a long pass runs at the power-capped clock: the sustained
+        # GEMM figure is its peak; a short burst is compared with the burst figure
+        sustained = (clk is not None and "sw_power_cap" in (clk.get("reasons") or [])) or timed_ms >= 250.0
+        peak = pk["bf16_tflops_sustained"] if sustained and pk.get("bf16_tflops_sustained") else pk["bf16_tflops"]
+        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "traffic": traffic, "kernel": f"{stage} {kernel_name(stage, path)}",
+                "algorithmic_flop_per_launch": flops, "launch_ms": launch_ms,
+                "peak_source": f"{pk['source']} bf16 dense ({'sustained' if peak != pk['bf16_tflops'] else 'burst'})",
+                "frac_of_fp4_dense_nominal_9pflops": achieved / 9000.0}
+    achieved = bytes_ / (launch_ms / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / pk["hbm_gbs"], "traffic": traffic, "kernel": f"{stage} {kernel_name(stage, path)}",
+            "algorithmic_bytes_per_launch": bytes_, "launch_ms": launch_ms, "peak_source": f"{pk['source']} HBM copy",
+            "frac_of_nominal_8tbs": achieved / 8000.0}
+
+
+def timed_steps(g: Group, blk, xd, od, steps: int, warmup: int, flush, stream, idd=None, wd=None):
+    """Device-timed steps: per-step CUDA events on the launching stream after an
+    L2 flush; returns (mean ms of this rank, clocks, launches in the region)."""
+    torch = g.torch
+    for i in range(warmup):
+        flush(i)  # the first call allocates (a host stall the other ranks would wait out)
+        blk.forward_device(xd, od, topk_idx=idd, topk_w=wd, stream=stream)
+    torch.cuda.synchronize()
+    blk.stats(reset=True)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    clocks = clock_sampler(g.local)
+    torch.cuda.synchronize()
+    g.barrier()
+    clocks.begin()
+    for i in range(steps):
+        flush(i)
+        starts[i].record(stream)
+        blk.forward_device(xd, od, topk_idx=idd, topk_w=wd, stream=stream)
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    g.barrier()
+    clk = clocks.stop()
+    launches = int(blk.stats(reset=True)["launches"])
+    return statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends)), clk, launches
+
+
+def profiled_steps(g: Group, blk, xd, od, steps: int, flush, stream, idd=None, wd=None) -> dict:
+    """The same steps with the library's per-stage events (kept out of the timed
+    region: the events sit between its launches)."""
+    blk.set_profiling(True)
+    g.barrier()
+    for i in range(steps):
+        flush(i)
+        blk.forward_device(xd, od, topk_idx=idd, topk_w=wd, stream=stream)
+    g.torch.cuda.synchronize()
+    blk.set_profiling(False)
+    st = blk.stats(reset=True)
+    n = max(st["timed_forwards"], 1)
+    return {"stage_ms": {k: v / n for k, v in st["stage_ms"].items() if v > 0}, "path": st["last_path"]}
+
+
+def e2e_steps(g: Group, blk, x: np.ndarray, steps: int, flush) -> float:
+    """Host-buffer call (amoe_forward) with pinned input/output: H2D, the block and
+    D2H in every step; mean ms of this rank."""
+    torch = g.torch
+    xh = torch.from_numpy(x).pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    for _ in range(2):
+        blk.forward_into(xh.numpy(), oh.numpy())
+    times = []
+    g.barrier()
+    for i in range(steps):
+        flush(i)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        blk.forward_into(xh.numpy(), oh.numpy())
+        times.append(time.perf_counter() - t0)
+    g.barrier()
+    return statistics.mean(times) * 1e3
+
+
+# ---- expert-parallel block (configs 3 and 4; the default line) ------------------------
+
+def ep_record(g: Group, cfg: int, T: int, steps: int, warmup: int, path: int, with_e2e: bool = True) -> dict:
+    """Configs 3/4: the 120B-shaped block with its 128 experts sharded 128/N; each
+    rank routes T/N tokens.  Per-step CUDA events, max over ranks."""
+    torch = g.torch
+    from airllm_b200 import moe
+
+    if T % g.world:
+        raise SystemExit("tokens must divide by the GPU count")
+    Tr = T // g.world
+    layer = W.config_layer(cfg)
+    x = W.make_tokens(W.CONFIG_SHAPE[cfg], T, cfg)[g.rank * Tr:(g.rank + 1) * Tr]
+    uid = None
+    if g.world > 1:
+        obj = [moe.ep_unique_id() if g.rank == 0 else None]
+        g.dist.broadcast_object_list(obj, src=0)
+        uid = obj[0]
+    blk = moe.MoEBlock.for_layer(layer, max_tokens=Tr, device=g.local, path=path,
+                                 ep_size=g.world, ep_rank=g.rank, nccl_id=uid)
+    blk.upload_layer(0, layer)
+    shape = {k: layer[k] for k in ("hidden", "intermediate", "experts", "top_k")}
+    del layer
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    xd = torch.from_numpy(x).cuda()
+    od = torch.empty_like(xd)
+    idd = torch.empty((Tr, 4), dtype=torch.int32, device="cuda")
+    flush = L2Flush(torch)
+    ms_local, clk, launches = timed_steps(g, blk, xd, od, steps, warmup, flush, stream, idd=idd)
+    ms = g.max(ms_local)
+    prof = profiled_steps(g, blk, xd, od, steps, flush, stream, idd=idd)
+    e2e_local = e2e_steps(g, blk, x, steps, flush) if with_e2e else None
+    e2e_ms = g.max(e2e_local) if with_e2e else None
+    # the pairs each rank's experts received (for its gate_up's algorithmic work)
+    counts = np.bincount(idd.cpu().numpy().ravel(), minlength=shape["experts"])
+    all_counts = np.sum(g.gather(counts.tolist()), axis=0)
+    El = shape["experts"] // g.world
+    own = all_counts[g.rank * El:(g.rank + 1) * El]
+    rank_info = {"ms": ms_local, "stage_ms": prof["stage_ms"], "pairs": int(own.sum()),
+                 "active": int((own > 0).sum()), "launches": launches, "path": prof["path"], "clocks": clk,
+                 "e2e_ms": e2e_local}
+    infos = g.gather(rank_info)
+    torch.cuda.synchronize()
+    g.barrier()  # no rank frees its window while a peer may still store into it
+    blk.close()
+    if g.rank != 0:
+        return {}
+    # roofline: the gate_up of the rank that takes longest
+    dom = "gate_up"
+    worst = max(range(g.world), key=lambda r: infos[r]["stage_ms"].get(dom, 0.0))
+    wi = infos[worst]
+    flops, bytes_ = algorithmic(Tr, shape, None, dom, pairs=wi["pairs"], active=wi["active"])
+    roof = roofline(dom, flops, bytes_, wi["stage_ms"].get(dom, float("nan")), True, infos[0]["clocks"],
+                    ms * steps, f"{dom}:{cfg}", wi["path"])
+    roof["rank"] = worst
+    rec = {
+        "value": T / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "steps": steps, "warmup": warmup,
+        "scaling": "strong", "dtype": DTYPE_TENSOR if wi["path"] == 2 else DTYPE_GEMV,
+        "roofline": roof, "gpu_launches": int(sum(i["launches"] for i in infos)),
+        "gpu_launches_rank0": infos[0]["launches"],
+        "per_rank_ms": [i["ms"] for i in infos], "pairs_by_rank": [i["pairs"] for i in infos],
+        "stage_ms_per_step_by_rank": [{k: round(v, 4) for k, v in i["stage_ms"].items()} for i in infos],
+        "clocks": infos[0]["clocks"], "clocks_by_rank": [i["clocks"] for i in infos],
+        "tensor_tflops_algorithmic": T * shape["top_k"] * FLOP_PER_PAIR / (ms / 1e3) / 1e12,
+    }
+    if with_e2e:
+        rec["e2e"] = {"value": T / (e2e_ms / 1e3), "unit": UNIT, "ms_per_step": e2e_ms,
+                      "h2d_bytes_per_step": T * shape["hidden"] * 4, "d2h_bytes_per_step": T * shape["hidden"] * 4,
+                      "per_rank_ms": [i["e2e_ms"] for i in infos],
+                      "call": "amoe_forward on every rank (pinned host in/out; each rank copies its T/N rows)"}
+    return rec
+
+
+# ---- one GPU, configs 0 and 1 --------------------------------------------------------
+
+def single_record(g: Group, cfg: int, steps: int, warmup: int, path: int) -> dict:
+    torch = g.torch
+    from airllm_b200 import moe
+
+    layer = W.config_layer(cfg)
+    T = W.CONFIG_TOKENS[cfg]
+    x = W.config_tokens(cfg)
+    blk = moe.MoEBlock.for_layer(layer, max_tokens=T, device=g.local, path=path)
+    blk.upload_layer(0, layer)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    xd = torch.from_numpy(x).cuda()
+    od = torch.empty_like(xd)
+    idd = torch.empty((T, layer["top_k"]), dtype=torch.int32, device="cuda")
+    wd = torch.empty((T, layer["top_k"]), dtype=torch.float32, device="cuda")
+    flush = L2Flush(torch)
+    ms, clk, launches = timed_steps(g, blk, xd, od, steps, warmup, flush, stream, idd=idd, wd=wd)
+    prof = profiled_steps(g, blk, xd, od, steps, flush, stream, idd=idd, wd=wd)
+    e2e_ms = e2e_steps(g, blk, x, steps, flush)
+    blk.close()
+    stage = prof["stage_ms"]
+    dom = max(("gate_up", "down", "decode_experts"), key=lambda s: stage.get(s, 0.0))
+    idx_host = idd.cpu().numpy()
+    flops, bytes_ = algorithmic(T, layer, idx_host, dom)
+    tensor = T * layer["top_k"] / layer["experts"] >= 32
+    roof = roofline(dom, flops, bytes_, stage.get(dom, float("nan")), tensor, clk, ms * steps, f"{dom}:{cfg}",
+                    prof["path"])
+    return {
+        "metric": METRIC_BY_CONFIG[cfg], "value": T / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "steps": steps,
+        "warmup": warmup, "dtype": DTYPE_DECODE if dom == "decode_experts" else
+        {1: DTYPE_GEMV, 2: DTYPE_TENSOR}[prof["path"] or 1],
+        "config": workload_desc(cfg, T), "roofline": roof,
+        "e2e": {"value": T / (e2e_ms / 1e3), "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": T * layer["hidden"] * 4, "d2h_bytes_per_step": T * layer["hidden"] * 4,
+                "call": "amoe_forward (pinned host in/out)"},
+        "gpu_launches": launches, "stage_ms_per_step": {k: round(v, 4) for k, v in stage.items()}, "clocks": clk,
+    }
+
+
+# ---- config 2: the streamed 24-layer stack ----------------------------------------------
+
+def stream_record(g: Group, steps: int, warmup: int, stream_experts: int = 1) -> dict:
     """Config 2: the 24-layer stack of config-0 blocks streamed AirLLM-style.
 
-    All MXFP4 weights (24 x 423 MB) live in pinned host memory; two device slots
-    are refilled on a copy stream (layer L+1 is copied while layer L computes).
-    A step is one decode token through all 24 layers (the output of layer L is
-    the input of layer L+1).  Metric: decode tokens/s; the H2D traffic is the
-    full layer per layer visit."""
-    import torch
-
+    All MXFP4 weights (24 x 423 MB) live in pinned host memory.  With
+    stream_experts (default) every layer keeps its norm and router resident, each
+    call routes on the device and copies only the routed experts; otherwise two
+    whole-layer slots are refilled on a copy stream.  A step is one decode token
+    through all 24 layers (the output of layer L is the input of layer L+1)."""
+    torch = g.torch
     from airllm_b200 import moe
 
     L = W.STREAM_LAYERS
     t0 = time.perf_counter()
-    layers = [W.stream_layer(i) for i in range(L)]
-    blk = moe.MoEBlock.for_layer(layers[0], layers=L, max_tokens=1, stream_slots=2, path=moe.PATH_AUTO,
-                                 stream_experts=args.stream_experts)
-    for i, layer in enumerate(layers):
-        blk.upload_layer(i, layer)
+    first = W.stream_layer(0)
+    blk = moe.MoEBlock.for_layer(first, layers=L, max_tokens=1, stream_slots=2, path=moe.PATH_AUTO,
+                                 stream_experts=stream_experts, device=g.local)
+    dims = (first["hidden"], first["intermediate"], first["top_k"])
+    gguf_bytes = sum(int(np.asarray(v).nbytes) for v in first.values() if isinstance(v, np.ndarray))
+    blk.upload_layer(0, first)
+    del first
+    for i in range(1, L):
+        blk.upload_layer(i, W.stream_layer(i))
     setup_s = time.perf_counter() - t0
-    gguf_bytes = sum(int(np.asarray(v).nbytes) for k, v in layers[0].items() if isinstance(v, np.ndarray))
-    dims = (layers[0]["hidden"], layers[0]["intermediate"], layers[0]["top_k"])
-    del layers
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     x = torch.from_numpy(W.make_tokens(W.GPTOSS_20B, 1, 2)).cuda()
@@ -267,13 +653,13 @@ def run_streaming(args):
             h = out
         return h
 
-    for _ in range(max(1, args.warmup // 3)):
+    for _ in range(max(1, warmup // 3)):
         token(x)
     torch.cuda.synchronize()
     blk.stats(reset=True)
-    n = min(args.steps, W.STREAM_DECODE_TOKENS)
+    n = min(steps, W.STREAM_DECODE_TOKENS)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = ClockSampler(0)
+    clocks = clock_sampler(g.local)
     clocks.begin()
     ev0.record(stream)
     h = x
@@ -284,7 +670,7 @@ def run_streaming(args):
     clk = clocks.stop()
     st = blk.stats(reset=True)
     ms = ev0.elapsed_time(ev1) / n
-    if args.stream_experts:
+    if stream_experts:
         # each layer visit copies the routed experts' box planes, scale chunks and biases (k experts at T = 1)
         def planes(R, K):
             kp = (K + 127) // 128 * 128
@@ -293,142 +679,95 @@ def run_streaming(args):
         layer_bytes = dims[2] * per_expert
     else:
         layer_bytes = int(st["layer_bytes"])  # what each layer visit copies (device format)
+    blk.close()
     h2d = L * layer_bytes / (ms / 1e3) / 1e9
-    line = {
-        "metric": "decode tokens/s, 24-layer GPT-OSS-20B-shaped MoE stack streamed from pinned host memory",
-        "value": 1e3 / ms, "unit": "tokens/s", "n_gpus": 1, "steps": n, "warmup": args.warmup,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": DTYPE_TENSOR if args.stream_experts else DTYPE_DECODE, "data": "synthetic (seeded, seed (2, layer))",
+    return {
+        "metric": METRIC_BY_CONFIG[2], "value": 1e3 / ms, "unit": "tokens/s", "ms_per_step": ms, "steps": n,
+        "warmup": warmup, "dtype": DTYPE_TENSOR if stream_experts else DTYPE_DECODE,
         "config": {"workload": f"gptoss20b-moe-stream layers={L} T=1 "
-                               + ("routed experts per layer" if args.stream_experts else "whole layers, 2 slots"),
-                   "config_index": 2, "stream_experts": args.stream_experts,
-                   "layer_bytes": layer_bytes, "setup_s": setup_s},
-        "h2d_gbs": h2d, "h2d_bytes_per_step": L * layer_bytes,
-        "gpu_launches": int(st["launches"]), "clocks": clk,
+                               + ("routed experts per layer" if stream_experts else "whole layers, 2 slots"),
+                   "config_index": 2, "stream_experts": stream_experts, "layer_bytes": layer_bytes,
+                   "setup_s": setup_s},
+        "h2d_gbs": h2d, "h2d_bytes_per_step": L * layer_bytes, "gpu_launches": int(st["launches"]), "clocks": clk,
         "gguf_layer_bytes": gguf_bytes,
+        "roofline": {"bound": "host link", "achieved": h2d, "unit": "GB/s",
+                     "note": "pinned host -> HBM bytes of the routed experts per token / token time"},
         "note": ("each layer visit routes on the device, then copies only the 4 routed experts' MXFP4 box planes, "
                  "scale chunks and biases (the reference reads only the selected experts too); bound by the host "
-                 "link and the per-layer routing round trip") if args.stream_experts else
+                 "link and the per-layer routing round trip") if stream_experts else
                 ("every layer visit copies the whole layer (AirLLM streaming): the MXFP4 box planes and scale "
                  "chunks, biases, router; bound by the host link"),
     }
-    print(json.dumps(line), flush=True)
-    blk.close()
+
+
+# ---- entry points ----------------------------------------------------------------------
+
+def base_line(rec: dict, g: Group, metric: str, config: dict) -> dict:
+    line = {"metric": metric, "value": rec["value"], "unit": rec["unit"], "n_gpus": g.world, "steps": rec["steps"],
+            "warmup": rec["warmup"], "ms_per_step": rec["ms_per_step"], "higher_is_better": True,
+            "scaling": rec.get("scaling", "weak"), "vs_baseline": None, "dtype": rec["dtype"],
+            "data": "synthetic (seeded MXFP4 weights, N(0,1) tokens)", "config": config}
+    for k, v in rec.items():
+        line.setdefault(k, v)
+    return line
+
+
+def run_default(args) -> int:
+    g = Group()
+    steps = args.steps or DEFAULT_STEPS[3]
+    rec = ep_record(g, 3, 8192, steps, args.warmup, args.path)
+    line = base_line(rec, g, METRIC, default_config(g.world)) if g.rank == 0 else None
+    sub = {}
+    if g.world == 1:
+        sub["config1_prefill_20b_T4096"] = single_record(g, 1, args.steps or DEFAULT_STEPS[1], args.warmup, args.path)
+        sub["config0_decode_20b_T1"] = single_record(g, 0, max(args.steps or DEFAULT_STEPS[0], MIN_STEPS[0]),
+                                                     args.warmup, args.path)
+        if not args.no_stream:
+            sub["config2_stream_24_layers"] = stream_record(g, max(args.steps or DEFAULT_STEPS[2], MIN_STEPS[2]),
+                                                            args.warmup)
+        if not args.no_cpu_baseline:
+            layer = W.config_layer(3)
+            line["cpu_baseline"] = cpu_baseline(layer, W.config_tokens(3, 8192), 8192)
+    if g.world == 8 and not args.no_adversarial:
+        r4 = ep_record(g, 4, 16384, args.steps or DEFAULT_STEPS[4], args.warmup, args.path, with_e2e=False)
+        if g.rank == 0:
+            r4["metric"] = METRIC_BY_CONFIG[4]
+            r4["note"] = ("router bias +4 on experts 0-7 (all on rank 0): with N(0,1)-scale logits about 99.5 % of "
+                          "the pairs go to the hot experts, so rank 0 runs nearly all expert work; per-rank times "
+                          "in per_rank_ms")
+            sub["config4_adversarial_T16384"] = r4
+    if g.rank == 0:
+        if "cpu_baseline" not in line:
+            line["cpu_baseline"] = None
+        line["sub"] = sub
+        print(json.dumps(line), flush=True)
+    g.close()
     return 0
 
 
-def run_ep(args):
-    """Configs 3 and 4: the GPT-OSS-120B-shaped block (128 experts) with its
-    experts sharded 128/N over the N GPUs (expert parallelism: rows dispatched
-    and outputs returned by stores into the peers' memory over NVLink).  Total
-    tokens are fixed (strong scaling); each rank routes T/N of them.  Timed per
-    step with CUDA events, max over ranks."""
-    import datetime
-
-    import torch
-    import torch.distributed as dist
-
-    from airllm_b200 import moe
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device("cuda", local))
+def run_config(args) -> int:
+    g = Group()
     cfg = args.config
-    T = args.tokens or (8192 if cfg == 3 else W.CONFIG_TOKENS[cfg])
-    if T % world:
-        raise SystemExit("tokens must divide by the GPU count")
-    Tr = T // world
-    layer = W.config_layer(cfg)
-    x = W.make_tokens(W.CONFIG_SHAPE[cfg], T, cfg)[rank * Tr:(rank + 1) * Tr]
-    uid = None
-    if world > 1:
-        obj = [moe.ep_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        uid = obj[0]
-    blk = moe.MoEBlock.for_layer(layer, max_tokens=Tr, device=local, path=args.path,
-                                 ep_size=world, ep_rank=rank, nccl_id=uid)
-    blk.upload_layer(0, layer)
-    del layer
-    stream = torch.cuda.Stream()
-    torch.cuda.set_stream(stream)
-    xd = torch.from_numpy(x).cuda()
-    od = torch.empty_like(xd)
-    flush = L2Flush(torch)
-    for i in range(args.warmup):
-        flush(i)  # its first call allocates (a host stall the other ranks would wait out)
-        blk.forward_device(xd, od, stream=stream)
-    torch.cuda.synchronize()
-    blk.stats(reset=True)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    clocks = ClockSampler(local)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    clocks.begin()
-    h0 = time.perf_counter()
-    for i in range(args.steps):
-        flush(i)
-        starts[i].record(stream)
-        blk.forward_device(xd, od, stream=stream)
-        ends[i].record(stream)
-    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps  # enqueue cost per step
-    torch.cuda.synchronize()
-    clk = clocks.stop()
-    launches = int(blk.stats(reset=True)["launches"])
-    ms_local = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
-    # per-stage breakdown: a second, profiled pass (stage events add gaps)
-    blk.set_profiling(True)
-    if world > 1:
-        dist.barrier()
-    for i in range(args.steps):
-        flush(i)
-        blk.forward_device(xd, od, stream=stream)
-    torch.cuda.synchronize()
-    blk.set_profiling(False)
-    st = blk.stats(reset=True)
-    ms = ms_local
-    per_rank = [ms_local]
-    if world > 1:
-        t = torch.tensor([ms_local], dtype=torch.float64, device="cuda")
-        allt = [torch.zeros_like(t) for _ in range(world)]
-        dist.all_gather(allt, t)
-        per_rank = [float(v.item()) for v in allt]
-        ms = max(per_rank)
-    n = max(st["timed_forwards"], 1)
-    stage = {k: round(v / n, 4) for k, v in st["stage_ms"].items() if v > 0}
-    stages_by_rank, host_by_rank = [stage], [host_ms]
-    if world > 1:
-        stages_by_rank, host_by_rank = [None] * world, [None] * world
-        dist.all_gather_object(stages_by_rank, stage)
-        dist.all_gather_object(host_by_rank, host_ms)
-    flops = T * 4 * FLOP_PER_PAIR
-    pk = peaks()
-    line = {
-        "metric": f"MoE-block tokens/s, GPT-OSS-120B shape (E=128), expert parallel over {world} GPU(s)",
-        "value": T / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": DTYPE_TENSOR, "data": "synthetic (seeded)",
-        "config": {"workload": f"gptoss120b-moe-ep T={T} E=128 k=4 H=I=2880 mxfp4"
-                               + (" adversarial(8 hot experts on rank 0)" if cfg == 4 else ""),
-                   "config_index": cfg, "tokens": T, "tokens_per_rank": Tr, "experts_per_rank": 128 // world,
-                   "parallelism": f"ep{world}", "l2": L2_NOTE},
-        "per_rank_ms": per_rank, "stage_ms_per_step_by_rank": stages_by_rank,
-        "host_enqueue_ms_per_step_by_rank": host_by_rank,
-        "tensor_tflops_algorithmic": flops / (ms / 1e3) / 1e12, "peak_bf16_tflops": pk["bf16_tflops"] * world,
-        "gpu_launches": launches, "clocks": clk,
-    }
-    if rank == 0:
+    if cfg in (3, 4):
+        T = args.tokens or (8192 if cfg == 3 else W.CONFIG_TOKENS[cfg])
+        rec = ep_record(g, cfg, T, args.steps or DEFAULT_STEPS[cfg], args.warmup, args.path)
+        config = default_config(g.world) if (cfg == 3 and T == 8192) else dict(workload_desc(cfg, T),
+                                                                              parallelism=f"ep{g.world}")
+        line = base_line(rec, g, METRIC_BY_CONFIG[cfg] if T == 8192 or cfg == 4 else METRIC_BY_CONFIG[cfg],
+                         config) if g.rank == 0 else None
+    elif g.world > 1:
+        raise SystemExit("configs 0-2 run on one GPU (--config 3/4 or the default line shard over GPUs)")
+    elif cfg == 2:
+        rec = stream_record(g, args.steps or DEFAULT_STEPS[2], args.warmup, args.stream_experts)
+        line = base_line(rec, g, rec["metric"], rec["config"])
+    else:
+        rec = single_record(g, cfg, args.steps or DEFAULT_STEPS[cfg], args.warmup, args.path)
+        line = base_line(rec, g, rec["metric"], rec["config"])
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(W.config_layer(cfg), W.config_tokens(cfg), W.CONFIG_TOKENS[cfg])
+    if g.rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()  # no rank frees its window while a peer may still store into it
-    blk.close()
-    if world > 1:
-        dist.destroy_process_group()
+    g.close()
     return 0
 
 
@@ -436,190 +775,27 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=0,
-                    help="timed steps (default per config, so the timed region spans several clock samples)")
+                    help="timed steps (default per config, so the timed region spans many clock samples)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--config", type=int, default=None, help="one configuration (0-4) instead of the default line")
     ap.add_argument("--path", type=int, default=0, help="0 auto, 1 GEMV, 2 tcgen05")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-stream", action="store_true", help="default line: leave out the config-2 sub-record")
+    ap.add_argument("--no-adversarial", action="store_true", help="default line: leave out config 4 at 8 GPUs")
     ap.add_argument("--tokens", type=int, default=0, help="configs 3/4: total tokens (default 8192 / 16384)")
     ap.add_argument("--stream-experts", type=int, default=1, choices=[0, 1],
                     help="config 2: 1 copies only each layer's routed experts, 0 whole layers")
     args = ap.parse_args()
-    if args.steps <= 0:  # the reference arm's steps are CPU samples of about a second each
-        args.steps = 5 if args.impl == "reference" else DEFAULT_STEPS.get(args.config, 20)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
+        if args.steps <= 0:  # the reference arm's steps are CPU samples of about a second each
+            args.steps = 5
         return run_reference(args)
-    if args.config == 2:
-        return run_streaming(args)
-    if args.config in (3, 4):
-        return run_ep(args)
-
-    import torch
-    import torch.distributed as dist
-
-    from airllm_b200 import moe
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    cfg = args.config
-    layer = W.config_layer(cfg)
-    T = W.CONFIG_TOKENS[cfg]
-    x = W.config_tokens(cfg)
-    blk = moe.MoEBlock.for_layer(layer, max_tokens=T, device=local, path=args.path)
-    blk.upload_layer(0, layer)
-
-    stream = torch.cuda.Stream()
-    torch.cuda.set_stream(stream)
-    xd = torch.from_numpy(x).cuda()
-    od = torch.empty_like(xd)
-    idd = torch.empty((T, layer["top_k"]), dtype=torch.int32, device="cuda")
-    wd = torch.empty((T, layer["top_k"]), dtype=torch.float32, device="cuda")
-    flush = L2Flush(torch)
-
-    for i in range(args.warmup):
-        flush(i)
-        blk.forward_device(xd, od, topk_idx=idd, topk_w=wd, stream=stream)
-    torch.cuda.synchronize()
-    blk.stats(reset=True)
-
-    # ---- device-timed region ------------------------------------------------
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    clocks = ClockSampler(local)
-    torch.cuda.synchronize()
-    barrier()
-    clocks.begin()
-    for i in range(args.steps):
-        flush(i)
-        starts[i].record(stream)
-        blk.forward_device(xd, od, topk_idx=idd, topk_w=wd, stream=stream)
-        ends[i].record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    clk = clocks.stop()
-    timed = blk.stats(reset=True)
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    ms = max_over_ranks(statistics.mean(step_ms))
-    value = world * T / (ms / 1e3)
-
-    # ---- per-stage CUDA events: a second pass of the same steps -----------------
-    # (the library's stage events sit between its launches, so they are kept out
-    # of the timed region above)
-    blk.set_profiling(True)
-    for i in range(args.steps):
-        flush(i)
-        blk.forward_device(xd, od, topk_idx=idd, topk_w=wd, stream=stream)
-    torch.cuda.synchronize()
-    blk.set_profiling(False)
-    st = blk.stats(reset=True)
-
-    # ---- end-to-end through the host-buffer C-ABI call ----------------------
-    xh = torch.from_numpy(x).pin_memory()
-    oh = torch.empty_like(xh).pin_memory()
-    for _ in range(2):
-        blk.forward_into(xh.numpy(), oh.numpy())
-    e2e_s = []
-    barrier()
-    for i in range(args.steps):
-        flush(i)
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        blk.forward_into(xh.numpy(), oh.numpy())
-        e2e_s.append(time.perf_counter() - t0)
-    barrier()
-    e2e_ms = max_over_ranks(statistics.mean(e2e_s) * 1e3)
-    e2e = {"value": world * T / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": T * layer["hidden"] * 4,
-           "d2h_bytes_per_step": T * layer["hidden"] * 4, "ms_per_step": e2e_ms,
-           "call": "amoe_forward (pinned host in/out)"}
-
-    # ---- roofline of the dominant kernel --------------------------------------
-    pk = peaks()
-    idx_host = idd.cpu().numpy()
-    n = max(st["timed_forwards"], 1)
-    stage_avg = {k: v / n for k, v in st["stage_ms"].items() if v > 0}
-    dom = max(("gate_up", "down", "decode_experts"), key=lambda s: stage_avg.get(s, 0.0))
-    flops, bytes_ = algorithmic(cfg, T, layer, idx_host, dom)
-    dom_ms = stage_avg.get(dom, float("nan"))
-    pairs_per_expert = T * layer["top_k"] / layer["experts"]
-    kernel_name = {1: "gemv_kernel (mma.sync MXFP4)",
-                   2: "bs_gemm_kernel (tcgen05 kind::mxf8f6f4 block-scaled: E2M1 weights x 4-term E4M3 "
-                      "activations)"}[st["last_path"] or 1]
-    if dom == "decode_experts":
-        kernel_name = ("decode_kernel (one cooperative launch: routing + gate_up + down + combine; packed MXFP4 "
-                       "boxes expanded in registers, mma.sync with fp16 hi/lo activation columns)")
-    traffic = None
-    try:
-        traffic = json.load(open(TRAFFIC_FILE)).get(f"{dom}:{cfg}")
-    except Exception:
-        pass
-    if pairs_per_expert >= 32:
-        achieved = flops / (dom_ms / 1e3) / 1e12
-        # a kernel timed inside a long pass runs at the power-capped clock: the sustained
-        # GEMM figure is its peak; a short burst is compared with the burst figure
-        sustained = (clk is not None and "sw_power_cap" in (clk.get("reasons") or [])) or ms * args.steps >= 250.0
-        peak = pk["bf16_tflops_sustained"] if sustained and pk.get("bf16_tflops_sustained") else pk["bf16_tflops"]
-        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": traffic,
-                "kernel": f"{dom} {kernel_name}", "algorithmic_flop_per_launch": flops,
-                "launch_ms": dom_ms,
-                "peak_source": f"{pk['source']} bf16 dense ({'sustained' if peak != pk['bf16_tflops'] else 'burst'})",
-                "frac_of_fp4_dense_nominal_9pflops": achieved / 9000.0}
-    else:
-        achieved = bytes_ / (dom_ms / 1e3) / 1e9
-        roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / pk["hbm_gbs"], "traffic": traffic, "kernel": f"{dom} {kernel_name}",
-                "algorithmic_bytes_per_launch": bytes_, "launch_ms": dom_ms,
-                "peak_source": f"{pk['source']} HBM copy"}
-
-    # ---- CPU baseline (rank 0, N=1 only) --------------------------------------
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        sample = min(T, max(8, 2 * threads))
-        sec, ntok = cpu_reference_run(layer, x, sample, threads)
-        cpu = {"value": ntok / sec, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{ntok} of {T} tokens, oracle faithful mode (MXFP4 re-decode per (token, expert))"}
-
-    launches_per_step = timed["launches"] / max(timed["forwards"], 1)
-    line = {
-        "metric": METRIC_BY_CONFIG.get(cfg, METRIC), "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": {1: DTYPE_GEMV, 2: DTYPE_TENSOR}[st["last_path"] or 1]
-        if dom != "decode_experts" else DTYPE_DECODE,
-        "data": "synthetic (seeded MXFP4 weights, N(0,1) tokens)",
-        "config": dict(workload_desc(cfg, T), parallelism=f"replicas x{world}"),
-        "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
-        "gpu_launches": int(timed["launches"]), "gpu_launches_per_step": launches_per_step,
-        "stage_ms_per_step": stage_avg, "clocks": clk,
-    }
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()  # ranks leave together
-    blk.close()
-    if world > 1:
-        dist.destroy_process_group()
-    return 0
+    if args.config is None:
+        return run_default(args)
+    return run_config(args)
 
 
 if __name__ == "__main__":

@@ -3,8 +3,8 @@
  *
  * This is the drop-in boundary for the MoE half of the reference's
  * DecoderLayer.forward (internal/model/gptoss/layer.go:94-123 plus
- * forwardExpert, layer.go:126-188).  A Go cgo shim binds these entry points
- * (see INTEGRATION.md); plain pointers and sizes only, no C++ or torch types.
+ * forwardExpert, layer.go:126-188).  A Go cgo shim binds these entry points;
+ * plain pointers and sizes only, no C++ or torch types.
  *
  * Conventions
  *  - Every entry point returns AMOE_OK (0) or a negative AMOE_ERR_* code and
@@ -172,7 +172,8 @@ AMOE_API int amoe_get_stats(amoe_ctx *ctx, amoe_stats *out, int32_t reset);
  *     device inputs;  logits [T x E], topk_idx [T x k], topk_w [T x k]: device outputs.
  * Enqueued on `stream` (a cudaStream_t; NULL = the legacy default stream).
  * The first call on a device resolves the array's device address; make that
- * first call before any stream capture.  All calls share the array and it
+ * first call before any stream capture.  The calling thread's current device is
+ * the same after the call as before it.  All calls share the array and it
  * keeps the last call's contents (the counters that must start at zero are
  * cleared by each call), so calls that overlap on the GPU race. */
 AMOE_API int amoe_route_noalloc(int32_t device, int32_t hidden, int32_t experts, int32_t top_k,

@@ -10,7 +10,8 @@ Reference functions restated (paths relative to the reference project root):
   MoERouterTopK      internal/backend/cpuref/moe.go:12-41
   GPTOSSSwiGLU       internal/backend/cpuref/primitives.go:138-149
   MXFP4 decode       internal/model/gptoss/tensor.go:145-170, gguf/reader.go:442-449
-  MoE block          internal/model/gptoss/layer.go:94-188
+  MoE block          internal/model/gptoss/layer.go:94-188 (token by token, or
+                     expert-major with the same arithmetic: moe_block_grouped)
   FP4 activation terms  no reference counterpart: the bit-exact E2M1-term operand of a
                      block-scaled FP4 GEMM (oracle_e2m1_terms in moe_oracle.c)
   RoPE / YaRNRoPE    internal/backend/cpuref/rope.go:10-86           (attn_oracle.c)
@@ -100,6 +101,10 @@ def lib():
             L.oracle_moe_block.argtypes = [
                 ctypes.POINTER(OracleLayer), _f32p, ctypes.c_int, _f32p, _i32p, _f32p, _f32p,
                 _i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+            ]
+            L.oracle_moe_block_grouped.argtypes = [
+                ctypes.POINTER(OracleLayer), _f32p, ctypes.c_int, _f32p, _i32p, _f32p, _f32p,
+                _i32p, ctypes.c_int, ctypes.c_int,
             ]
             L.oracle_route.argtypes = [
                 ctypes.POINTER(OracleLayer), _f32p, ctypes.c_int, _f32p, _i32p, _f32p, ctypes.c_int,
@@ -230,6 +235,27 @@ def moe_block(layer: dict, residual, tokens=None, faithful=False, threads=None):
                                 _p(w, _f32p), _p(logits, _f32p), _p(tok, _i32p) if tok is not None else None,
                                 0 if tok is None else tok.size, 1 if faithful else 0, threads)
     _check(rc, "moe_block")
+    return out, idx, w, logits
+
+
+def moe_block_grouped(layer: dict, residual, tokens=None, threads=None):
+    """moe_block evaluated expert by expert (oracle_moe_block_grouped): the same
+    (out, topk_idx, topk_w, logits), bit for bit, fast enough for full prefill
+    outputs.  tokens: optional row indices to compute (others stay NaN / -1)."""
+    L = _Layer(layer)
+    res = _c(residual, np.float32)
+    T = res.shape[0]
+    H, k, E = layer["hidden"], layer["top_k"], layer["experts"]
+    out = np.full((T, H), np.nan, np.float32)
+    idx = np.full((T, k), -1, np.int32)
+    w = np.full((T, k), np.nan, np.float32)
+    logits = np.full((T, E), np.nan, np.float32)
+    tok = _c(tokens, np.int32) if tokens is not None else None
+    rc = lib().oracle_moe_block_grouped(ctypes.byref(L.s), _p(res, _f32p), T, _p(out, _f32p), _p(idx, _i32p),
+                                        _p(w, _f32p), _p(logits, _f32p),
+                                        _p(tok, _i32p) if tok is not None else None,
+                                        0 if tok is None else tok.size, threads or os.cpu_count() or 1)
+    _check(rc, "moe_block_grouped")
     return out, idx, w, logits
 
 

@@ -435,3 +435,240 @@ int oracle_e2m1_terms(const float *x, int64_t n, int terms, uint8_t *codes, uint
     return 0;
 }
 
+
+/* ---- expert-major evaluation (same arithmetic, all experts at once) ------------------
+ *
+ * oracle_moe_block_grouped computes exactly what oracle_moe_block computes, with
+ * the work reordered so that every expert's MXFP4 rows are decoded once per call
+ * instead of once per (token, expert): each output element is still the float64
+ * sum of float64(x_i) * float64(w_i) in increasing i from 0.0, rounded to float32
+ * once, then the float32 bias (primitives.go:23-30, 43-45); SwiGLU, the slot-order
+ * mixture and the residual add are the per-token code's.  A product of two
+ * float32 values is exact in float64, so vectorising over tokens (each token
+ * keeping its own sequential chain) changes no bit.  Used to check full
+ * prefill-sized outputs in seconds; tests pin it to oracle_moe_block. */
+
+#define GROUP_ROWS 16  /* weight rows decoded per work item */
+#define GROUP_TOK 8    /* tokens whose dot products run side by side */
+
+/* acc[r][j] = sum_i xt[i][j] * w[r][i] (sequential in i, from 0.0) for GROUP_ROWS
+ * rows of decoded weights w (nrows, a multiple of 8) and GROUP_TOK token columns
+ * xt: eight rows by eight tokens per pass, one float64 chain per (row, token). */
+typedef double v8d __attribute__((vector_size(64)));
+#if defined(__x86_64__) && defined(__GNUC__) && !defined(__clang__)
+__attribute__((target_clones("avx512f", "avx2", "default")))
+#endif
+static void dot_block(const double *xt, const double *w, int in_dim, int nrows, double acc[GROUP_ROWS][GROUP_TOK]) {
+    for (int r = 0; r < nrows; r += 8) {
+        v8d a[8];
+        for (int q = 0; q < 8; ++q) a[q] = (v8d){0, 0, 0, 0, 0, 0, 0, 0};
+        const double *wr = w + (int64_t)r * in_dim;
+        for (int i = 0; i < in_dim; ++i) {
+            v8d x;
+            memcpy(&x, xt + (int64_t)i * GROUP_TOK, sizeof(x));
+            for (int q = 0; q < 8; ++q) a[q] += x * wr[(int64_t)q * in_dim + i];
+        }
+        for (int q = 0; q < 8; ++q) memcpy(acc[r + q], &a[q], sizeof(v8d));
+    }
+}
+
+/* Decodes rows [r0, r0 + n) of one expert's MXFP4 tensor into float64 (via the
+ * float32 value scale * table[nibble], tensor.go:152-159).  Rows past n are zero. */
+static void decode_rows_f64(const uint8_t *w, int in_dim, int r0, int n, double *out) {
+    const int64_t row_bytes = (int64_t)in_dim / 32 * 17;
+    for (int r = 0; r < GROUP_ROWS; ++r) {
+        double *o = out + (int64_t)r * in_dim;
+        if (r >= n) {
+            memset(o, 0, sizeof(double) * (size_t)in_dim);
+            continue;
+        }
+        const uint8_t *row = w + (int64_t)(r0 + r) * row_bytes;
+        for (int b = 0; b < in_dim / 32; ++b) {
+            const uint8_t *enc = row + (int64_t)b * 17;
+            const float scale = e8m0_scale(enc[0]);
+            for (int i = 0; i < 16; ++i) {
+                o[b * 32 + 2 * i] = (double)(scale * kE2M1[enc[1 + i] & 0x0f]);
+                o[b * 32 + 2 * i + 1] = (double)(scale * kE2M1[enc[1 + i] >> 4]);
+            }
+        }
+    }
+}
+
+/* One linear layer over an expert's pairs: y[pair][o] = f32(sum) + b[o] for output
+ * rows [r0, r0 + GROUP_ROWS), x rows taken from x + rowsel[j] * in_dim. */
+static void expert_rows_block(const double *wdec, int in_dim, int r0, int nrows, const float *b,
+                              const float *x, const int64_t *rowsel, int npairs, float *y, int64_t y_pitch,
+                              double *xt) {
+    double acc[GROUP_ROWS][GROUP_TOK];
+    for (int j0 = 0; j0 < npairs; j0 += GROUP_TOK) {
+        const int nt = npairs - j0 < GROUP_TOK ? npairs - j0 : GROUP_TOK;
+        for (int j = 0; j < GROUP_TOK; ++j) {
+            const float *xr = j < nt ? x + rowsel[j0 + j] * in_dim : NULL;
+            for (int i = 0; i < in_dim; ++i) xt[(int64_t)i * GROUP_TOK + j] = xr ? (double)xr[i] : 0.0;
+        }
+        dot_block(xt, wdec, in_dim, (nrows + 7) & ~7, acc);
+        for (int j = 0; j < nt; ++j) {
+            float *yr = y + (int64_t)(j0 + j) * y_pitch;
+            for (int r = 0; r < nrows; ++r) yr[r0 + r] = (float)acc[r][j];
+        }
+    }
+    for (int j = 0; j < npairs; ++j) {
+        float *yr = y + (int64_t)j * y_pitch;
+        for (int r = 0; r < nrows; ++r) yr[r0 + r] += b[r0 + r];
+    }
+}
+
+int oracle_moe_block_grouped(const oracle_layer *L, const float *residual, int T, float *out,
+                             int32_t *topk_idx, float *topk_w, float *logits, const int32_t *tokens,
+                             int n_tokens, int threads) {
+    if (validate(L) || T < 0 || L->top_k > 256) return -1;
+    const int H = L->hidden, I = L->intermediate, E = L->experts, k = L->top_k;
+    const int n = tokens ? n_tokens : T;
+    const int nth = threads > 0 ? threads : 1;
+    if (n < 0) return -1;
+    for (int j = 0; j < n; ++j)
+        if (tokens && (tokens[j] < 0 || tokens[j] >= T)) return -1;
+    const int64_t P = (int64_t)n * k;
+    float *xn = (float *)malloc(sizeof(float) * ((size_t)n * H + 1));
+    int32_t *idx = (int32_t *)malloc(sizeof(int32_t) * ((size_t)P + 1));
+    float *w = (float *)malloc(sizeof(float) * ((size_t)P + 1));
+    float *lg = (float *)malloc(sizeof(float) * ((size_t)n * E + 1));
+    int64_t *order = (int64_t *)malloc(sizeof(int64_t) * ((size_t)P + 1)); /* pairs, expert-major */
+    int64_t *tok_of = (int64_t *)malloc(sizeof(int64_t) * ((size_t)P + 1)); /* x row of each sorted pair */
+    int64_t *start = (int64_t *)calloc((size_t)E + 1, sizeof(int64_t));
+    float *act = (float *)malloc(sizeof(float) * ((size_t)P * I + 1)); /* by sorted position */
+    float *y = (float *)malloc(sizeof(float) * ((size_t)P * H + 1));   /* by sorted position */
+    int status = 0;
+    if (!xn || !idx || !w || !lg || !order || !tok_of || !start || !act || !y) status = -1;
+    /* 1. routing (layer.go:96-108) */
+#pragma omp parallel num_threads(nth)
+    {
+        scratch s;
+        int ok = status == 0 && scratch_init(&s, L, 0) == 0;
+#pragma omp for schedule(static)
+        for (int j = 0; j < n; ++j) {
+            if (!ok) continue;
+            const int t = tokens ? tokens[j] : j;
+            if (route_row(L, residual + (int64_t)t * H, &s, idx + (int64_t)j * k, w + (int64_t)j * k)) {
+#pragma omp atomic write
+                status = -1;
+                continue;
+            }
+            memcpy(xn + (int64_t)j * H, s.normalized, sizeof(float) * H);
+            memcpy(lg + (int64_t)j * E, s.logits, sizeof(float) * E);
+        }
+        if (ok) scratch_free(&s);
+        else {
+#pragma omp atomic write
+            status = -1;
+        }
+    }
+    if (status == 0) {
+        /* 2. pairs grouped by expert, (token, slot) order within an expert */
+        for (int64_t p = 0; p < P; ++p) start[idx[p] + 1]++;
+        for (int e = 0; e < E; ++e) start[e + 1] += start[e];
+        int64_t *cur = (int64_t *)malloc(sizeof(int64_t) * ((size_t)E + 1));
+        if (!cur) status = -1;
+        else {
+            memcpy(cur, start, sizeof(int64_t) * (size_t)E);
+            for (int64_t p = 0; p < P; ++p) {
+                const int64_t pos = cur[idx[p]]++;
+                order[pos] = p;
+                tok_of[pos] = p / k;
+            }
+            free(cur);
+        }
+    }
+    if (status == 0) {
+        const int64_t gu_bytes = (int64_t)2 * I * (H / 32) * 17, dn_bytes = (int64_t)H * (I / 32) * 17;
+        const int gu_blocks = (2 * I + GROUP_ROWS - 1) / GROUP_ROWS, dn_blocks = (H + GROUP_ROWS - 1) / GROUP_ROWS;
+        const int kmax = H > I ? H : I;
+        /* 3. gate_up + SwiGLU (layer.go:126-175), then 4. down (layer.go:179-187) */
+        for (int phase = 0; phase < 2 && status == 0; ++phase) {
+            const int nblk = phase == 0 ? gu_blocks : dn_blocks;
+#pragma omp parallel num_threads(nth)
+            {
+                double *wdec = (double *)malloc(sizeof(double) * (size_t)GROUP_ROWS * kmax);
+                double *xt = (double *)malloc(sizeof(double) * (size_t)GROUP_TOK * kmax);
+                float *gu = (float *)malloc(sizeof(float) * (size_t)GROUP_TOK * GROUP_ROWS);
+                int64_t *rowsel = (int64_t *)malloc(sizeof(int64_t) * (size_t)GROUP_TOK);
+                const int ok = wdec && xt && gu && rowsel;
+                if (!ok) {
+#pragma omp atomic write
+                    status = -1;
+                }
+#pragma omp for schedule(dynamic, 1)
+                for (int64_t item = 0; item < (int64_t)E * nblk; ++item) {
+                    const int e = (int)(item / nblk), blk = (int)(item % nblk);
+                    const int64_t p0 = start[e], np = start[e + 1] - start[e];
+                    if (!ok || np == 0) continue;
+                    if (phase == 0) {
+                        const int r0 = blk * GROUP_ROWS;
+                        const int nr = 2 * I - r0 < GROUP_ROWS ? 2 * I - r0 : GROUP_ROWS;
+                        decode_rows_f64(L->gate_up + (int64_t)e * gu_bytes, H, r0, nr, wdec);
+                        const float *bias = L->gate_up_b + (int64_t)e * 2 * I;
+                        for (int64_t j0 = 0; j0 < np; j0 += GROUP_TOK) {
+                            const int nt = np - j0 < GROUP_TOK ? (int)(np - j0) : GROUP_TOK;
+                            for (int j = 0; j < nt; ++j) rowsel[j] = tok_of[p0 + j0 + j];
+                            /* gu[j][r]: rows r0.. of pair j (bias included) */
+                            expert_rows_block(wdec, H, 0, nr, bias + r0, xn, rowsel, nt, gu, GROUP_ROWS, xt);
+                            for (int j = 0; j < nt; ++j) {
+                                float *a = act + (p0 + j0 + j) * I;
+                                for (int r = 0; r + 1 < nr; r += 2) { /* layer.go:145-148 */
+                                    const int i = (r0 + r) / 2;
+                                    oracle_swiglu(&gu[j * GROUP_ROWS + r], &gu[j * GROUP_ROWS + r + 1], 1, &a[i]);
+                                }
+                            }
+                        }
+                    } else {
+                        const int r0 = blk * GROUP_ROWS;
+                        const int nr = H - r0 < GROUP_ROWS ? H - r0 : GROUP_ROWS;
+                        decode_rows_f64(L->down + (int64_t)e * dn_bytes, I, r0, nr, wdec);
+                        for (int64_t j0 = 0; j0 < np; j0 += GROUP_TOK) {
+                            const int nt = np - j0 < GROUP_TOK ? (int)(np - j0) : GROUP_TOK;
+                            for (int j = 0; j < nt; ++j) rowsel[j] = p0 + j0 + j;
+                            expert_rows_block(wdec, I, 0, nr, L->down_b + (int64_t)e * H + r0, act, rowsel, nt,
+                                              y + (p0 + j0) * H + r0, H, xt);
+                        }
+                    }
+                }
+                free(wdec);
+                free(xt);
+                free(gu);
+                free(rowsel);
+            }
+        }
+    }
+    if (status == 0) {
+        /* 5. slot-order mixture and residual (layer.go:109-121) */
+        int64_t *pos_of = tok_of; /* reuse: pair id -> sorted position */
+        for (int64_t q = 0; q < P; ++q) pos_of[order[q]] = q;
+#pragma omp parallel num_threads(nth)
+        {
+            double *mix = (double *)malloc(sizeof(double) * (size_t)H);
+#pragma omp for schedule(static)
+            for (int j = 0; j < n; ++j) {
+                if (!mix) continue;
+                const int t = tokens ? tokens[j] : j;
+                for (int i = 0; i < H; ++i) mix[i] = 0.0;
+                for (int s = 0; s < k; ++s) {
+                    const float *yr = y + pos_of[(int64_t)j * k + s] * H;
+                    const double ws = (double)w[(int64_t)j * k + s];
+                    for (int i = 0; i < H; ++i) mix[i] += ws * (double)yr[i];
+                }
+                const float *row = residual + (int64_t)t * H;
+                for (int i = 0; i < H; ++i) out[(int64_t)t * H + i] = row[i] + (float)mix[i];
+                if (topk_idx) memcpy(topk_idx + (int64_t)t * k, idx + (int64_t)j * k, sizeof(int32_t) * k);
+                if (topk_w) memcpy(topk_w + (int64_t)t * k, w + (int64_t)j * k, sizeof(float) * k);
+                if (logits) memcpy(logits + (int64_t)t * E, lg + (int64_t)j * E, sizeof(float) * E);
+            }
+            if (!mix) {
+#pragma omp atomic write
+                status = -1;
+            }
+            free(mix);
+        }
+    }
+    free(xn); free(idx); free(w); free(lg); free(order); free(tok_of); free(start); free(act); free(y);
+    return status;
+}

@@ -57,7 +57,9 @@ int64_t oracle_mxfp4_encoded_size(int64_t elements);
  * term j takes the remainder r_j (r_0 = x, f32), the smallest scale 2^e with
  * max|r_j| / 2^e <= 6 (E8M0 byte e + 127; 127 for an all-zero remainder), codes
  * round-to-nearest-even of r_j / 2^e on the E2M1 grid, saturated at +-6, and
- * r_{j+1} = r_j - q_j 2^e in f32.  codes [terms][n / 2]: two codes per byte, the
+ * r_{j+1} = r_j - q_j 2^e in f32.  A value that rounds to zero gets code 0 whatever
+ * its sign, never 8 (E2M1's negative zero): a GPU quantizer whose hardware conversion
+ * keeps the sign of zero must clear it to match.  codes [terms][n / 2]: two codes per byte, the
  * lower element in the low nibble; scales [terms][n / 32].  n must be a multiple
  * of 32 and every value finite.  Returns -1 on bad arguments. */
 int oracle_e2m1_terms(const float *x, int64_t n, int terms, uint8_t *codes, uint8_t *scales);
@@ -80,6 +82,15 @@ int oracle_e2m1_terms(const float *x, int64_t n, int terms, uint8_t *codes, uint
 int oracle_moe_block(const oracle_layer *L, const float *residual, int T, float *out,
                      int32_t *topk_idx, float *topk_w, float *logits,
                      const int32_t *tokens, int n_tokens, int faithful, int threads);
+
+/* oracle_moe_block with the work in expert-major order: each routed expert's MXFP4
+ * rows are decoded once per call and multiplied with all of its tokens, every
+ * output element keeping the reference's sequential float64 sum (layer.go:94-188,
+ * primitives.go:11-47).  Outputs are bit-identical to oracle_moe_block (tested);
+ * used to check full prefill-sized outputs.  Same arguments without `faithful`. */
+int oracle_moe_block_grouped(const oracle_layer *L, const float *residual, int T, float *out,
+                             int32_t *topk_idx, float *topk_w, float *logits,
+                             const int32_t *tokens, int n_tokens, int threads);
 
 /* forwardExpert (layer.go:126-188) of expert e on n normalized rows x [n x H]:
  * y [n x H] = down(SwiGLU(gate_up(x))) with biases. */

@@ -4,8 +4,8 @@
 // K-major, as the MXFP4 box planes are stored; E8M0 scales, one per 32 elements, go smem->TMEM
 // with tcgen05.cp 32x128b.warpx4 in the box planes' chunk layout ((r%32)*16 + (r/32)*4 + j);
 // the scale-factor id of an MMA is the byte index of its first scale (0, then 2).
-// Usage: mxf4_tile N unused second_sf_id.  Prints the largest relative error against a
-// float64 CPU product.  One CTA; every wait is bounded.
+// Usage: mxf4_tile N unused second_sf_id.  Prints the largest error against a float64 CPU
+// product, relative to the sum of the absolute products of each dot product.  One CTA; every wait is bounded.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -158,20 +158,26 @@ int main(int argc, char **argv) {
     CK(cudaDeviceSynchronize());
     int err = 0; CK(cudaMemcpy(&err, dErr, 4, cudaMemcpyDeviceToHost));
     std::vector<float> D(128 * 16); CK(cudaMemcpy(D.data(), dD, D.size() * 4, cudaMemcpyDeviceToHost));
-    double maxrel = 0; int bad = 0;
+    // f32 accumulation of 128 exact products: |err| <= 128 * 2^-24 * sum |a_i b_i|, so
+    // the error is measured against that sum (a near-cancelling dot product has a
+    // tiny |ref| but the same absolute rounding)
+    double maxerr = 0; int bad = 0;
     for (int r = 0; r < 128; ++r)
         for (int n = 0; n < N; ++n) {
-            double ref = 0;
+            double ref = 0, mag = 0;
             for (int kq = 0; kq < 128; ++kq) {
                 int nib = (A[r * 64 + kq / 2] >> (4 * (kq & 1))) & 15;
                 int nb = (Bm[n * 64 + kq / 2] >> (4 * (kq & 1))) & 15;
-                ref += (double)e2m1(nib) * ldexp(1.0, sa[r * 4 + kq / 32] - 127) * (double)e2m1(nb) * ldexp(1.0, sbv[n * 4 + kq / 32] - 127);
+                const double t = (double)e2m1(nib) * ldexp(1.0, sa[r * 4 + kq / 32] - 127) * (double)e2m1(nb) *
+                                 ldexp(1.0, sbv[n * 4 + kq / 32] - 127);
+                ref += t;
+                mag += fabs(t);
             }
             double g = D[r * 16 + n];
-            double rel = fabs(g - ref) / (fabs(ref) + 1e-6);
-            if (rel > maxrel) maxrel = rel;
-            if (rel > 1e-5 && bad < 8) { printf("mismatch r %d n %d gpu %g ref %g\n", r, n, g, ref); ++bad; }
+            double err = fabs(g - ref) / (mag > 0 ? mag : 1.0);
+            if (err > maxerr) maxerr = err;
+            if (err > 1e-5 && bad < 8) { printf("mismatch r %d n %d gpu %g ref %g\n", r, n, g, ref); ++bad; }
         }
-    printf("N %d second sf id %d err %d max rel %.3e\n", N, sf2, err, maxrel);
+    printf("N %d second sf id %d err %d max scaled err %.3e\n", N, sf2, err, maxerr);
     return 0;
 }

@@ -70,3 +70,52 @@ def test_no_nvidia_smi_gives_no_record(tmp_path, monkeypatch):
     c = bench.ClockSampler(0)
     c.begin()
     assert c.stop() is None
+
+
+class FakeNvml:
+    """Stand-in for pynvml: fixed SM clock, power and clock-event reason bits."""
+    NVML_CLOCK_SM = 1
+
+    def __init__(self, sm=1350, bits=0x4):
+        self.sm, self.bits = sm, bits
+
+    def nvmlInit(self):
+        pass
+
+    def nvmlDeviceGetHandleByUUID(self, uuid):
+        raise RuntimeError("no uuid lookup here")
+
+    def nvmlDeviceGetHandleByIndex(self, i):
+        return ("gpu", i)
+
+    def nvmlDeviceGetMaxClockInfo(self, h, which):
+        return 1965
+
+    def nvmlDeviceGetClockInfo(self, h, which):
+        return self.sm
+
+    def nvmlDeviceGetPowerUsage(self, h):
+        return 990500  # mW
+
+    def nvmlDeviceGetCurrentClocksEventReasons(self, h):
+        return self.bits
+
+
+def test_nvml_sampler_polls_inside_the_region():
+    c = bench.NvmlClockSampler(0, nvml=FakeNvml())
+    time.sleep(0.05)
+    c.begin()
+    time.sleep(0.2)
+    rec = c.stop()
+    assert rec["source"] == "nvml" and rec["period_ms"] == 10
+    assert rec["samples_in_region"] >= 8  # a 10 ms period lands many samples in a 30 ms region and more
+    assert rec["sm_mhz"] == 1350.0 and rec["sm_max_mhz"] == 1965.0
+    assert rec["reasons"] == ["sw_power_cap"] and rec["power_w_max"] == pytest.approx(990.5)
+
+
+def test_nvml_sampler_reports_thermal_and_hw_slowdown():
+    c = bench.NvmlClockSampler(0, nvml=FakeNvml(sm=700, bits=0x8 | 0x40))
+    c.begin()
+    time.sleep(0.05)
+    rec = c.stop()
+    assert rec["reasons"] == ["hw_slowdown", "hw_thermal_slowdown"] and rec["sm_mhz"] == 700.0

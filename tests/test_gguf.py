@@ -93,6 +93,11 @@ def test_rejects_malformed_files(tmp_path):
     _bad(tmp_path, gguf_bytes(md, [("x", [48], GGUF_MXFP4, bytes(17))]), "divisible by 32")
     _bad(tmp_path, gguf_bytes(md, [("x", [4], 99, bytes(16))]), "unsupported tensor type")
     _bad(tmp_path, gguf_bytes(dict(md, odd=Typed(77, 0)), []), "unknown metadata value type")
+    # element counts that fit int64 but whose encoded byte size does not
+    # (reader.go:429-466): rejected, not wrapped to a small size
+    for shape, ttype in [([1 << 62], 0), ([1 << 61, 2], 0), ([1 << 62], 1), ([1 << 62], 30),
+                         ([(1 << 63) - (1 << 58)], GGUF_Q8_0)]:
+        _bad(tmp_path, gguf_bytes(md, [("x", shape, ttype, b"")]), "encoded tensor size overflows int64")
 
 
 def test_config_needs_gptoss_metadata(tmp_path):

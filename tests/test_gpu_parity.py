@@ -130,25 +130,68 @@ def test_config0_decode_token(cuda_device, path):
     print(f"config0 max-abs {max_abs:.3e} rel-L2 {rel:.3e}")
 
 
-@pytest.mark.parametrize("path", PATHS)
-def test_config1_prefill_4096_sampled_rows(cuda_device, path):
-    layer = W.config_layer(1)
-    x = W.config_tokens(1)
-    _, ref_idx, _ = oracle.route(layer, x)
-    counts = np.bincount(ref_idx.ravel(), minlength=32)
-    busiest = np.nonzero((ref_idx == counts.argmax()).any(axis=1))[0][:6]
-    idlest = np.nonzero((ref_idx == counts.argmin()).any(axis=1))[0][:4]
-    rows = np.unique(np.concatenate([[0, 1, 4095], busiest, idlest, np.arange(100, 4096, 509)]))
-    max_abs, rel = check_against_oracle(layer, x, path, tokens=rows)
-    print(f"config1 rows={len(rows)} max-abs {max_abs:.3e} rel-L2 {rel:.3e}")
+_REF = {}
+
+
+def full_reference(config: int, T: int | None = None):
+    """(layer, x, oracle out, idx, w, logits) of a benchmark configuration, every row:
+    the expert-major oracle, bit-identical to the token-by-token one.  Cached per
+    module: several tests compare with the same reference."""
+    key = (config, T)
+    if key not in _REF:
+        layer = W.config_layer(config)
+        x = W.config_tokens(config, T)
+        _REF[key] = (layer, x) + oracle.moe_block_grouped(layer, x)
+    return _REF[key]
+
+
+def check_full(config: int, path: int, T: int | None = None, max_tokens: int | None = None):
+    """Every output row, the top-k of every row and the permutation of one run
+    against the oracle; returns (max-abs, rel-L2, rows compared, tie rows)."""
+    layer, x, ref_out, ref_idx, ref_w, ref_lg = full_reference(config, T)
+    out, idx, w, (logits, perm, counts, offsets) = run_block(layer, x, path, max_tokens)
+    ties, bad = routing_mismatches(idx, ref_idx, ref_lg)
+    assert not bad, f"routing differs beyond ties on rows {bad[:10]}"
+    np.testing.assert_allclose(logits, ref_lg, rtol=0, atol=1e-6)
+    p_ref, c_ref, o_ref, _ = oracle.permute(idx, layer["experts"])
+    assert np.array_equal(perm, p_ref) and np.array_equal(counts, c_ref) and np.array_equal(offsets, o_ref)
+    keep = np.setdiff1d(np.arange(x.shape[0]), ties)
+    np.testing.assert_allclose(w[keep], ref_w[keep], rtol=2e-6, atol=0)
+    max_abs, rel = assert_block_parity(out, ref_out, keep)
+    return max_abs, rel, len(keep), ties, idx
 
 
 @pytest.mark.parametrize("path", PATHS)
-def test_config3_decode_batch_128_experts(cuda_device, path):
-    layer = W.config_layer(3)
-    x = W.config_tokens(3)
-    rows = np.arange(0, 256, 17)
-    check_against_oracle(layer, x, path, tokens=rows)
+def test_config1_prefill_4096_every_row(cuda_device, path):
+    """Config 1 (T=4096, Zipf-skewed routing): all 4096 output rows on both expert paths."""
+    max_abs, rel, n, ties, _ = check_full(1, path)
+    assert n + len(ties) == 4096
+    print(f"config1 path {path}: rows {n} (ties {len(ties)}) max-abs {max_abs:.3e} rel-L2 {rel:.3e}")
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_config3_decode_batch_256_every_row(cuda_device, path):
+    """Config 3 decode batch (T=256, E=128): all 256 rows on both expert paths."""
+    max_abs, rel, n, ties, _ = check_full(3, path)
+    assert n + len(ties) == 256
+    print(f"config3 decode path {path}: rows {n} max-abs {max_abs:.3e} rel-L2 {rel:.3e}")
+
+
+def test_config3_prefill_8192_every_row(cuda_device):
+    """Config 3 prefill (T=8192, E=128, uniform logits) on one GPU: all 8192 rows."""
+    max_abs, rel, n, ties, _ = check_full(3, moe.PATH_AUTO, T=8192)
+    assert n + len(ties) == 8192
+    print(f"config3 prefill: rows {n} max-abs {max_abs:.3e} rel-L2 {rel:.3e}")
+
+
+def test_config4_adversarial_16384_every_row(cuda_device):
+    """Config 4 (T=16384, router bias +4 on experts 0-7) on one GPU: all 16384 rows,
+    among them every row routed to a hot expert."""
+    max_abs, rel, n, ties, idx = check_full(4, moe.PATH_AUTO)
+    assert n + len(ties) == 16384
+    hot = np.nonzero((idx < W.HOT_EXPERTS).any(axis=1))[0]
+    assert len(hot) > 8192  # the bias sends about half of the pairs to the hot experts
+    print(f"config4: rows {n}, hot rows {len(hot)}, max-abs {max_abs:.3e} rel-L2 {rel:.3e}")
 
 
 def test_device_forward_matches_host_forward_and_is_deterministic(cuda_device):
@@ -196,6 +239,34 @@ def test_errors_are_status_codes(cuda_device):
     out, _, _ = blk.forward(x[:2])  # still usable
     assert np.isfinite(out).all()
     blk.close()
+
+
+@pytest.mark.parametrize("stream_slots", [0, 2])
+def test_allocation_failures_return_nomem_and_keep_the_context_usable(cuda_device, monkeypatch, stream_slots):
+    """Host-side fault injection (AMOE_FAIL_ALLOC_ABOVE: device and pinned-host
+    allocations above the limit fail as out of memory): amoe_create and
+    amoe_upload_layer report AMOE_ERR_NOMEM with a message, and a context whose
+    upload failed still uploads and computes once memory is back."""
+    layer = W.small_layer(hidden=128, intermediate=128, experts=8, top_k=4, seed=5)
+    x = W.make_tokens(W.MoEShape(128, 128, 8, 4), 6, 5)
+    monkeypatch.setenv("AMOE_FAIL_ALLOC_ABOVE", "4096")
+    with pytest.raises(moe.AmoeError) as e:
+        moe.MoEBlock.for_layer(layer, max_tokens=64, stream_slots=stream_slots)
+    assert e.value.code == moe.AMOE_ERR_NOMEM and "out of memory" in str(e.value)
+    monkeypatch.delenv("AMOE_FAIL_ALLOC_ABOVE")
+    blk = moe.MoEBlock.for_layer(layer, max_tokens=64, stream_slots=stream_slots)
+    monkeypatch.setenv("AMOE_FAIL_ALLOC_ABOVE", "65536")  # below one layer's device block
+    with pytest.raises(moe.AmoeError) as e:
+        blk.upload_layer(0, layer)
+    assert e.value.code == moe.AMOE_ERR_NOMEM
+    with pytest.raises(moe.AmoeError) as e:
+        blk.forward(x)  # the layer is still absent
+    assert e.value.code == moe.AMOE_ERR_STATE
+    monkeypatch.delenv("AMOE_FAIL_ALLOC_ABOVE")
+    blk.upload_layer(0, layer)
+    out = blk.forward(x)[0]
+    blk.close()
+    assert_block_parity(out, oracle.moe_block(layer, x)[0])
 
 
 @pytest.mark.parametrize("T,res_path", [(5, moe.PATH_TENSOR), (3, moe.PATH_AUTO)])
@@ -274,3 +345,29 @@ def test_expert_streaming_matches_resident_layers(cuda_device, T):
     stm.prefetch_layer(2)  # nothing to prefetch before routing: a no-op
     res.close()
     stm.close()
+
+
+@pytest.mark.parametrize("stream_experts", [0, 1])
+def test_streamed_stack_matches_oracle_layer_by_layer(cuda_device, stream_experts):
+    """A streamed stack of four config-0-statistics layers (the 20B shape, weights in
+    pinned host memory, two device slots or routed-expert copies) decoding three
+    steps of two tokens; every layer's output is checked against the oracle run on
+    the same input (Generate's layer loop, runtime.go:146-199)."""
+    L = 4
+    layers = [W.stream_layer(i) for i in range(L)]
+    blk = moe.MoEBlock.for_layer(layers[0], layers=L, max_tokens=2, stream_slots=2, stream_experts=stream_experts)
+    for i, layer in enumerate(layers):
+        blk.upload_layer(i, layer)
+    h = W.make_tokens(W.GPTOSS_20B, 2, 2)
+    worst = (0.0, 0.0)
+    for step in range(3):
+        for i in range(L):
+            out, idx, _ = blk.forward(h, layer=i)
+            ref, ref_idx, _, ref_lg = oracle.moe_block(layers[i], h)
+            ties, bad = routing_mismatches(idx, ref_idx, ref_lg)
+            assert not bad and not ties, (step, i)
+            max_abs, rel = assert_block_parity(out, ref)
+            worst = (max(worst[0], max_abs), max(worst[1], rel))
+            h = out
+    blk.close()
+    print(f"streamed stack (stream_experts={stream_experts}): max-abs {worst[0]:.3e} rel-L2 {worst[1]:.3e}")

@@ -25,6 +25,6 @@ def tile_binary(tmp_path_factory):
 def test_mxf4_tile_matches_cpu_product(cuda_device, tile_binary, n):
     out = subprocess.run([tile_binary, str(n), "0", "2"], capture_output=True, text=True, timeout=120)
     assert out.returncode == 0, out.stdout + out.stderr
-    m = re.search(r"err (\d+) max rel ([0-9.e+-]+)", out.stdout)
+    m = re.search(r"err (\d+) max scaled err ([0-9.e+-]+)", out.stdout)
     assert m, out.stdout
     assert int(m.group(1)) == 0 and float(m.group(2)) < 1e-5, out.stdout

@@ -175,3 +175,32 @@ def test_route_matches_block_routing():
     lg, idx, w = oracle.route(layer, x)
     _, idx2, w2, lg2 = oracle.moe_block(layer, x)
     assert np.array_equal(idx, idx2) and np.array_equal(w, w2) and np.array_equal(lg, lg2)
+
+
+@pytest.mark.parametrize("H,I,E,k,T,threads", [(64, 96, 6, 3, 7, 1), (192, 320, 16, 4, 77, 4),
+                                                (2880, 2880, 32, 4, 9, 8), (64, 64, 128, 4, 40, 3)])
+def test_expert_major_oracle_is_bit_identical_to_token_by_token(H, I, E, k, T, threads):
+    """moe_block_grouped (every expert decoded once, its tokens' dot products side by
+    side, each keeping the reference's sequential float64 order) returns exactly what
+    the token-by-token oracle returns: outputs, routing and logits, bit for bit."""
+    layer = W.small_layer(hidden=H, intermediate=I, experts=E, top_k=k, seed=H + E + T)
+    x = W.make_tokens(W.MoEShape(H, I, E, k), T, T)
+    a = oracle.moe_block(layer, x, threads=threads)
+    b = oracle.moe_block_grouped(layer, x, threads=threads)
+    for u, v in zip(a, b):
+        assert np.array_equal(u, v, equal_nan=True)
+    rows = [T - 1, 0, T // 2]
+    a = oracle.moe_block(layer, x, tokens=rows)
+    b = oracle.moe_block_grouped(layer, x, tokens=rows)
+    for u, v in zip(a, b):
+        assert np.array_equal(u, v, equal_nan=True)
+
+
+def test_expert_major_oracle_keeps_nan_scales_and_denormals():
+    layer = W.small_layer(hidden=128, intermediate=128, experts=8, top_k=4, seed=4, scale_lo=0, scale_hi=123)
+    layer["down"].reshape(-1, 17)[5, 0] = 0xFF
+    x = W.make_tokens(W.MoEShape(128, 128, 8, 4), 10, 4)
+    a = oracle.moe_block(layer, x)
+    b = oracle.moe_block_grouped(layer, x)
+    for u, v in zip(a, b):
+        assert np.array_equal(u, v, equal_nan=True)
