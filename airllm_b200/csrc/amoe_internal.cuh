@@ -57,44 +57,42 @@ struct LayerDev {
     uint8_t *dn_q = nullptr;      // [E][H/16][I/64][512]
     uint8_t *dn_s = nullptr;      // [E][H/16][I/64][32]
     float *dn_b = nullptr;        // [E][H]
-    // Block-scaled tensor-core planes (see "TMA planes" below)
-    uint8_t *gu_tq = nullptr;     // [E][2I/128][Hp/128][128][64] E2M1 boxes, rows in fragment order
-    uint8_t *gu_tsf = nullptr;    // [E][2I/128][Hp/128][512] E8M0 in scale-factor chunks
-    uint8_t *dn_tq = nullptr;     // [E][ceil(H/128)][Ip/128][128][64]
-    uint8_t *dn_tsf = nullptr;    // [E][ceil(H/128)][Ip/128][512]
+    // Box planes of the tensor-core GEMMs and the decode kernel (see "Box planes" below)
+    uint8_t *gu_tq = nullptr;     // [E][2I/128][Hp/128] boxes of kBoxStride bytes, rows in fragment order
+    uint8_t *dn_tq = nullptr;     // [E][ceil(H/128)][Ip/128] boxes of kBoxStride bytes
 };
 
 // ---------------------------------------------------------------------------
-// TMA planes for the block-scaled tensor-core path (tcgen05.mma
-// kind::mxf8f6f4.block_scale: E2M1 weights x E4M3 activations, E8M0 scales).
+// Box planes for the block-scaled tensor-core path (tcgen05.mma kind::mxf4:
+// E2M1 weights x E2M1 activation terms, E8M0 scales) and the decode kernel.
 //
-//   tq[e][m][kb][r][64]  box (m, kb): rows 128m..128m+127, elements
-//                   128kb..128kb+127, as the rows' GGUF nibble bytes unchanged
-//                   (byte j: low nibble element 2j, high nibble 2j+1); K padded
-//                   with zeros to Kp = K rounded up to 128 (the TMA 4-bit
-//                   unpacking box is 128 elements wide), rows past R zero.
-//                   Each box is 8 KB contiguous in HBM (whole DRAM pages, not
-//                   64-byte pieces of 128 long rows); TMA loads it as
-//                   CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B into SWIZZLE_128B
-//                   shared memory, the layout the tensor core reads.
-//   tsf[e][m][kc][512]  the E8M0 bytes of the 128-row tile m and the four
-//                   32-element blocks 4kc..4kc+3, at byte
-//                   (r % 32) * 16 + (r / 32) * 4 + j: the scale-factor chunk that
-//                   tcgen05.cp.32x128b.warpx4 spreads over the 128 TMEM lanes
-//                   (lane r, column base + r / 32, byte j).  Padding rows and
-//                   blocks hold 127 (2^0) over zero weights.
+//   tq[e][m][kb]    box (m, kb): rows 128m..128m+127, elements 128kb..128kb+127,
+//                   kBoxStride = 8704 contiguous bytes:
+//     bytes 0..8191     the 128 rows' GGUF nibble bytes (64 per row; byte j: low
+//                       nibble element 2j, high nibble 2j+1), each row's four
+//                       16-byte chunks in the 64-byte swizzle order (chunk c at
+//                       position c ^ ((r / 2) % 4)), the K-major layout the tensor
+//                       core reads;
+//     bytes 8192..8703  the rows' E8M0 bytes, block j of row r at
+//                       (r % 32) * 16 + (r / 32) * 4 + j: the scale-factor chunk
+//                       that tcgen05.cp.32x128b.warpx4 spreads over the 128 TMEM
+//                       lanes (lane r, column base + r / 32, byte j).
+//   So one box -- weights and scales -- reaches shared memory as one copy: a TMA
+//   copy costs tens of cycles of fixed work per copy in the SM's copy engine, so
+//   the pipelines move few, large pieces.  K is padded with zeros to Kp = K
+//   rounded up to 128; rows past R are zero; padding scales are 127 (2^0).
 // gate_up rows use the fragment order of the tiled planes (row 16t + j, j < 8:
 // gate of pair 8t + j; j >= 8: its up row), so a SwiGLU pair sits in TMEM
 // lanes 8 apart.
 // ---------------------------------------------------------------------------
 constexpr int kTmaBoxK = 128;
+constexpr size_t kBoxData = 128 * 64;                  // the box's E2M1 rows
+constexpr size_t kBoxStride = kBoxData + 512;          // ... then its E8M0 chunk
 inline int kpad128(int K) { return (K + kTmaBoxK - 1) / kTmaBoxK * kTmaBoxK; }
-inline size_t tq_bytes(int E, int R, int K) { return (size_t)E * ((R + 127) / 128) * 128 * (kpad128(K) / 2); }
-inline size_t tsf_bytes(int E, int R, int K) {
-    return (size_t)E * ((R + 127) / 128) * (kpad128(K) / kTmaBoxK) * 512;
+inline size_t box_plane_bytes(int E, int R, int K) {
+    return (size_t)E * ((R + 127) / 128) * (kpad128(K) / kTmaBoxK) * kBoxStride;
 }
-cudaError_t launch_repack_tma(const uint8_t *gguf, int E, int R, int K, bool pair_rows, uint8_t *tq, uint8_t *tsf,
-                              cudaStream_t st);
+cudaError_t launch_repack_tma(const uint8_t *gguf, int E, int R, int K, bool pair_rows, uint8_t *tq, cudaStream_t st);
 
 struct Dims {
     int H, I, E, k;

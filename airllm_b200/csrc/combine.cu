@@ -78,10 +78,10 @@ __global__ void repack_kernel(const uint8_t *__restrict__ gguf, int E, int R, in
     }
 }
 
-// K8b: GGUF MXFP4 -> TMA planes (amoe_internal.cuh).  One thread per
+// K8b: GGUF MXFP4 -> box planes (amoe_internal.cuh).  One thread per
 // (expert, padded row, 32-element block) of the padded K range; lossless.
 __global__ void repack_tma_kernel(const uint8_t *__restrict__ gguf, int E, int R, int K, int pair_rows,
-                                  uint8_t *__restrict__ tq, uint8_t *__restrict__ tsf) {
+                                  uint8_t *__restrict__ tq) {
     const int Kp = (K + kTmaBoxK - 1) / kTmaBoxK * kTmaBoxK;
     const int nblk = K / 32, nblkp = Kp / 32, nmt = (R + 127) / 128, Rp = nmt * 128;
     const long long total = (long long)E * Rp * nblkp;
@@ -108,18 +108,21 @@ __global__ void repack_tma_kernel(const uint8_t *__restrict__ gguf, int E, int R
     }
     const int mt = r / 128, rr = r % 128, kc = kb / 4, j = kb % 4;
     const size_t box = ((size_t)e * nmt + mt) * (Kp / kTmaBoxK) + kc;
-    *reinterpret_cast<uint4 *>(tq + box * (128 * 64) + (size_t)rr * 64 + (size_t)j * 16) = q;
-    tsf[box * 512 + (rr % 32) * 16 + (rr / 32) * 4 + j] = scale;
+    // 16-byte chunk j of row rr sits at chunk j ^ ((rr / 2) % 4): the 64-byte swizzle the
+    // tensor core and the decode kernel read, applied here so that a box (rows, then
+    // its scale chunk) moves as one plain copy
+    uint8_t *bx = tq + box * kBoxStride;
+    *reinterpret_cast<uint4 *>(bx + (size_t)rr * 64 + (size_t)((j ^ ((rr >> 1) & 3)) * 16)) = q;
+    bx[kBoxData + (rr % 32) * 16 + (rr / 32) * 4 + j] = scale;
 }
 
 }  // namespace
 
-cudaError_t launch_repack_tma(const uint8_t *gguf, int E, int R, int K, bool pair_rows, uint8_t *tq, uint8_t *tsf,
-                              cudaStream_t st) {
+cudaError_t launch_repack_tma(const uint8_t *gguf, int E, int R, int K, bool pair_rows, uint8_t *tq, cudaStream_t st) {
     const long long total = (long long)E * ((R + 127) / 128) * 128 * (kpad128(K) / 32);
     const int threads = 256;
     repack_tma_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, st>>>(gguf, E, R, K,
-                                                                                       pair_rows ? 1 : 0, tq, tsf);
+                                                                                       pair_rows ? 1 : 0, tq);
     return cudaGetLastError();
 }
 

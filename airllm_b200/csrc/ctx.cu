@@ -30,7 +30,7 @@ struct Status {
 
 struct LayerBlock {
     // byte offsets inside one layer's device-format block (256-B aligned parts)
-    size_t norm, router_w, router_b, gu_b, dn_b, gu_s, dn_s, gu_q, dn_q, gu_tsf, dn_tsf, gu_tq, dn_tq, total;
+    size_t norm, router_w, router_b, gu_b, dn_b, gu_s, dn_s, gu_q, dn_q, gu_tq, dn_tq, total;
     bool frag;  // GEMV fragment tiles stored
 };
 
@@ -53,10 +53,8 @@ LayerBlock layer_block(const Dims &d, int E_x, bool frag) {
     b.router_b = take((size_t)d.E * 4);
     b.gu_b = take(E * 2 * I * 4);
     b.dn_b = take(E * H * 4);
-    b.gu_tsf = take(tsf_bytes((int)E, (int)(2 * I), (int)H));
-    b.dn_tsf = take(tsf_bytes((int)E, (int)H, (int)I));
-    b.gu_tq = take(tq_bytes((int)E, (int)(2 * I), (int)H));
-    b.dn_tq = take(tq_bytes((int)E, (int)H, (int)I));
+    b.gu_tq = take(box_plane_bytes((int)E, (int)(2 * I), (int)H));
+    b.dn_tq = take(box_plane_bytes((int)E, (int)H, (int)I));
     b.frag = frag;
     if (frag) {
         b.gu_s = take(E * 2 * I * (H / 32));
@@ -81,8 +79,6 @@ LayerDev layer_view(uint8_t *base, const LayerBlock &b) {
         L.gu_q = base + b.gu_q;
         L.dn_q = base + b.dn_q;
     }
-    L.gu_tsf = base + b.gu_tsf;
-    L.dn_tsf = base + b.dn_tsf;
     L.gu_tq = base + b.gu_tq;
     L.dn_tq = base + b.dn_tq;
     return L;
@@ -707,8 +703,7 @@ int forward_selected(amoe_ctx *c, int32_t layer, const float *residual, int32_t 
     timer.mark(1);
     // the routed experts, ascending, into slot positions 0..n-1
     const LayerBlock &b = c->blk, &x = c->xblk;
-    const size_t gq = tq_bytes(1, 2 * d.I, d.H), gs = tsf_bytes(1, 2 * d.I, d.H);
-    const size_t dq = tq_bytes(1, d.H, d.I), ds = tsf_bytes(1, d.H, d.I);
+    const size_t gq = box_plane_bytes(1, 2 * d.I, d.H), dq = box_plane_bytes(1, d.H, d.I);
     const size_t gb = (size_t)2 * d.I * 4, db = H * 4;
     const uint8_t *host = c->layer_host[layer];
     const int P = h_off[E];
@@ -718,8 +713,7 @@ int forward_selected(amoe_ctx *c, int32_t layer, const float *residual, int32_t 
         const size_t j = (size_t)n;
         struct Part {
             size_t src, dst, bytes;
-        } parts[] = {{b.gu_tq + e * gq, x.gu_tq + j * gq, gq}, {b.gu_tsf + e * gs, x.gu_tsf + j * gs, gs},
-                     {b.dn_tq + e * dq, x.dn_tq + j * dq, dq}, {b.dn_tsf + e * ds, x.dn_tsf + j * ds, ds},
+        } parts[] = {{b.gu_tq + e * gq, x.gu_tq + j * gq, gq}, {b.dn_tq + e * dq, x.dn_tq + j * dq, dq},
                      {b.gu_b + e * gb, x.gu_b + j * gb, gb},    {b.dn_b + e * db, x.dn_b + j * db, db}};
         for (const Part &q : parts)
             AMOE_CUDA(c, cudaMemcpyAsync(c->xslot + q.dst, host + q.src, q.bytes, cudaMemcpyHostToDevice, st));
@@ -1062,11 +1056,11 @@ int amoe_upload_layer(amoe_ctx *c, int32_t layer, const float *norm_gain, const 
     UP_CUDA(cudaMemcpyAsync(L.dn_b, down_b + e0 * H, E * H * 4, cudaMemcpyHostToDevice, st));
     UP_CUDA(cudaMemcpyAsync(staging, gate_up + e0 * gu_expert, gu_bytes, cudaMemcpyHostToDevice, st));
     if (c->blk.frag) UP_CUDA(launch_repack(staging, (int)E, (int)(2 * I), (int)H, true, L.gu_q, L.gu_s, st));
-    UP_CUDA(launch_repack_tma(staging, (int)E, (int)(2 * I), (int)H, true, L.gu_tq, L.gu_tsf, st));
+    UP_CUDA(launch_repack_tma(staging, (int)E, (int)(2 * I), (int)H, true, L.gu_tq, st));
     UP_CUDA(cudaStreamSynchronize(st));  // staging is reused for down
     UP_CUDA(cudaMemcpyAsync(staging, down + e0 * dn_expert, dn_bytes, cudaMemcpyHostToDevice, st));
     if (c->blk.frag) UP_CUDA(launch_repack(staging, (int)E, (int)H, (int)I, false, L.dn_q, L.dn_s, st));
-    UP_CUDA(launch_repack_tma(staging, (int)E, (int)H, (int)I, false, L.dn_tq, L.dn_tsf, st));
+    UP_CUDA(launch_repack_tma(staging, (int)E, (int)H, (int)I, false, L.dn_tq, st));
     if (streaming(c)) {
         if (c->router_res) {  // expert streaming: the layer's norm and router stay on the device
             float *dst = c->router_res + (size_t)layer * (H + E_all * H + E_all);

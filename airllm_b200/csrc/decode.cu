@@ -27,8 +27,10 @@
 //
 // Weights.  The units' boxes stream from the TMA box planes (128 rows x 64 B of
 // GGUF nibble bytes per 128-element K box, 8 KB, plus the box's 512-byte E8M0
-// chunk) into a ring of 17 KB stages, two boxes per stage, with SWIZZLE_64B so
-// the fragment loads below are free of bank conflicts.  There is no producer
+// chunk) into a ring of 17 KB stages, two boxes per stage, one bulk copy per
+// stage (a box's rows and its scale chunk are stored together); the planes hold
+// every row in the 64-byte swizzle order, so the fragment loads below are free
+// of bank conflicts.  There is no producer
 // warp: one thread fills the first stages, and afterwards the last warp to
 // finish with a stage refills its slot with the stage a ring further on (all 16
 // warps then fit four per SM sub-partition with 128 registers each).  The
@@ -66,7 +68,8 @@ constexpr int kComputeWarps = kGroups * kGroupWarps;
 constexpr int kComputeThreads = kComputeWarps * 32;
 constexpr int kDecThreads = kComputeWarps * 32;  // no producer warp: the last releaser of a stage refills it
 constexpr uint32_t kBoxBytes = 128 * 64;        // one packed box: 128 rows x 128 E2M1 values
-constexpr uint32_t kStageBytes = 2 * kBoxBytes + 2 * 512;  // two boxes, then their scale chunks
+constexpr uint32_t kBoxStep = (uint32_t)kBoxStride;  // a box's rows and its scale chunk, as stored
+constexpr uint32_t kStageBytes = 2 * kBoxStep;       // two boxes, each followed by its scale chunk
 constexpr int kMaxStages = 12;
 constexpr int kMaxUnits = 64;                   // units per CTA
 constexpr int kSchedWords = 1024;               // one CTA's schedule rows (int32)
@@ -88,7 +91,7 @@ struct DecodeParams {
     float eps;
     RouteOut route;             // routing outputs (logits doubles as the cross-CTA exchange buffer)
     unsigned *rflag;            // [G] launch epoch once a CTA's router dot products are stored
-    const uint8_t *gu_tsf, *dn_tsf;
+    const uint8_t *gu_tq, *dn_tq;    // box planes: per box its swizzled rows, then its scale chunk
     const float *gu_b, *dn_b;
     float *act;                 // [S][T][Ip] SwiGLU outputs of every token for every slot (padding stays 0)
     float *yb;                  // [S][2][T][H] down outputs, one plane per K half
@@ -207,9 +210,7 @@ __device__ __forceinline__ void put_split8(uint8_t *buf, uint32_t stride, int t,
 
 template <int NCOL>
 __launch_bounds__(kDecThreads, 1) __global__
-    void decode_kernel(const __grid_constant__ CUtensorMap tm_gu2, const __grid_constant__ CUtensorMap tm_gu1,
-                       const __grid_constant__ CUtensorMap tm_dn2, const __grid_constant__ CUtensorMap tm_dn1,
-                       DecodeParams p) {
+    void decode_kernel(DecodeParams p) {
     extern __shared__ __align__(1024) uint8_t sm_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
     const DecLayout lay = dec_layout(p.T, p.Hp, p.Ip, p.E, p.k, p.stages, NCOL);
@@ -235,8 +236,6 @@ __launch_bounds__(kDecThreads, 1) __global__
     const unsigned epoch = p.bar->epoch[blockIdx.x] + 1u;
 
     if (tid == 0) {
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_gu2)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_dn2)) : "memory");
         misc[0] = 0;
         for (int s = 0; s < R; ++s) {
             mbar_init(full + s, 1);
@@ -500,10 +499,8 @@ __launch_bounds__(kDecThreads, 1) __global__
         const int sl = j % R;
         uint8_t *st = ring + (size_t)sl * kStageBytes;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the slot's reads before the copy's writes
-        mbar_expect_tx(full + sl, (uint32_t)nb * (kBoxBytes + 512));
-        const CUtensorMap *tm = phase ? (nb == 2 ? &tm_dn2 : &tm_dn1) : (nb == 2 ? &tm_gu2 : &tm_gu1);
-        tma_2d(st, tm, full + sl, 0, (int)(box * 128));
-        bulk_g2s(st + 2 * kBoxBytes, (phase ? p.dn_tsf : p.gu_tsf) + box * 512, (uint32_t)nb * 512, full + sl);
+        mbar_expect_tx(full + sl, (uint32_t)nb * kBoxStep);
+        bulk_g2s(st, (phase ? p.dn_tq : p.gu_tq) + box * kBoxStep, (uint32_t)nb * kBoxStep, full + sl);
         rel_s[R + sl] = j;
     };
     if (tid == 0) {
@@ -584,10 +581,10 @@ __launch_bounds__(kDecThreads, 1) __global__
 #pragma unroll
                 for (int b = 0; b < 2; ++b) {
                     if (b < nb) {
-                        const uint8_t *rows = st + b * kBoxBytes + r0 * 64;
+                        const uint8_t *rows = st + b * kBoxStep + r0 * 64;
                         const uint8_t *xk = bcol + 2 * 128 * (kb + b);
-                        sv0[b] = *reinterpret_cast<const uint32_t *>(st + 2 * kBoxBytes + b * 512 + sc0);
-                        sv1[b] = *reinterpret_cast<const uint32_t *>(st + 2 * kBoxBytes + b * 512 + sc1);
+                        sv0[b] = *reinterpret_cast<const uint32_t *>(st + b * kBoxStep + kBoxBytes + sc0);
+                        sv1[b] = *reinterpret_cast<const uint32_t *>(st + b * kBoxStep + kBoxBytes + sc1);
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
                             w0[b][q] = *reinterpret_cast<const uint32_t *>(rows + off[q]);
@@ -804,19 +801,6 @@ DecScratch dec_scratch(const Dims &d, int G, const Schedule &s) {
 
 int grid_of(int device) { return device >= 0 && device < 64 && caps(device).sms > 0 ? caps(device).sms : 1; }
 
-// Box-tiled E2M1 plane as bytes: rows of 64 B (128 packed values), boxes of
-// box_rows rows (one or two 128-row K boxes), SWIZZLE_64B.
-cudaError_t map_plane(CUtensorMap *tm, const void *base, uint64_t rows, uint32_t box_rows) {
-    cuuint64_t dims[2] = {64, rows};
-    cuuint64_t strides[1] = {64};
-    cuuint32_t box[2] = {64, box_rows};
-    cuuint32_t es[2] = {1, 1};
-    CUresult r = encode_fn()(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, es,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
-                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
-}
-
 }  // namespace
 
 size_t decode_scratch_bytes(const Dims &d, int device) {
@@ -838,7 +822,7 @@ cudaError_t init_decode_scratch(const Dims &d, int device, void *scratch, cudaSt
 bool decode_supported(const Dims &d, int T, int device) {
     if (T < 1 || T > kDecodeMaxTokens || device < 0 || device >= 64) return false;
     const DecodeCaps &cp = caps(device);
-    if (!cp.coop || cp.sms <= 0 || cp.sms > kDecodeMaxCtas || !get_encode()) return false;
+    if (!cp.coop || cp.sms <= 0 || cp.sms > kDecodeMaxCtas) return false;
     if ((2 * d.I) % 128 || d.H > 4096 || d.I > 4096 || d.E > 256 || d.k > 32 || dec_slots(d) > 1023) return false;
     if (2 * d.I / 128 > 4095 || (d.H + 127) / 128 > 4095) return false;
     if (dec_stages(T, kpad128(d.H), kpad128(d.I), d.E, d.k) < 2) return false;
@@ -883,8 +867,8 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
     p.eps = d.eps;
     p.route = r;
     p.rflag = reinterpret_cast<unsigned *>(b + lay.rflag);
-    p.gu_tsf = L.gu_tsf;
-    p.dn_tsf = L.dn_tsf;
+    p.gu_tq = L.gu_tq;
+    p.dn_tq = L.dn_tq;
     p.gu_b = L.gu_b;
     p.dn_b = L.dn_b;
     p.act = reinterpret_cast<float *>(b + lay.act);
@@ -904,17 +888,10 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
     p.Ip = Ip;
     p.S = S;
     p.stages = dec_stages(T, Hp, Ip, d.E, d.k);
-    if (p.stages < 2 || !get_encode()) return cudaErrorInvalidValue;
-    CUtensorMap tm_gu2, tm_gu1, tm_dn2, tm_dn1;
-    const uint64_t gu_rows = tq_bytes(d.E, 2 * d.I, d.H) / 64, dn_rows = tq_bytes(d.E, d.H, d.I) / 64;
-    cudaError_t e = map_plane(&tm_gu2, L.gu_tq, gu_rows, 256);
-    if (e == cudaSuccess) e = map_plane(&tm_gu1, L.gu_tq, gu_rows, 128);
-    if (e == cudaSuccess) e = map_plane(&tm_dn2, L.dn_tq, dn_rows, 256);
-    if (e == cudaSuccess) e = map_plane(&tm_dn1, L.dn_tq, dn_rows, 128);
-    if (e != cudaSuccess) return e;
+    if (p.stages < 2) return cudaErrorInvalidValue;
     const size_t smem = dec_layout(T, Hp, Ip, d.E, d.k, p.stages, ncol).total;
     auto kern = ncol == 2 ? decode_kernel<2> : (ncol == 4 ? decode_kernel<4> : decode_kernel<8>);
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(G);
@@ -926,7 +903,7 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, tm_gu2, tm_gu1, tm_dn2, tm_dn1, p);
+    return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 }  // namespace amoe

@@ -1,42 +1,50 @@
 // gemm_bs.cu -- K4/K5: the grouped expert GEMMs of prefill on the block-scaled
-// 5th-generation tensor cores (tcgen05.mma kind::mxf8f6f4.block_scale).
+// FP4 rate of the 5th-generation tensor cores (tcgen05.mma kind::mxf4).
 //
 // Per expert e with m_e routed rows (positions offsets[e]..offsets[e+1] of the
 // expert-sorted pairs):
 //   gate_up: act = SwiGLU(W_gu . x + b_gu)   (layer.go:139-148, 175; primitives.go:138-149)
 //   down:    y   = W_dn . act + b_dn          (layer.go:179-187)
 //
-// A = the MXFP4 weights as stored: E2M1 nibbles from the box-tiled TMA planes
-//     (TMA unpacks them into the tensor core's shared-memory format) with the
-//     GGUF E8M0 bytes as the hardware block scales -- no conversion pass.
-// B = the activations as four E4M3 terms per element, x ~= sum_j q_j 2^(e0-4j)
-//     per 32-element block (e0 from the block's largest magnitude), one term per
-//     MMA column: a tile of 60 tokens is N = 240 columns, and the epilogue adds
-//     each token's four columns.  Four terms carry ~16 significant bits; the
-//     tensor core accumulates in f32.
+// A = the MXFP4 weights exactly as stored: the box-tiled E2M1 planes (64-byte
+//     rows of 128 packed elements, kept in global memory in the 64-byte swizzle
+//     order the tensor core reads) with the GGUF E8M0 bytes as the hardware block
+//     scales.
+// B = the activations as five E2M1 terms per element with their own E8M0 scale
+//     per 32 elements and term (fp4_terms.cuh), one term per MMA column: a tile
+//     of 48 tokens is N = 240 columns, and the epilogue adds each token's five
+//     columns.  The tensor core multiplies E2M1 x E2M1 exactly and accumulates in
+//     f32.
 //
-// Tokens are tiled per expert (60 per tile, the last tile of an expert ragged).
-// The B operand of every (tile, 128-element K box) sits in global memory as one
-// 32 KB blob of two halves, one per CTA of a pair: the box's E8M0 scale chunks
-// (1 KB), then 120 pre-swizzled rows of E4M3 terms.  gate_up's epilogue writes
-// down's B operand in the same form: SwiGLU, block maxima, quantization to four
-// terms, 16-byte swizzled stores.
+// Tokens are tiled per expert (48 per tile, the last tile of an expert ragged).
+// The B operand of every (tile, 128-element K box) sits in global memory as 240
+// rows of 64 bytes (row 5i + j: token i, term j), also in the swizzle order:
+// each CTA's 120 rows followed by the 1 KB of scale chunks of all 240 rows.  gate_up's epilogue writes down's B
+// operand in the same form: SwiGLU, then the five terms of every (token, 32-pair
+// block).
+//
+// Every operand therefore reaches shared memory as one plain copy (TMA without
+// swizzle) of data and scales stored side by side: a stage is two copies of
+// 17 KB per CTA: two adjacent A boxes, and this CTA's parts of the same two B
+// boxes.  Each TMA copy costs the SM's copy engine about 50-60 cycles of fixed
+// work besides its bytes, and a copy's latency is long, so the pipeline moves few,
+// large copies: rows and scales in separate small copies fed the FP4 MMAs at half
+// their rate.
 //
 // The MMAs are 2-SM (tcgen05 cta_group::2): a cluster of two CTAs computes a
-// 256-row weight tile x 60 tokens.  Each CTA loads its own 128-row A box, its
-// half of the B rows and the full B scales; every load signals the leader CTA's
-// barrier, the leader issues the MMAs (M = 256, N = 240) and commits to both
-// CTAs' barriers, and each CTA's epilogue reads the accumulator rows in its own
-// TMEM.  Each SM thus loads half of every B tile it multiplies, which halves the
-// operand traffic per MMA compared with one CTA per 128-row tile.
+// 256-row weight tile x 48 tokens.  Each CTA loads its own 128-row A box, its
+// half of the B rows (120) and the full B scales; every load signals the leader
+// CTA's barrier, the leader issues the MMAs (M = 256, N = 240, K = 64, two per
+// box) and commits to both CTAs' barriers, and each CTA's epilogue reads the
+// accumulator rows in its own TMEM.
 //
 // Work item = (token tile, 256-row weight pair), clusters striding over items.
-// Roles per CTA: warps 0-5 TMA producers (stage i by warp i % 6: one warp per
-// ring slot), warp 6 MMA issuer (leader) and TMEM owner, warps 7-14 epilogue
-// (two per TMEM lane quadrant, splitting the tile's tokens).  TMEM: two
-// 240-column accumulators (the epilogue of one item overlaps the next item's
-// MMAs) and two 12-column scale-factor slots.  Every wait is bounded; on timeout
-// the kernel records a code in the error flag and winds down.
+// Roles per CTA: warp 0 TMA producer, warp 1 MMA issuer (leader) and TMEM owner,
+// warps 2-13 epilogue (three per TMEM lane quadrant, each with a third of the
+// tile's tokens).  TMEM: two 240-column accumulators (the epilogue of one item overlaps
+// the next item's MMAs) and two 12-column scale-factor slots used alternately.  Every wait is
+// bounded; on timeout the kernel records a code in the error flag and winds down.
+#include "fp4_terms.cuh"
 #include "tc_ptx.cuh"
 
 namespace amoe {
@@ -45,35 +53,42 @@ namespace {
 
 using namespace bs;
 
-constexpr int kTok = 60;                          // tokens per tile
-constexpr int kN = 4 * kTok;                      // MMA N: four E4M3 terms per token
+constexpr int kTerms = fp4::kTerms;               // E2M1 terms per activation value
+constexpr int kTok = 48;                          // tokens per tile
+constexpr int kN = kTerms * kTok;                 // MMA N: 240
 constexpr int kHalfRows = kN / 2;                 // B rows per CTA of a pair
-constexpr uint32_t kBSf = 1024;                   // a B box's scale chunks: rows 0-127, 128-239
-constexpr uint32_t kHalf = kBSf + kHalfRows * 128;  // 16384: scales + 120 pre-swizzled rows (one TMA box)
-constexpr uint32_t kBlob = 2 * kHalf;             // one (tile, K box) B operand
-constexpr uint32_t kABox = 128 * 128;             // unpacked A box in shared memory
-constexpr uint32_t kAPacked = 128 * 64;           // its bytes in global memory (TMA transaction size)
-constexpr uint32_t kStageBytes = 33792;           // A box | B half | A scales, padded to 1 KB
+constexpr uint32_t kRow = 64;                     // one 128-element K box of a row, packed E2M1
+constexpr uint32_t kABytes = 128 * kRow;          // A box rows
+constexpr uint32_t kBHalf = kHalfRows * kRow;     // this CTA's B rows of a box
+constexpr uint32_t kBSf = 1024;                   // B scale chunks of one (tile, box): rows 0-127, 128-239
+constexpr uint32_t kBPart = kBHalf + kBSf;        // what one CTA copies of a B blob: its rows, then all scales
+// Stage: two K boxes.  The A boxes as stored (rows, then the scale chunk, each),
+// then this CTA's B parts of the same two boxes.
+constexpr int kBoxes = 2;
+constexpr uint32_t kStageA = kBoxes * (uint32_t)kBoxStride;   // 17 KB
+constexpr uint32_t kStageBytes = kStageA + kBoxes * kBPart;   // 34 KB
 constexpr int kStages = 6;
-constexpr int kProdWarps = kStages;
-constexpr int kMmaWarp = kProdWarps;
-constexpr int kEpiWarp0 = kMmaWarp + 1;
-constexpr int kEpiWarps = 8;                      // two per TMEM lane quadrant (token halves 0-31, 32-59)
+constexpr uint32_t kCopyRow = 512;                // TMA row width: both copies of a stage are whole rows
+constexpr int kProdWarp = 0, kMmaWarp = 1, kEpiWarp0 = 2;
+constexpr int kEpiGroups = 3;                     // epilogue warps per TMEM lane quadrant
+constexpr int kEpiWarps = 4 * kEpiGroups;
 constexpr int kEpiThreads = kEpiWarps * 32;
-constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 480
+constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 448
+constexpr int kGroupTok = kTok / kEpiGroups;      // tokens per epilogue warp: 16
 constexpr uint32_t kSfCol = 2 * kN;               // TMEM column of scale-factor slot 0 (slot 1: +16)
-constexpr int kActPitch = 68;                     // gate_up epilogue staging: [60 tokens][64 pairs] f32, padded rows
+constexpr int kActPitch = 68;                     // gate_up staging: [48 tokens][64 pairs] f32, padded rows
 constexpr uint32_t kOutStage = kTok * kActPitch * 4;
-constexpr size_t kSmem = 1024 + kStages * kStageBytes + kOutStage + 16 * 8 + 16;
-constexpr uint32_t kStageTx = 2 * (kAPacked + kHalf + 512);  // bytes both CTAs' loads bring per stage
+constexpr size_t kSmem = 1024 + kStages * kStageBytes + kOutStage + 32 * 8 + 16;
 
-static_assert(kABox + kHalf + 512 <= kStageBytes && kStageBytes % 1024 == 0, "stage layout");
-static_assert(kHalfRows % 8 == 0, "B halves start on a swizzle atom");
-// Each producer warp owns one ring slot, so its waits on that slot's empty
-// barrier are for consecutive phases (a parity wait two phases ahead would pass).
-static_assert(kProdWarps == kStages, "one producer warp per ring slot");
+static_assert(kN % 16 == 0 && kN <= 256, "MMA N for M = 256");
+static_assert(kStageA % 1024 == 0 && kStageBytes % 1024 == 0 && kBoxStride % 512 == 0 && kBPart % 512 == 0,
+              "64-byte swizzle atoms start on 512 B");
 static_assert(kSfCol + 16 + 12 <= 512, "TMEM budget");
 static_assert(kSmem <= 232448, "shared memory budget");
+static_assert(kGroupTok * kTerms == 80, "an epilogue warp reads 80 TMEM columns (tmem_ld80)");
+static_assert(kEpiThreads == 4 * 2 * kTok, "four lanes per (token, 32-pair block) in the gate_up quantization");
+static_assert(kBoxStride % kCopyRow == 0 && kBPart % kCopyRow == 0 && kHalfRows % 8 == 0, "copies of whole rows");
+constexpr uint32_t kARows = (uint32_t)kBoxStride / kCopyRow, kBRows = kBPart / kCopyRow;
 
 struct BsParams {
     const int4 *tiles;     // [tiles] {expert, first position, tokens, 0}
@@ -93,22 +108,42 @@ struct BsParams {
     int gate_want;
 };
 
-// Blob byte offset of B row n (token 4i + term j), 16-byte chunk c: half n / 120,
-// after its scale chunks; SWIZZLE_128B within the half (120 is a multiple of 8).
-__device__ __forceinline__ uint32_t swz(int n, int c) {
-    const int h = n >= kHalfRows, r = n - kHalfRows * h;
-    return (uint32_t)h * kHalf + kBSf + (uint32_t)r * 128u + (uint32_t)((c ^ (r & 7)) << 4);
-}
-
-// Scale byte of B row n, 32-element block jb of a box, inside one half's chunks
+// Scale byte of B row n, 32-element block jb of a box, inside its 1 KB of chunks
 // (chunk n / 128 in the layout tcgen05.cp.32x128b.warpx4 spreads over TMEM).
 __device__ __forceinline__ uint32_t sf_at(int n, int jb) {
     return (uint32_t)(n >> 7) * 512u + (uint32_t)(n & 31) * 16u + (uint32_t)((n & 127) >> 5) * 4u + (uint32_t)jb;
 }
 
-__device__ __forceinline__ void put_sf(uint8_t *blob, int n, int jb, uint8_t v) {  // both halves carry the scales
-    blob[sf_at(n, jb)] = v;
-    blob[kHalf + sf_at(n, jb)] = v;
+// B operand in global memory: part (t, kb, h) -- CTA h's 120 rows of tile t's K
+// box kb, then the scale chunks of all 240 rows -- is kBPart bytes at index
+// ((t * nkb2 + kb / 2) * 2 + h) * 2 + kb % 2 (nkb2: boxes rounded up to pairs), so
+// that a CTA's parts of a stage's two boxes are adjacent: one copy.
+__device__ __forceinline__ size_t bpart_index(int t, int kb, int h, int nkb2) {
+    return (((size_t)t * nkb2 + (kb >> 1)) * 2 + h) * kBoxes + (kb & 1);
+}
+__device__ __forceinline__ uint8_t *bpart(uint8_t *b, int t, int kb, int h, int nkb2) {
+    return b + bpart_index(t, kb, h, nkb2) * kBPart;
+}
+// Byte offset of 16-byte chunk c of B row r (0..119) inside its part: the rows are
+// stored in the 64-byte swizzle order (chunk c at c ^ ((r / 2) % 4)).
+__device__ __forceinline__ uint32_t brow_at(int r, int c) {
+    return (uint32_t)r * kRow + (uint32_t)((c ^ ((r >> 1) & 3)) << 4);
+}
+// Stores the codes of row n (token n / 5, term n % 5), 32-element block jb, bytes
+// [NB sub, NB (sub + 1)) of the block's 16.
+template <int NB>
+__device__ __forceinline__ void put_codes(uint8_t *b, int t, int kb, int nkb2, int n, int jb, int sub,
+                                          const uint32_t (&w)[NB / 4]) {
+    const int h = n >= kHalfRows, r = n - kHalfRows * h;
+    uint8_t *dst = bpart(b, t, kb, h, nkb2) + brow_at(r, jb) + sub * NB;
+    if (NB == 16) *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    else if (NB == 8) *reinterpret_cast<uint2 *>(dst) = make_uint2(w[0], w[1]);
+    else *reinterpret_cast<uint32_t *>(dst) = w[0];
+}
+// The scale byte of row n, block jb, into both CTA parts of the blob.
+__device__ __forceinline__ void put_scale(uint8_t *b, int t, int kb, int nkb2, int n, int jb, uint32_t sbyte) {
+    bpart(b, t, kb, 0, nkb2)[kBHalf + sf_at(n, jb)] = (uint8_t)sbyte;
+    bpart(b, t, kb, 1, nkb2)[kBHalf + sf_at(n, jb)] = (uint8_t)sbyte;
 }
 
 // Token tiles of every expert: tile t = {e, first position, tokens}.
@@ -135,18 +170,20 @@ __global__ void __launch_bounds__(256) bs_plan_kernel(const int32_t *__restrict_
 
 // The gate_up B operand: one CTA per (tile, K box), one thread per (token, 32-element
 // block).  Rows are the fp16 hi + lo split of the normalized tokens, gathered
-// through the permutation (or, with perm NULL, already by position).
-__global__ void __launch_bounds__(256) bs_quant_kernel(const __half *__restrict__ x_hi, const __half *__restrict__ x_lo,
-                                                       const int32_t *__restrict__ perm, int k, int K, int nkb,
-                                                       const int4 *__restrict__ tiles, const int32_t *ntiles,
-                                                       uint8_t *bq) {
+// through the permutation (or, with perm NULL, already by position).  Tokens past
+// the tile's count and elements past K are zeros.
+__global__ void __launch_bounds__(kTok * 4) bs_quant_kernel(const __half *__restrict__ x_hi,
+                                                            const __half *__restrict__ x_lo,
+                                                            const int32_t *__restrict__ perm, int k, int K, int nkb,
+                                                            const int4 *__restrict__ tiles, const int32_t *ntiles,
+                                                            uint8_t *bq) {
     const int t = blockIdx.x / nkb, kb = blockIdx.x - t * nkb;
-    if (t >= *ntiles || threadIdx.x >= kTok * 4) return;
+    if (t >= *ntiles) return;  // uniform over the CTA
     const int4 ti = tiles[t];
     const int i = threadIdx.x >> 2, jb = threadIdx.x & 3;
     const int k0 = kb * 128 + jb * 32;
     float x[32];
-    bool live = i < ti.z && k0 < K;
+    const bool live = i < ti.z && k0 < K;
     if (live) {
         const int pos = ti.y + i;
         const size_t row = perm ? (size_t)(perm[pos] / k) : (size_t)pos;
@@ -164,37 +201,25 @@ __global__ void __launch_bounds__(256) bs_quant_kernel(const __half *__restrict_
                 x[8 * c + 2 * q + 1] = a.y + b.y;
             }
         }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) x[j] = 0.0f;
     }
-    float amax = 0.0f;
+    uint32_t codes[kTerms][4], sbyte[kTerms];
+    fp4::quantize<32, 1>(x, codes, sbyte);
+    const int nkb2 = (nkb + 1) >> 1;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) amax = live ? fmaxf(amax, fabsf(x[j])) : 0.0f;
-    const int e0 = block_exp(amax);
-    const TermScales ts = term_scales(e0);
-    uint32_t w[4][8];  // [term][4 elements]
-#pragma unroll
-    for (int g = 0; g < 8; ++g) {
-        uint32_t lo[4], hi[4];
-        quant4_pair(live ? x[4 * g] : 0.0f, live ? x[4 * g + 1] : 0.0f, ts, lo);
-        quant4_pair(live ? x[4 * g + 2] : 0.0f, live ? x[4 * g + 3] : 0.0f, ts, hi);
-#pragma unroll
-        for (int term = 0; term < 4; ++term) w[term][g] = (lo[term] & 0xffffu) | (hi[term] << 16);
-    }
-    uint8_t *blob = bq + ((size_t)t * nkb + kb) * kBlob;
-#pragma unroll
-    for (int term = 0; term < 4; ++term) {
-        const uint32_t *wt = w[term];
-        const int r = 4 * i + term;
-        *reinterpret_cast<uint4 *>(blob + swz(r, 2 * jb)) = make_uint4(wt[0], wt[1], wt[2], wt[3]);
-        *reinterpret_cast<uint4 *>(blob + swz(r, 2 * jb + 1)) = make_uint4(wt[4], wt[5], wt[6], wt[7]);
-        put_sf(blob, r, jb, live ? (uint8_t)term_scale_byte(e0, term) : (uint8_t)127);
+    for (int term = 0; term < kTerms; ++term) {
+        put_codes<16>(bq, t, kb, nkb2, kTerms * i + term, jb, 0, codes[term]);
+        put_scale(bq, t, kb, nkb2, kTerms * i + term, jb, sbyte[term]);
     }
 }
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
 
 // GPT-OSS clamped SwiGLU (primitives.go:144-146; NaN propagates) with the fast
-// exponential and division: the result is rounded to 16 significant bits (four
-// E4M3 terms) right after, far coarser than their error.
+// exponential and division: the result is carried by five E2M1 terms right
+// after (about 2^-12 of its block maximum), far coarser than their error.
 __device__ __forceinline__ float swiglu_fast(float gate, float up) {
     const float g = isnan(gate) ? gate : fminf(gate, 7.0f);
     const float u = isnan(up) ? up : fminf(fmaxf(up, -7.0f), 7.0f);
@@ -217,10 +242,10 @@ __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 // 2-D TMA load into this CTA's shared memory, completing on the leader CTA's barrier.
-__device__ __forceinline__ void tma_pair(void *dst, const CUtensorMap *tm, uint32_t bar, int x, int y) {
+__device__ __forceinline__ void tma_pair(uint32_t dst, const CUtensorMap *tm, uint32_t bar, int x, int y) {
     asm volatile(
         "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-        "[%4];" ::"r"(smem_u32(dst)),
+        "[%4];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(bar)
         : "memory");
 }
@@ -231,7 +256,7 @@ __device__ __forceinline__ void umma_pair(uint32_t d, uint64_t a, uint64_t b, ui
                                           uint32_t sfb) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n}" ::"r"(d),
+        " tcgen05.mma.cta_group::2.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n}" ::"r"(d),
         "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
         : "memory");
 }
@@ -242,15 +267,17 @@ __device__ __forceinline__ void commit_pair(uint32_t bar) {
 __device__ __forceinline__ void arrive_remote(uint32_t bar) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
 }
-// Instruction descriptor for the pair: M = 256.
+// Instruction descriptor, kind::mxf4 block-scaled, the pair (M = 256): A and B
+// E2M1, K-major, E8M0 scales; sf_id is the first of the two scale bytes (32-element
+// blocks) the K = 64 MMA uses.
 __device__ __forceinline__ uint32_t idesc_pair(uint32_t sf_id, int n) {
-    return (sf_id << 4) | (5u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) | (1u << 23) | ((256u >> 4) << 24) |
+    return (sf_id << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | (1u << 23) | ((256u >> 4) << 24) |
            (sf_id << 29);
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    bs_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                   const __grid_constant__ CUtensorMap tm_sfa, BsParams p) {
+    bs_gemm_kernel(const __grid_constant__ CUtensorMap tm_a1, const __grid_constant__ CUtensorMap tm_a2,
+                   const __grid_constant__ CUtensorMap tm_b1, const __grid_constant__ CUtensorMap tm_b2, BsParams p) {
     extern __shared__ __align__(1024) uint8_t sm_raw[];
     if (p.gate && *p.gate != p.gate_want) return;  // the other expert path runs this step (both CTAs)
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
@@ -289,29 +316,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_slot;
     const uint32_t lead_full = peer_addr(smem_u32(full), 0);  // full[s] of the leader: + 8 s
 
-    if (warp < kProdWarps) {
-        // ---------------- TMA producers (both CTAs) ----------------
+    if (warp == kProdWarp) {
+        // ---------------- TMA producer (both CTAs; one thread, stages in order) ----------------
         if (lane == 0) {
+            const uint32_t ring_a = smem_u32(ring);
             int i = 0;
             bool ok = true;
             for (int w = cl; w < items && ok; w += ncl) {
                 const int t = w / nmp, mp = w - t * nmp;
                 const int m = 2 * mp + (int)rank;  // m == nmt: no such tile (odd nmt); its rows are not stored
                 const int e = p.tiles[t].x;
-                for (int kb = 0; kb < p.nkb; ++kb, ++i) {
-                    if (i % kProdWarps != warp) continue;
-                    const int s = i % kStages;
+                for (int kb = 0; kb < p.nkb; kb += kBoxes, ++i) {
+                    const int s = i % kStages, nb = min(kBoxes, p.nkb - kb);
                     if (i >= kStages && !mbar_wait(empty + s, ((i / kStages) - 1) & 1, p.err, 40)) {
                         ok = false;
                         break;
                     }
-                    uint8_t *st = ring + (size_t)s * kStageBytes;
-                    if (rank == 0) mbar_expect_tx(full + s, kStageTx);
-                    const int box = (e * p.nmt + m) * p.nkb + kb;  // box-tiled plane: row origin 128 * box
+                    const uint32_t st = ring_a + (uint32_t)s * kStageBytes;
+                    if (rank == 0) mbar_expect_tx(full + s, 2u * (uint32_t)nb * ((uint32_t)kBoxStride + kBPart));
+                    const int box = (e * p.nmt + m) * p.nkb + kb;  // first of the stage's boxes in the plane
+                    const int part = (int)bpart_index(t, kb, (int)rank, (p.nkb + 1) >> 1);
                     const uint32_t bar = lead_full + 8u * (uint32_t)s;
-                    tma_pair(st, &tm_a, bar, 0, box * 128);
-                    tma_pair(st + kABox, &tm_b, bar, 0, (t * p.nkb + kb) * (int)(kBlob / 128) + (int)rank * (int)(kHalf / 128));
-                    tma_pair(st + kABox + kHalf, &tm_sfa, bar, 0, box * 4);
+                    tma_pair(st, nb == 2 ? &tm_a2 : &tm_a1, bar, 0, box * (int)kARows);
+                    tma_pair(st + kStageA, nb == 2 ? &tm_b2 : &tm_b1, bar, 0, part * (int)kBRows);
                 }
             }
         }
@@ -321,9 +348,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (rank == 0) {
             uint32_t elected;
             asm volatile("{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}" : "=r"(elected));
-            uint32_t idesc[4];
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) idesc[kk] = idesc_pair(kk, kN);
+            const uint32_t idesc0 = idesc_pair(0, kN), idesc1 = idesc_pair(2, kN);
             const uint32_t ring_a = smem_u32(ring);
             const uint32_t empty0 = smem_u32(empty), accfull0 = smem_u32(accfull);
             int i = 0, it = 0;
@@ -333,25 +358,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (!mbar_wait(accempty + buf, ((it >> 1) & 1) ^ 1, p.err, 41)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(buf * kN);
-                for (int kb = 0; kb < p.nkb; ++kb, ++i) {
-                    const int s = i % kStages;
-                    // scale-factor slot i % 2 is free once the MMAs of iteration i - 2 completed
-                    if (!mbar_wait(full + s, (i / kStages) & 1, p.err, 42) ||
-                        (i >= 2 && !mbar_wait(empty + (i - 2) % kStages, ((i - 2) / kStages) & 1, p.err, 43))) {
+                for (int kb = 0; kb < p.nkb; kb += kBoxes, ++i) {
+                    const int s = i % kStages, nb = min(kBoxes, p.nkb - kb);
+                    // tcgen05.cp and tcgen05.mma issued by this thread execute in issue order,
+                    // so a scale-factor slot is rewritten only after the MMAs that read it
+                    if (!mbar_wait(full + s, (i / kStages) & 1, p.err, 42)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint32_t st = ring_a + (uint32_t)s * kStageBytes;
-                    const uint32_t sf = tmem + kSfCol + 16u * (uint32_t)(i & 1);
                     if (elected) {
-                        sf_copy_pair(sf, st + kABox + kHalf);      // A scales (each CTA its 128 rows)
-                        sf_copy_pair(sf + 4, st + kABox);          // B scales, rows 0-127 (both CTAs)
-                        sf_copy_pair(sf + 8, st + kABox + 512);    // rows 128-239
-#pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            umma_pair(d, desc_sw128(st + 32 * kk), desc_sw128(st + kABox + kBSf + 32 * kk), idesc[kk],
-                                      (kb | kk) ? 1u : 0u, sf, sf + 4);
+                        for (int b = 0; b < nb; ++b) {
+                            const uint32_t a = st + (uint32_t)b * (uint32_t)kBoxStride, bb = st + kStageA + b * kBPart;
+                            const uint32_t sf = tmem + kSfCol + 16u * (uint32_t)((kb + b) & 1);
+                            sf_copy_pair(sf, a + kABytes);              // A scales (each CTA its 128 rows)
+                            sf_copy_pair(sf + 4, bb + kBHalf);          // B scales, rows 0-127 (both CTAs)
+                            sf_copy_pair(sf + 8, bb + kBHalf + 512);    // rows 128-239
+                            umma_pair(d, desc_sw64(a), desc_sw64(bb), idesc0, (kb + b) ? 1u : 0u, sf, sf + 4);
+                            umma_pair(d, desc_sw64(a + 32), desc_sw64(bb + 32), idesc1, 1u, sf, sf + 4);
+                        }
                         const uint32_t eb = empty0 + 8u * (uint32_t)s;
                         commit_pair(peer_addr(eb, 0));
                         commit_pair(peer_addr(eb, 1));
@@ -367,109 +393,105 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // ---------------- epilogue (warps 7-14 of both CTAs; TMEM lane quadrant = warp % 4) ----------------
+        // ---------------- epilogue (warps 2-13 of both CTAs; TMEM lane quadrant = warp % 4) ----------------
         const int quad = warp & 3;
         const int row = quad * 32 + lane;  // row of this CTA's 128-row weight tile
         const int et = tid - kEpiWarp0 * 32;
-        const int c0 = (et >> 7) * 32;     // this warp's tokens: c0 .. c0 + 31 (the second half has 28)
+        const int c0 = (et >> 7) * kGroupTok;  // this warp's tokens: c0 .. c0 + kGroupTok - 1
         const uint32_t lead_accempty = peer_addr(smem_u32(accempty), 0);
+        // gate_up: rows 16g + j (j < 8) hold the gate of pair 8g + j, row + 8 its up row
+        const int j16 = row & 15;
+        const bool gate_lane = j16 < 8;
+        const int pl = 8 * (row >> 4) + (j16 & 7);  // pair within this tile (0..63)
+        // an item's tile and this thread's bias, loaded one item ahead (global latency
+        // would otherwise sit in every item)
+        auto item_tile = [&](int w) { return w < items ? p.tiles[w / nmp] : make_int4(0, 0, 0, 0); };
+        auto item_bias = [&](int w, const int4 &ti) {
+            if (w >= items) return 0.0f;
+            const int m = 2 * (w % nmp) + (int)rank;
+            if (m >= p.nmt) return 0.0f;
+            if (!p.gate_up) return 128 * m + row < p.R ? __ldg(p.bias + (size_t)ti.x * p.R + 128 * m + row) : 0.0f;
+            return __ldg(p.bias + (size_t)ti.x * p.R + 2 * (64 * m + pl) + (gate_lane ? 0 : 1));
+        };
+        int4 ti_next = item_tile(cl);
+        float bias_next = item_bias(cl, ti_next);
         int it = 0;
         bool ok = true;
         for (int w = cl; w < items; w += ncl, ++it) {
             const int t = w / nmp, mp = w - t * nmp;
             const int m = 2 * mp + (int)rank;
             const bool real = m < p.nmt;  // an odd nmt leaves the last pair's second tile empty
-            const int4 ti = p.tiles[t];
-            const int e = ti.x;
+            const int4 ti = ti_next;
+            const float bias = bias_next;
             const int buf = it & 1;
-            float v[32];
+            float v[kGroupTok];
 #pragma unroll
-            for (int c = 0; c < 32; ++c) v[c] = 0.0f;
+            for (int c = 0; c < kGroupTok; ++c) v[c] = 0.0f;
             if (ok) ok = mbar_wait(accfull + buf, (it >> 1) & 1, p.err, 44);
             if (ok) {
                 tc_fence_after();
-                const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * kN + 4 * c0);
-#pragma unroll
-                for (int g = 0; g < 4; ++g) {  // 8 tokens per load
-                    if (c0 != 0 && g == 3) {
-                        float r16[16];
-                        tmem_ld16(ta + 96u, r16);
-#pragma unroll
-                        for (int u = 0; u < 4; ++u)
-                            v[24 + u] = ((r16[4 * u] + r16[4 * u + 1]) + r16[4 * u + 2]) + r16[4 * u + 3];
-                    } else {
-                        float r32[32];
-                        tmem_ld32(ta + 32u * g, r32);
-#pragma unroll
-                        for (int u = 0; u < 8; ++u)
-                            v[8 * g + u] = ((r32[4 * u] + r32[4 * u + 1]) + r32[4 * u + 2]) + r32[4 * u + 3];
-                    }
-                }
+                const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * kN + kTerms * c0);
+                float a[kGroupTok * kTerms];  // this warp's columns: five terms per token
+                tmem_ld80(ta, a);
                 tc_fence_before();
                 arrive_remote(lead_accempty + 8u * (uint32_t)buf);
+#pragma unroll
+                for (int c = 0; c < kGroupTok; ++c) {
+                    float sum = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < kTerms; ++j) sum += a[kTerms * c + j];
+                    v[c] = sum;
+                }
             }
-            const int nc = min(32, kTok - c0);
+            ti_next = item_tile(w + ncl);
+            bias_next = item_bias(w + ncl, ti_next);
+            const int nc = min(kGroupTok, ti.z - c0);
             if (!p.gate_up) {
                 const int h = 128 * m + row;
                 if (ok && h < p.R) {
-                    const float bias = p.bias[(size_t)e * p.R + h];
 #pragma unroll
-                    for (int c = 0; c < 32; ++c)
-                        if (c < nc && c0 + c < ti.z) ep_out_row(p.y, p.y_rows, p.ret, ti.y + c0 + c, p.R)[h] = v[c] + bias;
+                    for (int c = 0; c < kGroupTok; ++c)
+                        if (c < nc) ep_out_row(p.y, p.y_rows, p.ret, ti.y + c0 + c, p.R)[h] = v[c] + bias;
                 }
                 continue;
             }
-            // gate_up: rows 16g + j (j < 8) hold the gate of pair 8g + j, row + 8 its up row
-            const int j16 = row & 15;
-            const bool gate_lane = j16 < 8;
-            const int pl = 8 * (row >> 4) + (j16 & 7);  // pair within this tile (0..63)
-            const float bias = real ? p.bias[(size_t)e * p.R + 2 * (64 * m + pl) + (gate_lane ? 0 : 1)] : 0.0f;
+            // gate_up: partner lanes (8 apart) swap values; the gate lane finishes the first
+            // half of the tokens, the up lane the second half
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
+            for (int c = 0; c < kGroupTok; ++c) {
                 const float val = v[c] + bias;
-                const float up = __shfl_down_sync(0xffffffffu, val, 8);
-                if (gate_lane && c < nc) act_s[(c0 + c) * kActPitch + pl] = swiglu_fast(val, up);
+                const float other = __shfl_xor_sync(0xffffffffu, val, 8);
+                const bool mine = gate_lane ? c < kGroupTok / 2 : c >= kGroupTok / 2;
+                if (mine)
+                    act_s[(c0 + c) * kActPitch + pl] =
+                        c < nc ? swiglu_fast(gate_lane ? val : other, gate_lane ? other : val) : 0.0f;
             }
             epi_bar();
-            // two threads per (token, 32-pair block), 16 pairs each: block maximum, four
-            // E4M3 terms, their scales, written into down's B blob (pairs 64(m%2).. of box m/2)
+            // four threads per (token, 32-pair block), 8 pairs each: five E2M1 terms and
+            // their scales into down's B operand (pairs 64 (m % 2).. of box m / 2)
             {
-                const bool live = real && et < 4 * kTok;  // the shuffle below runs on every lane
-                const int c = min(et >> 2, kTok - 1), b = (et >> 1) & 1, sub = et & 1;
-                const float4 *src = reinterpret_cast<const float4 *>(act_s + c * kActPitch + 32 * b + 16 * sub);
-                float x[16];
-                float amax = 0.0f;
+                const int unit = et >> 2, sub = et & 3;
+                const int c = unit >> 1, b = unit & 1;
+                const bool live = real;  // every lane takes part in the shuffles inside quantize
+                const float4 *src = reinterpret_cast<const float4 *>(act_s + c * kActPitch + 32 * b + 8 * sub);
+                float x[8];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
+                for (int q = 0; q < 2; ++q) {
                     const float4 f = live ? src[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                     x[4 * q] = f.x;
                     x[4 * q + 1] = f.y;
                     x[4 * q + 2] = f.z;
                     x[4 * q + 3] = f.w;
                 }
+                uint32_t codes[kTerms][1], sbyte[kTerms];
+                fp4::quantize<8, 4>(x, codes, sbyte);
+                const int jb = 2 * (m & 1) + b, onkb2 = (p.onkb + 1) >> 1;
+                if (live) {
 #pragma unroll
-                for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(x[j]));
-                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-                const int e0 = block_exp(amax);
-                const TermScales ts = term_scales(e0);
-                uint32_t wq[4][4];  // [term][4 pairs]
-#pragma unroll
-                for (int g = 0; g < 4; ++g) {
-                    uint32_t lo[4], hi[4];
-                    quant4_pair(x[4 * g], x[4 * g + 1], ts, lo);
-                    quant4_pair(x[4 * g + 2], x[4 * g + 3], ts, hi);
-#pragma unroll
-                    for (int term = 0; term < 4; ++term) wq[term][g] = (lo[term] & 0xffffu) | (hi[term] << 16);
-                }
-                uint8_t *blob = p.oq + ((size_t)t * p.onkb + (m >> 1)) * kBlob;
-                const int chunk = 4 * (m & 1) + 2 * b + sub, jb = 2 * (m & 1) + b;
-#pragma unroll
-                for (int term = 0; term < 4; ++term) {
-                    const int r = 4 * c + term;
-                    if (live)
-                        *reinterpret_cast<uint4 *>(blob + swz(r, chunk)) =
-                            make_uint4(wq[term][0], wq[term][1], wq[term][2], wq[term][3]);
-                    if (live && sub == 0) put_sf(blob, r, jb, (uint8_t)term_scale_byte(e0, term));
+                    for (int term = 0; term < kTerms; ++term) {
+                        put_codes<4>(p.oq, t, m >> 1, onkb2, kTerms * c + term, jb, sub, codes[term]);
+                        if (term % 4 == sub) put_scale(p.oq, t, m >> 1, onkb2, kTerms * c + term, jb, sbyte[term]);
+                    }
                 }
             }
             epi_bar();  // act_s is rewritten by the next item
@@ -494,11 +516,14 @@ namespace {
 struct BsScratch {
     int4 *tiles;
     int32_t *ntiles;
-    uint8_t *xq, *aq;  // B blobs of gate_up (quantized tokens) and down (quantized activations)
+    uint8_t *xq;  // gate_up's B operand (the quantized tokens)
+    uint8_t *aq;  // down's B operand (the quantized activations)
     int max_tiles;
 };
 
 inline size_t up1k(size_t v) { return (v + 1023) & ~size_t(1023); }
+// B operand bytes of `tiles` tiles of nkb K boxes (boxes rounded up to pairs, two parts each).
+inline size_t b_bytes(size_t tiles, size_t nkb) { return tiles * ((nkb + 1) / 2) * 2 * kBoxes * kBPart; }
 
 BsScratch carve_bs(void *base, int rows_cap, int E, int H, int I) {
     BsScratch s{};
@@ -506,13 +531,15 @@ BsScratch carve_bs(void *base, int rows_cap, int E, int H, int I) {
     const size_t nkb_gu = kpad128(H) / 128, nkb_dn = kpad128(I) / 128;
     uint8_t *p = static_cast<uint8_t *>(base);
     size_t off = 0;
-    s.tiles = reinterpret_cast<int4 *>(p + off);
-    off = up1k(off + (size_t)s.max_tiles * sizeof(int4));
-    s.ntiles = reinterpret_cast<int32_t *>(p + off);
-    off = up1k(off + 16);
-    s.xq = p + off;
-    off = up1k(off + (size_t)s.max_tiles * nkb_gu * kBlob);
-    s.aq = p + off;
+    auto take = [&](size_t bytes) {
+        uint8_t *at = p + off;
+        off = up1k(off + bytes);
+        return at;
+    };
+    s.tiles = reinterpret_cast<int4 *>(take((size_t)s.max_tiles * sizeof(int4)));
+    s.ntiles = reinterpret_cast<int32_t *>(take(16));
+    s.xq = take(b_bytes(s.max_tiles, nkb_gu));
+    s.aq = take(b_bytes(s.max_tiles, nkb_dn));
     return s;
 }
 
@@ -534,29 +561,30 @@ bool tc_supported() {
 size_t bs_scratch_bytes(int rows_cap, int E, int H, int I) {
     const size_t max_tiles = (size_t)(rows_cap + kTok - 1) / kTok + E;
     const size_t nkb_gu = kpad128(H) / 128, nkb_dn = kpad128(I) / 128;
-    return up1k(max_tiles * sizeof(int4)) + 1024 + up1k(max_tiles * nkb_gu * kBlob) + up1k(max_tiles * nkb_dn * kBlob);
+    return up1k(max_tiles * sizeof(int4)) + 1024 + up1k(b_bytes(max_tiles, nkb_gu)) + up1k(b_bytes(max_tiles, nkb_dn));
 }
 
 cudaError_t init_bs_scratch(void *scratch, int rows_cap, int E, int H, int I) {
-    // down's B operand: bytes no gate_up tile writes (K padding past I) must read as
-    // zero terms with a unit scale
+    // down's B operand: rows no gate_up tile writes (K padding past I) must read as
+    // zero codes with a unit scale
     const BsScratch s = carve_bs(scratch, rows_cap, E, H, I);
-    const size_t nkb_dn = kpad128(I) / 128;
-    const size_t blobs = (size_t)s.max_tiles * nkb_dn;
-    cudaError_t e = cudaMemset(s.aq, 0, blobs * kBlob);
-    if (e == cudaSuccess) e = cudaMemset2D(s.aq, kHalf, 127, kBSf, 2 * blobs);  // both halves' scale chunks
+    const size_t parts = b_bytes(s.max_tiles, kpad128(I) / 128) / kBPart;
+    cudaError_t e = cudaMemset(s.aq, 0, parts * kBPart);
+    if (e == cudaSuccess) e = cudaMemset2D(s.aq + kBHalf, kBPart, 127, kBSf, parts);
     return e;
 }
 
 namespace {
 
-// Rows of 128 bytes, boxes of `box_rows` rows, no swizzle (the data is stored pre-swizzled).
-cudaError_t map_rows(CUtensorMap *tm, const void *base, uint64_t rows, uint32_t box_rows) {
-    cuuint64_t dims[2] = {128, rows};
-    cuuint64_t strides[1] = {128};
-    cuuint32_t box[2] = {128, box_rows};
+// A byte array seen as rows of `row_bytes` (a multiple of 8) moved by TMA as
+// 8-byte elements, `box_rows` rows per copy, no swizzle: the bytes land in
+// shared memory exactly as stored.
+cudaError_t map_rows(CUtensorMap *tm, const void *base, size_t bytes, uint32_t row_bytes, uint32_t box_rows) {
+    cuuint64_t dims[2] = {row_bytes / 8, bytes / row_bytes};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {row_bytes / 8, box_rows};
     cuuint32_t es[2] = {1, 1};
-    CUresult r = encode_fn()(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, es,
+    CUresult r = encode_fn()(tm, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(base), dims, strides, box, es,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
@@ -613,20 +641,24 @@ cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *o
     *launches = 0;
     // 1. token tiles, then the gate_up B operand
     bs_plan_kernel<<<1, 256, 0, st>>>(offsets, d.E, s.tiles, s.ntiles, s.max_tiles, err);
-    bs_quant_kernel<<<s.max_tiles * nkb_gu, 256, 0, st>>>(x_hi, x_lo, perm, d.k, d.H, nkb_gu, s.tiles, s.ntiles,
-                                                         s.xq);
+    bs_quant_kernel<<<s.max_tiles * nkb_gu, kTok * 4, 0, st>>>(x_hi, x_lo, perm, d.k, d.H, nkb_gu, s.tiles, s.ntiles,
+                                                               s.xq);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     *launches += 2;
     if (hook) hook(hook_arg, 5);
     // 2. gate_up + SwiGLU, writing down's B operand
-    CUtensorMap tm_gu, tm_dn, tm_xq, tm_aq, tm_gsf, tm_dsf;
-    e = map_boxes(&tm_gu, L.gu_tq, tq_bytes(d.E, 2 * d.I, d.H) / 64);
-    if (e == cudaSuccess) e = map_boxes(&tm_dn, L.dn_tq, tq_bytes(d.E, d.H, d.I) / 64);
-    if (e == cudaSuccess) e = map_rows(&tm_xq, s.xq, (uint64_t)s.max_tiles * nkb_gu * (kBlob / 128), kHalf / 128);
-    if (e == cudaSuccess) e = map_rows(&tm_aq, s.aq, (uint64_t)s.max_tiles * nkb_dn * (kBlob / 128), kHalf / 128);
-    if (e == cudaSuccess) e = map_rows(&tm_gsf, L.gu_tsf, tsf_bytes(d.E, 2 * d.I, d.H) / 128, 4);
-    if (e == cudaSuccess) e = map_rows(&tm_dsf, L.dn_tsf, tsf_bytes(d.E, d.H, d.I) / 128, 4);
+    CUtensorMap tm_gu1, tm_gu2, tm_dn1, tm_dn2, tm_xq1, tm_xq2, tm_aq1, tm_aq2;
+    const size_t gu_bytes = box_plane_bytes(d.E, 2 * d.I, d.H), dn_bytes = box_plane_bytes(d.E, d.H, d.I);
+    const size_t xq_bytes = b_bytes(s.max_tiles, nkb_gu), aq_bytes = b_bytes(s.max_tiles, nkb_dn);
+    e = map_rows(&tm_gu1, L.gu_tq, gu_bytes, kCopyRow, kARows);
+    if (e == cudaSuccess) e = map_rows(&tm_gu2, L.gu_tq, gu_bytes, kCopyRow, 2 * kARows);
+    if (e == cudaSuccess) e = map_rows(&tm_dn1, L.dn_tq, dn_bytes, kCopyRow, kARows);
+    if (e == cudaSuccess) e = map_rows(&tm_dn2, L.dn_tq, dn_bytes, kCopyRow, 2 * kARows);
+    if (e == cudaSuccess) e = map_rows(&tm_xq1, s.xq, xq_bytes, kCopyRow, kBRows);
+    if (e == cudaSuccess) e = map_rows(&tm_xq2, s.xq, xq_bytes, kCopyRow, 2 * kBRows);
+    if (e == cudaSuccess) e = map_rows(&tm_aq1, s.aq, aq_bytes, kCopyRow, kBRows);
+    if (e == cudaSuccess) e = map_rows(&tm_aq2, s.aq, aq_bytes, kCopyRow, 2 * kBRows);
     if (e != cudaSuccess) return e;
     BsParams p{};
     p.tiles = s.tiles;
@@ -641,7 +673,7 @@ cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *o
     p.gate_up = 1;
     p.oq = s.aq;
     p.onkb = nkb_dn;
-    bs_gemm_kernel<<<grid, kThreads, kSmem, st>>>(tm_gu, tm_xq, tm_gsf, p);
+    bs_gemm_kernel<<<grid, kThreads, kSmem, st>>>(tm_gu1, tm_gu2, tm_xq1, tm_xq2, p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     ++*launches;
@@ -656,7 +688,7 @@ cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *o
     p.y = y;
     p.y_rows = y_rows;
     if (ret) p.ret = *ret;
-    bs_gemm_kernel<<<grid, kThreads, kSmem, st>>>(tm_dn, tm_aq, tm_dsf, p);
+    bs_gemm_kernel<<<grid, kThreads, kSmem, st>>>(tm_dn1, tm_dn2, tm_aq1, tm_aq2, p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     ++*launches;

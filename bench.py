@@ -65,7 +65,7 @@ FLOP_PER_PAIR = 2 * 2880 * (2 * 2880 + 2880)  # 49,766,400
 MEASURED_PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_FILE = os.path.join(ROOT, "profiles", "ncu_traffic.json")
 # arithmetic of each expert path (weights stay MXFP4; accumulation f32; router and softmax f64)
-DTYPE_TENSOR = "mxfp4 x e4m3 (4 terms per value) -> f32"
+DTYPE_TENSOR = "mxfp4 x e2m1 (5 block-scaled terms per value) -> f32"
 DTYPE_DECODE = "mxfp4 x fp16 (hi + lo) -> f32"
 DTYPE_GEMV = "mxfp4 x fp16 (hi + lo) -> f32"
 FLUSH_BYTES = 256 << 20  # > 126 MB L2
@@ -410,7 +410,7 @@ def kernel_name(stage: str, path: int) -> str:
         return ("decode_kernel (one cooperative launch: routing + gate_up + down + combine; packed MXFP4 boxes "
                 "expanded in registers, mma.sync with fp16 hi/lo activation columns)")
     return {1: "gemv_kernel (mma.sync MXFP4)",
-            2: "bs_gemm_kernel (tcgen05 kind::mxf8f6f4 block-scaled: E2M1 weights x 4-term E4M3 activations)"}[path or 1]
+            2: "bs_gemm_kernel (tcgen05 kind::mxf4 block-scaled, CTA pairs: E2M1 weights x 5-term E2M1 activations)"}[path or 1]
 
 
 def roofline(stage: str, flops: float, bytes_: float, launch_ms: float, tensor: bool, clk, timed_ms: float,
