@@ -298,6 +298,17 @@ struct GgufLayer {
 // 0, or -1 with a message in *err.
 int gguf_layer(const ::amoe_gguf *g, int layer, int H, int I, int E, GgufLayer *L, std::string *err);
 
+// The head's tensors: output_norm.weight widened to f32, and the lm head's bytes as
+// stored (output.weight, or token_embd.weight when the file ties them), F32/F16/BF16.
+struct GgufHead {
+    const float *norm = nullptr;
+    const void *lm_head = nullptr;
+    int type = 0;
+    std::vector<float> buf;
+    std::vector<uint8_t> head_buf;
+};
+int gguf_head(const ::amoe_gguf *g, int H, int V, GgufHead *h, std::string *err);
+
 // Sets the message amoe_last_error(NULL) returns on the calling thread.
 void set_thread_error(const std::string &msg);
 

@@ -859,14 +859,18 @@ int check_forward_args(amoe_ctx *c, int32_t layer, const float *residual, int32_
 }
 
 // Token slices of a host-buffer call: one pass unless the call is large enough
-// that overlapping its host copies with compute pays (>= 2048 tokens), and only
+// that overlapping its host copies with compute pays (>= 2048 tokens and two
+// passes of the size below), and only
 // when every slice takes the same expert path as the whole call (so the output
 // is bit-identical to one pass: tokens are independent).  Expert-parallel calls
 // stay whole: every rank must make the same sequence of exchanges.
 std::vector<int> plan_passes(const amoe_ctx *c, int T) {
     std::vector<int> one{T};
     if (T < 2048 || c->ep_n > 1) return one;
-    const int target = std::max(1024, (T + kMaxIoChunks - 1) / kMaxIoChunks);
+    // a pass keeps at least 64 pairs per expert on average, so that the tensor-core GEMM's
+    // 48-token tiles stay mostly full (128 experts: 2048-token passes)
+    const int per_expert = (int)std::min<long long>(1 << 20, (64LL * c->d.E + c->d.k - 1) / c->d.k);
+    const int target = std::max({1024, per_expert, (T + kMaxIoChunks - 1) / kMaxIoChunks});
     const int n = (T + target - 1) / target;
     int len = (T + n - 1) / n;
     len = (len + kRouteTokens - 1) / kRouteTokens * kRouteTokens;  // slices start on routing-chunk bounds

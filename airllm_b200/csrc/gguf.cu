@@ -432,6 +432,34 @@ const float *f32_view(const amoe_gguf *g, const amoe_gguf::Tensor *t, std::vecto
 
 namespace amoe {
 
+// The head (loadResidentWeights, internal/model/gptoss/weights.go:19-33): output_norm.weight [H],
+// and output.weight [H, V], or token_embd.weight [H, V] when the file has no output.weight (the
+// reference then reuses the embeddings as the lm head).  The lm head stays in its GGUF encoding
+// (F32, F16 or BF16; the reference decodes those three, tensor.go:137-144).
+int gguf_head(const amoe_gguf *g, int H, int V, GgufHead *out, std::string *err) {
+    const uint64_t h = H, v = V;
+    const amoe_gguf::Tensor *n = shaped(g, "output_norm.weight", {h}, err);
+    if (!n || !(out->norm = f32_view(g, n, out->buf, err, "output_norm.weight"))) return -1;
+    const char *name = find(g, "output.weight") ? "output.weight" : "token_embd.weight";
+    const amoe_gguf::Tensor *w = shaped(g, name, {h, v}, err);
+    if (!w) return -1;
+    if (w->type != AMOE_GGUF_F32 && w->type != AMOE_GGUF_F16 && w->type != AMOE_GGUF_BF16) {
+        *err = std::string("gptoss: tensor \"") + name + "\" type " + std::to_string(w->type) +
+               ": the lm head takes f32, f16 or bf16";
+        return -1;
+    }
+    out->type = (int)w->type;
+    const uint8_t *p = g->base + w->offset;
+    const size_t align = w->type == AMOE_GGUF_F32 ? 4 : 2;
+    if (reinterpret_cast<uintptr_t>(p) % align == 0) {
+        out->lm_head = p;
+    } else {
+        out->head_buf.assign(p, p + w->bytes);
+        out->lm_head = out->head_buf.data();
+    }
+    return 0;
+}
+
 // Layer `layer`'s MoE tensors (loadDecoderLayer, internal/model/gptoss/weights.go:35-124, its MoE
 // part): the post-attention norm (ffn_norm or post_attention_norm), the router, and the experts
 // either fused (ffn_gate_up_exps, rows interleaving gate and up) or split (ffn_gate_exps +

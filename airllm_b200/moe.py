@@ -91,6 +91,13 @@ SIGNATURES = {
     "amoe_gguf_tensor": (ctypes.c_int, [_vp, ctypes.c_char_p, _vp, _vp, _vp, _vp, _vp]),
     "amoe_gguf_moe_config": (ctypes.c_int, [_vp, ctypes.POINTER(AmoeConfig)]),
     "amoe_upload_layer_gguf": (ctypes.c_int, [_vp, _vp, _i32]),
+    "amoe_head_create": (ctypes.c_int, [_i32, _i32, ctypes.c_float, _i32, ctypes.POINTER(_vp)]),
+    "amoe_head_destroy": (None, [_vp]),
+    "amoe_head_last_error": (ctypes.c_char_p, [_vp]),
+    "amoe_head_upload": (ctypes.c_int, [_vp, _vp, _vp, _i32]),
+    "amoe_head_upload_gguf": (ctypes.c_int, [_vp, _vp]),
+    "amoe_head_next_token": (ctypes.c_int, [_vp, _vp, _i32, _vp, _vp]),
+    "amoe_head_next_token_device": (ctypes.c_int, [_vp, _vp, _i32, _vp, _vp, _vp]),
 }
 
 GGUF_F32, GGUF_F16, GGUF_BF16, GGUF_MXFP4 = 0, 1, 30, 39
@@ -348,3 +355,69 @@ class MoEBlock:
         self._check(self._lib.amoe_last_routing(self._h, logits.ctypes.data, perm.ctypes.data,
                                                 counts.ctypes.data, offsets.ctypes.data))
         return logits, perm, counts, offsets
+
+
+class Head:
+    """The model head (amoe_head): final RMSNorm, lm_head and greedy token choice,
+    as Runtime.nextToken does it (internal/model/gptoss/runtime.go:234-250)."""
+
+    MAX_TOKENS = 16
+
+    def __init__(self, hidden: int, vocab: int, eps: float = 1e-5, device: int = 0):
+        self._lib = load_library()
+        self.hidden, self.vocab = hidden, vocab
+        h = _vp()
+        rc = self._lib.amoe_head_create(hidden, vocab, eps, device, ctypes.byref(h))
+        if rc != AMOE_OK:
+            raise AmoeError(rc, self._lib.amoe_head_last_error(None).decode())
+        self._h = h
+
+    def _check(self, rc: int):
+        if rc != AMOE_OK:
+            raise AmoeError(rc, self._lib.amoe_head_last_error(self._h).decode())
+
+    def upload(self, final_norm, lm_head, gguf_type: int = GGUF_F32):
+        """final_norm [H] f32; lm_head [V, H] as f32 (GGUF_F32), or its raw 16-bit words
+        (uint16/float16 array) for GGUF_F16 / GGUF_BF16."""
+        g = _c(final_norm, np.float32)
+        if g.size != self.hidden:
+            raise AmoeError(AMOE_ERR_INVALID, f"final norm length {g.size}, want {self.hidden}")
+        w = np.ascontiguousarray(lm_head)
+        want = 4 if gguf_type == GGUF_F32 else 2
+        if w.size != self.vocab * self.hidden or w.itemsize != want:
+            raise AmoeError(AMOE_ERR_INVALID, "lm head must hold vocab x hidden elements of its encoding")
+        self._check(self._lib.amoe_head_upload(self._h, g.ctypes.data, w.ctypes.data, gguf_type))
+
+    def upload_gguf(self, gguf: "GGUFFile"):
+        self._check(self._lib.amoe_head_upload_gguf(self._h, gguf.handle))
+
+    def next_token(self, hidden, want_logits: bool = False):
+        """hidden [T, H] host rows -> tokens [T] (and logits [T, V])."""
+        x = _c(hidden, np.float32).reshape(-1, self.hidden)
+        T = x.shape[0]
+        tokens = np.empty(T, np.int32)
+        logits = np.empty((T, self.vocab), np.float32) if want_logits else None
+        self._check(self._lib.amoe_head_next_token(self._h, x.ctypes.data, T, tokens.ctypes.data,
+                                                   logits.ctypes.data if want_logits else None))
+        return (tokens, logits) if want_logits else tokens
+
+    def next_token_device(self, hidden, tokens, logits=None, stream=None):
+        """Device-buffer call on torch tensors; asynchronous."""
+        st = None
+        if stream is not None:
+            st = stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+            if st == 0:
+                st = 1
+        self._check(self._lib.amoe_head_next_token_device(self._h, _ptr(hidden), hidden.shape[0], _ptr(tokens),
+                                                          _ptr(logits), st))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.amoe_head_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

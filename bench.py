@@ -18,8 +18,9 @@ it is the plain single-GPU block.  A "step" is one forward over the 8192 tokens.
             events in a second pass of the same steps; the rank whose gate_up
             takes longest
   sub       N = 1: the 20B-shaped prefill (4096 tokens, Zipf-skewed routing),
-            the 20B decode token and the 24-layer streamed decode stack, each
-            with its own value / e2e / roofline; N = 8: the adversarial
+            the 20B decode token, the model head (final norm, lm_head, greedy
+            token) and the 24-layer streamed decode stack, each with its own
+            value / e2e / roofline; N = 8: the adversarial
             16384-token configuration (8 hot experts on rank 0), per-rank times
 
 --impl reference times the reference's CPU path (the C restatement in oracle/,
@@ -700,6 +701,71 @@ def stream_record(g: Group, steps: int, warmup: int, stream_experts: int = 1) ->
     }
 
 
+# ---- the model head (final RMSNorm + lm_head + greedy token) ----------------------------
+
+HEAD_VOCAB = 201088  # GPT-OSS vocabulary
+
+
+def head_record(g: Group, steps: int, warmup: int) -> dict:
+    """Runtime.nextToken on the device: one decode row through a GPT-OSS-shaped head
+    (hidden 2880, vocabulary 201,088, bf16 lm_head, random N(0, 0.02)); HBM-bound."""
+    torch = g.torch
+    from airllm_b200 import moe
+
+    H, V = 2880, HEAD_VOCAB
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    W = (torch.randn((V, H), device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+    head = moe.Head(H, V, device=g.local)
+    head.upload(np.ones(H, np.float32), W.view(torch.int16).cpu().numpy().view(np.uint16), moe.GGUF_BF16)
+    del W
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    x = torch.randn((1, H), device="cuda", generator=gen)
+    tok = torch.empty(1, dtype=torch.int32, device="cuda")
+    flush = L2Flush(torch)
+    for i in range(warmup):
+        flush(i)
+        head.next_token_device(x, tok, stream=stream)
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    clocks = clock_sampler(g.local)
+    clocks.begin()
+    for i in range(steps):
+        flush(i)
+        starts[i].record(stream)
+        head.next_token_device(x, tok, stream=stream)
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    xh = x.cpu().numpy()
+    e2e = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        head.next_token(xh)
+        e2e.append(time.perf_counter() - t0)
+    head.close()
+    bytes_ = V * H * 2 + H * 4 * 2 + 4
+    pk = peaks()
+    achieved = bytes_ / (ms / 1e3) / 1e9
+    return {
+        "metric": "greedy next tokens/s, GPT-OSS head (final RMSNorm + lm_head 2880 x 201088 bf16 + argmax)",
+        "value": 1e3 / ms, "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "warmup": warmup,
+        "dtype": "bf16 weights, f64 accumulation -> f32 logits",
+        "config": {"workload": "gptoss-head T=1 H=2880 V=201088 bf16", "hidden": H, "vocab": V, "tokens": 1},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                     "kernel": "head_kernel (lm_head GEMV, f64 accumulation, fused argmax)",
+                     "algorithmic_bytes_per_launch": bytes_, "launch_ms": ms,
+                     "peak_source": f"{pk['source']} HBM copy"},
+        "e2e": {"value": 1e3 / (statistics.mean(e2e) * 1e3), "unit": "tokens/s",
+                "ms_per_step": statistics.mean(e2e) * 1e3, "h2d_bytes_per_step": H * 4, "d2h_bytes_per_step": 4,
+                "call": "amoe_head_next_token (host row in, token out)"},
+        "gpu_launches": 2 * steps, "clocks": clk,
+    }
+
+
 # ---- entry points ----------------------------------------------------------------------
 
 def base_line(rec: dict, g: Group, metric: str, config: dict) -> dict:
@@ -722,6 +788,7 @@ def run_default(args) -> int:
         sub["config1_prefill_20b_T4096"] = single_record(g, 1, args.steps or DEFAULT_STEPS[1], args.warmup, args.path)
         sub["config0_decode_20b_T1"] = single_record(g, 0, max(args.steps or DEFAULT_STEPS[0], MIN_STEPS[0]),
                                                      args.warmup, args.path)
+        sub["head_gptoss_T1"] = head_record(g, max(args.steps or 200, 50), args.warmup)
         if not args.no_stream:
             sub["config2_stream_24_layers"] = stream_record(g, max(args.steps or DEFAULT_STEPS[2], MIN_STEPS[2]),
                                                             args.warmup)

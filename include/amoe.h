@@ -268,6 +268,44 @@ AMOE_API int amoe_gguf_moe_config(const amoe_gguf *g, amoe_config *cfg);
  * device without a host-side decode. */
 AMOE_API int amoe_upload_layer_gguf(amoe_ctx *ctx, const amoe_gguf *g, int32_t layer);
 
+/* ---- the model head ----------------------------------------------------------------
+ * Replaces: Runtime.nextToken (internal/model/gptoss/runtime.go:234-250) with the head
+ * weights of loadResidentWeights (weights.go:19-33): RMSNorm of each hidden row with the
+ * final norm gain (output_norm.weight), logits = lm_head . normalized (output.weight,
+ * [V x H] row-major, no bias; the dot products accumulate in float64 and round to f32 once,
+ * as cpuref.Linear does), and the token = the first index of the largest logit (a later
+ * logit must be strictly larger; a NaN never wins; a NaN at index 0 gives token 0).  The
+ * lm head stays on the device in its GGUF encoding (F32, F16 or BF16) and is streamed once
+ * per call for every row of the call.  A head is independent of the MoE contexts (the
+ * reference keeps these weights resident while it streams the layers). */
+typedef struct amoe_head amoe_head;
+
+/* Replaces: the finalNorm / lmHead fields of Runtime (runtime.go:27-28).  hidden >= 1,
+ * vocab >= 1, rms_eps > 0; the head's buffers for up to 16 rows per call. */
+AMOE_API int amoe_head_create(int32_t hidden, int32_t vocab, float rms_eps, int32_t device, amoe_head **out);
+AMOE_API void amoe_head_destroy(amoe_head *h);
+
+/* Description of the last failure on h (h NULL: of the last amoe_head_create on this thread). */
+AMOE_API const char *amoe_head_last_error(const amoe_head *h);
+
+/* Replaces: loadResidentWeights (weights.go:19-33).  final_norm [H] f32; lm_head [V x H] in
+ * the encoding `type` (AMOE_GGUF_F32, AMOE_GGUF_F16 or AMOE_GGUF_BF16), host memory. */
+AMOE_API int amoe_head_upload(amoe_head *h, const float *final_norm, const void *lm_head, int32_t type);
+
+/* The same from an open GGUF file: output_norm.weight and output.weight, or token_embd.weight
+ * when the file has no output.weight (weights.go:27-31), with the reference's GGUF shapes
+ * ([H] and [H, V]). */
+AMOE_API int amoe_head_upload_gguf(amoe_head *h, const amoe_gguf *g);
+
+/* Replaces: Runtime.nextToken (runtime.go:234-250) for T rows at once (1 <= T <= 16):
+ * hidden [T x H] f32 host rows (the last layer's outputs), tokens [T] receives each row's
+ * token, logits [T x V] (nullable) the logits.  Synchronous. */
+AMOE_API int amoe_head_next_token(amoe_head *h, const float *hidden, int32_t T, int32_t *tokens, float *logits);
+
+/* The same on device buffers, enqueued on `stream` (NULL = the head's own stream). */
+AMOE_API int amoe_head_next_token_device(amoe_head *h, const float *hidden, int32_t T, int32_t *tokens,
+                                         float *logits, void *stream);
+
 /* ABI version (AMOE_ABI_VERSION). */
 AMOE_API int amoe_abi_version(void);
 

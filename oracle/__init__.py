@@ -14,6 +14,8 @@ Reference functions restated (paths relative to the reference project root):
                      expert-major with the same arithmetic: moe_block_grouped)
   FP4 activation terms  no reference counterpart: the bit-exact E2M1-term operand of a
                      block-scaled FP4 GEMM (oracle_e2m1_terms in moe_oracle.c)
+  Runtime.nextToken  internal/model/gptoss/runtime.go:234-250 (final RMSNorm,
+                     lm_head Linear, first-max argmax)
   RoPE / YaRNRoPE    internal/backend/cpuref/rope.go:10-86           (attn_oracle.c)
   KVCache            internal/backend/cpuref/attention.go:8-59       (KVCache below)
   CausalAttention    internal/backend/cpuref/attention.go:61-171     (attn_oracle.c)
@@ -113,6 +115,8 @@ def lib():
                                              _f32p, ctypes.c_int]
             L.oracle_permute.argtypes = [_i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                          _i32p, _i32p, _i32p, _i32p]
+            L.oracle_next_token.argtypes = [_f32p, ctypes.c_int, _f32p, ctypes.c_float, _f32p, ctypes.c_int, _f32p,
+                                            _i32p]
             L.oracle_e2m1_terms.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int, _u8p, _u8p]
             L.oracle_rope.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_double,
                                       ctypes.c_int, _f32p]
@@ -301,6 +305,23 @@ def permute(topk_idx, experts):
     _check(lib().oracle_permute(_p(idx, _i32p), T, k, experts, _p(perm, _i32p), _p(counts, _i32p),
                                 _p(offsets, _i32p), _p(inv, _i32p)), "permute")
     return perm, counts, offsets, inv
+
+
+# ---- the model head -------------------------------------------------------------------
+
+def next_token(hidden, gain, eps, lm_head):
+    """Runtime.nextToken (runtime.go:234-250) on one hidden row: (token, logits).
+    lm_head [V, H] float32 (decoded from the GGUF encoding first, as the reference does)."""
+    hidden, gain = _c(hidden, np.float32).ravel(), _c(gain, np.float32).ravel()
+    W = _c(lm_head, np.float32)
+    V, H = W.shape
+    if hidden.size != H or gain.size != H:
+        raise OracleError("head lengths do not match")
+    logits = np.empty(V, np.float32)
+    tok = np.zeros(1, np.int32)
+    _check(lib().oracle_next_token(_p(hidden, _f32p), H, _p(gain, _f32p), eps, _p(W, _f32p), V, _p(logits, _f32p),
+                                   _p(tok, _i32p)), "next_token")
+    return int(tok[0]), logits
 
 
 # ---- block-scaled FP4 activation terms ------------------------------------------------

@@ -672,3 +672,28 @@ int oracle_moe_block_grouped(const oracle_layer *L, const float *residual, int T
     free(xn); free(idx); free(w); free(lg); free(order); free(tok_of); free(start); free(act); free(y);
     return status;
 }
+
+/* ---- the model head: Runtime.nextToken, internal/model/gptoss/runtime.go:234-250 ---- */
+
+int oracle_next_token(const float *hidden, int H, const float *gain, float eps, const float *lm_head, int V,
+                      float *logits, int32_t *token) {
+    if (!hidden || !gain || !lm_head || !token || H <= 0 || V <= 0) return -1;
+    float *normalized = (float *)malloc(sizeof(float) * (size_t)H);
+    float *lg = logits ? logits : (float *)malloc(sizeof(float) * (size_t)V);
+    if (!normalized || !lg) {
+        free(normalized);
+        if (!logits) free(lg);
+        return -1;
+    }
+    int rc = oracle_rmsnorm(hidden, gain, H, eps, normalized); /* runtime.go:235 */
+    if (rc == 0) rc = oracle_linear_bias(normalized, lm_head, NULL, H, V, lg); /* runtime.go:239, no bias */
+    if (rc == 0) {
+        int best = 0; /* runtime.go:243-248: strict >, so the first of equal maxima wins */
+        for (int i = 1; i < V; ++i)
+            if (lg[i] > lg[best]) best = i;
+        *token = best;
+    }
+    free(normalized);
+    if (!logits) free(lg);
+    return rc;
+}

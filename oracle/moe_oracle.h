@@ -92,6 +92,14 @@ int oracle_moe_block_grouped(const oracle_layer *L, const float *residual, int T
                              int32_t *topk_idx, float *topk_w, float *logits,
                              const int32_t *tokens, int n_tokens, int threads);
 
+/* Runtime.nextToken (internal/model/gptoss/runtime.go:234-250): RMSNorm of one
+ * hidden row with the final norm gain, logits = Linear(normalized, lm_head) with
+ * lm_head [V x H] row-major and no bias, token = the first index of the largest
+ * logit (a later logit must be strictly larger to win; a NaN never wins, and a
+ * NaN at index 0 is never replaced).  logits [V] nullable. */
+int oracle_next_token(const float *hidden, int H, const float *gain, float eps, const float *lm_head, int V,
+                      float *logits, int32_t *token);
+
 /* forwardExpert (layer.go:126-188) of expert e on n normalized rows x [n x H]:
  * y [n x H] = down(SwiGLU(gate_up(x))) with biases. */
 int oracle_expert_rows(const oracle_layer *L, int expert, const float *x, int n, float *y, int threads);
