@@ -767,7 +767,9 @@ int forward_impl(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, f
     const int nchunk = (T + kRouteTokens - 1) / kRouteTokens;
     bool tc = use_tensor_path(c, T);
     // decode: routing, gate_up, down and the combine in one cooperative launch
-    const bool fused_decode = c->ep_n == 1 && !tc && decode_supported(d, T, c->cfg.device);
+    // (the fused kernel reads the residual rows as float4)
+    const bool fused_decode = c->ep_n == 1 && !tc && decode_supported(d, T, c->cfg.device) &&
+                              reinterpret_cast<uintptr_t>(residual) % 16 == 0;
     if (!c->blk.frag && !fused_decode) tc = true;  // streamed layers carry no GEMV tiles
     if (!fused_decode) {
         AMOE_CUDA(c, launch_route_impl(d, L, residual, T, r, c->partial, c->arrivals, st, &timer_hook, &timer));

@@ -8,8 +8,8 @@
 //
 // A decode step is a batched matrix-vector product over the selected experts'
 // MXFP4 weights (53 MB per token for the 20B shape): the bound is HBM, and the
-// design goal is to keep every SM streaming weight boxes from the first moment
-// the routing is known to the end.
+// design goal is to keep every SM streaming weight boxes from the moment the
+// routing is known to the end, with next to no instructions per weight.
 //
 // Work.  A unit is one 128-row weight tile of one selected expert over its K
 // range: every gate_up tile over all of K (SwiGLU needs the whole sum), every
@@ -19,41 +19,46 @@
 // slot order.  No unit is shared between CTAs, so no tile needs a cross-CTA
 // reduction.  Two hand-offs cross CTAs, both through L2:
 //   - the last gate_up unit of a slot to finish publishes the slot's
-//     activation (a per-slot flag carrying the launch epoch); a down unit
-//     waits for it before it builds its operand (its weights are already
-//     streaming into the ring meanwhile);
+//     activation (a per-slot flag carrying the launch epoch); a down unit's
+//     activation operand is copied in once the flag is up (its weights are
+//     already streaming into the ring meanwhile);
 //   - the last down unit of a 128-row output tile to finish combines that
 //     tile for every token (self-resetting arrival counters).
 //
-// Weights.  The units' boxes stream from the TMA box planes (128 rows x 64 B of
-// GGUF nibble bytes per 128-element K box, 8 KB, plus the box's 512-byte E8M0
-// chunk) into a ring of 17 KB stages, two boxes per stage, one bulk copy per
-// stage (a box's rows and its scale chunk are stored together); the planes hold
-// every row in the 64-byte swizzle order, so the fragment loads below are free
-// of bank conflicts.  There is no producer
-// warp: one thread fills the first stages, and afterwards the last warp to
-// finish with a stage refills its slot with the stage a ring further on (all 16
-// warps then fit four per SM sub-partition with 128 registers each).  The
-// boxes stay packed in shared memory: 16 warps (two groups of 8
-// that take alternate stages) expand them in registers with
-// cvt.rn.f16x2.e2m1x2 (E2M1 is exact in fp16) and multiply on mma.sync
-// m16n8k16, 16 weight rows per warp.  The activations are the n = 8 columns:
-// each token as an fp16 hi + lo pair (x ~= hi + lo to ~2^-22), so one MMA
-// covers up to four tokens.  Byte i of a 32-element block holds elements 2i
-// and 2i+1 (tensor.go:156-158), so lane (g, c)'s four bytes of a block are
-// elements 8c..8c+7: one 32-bit load per row and one 16-byte load of the
-// activation column give both k-steps of the block.  Each block's two MMAs
-// go to a fresh f32 accumulator that is then scaled by the row's E8M0 block
-// scale, so the scale never has to fit fp16's range.
+// Tensor cores.  The weights never leave their packed form: each unit's boxes
+// (128 rows x 64 B of E2M1 codes per 128-element K box, plus the box's 512-byte
+// E8M0 chunk, stored together in the 64-byte swizzle order) stream by bulk copy
+// into a ring of 17 KB stages, two boxes per stage, and go straight into
+// tcgen05.mma kind::mxf4 (M = 128, K = 64, two per box) with the E8M0 chunk as
+// the hardware block scales.  The tokens are the N columns, each as five
+// block-scaled E2M1 terms (fp4_terms.cuh): N = 8, 16 or 32 for 1, 2-3 or 4
+// tokens.  gate_up's operand (the normalized tokens) is quantized once per CTA
+// into shared memory; gate_up's epilogue writes down's operand, the SwiGLU
+// outputs' terms, to global memory in the same box form, and a down unit copies
+// its K half of it in one bulk copy.
 //
-// Every wait is bounded (~1 s of clock): it records a code (50-54) in the error flag,
-// marks the CTA dead (later waits return at once, no further stage is issued,
-// the copies in flight are waited for) and the kernel winds down.
+// Roles after the routing: warp 0 lane 0 streams the ring (waiting for the
+// MMAs to release a stage), warp 1 issues the MMAs into two TMEM accumulators
+// (the epilogue of one unit overlaps the next unit's MMAs), warp 2 lane 0
+// copies the down units' operands as their flags come up, warps 4-15 first
+// quantize gate_up's operand (while the first stages are in flight) and warps
+// 4-7 (one per TMEM lane quadrant) then run the unit epilogues.
+//
+// The routing is a chain of short dependent steps, so it is written for
+// latency: every global load in flight at once, warp-uniform control flow around
+// every shuffle (a warp split by a lane-0-only branch pays for each full-mask
+// shuffle), one warp per token for the top-k and one warp for the permutation.
+//
+// Every wait is bounded (~1 s of clock): it records a code (50-59) in the error
+// flag, marks the CTA dead (later waits return at once, no further copy is
+// issued, the copies and MMAs in flight are waited for) and the kernel winds
+// down through the same barriers.
 #include <algorithm>
 #include <cstring>
 #include <vector>
 
 #include "../../include/amoe.h"
+#include "fp4_terms.cuh"
 #include "tc_ptx.cuh"
 
 namespace amoe {
@@ -62,22 +67,32 @@ namespace {
 
 using namespace bs;
 
-constexpr int kGroups = 2;                      // consumer groups, alternate stages
-constexpr int kGroupWarps = 8;                  // 8 warps x 16 rows = one 128-row tile
-constexpr int kComputeWarps = kGroups * kGroupWarps;
-constexpr int kComputeThreads = kComputeWarps * 32;
-constexpr int kDecThreads = kComputeWarps * 32;  // no producer warp: the last releaser of a stage refills it
+constexpr int kDecThreads = 512;                // 16 warps: the routing spreads H over all of them
+constexpr int kProdWarp = 0, kMmaWarp = 1, kLoadWarp = 2, kEpiWarp0 = 4;
+constexpr int kEpiThreads = 128;                // warps 4-7, one per TMEM lane quadrant
+constexpr int kBuildThreads = kDecThreads - kEpiWarp0 * 32;  // warps 4-15 quantize gate_up's operand
+constexpr int kTerms = fp4::kTerms;
 constexpr uint32_t kBoxBytes = 128 * 64;        // one packed box: 128 rows x 128 E2M1 values
 constexpr uint32_t kBoxStep = (uint32_t)kBoxStride;  // a box's rows and its scale chunk, as stored
 constexpr uint32_t kStageBytes = 2 * kBoxStep;       // two boxes, each followed by its scale chunk
+constexpr uint32_t kSfChunk = 512;              // E8M0 chunk of 128 rows x 4 blocks
 constexpr int kMaxStages = 12;
+constexpr int kMinStages = 4;
 constexpr int kMaxUnits = 64;                   // units per CTA
 constexpr int kSchedWords = 1024;               // one CTA's schedule rows (int32)
 static_assert(kSchedWords == AMOE_DECODE_SCHED_WORDS, "the table row size is part of the C ABI");
 constexpr int kMaxCtaStages = kMaxUnits * 16;   // ring stages of one CTA (a unit has <= 16: K <= 4096)
 constexpr size_t kSmemBudget = 232448;          // dynamic shared memory per block (227 KB)
+constexpr uint32_t kTmemCols = 128;             // accumulators at columns 0 and 32, scale slots at 64 and 80
+constexpr uint32_t kAccCols = 32;
+constexpr uint32_t kSfCol = 64;
 
-static_assert(kStageBytes % 1024 == 0, "stages keep the 1 KB alignment SWIZZLE_64B needs");
+static_assert(kStageBytes % 1024 == 0 && kBoxStep % 512 == 0, "64-byte swizzle atoms start on 512 B");
+static_assert((size_t)kMinStages * kStageBytes >= 4 * kSchedWords, "the routing stages the schedule rows in the ring");
+
+// An activation operand box: N rows x 64 B of codes (swizzled like the weights),
+// then the N rows' E8M0 bytes in a 512-byte chunk (byte 16 n + j: row n, block j).
+__host__ __device__ constexpr uint32_t bbox_bytes(int ncol) { return (uint32_t)ncol * 64u + kSfChunk; }
 
 // Unit encoding in the schedule table.
 __host__ __device__ constexpr int32_t unit_code(int phase, int slot, int mt, int kpart) {
@@ -90,10 +105,11 @@ struct DecodeParams {
     const float *gain, *router_w, *router_b;  // RMSNorm gain [H], router [E][H] and bias [E]
     float eps;
     RouteOut route;             // routing outputs (logits doubles as the cross-CTA exchange buffer)
-    unsigned *rflag;            // [G] launch epoch once a CTA's router dot products are stored
+    unsigned *rcnt;             // [2] CTAs whose router dot products are stored: the launch with epoch e
+                                //     counts on [e % 2] and clears [(e + 1) % 2] for the next launch
     const uint8_t *gu_tq, *dn_tq;    // box planes: per box its swizzled rows, then its scale chunk
     const float *gu_b, *dn_b;
-    float *act;                 // [S][T][Ip] SwiGLU outputs of every token for every slot (padding stays 0)
+    uint8_t *aq;                // [S][nkb2] down operand boxes: the five E2M1 terms of every token's activation
     float *yb;                  // [S][2][T][H] down outputs, one plane per K half
     uint32_t *cnt_gu;           // [S] self-resetting arrival counters of the gate_up units
     uint32_t *cnt_dn;           // [nmt2] ... of the down units per output tile
@@ -105,11 +121,16 @@ struct DecodeParams {
     int stages;
 };
 
-// Shared-memory layout (offsets from a 1 KB-aligned base).
-__host__ __device__ constexpr uint32_t col_stride(int K) { return (uint32_t)(2 * K + 64); }  // fp16 column + pad
+// Boxes of the longest down unit (one K half, or all of K when it is one box).
+__host__ __device__ inline int down_boxes(int Ip) {
+    const int nkb2 = Ip / 128;
+    return nkb2 >= 2 ? (nkb2 + 1) / 2 : nkb2;
+}
 
+// Shared-memory layout (offsets from a 1 KB-aligned base).
 struct DecLayout {
-    uint32_t ring, bx, bd, red, units, stg, rel, offs, act, perm, inv, w, sl, rms, lg, tk, misc, bars, total;
+    uint32_t ring, bx, bd, actst, units, stg, rel, offs, act, perm, inv, w, sl, rms, lg, tk, amask, misc, bars, tslot,
+        total;
 };
 
 __host__ __device__ inline DecLayout dec_layout(int T, int Hp, int Ip, int E, int k, int stages, int ncol) {
@@ -118,18 +139,21 @@ __host__ __device__ inline DecLayout dec_layout(int T, int Hp, int Ip, int E, in
     const uint32_t P = (uint32_t)(T * k);
     L.ring = o;
     o += (uint32_t)stages * kStageBytes;
-    L.bx = o;  // gate_up operand: ncol fp16 columns of Hp
-    o += (uint32_t)ncol * col_stride(Hp);
-    L.bd = o;  // down operand: ncol fp16 columns of Ip
-    o += (uint32_t)ncol * col_stride(Ip);
-    L.red = o;  // group 1's accumulators at the end of a unit
-    o += (uint32_t)kGroupWarps * 32 * 4 * 4;
+    L.bx = o;  // gate_up operand: every K box of the normalized tokens' terms
+    o += (uint32_t)(Hp / 128) * bbox_bytes(ncol);
+    L.bd = o;  // down operand: two buffers of one unit's K boxes; first the normalized tokens [T][Hp] f32
+    {
+        const uint32_t boxes = 2u * (uint32_t)down_boxes(Ip) * bbox_bytes(ncol), xn = (uint32_t)(T * Hp) * 4u;
+        o += ((boxes > xn ? boxes : xn) + 511u) & ~511u;
+    }
+    L.actst = o;  // [T][64] SwiGLU outputs of one gate_up tile
+    o += (uint32_t)T * 64 * 4;
     L.units = o;
     o += kMaxUnits * 4;
     L.stg = o;  // [kMaxCtaStages] this CTA's ring stages: phase << 31 | (boxes - 1) << 30 | first box
     o += kMaxCtaStages * 4;
-    L.rel = o;  // [stages] warps of the consuming group done with the slot; [stages] last stage issued into it
-    o += 2u * (uint32_t)stages * 4;
+    L.rel = o;  // [stages] last stage issued into each ring slot
+    o += (uint32_t)stages * 4;
     L.offs = o;
     o += (uint32_t)(E + 1) * 4;
     L.act = o;
@@ -149,27 +173,21 @@ __host__ __device__ inline DecLayout dec_layout(int T, int Hp, int Ip, int E, in
     o += (uint32_t)(T * E) * 4;
     L.tk = o;  // [P] selected experts in slot order
     o += P * 4;
+    L.amask = o;  // [8] active-expert bit mask
+    o += 32;
     L.misc = o;  // broadcast words
     o += 64;
     o = (o + 7u) & ~7u;
-    L.bars = o;  // [stages] full barriers
-    o += (uint32_t)stages * 8;
+    L.bars = o;  // full[stages], empty[stages], accfull[2], accempty[2], bfull[2], bempty[2], done, bxready
+    o += (uint32_t)(2 * stages + 10) * 8;
+    L.tslot = o;
+    o += 16;
     L.total = o + 1024;  // base alignment slack
     return L;
 }
 
-__device__ __forceinline__ void compute_bar() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kComputeThreads) : "memory");
-}
-
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
+__device__ __forceinline__ void build_bar() { asm volatile("bar.sync 2, %0;" ::"n"(kBuildThreads) : "memory"); }
 
 // Bounded mbarrier wait that returns at once once the CTA is dead.
 __device__ __forceinline__ bool ring_wait(uint64_t *bar, uint32_t parity, volatile int *dead, int32_t *err,
@@ -193,31 +211,76 @@ __device__ __forceinline__ bool ring_wait(uint64_t *bar, uint32_t parity, volati
     }
 }
 
-// x (f32, natural order) -> fp16 hi / lo columns 2t, 2t+1 of an operand buffer.
-__device__ __forceinline__ void put_split8(uint8_t *buf, uint32_t stride, int t, int k0, const float (&v)[8]) {
-    uint32_t hi[4], lo[4];
+// ---- tcgen05, one CTA (M = 128) ----
+__device__ __forceinline__ void sf_copy(uint32_t tmem_col, uint32_t saddr) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tmem_col), "l"(desc_sf(saddr)) : "memory");
+}
+__device__ __forceinline__ void umma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc, uint32_t sfa,
+                                     uint32_t sfb) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
+        : "memory");
+}
+// Arrives on `bar` once the MMAs (and scale copies) issued so far complete.
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+// Instruction descriptor, kind::mxf4 block-scaled, M = 128: A and B E2M1,
+// K-major, E8M0 scales; sf_id is the first of the two scale bytes (32-element
+// blocks) the K = 64 MMA uses.
+__device__ __forceinline__ uint32_t idesc_dec(uint32_t sf_id, int n) {
+    return (sf_id << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24) |
+           (sf_id << 29);
+}
+template <int NCOL>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[NCOL]) {
+    if constexpr (NCOL == 8) tmem_ld8(taddr, v);
+    else if constexpr (NCOL == 16) tmem_ld16(taddr, v);
+    else tmem_ld32(taddr, v);
+}
+__device__ __forceinline__ uint32_t elect_one() {
+    uint32_t e;
+    asm volatile("{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}" : "=r"(e));
+    return e;
+}
+
+// Orders (logit, expert) as moe.go:20-27 does: larger value first, ties to the
+// lower id, NaN after every number; -0 ties with +0.  The largest key wins.
+__device__ __forceinline__ uint64_t topk_key(float v, int e) {
+    const uint32_t u = __float_as_uint(v == 0.0f ? 0.0f : v);
+    const uint32_t ord = isnan(v) ? 1u : ((u & 0x80000000u) ? ~u : (u | 0x80000000u));
+    return ((uint64_t)ord << 32) | (uint64_t)(0xffffffffu - (uint32_t)e);
+}
+
+// Writes the five E2M1 terms of eight elements (this lane's part `sub` of 32-element
+// block jb, token t) into an operand box: codes of row 5 t + j, and the scale bytes
+// (each lane of the block writes the scales of the terms j % 4 == sub).
+__device__ __forceinline__ void put_terms(uint8_t *box, uint32_t cb, int t, int jb, int sub,
+                                          const uint32_t (&codes)[kTerms][1], const uint32_t (&sbyte)[kTerms]) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-        const float2 f = __half22float2(h);
-        const __half2 l = __floats2half2_rn(v[2 * j] - f.x, v[2 * j + 1] - f.y);
-        hi[j] = *reinterpret_cast<const uint32_t *>(&h);
-        lo[j] = *reinterpret_cast<const uint32_t *>(&l);
+    for (int j = 0; j < kTerms; ++j) {
+        const int n = kTerms * t + j;
+        *reinterpret_cast<uint32_t *>(box + n * 64 + ((jb ^ ((n >> 1) & 3)) << 4) + 4 * sub) = codes[j][0];
+        if (j % 4 == sub) box[cb + n * 16 + jb] = (uint8_t)sbyte[j];
     }
-    *reinterpret_cast<uint4 *>(buf + (size_t)(2 * t) * stride + 2 * k0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    *reinterpret_cast<uint4 *>(buf + (size_t)(2 * t + 1) * stride + 2 * k0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
 
 template <int NCOL>
 __launch_bounds__(kDecThreads, 1) __global__
     void decode_kernel(DecodeParams p) {
+    static_assert(NCOL == 8 || NCOL == 16 || NCOL == 32, "MMA N");
+    constexpr uint32_t kCb = NCOL * 64;               // codes of one operand box
+    constexpr uint32_t kBb = bbox_bytes(NCOL);        // codes + scale chunk
     extern __shared__ __align__(1024) uint8_t sm_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
     const DecLayout lay = dec_layout(p.T, p.Hp, p.Ip, p.E, p.k, p.stages, NCOL);
     uint8_t *ring = sm + lay.ring;
     uint8_t *bx = sm + lay.bx;
     uint8_t *bd = sm + lay.bd;
-    float *red = reinterpret_cast<float *>(sm + lay.red);
+    float *actst = reinterpret_cast<float *>(sm + lay.actst);
     int32_t *units_s = reinterpret_cast<int32_t *>(sm + lay.units);
     int32_t *offs_s = reinterpret_cast<int32_t *>(sm + lay.offs);
     int32_t *act_s = reinterpret_cast<int32_t *>(sm + lay.act);
@@ -225,89 +288,102 @@ __launch_bounds__(kDecThreads, 1) __global__
     int32_t *inv_s = reinterpret_cast<int32_t *>(sm + lay.inv);
     float *w_s = reinterpret_cast<float *>(sm + lay.w);
     int32_t *sl_s = reinterpret_cast<int32_t *>(sm + lay.sl);
-    volatile int *misc = reinterpret_cast<volatile int *>(sm + lay.misc);  // [0] dead, [1] last, [2] units
+    volatile int *misc = reinterpret_cast<volatile int *>(sm + lay.misc);  // [0] dead, [1] last, [2] units, [3] stages
     int32_t *stg_s = reinterpret_cast<int32_t *>(sm + lay.stg);
-    int *rel_s = reinterpret_cast<int *>(sm + lay.rel);  // [R] releases, then [R] last stage issued per slot
+    int *rel_s = reinterpret_cast<int *>(sm + lay.rel);  // [R] last stage issued into each slot
+    const int R = p.stages;
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + lay.bars);
+    uint64_t *empty = full + R;
+    uint64_t *accfull = empty + R;
+    uint64_t *accempty = accfull + 2;
+    uint64_t *bfull = accempty + 2;
+    uint64_t *bempty = bfull + 2;
+    uint64_t *done = bempty + 2;
+    uint64_t *bxready = done + 1;  // gate_up's operand is in shared memory (one arrival per builder warp)
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(sm + lay.tslot);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int E = p.E, P = p.T * p.k, R = p.stages, G = gridDim.x;
-    const uint32_t sx = col_stride(p.Hp), sd = col_stride(p.Ip);
+    const int E = p.E, P = p.T * p.k, G = gridDim.x;
     const unsigned epoch = p.bar->epoch[blockIdx.x] + 1u;
 
     if (tid == 0) {
         misc[0] = 0;
         for (int s = 0; s < R; ++s) {
             mbar_init(full + s, 1);
-            rel_s[s] = 0;
-            rel_s[R + s] = -1;
+            mbar_init(empty + s, 1);
+            rel_s[s] = -1;
         }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(accfull + b, 1);
+            mbar_init(accempty + b, kEpiThreads);
+            mbar_init(bfull + b, 1);
+            mbar_init(bempty + b, 1);
+        }
+        mbar_init(done, 1);
+        mbar_init(bxready, kBuildThreads / 32);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
+                     "n"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
     // ---------------- routing, in every CTA ----------------
     // RMSNorm (primitives.go:50-72), router logits (primitives.go:11-47), top-k and
     // softmax over the selected logits (moe.go:12-41), stable (expert, token, slot)
     // permutation.  The T x E router dot products are spread over the CTAs; each
-    // publishes its flag, and every CTA then reads all logits and derives the same
-    // routing.
+    // counts itself in once its logits are stored, and every CTA then reads all
+    // logits and derives the same routing.
     {
         constexpr int kWarps = kDecThreads / 32;
+        constexpr int kPer = (4096 / 4 + kDecThreads - 1) / kDecThreads;  // float4 per thread, H <= 4096
+        constexpr int kSchedPer = kSchedWords / kDecThreads;
         double *rms_s = reinterpret_cast<double *>(sm + lay.rms);
         double *red_s = rms_s + 4;
         float *lg_s = reinterpret_cast<float *>(sm + lay.lg);
         int *tk_s = reinterpret_cast<int *>(sm + lay.tk);
-        const int T = p.T, H = p.H;
-        // (0) every global input of the routing in one batch, staged in the ring (no
-        //     copy uses it before the routing is done): this CTA's schedule rows for
-        //     every number of active slots, the T residual rows, the gain and, for a
-        //     CTA that owns a router dot product, the first router row it needs.
-        constexpr int kPer = (4096 + kDecThreads - 1) / kDecThreads;  // elements per thread, H <= 4096
-        int32_t *sched_s = reinterpret_cast<int32_t *>(ring);
-        float *xs_s = reinterpret_cast<float *>(ring + kSchedWords * 4);  // [T][Hp] residual rows
-        float *gs_s = xs_s + (size_t)T * p.Hp;                            // [Hp] gain
-        const int ndots = T * E;
-        for (int i = tid; i < kSchedWords; i += kDecThreads)
-            sched_s[i] = __ldg(p.sched + (size_t)blockIdx.x * kSchedWords + i);
-        float wv[kPer];
+        uint32_t *amask_s = reinterpret_cast<uint32_t *>(sm + lay.amask);
+        int32_t *sched_s = reinterpret_cast<int32_t *>(ring);  // read before any copy lands in the ring
+        float *xn_s = reinterpret_cast<float *>(bd);           // [T][Hp]: bd is idle until the first down unit
+        const int T = p.T, H = p.H, Hp = p.Hp;
+        const int ndots = T * E, dot_ctas = min(G, ndots);
+        if (blockIdx.x == 0 && tid == 0) p.rcnt[(epoch + 1u) & 1u] = 0u;  // the previous launch is over
+        // (0) every global input of the routing in flight at once: this CTA's schedule
+        //     rows for every number of active slots, the T residual rows, the gain
+        //     and, for a CTA that owns a router dot product, the first router row
+        //     (elements 4 (tid + 512 r) .. + 3 of each row)
+        int32_t sv[kSchedPer];
+        float4 wv[kPer], gv[kPer], xv[kDecodeMaxTokens][kPer];
         {
+            const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             const int e0 = (int)blockIdx.x < ndots ? (int)blockIdx.x % E : 0;
-            float gv[kPer];
+#pragma unroll
+            for (int r = 0; r < kSchedPer; ++r)
+                sv[r] = __ldg(p.sched + (size_t)blockIdx.x * kSchedWords + tid + r * kDecThreads);
 #pragma unroll
             for (int r = 0; r < kPer; ++r) {
-                const int i = tid + r * kDecThreads;
-                const bool in = i < H;
-                wv[r] = in && (int)blockIdx.x < ndots ? __ldg(p.router_w + (size_t)e0 * H + i) : 0.0f;
-                gv[r] = in ? __ldg(p.gain + i) : 0.0f;
+                const int i4 = tid + r * kDecThreads;
+                const bool in = 4 * i4 < H;
+                wv[r] = in && (int)blockIdx.x < ndots
+                            ? __ldg(reinterpret_cast<const float4 *>(p.router_w + (size_t)e0 * H) + i4)
+                            : z;
+                gv[r] = in ? __ldg(reinterpret_cast<const float4 *>(p.gain) + i4) : z;
+#pragma unroll
+                for (int t = 0; t < kDecodeMaxTokens; ++t)
+                    xv[t][r] = in && t < T ? __ldg(reinterpret_cast<const float4 *>(p.residual + (size_t)t * H) + i4) : z;
             }
 #pragma unroll
-            for (int r = 0; r < kPer; ++r) {
-                const int i = tid + r * kDecThreads;
-                if (i < p.Hp) gs_s[i] = gv[r];
-            }
+            for (int r = 0; r < kSchedPer; ++r) sched_s[tid + r * kDecThreads] = sv[r];
         }
         // (1) float64 sums of squares of the T residual rows
-        double ss[kDecodeMaxTokens];
 #pragma unroll
         for (int t = 0; t < kDecodeMaxTokens; ++t) {
-            ss[t] = 0.0;
-            if (t < T) {
-                float xv[kPer];
+            double v = 0.0;
 #pragma unroll
-                for (int r = 0; r < kPer; ++r) {
-                    const int i = tid + r * kDecThreads;
-                    xv[r] = i < H ? __ldg(p.residual + (size_t)t * H + i) : 0.0f;
-                }
-#pragma unroll
-                for (int r = 0; r < kPer; ++r) {
-                    const int i = tid + r * kDecThreads;
-                    ss[t] += (double)xv[r] * (double)xv[r];
-                    if (i < p.Hp) xs_s[(size_t)t * p.Hp + i] = xv[r];
-                }
-            }
-        }
-#pragma unroll
-        for (int t = 0; t < kDecodeMaxTokens; ++t) {
-            double v = ss[t];
+            for (int r = 0; r < kPer; ++r)
+                v += (double)xv[t][r].x * (double)xv[t][r].x + (double)xv[t][r].y * (double)xv[t][r].y +
+                     (double)xv[t][r].z * (double)xv[t][r].z + (double)xv[t][r].w * (double)xv[t][r].w;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
             if (lane == 0) red_s[warp * 4 + t] = v;
@@ -319,19 +395,46 @@ __launch_bounds__(kDecThreads, 1) __global__
             rms_s[tid] = 1.0 / sqrt(sum / (double)H + (double)p.eps);
         }
         __syncthreads();
-        // (2) router dot products, one per CTA (dot d on CTA d mod G):
-        //     logit = f32(sum f64(x_n) f64(W)) + b, partials added in a fixed order
+        // (2) the normalized rows, rounded to f32 as RMSNorm stores them
+        //     (primitives.go:68-70), zero past H; then the router dot products, one
+        //     per CTA (dot d on CTA d mod G): logit = f32(sum f64(x_n) f64(W)) + b,
+        //     partials added in a fixed order.  Each thread reads back only its own
+        //     elements of xn_s.
+#pragma unroll
+        for (int t = 0; t < kDecodeMaxTokens; ++t) {
+            if (t < T) {
+                const double inv = rms_s[t];
+#pragma unroll
+                for (int r = 0; r < kPer; ++r) {
+                    const int i4 = tid + r * kDecThreads;
+                    if (4 * i4 < Hp) {
+                        const float4 x = xv[t][r], g = gv[r];
+                        const bool in = 4 * i4 < H;
+                        float4 n;
+                        n.x = in ? (float)((double)x.x * inv * (double)g.x) : 0.0f;
+                        n.y = in ? (float)((double)x.y * inv * (double)g.y) : 0.0f;
+                        n.z = in ? (float)((double)x.z * inv * (double)g.z) : 0.0f;
+                        n.w = in ? (float)((double)x.w * inv * (double)g.w) : 0.0f;
+                        reinterpret_cast<float4 *>(xn_s + (size_t)t * Hp)[i4] = n;
+                    }
+                }
+            }
+        }
         for (int dd = blockIdx.x; dd < ndots; dd += G) {
             const int t = dd / E, e = dd - t * E;
-            const double inv = rms_s[t];
             double acc = 0.0;
 #pragma unroll
             for (int r = 0; r < kPer; ++r) {
-                const int i = tid + r * kDecThreads;
-                if (i < H) {
-                    const float w = dd == (int)blockIdx.x ? wv[r] : __ldg(p.router_w + (size_t)e * H + i);
-                    const float xn = (float)((double)xs_s[(size_t)t * p.Hp + i] * inv * (double)gs_s[i]);
-                    acc = fma((double)xn, (double)w, acc);
+                const int i4 = tid + r * kDecThreads;
+                if (4 * i4 < H) {
+                    const float4 w = dd == (int)blockIdx.x
+                                         ? wv[r]
+                                         : __ldg(reinterpret_cast<const float4 *>(p.router_w + (size_t)e * H) + i4);
+                    const float4 x = reinterpret_cast<const float4 *>(xn_s + (size_t)t * Hp)[i4];
+                    acc = fma((double)x.x, (double)w.x, acc);
+                    acc = fma((double)x.y, (double)w.y, acc);
+                    acc = fma((double)x.z, (double)w.z, acc);
+                    acc = fma((double)x.w, (double)w.w, acc);
                 }
             }
 #pragma unroll
@@ -345,62 +448,80 @@ __launch_bounds__(kDecThreads, 1) __global__
                 p.route.logits[dd] = (float)sum + p.router_b[e];
             }
         }
-        __syncthreads();
-        if (tid == 0 && (int)blockIdx.x < min(G, ndots)) publish(p.rflag + blockIdx.x, epoch);
-        // (2b) the gate_up operand, while other CTAs finish their dot products: every
-        //      token's normalized row (rounded to f32 as RMSNorm stores it,
-        //      primitives.go:68-70) as fp16 hi / lo columns; zero past H and in the
-        //      columns of absent tokens.
-        {
-            const int n8 = p.Hp / 8;
-            for (int it = tid; it < (NCOL / 2) * n8; it += kDecThreads) {
-                const int t = it / n8, k0 = 8 * (it - t * n8);
-                float v[8];
-                if (t < T && k0 < H) {
-                    const double inv = rms_s[t];
-#pragma unroll
-                    for (int q = 0; q < 8; ++q)
-                        v[q] = (float)((double)xs_s[(size_t)t * p.Hp + k0 + q] * inv * (double)gs_s[k0 + q]);
-                } else {
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) v[q] = 0.0f;
-                }
-                put_split8(bx, sx, t, k0, v);
-            }
+        if (tid == 0 && (int)blockIdx.x < dot_ctas) {  // this CTA's logits are stored
+            __threadfence();
+            atomicAdd(p.rcnt + (epoch & 1u), 1u);
         }
-        const int dot_ctas = min(G, ndots);
-        // (3) every CTA's logits
-        if (warp == 0) wait_flags(p.rflag, dot_ctas, epoch, lane, p.err, 53);
-        __syncthreads();
-        for (int i = tid; i < ndots; i += kDecThreads) lg_s[i] = __ldcg(p.route.logits + i);
-        __syncthreads();
-        // (4) top-k: the rank of every (token, expert) in the stable descending order
-        //     (moe.go:20-27) in parallel; ranks below k are the selected slots.  Then
-        //     the softmax over the selected logits per token (moe.go:29-39): the k
-        //     exponentials in parallel, the denominator summed in slot order.
-        for (int te = tid; te < ndots; te += kDecThreads) {
-            const int t = te / E, e = te - t * E;
-            const float v = lg_s[te];
-            int rank = 0;
-            for (int f2 = 0; f2 < E; ++f2) rank += topk_better(lg_s[t * E + f2], f2, v, e);
-            if (rank < p.k) tk_s[t * p.k + rank] = e;
-        }
-        __syncthreads();
+        // (3) one warp per token: its E logits, then the top-k as k rounds of a warp
+        //     argmax over 64-bit keys ordered as moe.go:20-27 orders the experts
+        //     (value descending, ties to the lower id, NaN after every number), then
+        //     the softmax over the selected logits (moe.go:29-39): the k exponentials
+        //     in parallel, the denominator summed in slot order.  The whole warp polls
+        //     (one request per poll) so that it stays converged.
         if (warp < T) {
             const int t = warp;
-            const double maxv = (double)lg_s[t * E + tk_s[t * p.k]];
-            const double ex = lane < p.k ? exp((double)lg_s[t * E + tk_s[t * p.k + lane]] - maxv) : 0.0;
+            {
+                const long long t0 = clock64();
+                for (;;) {
+                    const bool ready = ld_acquire(p.rcnt + (epoch & 1u)) >= (unsigned)dot_ctas;
+                    if (__all_sync(0xffffffffu, ready)) break;
+                    if (__shfl_sync(0xffffffffu, (int)(clock64() - t0 > kWaitLimit), 0)) {
+                        if (lane == 0) atomicCAS(p.err, 0, 53);
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+            uint64_t key[8];  // lane holds experts lane + 32 j (E <= 256)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int e = lane + 32 * j;
+                const bool in = e < E;
+                const float v = __ldcg(p.route.logits + (size_t)t * E + (in ? e : 0));
+                if (in) lg_s[t * E + e] = v;
+                key[j] = in ? topk_key(v, e) : 0ull;
+            }
+            __syncwarp();
+            int my_e = 0;
+            for (int s = 0; s < p.k; ++s) {
+                uint64_t b = key[0];
+#pragma unroll
+                for (int j = 1; j < 8; ++j) b = key[j] > b ? key[j] : b;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const uint64_t ob = __shfl_xor_sync(0xffffffffu, b, o);
+                    b = ob > b ? ob : b;
+                }
+                const int es = (int)(0xffffffffu - (uint32_t)b);
+                my_e = lane == s ? es : my_e;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) key[j] = lane + 32 * j == es ? 0ull : key[j];
+            }
+            if (lane < p.k) tk_s[t * p.k + lane] = my_e;
+            const double maxv = (double)lg_s[t * E + __shfl_sync(0xffffffffu, my_e, 0)];
+            const double ex_all = exp((double)lg_s[t * E + my_e] - maxv);
+            const double ex = lane < p.k ? ex_all : 0.0;
             double den = 0.0;
             for (int sl = 0; sl < p.k; ++sl) den += __shfl_sync(0xffffffffu, ex, sl);
             if (lane < p.k) w_s[t * p.k + lane] = (float)((double)(float)ex / den);
         }
         __syncthreads();
-        // (5) counts, offsets, active experts and the stable permutation
-        for (int e = tid; e <= E; e += kDecThreads) offs_s[e] = 0;
-        __syncthreads();
-        for (int q = tid; q < P; q += kDecThreads) atomicAdd(&offs_s[tk_s[q]], 1);
-        __syncthreads();
+        // (4) one warp: counts, offsets, active experts, the stable permutation, each
+        //     pair's active slot, and this CTA's units for this number of active slots
         if (warp == 0) {
+            for (int e0 = 0; e0 <= E; e0 += 32)
+                if (e0 + lane <= E) offs_s[e0 + lane] = 0;
+            if (lane < 8) amask_s[lane] = 0u;
+            __syncwarp();
+            for (int q0 = 0; q0 < P; q0 += 32) {
+                const int q = q0 + lane;
+                if (q < P) {
+                    const int e = tk_s[q];
+                    atomicAdd(&offs_s[e], 1);
+                    atomicOr(&amask_s[e >> 5], 1u << (e & 31));
+                }
+            }
+            __syncwarp();
             // warp scan over experts (lane owns experts 8 lane .. 8 lane + 7; E <= 256)
             int c[8], a[8];
             int cs = 0, as = 0;
@@ -416,10 +537,8 @@ __launch_bounds__(kDecThreads, 1) __global__
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const int cu = __shfl_up_sync(0xffffffffu, cx, o), au = __shfl_up_sync(0xffffffffu, ax, o);
-                if (lane >= o) {
-                    cx += cu;
-                    ax += au;
-                }
+                cx += lane >= o ? cu : 0;
+                ax += lane >= o ? au : 0;
             }
             int co = cx - cs, ao = ax - as;
             __syncwarp();
@@ -437,25 +556,27 @@ __launch_bounds__(kDecThreads, 1) __global__
                 offs_s[E] = cx;
                 act_s[E] = ax;
             }
-        }
-        __syncthreads();
-        for (int q = tid; q < P; q += kDecThreads) {  // pairs in (token, slot) order land stably
-            const int e = tk_s[q];
-            int pos = offs_s[e];
-            for (int r = 0; r < q; ++r) pos += tk_s[r] == e;
-            perm_s[pos] = q;
-            inv_s[q] = pos;
-            int slot = 0;
-            while (act_s[slot] != e) ++slot;  // e is active, so the search ends within act_s[0..E)
-            sl_s[q] = slot;
-        }
-        {
-            // this CTA's units for this number of active slots (its staged schedule rows)
-            const int n_active = act_s[E];
-            const int u0 = sched_s[n_active - 1], u1 = sched_s[n_active];
+            const int na = __shfl_sync(0xffffffffu, ax, 31);  // active experts (>= 1)
+            __syncwarp();
+            for (int q0 = 0; q0 < P; q0 += 32) {  // pairs in (token, slot) order land stably
+                const int q = q0 + lane;
+                const int e = tk_s[q < P ? q : 0];
+                int pos = offs_s[e];
+                for (int r = 0; r < P; ++r) pos += (r < q) & (tk_s[r] == e);
+                int slot = __popc(amask_s[e >> 5] & ((1u << (e & 31)) - 1u));  // active experts below e
+#pragma unroll
+                for (int w = 0; w < 8; ++w) slot += w < (e >> 5) ? __popc(amask_s[w]) : 0;
+                if (q < P) {
+                    perm_s[pos] = q;
+                    inv_s[q] = pos;
+                    sl_s[q] = slot;
+                }
+            }
+            const int u0 = sched_s[na - 1], u1 = sched_s[na];
             const int n = min(u1 - u0, kMaxUnits);
-            for (int u = tid; u < n; u += kDecThreads) units_s[u] = sched_s[u0 + u];
-            if (tid == 0) misc[2] = n;
+            for (int u0w = 0; u0w < n; u0w += 32)
+                if (u0w + lane < n) units_s[u0w + lane] = sched_s[u0 + u0w + lane];
+            if (lane == 0) misc[2] = n;
         }
         __syncthreads();
         if (blockIdx.x == 0) {  // the routing the C ABI reports
@@ -478,6 +599,7 @@ __launch_bounds__(kDecThreads, 1) __global__
     const int nkb1 = p.Hp / 128, nkb2 = p.Ip / 128;
     const int nmt1 = 2 * p.I / 128, nmt2 = (p.H + 127) / 128;
     const int nkp = nkb2 >= 2 ? 2 : 1, half2 = (nkb2 + 1) / 2;  // down units: K halves
+    const int dmax = down_boxes(p.Ip);
     // a unit's phase (0 gate_up, 1 down), slot, weight tile, K part and box range
     auto unit_span = [&](int32_t code, int &phase, int &slot, int &mt, int &kpart, int &kb0, int &kb1) {
         phase = (code >> 30) & 1;
@@ -489,19 +611,16 @@ __launch_bounds__(kDecThreads, 1) __global__
     };
 
     // ---------------- the ring: this CTA's stages, two boxes each ----------------
-    // Stage j is filled into slot j % R.  The first R go out now; afterwards the
-    // last warp of the consuming group to finish with a slot refills it with the
-    // stage R further on, so no warp ever polls for free slots.
+    // Stage j is filled into slot j % R once the MMAs of stage j - R released it.
     auto issue = [&](int j) {
         const int32_t code = stg_s[j];
         const int phase = (int)(((uint32_t)code >> 31) & 1u), nb = ((code >> 30) & 1) + 1;
         const size_t box = (size_t)(code & 0x3fffffff);  // plane row of the first box: 128 * box
         const int sl = j % R;
         uint8_t *st = ring + (size_t)sl * kStageBytes;
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the slot's reads before the copy's writes
         mbar_expect_tx(full + sl, (uint32_t)nb * kBoxStep);
         bulk_g2s(st, (phase ? p.dn_tq : p.gu_tq) + box * kBoxStep, (uint32_t)nb * kBoxStep, full + sl);
-        rel_s[R + sl] = j;
+        rel_s[sl] = j;
     };
     if (tid == 0) {
         int j = 0;
@@ -515,176 +634,255 @@ __launch_bounds__(kDecThreads, 1) __global__
                                      (uint32_t)(((size_t)e * nmt + mt) * nkb + kb));
         }
         misc[3] = j;
+        // the routing's staged rows in the ring are read by now (barrier above)
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         for (int i = 0; i < min(R, j); ++i) issue(i);
     }
     __syncthreads();
+    tc_fence_after();
     const int nst = misc[3];
-    {
-        // ---------------- consumers: 16 warps, two groups taking alternate stages ----------------
-        const int grp = warp / kGroupWarps, wl = warp % kGroupWarps;
-        const int g = lane >> 2, c = lane & 3;
-        const int r0 = 16 * wl + g;  // this lane's rows r0 and r0 + 8 of the 128-row tile
-        const uint32_t swz = (uint32_t)((r0 >> 1) & 3);  // SWIZZLE_64B: 16-B chunk ^= (row / 2) % 4
-        const uint32_t sc0 = (uint32_t)((r0 & 31) * 16 + (r0 >> 5) * 4);  // E8M0 chunk: byte (r%32)*16 + (r/32)*4 + j
-        const uint32_t sc1 = (uint32_t)(((r0 + 8) & 31) * 16 + ((r0 + 8) >> 5) * 4);
-        uint32_t off[4];  // this lane's 4 bytes of block q in a swizzled 64-B row
+    const uint32_t tmem = *tslot;
+
+    if (warp >= kEpiWarp0) {
+        // ---------------- gate_up's operand, while the first stages stream in ----------------
+        // every token's normalized row as five E2M1 terms per 32-element block, row
+        // 5 t + j of every K box; rows of absent tokens and K past H read as zero
+        // codes at unit scale
+        const int bt = tid - kEpiWarp0 * 32;
+        const float *xn_s = reinterpret_cast<const float *>(bd);
+        for (uint32_t o = 16u * (uint32_t)bt; o < (uint32_t)nkb1 * kBb; o += 16u * kBuildThreads)
+            *reinterpret_cast<uint4 *>(bx + o) =
+                o % kBb < kCb ? make_uint4(0u, 0u, 0u, 0u) : make_uint4(0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu);
+        build_bar();
+        const int nblk = p.Hp / 32, total = 4 * p.T * nblk;  // four lanes per (token, 32-element block)
+        for (int base = (warp - kEpiWarp0) * 32; base < total; base += kBuildThreads) {  // whole warps
+            const int it = base + lane;
+            const bool live = it < total;
+            const int unit = it >> 2, sub = it & 3;
+            const int t = live ? unit / nblk : 0, blk = live ? unit - t * nblk : 0;
+            float x[8];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) off[q] = (((uint32_t)q ^ swz) << 4) + 4 * c;
-        int i = 0;  // stage counter, the same walk as the producer's
+            for (int q = 0; q < 8; ++q) x[q] = live ? xn_s[(size_t)t * p.Hp + 32 * blk + 8 * sub + q] : 0.0f;
+            uint32_t codes[kTerms][1], sbyte[kTerms];
+            fp4::quantize<8, 4>(x, codes, sbyte);
+            if (live) put_terms(bx + (size_t)(blk >> 2) * kBb, kCb, t, blk & 3, sub, codes, sbyte);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // read by the tensor core
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bxready);
+    }
+
+    if (warp == kProdWarp) {
+        // ---------------- producer: refill each slot once its MMAs are done ----------------
+        if (lane == 0) {
+            for (int j = R; j < nst; ++j)
+                if (!ring_wait(empty + j % R, ((j / R) - 1) & 1, misc, p.err, 51)) break;
+                else issue(j);
+            // copies in flight (only after a failed wait) land before the CTA exits
+            for (int sl = 0; sl < R; ++sl)
+                if (rel_s[sl] >= 0) mbar_wait(full + sl, (rel_s[sl] / R) & 1, p.err, 54);
+        }
+    } else if (warp == kMmaWarp) {
+        // ---------------- MMA issuer ----------------
+        const uint32_t elected = elect_one();
+        const uint32_t idesc0 = idesc_dec(0, NCOL), idesc1 = idesc_dec(2, NCOL);
+        const uint32_t ring_a = smem_u32(ring), bx_a = smem_u32(bx), bd_a = smem_u32(bd);
+        int i = 0, dn = 0, nbox = 0;
+        bool ok = true, bx_ready = false;
+        for (int u = 0; u < nunits && ok; ++u) {
+            int phase, slot, mt, kpart, kb0, kb1;
+            unit_span(units_s[u], phase, slot, mt, kpart, kb0, kb1);
+            const int buf = u & 1, ub = dn & 1;
+            if (phase == 0 && !bx_ready) {
+                if (!ring_wait(bxready, 0, misc, p.err, 50)) break;
+                bx_ready = true;
+            }
+            if (u >= 2 && !ring_wait(accempty + buf, ((u >> 1) - 1) & 1, misc, p.err, 55)) break;
+            if (phase == 1 && !ring_wait(bfull + ub, (dn >> 1) & 1, misc, p.err, 56)) break;
+            tc_fence_after();
+            const uint32_t d = tmem + (uint32_t)buf * kAccCols;
+            const uint32_t bbase = phase ? bd_a + (uint32_t)(ub * dmax) * kBb : bx_a;
+            const int kbase = phase ? kb0 : 0;
+            for (int kb = kb0; kb < kb1; kb += 2, ++i) {
+                const int s = i % R, nb = min(2, kb1 - kb);
+                if (!ring_wait(full + s, (i / R) & 1, misc, p.err, 51)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int b = 0; b < nb; ++b, ++nbox) {
+                    if (elected) {
+                        // tcgen05.cp and tcgen05.mma issued by this thread execute in issue
+                        // order, so a scale slot is rewritten only after the MMAs that read it
+                        const uint32_t a = ring_a + (uint32_t)s * kStageBytes + (uint32_t)b * kBoxStep;
+                        const uint32_t bq = bbase + (uint32_t)(kb + b - kbase) * kBb;
+                        const uint32_t sf = tmem + kSfCol + 16u * (uint32_t)(nbox & 1);
+                        sf_copy(sf, a + kBoxBytes);  // the weights' E8M0 chunk
+                        sf_copy(sf + 4, bq + kCb);   // the tokens' term scales
+                        umma(d, desc_sw64(a), desc_sw64(bq), idesc0, (kb + b > kb0) ? 1u : 0u, sf, sf + 4);
+                        umma(d, desc_sw64(a + 32), desc_sw64(bq + 32), idesc1, 1u, sf, sf + 4);
+                    }
+                }
+                if (elected) mma_commit(empty + s);
+                __syncwarp();
+            }
+            if (!ok) break;
+            if (elected) {
+                mma_commit(accfull + buf);
+                if (phase == 1) mma_commit(bempty + ub);
+            }
+            __syncwarp();
+            if (phase == 1) ++dn;
+        }
+        // every MMA issued so far completes before the TMEM is released
+        if (elected) mma_commit(done);
+        __syncwarp();
+        mbar_wait(done, 0, p.err, 59);
+    } else if (warp == kLoadWarp) {
+        // ---------------- down operands: one bulk copy per unit once the slot is published ----------------
+        if (lane == 0) {
+            int dn = 0, last[2] = {-1, -1};
+            bool bx_ready = false;
+            for (int u = 0; u < nunits && !misc[0]; ++u) {
+                int phase, slot, mt, kpart, kb0, kb1;
+                unit_span(units_s[u], phase, slot, mt, kpart, kb0, kb1);
+                if (phase == 0) continue;
+                // bd holds the normalized tokens until gate_up's operand is built from them
+                if (!bx_ready && !ring_wait(bxready, 0, misc, p.err, 50)) break;
+                bx_ready = true;
+                const int ub = dn & 1;
+                if (dn >= 2 && !ring_wait(bempty + ub, ((dn >> 1) - 1) & 1, misc, p.err, 57)) break;
+                const long long t0 = clock64();
+                while ((int)(ld_acquire(p.aflag + slot) - epoch) < 0 && !misc[0]) {
+                    if (clock64() - t0 > kWaitLimit) {
+                        atomicCAS(p.err, 0, 52);
+                        misc[0] = 1;
+                    }
+                    __nanosleep(32);
+                }
+                if (misc[0]) break;
+                asm volatile("fence.proxy.async.global;" ::: "memory");  // generic stores of other CTAs -> bulk copy
+                const uint32_t bytes = (uint32_t)(kb1 - kb0) * kBb;
+                mbar_expect_tx(bfull + ub, bytes);
+                bulk_g2s(bd + (size_t)(ub * dmax) * kBb, p.aq + ((size_t)slot * nkb2 + kb0) * kBb, bytes, bfull + ub);
+                last[ub] = dn;
+                ++dn;
+            }
+            for (int b = 0; b < 2; ++b)
+                if (last[b] >= 0) mbar_wait(bfull + b, (last[b] >> 1) & 1, p.err, 54);
+        }
+    } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
+        // ---------------- unit epilogues (one thread per tile row; the same barriers on every path) ----------------
+        const int quad = warp & 3, row = quad * 32 + lane, et = tid - kEpiWarp0 * 32;
+        // gate_up: rows 16 g + j (j < 8) hold the gate of pair 8 g + j, row + 8 its up row
+        const int j16 = row & 15;
+        const bool gate_lane = j16 < 8;
+        const int pl = 8 * (row >> 4) + (j16 & 7);  // pair within the tile (0..63)
         for (int u = 0; u < nunits; ++u) {
             int phase, slot, mt, kpart, kb0, kb1;
             unit_span(units_s[u], phase, slot, mt, kpart, kb0, kb1);
             const int e = act_s[slot];
-            if (phase == 1) {
-                // the slot's activation: complete once its last gate_up unit published it
-                if (tid == 0 && !misc[0]) {
-                    const long long t0 = clock64();
-                    while ((int)(ld_acquire(p.aflag + slot) - epoch) < 0) {
-                        if (clock64() - t0 > kWaitLimit) {
-                            atomicCAS(p.err, 0, 52);
-                            misc[0] = 1;
-                            break;
-                        }
-                        __nanosleep(32);
-                    }
-                }
-                compute_bar();
-                // this unit's operand columns: the activation over its K range, fp16 hi / lo
-                const int n8 = 16 * (kb1 - kb0);
-                for (int it = tid; it < (NCOL / 2) * n8; it += kComputeThreads) {
-                    const int t = it / n8, k0 = 128 * kb0 + 8 * (it - t * n8);
-                    float v[8];
-                    if (t < p.T) {
-                        const float *src = p.act + ((size_t)slot * p.T + t) * p.Ip + k0;
-                        const float4 a0 = __ldcg(reinterpret_cast<const float4 *>(src));
-                        const float4 a1 = __ldcg(reinterpret_cast<const float4 *>(src + 4));
-                        v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w;
-                        v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
-                    } else {
+            const int buf = u & 1, h = 128 * mt + row;
+            // the bias first: its load overlaps the wait
+            float bias;
+            if (phase == 0) bias = __ldg(p.gu_b + (size_t)e * 2 * p.I + 2 * (64 * mt + pl) + (gate_lane ? 0 : 1));
+            else bias = kpart == 0 && h < p.H ? __ldg(p.dn_b + (size_t)e * p.H + h) : 0.0f;
+            float v[kDecodeMaxTokens] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (ring_wait(accfull + buf, (u >> 1) & 1, misc, p.err, 58)) {
+                tc_fence_after();
+                float a[NCOL];
+                tmem_ld_cols<NCOL>(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)buf * kAccCols, a);
 #pragma unroll
-                        for (int q = 0; q < 8; ++q) v[q] = 0.0f;
+                for (int t = 0; t < kDecodeMaxTokens; ++t)
+                    if (kTerms * (t + 1) <= NCOL && t < p.T) {
+                        float s = 0.0f;
+#pragma unroll
+                        for (int j = 0; j < kTerms; ++j) s += a[kTerms * t + j];
+                        v[t] = s;
                     }
-                    put_split8(bd, sd, t, k0, v);
-                }
-                compute_bar();
             }
-            const uint8_t *bcol = (phase ? bd : bx) + (size_t)g * (phase ? sd : sx) + 16 * c;
-            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            for (int kb = kb0; kb < kb1; kb += 2, ++i) {
-                if ((i & 1) != grp) continue;
-                const int nb = min(2, kb1 - kb), s = i % R;
-                ring_wait(full + s, (i / R) & 1, misc, p.err, 51);  // when dead: compute on stale data
-                const uint8_t *st = ring + (size_t)s * kStageBytes;
-                // all of the stage's shared-memory loads first, then up to eight independent blocks
-                uint32_t w0[2][4], w1[2][4], sv0[2], sv1[2];
-                uint4 bv[2][4];
+            tc_fence_before();
+            mbar_arrive(accempty + buf);
+            if (phase == 0) {
+                // SwiGLU of the tile's 64 pairs (partner lanes 8 apart swap values)
 #pragma unroll
-                for (int b = 0; b < 2; ++b) {
-                    if (b < nb) {
-                        const uint8_t *rows = st + b * kBoxStep + r0 * 64;
-                        const uint8_t *xk = bcol + 2 * 128 * (kb + b);
-                        sv0[b] = *reinterpret_cast<const uint32_t *>(st + b * kBoxStep + kBoxBytes + sc0);
-                        sv1[b] = *reinterpret_cast<const uint32_t *>(st + b * kBoxStep + kBoxBytes + sc1);
+                for (int t = 0; t < kDecodeMaxTokens; ++t) {
+                    if (t < p.T) {  // uniform
+                        const float val = v[t] + bias;
+                        const float other = __shfl_xor_sync(0xffffffffu, val, 8);
+                        if (gate_lane) actst[t * 64 + pl] = swiglu(val, other);
+                    }
+                }
+                epi_bar();
+                if (warp == kEpiWarp0) {
+                    // four lanes per (token, 32-pair block): the five E2M1 terms and their
+                    // scales into down's operand, blocks 2 (mt % 2) + b of box mt / 2
+                    const int unitq = lane >> 2, sub = lane & 3, t = unitq >> 1, b = unitq & 1;
+                    const bool live = t < p.T;
+                    float x[8];
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            w0[b][q] = *reinterpret_cast<const uint32_t *>(rows + off[q]);
-                            w1[b][q] = *reinterpret_cast<const uint32_t *>(rows + 8 * 64 + off[q]);
-                            bv[b][q] = g < NCOL ? *reinterpret_cast<const uint4 *>(xk + 64 * q) : make_uint4(0u, 0u, 0u, 0u);
+                    for (int q = 0; q < 8; ++q) x[q] = live ? actst[t * 64 + 32 * b + 8 * sub + q] : 0.0f;
+                    uint32_t codes[kTerms][1], sbyte[kTerms];
+                    fp4::quantize<8, 4>(x, codes, sbyte);
+                    uint8_t *box = p.aq + ((size_t)slot * nkb2 + (mt >> 1)) * kBb;
+                    if (live) put_terms(box, kCb, t, 2 * (mt & 1) + b, sub, codes, sbyte);
+                    if (mt == nmt1 - 1 && (mt & 1) == 0) {
+                        // K past I (blocks 2 and 3 of the last box): zero codes at unit scale
+                        for (int q = lane; q < 2 * NCOL; q += 32) {
+                            const int n = q >> 1, jz = 2 + (q & 1);
+                            *reinterpret_cast<uint4 *>(box + n * 64 + ((jz ^ ((n >> 1) & 3)) << 4)) =
+                                make_uint4(0u, 0u, 0u, 0u);
+                            box[kCb + n * 16 + jz] = 127;
                         }
                     }
+                    asm volatile("fence.proxy.async.global;" ::: "memory");  // read by other CTAs' bulk copies
+                    __threadfence();
                 }
+            } else {
+                if (h < p.H) {
+                    float *yrow = p.yb + ((size_t)slot * 2 + kpart) * p.T * p.H + h;
 #pragma unroll
-                for (int b = 0; b < 2; ++b) {
-                    if (b < nb) {
-                        float f0[4], f1[4];
-                        e8m0x4_to_float(sv0[b], f0);
-                        e8m0x4_to_float(sv1[b], f1);
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            const uint4 a = e2m1x8_to_f16(w0[b][q]), a8 = e2m1x8_to_f16(w1[b][q]);
-                            // the block's two k-steps into separate accumulators: no MMA waits on another
-                            float d0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, d1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                            mma16816(d0, a.x, a8.x, a.y, a8.y, bv[b][q].x, bv[b][q].y);  // elements 8c..8c+3
-                            mma16816(d1, a.z, a8.z, a.w, a8.w, bv[b][q].z, bv[b][q].w);  // elements 8c+4..8c+7
-                            acc[0] = fmaf(d0[0] + d1[0], f0[q], acc[0]);
-                            acc[1] = fmaf(d0[1] + d1[1], f0[q], acc[1]);
-                            acc[2] = fmaf(d0[2] + d1[2], f1[q], acc[2]);
-                            acc[3] = fmaf(d0[3] + d1[3], f1[q], acc[3]);
-                        }
-                    }
-                }
-                // release the slot; the group's last warp refills it with stage i + R
-                __syncwarp();
-                if (lane == 0) {
-                    if (atomicAdd(rel_s + s, 1) == kGroupWarps - 1) {
-                        rel_s[s] = 0;
-                        if (i + R < nst && !misc[0]) issue(i + R);
-                    }
-                }
-                __syncwarp();
-            }
-            // ---- unit epilogue: group 1's sums join group 0's (fixed order) ----
-            if (grp == 1)
-                *reinterpret_cast<float4 *>(red + (wl * 32 + lane) * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-            compute_bar();
-            if (grp == 0) {
-                const float4 o = *reinterpret_cast<const float4 *>(red + (wl * 32 + lane) * 4);
-                // lane (g, c) holds rows r0, r0 + 8 for columns 2c (hi) and 2c + 1 (lo): token c
-                const float v0 = (acc[0] + o.x) + (acc[1] + o.y);
-                const float v1 = (acc[2] + o.z) + (acc[3] + o.w);
-                if (c < p.T) {
-                    if (phase == 0) {
-                        // rows 16w + g and 16w + g + 8 are the gate and up rows of pair 64 mt + 8w + g
-                        const int pr = 64 * mt + 8 * wl + g;
-                        const float gate = v0 + p.gu_b[(size_t)e * 2 * p.I + 2 * pr];
-                        const float up = v1 + p.gu_b[(size_t)e * 2 * p.I + 2 * pr + 1];
-                        p.act[((size_t)slot * p.T + c) * p.Ip + pr] = swiglu(gate, up);
-                    } else {
-                        const int h0 = 128 * mt + r0, h1 = h0 + 8;
-                        float *yrow = p.yb + (((size_t)slot * 2 + kpart) * p.T + c) * p.H;
-                        if (h0 < p.H) yrow[h0] = v0 + (kpart == 0 ? p.dn_b[(size_t)e * p.H + h0] : 0.0f);
-                        if (h1 < p.H) yrow[h1] = v1 + (kpart == 0 ? p.dn_b[(size_t)e * p.H + h1] : 0.0f);
-                    }
+                    for (int t = 0; t < kDecodeMaxTokens; ++t)
+                        if (t < p.T) yrow[(size_t)t * p.H] = v[t] + bias;
                 }
                 __threadfence();
             }
-            compute_bar();
-            if (tid == 0) {
+            epi_bar();
+            if (et == 0) {
                 const unsigned n = phase == 0 ? (unsigned)nmt1 : (unsigned)(nkp * n_active);
                 unsigned *cnt = phase == 0 ? p.cnt_gu + slot : p.cnt_dn + mt;
                 const unsigned old = atomicInc(cnt, n - 1u);
                 misc[1] = old == n - 1u;
                 if (old == n - 1u && phase == 0) publish(p.aflag + slot, epoch);
             }
-            compute_bar();
+            epi_bar();
             if (phase == 1 && misc[1]) {
                 // the last down unit of output tile mt: combine its rows for every token in
                 // slot order (layer.go:109-121)
                 __threadfence();
-                for (int it = tid; it < p.T * 128; it += kComputeThreads) {
-                    const int t = it >> 7, h = 128 * mt + (it & 127);
-                    if (h >= p.H) continue;
+                for (int it = et; it < p.T * 128; it += kEpiThreads) {
+                    const int t = it >> 7, hh = 128 * mt + (it & 127);
+                    if (hh >= p.H) continue;
                     double m = 0.0;
                     for (int s = 0; s < p.k; ++s) {
                         const int q = t * p.k + s;
-                        const float *yp = p.yb + ((size_t)sl_s[q] * 2 * p.T + t) * p.H + h;
+                        const float *yp = p.yb + ((size_t)sl_s[q] * 2 * p.T + t) * p.H + hh;
                         float yv = __ldcg(yp);
                         if (nkp == 2) yv += __ldcg(yp + (size_t)p.T * p.H);
                         m += (double)w_s[q] * (double)yv;
                     }
-                    p.out[(size_t)t * p.H + h] = p.residual[(size_t)t * p.H + h] + (float)m;
+                    p.out[(size_t)t * p.H + hh] = p.residual[(size_t)t * p.H + hh] + (float)m;
                 }
             }
         }
     }
+    tc_fence_before();
     __syncthreads();
-    if (tid == 0) {
-        // copies still in flight (only after a failed wait) land before the CTA exits
-        if (misc[0])
-            for (int sl = 0; sl < R; ++sl)
-                if (rel_s[R + sl] >= 0) mbar_wait(full + sl, (rel_s[R + sl] / R) & 1, p.err, 54);
-        p.bar->epoch[blockIdx.x] = epoch;
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(kTmemCols));
     }
+    if (tid == 0) p.bar->epoch[blockIdx.x] = epoch;
 }
 
 // ---- host side -------------------------------------------------------------------------
@@ -706,15 +904,15 @@ const DecodeCaps &caps(int device) {
     return g_caps[device];
 }
 
-int dec_ncol(int T) { return T <= 1 ? 2 : (T <= 2 ? 4 : 8); }
+int dec_ncol(int T) { return T <= 1 ? 8 : (T <= 3 ? 16 : 32); }
 
-// Ring stages that fit beside the operand columns (even: each slot serves one group).
+// Ring stages that fit beside the operand boxes.
 int dec_stages(int T, int Hp, int Ip, int E, int k) {
     const DecLayout none = dec_layout(T, Hp, Ip, E, k, 0, dec_ncol(T));
-    if (none.total >= kSmemBudget) return 0;
-    int st = (int)((kSmemBudget - none.total) / (kStageBytes + 16));
-    st = std::min(st, kMaxStages);
-    return st & ~1;
+    if (none.total + 64 >= kSmemBudget) return 0;
+    // a slot, its index and two barriers per stage; 64 bytes for the layout's alignment rounding
+    const int st = (int)((kSmemBudget - none.total - 64) / (kStageBytes + 4 + 16));
+    return std::min(st, kMaxStages);
 }
 
 int dec_slots(const Dims &d) { return d.E < kDecodeMaxTokens * d.k ? d.E : kDecodeMaxTokens * d.k; }
@@ -774,15 +972,15 @@ Schedule build_schedule(const Dims &d, int G) {
 }
 
 struct DecScratch {
-    size_t act, yb, cnt_gu, cnt_dn, aflag, rflag, sched, total;
+    size_t aq, yb, cnt_gu, cnt_dn, aflag, rcnt, sched, total;
 };
 
 DecScratch dec_scratch(const Dims &d, int G, const Schedule &s) {
     const int S = dec_slots(d), Ip = kpad128(d.I), nmt2 = (d.H + 127) / 128;
     DecScratch L;
     size_t o = 0;
-    L.act = o;
-    o += align256((size_t)S * kDecodeMaxTokens * Ip * 4);
+    L.aq = o;  // down operand boxes, laid out for the widest N
+    o += align256((size_t)S * (Ip / 128) * bbox_bytes(32));
     L.yb = o;
     o += align256((size_t)S * 2 * kDecodeMaxTokens * d.H * 4);
     L.cnt_gu = o;
@@ -791,8 +989,8 @@ DecScratch dec_scratch(const Dims &d, int G, const Schedule &s) {
     o += align256((size_t)nmt2 * 4);
     L.aflag = o;
     o += align256((size_t)S * 4);
-    L.rflag = o;
-    o += align256((size_t)G * 4);
+    L.rcnt = o;
+    o += align256(2 * 4);
     L.sched = o;
     o += align256(s.rows.size() * 4);
     L.total = o;
@@ -823,14 +1021,9 @@ bool decode_supported(const Dims &d, int T, int device) {
     if (T < 1 || T > kDecodeMaxTokens || device < 0 || device >= 64) return false;
     const DecodeCaps &cp = caps(device);
     if (!cp.coop || cp.sms <= 0 || cp.sms > kDecodeMaxCtas) return false;
-    if ((2 * d.I) % 128 || d.H > 4096 || d.I > 4096 || d.E > 256 || d.k > 32 || dec_slots(d) > 1023) return false;
+    if ((2 * d.I) % 128 || d.H % 4 || d.H > 4096 || d.I > 4096 || d.E > 256 || d.k > 32 || dec_slots(d) > 1023) return false;
     if (2 * d.I / 128 > 4095 || (d.H + 127) / 128 > 4095) return false;
-    if (dec_stages(T, kpad128(d.H), kpad128(d.I), d.E, d.k) < 2) return false;
-    // the routing stages the schedule rows, the residual rows and the gain in the ring
-    const int Hp = kpad128(d.H);
-    if ((size_t)dec_stages(T, Hp, kpad128(d.I), d.E, d.k) * kStageBytes <
-        (size_t)4 * (kSchedWords + (size_t)(T + 1) * Hp))
-        return false;
+    if (dec_stages(T, kpad128(d.H), kpad128(d.I), d.E, d.k) < kMinStages) return false;
     static thread_local Dims last{};
     static thread_local int last_dev = -1;
     static thread_local bool last_ok = false;
@@ -866,12 +1059,12 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
     p.router_b = L.router_b;
     p.eps = d.eps;
     p.route = r;
-    p.rflag = reinterpret_cast<unsigned *>(b + lay.rflag);
+    p.rcnt = reinterpret_cast<unsigned *>(b + lay.rcnt);
     p.gu_tq = L.gu_tq;
     p.dn_tq = L.dn_tq;
     p.gu_b = L.gu_b;
     p.dn_b = L.dn_b;
-    p.act = reinterpret_cast<float *>(b + lay.act);
+    p.aq = b + lay.aq;
     p.yb = reinterpret_cast<float *>(b + lay.yb);
     p.cnt_gu = reinterpret_cast<uint32_t *>(b + lay.cnt_gu);
     p.cnt_dn = reinterpret_cast<uint32_t *>(b + lay.cnt_dn);
@@ -888,9 +1081,9 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
     p.Ip = Ip;
     p.S = S;
     p.stages = dec_stages(T, Hp, Ip, d.E, d.k);
-    if (p.stages < 2) return cudaErrorInvalidValue;
+    if (p.stages < kMinStages) return cudaErrorInvalidValue;
     const size_t smem = dec_layout(T, Hp, Ip, d.E, d.k, p.stages, ncol).total;
-    auto kern = ncol == 2 ? decode_kernel<2> : (ncol == 4 ? decode_kernel<4> : decode_kernel<8>);
+    auto kern = ncol == 8 ? decode_kernel<8> : (ncol == 16 ? decode_kernel<16> : decode_kernel<32>);
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
