@@ -11,17 +11,18 @@
 // design goal is to keep every SM streaming weight boxes from the moment the
 // routing is known to the end, with next to no instructions per weight.
 //
-// Work.  A unit is one 128-row weight tile of one selected expert over its K
-// range: every gate_up tile over all of K (SwiGLU needs the whole sum), every
-// down tile over one half of K.  A host-built table (longest-processing-time
-// first over the units' box counts, one table per number of active experts)
-// gives each CTA its units: gate_up units first, then down units, both in
-// slot order.  No unit is shared between CTAs, so no tile needs a cross-CTA
-// reduction.  Two hand-offs cross CTAs, both through L2:
-//   - the last gate_up unit of a slot to finish publishes the slot's
-//     activation (a per-slot flag carrying the launch epoch); a down unit's
-//     activation operand is copied in once the flag is up (its weights are
-//     already streaming into the ring meanwhile);
+// Work.  A unit is a K range of one 128-row weight tile of one selected expert.
+// A host-built table (one per number of active experts) gives each CTA its units:
+// the down tiles as K halves, placed longest-processing-time first, then the
+// gate_up boxes in (slot, tile, K) order cut into contiguous ranges so that every
+// CTA's total box count comes out even (stream-K).  A gate_up tile whose range
+// spans CTAs becomes pieces: the later pieces store their partial sums, and piece
+// 0 (the end of an earlier CTA's range, so the last to run) adds them in piece
+// order.  Within a CTA the gate_up pieces run first.  The hand-offs between CTAs
+// go through L2:
+//   - every finished gate_up tile counts itself into its slot's counter; a down
+//     unit's activation operand is copied in once the counter is complete (its
+//     weights are already streaming into the ring meanwhile);
 //   - the last down unit of a 128-row output tile to finish combines that
 //     tile for every token (self-resetting arrival counters).
 //
@@ -37,12 +38,15 @@
 // outputs' terms, to global memory in the same box form, and a down unit copies
 // its K half of it in one bulk copy.
 //
-// Roles after the routing: warp 0 lane 0 streams the ring (waiting for the
-// MMAs to release a stage), warp 1 issues the MMAs into two TMEM accumulators
-// (the epilogue of one unit overlaps the next unit's MMAs), warp 2 lane 0
-// copies the down units' operands as their flags come up, warps 4-15 first
-// quantize gate_up's operand (while the first stages are in flight) and warps
-// 4-7 (one per TMEM lane quadrant) then run the unit epilogues.
+// Roles once the CTA's units are known: warp 0 lane 0 streams the ring (a slot
+// refilled once the MMAs released it), warp 1 issues the MMAs into two TMEM
+// accumulators, warp 2 lane 0 copies the down units' operands as their counters
+// complete, warp 3 finishes the routing that only the combine needs (softmax
+// weights, permutation, slots), and two epilogue groups of four warps (one per
+// TMEM lane quadrant) run the unit epilogues: warps 4-7 take the units of
+// accumulator 0, warps 8-11 those of accumulator 1, so two epilogues (each a chain
+// of global round trips) and the next unit's MMAs overlap.  Before that, while
+// warps 0-3 select the experts, warps 4-15 quantize gate_up's operand.
 //
 // The routing is a chain of short dependent steps, so it is written for
 // latency: every global load in flight at once, warp-uniform control flow around
@@ -68,8 +72,9 @@ namespace {
 using namespace bs;
 
 constexpr int kDecThreads = 512;                // 16 warps: the routing spreads H over all of them
-constexpr int kProdWarp = 0, kMmaWarp = 1, kLoadWarp = 2, kEpiWarp0 = 4;
-constexpr int kEpiThreads = 128;                // warps 4-7, one per TMEM lane quadrant
+constexpr int kProdWarp = 0, kMmaWarp = 1, kLoadWarp = 2, kRestWarp = 3, kEpiWarp0 = 4;
+constexpr int kEpiThreads = 128;                // an epilogue group: four warps, one per TMEM lane quadrant
+constexpr int kEpiGroups = 2;                   // warps 4-7 take the units of accumulator 0, warps 8-11 those of 1
 constexpr int kBuildThreads = kDecThreads - kEpiWarp0 * 32;  // warps 4-15 quantize gate_up's operand
 constexpr int kTerms = fp4::kTerms;
 constexpr uint32_t kBoxBytes = 128 * 64;        // one packed box: 128 rows x 128 E2M1 values
@@ -81,7 +86,6 @@ constexpr int kMinStages = 4;
 constexpr int kMaxUnits = 64;                   // units per CTA
 constexpr int kSchedWords = 1024;               // one CTA's schedule rows (int32)
 static_assert(kSchedWords == AMOE_DECODE_SCHED_WORDS, "the table row size is part of the C ABI");
-constexpr int kMaxCtaStages = kMaxUnits * 16;   // ring stages of one CTA (a unit has <= 16: K <= 4096)
 constexpr size_t kSmemBudget = 232448;          // dynamic shared memory per block (227 KB)
 constexpr uint32_t kTmemCols = 128;             // accumulators at columns 0 and 32, scale slots at 64 and 80
 constexpr uint32_t kAccCols = 32;
@@ -94,9 +98,18 @@ static_assert((size_t)kMinStages * kStageBytes >= 4 * kSchedWords, "the routing 
 // then the N rows' E8M0 bytes in a 512-byte chunk (byte 16 n + j: row n, block j).
 __host__ __device__ constexpr uint32_t bbox_bytes(int ncol) { return (uint32_t)ncol * 64u + kSfChunk; }
 
-// Unit encoding in the schedule table.
-__host__ __device__ constexpr int32_t unit_code(int phase, int slot, int mt, int kpart) {
-    return (phase << 30) | (slot << 20) | (mt << 8) | kpart;
+// A unit in the schedule table is two words:
+//   w0 = phase << 31 | slot << 20 | tile << 8 | piece << 4 | pieces
+//   w1 = first K box << 24 | end K box << 16 | split index
+// gate_up tiles cut between CTAs (pieces > 1) meet through the partial-sum
+// buffer of their split index; a down unit's piece is its K half.
+constexpr int kMaxPieces = 4;
+__host__ __device__ constexpr int32_t unit_w0(int phase, int slot, int mt, int piece, int pieces) {
+    return (int32_t)(((uint32_t)phase << 31) | ((uint32_t)slot << 20) | ((uint32_t)mt << 8) | ((uint32_t)piece << 4) |
+                     (uint32_t)pieces);
+}
+__host__ __device__ constexpr int32_t unit_w1(int kb0, int kb1, int split) {
+    return (int32_t)(((uint32_t)kb0 << 24) | ((uint32_t)kb1 << 16) | (uint32_t)split);
 }
 
 struct DecodeParams {
@@ -111,9 +124,11 @@ struct DecodeParams {
     const float *gu_b, *dn_b;
     uint8_t *aq;                // [S][nkb2] down operand boxes: the five E2M1 terms of every token's activation
     float *yb;                  // [S][2][T][H] down outputs, one plane per K half
-    uint32_t *cnt_gu;           // [S] self-resetting arrival counters of the gate_up units
+    uint32_t *cnt_gu;           // [2][S] finished gate_up tiles per slot: the launch with epoch e counts
+                                //     on [e % 2] and clears [(e + 1) % 2] for the next launch
+    float *gpart;               // [G][kMaxPieces][4][128] partial sums of the gate_up tiles cut between CTAs
+    uint32_t *cnt_split;        // [2][G] pieces of those tiles stored besides piece 0 (epoch parity as cnt_gu)
     uint32_t *cnt_dn;           // [nmt2] ... of the down units per output tile
-    unsigned *aflag;            // [S] launch epoch once the slot's activation is complete
     const int32_t *sched;       // [G][kSchedWords]: per CTA, [n - 1]..[n] delimit its units when n slots are active
     DecodeBarrier *bar;
     int32_t *err;
@@ -129,7 +144,7 @@ __host__ __device__ inline int down_boxes(int Ip) {
 
 // Shared-memory layout (offsets from a 1 KB-aligned base).
 struct DecLayout {
-    uint32_t ring, bx, bd, actst, units, stg, rel, offs, act, perm, inv, w, sl, rms, lg, tk, amask, misc, bars, tslot,
+    uint32_t ring, bx, bd, actst, units, rel, offs, act, perm, inv, w, sl, rms, lg, tk, amask, misc, bars, tslot,
         total;
 };
 
@@ -146,12 +161,10 @@ __host__ __device__ inline DecLayout dec_layout(int T, int Hp, int Ip, int E, in
         const uint32_t boxes = 2u * (uint32_t)down_boxes(Ip) * bbox_bytes(ncol), xn = (uint32_t)(T * Hp) * 4u;
         o += ((boxes > xn ? boxes : xn) + 511u) & ~511u;
     }
-    L.actst = o;  // [T][64] SwiGLU outputs of one gate_up tile
-    o += (uint32_t)T * 64 * 4;
-    L.units = o;
-    o += kMaxUnits * 4;
-    L.stg = o;  // [kMaxCtaStages] this CTA's ring stages: phase << 31 | (boxes - 1) << 30 | first box
-    o += kMaxCtaStages * 4;
+    L.actst = o;  // [group][T][64] SwiGLU outputs of one gate_up tile
+    o += (uint32_t)kEpiGroups * T * 64 * 4;
+    L.units = o;  // [kMaxUnits][2] this CTA's units
+    o += kMaxUnits * 8;
     L.rel = o;  // [stages] last stage issued into each ring slot
     o += (uint32_t)stages * 4;
     L.offs = o;
@@ -178,15 +191,28 @@ __host__ __device__ inline DecLayout dec_layout(int T, int Hp, int Ip, int E, in
     L.misc = o;  // broadcast words
     o += 64;
     o = (o + 7u) & ~7u;
-    L.bars = o;  // full[stages], empty[stages], accfull[2], accempty[2], bfull[2], bempty[2], done, bxready
-    o += (uint32_t)(2 * stages + 10) * 8;
+    L.bars = o;  // full[stages], empty[stages], accfull[2], accempty[2], bfull[2], bempty[2], done, bxready, rdone
+    o += (uint32_t)(2 * stages + 11) * 8;
     L.tslot = o;
     o += 16;
     L.total = o + 1024;  // base alignment slack
     return L;
 }
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
+// Barrier of epilogue group g (named barriers 4 and 5).
+__device__ __forceinline__ void epi_bar(int g) { asm volatile("bar.sync %0, %1;" ::"r"(4 + g), "n"(kEpiThreads) : "memory"); }
+// Arrival on a cross-CTA counter (wraps to 0 after `lim`): release for the
+// stores that precede it in this CTA (ordered by a barrier), acquire for the
+// other CTAs' stores that precede their arrivals.
+__device__ __forceinline__ unsigned atom_inc_acq_rel(unsigned *p, unsigned lim) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(lim) : "memory");
+    return old;
+}
+__device__ __forceinline__ void red_add_release(unsigned *p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void route_bar() { asm volatile("bar.sync 3, %0;" ::"n"(kEpiWarp0 * 32) : "memory"); }
 __device__ __forceinline__ void build_bar() { asm volatile("bar.sync 2, %0;" ::"n"(kBuildThreads) : "memory"); }
 
 // Bounded mbarrier wait that returns at once once the CTA is dead.
@@ -288,8 +314,7 @@ __launch_bounds__(kDecThreads, 1) __global__
     int32_t *inv_s = reinterpret_cast<int32_t *>(sm + lay.inv);
     float *w_s = reinterpret_cast<float *>(sm + lay.w);
     int32_t *sl_s = reinterpret_cast<int32_t *>(sm + lay.sl);
-    volatile int *misc = reinterpret_cast<volatile int *>(sm + lay.misc);  // [0] dead, [1] last, [2] units, [3] stages
-    int32_t *stg_s = reinterpret_cast<int32_t *>(sm + lay.stg);
+    volatile int *misc = reinterpret_cast<volatile int *>(sm + lay.misc);  // [0] dead, [1] last, [2] units, [3] stages, [4] last piece
     int *rel_s = reinterpret_cast<int *>(sm + lay.rel);  // [R] last stage issued into each slot
     const int R = p.stages;
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + lay.bars);
@@ -300,6 +325,7 @@ __launch_bounds__(kDecThreads, 1) __global__
     uint64_t *bempty = bfull + 2;
     uint64_t *done = bempty + 2;
     uint64_t *bxready = done + 1;  // gate_up's operand is in shared memory (one arrival per builder warp)
+    uint64_t *rdone = bxready + 1;  // the softmax weights and each pair's slot are in shared memory (for the combine)
     uint32_t *tslot = reinterpret_cast<uint32_t *>(sm + lay.tslot);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -321,6 +347,7 @@ __launch_bounds__(kDecThreads, 1) __global__
         }
         mbar_init(done, 1);
         mbar_init(bxready, kBuildThreads / 32);
+        mbar_init(rdone, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == kMmaWarp) {
@@ -329,6 +356,39 @@ __launch_bounds__(kDecThreads, 1) __global__
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
+    const int nkb1 = p.Hp / 128, nkb2 = p.Ip / 128;
+    const int nmt1 = 2 * p.I / 128, nmt2 = (p.H + 127) / 128;
+    const int nkp = nkb2 >= 2 ? 2 : 1;  // down units: K halves
+    const int dmax = down_boxes(p.Ip);
+    // unit u's phase (0 gate_up, 1 down), slot, weight tile, piece (a down unit's K
+    // half), pieces of its tile, K box range and split index
+    auto unit_span = [&](int u, int &phase, int &slot, int &mt, int &kpart, int &np, int &kb0, int &kb1, int &split) {
+        const uint32_t w0 = (uint32_t)units_s[2 * u], w1 = (uint32_t)units_s[2 * u + 1];
+        phase = (int)(w0 >> 31);
+        slot = (int)((w0 >> 20) & 1023u);
+        mt = (int)((w0 >> 8) & 4095u);
+        kpart = (int)((w0 >> 4) & 15u);
+        np = (int)(w0 & 15u);
+        kb0 = (int)(w1 >> 24);
+        kb1 = (int)((w1 >> 16) & 255u);
+        split = (int)(w1 & 0xffffu);
+    };
+
+    // ---------------- the ring: this CTA's stages, two boxes each ----------------
+    // Stage j (the units' K ranges in order, two boxes a stage) is filled into slot
+    // j % R once the MMAs of stage j - R released it.
+    auto issue = [&](int j, int u, int kb) {  // boxes kb, kb + 1 (kb alone at the range's end) of unit u
+        int phase, slot, mt, kpart, np, kb0, kb1, split;
+        unit_span(u, phase, slot, mt, kpart, np, kb0, kb1, split);
+        const size_t e = (size_t)act_s[slot];
+        const uint32_t nb = (uint32_t)min(2, kb1 - kb);
+        const size_t box = phase ? (e * nmt2 + mt) * nkb2 + kb : (e * nmt1 + mt) * nkb1 + kb;
+        const int sl = j % R;
+        mbar_expect_tx(full + sl, nb * kBoxStep);
+        bulk_g2s(ring + (size_t)sl * kStageBytes, (phase ? p.dn_tq : p.gu_tq) + box * kBoxStep, nb * kBoxStep, full + sl);
+        rel_s[sl] = j;
+    };
+
     // ---------------- routing, in every CTA ----------------
     // RMSNorm (primitives.go:50-72), router logits (primitives.go:11-47), top-k and
     // softmax over the selected logits (moe.go:12-41), stable (expert, token, slot)
@@ -348,7 +408,11 @@ __launch_bounds__(kDecThreads, 1) __global__
         float *xn_s = reinterpret_cast<float *>(bd);           // [T][Hp]: bd is idle until the first down unit
         const int T = p.T, H = p.H, Hp = p.Hp;
         const int ndots = T * E, dot_ctas = min(G, ndots);
-        if (blockIdx.x == 0 && tid == 0) p.rcnt[(epoch + 1u) & 1u] = 0u;  // the previous launch is over
+        if (blockIdx.x == 0) {  // the previous launch is over: clear the next one's counters
+            if (tid == 0) p.rcnt[(epoch + 1u) & 1u] = 0u;
+            for (int i = tid; i < p.S; i += kDecThreads) p.cnt_gu[((epoch + 1u) & 1u) * p.S + i] = 0u;
+            for (int i = tid; i < G; i += kDecThreads) p.cnt_split[((epoch + 1u) & 1u) * G + i] = 0u;
+        }
         // (0) every global input of the routing in flight at once: this CTA's schedule
         //     rows for every number of active slots, the T residual rows, the gain
         //     and, for a CTA that owns a router dot product, the first router row
@@ -420,6 +484,7 @@ __launch_bounds__(kDecThreads, 1) __global__
                 }
             }
         }
+        __syncthreads();  // the operand builders read every thread's rows
         for (int dd = blockIdx.x; dd < ndots; dd += G) {
             const int t = dd / E, e = dd - t * E;
             double acc = 0.0;
@@ -448,236 +513,149 @@ __launch_bounds__(kDecThreads, 1) __global__
                 p.route.logits[dd] = (float)sum + p.router_b[e];
             }
         }
-        if (tid == 0 && (int)blockIdx.x < dot_ctas) {  // this CTA's logits are stored
-            __threadfence();
-            atomicAdd(p.rcnt + (epoch & 1u), 1u);
-        }
-        // (3) one warp per token: its E logits, then the top-k as k rounds of a warp
-        //     argmax over 64-bit keys ordered as moe.go:20-27 orders the experts
-        //     (value descending, ties to the lower id, NaN after every number), then
-        //     the softmax over the selected logits (moe.go:29-39): the k exponentials
-        //     in parallel, the denominator summed in slot order.  The whole warp polls
-        //     (one request per poll) so that it stays converged.
-        if (warp < T) {
-            const int t = warp;
-            {
-                const long long t0 = clock64();
-                for (;;) {
-                    const bool ready = ld_acquire(p.rcnt + (epoch & 1u)) >= (unsigned)dot_ctas;
-                    if (__all_sync(0xffffffffu, ready)) break;
-                    if (__shfl_sync(0xffffffffu, (int)(clock64() - t0 > kWaitLimit), 0)) {
-                        if (lane == 0) atomicCAS(p.err, 0, 53);
-                        break;
+        if (tid == 0 && (int)blockIdx.x < dot_ctas)  // this CTA's logits are stored (release orders them first)
+            red_add_release(p.rcnt + (epoch & 1u), 1u);
+        if (warp >= kEpiWarp0) {
+            // ---------------- gate_up's operand, while warps 0-3 finish the routing ----------------
+            // every token's normalized row as five E2M1 terms per 32-element block, row
+            // 5 t + j of every K box; rows of absent tokens and K past H read as zero
+            // codes at unit scale
+            const int bt = tid - kEpiWarp0 * 32;
+            for (uint32_t o = 16u * (uint32_t)bt; o < (uint32_t)nkb1 * kBb; o += 16u * kBuildThreads)
+                *reinterpret_cast<uint4 *>(bx + o) = o % kBb < kCb ? make_uint4(0u, 0u, 0u, 0u)
+                                                                   : make_uint4(0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu);
+            build_bar();
+            const int nblk = Hp / 32, total = 4 * T * nblk;  // four lanes per (token, 32-element block)
+            for (int base = (warp - kEpiWarp0) * 32; base < total; base += kBuildThreads) {  // whole warps
+                const int it = base + lane;
+                const bool live = it < total;
+                const int unit = it >> 2, sub = it & 3;
+                const int t = live ? unit / nblk : 0, blk = live ? unit - t * nblk : 0;
+                float x[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) x[q] = live ? xn_s[(size_t)t * Hp + 32 * blk + 8 * sub + q] : 0.0f;
+                uint32_t codes[kTerms][1], sbyte[kTerms];
+                fp4::quantize<8, 4>(x, codes, sbyte);
+                if (live) put_terms(bx + (size_t)(blk >> 2) * kBb, kCb, t, blk & 3, sub, codes, sbyte);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // read by the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bxready);
+        } else {
+            // (3) one warp per token: its E logits, then the top-k as k rounds of a warp
+            //     argmax over 64-bit keys ordered as moe.go:20-27 orders the experts
+            //     (value descending, ties to the lower id, NaN after every number).  The
+            //     whole warp spins on the counter (one request per poll): it stays
+            //     converged, and a warp that slept runs its shuffles slowly afterwards.
+            if (warp < T) {
+                const int t = warp;
+                {
+                    const long long t0 = clock64();
+                    for (;;) {
+                        const bool ready = ld_acquire(p.rcnt + (epoch & 1u)) >= (unsigned)dot_ctas;
+                        if (__all_sync(0xffffffffu, ready)) break;
+                        if (__shfl_sync(0xffffffffu, (int)(clock64() - t0 > kWaitLimit), 0)) {
+                            if (lane == 0) atomicCAS(p.err, 0, 53);
+                            break;
+                        }
                     }
-                    __nanosleep(64);
                 }
-            }
-            uint64_t key[8];  // lane holds experts lane + 32 j (E <= 256)
+                uint64_t key[8];  // lane holds experts lane + 32 j (E <= 256)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int e = lane + 32 * j;
-                const bool in = e < E;
-                const float v = __ldcg(p.route.logits + (size_t)t * E + (in ? e : 0));
-                if (in) lg_s[t * E + e] = v;
-                key[j] = in ? topk_key(v, e) : 0ull;
-            }
-            __syncwarp();
-            int my_e = 0;
-            for (int s = 0; s < p.k; ++s) {
-                uint64_t b = key[0];
-#pragma unroll
-                for (int j = 1; j < 8; ++j) b = key[j] > b ? key[j] : b;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const uint64_t ob = __shfl_xor_sync(0xffffffffu, b, o);
-                    b = ob > b ? ob : b;
+                for (int j = 0; j < 8; ++j) {
+                    const int e = lane + 32 * j;
+                    const bool in = e < E;
+                    const float v = __ldcg(p.route.logits + (size_t)t * E + (in ? e : 0));
+                    if (in) lg_s[t * E + e] = v;
+                    key[j] = in ? topk_key(v, e) : 0ull;
                 }
-                const int es = (int)(0xffffffffu - (uint32_t)b);
-                my_e = lane == s ? es : my_e;
+                __syncwarp();
+                int my_e = 0;
+                for (int s = 0; s < p.k; ++s) {
+                    uint64_t b = key[0];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) key[j] = lane + 32 * j == es ? 0ull : key[j];
-            }
-            if (lane < p.k) tk_s[t * p.k + lane] = my_e;
-            const double maxv = (double)lg_s[t * E + __shfl_sync(0xffffffffu, my_e, 0)];
-            const double ex_all = exp((double)lg_s[t * E + my_e] - maxv);
-            const double ex = lane < p.k ? ex_all : 0.0;
-            double den = 0.0;
-            for (int sl = 0; sl < p.k; ++sl) den += __shfl_sync(0xffffffffu, ex, sl);
-            if (lane < p.k) w_s[t * p.k + lane] = (float)((double)(float)ex / den);
-        }
-        __syncthreads();
-        // (4) one warp: counts, offsets, active experts, the stable permutation, each
-        //     pair's active slot, and this CTA's units for this number of active slots
-        if (warp == 0) {
-            for (int e0 = 0; e0 <= E; e0 += 32)
-                if (e0 + lane <= E) offs_s[e0 + lane] = 0;
-            if (lane < 8) amask_s[lane] = 0u;
-            __syncwarp();
-            for (int q0 = 0; q0 < P; q0 += 32) {
-                const int q = q0 + lane;
-                if (q < P) {
-                    const int e = tk_s[q];
-                    atomicAdd(&offs_s[e], 1);
-                    atomicOr(&amask_s[e >> 5], 1u << (e & 31));
+                    for (int j = 1; j < 8; ++j) b = key[j] > b ? key[j] : b;
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        const uint64_t ob = __shfl_xor_sync(0xffffffffu, b, o);
+                        b = ob > b ? ob : b;
+                    }
+                    const int es = (int)(0xffffffffu - (uint32_t)b);
+                    my_e = lane == s ? es : my_e;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) key[j] = lane + 32 * j == es ? 0ull : key[j];
                 }
+                if (lane < p.k) tk_s[t * p.k + lane] = my_e;
             }
-            __syncwarp();
-            // warp scan over experts (lane owns experts 8 lane .. 8 lane + 7; E <= 256)
-            int c[8], a[8];
-            int cs = 0, as = 0;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int e = 8 * lane + j;
-                c[j] = e < E ? offs_s[e] : 0;
-                a[j] = c[j] > 0;
-                cs += c[j];
-                as += a[j];
-            }
-            int cx = cs, ax = as;  // inclusive warp prefix sums
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int cu = __shfl_up_sync(0xffffffffu, cx, o), au = __shfl_up_sync(0xffffffffu, ax, o);
-                cx += lane >= o ? cu : 0;
-                ax += lane >= o ? au : 0;
-            }
-            int co = cx - cs, ao = ax - as;
-            __syncwarp();
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int e = 8 * lane + j;
-                if (e < E) {
-                    offs_s[e] = co;
-                    if (a[j]) act_s[ao] = e;
+            route_bar();
+            // (4) one warp: the active experts (their slots in ascending id order), this
+            //     CTA's units for that many, and the first copies.  Everything else of
+            //     the routing is needed only by the combine and the reported routing.
+            if (warp == 0) {
+                if (lane < 8) amask_s[lane] = 0u;
+                __syncwarp();
+                for (int q0 = 0; q0 < P; q0 += 32) {
+                    const int q = q0 + lane;
+                    if (q < P) atomicOr(&amask_s[tk_s[q] >> 5], 1u << (tk_s[q] & 31));
                 }
-                co += c[j];
-                ao += a[j];
-            }
-            if (lane == 31) {
-                offs_s[E] = cx;
-                act_s[E] = ax;
-            }
-            const int na = __shfl_sync(0xffffffffu, ax, 31);  // active experts (>= 1)
-            __syncwarp();
-            for (int q0 = 0; q0 < P; q0 += 32) {  // pairs in (token, slot) order land stably
-                const int q = q0 + lane;
-                const int e = tk_s[q < P ? q : 0];
-                int pos = offs_s[e];
-                for (int r = 0; r < P; ++r) pos += (r < q) & (tk_s[r] == e);
-                int slot = __popc(amask_s[e >> 5] & ((1u << (e & 31)) - 1u));  // active experts below e
+                __syncwarp();
+                const uint32_t word = lane < 8 ? amask_s[lane] : 0u;
+                int pre = __popc(word);  // inclusive scan of the words' counts
 #pragma unroll
-                for (int w = 0; w < 8; ++w) slot += w < (e >> 5) ? __popc(amask_s[w]) : 0;
-                if (q < P) {
-                    perm_s[pos] = q;
-                    inv_s[q] = pos;
-                    sl_s[q] = slot;
+                for (int o = 1; o < 8; o <<= 1) {
+                    const int x = __shfl_up_sync(0xffffffffu, pre, o);
+                    pre += lane >= o ? x : 0;
                 }
-            }
-            const int u0 = sched_s[na - 1], u1 = sched_s[na];
-            const int n = min(u1 - u0, kMaxUnits);
-            for (int u0w = 0; u0w < n; u0w += 32)
-                if (u0w + lane < n) units_s[u0w + lane] = sched_s[u0 + u0w + lane];
-            if (lane == 0) misc[2] = n;
-        }
-        __syncthreads();
-        if (blockIdx.x == 0) {  // the routing the C ABI reports
-            for (int q = tid; q < P; q += kDecThreads) {
-                p.route.topk_idx[q] = tk_s[q];
-                p.route.topk_w[q] = w_s[q];
-                p.route.perm_pair[q] = perm_s[q];
-                p.route.inv[q] = inv_s[q];
-            }
-            for (int e = tid; e <= E; e += kDecThreads) {
-                p.route.offsets[e] = offs_s[e];
-                p.route.active[e] = act_s[e];
-                if (e < E) p.route.counts[e] = offs_s[e + 1] - offs_s[e];
+                const int na = __shfl_sync(0xffffffffu, pre, 7);  // active experts (>= 1)
+                int pos = pre - __popc(word);
+                for (int bit = 0; bit < 32; ++bit)
+                    if ((word >> bit) & 1u) act_s[pos++] = 32 * lane + bit;
+                if (lane == 0) act_s[E] = na;
+                const int u0 = sched_s[na - 1], u1 = sched_s[na];
+                const int n = min((u1 - u0) / 2, kMaxUnits);
+                for (int w0 = 0; w0 < 2 * n; w0 += 32)
+                    if (w0 + lane < 2 * n) units_s[w0 + lane] = sched_s[u0 + w0 + lane];
+                if (lane == 0) misc[2] = n;
+                __syncwarp();
+                if (lane == 0) {  // the first copies
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the staged schedule rows are read
+                    const int first = R;
+                    int j = 0;
+                    for (int u = 0; u < n && j < first; ++u) {
+                        int phase, slot, mt, kpart, np, kb0, kb1, split;
+                        unit_span(u, phase, slot, mt, kpart, np, kb0, kb1, split);
+                        for (int kb = kb0; kb < kb1 && j < first; kb += 2, ++j) issue(j, u, kb);
+                    }
+                    misc[3] = j;  // stages issued
+                }
             }
         }
-    }
-
-    const int n_active = act_s[E];
-    const int nunits = misc[2];
-    const int nkb1 = p.Hp / 128, nkb2 = p.Ip / 128;
-    const int nmt1 = 2 * p.I / 128, nmt2 = (p.H + 127) / 128;
-    const int nkp = nkb2 >= 2 ? 2 : 1, half2 = (nkb2 + 1) / 2;  // down units: K halves
-    const int dmax = down_boxes(p.Ip);
-    // a unit's phase (0 gate_up, 1 down), slot, weight tile, K part and box range
-    auto unit_span = [&](int32_t code, int &phase, int &slot, int &mt, int &kpart, int &kb0, int &kb1) {
-        phase = (code >> 30) & 1;
-        slot = (code >> 20) & 1023;
-        mt = (code >> 8) & 4095;
-        kpart = code & 1;
-        kb0 = phase == 0 || kpart == 0 ? 0 : half2;
-        kb1 = phase == 0 ? nkb1 : (nkp == 1 || kpart == 1 ? nkb2 : half2);
-    };
-
-    // ---------------- the ring: this CTA's stages, two boxes each ----------------
-    // Stage j is filled into slot j % R once the MMAs of stage j - R released it.
-    auto issue = [&](int j) {
-        const int32_t code = stg_s[j];
-        const int phase = (int)(((uint32_t)code >> 31) & 1u), nb = ((code >> 30) & 1) + 1;
-        const size_t box = (size_t)(code & 0x3fffffff);  // plane row of the first box: 128 * box
-        const int sl = j % R;
-        uint8_t *st = ring + (size_t)sl * kStageBytes;
-        mbar_expect_tx(full + sl, (uint32_t)nb * kBoxStep);
-        bulk_g2s(st, (phase ? p.dn_tq : p.gu_tq) + box * kBoxStep, (uint32_t)nb * kBoxStep, full + sl);
-        rel_s[sl] = j;
-    };
-    if (tid == 0) {
-        int j = 0;
-        for (int u = 0; u < nunits; ++u) {
-            int phase, slot, mt, kpart, kb0, kb1;
-            unit_span(units_s[u], phase, slot, mt, kpart, kb0, kb1);
-            const int e = act_s[slot];
-            const int nmt = phase ? nmt2 : nmt1, nkb = phase ? nkb2 : nkb1;
-            for (int kb = kb0; kb < kb1 && j < kMaxCtaStages; kb += 2, ++j)
-                stg_s[j] = (int32_t)(((uint32_t)phase << 31) | ((uint32_t)(min(2, kb1 - kb) - 1) << 30) |
-                                     (uint32_t)(((size_t)e * nmt + mt) * nkb + kb));
-        }
-        misc[3] = j;
-        // the routing's staged rows in the ring are read by now (barrier above)
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        for (int i = 0; i < min(R, j); ++i) issue(i);
     }
     __syncthreads();
     tc_fence_after();
-    const int nst = misc[3];
+    const int n_active = act_s[E];
+    const int nunits = misc[2];
+    const int issued = misc[3];
     const uint32_t tmem = *tslot;
 
-    if (warp >= kEpiWarp0) {
-        // ---------------- gate_up's operand, while the first stages stream in ----------------
-        // every token's normalized row as five E2M1 terms per 32-element block, row
-        // 5 t + j of every K box; rows of absent tokens and K past H read as zero
-        // codes at unit scale
-        const int bt = tid - kEpiWarp0 * 32;
-        const float *xn_s = reinterpret_cast<const float *>(bd);
-        for (uint32_t o = 16u * (uint32_t)bt; o < (uint32_t)nkb1 * kBb; o += 16u * kBuildThreads)
-            *reinterpret_cast<uint4 *>(bx + o) =
-                o % kBb < kCb ? make_uint4(0u, 0u, 0u, 0u) : make_uint4(0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu, 0x7f7f7f7fu);
-        build_bar();
-        const int nblk = p.Hp / 32, total = 4 * p.T * nblk;  // four lanes per (token, 32-element block)
-        for (int base = (warp - kEpiWarp0) * 32; base < total; base += kBuildThreads) {  // whole warps
-            const int it = base + lane;
-            const bool live = it < total;
-            const int unit = it >> 2, sub = it & 3;
-            const int t = live ? unit / nblk : 0, blk = live ? unit - t * nblk : 0;
-            float x[8];
-#pragma unroll
-            for (int q = 0; q < 8; ++q) x[q] = live ? xn_s[(size_t)t * p.Hp + 32 * blk + 8 * sub + q] : 0.0f;
-            uint32_t codes[kTerms][1], sbyte[kTerms];
-            fp4::quantize<8, 4>(x, codes, sbyte);
-            if (live) put_terms(bx + (size_t)(blk >> 2) * kBb, kCb, t, blk & 3, sub, codes, sbyte);
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // read by the tensor core
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bxready);
-    }
-
     if (warp == kProdWarp) {
-        // ---------------- producer: refill each slot once its MMAs are done ----------------
+        // ---------------- producer: the rest of the stages, in order ----------------
         if (lane == 0) {
-            for (int j = R; j < nst; ++j)
-                if (!ring_wait(empty + j % R, ((j / R) - 1) & 1, misc, p.err, 51)) break;
-                else issue(j);
+            bool ok = true;
+            int j = 0;
+            for (int u = 0; u < nunits && ok; ++u) {
+                int phase, slot, mt, kpart, np, kb0, kb1, split;
+                unit_span(u, phase, slot, mt, kpart, np, kb0, kb1, split);
+                for (int kb = kb0; kb < kb1; kb += 2, ++j) {
+                    if (j < issued) continue;
+                    // the MMAs released stage j - R's slot
+                    if (j >= R && !ring_wait(empty + j % R, ((j / R) - 1) & 1, misc, p.err, 51)) {
+                        ok = false;
+                        break;
+                    }
+                    issue(j, u, kb);
+                }
+            }
             // copies in flight (only after a failed wait) land before the CTA exits
             for (int sl = 0; sl < R; ++sl)
                 if (rel_s[sl] >= 0) mbar_wait(full + sl, (rel_s[sl] / R) & 1, p.err, 54);
@@ -690,8 +668,8 @@ __launch_bounds__(kDecThreads, 1) __global__
         int i = 0, dn = 0, nbox = 0;
         bool ok = true, bx_ready = false;
         for (int u = 0; u < nunits && ok; ++u) {
-            int phase, slot, mt, kpart, kb0, kb1;
-            unit_span(units_s[u], phase, slot, mt, kpart, kb0, kb1);
+            int phase, slot, mt, kpart, np, kb0, kb1, split;
+            unit_span(u, phase, slot, mt, kpart, np, kb0, kb1, split);
             const int buf = u & 1, ub = dn & 1;
             if (phase == 0 && !bx_ready) {
                 if (!ring_wait(bxready, 0, misc, p.err, 50)) break;
@@ -738,14 +716,93 @@ __launch_bounds__(kDecThreads, 1) __global__
         if (elected) mma_commit(done);
         __syncwarp();
         mbar_wait(done, 0, p.err, 59);
+    } else if (warp == kRestWarp) {
+        // ---------------- the rest of the routing, off the critical path ----------------
+        // the softmax over each token's selected logits (moe.go:29-39): the k
+        // exponentials in parallel, the denominator summed in slot order
+        const float *lg_s = reinterpret_cast<const float *>(sm + lay.lg);
+        const int *tk_s = reinterpret_cast<const int *>(sm + lay.tk);
+        const uint32_t *amask_s = reinterpret_cast<const uint32_t *>(sm + lay.amask);
+        for (int t = 0; t < p.T; ++t) {
+            const int my_e = tk_s[t * p.k + (lane < p.k ? lane : 0)];
+            const double maxv = (double)lg_s[t * E + tk_s[t * p.k]];
+            const double ex_all = exp((double)lg_s[t * E + my_e] - maxv);
+            const double ex = lane < p.k ? ex_all : 0.0;
+            double den = 0.0;
+            for (int sl = 0; sl < p.k; ++sl) den += __shfl_sync(0xffffffffu, ex, sl);
+            if (lane < p.k) w_s[t * p.k + lane] = (float)((double)(float)ex / den);
+        }
+        // counts, offsets, the stable permutation and each pair's active slot
+        for (int e0 = 0; e0 <= E; e0 += 32)
+            if (e0 + lane <= E) offs_s[e0 + lane] = 0;
+        __syncwarp();
+        for (int q0 = 0; q0 < P; q0 += 32) {
+            const int q = q0 + lane;
+            if (q < P) atomicAdd(&offs_s[tk_s[q]], 1);
+        }
+        __syncwarp();
+        int c[8];  // warp scan over experts (lane owns experts 8 lane .. 8 lane + 7; E <= 256)
+        int cs = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = 8 * lane + j;
+            c[j] = e < E ? offs_s[e] : 0;
+            cs += c[j];
+        }
+        int cx = cs;  // inclusive warp prefix sum
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int cu = __shfl_up_sync(0xffffffffu, cx, o);
+            cx += lane >= o ? cu : 0;
+        }
+        int co = cx - cs;
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = 8 * lane + j;
+            if (e < E) offs_s[e] = co;
+            co += c[j];
+        }
+        if (lane == 31) offs_s[E] = cx;
+        __syncwarp();
+        for (int q0 = 0; q0 < P; q0 += 32) {  // pairs in (token, slot) order land stably
+            const int q = q0 + lane;
+            const int e = tk_s[q < P ? q : 0];
+            int pos = offs_s[e];
+            for (int r = 0; r < P; ++r) pos += (r < q) & (tk_s[r] == e);
+            int slot = __popc(amask_s[e >> 5] & ((1u << (e & 31)) - 1u));  // active experts below e
+#pragma unroll
+            for (int w = 0; w < 8; ++w) slot += w < (e >> 5) ? __popc(amask_s[w]) : 0;
+            if (q < P) {
+                perm_s[pos] = q;
+                inv_s[q] = pos;
+                sl_s[q] = slot;
+            }
+        }
+        __syncwarp();
+        if (blockIdx.x == 0) {  // the routing the C ABI reports
+            for (int q = lane; q < P; q += 32) {
+                p.route.topk_idx[q] = tk_s[q];
+                p.route.topk_w[q] = w_s[q];
+                p.route.perm_pair[q] = perm_s[q];
+                p.route.inv[q] = inv_s[q];
+            }
+            for (int e = lane; e <= E; e += 32) {
+                p.route.offsets[e] = offs_s[e];
+                p.route.active[e] = act_s[e];
+                if (e < E) p.route.counts[e] = offs_s[e + 1] - offs_s[e];
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(rdone);
     } else if (warp == kLoadWarp) {
         // ---------------- down operands: one bulk copy per unit once the slot is published ----------------
         if (lane == 0) {
             int dn = 0, last[2] = {-1, -1};
             bool bx_ready = false;
             for (int u = 0; u < nunits && !misc[0]; ++u) {
-                int phase, slot, mt, kpart, kb0, kb1;
-                unit_span(units_s[u], phase, slot, mt, kpart, kb0, kb1);
+                int phase, slot, mt, kpart, np, kb0, kb1, split;
+                unit_span(u, phase, slot, mt, kpart, np, kb0, kb1, split);
                 if (phase == 0) continue;
                 // bd holds the normalized tokens until gate_up's operand is built from them
                 if (!bx_ready && !ring_wait(bxready, 0, misc, p.err, 50)) break;
@@ -753,12 +810,12 @@ __launch_bounds__(kDecThreads, 1) __global__
                 const int ub = dn & 1;
                 if (dn >= 2 && !ring_wait(bempty + ub, ((dn >> 1) - 1) & 1, misc, p.err, 57)) break;
                 const long long t0 = clock64();
-                while ((int)(ld_acquire(p.aflag + slot) - epoch) < 0 && !misc[0]) {
+                // the slot's gate_up tiles all finished (spins: a sleep slows the warp after)
+                while (ld_acquire(p.cnt_gu + (epoch & 1u) * p.S + slot) < (unsigned)nmt1 && !misc[0]) {
                     if (clock64() - t0 > kWaitLimit) {
                         atomicCAS(p.err, 0, 52);
                         misc[0] = 1;
                     }
-                    __nanosleep(32);
                 }
                 if (misc[0]) break;
                 asm volatile("fence.proxy.async.global;" ::: "memory");  // generic stores of other CTAs -> bulk copy
@@ -771,22 +828,36 @@ __launch_bounds__(kDecThreads, 1) __global__
             for (int b = 0; b < 2; ++b)
                 if (last[b] >= 0) mbar_wait(bfull + b, (last[b] >> 1) & 1, p.err, 54);
         }
-    } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
+    } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4 * kEpiGroups) {
         // ---------------- unit epilogues (one thread per tile row; the same barriers on every path) ----------------
-        const int quad = warp & 3, row = quad * 32 + lane, et = tid - kEpiWarp0 * 32;
+        // group grp takes the units of accumulator grp (u = grp, grp + 2, ...), so two
+        // epilogues, each a chain of global round trips, run at once
+        const int grp = (warp - kEpiWarp0) >> 2;
+        const int quad = warp & 3, row = quad * 32 + lane, et = tid - (kEpiWarp0 + 4 * grp) * 32;
+        volatile int *gmisc = misc + 8 + grp;  // the group's unit was the last down unit of its output tile
+        float *actg = actst + grp * p.T * 64;
         // gate_up: rows 16 g + j (j < 8) hold the gate of pair 8 g + j, row + 8 its up row
         const int j16 = row & 15;
         const bool gate_lane = j16 < 8;
         const int pl = 8 * (row >> 4) + (j16 & 7);  // pair within the tile (0..63)
-        for (int u = 0; u < nunits; ++u) {
-            int phase, slot, mt, kpart, kb0, kb1;
-            unit_span(units_s[u], phase, slot, mt, kpart, kb0, kb1);
-            const int e = act_s[slot];
+        bool rdone_seen = false;
+        // this thread's bias of unit u: loaded a unit ahead, so its latency hides behind a whole unit
+        auto unit_bias = [&](int u) {
+            if (u >= nunits) return 0.0f;
+            int phase, slot, mt, kpart, np, kb0, kb1, split;
+            unit_span(u, phase, slot, mt, kpart, np, kb0, kb1, split);
+            const size_t e = (size_t)act_s[slot];
+            const int h = 128 * mt + row;
+            if (phase == 0) return __ldg(p.gu_b + e * 2 * p.I + 2 * (64 * mt + pl) + (gate_lane ? 0 : 1));
+            return kpart == 0 && h < p.H ? __ldg(p.dn_b + e * p.H + h) : 0.0f;
+        };
+        float bias_next = unit_bias(grp);
+        for (int u = grp; u < nunits; u += kEpiGroups) {
+            int phase, slot, mt, kpart, np, kb0, kb1, split;
+            unit_span(u, phase, slot, mt, kpart, np, kb0, kb1, split);
             const int buf = u & 1, h = 128 * mt + row;
-            // the bias first: its load overlaps the wait
-            float bias;
-            if (phase == 0) bias = __ldg(p.gu_b + (size_t)e * 2 * p.I + 2 * (64 * mt + pl) + (gate_lane ? 0 : 1));
-            else bias = kpart == 0 && h < p.H ? __ldg(p.dn_b + (size_t)e * p.H + h) : 0.0f;
+            const float bias = bias_next;
+            bias_next = unit_bias(u + kEpiGroups);
             float v[kDecodeMaxTokens] = {0.0f, 0.0f, 0.0f, 0.0f};
             if (ring_wait(accfull + buf, (u >> 1) & 1, misc, p.err, 58)) {
                 tc_fence_after();
@@ -803,25 +874,59 @@ __launch_bounds__(kDecThreads, 1) __global__
             }
             tc_fence_before();
             mbar_arrive(accempty + buf);
-            if (phase == 0) {
+            bool finish = true;  // this unit completes its tile (uniform over the epilogue threads)
+            if (phase == 0 && np > 1) {
+                // a tile cut between CTAs: pieces 1.. store their partial sums and count
+                // themselves in without waiting; piece 0, the end of an earlier CTA's range
+                // and so the last to run, waits for them and adds all in piece order
+                float *gp = p.gpart + (size_t)split * kMaxPieces * kDecodeMaxTokens * 128 + row;
+                unsigned *cs = p.cnt_split + (epoch & 1u) * G + split;
+                finish = kpart == 0;
+                if (!finish) {
+#pragma unroll
+                    for (int t = 0; t < kDecodeMaxTokens; ++t)
+                        if (t < p.T) gp[(kpart * kDecodeMaxTokens + t) * 128] = v[t];
+                    epi_bar(grp);  // every thread's partials before the release below
+                    if (et == 0) red_add_release(cs, 1u);
+                } else {
+                    if (et == 0) {
+                        const long long t0 = clock64();
+                        while (ld_acquire(cs) < (unsigned)np - 1u && !misc[0])
+                            if (clock64() - t0 > kWaitLimit) {
+                                atomicCAS(p.err, 0, 57);
+                                misc[0] = 1;
+                            }
+                    }
+                    epi_bar(grp);  // the acquire above orders the other pieces' partials before the reads
+#pragma unroll
+                    for (int t = 0; t < kDecodeMaxTokens; ++t) {
+                        if (t < p.T) {
+                            float sum = v[t];
+                            for (int pc = 1; pc < np; ++pc) sum += __ldcg(gp + (pc * kDecodeMaxTokens + t) * 128);
+                            v[t] = sum;
+                        }
+                    }
+                }
+            }
+            if (phase == 0 && finish) {
                 // SwiGLU of the tile's 64 pairs (partner lanes 8 apart swap values)
 #pragma unroll
                 for (int t = 0; t < kDecodeMaxTokens; ++t) {
                     if (t < p.T) {  // uniform
                         const float val = v[t] + bias;
                         const float other = __shfl_xor_sync(0xffffffffu, val, 8);
-                        if (gate_lane) actst[t * 64 + pl] = swiglu(val, other);
+                        if (gate_lane) actg[t * 64 + pl] = swiglu(val, other);
                     }
                 }
-                epi_bar();
-                if (warp == kEpiWarp0) {
+                epi_bar(grp);
+                if (quad == 0) {
                     // four lanes per (token, 32-pair block): the five E2M1 terms and their
                     // scales into down's operand, blocks 2 (mt % 2) + b of box mt / 2
                     const int unitq = lane >> 2, sub = lane & 3, t = unitq >> 1, b = unitq & 1;
                     const bool live = t < p.T;
                     float x[8];
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) x[q] = live ? actst[t * 64 + 32 * b + 8 * sub + q] : 0.0f;
+                    for (int q = 0; q < 8; ++q) x[q] = live ? actg[t * 64 + 32 * b + 8 * sub + q] : 0.0f;
                     uint32_t codes[kTerms][1], sbyte[kTerms];
                     fp4::quantize<8, 4>(x, codes, sbyte);
                     uint8_t *box = p.aq + ((size_t)slot * nkb2 + (mt >> 1)) * kBb;
@@ -836,30 +941,28 @@ __launch_bounds__(kDecThreads, 1) __global__
                         }
                     }
                     asm volatile("fence.proxy.async.global;" ::: "memory");  // read by other CTAs' bulk copies
-                    __threadfence();
                 }
-            } else {
+            } else if (phase == 1) {
                 if (h < p.H) {
                     float *yrow = p.yb + ((size_t)slot * 2 + kpart) * p.T * p.H + h;
 #pragma unroll
                     for (int t = 0; t < kDecodeMaxTokens; ++t)
                         if (t < p.T) yrow[(size_t)t * p.H] = v[t] + bias;
                 }
-                __threadfence();
             }
-            epi_bar();
-            if (et == 0) {
-                const unsigned n = phase == 0 ? (unsigned)nmt1 : (unsigned)(nkp * n_active);
-                unsigned *cnt = phase == 0 ? p.cnt_gu + slot : p.cnt_dn + mt;
-                const unsigned old = atomicInc(cnt, n - 1u);
-                misc[1] = old == n - 1u;
-                if (old == n - 1u && phase == 0) publish(p.aflag + slot, epoch);
+            epi_bar(grp);
+            // the barrier above orders every epilogue thread's stores before this thread's
+            // release; a down unit's acquire orders the other CTAs' outputs before the combine
+            if (et == 0 && finish && phase == 0) red_add_release(p.cnt_gu + (epoch & 1u) * p.S + slot, 1u);
+            if (et == 0 && phase == 1) {
+                const unsigned n = (unsigned)(nkp * n_active);
+                gmisc[0] = atom_inc_acq_rel(p.cnt_dn + mt, n - 1u) == n - 1u;
             }
-            epi_bar();
-            if (phase == 1 && misc[1]) {
+            epi_bar(grp);
+            if (phase == 1 && gmisc[0] && (rdone_seen || ring_wait(rdone, 0, misc, p.err, 50))) {
                 // the last down unit of output tile mt: combine its rows for every token in
                 // slot order (layer.go:109-121)
-                __threadfence();
+                rdone_seen = true;
                 for (int it = et; it < p.T * 128; it += kEpiThreads) {
                     const int t = it >> 7, hh = 128 * mt + (it & 127);
                     if (hh >= p.H) continue;
@@ -919,12 +1022,16 @@ int dec_slots(const Dims &d) { return d.E < kDecodeMaxTokens * d.k ? d.E : kDeco
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// The units of every CTA for each number of active slots n = 1..S: longest
-// processing time first over the units' box counts (all units of a phase are
-// the same size, so this is a balanced round over the least-loaded CTAs),
-// gate_up units before down units, each in slot order.  CTA b's rows sit in
-// words [b * kSchedWords, (b + 1) * kSchedWords): S + 1 offsets (relative to
-// the row start), then the unit lists for n = 1..S.
+// The units of every CTA for each number of active slots n = 1..S.  Down units
+// (one per output tile and K half) go first to the least-loaded CTAs; then the
+// gate_up boxes, in (slot, tile, K box) order, are cut into contiguous ranges so
+// that every CTA's total box count comes out even: CTA b takes the next
+// (target - its down boxes) boxes.  A tile whose range spans CTAs becomes pieces
+// (at most kMaxPieces) joined through a split index.  Within a CTA the gate_up
+// pieces run first.  CTA b's rows sit in words [b * kSchedWords, (b + 1) *
+// kSchedWords): S + 1 offsets (relative to the row start), then the unit lists for
+// n = 1..S, two words per unit.  Should a tile need more pieces than allowed, the
+// gate_up tiles of that n are placed whole, longest processing time first.
 struct Schedule {
     std::vector<int32_t> rows;   // [G][kSchedWords]
     int max_units = 0;           // most units of one CTA for one n
@@ -938,41 +1045,105 @@ Schedule build_schedule(const Dims &d, int G) {
     const int nmt1 = 2 * d.I / 128, nmt2 = (d.H + 127) / 128;
     const int nkp = nkb2 >= 2 ? 2 : 1, half2 = (nkb2 + 1) / 2;
     std::vector<std::vector<int32_t>> rows(G, std::vector<int32_t>(S + 1, 0));
-    std::vector<std::vector<int32_t>> lists(G);
-    std::vector<long long> load(G);
+    std::vector<std::vector<int32_t>> gu(G), dn(G);
+    std::vector<long long> load(G), quota(G);
     for (int b = 0; b < G; ++b) rows[b][0] = S + 1;
+    auto least = [&]() {
+        int best = 0;
+        for (int b = 1; b < G; ++b)
+            if (load[b] < load[best]) best = b;
+        return best;
+    };
+    auto push = [](std::vector<int32_t> &l, int32_t w0, int32_t w1) {
+        l.push_back(w0);
+        l.push_back(w1);
+    };
     for (int n = 1; n <= S; ++n) {
-        for (auto &l : lists) l.clear();
-        std::fill(load.begin(), load.end(), 0);
-        auto place = [&](int32_t code, int cost) {
-            int best = 0;
-            for (int b = 1; b < G; ++b)
-                if (load[b] < load[best]) best = b;
-            lists[best].push_back(code);
-            load[best] += cost;
-        };
-        for (int sl = 0; sl < n; ++sl)
-            for (int m = 0; m < nmt1; ++m) place(unit_code(0, sl, m, 0), nkb1);
+        for (int b = 0; b < G; ++b) {
+            gu[b].clear();
+            dn[b].clear();
+            load[b] = 0;
+        }
         for (int sl = 0; sl < n; ++sl)
             for (int m = 0; m < nmt2; ++m)
-                for (int kp = 0; kp < nkp; ++kp)
-                    place(unit_code(1, sl, m, kp), nkp == 1 ? nkb2 : (kp ? nkb2 - half2 : half2));
-        for (int b = 0; b < G; ++b) {
-            rows[b].insert(rows[b].end(), lists[b].begin(), lists[b].end());
-            rows[b][n] = (int32_t)rows[b].size();
-            s.max_units = std::max(s.max_units, (int)lists[b].size());
+                for (int kp = 0; kp < nkp; ++kp) {
+                    const int kb0 = kp ? half2 : 0, kb1 = nkp == 1 || kp ? nkb2 : half2;
+                    const int b = least();
+                    push(dn[b], unit_w0(1, sl, m, kp, nkp), unit_w1(kb0, kb1, 0));
+                    load[b] += kb1 - kb0;
+                }
+        // water level L: the smallest with sum max(0, L - load) >= the gate_up boxes;
+        // the surplus comes off the first CTAs that have a share
+        const long long gu_total = (long long)n * nmt1 * nkb1;
+        auto fill = [&](long long L) {
+            long long f = 0;
+            for (int c = 0; c < G; ++c) f += std::max(0LL, L - load[c]);
+            return f;
+        };
+        long long lo = 0, hi = gu_total + *std::max_element(load.begin(), load.end());
+        while (lo < hi) {
+            const long long mid = (lo + hi) / 2;
+            if (fill(mid) >= gu_total) hi = mid;
+            else lo = mid + 1;
+        }
+        long long surplus = fill(lo) - gu_total;
+        for (int c = 0; c < G; ++c) {
+            quota[c] = std::max(0LL, lo - load[c]);
+            if (surplus > 0 && quota[c] > 0) {
+                --quota[c];
+                --surplus;
+            }
+        }
+        int b = 0, nsplit = 0;
+        long long rem = quota[0];
+        bool ok = true;
+        for (int sl = 0; sl < n && ok; ++sl)
+            for (int m = 0; m < nmt1 && ok; ++m) {
+                int cta[kMaxPieces + 1], k0[kMaxPieces + 1], k1[kMaxPieces + 1], np = 0;
+                for (int kb = 0; kb < nkb1;) {
+                    while (rem == 0 && b < G - 1) rem = quota[++b];
+                    const int take = rem == 0 ? nkb1 - kb : (int)std::min<long long>(rem, nkb1 - kb);  // the last CTA takes any rest
+                    if (np == kMaxPieces) {
+                        ok = false;
+                        break;
+                    }
+                    cta[np] = b;
+                    k0[np] = kb;
+                    k1[np] = kb + take;
+                    ++np;
+                    kb += take;
+                    rem -= std::min<long long>(rem, take);
+                }
+                if (!ok) break;
+                const int split = np > 1 ? nsplit++ : 0;
+                for (int pc = 0; pc < np; ++pc) push(gu[cta[pc]], unit_w0(0, sl, m, pc, np), unit_w1(k0[pc], k1[pc], split));
+            }
+        if (!ok || nsplit >= G) {
+            for (int c = 0; c < G; ++c) gu[c].clear();
+            for (int sl = 0; sl < n; ++sl)
+                for (int m = 0; m < nmt1; ++m) {
+                    const int c = least();
+                    push(gu[c], unit_w0(0, sl, m, 0, 1), unit_w1(0, nkb1, 0));
+                    load[c] += nkb1;
+                }
+        }
+        for (int c = 0; c < G; ++c) {
+            rows[c].insert(rows[c].end(), gu[c].begin(), gu[c].end());
+            rows[c].insert(rows[c].end(), dn[c].begin(), dn[c].end());
+            rows[c][n] = (int32_t)rows[c].size();
+            s.max_units = std::max(s.max_units, (int)(gu[c].size() + dn[c].size()) / 2);
         }
     }
     s.rows.assign((size_t)G * kSchedWords, 0);
-    for (int b = 0; b < G; ++b) {
-        s.max_words = std::max(s.max_words, (int)rows[b].size());
-        std::copy_n(rows[b].begin(), std::min<size_t>(rows[b].size(), kSchedWords), s.rows.begin() + (size_t)b * kSchedWords);
+    for (int c = 0; c < G; ++c) {
+        s.max_words = std::max(s.max_words, (int)rows[c].size());
+        std::copy_n(rows[c].begin(), std::min<size_t>(rows[c].size(), kSchedWords), s.rows.begin() + (size_t)c * kSchedWords);
     }
     return s;
 }
 
 struct DecScratch {
-    size_t aq, yb, cnt_gu, cnt_dn, aflag, rcnt, sched, total;
+    size_t aq, yb, cnt_gu, cnt_dn, rcnt, gpart, cnt_split, sched, total;
 };
 
 DecScratch dec_scratch(const Dims &d, int G, const Schedule &s) {
@@ -984,13 +1155,15 @@ DecScratch dec_scratch(const Dims &d, int G, const Schedule &s) {
     L.yb = o;
     o += align256((size_t)S * 2 * kDecodeMaxTokens * d.H * 4);
     L.cnt_gu = o;
-    o += align256((size_t)S * 4);
+    o += align256((size_t)2 * S * 4);
     L.cnt_dn = o;
     o += align256((size_t)nmt2 * 4);
-    L.aflag = o;
-    o += align256((size_t)S * 4);
     L.rcnt = o;
     o += align256(2 * 4);
+    L.gpart = o;
+    o += align256((size_t)G * kMaxPieces * kDecodeMaxTokens * 128 * 4);
+    L.cnt_split = o;
+    o += align256((size_t)2 * G * 4);
     L.sched = o;
     o += align256(s.rows.size() * 4);
     L.total = o;
@@ -1067,8 +1240,9 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
     p.aq = b + lay.aq;
     p.yb = reinterpret_cast<float *>(b + lay.yb);
     p.cnt_gu = reinterpret_cast<uint32_t *>(b + lay.cnt_gu);
+    p.gpart = reinterpret_cast<float *>(b + lay.gpart);
+    p.cnt_split = reinterpret_cast<uint32_t *>(b + lay.cnt_split);
     p.cnt_dn = reinterpret_cast<uint32_t *>(b + lay.cnt_dn);
-    p.aflag = reinterpret_cast<unsigned *>(b + lay.aflag);
     p.sched = reinterpret_cast<const int32_t *>(b + lay.sched);
     p.bar = bar;
     p.err = err;
@@ -1083,9 +1257,16 @@ cudaError_t launch_decode(const Dims &d, const LayerDev &L, const RouteOut &r, c
     p.stages = dec_stages(T, Hp, Ip, d.E, d.k);
     if (p.stages < kMinStages) return cudaErrorInvalidValue;
     const size_t smem = dec_layout(T, Hp, Ip, d.E, d.k, p.stages, ncol).total;
-    auto kern = ncol == 8 ? decode_kernel<8> : (ncol == 16 ? decode_kernel<16> : decode_kernel<32>);
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+    const int var = ncol == 8 ? 0 : (ncol == 16 ? 1 : 2);
+    auto kern = var == 0 ? decode_kernel<8> : (var == 1 ? decode_kernel<16> : decode_kernel<32>);
+    // the shared-memory ceiling once per device and variant (a driver call on every
+    // step would sit between the step's start and its launch)
+    static thread_local bool attr_set[64][3] = {};
+    if (!attr_set[device][var]) {
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBudget);
+        if (e != cudaSuccess) return e;
+        attr_set[device][var] = true;
+    }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(G);
     cfg.blockDim = dim3(kDecThreads);
