@@ -919,29 +919,33 @@ __launch_bounds__(kDecThreads, 1) __global__
                     }
                 }
                 epi_bar(grp);
-                if (quad == 0) {
-                    // four lanes per (token, 32-pair block): the five E2M1 terms and their
-                    // scales into down's operand, blocks 2 (mt % 2) + b of box mt / 2
-                    const int unitq = lane >> 2, sub = lane & 3, t = unitq >> 1, b = unitq & 1;
-                    const bool live = t < p.T;
-                    float x[8];
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) x[q] = live ? actg[t * 64 + 32 * b + 8 * sub + q] : 0.0f;
+                if (quad < p.T) {  // warp t: token t (uniform per warp)
+                    // sixteen lanes per (token, 32-pair block), two pairs each (the terms are a
+                    // dependent chain: fewer elements a lane shorten it): the five E2M1 terms
+                    // and their scales into down's operand, blocks 2 (mt % 2) + b of box mt / 2
+                    const int t = quad, b = lane >> 4, sub = lane & 15, jb = 2 * (mt & 1) + b;
+                    float x[2] = {actg[t * 64 + 32 * b + 2 * sub], actg[t * 64 + 32 * b + 2 * sub + 1]};
                     uint32_t codes[kTerms][1], sbyte[kTerms];
-                    fp4::quantize<8, 4>(x, codes, sbyte);
+                    fp4::quantize<2, 16>(x, codes, sbyte);
                     uint8_t *box = p.aq + ((size_t)slot * nkb2 + (mt >> 1)) * kBb;
-                    if (live) put_terms(box, kCb, t, 2 * (mt & 1) + b, sub, codes, sbyte);
-                    if (mt == nmt1 - 1 && (mt & 1) == 0) {
-                        // K past I (blocks 2 and 3 of the last box): zero codes at unit scale
-                        for (int q = lane; q < 2 * NCOL; q += 32) {
-                            const int n = q >> 1, jz = 2 + (q & 1);
-                            *reinterpret_cast<uint4 *>(box + n * 64 + ((jz ^ ((n >> 1) & 3)) << 4)) =
-                                make_uint4(0u, 0u, 0u, 0u);
-                            box[kCb + n * 16 + jz] = 127;
-                        }
+#pragma unroll
+                    for (int j = 0; j < kTerms; ++j) {
+                        const int n = kTerms * t + j;
+                        box[n * 64 + ((jb ^ ((n >> 1) & 3)) << 4) + sub] = (uint8_t)codes[j][0];
+                        if (sub == j) box[kCb + n * 16 + jb] = (uint8_t)sbyte[j];
                     }
-                    asm volatile("fence.proxy.async.global;" ::: "memory");  // read by other CTAs' bulk copies
                 }
+                if (quad == 0 && mt == nmt1 - 1 && (mt & 1) == 0) {
+                    // K past I (blocks 2 and 3 of the last box): zero codes at unit scale
+                    uint8_t *box = p.aq + ((size_t)slot * nkb2 + (mt >> 1)) * kBb;
+                    for (int q = lane; q < 2 * NCOL; q += 32) {
+                        const int n = q >> 1, jz = 2 + (q & 1);
+                        *reinterpret_cast<uint4 *>(box + n * 64 + ((jz ^ ((n >> 1) & 3)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+                        box[kCb + n * 16 + jz] = 127;
+                    }
+                }
+                if (quad < p.T || quad == 0)
+                    asm volatile("fence.proxy.async.global;" ::: "memory");  // read by other CTAs' bulk copies
             } else if (phase == 1) {
                 if (h < p.H) {
                     float *yrow = p.yb + ((size_t)slot * 2 + kpart) * p.T * p.H + h;

@@ -68,11 +68,14 @@ __device__ __forceinline__ uint32_t clear_negative_zero(uint32_t w) {
 // The terms of one block of 32 elements held as N elements by each of L
 // consecutive lanes (N * L == 32; lanes xor-reducible, all 32 lanes of the warp
 // call it).  codes[j][w]: term j, elements 8w..8w+7 of this lane's part (low
-// nibble first); sbyte[j]: term j's E8M0 byte.  r is consumed (left holding the
-// final remainder).
+// nibble first; with N < 8 the word holds the lane's N codes); sbyte[j]: term j's
+// E8M0 byte.  r is consumed (left holding the final remainder).  The terms form one
+// dependent chain, so fewer elements per lane (more lanes per block) shorten it.
 template <int N, int L>
-__device__ __forceinline__ void quantize(float (&r)[N], uint32_t (&codes)[kTerms][N / 8], uint32_t (&sbyte)[kTerms]) {
-    static_assert(N * L == 32 && N % 8 == 0 && (N & (N - 1)) == 0, "a block is 32 elements in words of eight codes");
+__device__ __forceinline__ void quantize(float (&r)[N], uint32_t (&codes)[kTerms][(N + 7) / 8],
+                                         uint32_t (&sbyte)[kTerms]) {
+    static_assert(N * L == 32 && N % 2 == 0 && (N & (N - 1)) == 0, "a block is 32 elements, two codes a byte");
+    constexpr int kWords = (N + 7) / 8, kPairs = N < 8 ? N / 2 : 4;  // code words, byte pairs per word
     bool bad = false;
 #pragma unroll
     for (int i = 0; i < N; ++i) bad |= !isfinite(r[i]);
@@ -94,10 +97,10 @@ __device__ __forceinline__ void quantize(float (&r)[N], uint32_t (&codes)[kTerms
         sbyte[j] = (bad && j == 0) ? 0xffu : (uint32_t)(e + 127);
         const float inv = pow2(-e), s = pow2(e);
 #pragma unroll
-        for (int w = 0; w < N / 8; ++w) {
+        for (int w = 0; w < kWords; ++w) {
             uint32_t word = 0;
 #pragma unroll
-            for (int b = 0; b < 4; ++b) {
+            for (int b = 0; b < kPairs; ++b) {
                 float &x0 = r[8 * w + 2 * b], &x1 = r[8 * w + 2 * b + 1];
                 const uint32_t byte = bad ? 0u : e2m1x2(x0 * inv, x1 * inv);
                 const float2 q = e2m1x2_value(byte);

@@ -1,8 +1,8 @@
 // Runs the device quantizer of airllm_b200/csrc/fp4_terms.cuh (5 block-scaled
-// E2M1 terms) over a file of float32 values, with one lane per 32-element
-// block (L = 1) and with two lanes per block (L = 2), and writes the codes
+// E2M1 terms) over a file of float32 values with L = 1, 2, 4 and 16 lanes per
+// 32-element block (the layouts the kernels use), and writes the codes
 // [terms][n/2] and scale bytes [terms][n/32] of each mode in the layout of
-// oracle_e2m1_terms.  Usage: fp4_terms_check in.f32 out_l1.bin out_l2.bin
+// oracle_e2m1_terms.  Usage: fp4_terms_check in.f32 out_l1 out_l2 out_l4 out_l16
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -22,13 +22,13 @@ __global__ void run(const float *x, long long nb, uint8_t *codes, uint8_t *scale
     const bool live = blk < nb;  // every lane of the warp runs quantize (shuffles)
     float r[N];
     for (int i = 0; i < N; ++i) r[i] = live ? x[blk * 32 + part * N + i] : 0.0f;
-    uint32_t c[fp4::kTerms][N / 8], s[fp4::kTerms];
+    uint32_t c[fp4::kTerms][(N + 7) / 8], s[fp4::kTerms];
     fp4::quantize<N, L>(r, c, s);
     if (!live) return;
     const long long n = nb * 32;
     for (int j = 0; j < fp4::kTerms; ++j) {
-        uint32_t *dst = reinterpret_cast<uint32_t *>(codes + j * (n / 2) + blk * 16 + part * (N / 2));
-        for (int w = 0; w < N / 8; ++w) dst[w] = c[j][w];
+        uint8_t *dst = codes + j * (n / 2) + blk * 16 + part * (N / 2);
+        for (int b = 0; b < N / 2; ++b) dst[b] = (uint8_t)(c[j][b / 4] >> (8 * (b % 4)));
         if (part == 0) scales[j * nb + blk] = (uint8_t)s[j];
     }
 }
@@ -43,8 +43,8 @@ __global__ void run(const float *x, long long nb, uint8_t *codes, uint8_t *scale
     } while (0)
 
 int main(int argc, char **argv) {
-    if (argc != 4) {
-        printf("usage: fp4_terms_check in.f32 out_l1.bin out_l2.bin\n");
+    if (argc != 6) {
+        printf("usage: fp4_terms_check in.f32 out_l1 out_l2 out_l4 out_l16\n");
         return 1;
     }
     FILE *f = fopen(argv[1], "rb");
@@ -64,13 +64,17 @@ int main(int argc, char **argv) {
     CK(cudaMalloc(&ds, sbytes));
     CK(cudaMemcpy(dx, x.data(), n * 4, cudaMemcpyHostToDevice));
     std::vector<uint8_t> out(cbytes + sbytes);
-    for (int mode = 1; mode <= 2; ++mode) {
+    const int lanes[4] = {1, 2, 4, 16};
+    for (int mode = 1; mode <= 4; ++mode) {
         CK(cudaMemset(dc, 0xAA, cbytes));
         CK(cudaMemset(ds, 0xAA, sbytes));
-        const long long threads = nb * mode;
+        const int L = lanes[mode - 1];
+        const long long threads = nb * L;
         const int grid = (int)((threads + 127) / 128);
-        if (mode == 1) run<1><<<grid, 128>>>(dx, nb, dc, ds);
-        else run<2><<<grid, 128>>>(dx, nb, dc, ds);
+        if (L == 1) run<1><<<grid, 128>>>(dx, nb, dc, ds);
+        else if (L == 2) run<2><<<grid, 128>>>(dx, nb, dc, ds);
+        else if (L == 4) run<4><<<grid, 128>>>(dx, nb, dc, ds);
+        else run<16><<<grid, 128>>>(dx, nb, dc, ds);
         CK(cudaGetLastError());
         CK(cudaDeviceSynchronize());
         CK(cudaMemcpy(out.data(), dc, cbytes, cudaMemcpyDeviceToHost));

@@ -1,8 +1,7 @@
 """The device quantizer of the FP4 expert GEMMs (airllm_b200/csrc/fp4_terms.cuh:
 five block-scaled E2M1 terms per value) against its CPU definition,
-oracle_e2m1_terms, byte for byte: codes and E8M0 scale bytes, with one lane per
-32-element block and with two lanes sharing a block (the two layouts the GEMM
-kernels use).  Inputs cover many binades, exact ties on the E2M1 grid, negative
+oracle_e2m1_terms, byte for byte: codes and E8M0 scale bytes, with 1, 2, 4 and 16
+lanes sharing a 32-element block (the layouts the kernels use).  Inputs cover many binades, exact ties on the E2M1 grid, negative
 values that round to zero (code 0, never the negative zero 8), all-zero and
 subnormal blocks and the scale threshold at 6 * 2^e.  A block holding a NaN or an
 infinity gets the E8M0 NaN scale on its first term (tests/cuda/fp4_terms_check.cu)."""
@@ -17,6 +16,7 @@ import oracle
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(os.path.dirname(HERE), "airllm_b200", "csrc")
 TERMS = 5
+LANES = (1, 2, 4, 16)
 
 
 @pytest.fixture(scope="module")
@@ -51,7 +51,7 @@ def _inputs():
 def _run(checker, tmp_path, x):
     src = tmp_path / "x.f32"
     x.astype(np.float32).tofile(src)
-    outs = [tmp_path / "l1.bin", tmp_path / "l2.bin"]
+    outs = [tmp_path / f"l{lanes}.bin" for lanes in LANES]
     p = subprocess.run([checker, str(src), *map(str, outs)], capture_output=True, text=True, timeout=120)
     assert p.returncode == 0, p.stdout + p.stderr
     n = x.size
@@ -66,7 +66,7 @@ def _run(checker, tmp_path, x):
 def test_device_terms_equal_the_cpu_definition_byte_for_byte(cuda_device, checker, tmp_path):
     x = _inputs()
     want_codes, want_scales = oracle.e2m1_terms(x, TERMS)
-    for lanes, (codes, scales) in zip((1, 2), _run(checker, tmp_path, x)):
+    for lanes, (codes, scales) in zip(LANES, _run(checker, tmp_path, x)):
         bad_c = np.nonzero((codes != want_codes).any(axis=0))[0]
         bad_s = np.nonzero((scales != want_scales).any(axis=0))[0]
         assert not len(bad_s), f"{lanes} lane(s): scale bytes differ in blocks {bad_s[:8]}"
