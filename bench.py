@@ -409,7 +409,7 @@ def algorithmic(T: int, layer, idx, stage: str, pairs=None, active=None):
 def kernel_name(stage: str, path: int) -> str:
     if stage == "decode_experts":
         return ("decode_kernel (one cooperative launch: routing + gate_up + down + combine; packed MXFP4 boxes "
-                "expanded in registers, mma.sync with fp16 hi/lo activation columns)")
+                "bulk-copied into tcgen05 kind::mxf4 MMAs, M=128, tokens as 5-term E2M1 columns)")
     return {1: "gemv_kernel (mma.sync MXFP4)",
             2: "bs_gemm_kernel (tcgen05 kind::mxf4 block-scaled, CTA pairs: E2M1 weights x 5-term E2M1 activations)"}[path or 1]
 
