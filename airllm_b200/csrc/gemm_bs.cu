@@ -77,7 +77,7 @@ constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 448
 constexpr int kGroupTok = kTok / kEpiGroups;      // tokens per epilogue warp: 16
 constexpr uint32_t kSfCol = 2 * kN;               // TMEM column of scale-factor slot 0 (slot 1: +16)
 constexpr int kActPitch = 68;                     // gate_up staging: [48 tokens][64 pairs] f32, padded rows
-constexpr uint32_t kOutStage = kTok * kActPitch * 4;
+constexpr uint32_t kOutStage = (kTok * kActPitch + 16 * (kTok / 8 - 1)) * 4;
 constexpr size_t kSmem = 1024 + kStages * kStageBytes + kOutStage + 32 * 8 + 16;
 
 static_assert(kN % 16 == 0 && kN <= 256, "MMA N for M = 256");
@@ -217,6 +217,11 @@ __global__ void __launch_bounds__(kTok * 4) bs_quant_kernel(const __half *__rest
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
 
+// Row of token `tok` in the gate_up staging.  Each group of 8 tokens starts 16 floats
+// further on, so tokens 8 apart (stored by one instruction: gate lanes token c, up
+// lanes token c + 8, each over 16 consecutive pairs) fall in different banks.
+__device__ __forceinline__ int act_at(int tok) { return tok * kActPitch + (tok >> 3) * 16; }
+
 // GPT-OSS clamped SwiGLU (primitives.go:144-146; NaN propagates) with the fast
 // exponential and division: the result is carried by five E2M1 terms right
 // after (about 2^-12 of its block maximum), far coarser than their error.
@@ -283,7 +288,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *ring = sm;
     float *act_s = reinterpret_cast<float *>(ring + kStages * kStageBytes);  // gate_up SwiGLU outputs
-    uint64_t *full = reinterpret_cast<uint64_t *>(act_s + kTok * kActPitch);
+    uint64_t *full = reinterpret_cast<uint64_t *>(act_s + kOutStage / 4);
     uint64_t *empty = full + kStages;
     uint64_t *accfull = empty + kStages;  // [2]
     uint64_t *accempty = accfull + 2;     // [2] (the leader's counts both CTAs' epilogues)
@@ -455,16 +460,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 }
                 continue;
             }
-            // gate_up: partner lanes (8 apart) swap values; the gate lane finishes the first
-            // half of the tokens, the up lane the second half
+            // gate_up: the gate lane finishes the first half of the warp's tokens, its
+            // partner (the up lane, 8 apart) the second half; one exchange per token pair
+            // hands each the partner's value it needs, so no lane idles in a SwiGLU
 #pragma unroll
-            for (int c = 0; c < kGroupTok; ++c) {
-                const float val = v[c] + bias;
-                const float other = __shfl_xor_sync(0xffffffffu, val, 8);
-                const bool mine = gate_lane ? c < kGroupTok / 2 : c >= kGroupTok / 2;
-                if (mine)
-                    act_s[(c0 + c) * kActPitch + pl] =
-                        c < nc ? swiglu_fast(gate_lane ? val : other, gate_lane ? other : val) : 0.0f;
+            for (int c = 0; c < kGroupTok / 2; ++c) {
+                const float lo = v[c] + bias, hi = v[c + kGroupTok / 2] + bias;
+                const float got = __shfl_xor_sync(0xffffffffu, gate_lane ? hi : lo, 8);
+                const int cc = gate_lane ? c : c + kGroupTok / 2;
+                const float a = swiglu_fast(gate_lane ? lo : got, gate_lane ? got : hi);
+                act_s[act_at(c0 + cc) + pl] = cc < nc ? a : 0.0f;
             }
             epi_bar();
             // four threads per (token, 32-pair block), 8 pairs each: five E2M1 terms and
@@ -473,10 +478,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const int unit = et >> 2, sub = et & 3;
                 const int c = unit >> 1, b = unit & 1;
                 const bool live = real;  // every lane takes part in the shuffles inside quantize
-                const float4 *src = reinterpret_cast<const float4 *>(act_s + c * kActPitch + 32 * b + 8 * sub);
+                const float4 *src = reinterpret_cast<const float4 *>(act_s + act_at(c) + 32 * b + 8 * sub);
                 float x[8];
+                // block 1 reads its two halves in the other order: the eight threads of one
+                // shared-memory phase (a token's two blocks) then hit 32 different banks
 #pragma unroll
-                for (int q = 0; q < 2; ++q) {
+                for (int q0 = 0; q0 < 2; ++q0) {
+                    const int q = q0 ^ b;
                     const float4 f = live ? src[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                     x[4 * q] = f.x;
                     x[4 * q + 1] = f.y;
