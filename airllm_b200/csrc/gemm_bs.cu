@@ -269,8 +269,12 @@ __device__ __forceinline__ void umma_pair(uint32_t d, uint64_t a, uint64_t b, ui
 __device__ __forceinline__ void commit_pair(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
+// Frees an accumulator: the arrive follows tcgen05.wait::ld (the TMEM reads are
+// complete) and tcgen05.fence::before_thread_sync.  It is relaxed: a release would
+// first wait until this thread's global stores of the previous item are visible
+// at cluster scope, and nothing the MMA warp does next depends on them.
 __device__ __forceinline__ void arrive_remote(uint32_t bar) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 // Instruction descriptor, kind::mxf4 block-scaled, the pair (M = 256): A and B
 // E2M1, K-major, E8M0 scales; sf_id is the first of the two scale bytes (32-element
