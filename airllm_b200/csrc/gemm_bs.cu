@@ -39,11 +39,18 @@
 // accumulator rows in its own TMEM.
 //
 // Work item = (token tile, 256-row weight pair), clusters striding over items.
-// Roles per CTA: warp 0 TMA producer, warp 1 MMA issuer (leader) and TMEM owner,
-// warps 2-13 epilogue (three per TMEM lane quadrant, each with a third of the
-// tile's tokens).  TMEM: two 240-column accumulators (the epilogue of one item overlaps
-// the next item's MMAs) and two 12-column scale-factor slots used alternately.  Every wait is
-// bounded; on timeout the kernel records a code in the error flag and winds down.
+// Roles per CTA (16 warps): warp 0 TMA producer, warp 1 MMA issuer (leader) and TMEM
+// owner.  down: warps 2-13, three groups of four (one warp per TMEM lane quadrant),
+// each group reading a third of the tile's tokens from TMEM and storing the outputs.
+// gate_up runs a pipeline instead: warps 12-15 (one per quadrant) read the
+// accumulator 8 tokens at a time, apply bias and SwiGLU, and fill a ring of three
+// 16-token slots (chunks) in shared memory; two groups of four quantizer warps
+// (warps 2-5 and 6-9) take alternate chunks and write down's B operand.  The
+// quantization of one item thus overlaps the SwiGLU of the next, and both overlap
+// the MMAs.  TMEM: two
+// 240-column accumulators (the epilogue of one item overlaps the next item's MMAs)
+// and two 12-column scale-factor slots used alternately.  Every wait is bounded; on
+// timeout the kernel records a code in the error flag and winds down.
 #include "fp4_terms.cuh"
 #include "tc_ptx.cuh"
 
@@ -70,14 +77,19 @@ constexpr uint32_t kStageBytes = kStageA + kBoxes * kBPart;   // 34 KB
 constexpr int kStages = 6;
 constexpr uint32_t kCopyRow = 512;                // TMA row width: both copies of a stage are whole rows
 constexpr int kProdWarp = 0, kMmaWarp = 1, kEpiWarp0 = 2;
-constexpr int kEpiGroups = 3;                     // epilogue warps per TMEM lane quadrant
+constexpr int kEpiGroups = 3;                     // down: warps 2-13, groups of one warp per TMEM lane quadrant
 constexpr int kEpiWarps = 4 * kEpiGroups;
 constexpr int kEpiThreads = kEpiWarps * 32;
-constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 448
-constexpr int kGroupTok = kTok / kEpiGroups;      // tokens per epilogue warp: 16
+constexpr int kSwiWarp0 = 12;                     // gate_up: warps 12-15 read the accumulators
+constexpr int kSwiThreads = 4 * 32;
+constexpr int kQuantGroups = 2;                   // gate_up: warps 2-5 and 6-9 quantize alternate chunks
+constexpr int kThreads = 16 * 32;
+constexpr int kGroupTok = kTok / kEpiGroups;      // tokens per group (down) and per chunk (gate_up): 16
+constexpr int kSlots = kTok / kGroupTok;          // gate_up staging ring: one slot per chunk of an item
 constexpr uint32_t kSfCol = 2 * kN;               // TMEM column of scale-factor slot 0 (slot 1: +16)
-constexpr int kActPitch = 68;                     // gate_up staging: [48 tokens][64 pairs] f32, padded rows
-constexpr uint32_t kOutStage = (kTok * kActPitch + 16 * (kTok / 8 - 1)) * 4;
+constexpr int kActPitch = 68;                     // a slot: [16 tokens][64 pairs] f32, padded rows
+constexpr int kSlotFloats = kGroupTok * kActPitch;
+constexpr uint32_t kOutStage = kSlots * kSlotFloats * 4;
 constexpr size_t kSmem = 1024 + kStages * kStageBytes + kOutStage + 32 * 8 + 16;
 
 static_assert(kN % 16 == 0 && kN <= 256, "MMA N for M = 256");
@@ -85,8 +97,11 @@ static_assert(kStageA % 1024 == 0 && kStageBytes % 1024 == 0 && kBoxStride % 512
               "64-byte swizzle atoms start on 512 B");
 static_assert(kSfCol + 16 + 12 <= 512, "TMEM budget");
 static_assert(kSmem <= 232448, "shared memory budget");
-static_assert(kGroupTok * kTerms == 80, "an epilogue warp reads 80 TMEM columns (tmem_ld80)");
-static_assert(kEpiThreads == 4 * 2 * kTok, "four lanes per (token, 32-pair block) in the gate_up quantization");
+static_assert(kGroupTok == 16, "a down warp reads its tokens from TMEM as two halves of 8 (tmem_ld40)");
+static_assert(kThreads == (kEpiWarp0 + kEpiWarps + 2) * 32 && kSwiWarp0 % 4 == 0 &&
+              kEpiWarp0 + 4 * kQuantGroups <= kSwiWarp0, "warp roles");
+static_assert(4 * 32 == 4 * 2 * kGroupTok, "a quantizer group: four lanes per (token, 32-pair block) of a chunk");
+static_assert(kActPitch % 32 == 4, "tokens 4 apart (one SwiGLU store) fall 16 banks apart");
 static_assert(kBoxStride % kCopyRow == 0 && kBPart % kCopyRow == 0 && kHalfRows % 8 == 0, "copies of whole rows");
 constexpr uint32_t kARows = (uint32_t)kBoxStride / kCopyRow, kBRows = kBPart / kCopyRow;
 
@@ -215,12 +230,6 @@ __global__ void __launch_bounds__(kTok * 4) bs_quant_kernel(const __half *__rest
     }
 }
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
-
-// Row of token `tok` in the gate_up staging.  Each group of 8 tokens starts 16 floats
-// further on, so tokens 8 apart (stored by one instruction: gate lanes token c, up
-// lanes token c + 8, each over 16 consecutive pairs) fall in different banks.
-__device__ __forceinline__ int act_at(int tok) { return tok * kActPitch + (tok >> 3) * 16; }
 
 // GPT-OSS clamped SwiGLU (primitives.go:144-146; NaN propagates) with the fast
 // exponential and division: the result is carried by five E2M1 terms right
@@ -254,8 +263,8 @@ __device__ __forceinline__ void tma_pair(uint32_t dst, const CUtensorMap *tm, ui
         "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(bar)
         : "memory");
 }
-__device__ __forceinline__ void sf_copy_pair(uint32_t tmem_col, uint32_t saddr) {
-    asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(tmem_col), "l"(desc_sf(saddr)) : "memory");
+__device__ __forceinline__ void sf_copy_pair(uint32_t tmem_col, uint64_t desc) {
+    asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(tmem_col), "l"(desc) : "memory");
 }
 __device__ __forceinline__ void umma_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc, uint32_t sfa,
                                           uint32_t sfb) {
@@ -296,7 +305,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint64_t *empty = full + kStages;
     uint64_t *accfull = empty + kStages;  // [2]
     uint64_t *accempty = accfull + 2;     // [2] (the leader's counts both CTAs' epilogues)
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accempty + 2);
+    uint64_t *slot_full = accempty + 2;   // [kSlots] gate_up staging ring
+    uint64_t *slot_empty = slot_full + kSlots;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(slot_empty + kSlots);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t rank = cta_rank();
@@ -310,7 +321,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(accfull + b, 1);
-            mbar_init(accempty + b, 2 * kEpiThreads);
+            mbar_init(accempty + b, 2 * (p.gate_up ? kSwiThreads : kEpiThreads));
+        }
+        for (int k = 0; k < kSlots; ++k) {
+            mbar_init(slot_full + k, 4);   // lane 0 of each accumulator reader
+            mbar_init(slot_empty + k, 4);  // lane 0 of each warp of the quantizer group
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -327,27 +342,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
     if (warp == kProdWarp) {
         // ---------------- TMA producer (both CTAs; one thread, stages in order) ----------------
+        // The two control warps share their SM sub-partitions with busy epilogue warps,
+        // so their loops keep few instructions per stage: addresses advance by constants,
+        // and the next item's expert id is loaded an item ahead.
         if (lane == 0) {
             const uint32_t ring_a = smem_u32(ring);
-            int i = 0;
-            bool ok = true;
+            const int nkb2 = (p.nkb + 1) >> 1;
+            int s = 0;
+            uint32_t ph = 0;  // parity of the ring's current pass
+            bool ok = true, first = true;
+            int e_next = cl < items ? p.tiles[cl / nmp].x : 0;
             for (int w = cl; w < items && ok; w += ncl) {
                 const int t = w / nmp, mp = w - t * nmp;
                 const int m = 2 * mp + (int)rank;  // m == nmt: no such tile (odd nmt); its rows are not stored
-                const int e = p.tiles[t].x;
-                for (int kb = 0; kb < p.nkb; kb += kBoxes, ++i) {
-                    const int s = i % kStages, nb = min(kBoxes, p.nkb - kb);
-                    if (i >= kStages && !mbar_wait(empty + s, ((i / kStages) - 1) & 1, p.err, 40)) {
+                const int e = e_next;
+                if (w + ncl < items) e_next = p.tiles[(w + ncl) / nmp].x;
+                int arow = (e * p.nmt + m) * p.nkb * (int)kARows;  // the stage's first A box, in copy rows
+                int brow = (int)bpart_index(t, 0, (int)rank, nkb2) * (int)kBRows;
+                for (int kb = 0; kb < p.nkb; kb += kBoxes) {
+                    const bool two = kb + 1 < p.nkb;
+                    if (!first && !mbar_wait(empty + s, ph ^ 1u, p.err, 40)) {
                         ok = false;
                         break;
                     }
                     const uint32_t st = ring_a + (uint32_t)s * kStageBytes;
-                    if (rank == 0) mbar_expect_tx(full + s, 2u * (uint32_t)nb * ((uint32_t)kBoxStride + kBPart));
-                    const int box = (e * p.nmt + m) * p.nkb + kb;  // first of the stage's boxes in the plane
-                    const int part = (int)bpart_index(t, kb, (int)rank, (p.nkb + 1) >> 1);
                     const uint32_t bar = lead_full + 8u * (uint32_t)s;
-                    tma_pair(st, nb == 2 ? &tm_a2 : &tm_a1, bar, 0, box * (int)kARows);
-                    tma_pair(st + kStageA, nb == 2 ? &tm_b2 : &tm_b1, bar, 0, part * (int)kBRows);
+                    if (rank == 0) mbar_expect_tx(full + s, two ? 4u * (kBoxStride + kBPart) : 2u * (kBoxStride + kBPart));
+                    tma_pair(st, two ? &tm_a2 : &tm_a1, bar, 0, arow);
+                    tma_pair(st + kStageA, two ? &tm_b2 : &tm_b1, bar, 0, brow);
+                    arow += kBoxes * (int)kARows;
+                    brow += 2 * kBoxes * (int)kBRows;  // the other CTA's parts sit between
+                    if (++s == kStages) {
+                        s = 0;
+                        ph ^= 1u;
+                        first = false;
+                    }
                 }
             }
         }
@@ -358,155 +387,219 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t elected;
             asm volatile("{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}" : "=r"(elected));
             const uint32_t idesc0 = idesc_pair(0, kN), idesc1 = idesc_pair(2, kN);
+            // stage s, box b: the descriptors of stage 0 box 0 plus the start-address field
+            // (bits 0-13, 16-byte units; shared addresses stay below 256 KB, so no carry)
             const uint32_t ring_a = smem_u32(ring);
-            const uint32_t empty0 = smem_u32(empty), accfull0 = smem_u32(accfull);
-            int i = 0, it = 0;
+            const uint64_t da = desc_sw64(ring_a), db = desc_sw64(ring_a + kStageA);
+            const uint64_t sa = desc_sf(ring_a + kABytes), sb = desc_sf(ring_a + kStageA + kBHalf);
+            const uint32_t sf0 = tmem + kSfCol, sf1 = sf0 + 16u;  // the boxes of a stage alternate slots
+            const uint32_t empty_l = peer_addr(smem_u32(empty), 0), empty_r = peer_addr(smem_u32(empty), 1);
+            const uint32_t accfull_l = peer_addr(smem_u32(accfull), 0), accfull_r = peer_addr(smem_u32(accfull), 1);
+            int s = 0;
+            uint32_t ph = 0;
+            int it = 0;
             bool ok = true;
             for (int w = cl; w < items && ok; w += ncl, ++it) {
                 const int buf = it & 1;
                 if (!mbar_wait(accempty + buf, ((it >> 1) & 1) ^ 1, p.err, 41)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(buf * kN);
-                for (int kb = 0; kb < p.nkb; kb += kBoxes, ++i) {
-                    const int s = i % kStages, nb = min(kBoxes, p.nkb - kb);
+                for (int kb = 0; kb < p.nkb; kb += kBoxes) {
                     // tcgen05.cp and tcgen05.mma issued by this thread execute in issue order,
                     // so a scale-factor slot is rewritten only after the MMAs that read it
-                    if (!mbar_wait(full + s, (i / kStages) & 1, p.err, 42)) {
+                    if (!mbar_wait(full + s, ph, p.err, 42)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t st = ring_a + (uint32_t)s * kStageBytes;
                     if (elected) {
-                        for (int b = 0; b < nb; ++b) {
-                            const uint32_t a = st + (uint32_t)b * (uint32_t)kBoxStride, bb = st + kStageA + b * kBPart;
-                            const uint32_t sf = tmem + kSfCol + 16u * (uint32_t)((kb + b) & 1);
-                            sf_copy_pair(sf, a + kABytes);              // A scales (each CTA its 128 rows)
-                            sf_copy_pair(sf + 4, bb + kBHalf);          // B scales, rows 0-127 (both CTAs)
-                            sf_copy_pair(sf + 8, bb + kBHalf + 512);    // rows 128-239
-                            umma_pair(d, desc_sw64(a), desc_sw64(bb), idesc0, (kb + b) ? 1u : 0u, sf, sf + 4);
-                            umma_pair(d, desc_sw64(a + 32), desc_sw64(bb + 32), idesc1, 1u, sf, sf + 4);
+                        const uint64_t so = (uint64_t)((uint32_t)s * (kStageBytes >> 4));
+                        const uint64_t a0 = da + so, b0 = db + so, fa = sa + so, fb = sb + so;
+                        sf_copy_pair(sf0, fa);                        // A scales (each CTA its 128 rows)
+                        sf_copy_pair(sf0 + 4, fb);                    // B scales, rows 0-127 (both CTAs)
+                        sf_copy_pair(sf0 + 8, fb + (512 >> 4));       // rows 128-239
+                        umma_pair(d, a0, b0, idesc0, kb ? 1u : 0u, sf0, sf0 + 4);
+                        umma_pair(d, a0 + 2, b0 + 2, idesc1, 1u, sf0, sf0 + 4);
+                        if (kb + 1 < p.nkb) {
+                            constexpr uint32_t oa = kBoxStride >> 4, ob = kBPart >> 4;
+                            sf_copy_pair(sf1, fa + oa);
+                            sf_copy_pair(sf1 + 4, fb + ob);
+                            sf_copy_pair(sf1 + 8, fb + ob + (512 >> 4));
+                            umma_pair(d, a0 + oa, b0 + ob, idesc0, 1u, sf1, sf1 + 4);
+                            umma_pair(d, a0 + oa + 2, b0 + ob + 2, idesc1, 1u, sf1, sf1 + 4);
                         }
-                        const uint32_t eb = empty0 + 8u * (uint32_t)s;
-                        commit_pair(peer_addr(eb, 0));
-                        commit_pair(peer_addr(eb, 1));
+                        commit_pair(empty_l + 8u * (uint32_t)s);
+                        commit_pair(empty_r + 8u * (uint32_t)s);
                     }
                     __syncwarp();
+                    if (++s == kStages) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
                 }
                 if (!ok) break;
                 if (elected) {
-                    commit_pair(peer_addr(accfull0 + 8u * (uint32_t)buf, 0));
-                    commit_pair(peer_addr(accfull0 + 8u * (uint32_t)buf, 1));
+                    commit_pair(accfull_l + 8u * (uint32_t)buf);
+                    commit_pair(accfull_r + 8u * (uint32_t)buf);
                 }
                 __syncwarp();
             }
         }
-    } else {
-        // ---------------- epilogue (warps 2-13 of both CTAs; TMEM lane quadrant = warp % 4) ----------------
+    } else if (!p.gate_up ? warp < kEpiWarp0 + kEpiWarps : warp < kEpiWarp0 + 4 * kQuantGroups) {
+        // ---------------- down's epilogue (warps 2-13), gate_up's quantizers (warps 2-9) ----------------
         const int quad = warp & 3;
         const int row = quad * 32 + lane;  // row of this CTA's 128-row weight tile
         const int et = tid - kEpiWarp0 * 32;
-        const int c0 = (et >> 7) * kGroupTok;  // this warp's tokens: c0 .. c0 + kGroupTok - 1
+        const int g = et >> 7;             // group: down's tokens 16g.., gate_up's chunk parity
+        if (!p.gate_up) {
+            const uint32_t lead_accempty = peer_addr(smem_u32(accempty), 0);
+            // an item's tile and this thread's bias, loaded one item ahead (global latency
+            // would otherwise sit in every item)
+            auto item_tile = [&](int w) { return w < items ? p.tiles[w / nmp] : make_int4(0, 0, 0, 0); };
+            auto item_bias = [&](int w, const int4 &ti) {
+                if (w >= items) return 0.0f;
+                const int h = 128 * (2 * (w % nmp) + (int)rank) + row;
+                return h < p.R ? __ldg(p.bias + (size_t)ti.x * p.R + h) : 0.0f;
+            };
+            const int c0 = g * kGroupTok;
+            int4 ti_next = item_tile(cl);
+            float bias_next = item_bias(cl, ti_next);
+            int it = 0;
+            for (int w = cl; w < items; w += ncl, ++it) {
+                const int m = 2 * (w % nmp) + (int)rank;
+                const int4 ti = ti_next;
+                const float bias = bias_next;
+                const int buf = it & 1;
+                if (!mbar_wait(accfull + buf, (it >> 1) & 1, p.err, 44)) break;
+                tc_fence_after();
+                const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * kN + kTerms * c0);
+                float a[2][8 * kTerms];  // this warp's columns, two halves of 8 tokens: five terms per token
+                tmem_ld40(ta, a[0]);
+                tmem_ld40(ta + 8u * kTerms, a[1]);
+                tc_fence_before();
+                arrive_remote(lead_accempty + 8u * (uint32_t)buf);
+                ti_next = item_tile(w + ncl);
+                bias_next = item_bias(w + ncl, ti_next);
+                const int nc = min(kGroupTok, ti.z - c0);
+                const int h = 128 * m + row;  // m == nmt (no such tile) gives h >= R
+                if (h < p.R) {
+#pragma unroll
+                    for (int c = 0; c < kGroupTok; ++c) {
+                        float sum = 0.0f;
+#pragma unroll
+                        for (int j = 0; j < kTerms; ++j) sum += a[c >> 3][kTerms * (c & 7) + j];
+                        if (c < nc) ep_out_row(p.y, p.y_rows, p.ret, ti.y + c0 + c, p.R)[h] = sum + bias;
+                    }
+                }
+            }
+        } else {
+            // gate_up: chunk q = 3 (item) + k (slot k, tokens 16k..) goes to group q % 2.
+            // Four threads per (token, 32-pair block), 8 pairs each: five E2M1 terms and
+            // their scales into down's B operand (pairs 64 (m % 2).. of box m / 2).  Block 1
+            // reads its two halves in the other order: the eight threads of one
+            // shared-memory phase (a token's two blocks) then hit 32 different banks.
+            const int ut = et & 127, unit = ut >> 2, sub = ut & 3;
+            const int c = unit >> 1, b = unit & 1;
+            const int onkb2 = (p.onkb + 1) >> 1;
+            int it = 0, k = g;  // this group's first chunk: slot g of item 0
+            for (int w = cl; w < items;) {
+                const int t = w / nmp;
+                const int m = 2 * (w - t * nmp) + (int)rank;
+                const bool live = m < p.nmt;  // every lane takes part in the shuffles inside quantize
+                const int c0 = k * kGroupTok;
+                const float4 *src =
+                    reinterpret_cast<const float4 *>(act_s + k * kSlotFloats + c * kActPitch + 32 * b + 8 * sub);
+                if (!mbar_wait(slot_full + k, it & 1, p.err, 47)) break;
+                const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                const float4 f0 = live ? src[b] : z, f1 = live ? src[b ^ 1] : z;
+                const float4 lo = b ? f1 : f0, hi = b ? f0 : f1;
+                float x[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+                __syncwarp();
+                if (lane == 0) mbar_arrive(slot_empty + k);  // a release: the warp's reads of the slot are done
+                uint32_t codes[kTerms][1], sbyte[kTerms];
+                fp4::quantize<8, 4>(x, codes, sbyte);
+                const int jb = 2 * (m & 1) + b, n0 = kTerms * (c0 + c);
+                if (live) {
+#pragma unroll
+                    for (int term = 0; term < kTerms; ++term) {
+                        put_codes<4>(p.oq, t, m >> 1, onkb2, n0 + term, jb, sub, codes[term]);
+                        if (term % 4 == sub) put_scale(p.oq, t, m >> 1, onkb2, n0 + term, jb, sbyte[term]);
+                    }
+                }
+                k += kQuantGroups;  // the group's next chunk
+                for (; k >= kSlots; k -= kSlots) {
+                    w += ncl;
+                    ++it;
+                }
+            }
+        }
+    } else if (p.gate_up && warp >= kSwiWarp0) {
+        // ---------------- warps 12-15 (gate_up): accumulator -> bias, SwiGLU -> the slots ----------------
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;
         const uint32_t lead_accempty = peer_addr(smem_u32(accempty), 0);
-        // gate_up: rows 16g + j (j < 8) hold the gate of pair 8g + j, row + 8 its up row
+        // rows 16g + j (j < 8) hold the gate of pair 8g + j, row + 8 its up row
         const int j16 = row & 15;
         const bool gate_lane = j16 < 8;
         const int pl = 8 * (row >> 4) + (j16 & 7);  // pair within this tile (0..63)
-        // an item's tile and this thread's bias, loaded one item ahead (global latency
-        // would otherwise sit in every item)
         auto item_tile = [&](int w) { return w < items ? p.tiles[w / nmp] : make_int4(0, 0, 0, 0); };
         auto item_bias = [&](int w, const int4 &ti) {
             if (w >= items) return 0.0f;
             const int m = 2 * (w % nmp) + (int)rank;
             if (m >= p.nmt) return 0.0f;
-            if (!p.gate_up) return 128 * m + row < p.R ? __ldg(p.bias + (size_t)ti.x * p.R + 128 * m + row) : 0.0f;
             return __ldg(p.bias + (size_t)ti.x * p.R + 2 * (64 * m + pl) + (gate_lane ? 0 : 1));
         };
         int4 ti_next = item_tile(cl);
         float bias_next = item_bias(cl, ti_next);
         int it = 0;
         bool ok = true;
-        for (int w = cl; w < items; w += ncl, ++it) {
-            const int t = w / nmp, mp = w - t * nmp;
-            const int m = 2 * mp + (int)rank;
-            const bool real = m < p.nmt;  // an odd nmt leaves the last pair's second tile empty
+        for (int w = cl; w < items && ok; w += ncl, ++it) {
             const int4 ti = ti_next;
             const float bias = bias_next;
             const int buf = it & 1;
-            float v[kGroupTok];
-#pragma unroll
-            for (int c = 0; c < kGroupTok; ++c) v[c] = 0.0f;
-            if (ok) ok = mbar_wait(accfull + buf, (it >> 1) & 1, p.err, 44);
-            if (ok) {
-                tc_fence_after();
-                const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * kN + kTerms * c0);
-                float a[kGroupTok * kTerms];  // this warp's columns: five terms per token
-                tmem_ld80(ta, a);
-                tc_fence_before();
-                arrive_remote(lead_accempty + 8u * (uint32_t)buf);
-#pragma unroll
-                for (int c = 0; c < kGroupTok; ++c) {
-                    float sum = 0.0f;
-#pragma unroll
-                    for (int j = 0; j < kTerms; ++j) sum += a[kTerms * c + j];
-                    v[c] = sum;
-                }
-            }
+            if (!mbar_wait(accfull + buf, (it >> 1) & 1, p.err, 44)) break;
+            tc_fence_after();
             ti_next = item_tile(w + ncl);
             bias_next = item_bias(w + ncl, ti_next);
-            const int nc = min(kGroupTok, ti.z - c0);
-            if (!p.gate_up) {
-                const int h = 128 * m + row;
-                if (ok && h < p.R) {
-#pragma unroll
-                    for (int c = 0; c < kGroupTok; ++c)
-                        if (c < nc) ep_out_row(p.y, p.y_rows, p.ret, ti.y + c0 + c, p.R)[h] = v[c] + bias;
+            const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * kN);
+            for (int k = 0; k < kSlots; ++k) {
+                if (it > 0 && !mbar_wait(slot_empty + k, (it - 1) & 1, p.err, 48)) {
+                    ok = false;
+                    break;
                 }
-                continue;
-            }
-            // gate_up: the gate lane finishes the first half of the warp's tokens, its
-            // partner (the up lane, 8 apart) the second half; one exchange per token pair
-            // hands each the partner's value it needs, so no lane idles in a SwiGLU
+                float *slot = act_s + k * kSlotFloats;
 #pragma unroll
-            for (int c = 0; c < kGroupTok / 2; ++c) {
-                const float lo = v[c] + bias, hi = v[c + kGroupTok / 2] + bias;
-                const float got = __shfl_xor_sync(0xffffffffu, gate_lane ? hi : lo, 8);
-                const int cc = gate_lane ? c : c + kGroupTok / 2;
-                const float a = swiglu_fast(gate_lane ? lo : got, gate_lane ? got : hi);
-                act_s[act_at(c0 + cc) + pl] = cc < nc ? a : 0.0f;
-            }
-            epi_bar();
-            // four threads per (token, 32-pair block), 8 pairs each: five E2M1 terms and
-            // their scales into down's B operand (pairs 64 (m % 2).. of box m / 2)
-            {
-                const int unit = et >> 2, sub = et & 3;
-                const int c = unit >> 1, b = unit & 1;
-                const bool live = real;  // every lane takes part in the shuffles inside quantize
-                const float4 *src = reinterpret_cast<const float4 *>(act_s + act_at(c) + 32 * b + 8 * sub);
-                float x[8];
-                // block 1 reads its two halves in the other order: the eight threads of one
-                // shared-memory phase (a token's two blocks) then hit 32 different banks
+                for (int hf = 0; hf < 2; ++hf) {
+                    const int tok0 = kGroupTok * k + 8 * hf;  // first of this half's 8 tokens
+                    float a[8 * kTerms];
+                    tmem_ld40(ta + (uint32_t)(kTerms * tok0), a);
+                    if (k == kSlots - 1 && hf == 1) {  // the item's last columns are read
+                        tc_fence_before();
+                        arrive_remote(lead_accempty + 8u * (uint32_t)buf);
+                    }
+                    float v[8];
 #pragma unroll
-                for (int q0 = 0; q0 < 2; ++q0) {
-                    const int q = q0 ^ b;
-                    const float4 f = live ? src[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    x[4 * q] = f.x;
-                    x[4 * q + 1] = f.y;
-                    x[4 * q + 2] = f.z;
-                    x[4 * q + 3] = f.w;
-                }
-                uint32_t codes[kTerms][1], sbyte[kTerms];
-                fp4::quantize<8, 4>(x, codes, sbyte);
-                const int jb = 2 * (m & 1) + b, onkb2 = (p.onkb + 1) >> 1;
-                if (live) {
+                    for (int c = 0; c < 8; ++c) {
+                        float sum = 0.0f;
 #pragma unroll
-                    for (int term = 0; term < kTerms; ++term) {
-                        put_codes<4>(p.oq, t, m >> 1, onkb2, kTerms * c + term, jb, sub, codes[term]);
-                        if (term % 4 == sub) put_scale(p.oq, t, m >> 1, onkb2, kTerms * c + term, jb, sbyte[term]);
+                        for (int j = 0; j < kTerms; ++j) sum += a[kTerms * c + j];
+                        v[c] = sum + bias;
+                    }
+                    // the gate lane finishes tokens 0-3 of the half, its partner (the up lane,
+                    // 8 lanes away) tokens 4-7: one exchange per token pair hands each lane the
+                    // partner's value it needs
+                    const int nc = ti.z - tok0;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const float got = __shfl_xor_sync(0xffffffffu, gate_lane ? v[c + 4] : v[c], 8);
+                        const int cc = gate_lane ? c : c + 4;
+                        const float r = swiglu_fast(gate_lane ? v[c] : got, gate_lane ? got : v[c + 4]);
+                        slot[(8 * hf + cc) * kActPitch + pl] = cc < nc ? r : 0.0f;
                     }
                 }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(slot_full + k);  // a release: the warp's slot stores
             }
-            epi_bar();  // act_s is rewritten by the next item
         }
     }
     tc_fence_before();
