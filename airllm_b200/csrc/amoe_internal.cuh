@@ -178,19 +178,18 @@ cudaError_t launch_gemv_down(const Dims &d, const LayerDev &L, const GemvRows &r
 bool tc_supported();
 // Block-scaled grouped GEMMs (gemm_bs.cu): gate_up(+SwiGLU) and down over
 // expert-sorted rows.  Rows come from (x_hi, x_lo) [*][H] through perm (position
-// -> pair id, token = pair / k) or, with perm NULL, by position; rows_cap bounds
-// the positions.  Outputs go to y[y_rows ? y_rows[pos] : pos][H] (with ret: the
-// source rank's y, see EpReturn).  scratch: bs_scratch_bytes(), prepared once by
-// init_bs_scratch().
-size_t bs_scratch_bytes(int rows_cap, int E, int H, int I);
-cudaError_t init_bs_scratch(void *scratch, int rows_cap, int E, int H, int I);
+// -> pair id, token = pair / k; `tokens` rows, each quantized once) or, with perm
+// NULL, by position; rows_cap bounds the positions, tok_cap the tokens.  Outputs
+// go to y[y_rows ? y_rows[pos] : pos][H] (with ret: the source rank's y, see
+// EpReturn).  scratch: bs_scratch_bytes(), prepared once by init_bs_scratch().
+size_t bs_scratch_bytes(int rows_cap, int tok_cap, int E, int H, int I);
+cudaError_t init_bs_scratch(void *scratch, int rows_cap, int tok_cap, int E, int H, int I);
 // scratch_e: the expert count the scratch was sized for (bs_scratch_bytes), >= d.E.
 cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *offsets, const __half *x_hi,
-                              const __half *x_lo, const int32_t *perm, int rows_cap, void *scratch, int scratch_e,
-                              float *y,
-                              const int32_t *y_rows, int32_t *err, cudaStream_t st, StageHook hook, void *hook_arg,
-                              int *launches, const EpReturn *ret = nullptr, const int32_t *gate = nullptr,
-                              int gate_want = 0);
+                              const __half *x_lo, const int32_t *perm, int tokens, int rows_cap, int tok_cap,
+                              void *scratch, int scratch_e, float *y, const int32_t *y_rows, int32_t *err,
+                              cudaStream_t st, StageHook hook, void *hook_arg, int *launches,
+                              const EpReturn *ret = nullptr, const int32_t *gate = nullptr, int gate_want = 0);
 // Combine --------------------------------------------------------------------
 cudaError_t launch_combine(const Dims &d, const float *residual, const RouteOut &r,
                            const float *y, int T, float *out, cudaStream_t st);

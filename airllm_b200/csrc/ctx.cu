@@ -287,7 +287,7 @@ int alloc_scratch(amoe_ctx *c) {
         {(void **)&c->act_lo, A * d.I * 2},
         {(void **)&c->y, P * d.H * 4},
         {(void **)&c->err_flag, 16},
-        {(void **)&c->bs_scratch, bs_scratch_bytes((int)A, c->dx.E, d.H, d.I)},
+        {(void **)&c->bs_scratch, bs_scratch_bytes((int)A, (int)T, c->dx.E, d.H, d.I)},
         {(void **)&c->dec_bar, sizeof(DecodeBarrier)},
         {(void **)&c->dec_scratch, decode_scratch_bytes(d, c->cfg.device)},
         {(void **)&c->io_in, T * d.H * 4},
@@ -317,7 +317,7 @@ int alloc_scratch(amoe_ctx *c) {
     AMOE_CUDA(c, cudaMemset(c->arrivals, 0, (size_t)c->nchunk_max * 4));
     AMOE_CUDA(c, cudaMemset(c->dec_bar, 0, sizeof(DecodeBarrier)));
     AMOE_CUDA(c, init_decode_scratch(d, c->cfg.device, c->dec_scratch, nullptr));
-    AMOE_CUDA(c, init_bs_scratch(c->bs_scratch, (int)A, c->dx.E, d.H, d.I));
+    AMOE_CUDA(c, init_bs_scratch(c->bs_scratch, (int)A, (int)T, c->dx.E, d.H, d.I));
     AMOE_CUDA(c, cudaDeviceSynchronize());
     AMOE_CUDA(c, cudaMemset(c->err_flag, 0, sizeof(int32_t)));
     if (R) {
@@ -634,8 +634,9 @@ int ep_experts(amoe_ctx *c, const LayerDev &L, const RouteOut &r, int T, int nch
     *used_tc = run_tc && (a.path == 2 || (long long)N * T * d.k >= 32LL * d.E);  // stats guess
     if (run_tc) {
         int n = 0;
-        AMOE_CUDA(c, launch_bs_experts(c->dx, L, c->ep_m.offsets_loc, rh, rl, nullptr, (int)c->r_max, c->bs_scratch,
-                                       c->dx.E, y_own, c->ep_m.y_rows, flag, st, &timer_hook, &timer, &n, &ret, gate, 1));
+        AMOE_CUDA(c, launch_bs_experts(c->dx, L, c->ep_m.offsets_loc, rh, rl, nullptr, 0, (int)c->r_max,
+                                       c->max_tokens, c->bs_scratch, c->dx.E, y_own, c->ep_m.y_rows, flag, st,
+                                       &timer_hook, &timer, &n, &ret, gate, 1));
         c->stats.launches += n;
     }
     if (run_gemv) {
@@ -731,9 +732,9 @@ int forward_selected(amoe_ctx *c, int32_t layer, const float *residual, int32_t 
     const Dims dx{d.H, d.I, c->xs, d.k, d.eps};
     LayerDev Lx = layer_view(c->xslot, x);
     int launches = 0;
-    AMOE_CUDA(c, launch_bs_experts(dx, Lx, rs.offsets, r.x_hi, r.x_lo, r.perm_pair, c->max_tokens * d.k,
-                                   c->bs_scratch, c->dx.E, c->y, nullptr, c->err_flag, st, &timer_hook, &timer,
-                                   &launches));
+    AMOE_CUDA(c, launch_bs_experts(dx, Lx, rs.offsets, r.x_hi, r.x_lo, r.perm_pair, T, c->max_tokens * d.k,
+                                   c->max_tokens, c->bs_scratch, c->dx.E, c->y, nullptr, c->err_flag, st, &timer_hook,
+                                   &timer, &launches));
     c->stats.launches += launches;
     AMOE_CUDA(c, launch_combine(d, residual, r, c->y, T, out, st));
     timer.mark(4);
@@ -804,8 +805,9 @@ int forward_impl(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, f
         }
         int n = 0;
         int32_t *flag = c->err_flag;
-        AMOE_CUDA(c, launch_bs_experts(d, L, r.offsets, r.x_hi, r.x_lo, r.perm_pair, c->max_tokens * d.k,
-                                       c->bs_scratch, c->dx.E, c->y, nullptr, flag, st, &timer_hook, &timer, &n));
+        AMOE_CUDA(c, launch_bs_experts(d, L, r.offsets, r.x_hi, r.x_lo, r.perm_pair, T, c->max_tokens * d.k,
+                                       c->max_tokens, c->bs_scratch, c->dx.E, c->y, nullptr, flag, st, &timer_hook,
+                                       &timer, &n));
         c->stats.launches += n;
     } else {
         timer.mark(1);

@@ -187,6 +187,82 @@ __global__ void __launch_bounds__(256) bs_plan_kernel(const int32_t *__restrict_
 // block).  Rows are the fp16 hi + lo split of the normalized tokens, gathered
 // through the permutation (or, with perm NULL, already by position).  Tokens past
 // the tile's count and elements past K are zeros.
+// Token-major quantized rows (single-GPU prefill, where each token feeds k pairs):
+// record (token, K box kb, 32-element block jb) = the five 16-byte code words of
+// the block (80 B at tq + 80 r) and its five E8M0 bytes (at ts + 8 r, 3 bytes
+// unused), r = (token * nkb + kb) * 4 + jb.  One thread per record; elements past
+// K quantize as zeros, exactly as bs_quant_kernel treats them.
+__global__ void __launch_bounds__(256) tok_quant_kernel(const __half *__restrict__ x_hi,
+                                                        const __half *__restrict__ x_lo, int tokens, int K,
+                                                        int nkb, uint4 *tq, uint2 *ts) {
+    const size_t r = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= (size_t)tokens * nkb * 4) return;
+    const int jb = (int)(r & 3);
+    const size_t tk = r >> 2;
+    const int tok = (int)(tk / nkb), kb = (int)(tk - (size_t)tok * nkb);
+    const int k0 = kb * 128 + jb * 32;
+    float x[32];
+    if (k0 < K) {
+        const uint4 *h = reinterpret_cast<const uint4 *>(x_hi + (size_t)tok * K + k0);
+        const uint4 *l = reinterpret_cast<const uint4 *>(x_lo + (size_t)tok * K + k0);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint4 hv = __ldg(h + c), lv = __ldg(l + c);
+            const __half2 *hh = reinterpret_cast<const __half2 *>(&hv);
+            const __half2 *ll = reinterpret_cast<const __half2 *>(&lv);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float2 a = __half22float2(hh[q]), b = __half22float2(ll[q]);
+                x[8 * c + 2 * q] = a.x + b.x;
+                x[8 * c + 2 * q + 1] = a.y + b.y;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) x[j] = 0.0f;
+    }
+    uint32_t codes[kTerms][4], sbyte[kTerms];
+    fp4::quantize<32, 1>(x, codes, sbyte);
+#pragma unroll
+    for (int term = 0; term < kTerms; ++term)
+        tq[r * kTerms + term] = make_uint4(codes[term][0], codes[term][1], codes[term][2], codes[term][3]);
+    static_assert(kTerms == 5, "five scale bytes in one 8-byte word");
+    ts[r] = make_uint2(sbyte[0] | sbyte[1] << 8 | sbyte[2] << 16 | sbyte[3] << 24, sbyte[4]);
+}
+
+// The gate_up B operand from the token-major records: one CTA per (tile, K box),
+// one thread per (token, 32-element block), the token found through the
+// permutation.  Tokens past the tile's count get zero codes with a unit scale,
+// as quantized zeros do.
+__global__ void __launch_bounds__(kTok * 4) bs_gather_kernel(const uint4 *__restrict__ tq,
+                                                             const uint2 *__restrict__ ts,
+                                                             const int32_t *__restrict__ perm, int k, int nkb,
+                                                             const int4 *__restrict__ tiles, const int32_t *ntiles,
+                                                             uint8_t *bq) {
+    const int t = blockIdx.x / nkb, kb = blockIdx.x - t * nkb;
+    if (t >= *ntiles) return;  // uniform over the CTA
+    const int4 ti = tiles[t];
+    const int i = threadIdx.x >> 2, jb = threadIdx.x & 3;
+    uint4 w[kTerms];
+    uint2 sc = make_uint2(0x7f7f7f7fu, 0x7fu);
+    if (i < ti.z) {
+        const size_t r = ((size_t)(perm[ti.y + i] / k) * nkb + kb) * 4 + jb;
+#pragma unroll
+        for (int term = 0; term < kTerms; ++term) w[term] = __ldg(tq + r * kTerms + term);
+        sc = __ldg(ts + r);
+    } else {
+#pragma unroll
+        for (int term = 0; term < kTerms; ++term) w[term] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    const int nkb2 = (nkb + 1) >> 1;
+#pragma unroll
+    for (int term = 0; term < kTerms; ++term) {
+        const uint32_t words[4] = {w[term].x, w[term].y, w[term].z, w[term].w};
+        put_codes<16>(bq, t, kb, nkb2, kTerms * i + term, jb, 0, words);
+        put_scale(bq, t, kb, nkb2, kTerms * i + term, jb, term < 4 ? (sc.x >> (8 * term)) & 0xffu : sc.y & 0xffu);
+    }
+}
+
 __global__ void __launch_bounds__(kTok * 4) bs_quant_kernel(const __half *__restrict__ x_hi,
                                                             const __half *__restrict__ x_lo,
                                                             const int32_t *__restrict__ perm, int k, int K, int nkb,
@@ -623,6 +699,8 @@ struct BsScratch {
     int32_t *ntiles;
     uint8_t *xq;  // gate_up's B operand (the quantized tokens)
     uint8_t *aq;  // down's B operand (the quantized activations)
+    uint4 *tq;    // token-major quantized rows (tok_quant_kernel), tok_cap tokens
+    uint2 *ts;
     int max_tiles;
 };
 
@@ -630,7 +708,7 @@ inline size_t up1k(size_t v) { return (v + 1023) & ~size_t(1023); }
 // B operand bytes of `tiles` tiles of nkb K boxes (boxes rounded up to pairs, two parts each).
 inline size_t b_bytes(size_t tiles, size_t nkb) { return tiles * ((nkb + 1) / 2) * 2 * kBoxes * kBPart; }
 
-BsScratch carve_bs(void *base, int rows_cap, int E, int H, int I) {
+BsScratch carve_bs(void *base, int rows_cap, int tok_cap, int E, int H, int I) {
     BsScratch s{};
     s.max_tiles = (rows_cap + kTok - 1) / kTok + E;
     const size_t nkb_gu = kpad128(H) / 128, nkb_dn = kpad128(I) / 128;
@@ -645,6 +723,8 @@ BsScratch carve_bs(void *base, int rows_cap, int E, int H, int I) {
     s.ntiles = reinterpret_cast<int32_t *>(take(16));
     s.xq = take(b_bytes(s.max_tiles, nkb_gu));
     s.aq = take(b_bytes(s.max_tiles, nkb_dn));
+    s.tq = reinterpret_cast<uint4 *>(take((size_t)tok_cap * nkb_gu * 4 * kTerms * 16));
+    s.ts = reinterpret_cast<uint2 *>(take((size_t)tok_cap * nkb_gu * 4 * 8));
     return s;
 }
 
@@ -663,16 +743,17 @@ bool tc_supported() {
     return known[dev] == 1;
 }
 
-size_t bs_scratch_bytes(int rows_cap, int E, int H, int I) {
+size_t bs_scratch_bytes(int rows_cap, int tok_cap, int E, int H, int I) {
     const size_t max_tiles = (size_t)(rows_cap + kTok - 1) / kTok + E;
     const size_t nkb_gu = kpad128(H) / 128, nkb_dn = kpad128(I) / 128;
-    return up1k(max_tiles * sizeof(int4)) + 1024 + up1k(b_bytes(max_tiles, nkb_gu)) + up1k(b_bytes(max_tiles, nkb_dn));
+    return up1k(max_tiles * sizeof(int4)) + 1024 + up1k(b_bytes(max_tiles, nkb_gu)) + up1k(b_bytes(max_tiles, nkb_dn)) +
+           up1k((size_t)tok_cap * nkb_gu * 4 * kTerms * 16) + up1k((size_t)tok_cap * nkb_gu * 4 * 8);
 }
 
-cudaError_t init_bs_scratch(void *scratch, int rows_cap, int E, int H, int I) {
+cudaError_t init_bs_scratch(void *scratch, int rows_cap, int tok_cap, int E, int H, int I) {
     // down's B operand: rows no gate_up tile writes (K padding past I) must read as
     // zero codes with a unit scale
-    const BsScratch s = carve_bs(scratch, rows_cap, E, H, I);
+    const BsScratch s = carve_bs(scratch, rows_cap, tok_cap, E, H, I);
     const size_t parts = b_bytes(s.max_tiles, kpad128(I) / 128) / kBPart;
     cudaError_t e = cudaMemset(s.aq, 0, parts * kBPart);
     if (e == cudaSuccess) e = cudaMemset2D(s.aq + kBHalf, kBPart, 127, kBSf, parts);
@@ -726,10 +807,10 @@ int pair_grid(int dev) {
 }  // namespace
 
 cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *offsets, const __half *x_hi,
-                              const __half *x_lo, const int32_t *perm, int rows_cap, void *scratch, int scratch_e,
-                              float *y,
-                              const int32_t *y_rows, int32_t *err, cudaStream_t st, StageHook hook, void *hook_arg,
-                              int *launches, const EpReturn *ret, const int32_t *gate, int gate_want) {
+                              const __half *x_lo, const int32_t *perm, int tokens, int rows_cap, int tok_cap,
+                              void *scratch, int scratch_e, float *y, const int32_t *y_rows, int32_t *err,
+                              cudaStream_t st, StageHook hook, void *hook_arg, int *launches, const EpReturn *ret,
+                              const int32_t *gate, int gate_want) {
     if (!get_encode()) return cudaErrorNotSupported;
     static bool attr_set = false;
     if (!attr_set) {
@@ -740,17 +821,26 @@ cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *o
     int dev = 0;
     cudaGetDevice(&dev);
     const int grid = pair_grid(dev);
-    const BsScratch s = carve_bs(scratch, rows_cap, scratch_e, d.H, d.I);
+    const BsScratch s = carve_bs(scratch, rows_cap, tok_cap, scratch_e, d.H, d.I);
     const int nkb_gu = kpad128(d.H) / 128, nkb_dn = kpad128(d.I) / 128;
     const int nmt_gu = (2 * d.I + 127) / 128, nmt_dn = (d.H + 127) / 128;
     *launches = 0;
     // 1. token tiles, then the gate_up B operand
     bs_plan_kernel<<<1, 256, 0, st>>>(offsets, d.E, s.tiles, s.ntiles, s.max_tiles, err);
-    bs_quant_kernel<<<s.max_tiles * nkb_gu, kTok * 4, 0, st>>>(x_hi, x_lo, perm, d.k, d.H, nkb_gu, s.tiles, s.ntiles,
-                                                               s.xq);
+    if (perm && tokens > 0 && tokens <= tok_cap) {
+        // each token feeds k pairs: quantize it once, then gather the tiles' rows
+        const size_t recs = (size_t)tokens * nkb_gu * 4;
+        tok_quant_kernel<<<(unsigned)((recs + 255) / 256), 256, 0, st>>>(x_hi, x_lo, tokens, d.H, nkb_gu, s.tq, s.ts);
+        bs_gather_kernel<<<s.max_tiles * nkb_gu, kTok * 4, 0, st>>>(s.tq, s.ts, perm, d.k, nkb_gu, s.tiles, s.ntiles,
+                                                                    s.xq);
+        *launches += 3;
+    } else {
+        bs_quant_kernel<<<s.max_tiles * nkb_gu, kTok * 4, 0, st>>>(x_hi, x_lo, perm, d.k, d.H, nkb_gu, s.tiles,
+                                                                   s.ntiles, s.xq);
+        *launches += 2;
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    *launches += 2;
     if (hook) hook(hook_arg, 5);
     // 2. gate_up + SwiGLU, writing down's B operand
     CUtensorMap tm_gu1, tm_gu2, tm_dn1, tm_dn2, tm_xq1, tm_xq2, tm_aq1, tm_aq2;

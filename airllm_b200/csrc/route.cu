@@ -328,9 +328,18 @@ __global__ void __launch_bounds__(1024) scan_kernel(int T, int E, RouteOut o) {
     const int e = tid % E, g = tid / E;
     const int per = (nchunk + groups - 1) / groups;
     const int c0 = min(nchunk, g * per), c1 = min(nchunk, c0 + per);
+    // a thread's histogram loads are independent: 16 in flight at a time, rather than
+    // one global-memory latency per chunk
+    constexpr int kBatch = 16;
     if (g < groups) {
         int s = 0;
-        for (int c = c0; c < c1; ++c) s += o.hist[(size_t)c * E + e];
+        for (int c = c0; c < c1; c += kBatch) {
+            int v[kBatch];
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) v[j] = c + j < c1 ? o.hist[(size_t)(c + j) * E + e] : 0;
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) s += v[j];
+        }
         gsum[g * E + e] = s;
     }
     __syncthreads();
@@ -360,9 +369,15 @@ __global__ void __launch_bounds__(1024) scan_kernel(int T, int E, RouteOut o) {
     __syncthreads();
     if (g < groups) {
         int s = eoff[e] + gsum[g * E + e];
-        for (int c = c0; c < c1; ++c) {
-            o.chunk_base[(size_t)c * E + e] = s;
-            s += o.hist[(size_t)c * E + e];
+        for (int c = c0; c < c1; c += kBatch) {
+            int v[kBatch];
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) v[j] = c + j < c1 ? o.hist[(size_t)(c + j) * E + e] : 0;
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) {
+                if (c + j < c1) o.chunk_base[(size_t)(c + j) * E + e] = s;
+                s += v[j];
+            }
         }
     }
 }
