@@ -215,9 +215,19 @@ __device__ __forceinline__ void red_add_release(unsigned *p, unsigned v) {
 __device__ __forceinline__ void route_bar() { asm volatile("bar.sync 3, %0;" ::"n"(kEpiWarp0 * 32) : "memory"); }
 __device__ __forceinline__ void build_bar() { asm volatile("bar.sync 2, %0;" ::"n"(kBuildThreads) : "memory"); }
 
-// Bounded mbarrier wait that returns at once once the CTA is dead.
+// Bounded mbarrier wait that returns at once once the CTA is dead (a phase that
+// has already completed is taken first: the common case costs one poll).
 __device__ __forceinline__ bool ring_wait(uint64_t *bar, uint32_t parity, volatile int *dead, int32_t *err,
                                           int code) {
+    {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+        if (ok) return true;
+    }
     if (*dead) return false;
     const long long t0 = clock64();
     for (;;) {
@@ -238,8 +248,8 @@ __device__ __forceinline__ bool ring_wait(uint64_t *bar, uint32_t parity, volati
 }
 
 // ---- tcgen05, one CTA (M = 128) ----
-__device__ __forceinline__ void sf_copy(uint32_t tmem_col, uint32_t saddr) {
-    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tmem_col), "l"(desc_sf(saddr)) : "memory");
+__device__ __forceinline__ void sf_copy(uint32_t tmem_col, uint64_t desc) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tmem_col), "l"(desc) : "memory");
 }
 __device__ __forceinline__ void umma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc, uint32_t sfa,
                                      uint32_t sfb) {
@@ -662,10 +672,17 @@ __launch_bounds__(kDecThreads, 1) __global__
         }
     } else if (warp == kMmaWarp) {
         // ---------------- MMA issuer ----------------
+        // The loop issues few instructions per box: every descriptor is its base plus
+        // an offset in the start-address field (bits 0-13, 16-byte units; shared
+        // addresses stay below 256 KB, so no carry leaves the field).
         const uint32_t elected = elect_one();
         const uint32_t idesc0 = idesc_dec(0, NCOL), idesc1 = idesc_dec(2, NCOL);
         const uint32_t ring_a = smem_u32(ring), bx_a = smem_u32(bx), bd_a = smem_u32(bd);
-        int i = 0, dn = 0, nbox = 0;
+        const uint64_t da = desc_sw64(ring_a), fa = desc_sf(ring_a + kBoxBytes);  // stage 0, box 0
+        const uint64_t dbx = desc_sw64(bx_a), fbx = desc_sf(bx_a + kCb);         // gate_up's operand
+        const uint64_t dbd = desc_sw64(bd_a), fbd = desc_sf(bd_a + kCb);         // down's, buffer 0
+        int i = 0, dn = 0, nbox = 0, s = 0;
+        uint32_t ph = 0;  // parity of the ring's current pass
         bool ok = true, bx_ready = false;
         for (int u = 0; u < nunits && ok; ++u) {
             int phase, slot, mt, kpart, np, kb0, kb1, split;
@@ -679,11 +696,12 @@ __launch_bounds__(kDecThreads, 1) __global__
             if (phase == 1 && !ring_wait(bfull + ub, (dn >> 1) & 1, misc, p.err, 56)) break;
             tc_fence_after();
             const uint32_t d = tmem + (uint32_t)buf * kAccCols;
-            const uint32_t bbase = phase ? bd_a + (uint32_t)(ub * dmax) * kBb : bx_a;
+            const uint32_t bo0 = phase ? (uint32_t)(ub * dmax) * (kBb >> 4) : 0u;
+            const uint64_t db = (phase ? dbd : dbx) + bo0, fb = (phase ? fbd : fbx) + bo0;
             const int kbase = phase ? kb0 : 0;
             for (int kb = kb0; kb < kb1; kb += 2, ++i) {
-                const int s = i % R, nb = min(2, kb1 - kb);
-                if (!ring_wait(full + s, (i / R) & 1, misc, p.err, 51)) {
+                const int nb = min(2, kb1 - kb);
+                if (!ring_wait(full + s, ph, misc, p.err, 51)) {
                     ok = false;
                     break;
                 }
@@ -692,17 +710,21 @@ __launch_bounds__(kDecThreads, 1) __global__
                     if (elected) {
                         // tcgen05.cp and tcgen05.mma issued by this thread execute in issue
                         // order, so a scale slot is rewritten only after the MMAs that read it
-                        const uint32_t a = ring_a + (uint32_t)s * kStageBytes + (uint32_t)b * kBoxStep;
-                        const uint32_t bq = bbase + (uint32_t)(kb + b - kbase) * kBb;
+                        const uint32_t ao = (uint32_t)s * (kStageBytes >> 4) + (uint32_t)b * (kBoxStep >> 4);
+                        const uint32_t bo = (uint32_t)(kb + b - kbase) * (kBb >> 4);
                         const uint32_t sf = tmem + kSfCol + 16u * (uint32_t)(nbox & 1);
-                        sf_copy(sf, a + kBoxBytes);  // the weights' E8M0 chunk
-                        sf_copy(sf + 4, bq + kCb);   // the tokens' term scales
-                        umma(d, desc_sw64(a), desc_sw64(bq), idesc0, (kb + b > kb0) ? 1u : 0u, sf, sf + 4);
-                        umma(d, desc_sw64(a + 32), desc_sw64(bq + 32), idesc1, 1u, sf, sf + 4);
+                        sf_copy(sf, fa + ao);      // the weights' E8M0 chunk
+                        sf_copy(sf + 4, fb + bo);  // the tokens' term scales
+                        umma(d, da + ao, db + bo, idesc0, (kb + b > kb0) ? 1u : 0u, sf, sf + 4);
+                        umma(d, da + ao + 2, db + bo + 2, idesc1, 1u, sf, sf + 4);
                     }
                 }
                 if (elected) mma_commit(empty + s);
                 __syncwarp();
+                if (++s == R) {
+                    s = 0;
+                    ph ^= 1u;
+                }
             }
             if (!ok) break;
             if (elected) {
