@@ -581,7 +581,18 @@ __launch_bounds__(kDecThreads, 1) __global__
                 }
                 __syncwarp();
                 int my_e = 0;
-                for (int s = 0; s < p.k; ++s) {
+                if (E <= 32) {
+                    // one expert per lane (e = lane): per round one 32-bit max reduction and a
+                    // ballot; equal keys go to the lowest lane, i.e. the lower id
+                    uint32_t ord = (uint32_t)(key[0] >> 32);
+                    for (int s = 0; s < p.k; ++s) {
+                        const uint32_t m = __reduce_max_sync(0xffffffffu, ord);
+                        const int win = __ffs(__ballot_sync(0xffffffffu, ord == m)) - 1;
+                        my_e = lane == s ? win : my_e;
+                        ord = lane == win ? 0u : ord;
+                    }
+                }
+                for (int s = 0; s < (E <= 32 ? 0 : p.k); ++s) {
                     uint64_t b = key[0];
 #pragma unroll
                     for (int j = 1; j < 8; ++j) b = key[j] > b ? key[j] : b;
@@ -627,16 +638,21 @@ __launch_bounds__(kDecThreads, 1) __global__
                     if (w0 + lane < 2 * n) units_s[w0 + lane] = sched_s[u0 + w0 + lane];
                 if (lane == 0) misc[2] = n;
                 __syncwarp();
-                if (lane == 0) {  // the first copies
+                {  // the first copies: stage j < R from lane j
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the staged schedule rows are read
-                    const int first = R;
-                    int j = 0;
-                    for (int u = 0; u < n && j < first; ++u) {
+                    int j = 0, mine_u = -1, mine_kb = 0;
+                    for (int u = 0; u < n && j < R; ++u) {
                         int phase, slot, mt, kpart, np, kb0, kb1, split;
                         unit_span(u, phase, slot, mt, kpart, np, kb0, kb1, split);
-                        for (int kb = kb0; kb < kb1 && j < first; kb += 2, ++j) issue(j, u, kb);
+                        const int ns = (kb1 - kb0 + 1) >> 1;  // the unit's stages
+                        if (lane >= j && lane < j + ns) {
+                            mine_u = u;
+                            mine_kb = kb0 + 2 * (lane - j);
+                        }
+                        j += ns;
                     }
-                    misc[3] = j;  // stages issued
+                    if (mine_u >= 0 && lane < R) issue(lane, mine_u, mine_kb);
+                    if (lane == 0) misc[3] = min(j, R);  // stages issued
                 }
             }
         }
