@@ -863,8 +863,8 @@ int check_forward_args(amoe_ctx *c, int32_t layer, const float *residual, int32_
 }
 
 // Token slices of a host-buffer call: one pass unless the call is large enough
-// that overlapping its host copies with compute pays (>= 2048 tokens and two
-// passes of the size below), and only
+// that overlapping its host copies with compute pays (>= 2048 tokens; n passes of
+// the size below become n + 1 with half-length ends), and only
 // when every slice takes the same expert path as the whole call (so the output
 // is bit-identical to one pass: tokens are independent).  Expert-parallel calls
 // stay whole: every rank must make the same sequence of exchanges.
@@ -875,11 +875,21 @@ std::vector<int> plan_passes(const amoe_ctx *c, int T) {
     // 48-token tiles stay mostly full (128 experts: 2048-token passes)
     const int per_expert = (int)std::min<long long>(1 << 20, (64LL * c->d.E + c->d.k - 1) / c->d.k);
     const int target = std::max({1024, per_expert, (T + kMaxIoChunks - 1) / kMaxIoChunks});
-    const int n = (T + target - 1) / target;
+    const int n = std::min((T + target - 1) / target, kMaxIoChunks - 1);  // n + 1 passes with the split end
     int len = (T + n - 1) / n;
     len = (len + kRouteTokens - 1) / kRouteTokens * kRouteTokens;  // slices start on routing-chunk bounds
+    // the first and last passes are half as long: the first pass's upload and the
+    // last pass's download are the two copies no compute overlaps
     std::vector<int> passes;
-    for (int t0 = 0; t0 < T; t0 += len) passes.push_back(std::min(len, T - t0));
+    if (n >= 2) {  // every pass but the last starts and ends on a routing-chunk bound
+        const int edge = (len / 2 + kRouteTokens - 1) / kRouteTokens * kRouteTokens;
+        const int last0 = (T - edge) / kRouteTokens * kRouteTokens;  // the last pass's first token
+        const int nm = n - 1, mid = last0 - edge;
+        const int ml = ((mid + nm - 1) / nm + kRouteTokens - 1) / kRouteTokens * kRouteTokens;
+        passes.push_back(edge);
+        for (int t0 = edge; t0 < last0; t0 += ml) passes.push_back(std::min(ml, last0 - t0));
+        passes.push_back(T - last0);
+    }
     if (passes.size() < 2 || (int)passes.size() > kMaxIoChunks) return one;
     const int smallest = *std::min_element(passes.begin(), passes.end());
     if (use_tensor_path(c, smallest) != use_tensor_path(c, T)) return one;
