@@ -233,14 +233,20 @@ __global__ void __launch_bounds__(256) tok_quant_kernel(const __half *__restrict
 // The gate_up B operand from the token-major records: one CTA per (tile, K box),
 // one thread per (token, 32-element block), the token found through the
 // permutation.  Tokens past the tile's count get zero codes with a unit scale,
-// as quantized zeros do.
+// as quantized zeros do.  The code words go straight to their rows; the scale
+// bytes are gathered into the box's 1 KB chunk in shared memory, which then goes
+// out to both CTA parts as 16-byte stores (rows 240-255 of the chunk, which no MMA
+// reads, are zero).
 __global__ void __launch_bounds__(kTok * 4) bs_gather_kernel(const uint4 *__restrict__ tq,
                                                              const uint2 *__restrict__ ts,
                                                              const int32_t *__restrict__ perm, int k, int nkb,
                                                              const int4 *__restrict__ tiles, const int32_t *ntiles,
                                                              uint8_t *bq) {
+    __shared__ __align__(16) uint8_t sf_s[kBSf];
     const int t = blockIdx.x / nkb, kb = blockIdx.x - t * nkb;
     if (t >= *ntiles) return;  // uniform over the CTA
+    for (int i = threadIdx.x; i < (int)(kBSf / 16); i += blockDim.x)
+        reinterpret_cast<uint4 *>(sf_s)[i] = make_uint4(0u, 0u, 0u, 0u);
     const int4 ti = tiles[t];
     const int i = threadIdx.x >> 2, jb = threadIdx.x & 3;
     uint4 w[kTerms];
@@ -255,11 +261,18 @@ __global__ void __launch_bounds__(kTok * 4) bs_gather_kernel(const uint4 *__rest
         for (int term = 0; term < kTerms; ++term) w[term] = make_uint4(0u, 0u, 0u, 0u);
     }
     const int nkb2 = (nkb + 1) >> 1;
+    __syncthreads();  // the chunk is zeroed
 #pragma unroll
     for (int term = 0; term < kTerms; ++term) {
         const uint32_t words[4] = {w[term].x, w[term].y, w[term].z, w[term].w};
         put_codes<16>(bq, t, kb, nkb2, kTerms * i + term, jb, 0, words);
-        put_scale(bq, t, kb, nkb2, kTerms * i + term, jb, term < 4 ? (sc.x >> (8 * term)) & 0xffu : sc.y & 0xffu);
+        sf_s[sf_at(kTerms * i + term, jb)] = (uint8_t)(term < 4 ? (sc.x >> (8 * term)) & 0xffu : sc.y & 0xffu);
+    }
+    __syncthreads();
+    constexpr int kChunk16 = (int)(kBSf / 16);
+    for (int q = threadIdx.x; q < 2 * kChunk16; q += blockDim.x) {
+        const int h = q / kChunk16, c = q - h * kChunk16;
+        reinterpret_cast<uint4 *>(bpart(bq, t, kb, h, nkb2) + kBHalf)[c] = reinterpret_cast<const uint4 *>(sf_s)[c];
     }
 }
 
