@@ -132,7 +132,7 @@ struct amoe_ctx {
     __half *act_hi = nullptr, *act_lo = nullptr;
     float *y = nullptr;
     int32_t *err_flag = nullptr;  // set by a kernel whose bounded wait gave up (0 = fine)
-    void *bs_scratch = nullptr;  // token tiles and the E4M3-term operands of the block-scaled GEMMs
+    void *bs_scratch = nullptr;  // token tiles and the five-term E2M1 operands of the block-scaled GEMMs
     DecodeBarrier *dec_bar = nullptr;  // launch counts of the fused decode kernel's CTAs
     void *dec_scratch = nullptr;       // its activation operand, partial tiles and tile counters
     float *io_in = nullptr, *io_out = nullptr;
