@@ -183,13 +183,21 @@ bool tc_supported();
 // go to y[y_rows ? y_rows[pos] : pos][H] (with ret: the source rank's y, see
 // EpReturn).  scratch: bs_scratch_bytes(), prepared once by init_bs_scratch().
 size_t bs_scratch_bytes(int rows_cap, int tok_cap, int E, int H, int I);
+// Each of `tokens` rows of (x_hi, x_lo) [tokens][H] as five-term E2M1 records in the
+// scratch's token-record arrays (returned in *tq, *ts); nothing to do unless *gate == 1
+// (gate NULL: always).
+cudaError_t launch_tok_quant(const __half *x_hi, const __half *x_lo, int tokens, int H, int I, void *scratch,
+                             int rows_cap, int tok_cap, int scratch_e, const int32_t *gate, cudaStream_t st,
+                             const uint4 **tq, const uint2 **ts);
 cudaError_t init_bs_scratch(void *scratch, int rows_cap, int tok_cap, int E, int H, int I);
 // scratch_e: the expert count the scratch was sized for (bs_scratch_bytes), >= d.E.
 cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *offsets, const __half *x_hi,
                               const __half *x_lo, const int32_t *perm, int tokens, int rows_cap, int tok_cap,
                               void *scratch, int scratch_e, float *y, const int32_t *y_rows, int32_t *err,
                               cudaStream_t st, StageHook hook, void *hook_arg, int *launches,
-                              const EpReturn *ret = nullptr, const int32_t *gate = nullptr, int gate_want = 0);
+                              const EpReturn *ret = nullptr, const int32_t *gate = nullptr, int gate_want = 0,
+                              const uint4 *rec_q = nullptr, const uint2 *rec_s = nullptr);
+// (rec_q, rec_s: the rows already as token records, row = position; x_hi/x_lo unused)
 // Combine --------------------------------------------------------------------
 cudaError_t launch_combine(const Dims &d, const float *residual, const RouteOut &r,
                            const float *y, int T, float *out, cudaStream_t st);
@@ -218,7 +226,8 @@ enum { kEpFlagCount = 0, kEpFlagDispatch = 1, kEpFlagReturn = 2 };
 struct EpWindow {
     size_t flags;             // int32 [3][kMaxEpRanks]: count / dispatch / return flag per source rank
     size_t table;             // int32 [N][E]: pairs source s routes to global expert e
-    size_t recv_hi, recv_lo;  // fp16 [r_cap][H]: rows for this rank's experts, expert-major
+    size_t recv_hi, recv_lo;  // fp16 [r_cap][H]: rows for this rank's experts, expert-major (GEMV path);
+                              // the tcgen05 path receives token records from recv_hi on (ep_recv_records)
     size_t y;                 // f32 [p_cap][H]: outputs for this rank's pairs, at their sorted position
     size_t bytes;
 };
@@ -249,8 +258,22 @@ struct EpArgs {
     EpMeta m;
     const int32_t *counts, *offsets, *topk_idx, *perm_pair;  // this rank's routing
     const __half *x_hi, *x_lo;                                // its normalized rows, by token
+    // the same rows as five-term token records (tok_quant_kernel), sent instead of the
+    // fp16 rows when the group takes the tcgen05 path (*m.mode == 1); NULL: never
+    const uint4 *tq;
+    const uint2 *ts;
+    int nkb;
     int32_t *err;
 };
+
+// Where the tcgen05 path's received token records sit in a window: the codes of row
+// p at q + p * nkb * 4 * 5 (uint4), its scale words at s + p * nkb * 4 (uint2).
+__host__ __device__ inline void ep_recv_records(uint8_t *win, const EpWindow &w, int r_cap, int H, uint4 **q,
+                                                uint2 **s) {
+    const size_t nkb = (size_t)(H + 127) / 128;
+    *q = reinterpret_cast<uint4 *>(win + w.recv_hi);
+    *s = reinterpret_cast<uint2 *>(win + w.recv_hi + (size_t)r_cap * nkb * 4 * 5 * 16);
+}
 
 // Down-GEMM epilogue of an expert-parallel step: output row y_rows[pos] goes to
 // ret_y[rank] at its position; the last CTA to finish publishes `epoch` in

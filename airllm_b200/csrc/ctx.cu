@@ -608,7 +608,22 @@ int ep_experts(amoe_ctx *c, const LayerDev &L, const RouteOut &r, int T, int nch
     a.err = flag;
     a.path = c->cfg.path == AMOE_PATH_GEMV ? 1 : c->cfg.path == AMOE_PATH_TENSOR ? 2 : 0;
     if (a.path == 0 && !tc_supported()) a.path = 1;
+    // Expert path: AUTO is decided on the device by the count kernel from the
+    // whole group's pairs (the single-GPU rule on the group's tokens), so every
+    // rank agrees and the result equals one GPU's; both paths are launched and
+    // the one not chosen returns at once.
+    const bool run_tc = tc_supported() && a.path != 1;
+    const bool run_gemv = a.path != 2;
+    const int32_t *gate = run_tc && run_gemv ? c->ep_m.mode : nullptr;
     AMOE_CUDA(c, launch_ep_counts(a, st));
+    a.tq = nullptr;
+    a.ts = nullptr;
+    a.nkb = (d.H + 127) / 128;
+    if (run_tc) {  // the tcgen05 path sends token records: this rank's tokens, quantized once
+        AMOE_CUDA(c, launch_tok_quant(r.x_hi, r.x_lo, T, d.H, d.I, c->bs_scratch, (int)c->r_max, c->max_tokens,
+                                      c->dx.E, c->ep_m.mode, st, &a.tq, &a.ts));
+        c->stats.launches += 1;
+    }
     AMOE_CUDA(c, launch_ep_dispatch(a, 2 * c->sms, st));
     timer.mark(5);
     AMOE_CUDA(c, launch_ep_wait(a, kEpFlagDispatch, 31, st));
@@ -624,19 +639,15 @@ int ep_experts(amoe_ctx *c, const LayerDev &L, const RouteOut &r, int T, int nch
     ret.status = c->ep_m.status;
     ret.n = N;
     ret.epoch = a.epoch;
-    // Expert path: AUTO is decided on the device by the count kernel from the
-    // whole group's pairs (the single-GPU rule on the group's tokens), so every
-    // rank agrees and the result equals one GPU's; both paths are launched and
-    // the one not chosen returns at once.
-    const bool run_tc = tc_supported() && a.path != 1;
-    const bool run_gemv = a.path != 2;
-    const int32_t *gate = run_tc && run_gemv ? c->ep_m.mode : nullptr;
     *used_tc = run_tc && (a.path == 2 || (long long)N * T * d.k >= 32LL * d.E);  // stats guess
     if (run_tc) {
         int n = 0;
+        uint4 *rq;
+        uint2 *rs;
+        ep_recv_records(c->ep_win, c->ep_w, (int)c->r_max, d.H, &rq, &rs);
         AMOE_CUDA(c, launch_bs_experts(c->dx, L, c->ep_m.offsets_loc, rh, rl, nullptr, 0, (int)c->r_max,
                                        c->max_tokens, c->bs_scratch, c->dx.E, y_own, c->ep_m.y_rows, flag, st,
-                                       &timer_hook, &timer, &n, &ret, gate, 1));
+                                       &timer_hook, &timer, &n, &ret, gate, 1, rq, rs));
         c->stats.launches += n;
     }
     if (run_gemv) {

@@ -75,6 +75,9 @@ EpWindow ep_window(int N, int E, int H, int p_cap, int r_cap) {
     off = up256(off + (size_t)r_cap * H * 2);
     w.recv_lo = off;
     off = up256(off + (size_t)r_cap * H * 2);
+    // the token records of the tcgen05 path share the two row buffers' space
+    const size_t rec = (size_t)r_cap * ((H + 127) / 128) * 4 * (5 * 16 + 8);
+    if (w.recv_hi + rec > off) off = up256(w.recv_hi + rec);
     w.y = off;
     off = up256(off + (size_t)p_cap * H * 4);
     w.bytes = off;
@@ -255,19 +258,23 @@ __global__ void __launch_bounds__(kCountThreads) ep_counts_kernel(EpArgs a) {
 constexpr int kDispatchThreads = 256;
 constexpr int kDispatchUnroll = 4;
 
-// Grid-stride over this rank's expert-sorted pairs, one warp per row: the fp16
-// hi and lo rows of the pair's token go into the owner's receive buffer.  Then
-// the return targets of the rows this rank receives.
+// Grid-stride over this rank's expert-sorted pairs, one warp per row: the pair's
+// token goes into the owner's receive buffer, as its five-term token records when
+// the group takes the tcgen05 path (2.75 bytes an element, quantized once at the
+// source), else as the fp16 hi and lo rows the GEMV reads.  Then the return
+// targets of the rows this rank receives.
 __global__ void __launch_bounds__(kDispatchThreads) ep_dispatch_kernel(EpArgs a) {
     __shared__ uint8_t *win[kMaxEpRanks];
     const int tid = threadIdx.x, lane = tid & 31;
     if (tid < a.N) win[tid] = a.m.win[tid];
     __syncthreads();
     const bool ok = *reinterpret_cast<const volatile int32_t *>(a.m.status) == 1;
+    const bool records = a.tq && *a.m.mode == 1;
     if (ok) {
         const int P = a.offsets[a.E];
         const int H8 = a.H / 8;
         const int warps = kDispatchThreads / 32;
+        const int rq = a.nkb * 4 * 5, rs = a.nkb * 4;  // a token's record words (uint4, uint2)
         for (int q = blockIdx.x * warps + (tid >> 5); q < P; q += gridDim.x * warps) {
             const int pair = a.perm_pair[q];
             const int e = a.topk_idx[pair];
@@ -276,6 +283,18 @@ __global__ void __launch_bounds__(kDispatchThreads) ep_dispatch_kernel(EpArgs a)
             const int row = a.m.send_base[e] + (q - a.offsets[e]);
             if (row < 0 || row >= a.r_cap || dst >= a.N) {  // inconsistent counts: skip the store
                 if (lane == 0) atomicCAS(a.err, 0, 33);
+                continue;
+            }
+            if (records) {
+                uint4 *dq;
+                uint2 *ds;
+                ep_recv_records(win[dst], a.w, a.r_cap, a.H, &dq, &ds);
+                const uint4 *sq = a.tq + (size_t)t * rq;
+                const uint2 *ss = a.ts + (size_t)t * rs;
+                dq += (size_t)row * rq;
+                ds += (size_t)row * rs;
+                for (int i = lane; i < rq; i += 32) dq[i] = __ldg(sq + i);
+                for (int i = lane; i < rs; i += 32) ds[i] = __ldg(ss + i);
                 continue;
             }
             const uint4 *sh = reinterpret_cast<const uint4 *>(a.x_hi + (size_t)t * a.H);

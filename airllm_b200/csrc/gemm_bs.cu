@@ -194,7 +194,8 @@ __global__ void __launch_bounds__(256) bs_plan_kernel(const int32_t *__restrict_
 // K quantize as zeros, exactly as bs_quant_kernel treats them.
 __global__ void __launch_bounds__(256) tok_quant_kernel(const __half *__restrict__ x_hi,
                                                         const __half *__restrict__ x_lo, int tokens, int K,
-                                                        int nkb, uint4 *tq, uint2 *ts) {
+                                                        int nkb, uint4 *tq, uint2 *ts, const int32_t *gate) {
+    if (gate && *gate != 1) return;  // the other expert path runs this step
     const size_t r = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= (size_t)tokens * nkb * 4) return;
     const int jb = (int)(r & 3);
@@ -232,7 +233,8 @@ __global__ void __launch_bounds__(256) tok_quant_kernel(const __half *__restrict
 
 // The gate_up B operand from the token-major records: one CTA per (tile, K box),
 // one thread per (token, 32-element block), the token found through the
-// permutation.  Tokens past the tile's count get zero codes with a unit scale,
+// permutation (perm NULL: record row = the pair's position, as expert parallelism
+// receives them).  Tokens past the tile's count get zero codes with a unit scale,
 // as quantized zeros do.  The code words go straight to their rows; the scale
 // bytes are gathered into the box's 1 KB chunk in shared memory, which then goes
 // out to both CTA parts as 16-byte stores (rows 240-255 of the chunk, which no MMA
@@ -252,7 +254,7 @@ __global__ void __launch_bounds__(kTok * 4) bs_gather_kernel(const uint4 *__rest
     uint4 w[kTerms];
     uint2 sc = make_uint2(0x7f7f7f7fu, 0x7fu);
     if (i < ti.z) {
-        const size_t r = ((size_t)(perm[ti.y + i] / k) * nkb + kb) * 4 + jb;
+        const size_t r = ((size_t)(perm ? perm[ti.y + i] / k : ti.y + i) * nkb + kb) * 4 + jb;
 #pragma unroll
         for (int term = 0; term < kTerms; ++term) w[term] = __ldg(tq + r * kTerms + term);
         sc = __ldg(ts + r);
@@ -763,6 +765,19 @@ size_t bs_scratch_bytes(int rows_cap, int tok_cap, int E, int H, int I) {
            up1k((size_t)tok_cap * nkb_gu * 4 * kTerms * 16) + up1k((size_t)tok_cap * nkb_gu * 4 * 8);
 }
 
+cudaError_t launch_tok_quant(const __half *x_hi, const __half *x_lo, int tokens, int H, int I, void *scratch,
+                             int rows_cap, int tok_cap, int scratch_e, const int32_t *gate, cudaStream_t st,
+                             const uint4 **tq, const uint2 **ts) {
+    const BsScratch s = carve_bs(scratch, rows_cap, tok_cap, scratch_e, H, I);
+    *tq = s.tq;
+    *ts = s.ts;
+    if (tokens <= 0 || tokens > tok_cap) return cudaErrorInvalidValue;
+    const int nkb = kpad128(H) / 128;
+    const size_t recs = (size_t)tokens * nkb * 4;
+    tok_quant_kernel<<<(unsigned)((recs + 255) / 256), 256, 0, st>>>(x_hi, x_lo, tokens, H, nkb, s.tq, s.ts, gate);
+    return cudaGetLastError();
+}
+
 cudaError_t init_bs_scratch(void *scratch, int rows_cap, int tok_cap, int E, int H, int I) {
     // down's B operand: rows no gate_up tile writes (K padding past I) must read as
     // zero codes with a unit scale
@@ -823,7 +838,7 @@ cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *o
                               const __half *x_lo, const int32_t *perm, int tokens, int rows_cap, int tok_cap,
                               void *scratch, int scratch_e, float *y, const int32_t *y_rows, int32_t *err,
                               cudaStream_t st, StageHook hook, void *hook_arg, int *launches, const EpReturn *ret,
-                              const int32_t *gate, int gate_want) {
+                              const int32_t *gate, int gate_want, const uint4 *rec_q, const uint2 *rec_s) {
     if (!get_encode()) return cudaErrorNotSupported;
     static bool attr_set = false;
     if (!attr_set) {
@@ -840,10 +855,16 @@ cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *o
     *launches = 0;
     // 1. token tiles, then the gate_up B operand
     bs_plan_kernel<<<1, 256, 0, st>>>(offsets, d.E, s.tiles, s.ntiles, s.max_tiles, err);
-    if (perm && tokens > 0 && tokens <= tok_cap) {
+    if (rec_q && rec_s) {
+        // the rows arrived as token records (expert parallelism): gather them by position
+        bs_gather_kernel<<<s.max_tiles * nkb_gu, kTok * 4, 0, st>>>(rec_q, rec_s, nullptr, 1, nkb_gu, s.tiles,
+                                                                    s.ntiles, s.xq);
+        *launches += 2;
+    } else if (perm && tokens > 0 && tokens <= tok_cap) {
         // each token feeds k pairs: quantize it once, then gather the tiles' rows
         const size_t recs = (size_t)tokens * nkb_gu * 4;
-        tok_quant_kernel<<<(unsigned)((recs + 255) / 256), 256, 0, st>>>(x_hi, x_lo, tokens, d.H, nkb_gu, s.tq, s.ts);
+        tok_quant_kernel<<<(unsigned)((recs + 255) / 256), 256, 0, st>>>(x_hi, x_lo, tokens, d.H, nkb_gu, s.tq, s.ts,
+                                                                         nullptr);
         bs_gather_kernel<<<s.max_tiles * nkb_gu, kTok * 4, 0, st>>>(s.tq, s.ts, perm, d.k, nkb_gu, s.tiles, s.ntiles,
                                                                     s.xq);
         *launches += 3;
