@@ -704,7 +704,7 @@ int forward_selected(amoe_ctx *c, int32_t layer, const float *residual, int32_t 
     Lr.router_w = res + H;
     Lr.router_b = res + H + E * H;
     AMOE_CUDA(c, launch_route_impl(d, Lr, residual, T, r, c->partial, c->arrivals, st, &timer_hook, &timer));
-    c->stats.launches += nchunk > 1 ? 2 : 1;
+    c->stats.launches += nchunk > 1 ? 3 : 1;  // route, then the two scan kernels
     if (nchunk > 1) {
         AMOE_CUDA(c, launch_scatter(d, T, r, false, nullptr, nullptr, st));
         c->stats.launches += 1;
@@ -785,7 +785,7 @@ int forward_impl(amoe_ctx *c, int32_t layer, const float *residual, int32_t T, f
     if (!c->blk.frag && !fused_decode) tc = true;  // streamed layers carry no GEMV tiles
     if (!fused_decode) {
         AMOE_CUDA(c, launch_route_impl(d, L, residual, T, r, c->partial, c->arrivals, st, &timer_hook, &timer));
-        c->stats.launches += nchunk > 1 ? 2 : 1;
+        c->stats.launches += nchunk > 1 ? 3 : 1;  // route, then the two scan kernels
     }
     if (c->ep_n > 1) {
         if (c->ep_broken)

@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteParams p) 
                 offs[e] = acc;
                 p.o.offsets[e] = acc;
                 p.o.counts[e] = hist_s[e];
-                p.o.chunk_base[e] = acc;
+                p.o.chunk_base[e] = 0;  // one chunk: the expert's pairs start at its offset
                 if (hist_s[e] > 0) p.o.active[na++] = e;
                 acc += hist_s[e];
             }
@@ -314,76 +314,67 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(RouteParams p) 
     }
 }
 
-// K2a: one CTA.  Column scan of the per-chunk expert histograms: expert
-// offsets (exclusive scan of the counts), the active-expert list, and for every
-// chunk the first position of each expert's pairs in that chunk.
-__global__ void __launch_bounds__(1024) scan_kernel(int T, int E, RouteOut o) {
-    extern __shared__ int sm[];
+// K2a: one CTA per expert e.  Its per-chunk pair counts hist[c][e], split into
+// contiguous chunk ranges over the threads (loads batched, 16 in flight), become
+// its chunk bases: chunk_base[c][e] = the expert's pairs in chunks before c (local
+// to the expert; the scatter adds offsets[e]); counts[e] = its total.
+constexpr int kScanThreads = 256;
+__global__ void __launch_bounds__(kScanThreads) scan_expert_kernel(int T, int E, RouteOut o) {
+    __shared__ int wsum[kScanThreads / 32];
+    const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nchunk = (T + kRouteTokens - 1) / kRouteTokens;
-    const int groups = max(1, (int)blockDim.x / E);
-    int *gsum = sm;                    // [groups][E]
-    int *tot = gsum + groups * E;      // [E]
-    int *eoff = tot + E;               // [E+1]
-    const int tid = threadIdx.x;
-    const int e = tid % E, g = tid / E;
-    const int per = (nchunk + groups - 1) / groups;
-    const int c0 = min(nchunk, g * per), c1 = min(nchunk, c0 + per);
-    // a thread's histogram loads are independent: 16 in flight at a time, rather than
-    // one global-memory latency per chunk
+    const int per = (nchunk + kScanThreads - 1) / kScanThreads;
+    const int c0 = min(nchunk, tid * per), c1 = min(nchunk, c0 + per);
     constexpr int kBatch = 16;
-    if (g < groups) {
-        int s = 0;
-        for (int c = c0; c < c1; c += kBatch) {
-            int v[kBatch];
+    int s = 0;
+    for (int c = c0; c < c1; c += kBatch) {
+        int v[kBatch];
 #pragma unroll
-            for (int j = 0; j < kBatch; ++j) v[j] = c + j < c1 ? o.hist[(size_t)(c + j) * E + e] : 0;
+        for (int j = 0; j < kBatch; ++j) v[j] = c + j < c1 ? o.hist[(size_t)(c + j) * E + e] : 0;
 #pragma unroll
-            for (int j = 0; j < kBatch; ++j) s += v[j];
-        }
-        gsum[g * E + e] = s;
+        for (int j = 0; j < kBatch; ++j) s += v[j];
     }
+    // exclusive scan of the threads' sums, in thread order
+    int incl = s;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int x = __shfl_up_sync(0xffffffffu, incl, d);
+        incl += lane >= d ? x : 0;
+    }
+    if (lane == 31) wsum[warp] = incl;
     __syncthreads();
-    if (tid < E) {
-        int s = 0;
-        for (int gg = 0; gg < groups; ++gg) {
-            int v = gsum[gg * E + tid];
-            gsum[gg * E + tid] = s;
-            s += v;
-        }
-        tot[tid] = s;
-    }
-    __syncthreads();
-    if (tid == 0) {
-        int s = 0, na = 0;
-        for (int x = 0; x < E; ++x) {
-            eoff[x] = s;
-            o.offsets[x] = s;
-            o.counts[x] = tot[x];
-            if (tot[x] > 0) o.active[na++] = x;
-            s += tot[x];
-        }
-        eoff[E] = s;
-        o.offsets[E] = s;
-        o.active[E] = na;
-    }
-    __syncthreads();
-    if (g < groups) {
-        int s = eoff[e] + gsum[g * E + e];
-        for (int c = c0; c < c1; c += kBatch) {
-            int v[kBatch];
+    int before = 0;
+    for (int w = 0; w < warp; ++w) before += wsum[w];
+    int base = before + incl - s;
+    for (int c = c0; c < c1; c += kBatch) {
+        int v[kBatch];
 #pragma unroll
-            for (int j = 0; j < kBatch; ++j) v[j] = c + j < c1 ? o.hist[(size_t)(c + j) * E + e] : 0;
+        for (int j = 0; j < kBatch; ++j) v[j] = c + j < c1 ? o.hist[(size_t)(c + j) * E + e] : 0;
 #pragma unroll
-            for (int j = 0; j < kBatch; ++j) {
-                if (c + j < c1) o.chunk_base[(size_t)(c + j) * E + e] = s;
-                s += v[j];
-            }
+        for (int j = 0; j < kBatch; ++j) {
+            if (c + j < c1) o.chunk_base[(size_t)(c + j) * E + e] = base;
+            base += v[j];
         }
     }
+    if (tid == kScanThreads - 1) o.counts[e] = base;  // the last thread ends at the expert's total
 }
 
-// K2b: one warp per chunk.  Pair (t, s) goes to chunk_base[chunk][e] + the number
-// of earlier pairs of expert e in the chunk (match_any ranks, carried across
+// K2b: one thread.  Expert offsets (exclusive scan of the counts) and the
+// active-expert list.
+__global__ void scan_offsets_kernel(int E, RouteOut o) {
+    int acc = 0, na = 0;
+    for (int e = 0; e < E; ++e) {
+        const int n = o.counts[e];
+        o.offsets[e] = acc;
+        if (n > 0) o.active[na++] = e;
+        acc += n;
+    }
+    o.offsets[E] = acc;
+    o.active[E] = na;
+}
+
+// K2c: one warp per chunk.  Pair (t, s) goes to offsets[e] + chunk_base[chunk][e] + the
+// number of earlier pairs of expert e in the chunk (match_any ranks, carried across
 // 32-pair rounds): a stable sort by (e, t, s).  With GATHER the warp also copies
 // the chunk's normalized rows (fp16 hi/lo) to their expert-sorted positions,
 // which is the B operand of the tensor-core gate_up GEMM.
@@ -404,7 +395,7 @@ __device__ __forceinline__ void chunk_positions(int chunk, int T, int E, int k, 
         const int ex = valid ? o.topk_idx[q] : E;  // E: sentinel group for idle lanes
         const unsigned peers = __match_any_sync(0xffffffffu, ex);
         if (valid) {
-            const int pos = o.chunk_base[(size_t)chunk * E + ex] + carry[ex] + __popc(peers & lt);
+            const int pos = o.offsets[ex] + o.chunk_base[(size_t)chunk * E + ex] + carry[ex] + __popc(peers & lt);
             o.perm_pair[pos] = q;
             o.inv[q] = pos;
             if (pos_s) pos_s[q - first] = pos;
@@ -415,7 +406,7 @@ __device__ __forceinline__ void chunk_positions(int chunk, int T, int E, int k, 
     }
 }
 
-// K2b (GEMV path): one warp per chunk.  Pair (t, s) goes to chunk_base[chunk][e]
+// K2c (GEMV path): one warp per chunk.  Pair (t, s) goes to offsets[e] + chunk_base[chunk][e]
 // + the number of earlier pairs of expert e in the chunk: a stable sort by
 // (e, t, s).
 __global__ void __launch_bounds__(kScatterWarps * 32) scatter_kernel(int T, int E, int k, RouteOut o) {
@@ -427,7 +418,7 @@ __global__ void __launch_bounds__(kScatterWarps * 32) scatter_kernel(int T, int 
     chunk_positions(chunk, T, E, k, o, carry_all + warp * E, nullptr, lane);
 }
 
-// K2b (tensor path): one CTA per chunk.  Warp 0 computes the positions, then
+// K2c (tensor path): one CTA per chunk.  Warp 0 computes the positions, then
 // warp t copies token t's normalized row (fp16 hi/lo) to its k expert-sorted
 // positions: the B operand of the tensor-core gate_up GEMM.
 __global__ void __launch_bounds__(kRouteTokens * 32)
@@ -513,10 +504,8 @@ cudaError_t launch_route_impl(const Dims &d, const LayerDev &L, const float *res
     if (err != cudaSuccess) return err;
     if (hook) hook(hook_arg, 0);
     if (nchunk == 1) return cudaSuccess;  // counts, offsets and chunk bases written by route_kernel
-    const int threads = 1024;
-    const int groups = threads / d.E > 0 ? threads / d.E : 1;
-    const size_t psmem = (size_t)(groups * d.E + d.E + d.E + 1) * sizeof(int);
-    scan_kernel<<<1, threads, psmem, st>>>(T, d.E, o);
+    scan_expert_kernel<<<d.E, kScanThreads, 0, st>>>(T, d.E, o);
+    scan_offsets_kernel<<<1, 1, 0, st>>>(d.E, o);
     return cudaGetLastError();
 }
 
