@@ -38,8 +38,9 @@
 // outputs' terms, to global memory in the same box form, and a down unit copies
 // its K half of it in one bulk copy.
 //
-// Roles once the CTA's units are known: warp 0 lane 0 streams the ring (a slot
-// refilled once the MMAs released it), warp 1 issues the MMAs into two TMEM
+// Roles once the CTA's units are known: warp 0 issues the ring's first stages at
+// once, one stage per lane, then lane 0 streams the rest (a slot refilled once the
+// MMAs released it), warp 1 issues the MMAs into two TMEM
 // accumulators, warp 2 lane 0 copies the down units' operands as their counters
 // complete, warp 3 finishes the routing that only the combine needs (softmax
 // weights, permutation, slots), and two epilogue groups of four warps (one per

@@ -21,7 +21,9 @@
 // rows of 64 bytes (row 5i + j: token i, term j), also in the swizzle order:
 // each CTA's 120 rows followed by the 1 KB of scale chunks of all 240 rows.  gate_up's epilogue writes down's B
 // operand in the same form: SwiGLU, then the five terms of every (token, 32-pair
-// block).
+// block).  gate_up's own B operand comes from token-major records: each token is
+// quantized once (tok_quant_kernel; with expert parallelism the source rank does it
+// and sends the records) and every tile gathers its tokens' rows (bs_gather_kernel).
 //
 // Every operand therefore reaches shared memory as one plain copy (TMA without
 // swizzle) of data and scales stored side by side: a stage is two copies of
