@@ -842,14 +842,14 @@ cudaError_t launch_bs_experts(const Dims &d, const LayerDev &L, const int32_t *o
                               cudaStream_t st, StageHook hook, void *hook_arg, int *launches, const EpReturn *ret,
                               const int32_t *gate, int gate_want, const uint4 *rec_q, const uint2 *rec_s) {
     if (!get_encode()) return cudaErrorNotSupported;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(bs_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
     int dev = 0;
     cudaGetDevice(&dev);
+    static int attr_set[64];  // the kernel's shared-memory ceiling, once per device (idempotent writes)
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(bs_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) attr_set[dev] = 1;
+    }
     const int grid = pair_grid(dev);
     const BsScratch s = carve_bs(scratch, rows_cap, tok_cap, scratch_e, d.H, d.I);
     const int nkb_gu = kpad128(d.H) / 128, nkb_dn = kpad128(d.I) / 128;
